@@ -1,0 +1,199 @@
+// Elementwise / gather kernels: SwiGLU forward+backward, token embedding
+// forward (vocab-slice aware, for the vocab-parallel embedding) and backward
+// (fp32 atomics), casts.
+//
+// Reference ops replaced: HF Qwen3MLP act_fn(gate)*up and nn.Embedding /
+// the TP EmbeddingParallel masked lookup (transformers/integrations/
+// tensor_parallel.py, used through parallel/parallel/engine/model_parallel/
+// models/qwen3.py:40).
+#include <cuda_bf16.h>
+
+#include "host_util.h"
+#include "ops.cuh"
+#include "ptx.cuh"
+
+namespace pb {
+namespace {
+
+__device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16(x)); }
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + __expf(-x)); }
+
+// 8 bf16 per thread per step.
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dh, int64_t lddh,
+                                  const __nv_bfloat16* __restrict__ gu, int64_t ldgu,
+                                  __nv_bfloat16* __restrict__ dgu, int64_t lddgu, int T, int I) {
+  const int vec_per_row = I / 8;
+  const int64_t total = (int64_t)T * vec_per_row;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(idx / vec_per_row);
+    const int c = (int)(idx % vec_per_row) * 8;
+    uint4 hraw = *reinterpret_cast<const uint4*>(dh + (int64_t)t * lddh + c);
+    uint4 graw = *reinterpret_cast<const uint4*>(gu + (int64_t)t * ldgu + c);
+    uint4 uraw = *reinterpret_cast<const uint4*>(gu + (int64_t)t * ldgu + I + c);
+    const uint32_t* hp = &hraw.x;
+    const uint32_t* gp = &graw.x;
+    const uint32_t* up = &uraw.x;
+    uint4 dg_out, du_out;
+    uint32_t* dgp = &dg_out.x;
+    uint32_t* dup = &du_out.x;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float2 h2 = unpack_bf16x2(hp[q]), g2 = unpack_bf16x2(gp[q]), u2 = unpack_bf16x2(up[q]);
+      float hv[2] = {h2.x, h2.y}, gv[2] = {g2.x, g2.y}, uv[2] = {u2.x, u2.y};
+      float dg[2], du[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float sg = sigmoid_f(gv[j]);
+        const float silu = gv[j] * sg;
+        du[j] = hv[j] * bfr(silu);
+        dg[j] = hv[j] * uv[j] * sg * (1.f + gv[j] * (1.f - sg));
+      }
+      dgp[q] = pack_bf16x2(dg[0], dg[1]);
+      dup[q] = pack_bf16x2(du[0], du[1]);
+    }
+    *reinterpret_cast<uint4*>(dgu + (int64_t)t * lddgu + c) = dg_out;
+    *reinterpret_cast<uint4*>(dgu + (int64_t)t * lddgu + I + c) = du_out;
+  }
+}
+
+__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, int64_t ldgu,
+                                  __nv_bfloat16* __restrict__ h, int64_t ldh, int T, int I) {
+  const int vec_per_row = I / 8;
+  const int64_t total = (int64_t)T * vec_per_row;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(idx / vec_per_row);
+    const int c = (int)(idx % vec_per_row) * 8;
+    uint4 graw = *reinterpret_cast<const uint4*>(gu + (int64_t)t * ldgu + c);
+    uint4 uraw = *reinterpret_cast<const uint4*>(gu + (int64_t)t * ldgu + I + c);
+    const uint32_t* gp = &graw.x;
+    const uint32_t* up = &uraw.x;
+    uint4 o;
+    uint32_t* op = &o.x;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float2 g2 = unpack_bf16x2(gp[q]), u2 = unpack_bf16x2(up[q]);
+      op[q] = pack_bf16x2(g2.x * sigmoid_f(g2.x) * u2.x, g2.y * sigmoid_f(g2.y) * u2.y);
+    }
+    *reinterpret_cast<uint4*>(h + (int64_t)t * ldh + c) = o;
+  }
+}
+
+// One warp per token; H % 8 == 0.
+__global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids,
+                                     const __nv_bfloat16* __restrict__ table, int64_t ldt,
+                                     __nv_bfloat16* __restrict__ out, int64_t ldo, int T, int H,
+                                     int64_t v0, int64_t vrows) {
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const int64_t row = ids[t] - v0;
+  const bool inside = row >= 0 && row < vrows;
+  __nv_bfloat16* o = out + (int64_t)t * ldo;
+  for (int c = lane * 8; c < H; c += 256) {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (inside) v = *reinterpret_cast<const uint4*>(table + row * ldt + c);
+    *reinterpret_cast<uint4*>(o + c) = v;
+  }
+}
+
+__global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids,
+                                     const __nv_bfloat16* __restrict__ dy, int64_t lddy,
+                                     float* __restrict__ grad, int64_t ldg, int T, int H, int64_t v0,
+                                     int64_t vrows) {
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const int64_t row = ids[t] - v0;
+  if (row < 0 || row >= vrows) return;
+  const __nv_bfloat16* g = dy + (int64_t)t * lddy;
+  float* dst = grad + row * ldg;
+  for (int c = lane * 8; c < H; c += 256) {
+    uint4 raw = *reinterpret_cast<const uint4*>(g + c);
+    const uint32_t* p = &raw.x;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float2 f = unpack_bf16x2(p[q]);
+      atomicAdd(dst + c + 2 * q, f.x);
+      atomicAdd(dst + c + 2 * q + 1, f.y);
+    }
+  }
+}
+
+__global__ void cast_f32_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst,
+                                     int64_t n) {
+  for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 4; i < n;
+       i += (int64_t)gridDim.x * blockDim.x * 4) {
+    if (i + 4 <= n) {
+      float4 v = *reinterpret_cast<const float4*>(src + i);
+      uint2 o;
+      o.x = pack_bf16x2(v.x, v.y);
+      o.y = pack_bf16x2(v.z, v.w);
+      *reinterpret_cast<uint2*>(dst + i) = o;
+    } else {
+      for (int64_t j = i; j < n; ++j) dst[j] = __float2bfloat16(src[j]);
+    }
+  }
+}
+
+__global__ void add_bf16_kernel(__nv_bfloat16* __restrict__ dst, const __nv_bfloat16* __restrict__ src,
+                                int64_t n, float alpha) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = __float2bfloat16(__bfloat162float(dst[i]) + alpha * __bfloat162float(src[i]));
+}
+
+int grid_for(int64_t work, int threads) {
+  int64_t g = (work + threads - 1) / threads;
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (g > cap) g = cap;
+  return (int)(g < 1 ? 1 : g);
+}
+
+}  // namespace
+
+void swiglu_bwd(const void* dh, int64_t lddh, const void* gu, int64_t ldgu, void* dgu,
+                int64_t lddgu, int T, int I, cudaStream_t s) {
+  PB_CHECK(I % 8 == 0, "swiglu: I must be a multiple of 8");
+  swiglu_bwd_kernel<<<grid_for((int64_t)T * I / 8, 256), 256, 0, s>>>(
+      (const __nv_bfloat16*)dh, lddh, (const __nv_bfloat16*)gu, ldgu, (__nv_bfloat16*)dgu, lddgu, T, I);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+void swiglu_fwd(const void* gu, int64_t ldgu, void* h, int64_t ldh, int T, int I, cudaStream_t s) {
+  PB_CHECK(I % 8 == 0, "swiglu: I must be a multiple of 8");
+  swiglu_fwd_kernel<<<grid_for((int64_t)T * I / 8, 256), 256, 0, s>>>(
+      (const __nv_bfloat16*)gu, ldgu, (__nv_bfloat16*)h, ldh, T, I);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+void embedding_fwd(const int64_t* ids, const void* table, int64_t ldt, void* out, int64_t ldo,
+                   int T, int H, int64_t vocab_start, int64_t vocab_rows, cudaStream_t s) {
+  PB_CHECK(H % 8 == 0, "embedding: H must be a multiple of 8");
+  embedding_fwd_kernel<<<(T + 7) / 8, 256, 0, s>>>(ids, (const __nv_bfloat16*)table, ldt,
+                                                   (__nv_bfloat16*)out, ldo, T, H, vocab_start,
+                                                   vocab_rows);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+void embedding_bwd(const int64_t* ids, const void* dy, int64_t lddy, float* grad, int64_t ldg,
+                   int T, int H, int64_t vocab_start, int64_t vocab_rows, cudaStream_t s) {
+  PB_CHECK(H % 8 == 0, "embedding: H must be a multiple of 8");
+  embedding_bwd_kernel<<<(T + 7) / 8, 256, 0, s>>>(ids, (const __nv_bfloat16*)dy, lddy, grad, ldg,
+                                                   T, H, vocab_start, vocab_rows);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+void cast_f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t s) {
+  cast_f32_bf16_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, s>>>(src, (__nv_bfloat16*)dst, n);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+void add_bf16_inplace(void* dst, const void* src, int64_t n, float alpha, cudaStream_t s) {
+  add_bf16_kernel<<<grid_for(n, 256), 256, 0, s>>>((__nv_bfloat16*)dst, (const __nv_bfloat16*)src, n,
+                                                   alpha);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace pb

@@ -1,0 +1,177 @@
+// Cross-entropy over a bf16 logits block, forward and backward in one pass
+// pair (row statistics, then the softmax-minus-onehot gradient written in
+// place over the logits), plus per-row statistics for the vocab-parallel
+// merge across tensor-parallel ranks.
+//
+// Reference semantics: HF ForCausalLMLoss (logits upcast to fp32, mean over
+// labels != -100; transformers/loss/loss_utils.py) on the non-model-parallel
+// path and DTensor loss_parallel cross-entropy on the vocab-sharded path
+// (parallel/parallel/engine/model_parallel/loss_parallel.py:22-69).
+#include <cuda_bf16.h>
+#include <float.h>
+
+#include "host_util.h"
+#include "ops.cuh"
+#include "ptx.cuh"
+
+namespace pb {
+namespace {
+
+constexpr int kThreads = 512;
+
+__device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2) {
+  const float mn = fmaxf(m, m2);
+  if (mn == -FLT_MAX) return;
+  s = s * __expf(m - mn) + s2 * __expf(m2 - mn);
+  m = mn;
+}
+
+__device__ __forceinline__ void block_stats(float& m, float& s) {
+  __shared__ float sm[kThreads / 32], ss[kThreads / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    online_merge(m, s, m2, s2);
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sm[w] = m; ss[w] = s; }
+  __syncthreads();
+  if (w == 0) {
+    m = lane < kThreads / 32 ? sm[lane] : -FLT_MAX;
+    s = lane < kThreads / 32 ? ss[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      online_merge(m, s, m2, s2);
+    }
+    if (lane == 0) { sm[0] = m; ss[0] = s; }
+  }
+  __syncthreads();
+  m = sm[0];
+  s = ss[0];
+  __syncthreads();
+}
+
+// Local row max / sum-exp with 8-wide vector loads (V % 8 == 0 and 16-byte
+// aligned rows) or a scalar fallback.
+__device__ __forceinline__ void row_local_stats(const __nv_bfloat16* row, int V, bool vec, float& m,
+                                                float& s) {
+  m = -FLT_MAX;
+  s = 0.f;
+  if (vec) {
+    for (int c = threadIdx.x * 8; c < V; c += kThreads * 8) {
+      uint4 raw = *reinterpret_cast<const uint4*>(row + c);
+      const uint32_t* p = &raw.x;
+      float v[8];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 f = unpack_bf16x2(p[q]);
+        v[2 * q] = f.x;
+        v[2 * q + 1] = f.y;
+      }
+      float lm = v[0];
+#pragma unroll
+      for (int j = 1; j < 8; ++j) lm = fmaxf(lm, v[j]);
+      float ls = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ls += __expf(v[j] - lm);
+      online_merge(m, s, lm, ls);
+    }
+  } else {
+    for (int c = threadIdx.x; c < V; c += kThreads) online_merge(m, s, __bfloat162float(row[c]), 1.f);
+  }
+  block_stats(m, s);
+}
+
+__global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld,
+                                                     const int64_t* __restrict__ labels, int T, int V,
+                                                     int64_t v0, const float* __restrict__ scale,
+                                                     float* __restrict__ row_lse, bool lse_given,
+                                                     float* __restrict__ row_target,
+                                                     float* __restrict__ loss_sum, bool write_grad) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  __nv_bfloat16* row = logits + (int64_t)t * ld;
+  const bool vec = (V % 8 == 0) && ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
+  float lse;
+  if (lse_given) {
+    lse = row_lse[t];
+  } else {
+    float m, s;
+    row_local_stats(row, V, vec, m, s);
+    lse = m + __logf(s);
+    if (threadIdx.x == 0 && row_lse) row_lse[t] = lse;
+  }
+  const int64_t label = labels[t];
+  const bool valid = label >= 0;
+  const int64_t local = label - v0;
+  const bool inside = valid && local >= 0 && local < V;
+  if (threadIdx.x == 0) {
+    const float tgt = inside ? __bfloat162float(row[local]) : 0.f;
+    if (row_target) row_target[t] = tgt;
+    if (loss_sum && valid) atomicAdd(loss_sum, lse - tgt);
+  }
+  if (!write_grad) return;
+  __syncthreads();  // the target logit is read before it is overwritten
+  const float sc = valid ? scale[0] : 0.f;
+  if (vec) {
+    for (int c = threadIdx.x * 8; c < V; c += kThreads * 8) {
+      uint4 raw = *reinterpret_cast<const uint4*>(row + c);
+      uint32_t* p = &raw.x;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 f = unpack_bf16x2(p[q]);
+        float g0 = __expf(f.x - lse), g1 = __expf(f.y - lse);
+        if (inside && c + 2 * q == local) g0 -= 1.f;
+        if (inside && c + 2 * q + 1 == local) g1 -= 1.f;
+        p[q] = pack_bf16x2(g0 * sc, g1 * sc);
+      }
+      *reinterpret_cast<uint4*>(row + c) = raw;
+    }
+  } else {
+    for (int c = threadIdx.x; c < V; c += kThreads) {
+      float g = __expf(__bfloat162float(row[c]) - lse);
+      if (inside && c == local) g -= 1.f;
+      row[c] = __float2bfloat16(g * sc);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) ce_stats_kernel(const __nv_bfloat16* __restrict__ logits,
+                                                           int64_t ld, int T, int V,
+                                                           float* __restrict__ row_max,
+                                                           float* __restrict__ row_sumexp) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  const __nv_bfloat16* row = logits + (int64_t)t * ld;
+  const bool vec = (V % 8 == 0) && ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
+  float m, s;
+  row_local_stats(row, V, vec, m, s);
+  if (threadIdx.x == 0) {
+    row_max[t] = m;
+    row_sumexp[t] = s;
+  }
+}
+
+}  // namespace
+
+void ce_fwd_bwd(void* logits, int64_t ld, const int64_t* labels, int T, int V, int64_t v0,
+                const float* scale, float* row_lse, bool lse_given, float* row_target,
+                float* loss_sum, bool write_grad, cudaStream_t s) {
+  if (T == 0) return;
+  PB_CHECK(!write_grad || scale != nullptr, "ce: gradient scale pointer required");
+  ce_kernel<<<T, kThreads, 0, s>>>((__nv_bfloat16*)logits, ld, labels, T, V, v0, scale, row_lse,
+                                   lse_given, row_target, loss_sum, write_grad);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+void ce_row_stats(const void* logits, int64_t ld, int T, int V, float* row_max, float* row_sumexp,
+                  cudaStream_t s) {
+  if (T == 0) return;
+  ce_stats_kernel<<<T, kThreads, 0, s>>>((const __nv_bfloat16*)logits, ld, T, V, row_max, row_sumexp);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace pb

@@ -1,0 +1,49 @@
+// Host-side helpers shared by every launcher: TMA descriptor encoding through
+// the driver entry point, the per-device error word, SM counts and launch
+// checks.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <stdexcept>
+#include <string>
+
+namespace pb {
+
+// Throws std::runtime_error with file/line context on a CUDA runtime error.
+#define PB_CUDA_CHECK(expr)                                                               \
+  do {                                                                                    \
+    cudaError_t _e = (expr);                                                              \
+    if (_e != cudaSuccess)                                                                \
+      throw std::runtime_error(std::string("CUDA error ") + cudaGetErrorString(_e) +      \
+                               " at " + __FILE__ + ":" + std::to_string(__LINE__));       \
+  } while (0)
+
+#define PB_CHECK(cond, msg)                                                        \
+  do {                                                                             \
+    if (!(cond)) throw std::runtime_error(std::string("parallel_b200: ") + (msg)); \
+  } while (0)
+
+// Device pointer to this device's 4-byte error word (allocated on first use,
+// zero-initialised).  Kernels record timeouts there; the host reads it with
+// read_error() and clears it with clear_error().
+int* error_word(int device = -1);
+int read_error(int device = -1);
+void clear_error(int device = -1);
+
+int num_sms(int device = -1);
+
+// Encode a 2-D bf16 tiled tensor map with 128-byte swizzle.
+//   inner/outer: extents in elements; row_stride_elems: stride of the outer
+//   dimension in elements; box_inner/box_outer: tile extents in elements.
+CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t inner, uint64_t outer,
+                              uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
+                              bool swizzle128 = true);
+
+// Encode a 3-D bf16 tiled tensor map with 128-byte swizzle.
+CUtensorMap make_tmap_3d_bf16(const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                              uint64_t stride1_elems, uint64_t stride2_elems, uint32_t b0,
+                              uint32_t b1, uint32_t b2);
+
+}  // namespace pb

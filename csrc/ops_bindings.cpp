@@ -1,0 +1,197 @@
+// Bindings of the memory-bound kernels (ops.cuh).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <vector>
+
+#include "ops.cuh"
+
+namespace {
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+#define CHECK_BF16(t) \
+  TORCH_CHECK((t).is_cuda() && (t).scalar_type() == at::kBFloat16 && (t).stride(-1) == 1, #t " must be CUDA bf16 with unit inner stride")
+#define CHECK_F32(t) \
+  TORCH_CHECK((t).is_cuda() && (t).scalar_type() == at::kFloat && (t).is_contiguous(), #t " must be contiguous CUDA fp32")
+
+float* opt_f32(const c10::optional<at::Tensor>& t) {
+  if (!t.has_value() || !t->defined()) return nullptr;
+  CHECK_F32(*t);
+  return t->data_ptr<float>();
+}
+
+void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& rstd,
+                 double eps) {
+  CHECK_BF16(x); CHECK_BF16(w); CHECK_BF16(y);
+  TORCH_CHECK(x.dim() == 2 && y.dim() == 2, "rmsnorm: 2-D");
+  const c10::cuda::CUDAGuard g(x.device());
+  pb::rmsnorm_fwd(x.data_ptr(), x.stride(0), w.data_ptr(), y.data_ptr(), y.stride(0), opt_f32(rstd), x.size(0),
+                  x.size(1), (float)eps, cur_stream());
+}
+
+void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd,
+                 at::Tensor& dx, const c10::optional<at::Tensor>& dw) {
+  CHECK_BF16(dy); CHECK_BF16(x); CHECK_BF16(w); CHECK_BF16(dx); CHECK_F32(rstd);
+  const c10::cuda::CUDAGuard g(x.device());
+  pb::rmsnorm_bwd(dy.data_ptr(), dy.stride(0), x.data_ptr(), x.stride(0), w.data_ptr(), rstd.data_ptr<float>(),
+                  dx.data_ptr(), dx.stride(0), opt_f32(dw), x.size(0), x.size(1), cur_stream());
+}
+
+void qknorm_rope_fwd(const at::Tensor& qkv, const at::Tensor& qw, const at::Tensor& kw, const at::Tensor& cos,
+                     const at::Tensor& sin, at::Tensor& q, at::Tensor& k, at::Tensor& rstd, int64_t S, int64_t nq,
+                     int64_t nkv, double eps) {
+  CHECK_BF16(qkv); CHECK_BF16(qw); CHECK_BF16(kw); CHECK_BF16(cos); CHECK_BF16(sin); CHECK_BF16(q); CHECK_BF16(k);
+  CHECK_F32(rstd);
+  const c10::cuda::CUDAGuard g(qkv.device());
+  const int D = (int)qw.size(0);
+  pb::qknorm_rope_fwd(qkv.data_ptr(), qkv.stride(0), qw.data_ptr(), kw.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                      q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), rstd.data_ptr<float>(), qkv.size(0),
+                      (int)S, (int)nq, (int)nkv, D, (float)eps, cur_stream());
+}
+
+void qknorm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tensor& qkv, const at::Tensor& qw,
+                     const at::Tensor& kw, const at::Tensor& cos, const at::Tensor& sin, const at::Tensor& rstd,
+                     at::Tensor& dqkv, const c10::optional<at::Tensor>& dqw, const c10::optional<at::Tensor>& dkw,
+                     int64_t S, int64_t nq, int64_t nkv) {
+  CHECK_BF16(dq); CHECK_BF16(dk); CHECK_BF16(qkv); CHECK_BF16(dqkv); CHECK_F32(rstd);
+  const c10::cuda::CUDAGuard g(qkv.device());
+  const int D = (int)qw.size(0);
+  pb::qknorm_rope_bwd(dq.data_ptr(), dq.stride(0), dk.data_ptr(), dk.stride(0), qkv.data_ptr(), qkv.stride(0),
+                      qw.data_ptr(), kw.data_ptr(), cos.data_ptr(), sin.data_ptr(), rstd.data_ptr<float>(),
+                      dqkv.data_ptr(), dqkv.stride(0), opt_f32(dqw), opt_f32(dkw), qkv.size(0), (int)S, (int)nq,
+                      (int)nkv, D, cur_stream());
+}
+
+void swiglu_bwd(const at::Tensor& dh, const at::Tensor& gu, at::Tensor& dgu) {
+  CHECK_BF16(dh); CHECK_BF16(gu); CHECK_BF16(dgu);
+  const c10::cuda::CUDAGuard g(dh.device());
+  pb::swiglu_bwd(dh.data_ptr(), dh.stride(0), gu.data_ptr(), gu.stride(0), dgu.data_ptr(), dgu.stride(0),
+                 dh.size(0), dh.size(1), cur_stream());
+}
+
+void swiglu_fwd(const at::Tensor& gu, at::Tensor& h) {
+  CHECK_BF16(gu); CHECK_BF16(h);
+  const c10::cuda::CUDAGuard g(gu.device());
+  pb::swiglu_fwd(gu.data_ptr(), gu.stride(0), h.data_ptr(), h.stride(0), h.size(0), h.size(1), cur_stream());
+}
+
+void embedding_fwd(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int64_t v0) {
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "ids must be contiguous int64");
+  CHECK_BF16(table); CHECK_BF16(out);
+  const c10::cuda::CUDAGuard g(table.device());
+  pb::embedding_fwd(ids.data_ptr<int64_t>(), table.data_ptr(), table.stride(0), out.data_ptr(), out.stride(0),
+                    ids.numel(), table.size(1), v0, table.size(0), cur_stream());
+}
+
+void embedding_bwd(const at::Tensor& ids, const at::Tensor& dy, at::Tensor& grad, int64_t v0) {
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "ids must be contiguous int64");
+  CHECK_BF16(dy); CHECK_F32(grad);
+  const c10::cuda::CUDAGuard g(dy.device());
+  pb::embedding_bwd(ids.data_ptr<int64_t>(), dy.data_ptr(), dy.stride(0), grad.data_ptr<float>(), grad.stride(0),
+                    ids.numel(), dy.size(1), v0, grad.size(0), cur_stream());
+}
+
+void ce_fwd_bwd(at::Tensor& logits, const at::Tensor& labels, int64_t v0, const c10::optional<at::Tensor>& scale,
+                const c10::optional<at::Tensor>& row_lse, bool lse_given, const c10::optional<at::Tensor>& row_target,
+                const c10::optional<at::Tensor>& loss_sum, bool write_grad) {
+  CHECK_BF16(logits);
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous(), "labels must be contiguous int64");
+  TORCH_CHECK(labels.numel() == logits.size(0), "ce: one label per row");
+  const c10::cuda::CUDAGuard g(logits.device());
+  pb::ce_fwd_bwd(logits.data_ptr(), logits.stride(0), labels.data_ptr<int64_t>(), logits.size(0), logits.size(1),
+                 v0, opt_f32(scale), opt_f32(row_lse), lse_given, opt_f32(row_target), opt_f32(loss_sum),
+                 write_grad, cur_stream());
+}
+
+void ce_row_stats(const at::Tensor& logits, at::Tensor& row_max, at::Tensor& row_sumexp) {
+  CHECK_BF16(logits); CHECK_F32(row_max); CHECK_F32(row_sumexp);
+  const c10::cuda::CUDAGuard g(logits.device());
+  pb::ce_row_stats(logits.data_ptr(), logits.stride(0), logits.size(0), logits.size(1), row_max.data_ptr<float>(),
+                   row_sumexp.data_ptr<float>(), cur_stream());
+}
+
+void cast_f32_to_bf16(const at::Tensor& src, at::Tensor& dst) {
+  CHECK_F32(src);
+  TORCH_CHECK(dst.is_contiguous() && dst.scalar_type() == at::kBFloat16 && dst.numel() == src.numel(), "cast: dst");
+  const c10::cuda::CUDAGuard g(src.device());
+  pb::cast_f32_to_bf16(src.data_ptr<float>(), dst.data_ptr(), src.numel(), cur_stream());
+}
+
+// params/grads/exp_avgs/exp_avg_sqs: lists of equally sized tensors (1 segment each)
+void adamw(const std::vector<at::Tensor>& params, const std::vector<at::Tensor>& grads,
+           const std::vector<at::Tensor>& exp_avgs, const std::vector<at::Tensor>& exp_avg_sqs, double lr,
+           double beta1, double beta2, double eps, double wd, int64_t step,
+           const c10::optional<at::Tensor>& grad_scale, const c10::optional<at::Tensor>& skip) {
+  TORCH_CHECK(params.size() == grads.size() && params.size() == exp_avgs.size() &&
+              params.size() == exp_avg_sqs.size(), "adamw: list sizes differ");
+  if (params.empty()) return;
+  const bool grad_f32 = grads[0].scalar_type() == at::kFloat;
+  const bool state_f32 = exp_avgs[0].scalar_type() == at::kFloat;
+  std::vector<pb::AdamSeg> segs;
+  segs.reserve(params.size());
+  for (size_t i = 0; i < params.size(); ++i) {
+    TORCH_CHECK(params[i].is_contiguous() && grads[i].is_contiguous() && exp_avgs[i].is_contiguous() &&
+                exp_avg_sqs[i].is_contiguous(), "adamw: tensors must be contiguous");
+    TORCH_CHECK(params[i].scalar_type() == at::kBFloat16, "adamw: bf16 params");
+    TORCH_CHECK((grads[i].scalar_type() == at::kFloat) == grad_f32, "adamw: mixed grad dtypes");
+    TORCH_CHECK((exp_avgs[i].scalar_type() == at::kFloat) == state_f32, "adamw: mixed state dtypes");
+    TORCH_CHECK(grads[i].numel() == params[i].numel() && exp_avgs[i].numel() == params[i].numel(),
+                "adamw: numel mismatch");
+    segs.push_back({params[i].data_ptr(), grads[i].data_ptr(), exp_avgs[i].data_ptr(), exp_avg_sqs[i].data_ptr(),
+                    params[i].numel()});
+  }
+  const c10::cuda::CUDAGuard g(params[0].device());
+  const int* skip_ptr = nullptr;
+  if (skip.has_value() && skip->defined()) {
+    TORCH_CHECK(skip->scalar_type() == at::kInt, "adamw: skip must be int32");
+    skip_ptr = skip->data_ptr<int>();
+  }
+  pb::adamw_multi(segs.data(), (int)segs.size(), (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd,
+                  (int)step, opt_f32(grad_scale), skip_ptr, grad_f32, state_f32, cur_stream());
+}
+
+void sumsq(const std::vector<at::Tensor>& grads, const std::vector<double>& weights, at::Tensor& out,
+           const c10::optional<at::Tensor>& flag) {
+  if (grads.empty()) return;
+  CHECK_F32(out);
+  const bool f32 = grads[0].scalar_type() == at::kFloat;
+  std::vector<pb::NormSeg> segs;
+  for (size_t i = 0; i < grads.size(); ++i) {
+    TORCH_CHECK(grads[i].is_contiguous(), "sumsq: contiguous grads");
+    TORCH_CHECK((grads[i].scalar_type() == at::kFloat) == f32, "sumsq: mixed dtypes");
+    segs.push_back({grads[i].data_ptr(), grads[i].numel(), (float)(weights.empty() ? 1.0 : weights[i])});
+  }
+  int* flag_ptr = nullptr;
+  if (flag.has_value() && flag->defined()) flag_ptr = flag->data_ptr<int>();
+  const c10::cuda::CUDAGuard g(out.device());
+  pb::sumsq_multi(segs.data(), (int)segs.size(), f32, out.data_ptr<float>(), flag_ptr, cur_stream());
+}
+
+void clip_coef(const at::Tensor& total, double max_norm, at::Tensor& out) {
+  CHECK_F32(total); CHECK_F32(out);
+  const c10::cuda::CUDAGuard g(total.device());
+  pb::clip_coef(total.data_ptr<float>(), (float)max_norm, out.data_ptr<float>(), cur_stream());
+}
+
+}  // namespace
+
+void register_ops(pybind11::module& m) {
+  namespace py = pybind11;
+  m.def("rmsnorm_fwd", &rmsnorm_fwd, py::arg("x"), py::arg("w"), py::arg("y"), py::arg("rstd"), py::arg("eps"));
+  m.def("rmsnorm_bwd", &rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dx"),
+        py::arg("dw"));
+  m.def("qknorm_rope_fwd", &qknorm_rope_fwd);
+  m.def("qknorm_rope_bwd", &qknorm_rope_bwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("ce_fwd_bwd", &ce_fwd_bwd);
+  m.def("ce_row_stats", &ce_row_stats);
+  m.def("cast_f32_to_bf16", &cast_f32_to_bf16);
+  m.def("adamw", &adamw);
+  m.def("sumsq", &sumsq);
+  m.def("clip_coef", &clip_coef);
+}

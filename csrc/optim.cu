@@ -1,0 +1,188 @@
+// Multi-tensor AdamW and the one-pass gradient sum-of-squares / finite check.
+//
+// Reference semantics: torch.optim.AdamW on the (bf16) parameter shards
+// (parallel/parallel/engine/engine.py:61-66) with clipping by the global norm
+// (parallel/parallel/engine/model_parallel/grad_norm.py:15-82,
+// parallel/parallel/engine/dp_sharded.py:453-472) and the finite check of
+// engine.py:249-268.  Here the clip coefficient never leaves the device: it
+// is computed by clip_coef() and multiplied into the gradient inside the
+// AdamW kernel, and a non-finite flag makes the update a no-op.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "host_util.h"
+#include "ops.cuh"
+#include "ptx.cuh"
+
+namespace pb {
+namespace {
+
+constexpr int kMaxSegs = 48;
+constexpr int kThreads = 256;
+constexpr int kChunk = 4096;  // elements per block-chunk
+
+struct SegTable {
+  AdamSeg seg[kMaxSegs];
+  int chunk_start[kMaxSegs + 1];
+  int nseg;
+};
+
+struct NormTable {
+  NormSeg seg[kMaxSegs];
+  int chunk_start[kMaxSegs + 1];
+  int nseg;
+};
+
+template <typename T>
+__device__ __forceinline__ float ldf(const void* p, int64_t i) {
+  if constexpr (sizeof(T) == 4)
+    return reinterpret_cast<const float*>(p)[i];
+  else
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+}
+template <typename T>
+__device__ __forceinline__ void stf(void* p, int64_t i, float v) {
+  if constexpr (sizeof(T) == 4)
+    reinterpret_cast<float*>(p)[i] = v;
+  else
+    reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16(v);
+}
+
+__device__ __forceinline__ int find_seg(const int* starts, int nseg, int chunk) {
+  int s = 0;
+  while (s + 1 < nseg && starts[s + 1] <= chunk) ++s;
+  return s;
+}
+
+template <typename GT, typename ST>
+__global__ void __launch_bounds__(kThreads) adamw_kernel(SegTable tab, float lr, float beta1,
+                                                         float beta2, float eps, float wd,
+                                                         float bc1, float bc2_sqrt,
+                                                         const float* __restrict__ gscale,
+                                                         const int* __restrict__ skip) {
+  if (skip && *skip) return;
+  const float gs = gscale ? *gscale : 1.f;
+  const int chunk = blockIdx.x;
+  const int si = find_seg(tab.chunk_start, tab.nseg, chunk);
+  const AdamSeg sg = tab.seg[si];
+  const int64_t base = (int64_t)(chunk - tab.chunk_start[si]) * kChunk;
+  const int64_t end = min(sg.n, base + kChunk);
+  const float step_size = lr / bc1;
+  for (int64_t i = base + threadIdx.x; i < end; i += kThreads) {
+    const float g = ldf<GT>(sg.g, i) * gs;
+    float p = ldf<__nv_bfloat16>(sg.p, i);
+    float m = ldf<ST>(sg.m, i);
+    float v = ldf<ST>(sg.v, i);
+    p *= 1.f - lr * wd;
+    m += (g - m) * (1.f - beta1);
+    v = v * beta2 + (1.f - beta2) * g * g;
+    const float denom = sqrtf(v) / bc2_sqrt + eps;
+    p -= step_size * m / denom;
+    stf<__nv_bfloat16>(sg.p, i, p);
+    stf<ST>(sg.m, i, m);
+    stf<ST>(sg.v, i, v);
+  }
+}
+
+template <typename GT>
+__global__ void __launch_bounds__(kThreads) sumsq_kernel(NormTable tab, float* __restrict__ out,
+                                                         int* __restrict__ flag) {
+  const int chunk = blockIdx.x;
+  const int si = find_seg(tab.chunk_start, tab.nseg, chunk);
+  const NormSeg sg = tab.seg[si];
+  const int64_t base = (int64_t)(chunk - tab.chunk_start[si]) * kChunk;
+  const int64_t end = min(sg.n, base + kChunk);
+  float acc = 0.f;
+  bool bad = false;
+  for (int64_t i = base + threadIdx.x; i < end; i += kThreads) {
+    const float g = ldf<GT>(sg.g, i);
+    bad |= !isfinite(g);
+    acc += g * g;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  const unsigned any_bad = __ballot_sync(0xffffffffu, bad);
+  __shared__ float sacc[kThreads / 32];
+  __shared__ int sbad;
+  if (threadIdx.x == 0) sbad = 0;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) {
+    sacc[threadIdx.x >> 5] = acc;
+    if (any_bad) sbad = 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < kThreads / 32; ++w) t += sacc[w];
+    atomicAdd(out, t * sg.weight);
+    if (sbad && flag) atomicExch(flag, 1);
+  }
+}
+
+__global__ void clip_coef_kernel(const float* total, float max_norm, float* out) {
+  const float n = sqrtf(*total);
+  out[0] = fminf(max_norm / (n + 1e-6f), 1.f);
+}
+
+}  // namespace
+
+void adamw_multi(const AdamSeg* segs, int nseg, float lr, float beta1, float beta2, float eps,
+                 float wd, int step, const float* grad_scale_dev, const int* skip_dev, bool grad_f32,
+                 bool state_f32, cudaStream_t s) {
+  const float bc1 = 1.f - powf(beta1, (float)step);
+  const float bc2_sqrt = sqrtf(1.f - powf(beta2, (float)step));
+  for (int off = 0; off < nseg; off += kMaxSegs) {
+    SegTable tab{};
+    tab.nseg = std::min(kMaxSegs, nseg - off);
+    int chunks = 0;
+    for (int i = 0; i < tab.nseg; ++i) {
+      tab.seg[i] = segs[off + i];
+      tab.chunk_start[i] = chunks;
+      chunks += (int)((segs[off + i].n + kChunk - 1) / kChunk);
+    }
+    tab.chunk_start[tab.nseg] = chunks;
+    if (chunks == 0) continue;
+    if (grad_f32 && state_f32)
+      adamw_kernel<float, float><<<chunks, kThreads, 0, s>>>(tab, lr, beta1, beta2, eps, wd, bc1,
+                                                             bc2_sqrt, grad_scale_dev, skip_dev);
+    else if (grad_f32)
+      adamw_kernel<float, __nv_bfloat16><<<chunks, kThreads, 0, s>>>(
+          tab, lr, beta1, beta2, eps, wd, bc1, bc2_sqrt, grad_scale_dev, skip_dev);
+    else if (state_f32)
+      adamw_kernel<__nv_bfloat16, float><<<chunks, kThreads, 0, s>>>(
+          tab, lr, beta1, beta2, eps, wd, bc1, bc2_sqrt, grad_scale_dev, skip_dev);
+    else
+      adamw_kernel<__nv_bfloat16, __nv_bfloat16><<<chunks, kThreads, 0, s>>>(
+          tab, lr, beta1, beta2, eps, wd, bc1, bc2_sqrt, grad_scale_dev, skip_dev);
+    PB_CUDA_CHECK(cudaGetLastError());
+  }
+}
+
+void sumsq_multi(const NormSeg* segs, int nseg, bool f32, float* out, int* out_flag, cudaStream_t s) {
+  for (int off = 0; off < nseg; off += kMaxSegs) {
+    NormTable tab{};
+    tab.nseg = std::min(kMaxSegs, nseg - off);
+    int chunks = 0;
+    for (int i = 0; i < tab.nseg; ++i) {
+      tab.seg[i] = segs[off + i];
+      tab.chunk_start[i] = chunks;
+      chunks += (int)((segs[off + i].n + kChunk - 1) / kChunk);
+    }
+    tab.chunk_start[tab.nseg] = chunks;
+    if (chunks == 0) continue;
+    if (f32)
+      sumsq_kernel<float><<<chunks, kThreads, 0, s>>>(tab, out, out_flag);
+    else
+      sumsq_kernel<__nv_bfloat16><<<chunks, kThreads, 0, s>>>(tab, out, out_flag);
+    PB_CUDA_CHECK(cudaGetLastError());
+  }
+}
+
+void clip_coef(const float* total_sumsq, float max_norm, float* scale_out, cudaStream_t s) {
+  clip_coef_kernel<<<1, 1, 0, s>>>(total_sumsq, max_norm, scale_out);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace pb

@@ -1,0 +1,249 @@
+"""Numerics of the sm_100a kernels against fp32 PyTorch restatements."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ext():
+    from parallel_b200.ops._ext import ext
+
+    return ext()
+
+
+def _check_no_device_error():
+    from parallel_b200.ops._ext import check_device_errors
+
+    torch.cuda.synchronize()
+    check_device_errors()
+
+
+def _rel_err(a, b):
+    return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 512, 256), (304, 200, 136), (1024, 1536, 1024),
+                                   (8192, 1024, 1024), (2048, 4096, 1024)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+def test_gemm_layouts(M, N, K, a_mn, b_mn):
+    C = _ext()
+    torch.manual_seed(0)
+    A = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    B = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    a_arg = A.t().contiguous() if a_mn else A
+    b_arg = B.t().contiguous() if b_mn else B
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm(a_arg, b_arg, out, a_mn, b_mn, 0, 1.0)
+    _check_no_device_error()
+    ref = A.float() @ B.float().t()
+    assert _rel_err(out, ref) < 1e-2
+
+
+def test_gemm_epilogues():
+    C = _ext()
+    torch.manual_seed(1)
+    M, N, K = 512, 384, 320
+    A = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    B = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    R = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+    ref = A.float() @ B.float().t()
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm(A, B, out, False, False, 1, 1.0, R)
+    assert _rel_err(out, ref + R.float()) < 1e-2
+    out32 = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    C.gemm(A, B, out32, False, False, 2, 0.5)
+    assert _rel_err(out32, 0.5 * ref) < 1e-3
+    C.gemm(A, B, out32, False, False, 4, 0.5)
+    assert _rel_err(out32, ref) < 1e-3
+    acc = R.clone()
+    C.gemm(A, B, acc, False, False, 3, 1.0)
+    assert _rel_err(acc, ref + R.float()) < 1e-2
+    _check_no_device_error()
+
+
+@pytest.mark.parametrize("T,I,H", [(256, 384, 256), (1024, 3072, 1024)])
+def test_gemm_swiglu(T, I, H):
+    from parallel_b200.ops.gemm import linear_swiglu
+
+    torch.manual_seed(2)
+    x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(2 * I, H, device="cuda", dtype=torch.bfloat16) / math.sqrt(H)
+    h, gu = linear_swiglu(x, w, I)
+    _check_no_device_error()
+    gu_ref = x.float() @ w.float().t()
+    g, u = gu_ref[:, :I], gu_ref[:, I:]
+    h_ref = torch.nn.functional.silu(g) * u
+    assert _rel_err(gu, gu_ref) < 1e-2
+    assert _rel_err(h, h_ref) < 2e-2
+
+
+def test_linear_products():
+    from parallel_b200.ops.gemm import linear, linear_dgrad, linear_wgrad
+
+    torch.manual_seed(3)
+    T, K, N = 1024, 512, 768
+    x = torch.randn(T, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    g = torch.randn(T, N, device="cuda", dtype=torch.bfloat16)
+    assert _rel_err(linear(x, w), x.float() @ w.float().t()) < 1e-2
+    assert _rel_err(linear_dgrad(g, w), g.float() @ w.float()) < 1e-2
+    assert _rel_err(linear_wgrad(g, x), g.float().t() @ x.float()) < 1e-2
+    _check_no_device_error()
+
+
+def test_rmsnorm_fwd_bwd():
+    C = _ext()
+    torch.manual_seed(4)
+    T, H = 1000, 1024
+    x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(H, device="cuda")).to(torch.bfloat16)
+    y = torch.empty_like(x)
+    rstd = torch.empty(T, device="cuda")
+    C.rmsnorm_fwd(x, w, y, rstd, 1e-6)
+    xf = x.float().requires_grad_(True)
+    wf = w.float().requires_grad_(True)
+    yr = wf * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6))
+    assert _rel_err(y, yr) < 1e-2
+    dy = torch.randn_like(x)
+    dx = torch.empty_like(x)
+    dw = torch.zeros(H, device="cuda")
+    C.rmsnorm_bwd(dy, x, w, rstd, dx, dw)
+    yr.backward(dy.float())
+    assert _rel_err(dx, xf.grad) < 1e-2
+    assert _rel_err(dw, wf.grad) < 1e-2
+    _check_no_device_error()
+
+
+def _rope_ref(q, cos, sin):
+    half = q.shape[-1] // 2
+    rot = torch.cat((-q[..., half:], q[..., :half]), dim=-1)
+    return q * cos + rot * sin
+
+
+def test_qknorm_rope_fwd_bwd():
+    C = _ext()
+    torch.manual_seed(5)
+    B, S, nq, nkv, D = 2, 64, 4, 2, 128
+    T = B * S
+    qkv = torch.randn(T, (nq + 2 * nkv) * D, device="cuda", dtype=torch.bfloat16)
+    qw = (1 + 0.1 * torch.randn(D, device="cuda")).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(D, device="cuda")).to(torch.bfloat16)
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, device="cuda").float() / D))
+    fr = torch.arange(S, device="cuda").float()[:, None] * inv[None]
+    emb = torch.cat((fr, fr), -1)
+    cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+    q = torch.empty(T, nq * D, device="cuda", dtype=torch.bfloat16)
+    k = torch.empty(T, nkv * D, device="cuda", dtype=torch.bfloat16)
+    rstd = torch.empty(T, nq + nkv, device="cuda")
+    C.qknorm_rope_fwd(qkv, qw, kw, cos, sin, q, k, rstd, S, nq, nkv, 1e-6)
+
+    qkvf = qkv.float().requires_grad_(True)
+    qwf, kwf = qw.float().requires_grad_(True), kw.float().requires_grad_(True)
+    qp = qkvf[:, : nq * D].view(T, nq, D)
+    kp = qkvf[:, nq * D:(nq + nkv) * D].view(T, nkv, D)
+
+    def nrm(x, w):
+        return w * (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6))
+
+    pos = torch.arange(T, device="cuda") % S
+    c, s = cos.float()[pos][:, None], sin.float()[pos][:, None]
+    qr = _rope_ref(nrm(qp, qwf), c, s).reshape(T, -1)
+    kr = _rope_ref(nrm(kp, kwf), c, s).reshape(T, -1)
+    assert _rel_err(q, qr) < 1e-2
+    assert _rel_err(k, kr) < 1e-2
+    dq = torch.randn_like(q)
+    dk = torch.randn_like(k)
+    dqkv = torch.zeros_like(qkv)
+    dqw = torch.zeros(D, device="cuda")
+    dkw = torch.zeros(D, device="cuda")
+    C.qknorm_rope_bwd(dq, dk, qkv, qw, kw, cos, sin, rstd, dqkv, dqw, dkw, S, nq, nkv)
+    (qr * dq.float()).sum().add((kr * dk.float()).sum()).backward()
+    assert _rel_err(dqkv[:, : (nq + nkv) * D], qkvf.grad[:, : (nq + nkv) * D]) < 2e-2
+    assert _rel_err(dqw, qwf.grad) < 2e-2
+    assert _rel_err(dkw, kwf.grad) < 2e-2
+    _check_no_device_error()
+
+
+def test_swiglu_bwd():
+    C = _ext()
+    torch.manual_seed(6)
+    T, I = 512, 768
+    gu = torch.randn(T, 2 * I, device="cuda", dtype=torch.bfloat16)
+    dh = torch.randn(T, I, device="cuda", dtype=torch.bfloat16)
+    dgu = torch.empty_like(gu)
+    C.swiglu_bwd(dh, gu, dgu)
+    guf = gu.float().requires_grad_(True)
+    h = torch.nn.functional.silu(guf[:, :I]) * guf[:, I:]
+    h.backward(dh.float())
+    assert _rel_err(dgu, guf.grad) < 1e-2
+    _check_no_device_error()
+
+
+def test_cross_entropy():
+    C = _ext()
+    torch.manual_seed(7)
+    T, V = 300, 5000
+    logits = (3 * torch.randn(T, V, device="cuda")).to(torch.bfloat16)
+    labels = torch.randint(0, V, (T,), device="cuda")
+    labels[::7] = -100
+    valid = (labels >= 0).sum()
+    scale = (1.0 / valid.float()).reshape(1)
+    lse = torch.empty(T, device="cuda")
+    tgt = torch.empty(T, device="cuda")
+    loss_sum = torch.zeros(1, device="cuda")
+    g = logits.clone()
+    C.ce_fwd_bwd(g, labels, 0, scale, lse, False, tgt, loss_sum, True)
+    lf = logits.float().requires_grad_(True)
+    ref = torch.nn.functional.cross_entropy(lf, labels, ignore_index=-100)
+    ref.backward()
+    assert abs(loss_sum.item() / valid.item() - ref.item()) < 1e-3
+    assert _rel_err(g, lf.grad) < 1e-2
+    _check_no_device_error()
+
+
+def test_adamw_and_sumsq():
+    C = _ext()
+    torch.manual_seed(8)
+    n = 10007
+    p = torch.randn(n, device="cuda").to(torch.bfloat16)
+    g = torch.randn(n, device="cuda").to(torch.bfloat16)
+    m = torch.zeros(n, device="cuda", dtype=torch.float32)
+    v = torch.zeros(n, device="cuda", dtype=torch.float32)
+    ref_p = p.float().clone().requires_grad_(False)
+    opt = torch.optim.AdamW([torch.nn.Parameter(ref_p)], lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, eps=1e-8)
+    for step in range(1, 4):
+        opt.param_groups[0]["params"][0].grad = g.float()
+        opt.step()
+        C.adamw([p], [g], [m], [v], 1e-2, 0.9, 0.95, 1e-8, 0.1, step, None, None)
+    assert _rel_err(p, opt.param_groups[0]["params"][0].detach()) < 1e-2
+    out = torch.zeros(1, device="cuda")
+    flag = torch.zeros(1, device="cuda", dtype=torch.int32)
+    C.sumsq([g, g[:100]], [1.0, 0.0], out, flag)
+    assert abs(out.item() - g.float().pow(2).sum().item()) / out.item() < 1e-4
+    assert flag.item() == 0
+    g2 = g.clone()
+    g2[5] = float("nan")
+    C.sumsq([g2], [1.0], out, flag)
+    assert flag.item() == 1
+    _check_no_device_error()
+
+
+def test_embedding():
+    C = _ext()
+    torch.manual_seed(9)
+    V, H, T = 1000, 256, 333
+    table = torch.randn(V, H, device="cuda").to(torch.bfloat16)
+    ids = torch.randint(0, V, (T,), device="cuda")
+    out = torch.empty(T, H, device="cuda", dtype=torch.bfloat16)
+    C.embedding_fwd(ids, table[200:600], out, 200)
+    ref = table[ids].clone()
+    ref[(ids < 200) | (ids >= 600)] = 0
+    assert torch.equal(out, ref)
+    dy = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    grad = torch.zeros(V, H, device="cuda")
+    C.embedding_bwd(ids, dy, grad, 0)
+    ref_g = torch.zeros(V, H, device="cuda").index_add_(0, ids, dy.float())
+    assert _rel_err(grad, ref_g) < 1e-5
+    _check_no_device_error()
