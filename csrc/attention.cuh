@@ -1,0 +1,51 @@
+// Causal GQA flash attention on the sm_100a tensor cores (attention_fwd.cu,
+// attention_bwd.cu).
+//
+// Layouts (token-major, exactly what the QKV GEMM / QK-norm kernels write):
+//   q  : [B*S, nq*D]   row stride ldq,  head h at column h*D
+//   k  : [B*S, nkv*D]  row stride ldk
+//   v  : [B*S, nkv*D]  row stride ldv   (may be a column view of the qkv buffer)
+//   o  : [B*S, nq*D]   row stride ldo
+//   lse: [B*nq, S]     fp32 natural-log sum-exp of the scaled scores
+// Query head h reads kv head h / (nq / nkv).  D == 128.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pb {
+
+struct AttnParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse;
+  int64_t ldq, ldk, ldv, ldo;
+  int B, S, nq, nkv, D;
+  float scale;  // softmax scale (1/sqrt(D))
+  bool causal;
+};
+
+void attention_fwd(const AttnParams& p, cudaStream_t s);
+
+struct AttnBwdParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;
+  const void* dout;
+  const float* lse;
+  float* delta;  // [B*nq, S] scratch: rowsum(dO * O)
+  float* dq_acc; // [B*S, nq*D] fp32 scratch (zeroed by the launcher)
+  void* dq;
+  void* dk;
+  void* dv;
+  int64_t ldq, ldk, ldv, ldo, lddo, lddq, lddk, lddv;
+  int B, S, nq, nkv, D;
+  float scale;
+  bool causal;
+};
+
+void attention_bwd(const AttnBwdParams& p, cudaStream_t s);
+
+}  // namespace pb

@@ -5,6 +5,7 @@
 
 #include <vector>
 
+#include "attention.cuh"
 #include "ops.cuh"
 
 namespace {
@@ -175,6 +176,41 @@ void clip_coef(const at::Tensor& total, double max_norm, at::Tensor& out) {
   pb::clip_coef(total.data_ptr<float>(), (float)max_norm, out.data_ptr<float>(), cur_stream());
 }
 
+void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
+              int64_t B, int64_t S, int64_t nq, int64_t nkv, double scale, bool causal) {
+  CHECK_BF16(q); CHECK_BF16(k); CHECK_BF16(v); CHECK_BF16(o); CHECK_F32(lse);
+  TORCH_CHECK(q.size(0) == B * S && k.size(0) == B * S && v.size(0) == B * S, "attn: token count");
+  TORCH_CHECK(lse.numel() >= B * nq * S, "attn: lse too small");
+  const c10::cuda::CUDAGuard g(q.device());
+  pb::AttnParams p{q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(),
+                   q.stride(0), k.stride(0), v.stride(0), o.stride(0), (int)B, (int)S, (int)nq, (int)nkv,
+                   (int)(q.size(1) / nq), (float)scale, causal};
+  pb::attention_fwd(p, cur_stream());
+}
+
+void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+              const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq_acc, at::Tensor& dq,
+              at::Tensor& dk, at::Tensor& dv, int64_t B, int64_t S, int64_t nq, int64_t nkv, double scale,
+              bool causal) {
+  CHECK_BF16(q); CHECK_BF16(k); CHECK_BF16(v); CHECK_BF16(o); CHECK_BF16(dout); CHECK_BF16(dq); CHECK_BF16(dk);
+  CHECK_BF16(dv); CHECK_F32(lse); CHECK_F32(delta); CHECK_F32(dq_acc);
+  const int64_t D = q.size(1) / nq;
+  // lse / delta are read in 128-row blocks: they must be padded by 128 entries
+  TORCH_CHECK(lse.numel() >= B * nq * S + 128 && delta.numel() >= B * nq * S + 128,
+              "attn bwd: lse/delta need 128 floats of padding");
+  TORCH_CHECK(dq_acc.numel() >= B * S * nq * D, "attn bwd: dq_acc too small");
+  const c10::cuda::CUDAGuard g(q.device());
+  pb::AttnBwdParams p{};
+  p.q = q.data_ptr(); p.k = k.data_ptr(); p.v = v.data_ptr(); p.o = o.data_ptr(); p.dout = dout.data_ptr();
+  p.lse = lse.data_ptr<float>(); p.delta = delta.data_ptr<float>(); p.dq_acc = dq_acc.data_ptr<float>();
+  p.dq = dq.data_ptr(); p.dk = dk.data_ptr(); p.dv = dv.data_ptr();
+  p.ldq = q.stride(0); p.ldk = k.stride(0); p.ldv = v.stride(0); p.ldo = o.stride(0); p.lddo = dout.stride(0);
+  p.lddq = dq.stride(0); p.lddk = dk.stride(0); p.lddv = dv.stride(0);
+  p.B = (int)B; p.S = (int)S; p.nq = (int)nq; p.nkv = (int)nkv; p.D = (int)D; p.scale = (float)scale;
+  p.causal = causal;
+  pb::attention_bwd(p, cur_stream());
+}
+
 }  // namespace
 
 void register_ops(pybind11::module& m) {
@@ -194,4 +230,6 @@ void register_ops(pybind11::module& m) {
   m.def("adamw", &adamw);
   m.def("sumsq", &sumsq);
   m.def("clip_coef", &clip_coef);
+  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
 }

@@ -247,3 +247,53 @@ def test_embedding():
     ref_g = torch.zeros(V, H, device="cuda").index_add_(0, ids, dy.float())
     assert _rel_err(grad, ref_g) < 1e-5
     _check_no_device_error()
+
+
+def _attn_ref(q, k, v, B, S, nq, nkv, causal=True):
+    D = 128
+    qf = q.float().view(B, S, nq, D).transpose(1, 2)
+    kf = k.float().view(B, S, nkv, D).transpose(1, 2).repeat_interleave(nq // nkv, dim=1)
+    vf = v.float().view(B, S, nkv, D).transpose(1, 2).repeat_interleave(nq // nkv, dim=1)
+    s = qf @ kf.transpose(-1, -2) / math.sqrt(D)
+    if causal:
+        mask = torch.ones(S, S, device=q.device, dtype=torch.bool).tril()
+        s = s.masked_fill(~mask, float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    o = torch.softmax(s, dim=-1) @ vf
+    return o.transpose(1, 2).reshape(B * S, nq * D), lse.reshape(B * nq, S)
+
+
+@pytest.mark.parametrize("B,S,nq,nkv", [(1, 128, 1, 1), (2, 256, 4, 2), (1, 384, 2, 1), (2, 200, 4, 4),
+                                        (1, 1024, 8, 2)])
+def test_attention_fwd_bwd(B, S, nq, nkv):
+    C = _ext()
+    torch.manual_seed(10)
+    D = 128
+    T = B * S
+    q = torch.randn(T, nq * D, device="cuda").to(torch.bfloat16)
+    k = torch.randn(T, nkv * D, device="cuda").to(torch.bfloat16)
+    # v as a column view of a wider buffer, like the fused qkv layout
+    vbuf = torch.randn(T, (nkv + 3) * D, device="cuda").to(torch.bfloat16)
+    v = vbuf[:, 3 * D:]
+    o = torch.empty(T, nq * D, device="cuda", dtype=torch.bfloat16)
+    lse = torch.zeros(B * nq * S + 128, device="cuda")
+    C.attn_fwd(q, k, v, o, lse, B, S, nq, nkv, 1 / math.sqrt(D), True)
+    _check_no_device_error()
+    qf, kf, vf = (t.float().requires_grad_(True) for t in (q, k, v))
+    o_ref, lse_ref = _attn_ref(qf, kf, vf, B, S, nq, nkv)
+    assert _rel_err(o, o_ref) < 2e-2
+    assert (lse[: B * nq * S].view(B * nq, S) - lse_ref).abs().max().item() < 2e-2
+    if S % 8:
+        return
+    do = torch.randn(T, nq * D, device="cuda").to(torch.bfloat16)
+    o_ref.backward(do.float())
+    delta = torch.zeros(B * nq * S + 128, device="cuda")
+    dq_acc = torch.empty(T, nq * D, device="cuda")
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty(T, nkv * D, device="cuda", dtype=torch.bfloat16)
+    C.attn_bwd(q, k, v, o, do, lse, delta, dq_acc, dq, dk, dv, B, S, nq, nkv, 1 / math.sqrt(D), True)
+    _check_no_device_error()
+    assert _rel_err(dv, vf.grad) < 3e-2
+    assert _rel_err(dk, kf.grad) < 3e-2
+    assert _rel_err(dq, qf.grad) < 3e-2
