@@ -1,0 +1,348 @@
+"""ParallelEngine: forward / backward / optimizer step over MP and FSDP.
+
+Same public surface as the reference engine (parallel/parallel/engine/
+engine.py:20-324): ``forward(x, y)``, ``backward(loss)``, ``step()``,
+``reduce_loss``, ``token_loss``, ``sync_buffers``, (sharded) state dicts,
+``save/load_checkpoint``, ``save/load_full_model``, ``step_memory_stats``,
+``lr``.  Composition order is the same: model-parallel wrapper first, then
+FSDP over the model-parallel-local parameters, then AdamW over the shards.
+
+Step differences (B200-first, same math):
+* the global gradient norm, the clip coefficient and the non-finite flag are
+  computed on the device in one multi-tensor pass and handed to the fused
+  AdamW kernel (no per-parameter ``.item()`` syncs); a non-finite step
+  leaves the parameters untouched and raises ``FloatingPointError`` on the
+  next ``step()`` call (or immediately with ``sync_finite_check=True``);
+* DP-replicate gradient averaging is one all-reduce per gradient bucket.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..profiling import (collective_phase, configure_collective_profiling, finish_collective_profile_step,
+                         start_collective_profile_step, collective_profile)
+from ..state import Strategies
+from ..utils import DTYPE_DICT
+from ..ops._ext import ext
+from .checkpoint import CheckpointManager
+from .fsdp import FSDPWrapper
+from .fsdp_utils import local_tensor
+from .model_parallel import ModelParallelWrapper
+from .optim import FusedAdamW
+
+
+def _cfg_get(node, key, default):
+    try:
+        return node.get(key, default)
+    except AttributeError:
+        return getattr(node, key, default)
+
+
+class ParallelEngine:
+    def __init__(self, model, tokenizer, pconfig, cfg, device, mp_plan=None):
+        self.tokenizer = tokenizer
+        self.pconfig = pconfig
+        self.cfg = cfg
+        self.device = device
+        self.use_amp = cfg.config.use_amp
+        if self.use_amp and cfg.config.amp_dtype not in ("bf16", "fp16"):
+            raise ValueError("amp_dtype must be either 'bf16' or 'fp16' when AMP is enabled")
+        self.amp_dtype = DTYPE_DICT.get(cfg.config.amp_dtype, torch.float32)
+        self.grad_scaler = torch.amp.GradScaler(pconfig.device_type or device.type,
+                                                enabled=self.use_amp and self.amp_dtype == torch.float16)
+        eng = cfg.engine
+        self.mp_wrapper = ModelParallelWrapper(model, pconfig, device=device, plan=mp_plan,
+                                               collectives=_cfg_get(eng, "collectives", "auto"))
+        self.fsdp_wrapper = FSDPWrapper(
+            model, pconfig, cpu_offload=eng.cpu_offload, activation_checkpoint=eng.activation_checkpoint,
+            checkpoint_every_n=eng.checkpoint_every_n,
+            find_unused_parameters=_cfg_get(eng, "find_unused_parameters", False),
+            overlap_backward_reductions=_cfg_get(eng, "overlap_backward_reductions", True), device=device,
+            collectives=_cfg_get(eng, "collectives", "auto"))
+        self.fsdp_wrapper.shard_model()
+        self.mp_wrapper.attach_fsdp(self.fsdp_wrapper)
+        self.model = model
+        self.optimizer_params = self.fsdp_wrapper.get_optimizer_params()
+        self._sync_initial_state()
+        self.optimizer = FusedAdamW(self.optimizer_params, lr=cfg.model.learning_rate,
+                                    betas=(cfg.optim.adam_beta1, cfg.optim.adam_beta2),
+                                    weight_decay=cfg.optim.weight_decay,
+                                    state_dtype=_cfg_get(eng, "optimizer_state_dtype", "param"))
+        self.optimizer.zero_grad(set_to_none=True)
+        self.checkpoint = CheckpointManager(self)
+        configure_collective_profiling(enabled=_cfg_get(eng, "collective_profiling", False), device=device)
+        self.sync_finite_check = bool(_cfg_get(eng, "sync_finite_check", False))
+        self._pending_nonfinite: torch.Tensor | None = None
+        self._last_grad_norm: torch.Tensor | None = None
+        self.reset_step_memory_stats()
+
+    # ------------------------------------------------------------------ init
+    def _sync_initial_state(self):
+        """Every data-parallel replica starts from identical state."""
+        if self.pconfig.device_mesh is None:
+            return
+        for dim in (Strategies.DP_REPLICATE, Strategies.DP_SHARD):
+            group = self.pconfig.group(dim)
+            if group is None:
+                continue
+            src = dist.get_global_rank(group, 0)
+            tensors = list(self.model.buffers())
+            if not self.fsdp_wrapper.is_active:
+                tensors += list(self.model.parameters())
+            elif dim == Strategies.DP_REPLICATE:
+                tensors += self.fsdp_wrapper.get_sharded_params()
+            for t in tensors:
+                v = local_tensor(t).detach()
+                if v.device.type == self.device.type:
+                    dist.broadcast(v, src=src, group=group)
+                else:
+                    staged = v.to(self.device)
+                    dist.broadcast(staged, src=src, group=group)
+                    v.copy_(staged.to(v.device))
+
+    @property
+    def lr(self):
+        return self.optimizer.param_groups[0]["lr"]
+
+    # ------------------------------------------------------------------ memory
+    def reset_step_memory_stats(self):
+        self._forward_peak_memory_allocated = 0
+        self._backward_peak_memory_allocated = 0
+        start_collective_profile_step()
+
+    def finish_step_collective_profile(self) -> list[str]:
+        return finish_collective_profile_step()
+
+    def _reset_peak(self):
+        if self.device.type == "cuda":
+            torch.cuda.reset_peak_memory_stats(self.device)
+
+    def _peak(self) -> int:
+        return torch.cuda.max_memory_allocated(self.device) if self.device.type == "cuda" else 0
+
+    def step_memory_stats(self) -> dict[str, int]:
+        peaks = torch.tensor([self._forward_peak_memory_allocated, self._backward_peak_memory_allocated],
+                             dtype=torch.int64, device=self.device)
+        if dist.is_initialized():
+            dist.all_reduce(peaks, op=dist.ReduceOp.MAX)
+        return {"forward_peak_allocated_bytes": int(peaks[0].item()),
+                "backward_peak_allocated_bytes": int(peaks[1].item())}
+
+    # ------------------------------------------------------------------ fwd / bwd
+    def forward(self, x, y):
+        self._reset_peak()
+        with collective_phase("forward"):
+            with torch.autocast(device_type=self.device.type, dtype=self.amp_dtype,
+                                enabled=self.use_amp and self.device.type == "cuda"):
+                if self.mp_wrapper.is_active:
+                    outputs = self.model(input_ids=x)
+                    outputs.loss = self.mp_wrapper.training_loss(outputs, y)
+                else:
+                    outputs = self.model(input_ids=x, labels=y)
+        self._forward_peak_memory_allocated = max(self._forward_peak_memory_allocated, self._peak())
+        return outputs
+
+    def sync_buffers(self):
+        """Broadcast every buffer from the first replica / shard rank."""
+        if self.pconfig.device_mesh is None:
+            return
+        bufs = list(self.model.buffers())
+        for dim in (Strategies.DP_REPLICATE, Strategies.DP_SHARD):
+            group = self.pconfig.group(dim)
+            if group is None:
+                continue
+            src = dist.get_global_rank(group, 0)
+            for b in bufs:
+                dist.broadcast(b, src=src, group=group)
+
+    def backward(self, loss):
+        self._reset_peak()
+        with collective_phase("backward"):
+            self.fsdp_wrapper.prepare_backward(loss)
+            with self.mp_wrapper.backward_context():
+                if self.grad_scaler.is_enabled():
+                    self.grad_scaler.scale(loss).backward()
+                else:
+                    loss.backward()
+            self.fsdp_wrapper.finalize_backward()
+        self._backward_peak_memory_allocated = max(self._backward_peak_memory_allocated, self._peak())
+
+    # ------------------------------------------------------------------ step
+    def step(self):
+        with collective_phase("optimizer"):
+            self._step_impl()
+
+    def _check_pending_nonfinite(self):
+        if self._pending_nonfinite is not None:
+            bad = bool(self._pending_nonfinite.item())
+            self._pending_nonfinite = None
+            if bad:
+                raise FloatingPointError("Non-finite gradients encountered")
+
+    def _grad_lists(self):
+        """(grad tensors, weights) for the norm: replicated TP params count once."""
+        grads, weights = [], []
+        rep_weight = self.mp_wrapper.replicated_grad_weight()
+        for p in self.optimizer_params:
+            if p.grad is None:
+                continue
+            g = local_tensor(p.grad)
+            w = rep_weight if self.mp_wrapper.is_replicated_param(p) else 1.0
+            grads.append(g)
+            weights.append(w)
+        return grads, weights
+
+    def _norm_groups(self):
+        groups = []
+        if self.mp_wrapper.is_active:
+            g = self.pconfig.group(Strategies.TP)
+            if g is not None:
+                groups.append(g)
+        if self.fsdp_wrapper.is_active:
+            groups.append(self.fsdp_wrapper.dp_shard_group)
+        return groups
+
+    def _step_impl(self):
+        self._check_pending_nonfinite()
+        self._average_gradients()
+        if self.grad_scaler.is_enabled():
+            self.grad_scaler.unscale_(self.optimizer)
+        cuda = self.device.type == "cuda" and all(local_tensor(p).is_cuda for p in self.optimizer_params)
+        max_norm = float(self.cfg.model.clip_grad_norm)
+        if cuda and not self.grad_scaler.is_enabled():
+            grads, weights = self._grad_lists()
+            sq = torch.zeros(1, dtype=torch.float32, device=self.device)
+            flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+            by_dtype: dict = {}
+            for g, w in zip(grads, weights):
+                by_dtype.setdefault(g.dtype, ([], []))
+                by_dtype[g.dtype][0].append(g if g.is_contiguous() else g.contiguous())
+                by_dtype[g.dtype][1].append(w)
+            for gs, ws in by_dtype.values():
+                ext().sumsq(gs, ws, sq, flag)
+            for group in self._norm_groups():
+                dist.all_reduce(sq, op=dist.ReduceOp.SUM, group=group)
+            for dim in (Strategies.DP_REPLICATE, Strategies.TP, Strategies.DP_SHARD):
+                group = self.pconfig.group(dim)
+                if group is not None:
+                    dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
+            scale = None
+            if max_norm > 0.0:
+                scale = torch.empty(1, dtype=torch.float32, device=self.device)
+                ext().clip_coef(sq, max_norm, scale)
+            self._last_grad_norm = sq.sqrt()
+            self.optimizer.step(grad_scale=scale, skip=flag)
+            self.optimizer.zero_grad(set_to_none=True)
+            self.fsdp_wrapper.zero_grad()
+            if self.sync_finite_check:
+                self._pending_nonfinite = flag
+                self._check_pending_nonfinite()
+            else:
+                self._pending_nonfinite = flag
+            return
+        # generic path (CPU / fp16 scaler): reference semantics with host syncs
+        finite = self._grads_are_finite()
+        if finite and max_norm > 0.0:
+            if self.mp_wrapper.is_active:
+                self._last_grad_norm = self.mp_wrapper.clip_grad_norm_(self.optimizer_params, max_norm)
+            else:
+                self._last_grad_norm = self.fsdp_wrapper.clip_grad_norm_(max_norm)
+        if not finite:
+            if not self.grad_scaler.is_enabled():
+                self.optimizer.zero_grad(set_to_none=True)
+                self.fsdp_wrapper.zero_grad()
+                raise FloatingPointError("Non-finite gradients encountered")
+            self.grad_scaler.update(new_scale=self.grad_scaler.get_scale() / 2.0)
+        else:
+            if self.grad_scaler.is_enabled():
+                self.grad_scaler.step(self.optimizer)
+                self.grad_scaler.update()
+            else:
+                self.optimizer.step()
+        self.optimizer.zero_grad(set_to_none=True)
+        self.fsdp_wrapper.zero_grad()
+
+    def _average_gradients(self):
+        """All-reduce mean of gradients over the replicate group."""
+        if self.pconfig.dp_replicate_size <= 1 or self.pconfig.device_mesh is None:
+            return
+        group = self.pconfig.group(Strategies.DP_REPLICATE)
+        if self.fsdp_wrapper.is_active:
+            for bucket in self.fsdp_wrapper.grad_buckets():
+                with collective_profile("fsdp_all_reduce", value=bucket, mode="replicate"):
+                    dist.all_reduce(bucket, op=dist.ReduceOp.SUM, group=group)
+                bucket.div_(self.pconfig.dp_replicate_size)
+            return
+        for p in self.optimizer_params:
+            has = torch.tensor(int(p.grad is not None), dtype=torch.int32, device=self.device)
+            dist.all_reduce(has, op=dist.ReduceOp.MAX, group=group)
+            if p.grad is None:
+                p.grad = torch.zeros_like(p)
+            g = local_tensor(p.grad)
+            dist.all_reduce(g, op=dist.ReduceOp.SUM, group=group)
+            g.div_(self.pconfig.dp_replicate_size)
+            if not has.item():
+                p.grad = None
+
+    def _grads_are_finite(self) -> bool:
+        finite = torch.ones((), dtype=torch.int32, device=self.device)
+        for p in self.optimizer_params:
+            g = p.grad
+            if g is None:
+                continue
+            if not torch.isfinite(local_tensor(g)).all():
+                finite.zero_()
+                break
+        if self.pconfig.device_mesh is not None:
+            for dim in (Strategies.DP_REPLICATE, Strategies.TP, Strategies.DP_SHARD):
+                group = self.pconfig.group(dim)
+                if group is not None:
+                    dist.all_reduce(finite, op=dist.ReduceOp.MIN, group=group)
+        return bool(finite.item())
+
+    @property
+    def last_grad_norm(self):
+        return self._last_grad_norm
+
+    # ------------------------------------------------------------------ checkpoint facade
+    def state_dict(self):
+        return self.checkpoint.full_state_dict()
+
+    def load_state_dict(self, state_dict, strict: bool = True):
+        return self.checkpoint.load_full_state_dict(state_dict, strict=strict)
+
+    def sharded_state_dict(self):
+        return self.checkpoint.sharded_state_dict()
+
+    def load_sharded_state_dict(self, state_dict, strict: bool = True):
+        return self.checkpoint.load_sharded_state_dict(state_dict, strict=strict)
+
+    def save_checkpoint(self, path, *, step: int, dataloader_state=None, eval_dataloader_state=None, metadata=None):
+        return self.checkpoint.save(path, step=step, dataloader_state=dataloader_state,
+                                    eval_dataloader_state=eval_dataloader_state, metadata=metadata)
+
+    def load_checkpoint(self, path, *, strict: bool = True):
+        return self.checkpoint.load(path, strict=strict)
+
+    def save_full_model(self, path):
+        return self.checkpoint.save_full_model(path)
+
+    def load_full_model(self, path, *, strict: bool = True):
+        return self.checkpoint.load_full_model(path, strict=strict)
+
+    # ------------------------------------------------------------------ losses
+    def reduce_loss(self, loss):
+        out = loss.detach().float().clone()
+        if not self.pconfig.dp_enabled or self.pconfig.device_mesh is None:
+            return out
+        for dim in (Strategies.DP_REPLICATE, Strategies.DP_SHARD):
+            group = self.pconfig.group(dim)
+            if group is None:
+                continue
+            dist.all_reduce(out, op=dist.ReduceOp.SUM, group=group)
+            out.div_(dist.get_world_size(group))
+        return out
+
+    def token_loss(self, logits, labels, reduction: str = "mean"):
+        return self.mp_wrapper.token_loss(logits, labels, reduction=reduction)

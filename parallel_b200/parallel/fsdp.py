@@ -1,0 +1,669 @@
+"""Fully sharded data parallelism over flat per-layer units.
+
+Public surface mirrors the reference FSDPWrapper (parallel/parallel/engine/
+dp_sharded.py:22-886): ``shard_model``, ``prepare_backward``,
+``finalize_backward``, ``get_optimizer_params``, ``clip_grad_norm_``, the
+full / local-full / sharded state-dict methods and ``checkpoint_layout``
+(same dict, so exact-topology checkpoints interchange).
+
+Execution model (B200-first):
+* each decoder layer runs through one autograd Function (``_UnitFn``) that
+  gathers the unit (or waits for the side-stream prefetch), starts the next
+  prefetch, runs the layer - under ``no_grad`` when activation checkpointing
+  is on, recomputing it in backward - and, in backward, produces the unit's
+  full gradients with one ``torch.autograd.grad`` call and immediately
+  launches its reduce-scatter.  Reductions therefore leave in strict reverse
+  unit order on every rank with at most two in flight, exactly the
+  reference's schedule, without per-parameter hooks;
+* the root unit (embedding, final norm, untied LM head) is gathered at the
+  start of forward and kept until the end of backward
+  (reshard_after_forward=False), as in the reference;
+* with ``find_unused_parameters`` the reductions are issued after backward
+  in fixed order (zeros for units/parameters without a local gradient) and
+  a participation bitmap all-reduced over the shard group decides which
+  parameters receive a gradient (globally unused ones keep ``grad=None``,
+  so AdamW skips them, as in the reference).
+"""
+from __future__ import annotations
+
+import copy
+from collections import OrderedDict
+from typing import Any, Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+from torch.distributed.tensor import DTensor
+
+from ..state import Strategies
+from .comm.unit_collectives import make_unit_collectives
+from .fsdp_utils import get_fsdp_units, group_named_parameters, local_tensor
+from .param_unit import DPParamUnit
+
+
+def _sink_of(unit):
+    return getattr(unit.module, "_router_sink", None)
+
+
+def _run_layer(unit, fwd, x, args):
+    """Run the layer; returns (y, extras) where extras are the tensors the
+    layer appended to its router sink (MoE router probabilities, which feed
+    the auxiliary loss and so must stay differentiable)."""
+    sink = _sink_of(unit)
+    n0 = len(sink) if sink is not None else 0
+    y = fwd(x, *args)
+    extras = []
+    if sink is not None and len(sink) > n0:
+        extras = list(sink[n0:])
+        del sink[n0:]
+    return y, extras
+
+
+class _UnitFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, wrapper, unit, fwd, nargs, x, *args):
+        unit.all_gather()
+        if unit.next_fwd is not None:
+            unit.next_fwd.prefetch()
+        if unit.use_activation_checkpoint:
+            with torch.no_grad():
+                y, extras = _run_layer(unit, fwd, x, args)
+            ctx.save_for_backward(x)
+            ctx.inner = None
+        else:
+            xi = x.detach().requires_grad_(True)
+            with torch.enable_grad():
+                y, extras = _run_layer(unit, fwd, xi, args)
+            ctx.inner = (xi, y, extras)
+            y = y.detach()
+            extras = [e.detach() for e in extras]
+        if unit.reshard_after_forward:
+            unit.free_full_params()
+        ctx.wrapper, ctx.unit, ctx.fwd, ctx.args = wrapper, unit, fwd, args
+        ctx.n_extra = len(extras)
+        return (y, *extras)
+
+    @staticmethod
+    def backward(ctx, gy, *gextras):
+        wrapper, unit = ctx.wrapper, ctx.unit
+        unit.all_gather()
+        if unit.next_bwd is not None:
+            unit.next_bwd.prefetch()
+        if ctx.inner is None:
+            (x,) = ctx.saved_tensors
+            xi = x.detach().requires_grad_(True)
+            with torch.enable_grad():
+                y, extras = _run_layer(unit, ctx.fwd, xi, ctx.args)
+        else:
+            xi, y, extras = ctx.inner
+        ctx.inner = None
+        outs, gouts = [y], [gy]
+        for e, g in zip(extras, gextras):
+            if g is not None and e.requires_grad:
+                outs.append(e)
+                gouts.append(g)
+        params = unit.parameters if unit.requires_grad else []
+        grads = torch.autograd.grad(outs, [xi] + params, gouts, allow_unused=True)
+        del y, extras, outs
+        if unit.requires_grad:
+            wrapper._unit_backward_done(unit, list(grads[1:]))
+        else:
+            unit.free_full_params()
+        return (None, None, None, None, grads[0]) + (None,) * len(ctx.args)
+
+
+class FSDPWrapper:
+    """FSDP over ``model.model.layers`` plus a root unit (see module docstring)."""
+
+    def __init__(self, model: nn.Module, pconfig, cpu_offload: bool = False, activation_checkpoint: bool = False,
+                 checkpoint_every_n: int = 1, find_unused_parameters: bool = False,
+                 overlap_backward_reductions: bool = True, device: Optional[torch.device] = None,
+                 collectives: str = "auto"):
+        self.model = model
+        self.pconfig = pconfig
+        self.cpu_offload = cpu_offload
+        self.activation_checkpoint = activation_checkpoint
+        self.checkpoint_every_n = max(checkpoint_every_n, 1)
+        self.find_unused_parameters = find_unused_parameters
+        self.overlap_backward_reductions = overlap_backward_reductions
+        first = next(model.parameters(), None)
+        self.device = device or (first.device if first is not None else torch.device("cpu"))
+        self.collectives_kind = collectives
+        self.units: list[DPParamUnit] = []
+        self.root_units: list[DPParamUnit] = []
+        self.dp_shard_group = None
+        self.dp_shard_mesh = None
+        self._inflight: list[DPParamUnit] = []
+        self._max_inflight = 2
+        self._backward_prepared = False
+        self._done_units: set[int] = set()
+        self._deferred: dict[int, list] = {}
+        self._state_dict_keys: tuple[str, ...] = ()
+        self._parameter_state_names: dict[int, tuple[str, ...]] = {}
+        self._parameter_state_keys: set[str] = set()
+        self._orig_forwards: dict[int, Any] = {}
+        self._root_hook = None
+        self.coll = None
+
+    # ------------------------------------------------------------------ layout
+    def _capture_state_dict_layout(self) -> None:
+        state = self.model.state_dict(keep_vars=True)
+        ids = {id(p) for p in self.model.parameters()}
+        names: dict[int, list[str]] = {i: [] for i in ids}
+        for name, value in state.items():
+            if id(value) in names:
+                names[id(value)].append(name)
+        missing = [n for n, p in self.model.named_parameters() if not names[id(p)]]
+        if missing:
+            raise RuntimeError(f"Every model parameter must be represented in model.state_dict(); missing: {missing}")
+        self._state_dict_keys = tuple(state.keys())
+        self._parameter_state_names = {i: tuple(v) for i, v in names.items()}
+        self._parameter_state_keys = {n for v in self._parameter_state_names.values() for n in v}
+
+    # ------------------------------------------------------------------ sharding
+    def shard_model(self):
+        self._capture_state_dict_layout()
+        if self.pconfig.dp_shard_size <= 1 or self.pconfig.device_mesh is None:
+            return
+        if self.units:
+            raise RuntimeError("FSDPWrapper.shard_model() can only be called once")
+        self.dp_shard_mesh = self.pconfig.device_mesh[Strategies.DP_SHARD.value]
+        self.dp_shard_group = self.dp_shard_mesh.get_group()
+        self.coll = make_unit_collectives(self.collectives_kind, self.device, self.dp_shard_group)
+        for buf in self.model.buffers():
+            buf.data = buf.data.to(self.device)
+        layers = get_fsdp_units(self.model)
+        specs = []
+        owned: set[int] = set()
+        for i, sub in enumerate(layers):
+            named = [(self._parameter_state_names[id(p)][0], p) for _, p in sub.named_parameters()]
+            if owned.intersection(id(p) for _, p in named):
+                raise ValueError("A parameter is shared by multiple FSDP units")
+            if not named:
+                continue
+            owned.update(id(p) for _, p in named)
+            ckpt = self.activation_checkpoint and (i % self.checkpoint_every_n == 0)
+            for gi, group in enumerate(group_named_parameters(named)):
+                specs.append((sub, group, ckpt and gi == 0, sub is not self.model, gi == 0))
+        root_specs = []
+        if layers != [self.model]:
+            root = [(self._parameter_state_names[id(p)][0], p) for _, p in self.model.named_parameters()
+                    if id(p) not in owned]
+            if root:
+                root_specs = [(self.model, g, False, False, False) for g in group_named_parameters(root)]
+                owned.update(id(p) for _, p in root)
+        if owned != {id(p) for p in self.model.parameters()}:
+            raise RuntimeError("Every model parameter must belong to exactly one FSDP unit")
+        all_specs = root_specs + specs
+        for i, (sub, named, ckpt, reshard, primary) in enumerate(all_specs):
+            unit = DPParamUnit(sub, self.dp_shard_mesh, i, self.coll, cpu_offload=self.cpu_offload,
+                               use_activation_checkpoint=ckpt, device=self.device, named_parameters=named,
+                               reshard_after_forward=reshard,
+                               overlap_backward_reductions=self.overlap_backward_reductions)
+            unit.shard()
+            unit._layer_primary = primary
+            self.units.append(unit)
+        self.root_units = [u for u in self.units if u.module is self.model]
+        for i, unit in enumerate(self.units):
+            unit.next_fwd = self.units[i + 1] if i + 1 < len(self.units) else None
+            unit.next_bwd = self.units[i - 1] if i > 0 else None
+        # route every layer's forward through the unit function
+        layer_units: dict[int, list[DPParamUnit]] = {}
+        for u in self.units:
+            if u.module is not self.model:
+                layer_units.setdefault(id(u.module), []).append(u)
+        for sub in layers:
+            us = layer_units.get(id(sub))
+            if not us:
+                continue
+            if len(us) != 1:
+                raise NotImplementedError("Layers mixing parameter dtypes / frozen parameters are not supported")
+            self._wrap_layer(sub, us[0])
+        self._root_hook = self.model.register_forward_pre_hook(self._root_pre_forward)
+
+    def _wrap_layer(self, layer: nn.Module, unit: DPParamUnit) -> None:
+        orig = layer.forward
+        self._orig_forwards[id(layer)] = orig
+        wrapper = self
+
+        def forward(x, *args):
+            if not torch.is_grad_enabled():
+                unit.all_gather()
+                if unit.next_fwd is not None:
+                    unit.next_fwd.prefetch()
+                out = orig(x, *args)
+                if unit.reshard_after_forward:
+                    unit.free_full_params()
+                return out
+            y, *extras = _UnitFn.apply(wrapper, unit, orig, len(args), x, *args)
+            sink = _sink_of(unit)
+            if sink is not None:
+                sink.extend(extras)
+            return y
+
+        layer.forward = forward
+
+    def _root_pre_forward(self, module, args):
+        for u in self.root_units:
+            u.all_gather()
+        nxt = self.root_units[-1].next_fwd if self.root_units else None
+        if nxt is not None:
+            nxt.prefetch()
+        return None
+
+    # ------------------------------------------------------------------ backward
+    def prepare_backward(self, loss: torch.Tensor):
+        if not self.is_active:
+            return
+        if not isinstance(loss, torch.Tensor):
+            raise TypeError("FSDPWrapper.prepare_backward() requires a loss tensor")
+        if self._backward_prepared:
+            raise RuntimeError("FSDP backward is already prepared")
+        self._done_units.clear()
+        self._deferred.clear()
+        self._backward_prepared = True
+
+    def _unit_backward_done(self, unit: DPParamUnit, grads: list) -> None:
+        if not self._backward_prepared:
+            raise RuntimeError("FSDP unit became ready before prepare_backward()")
+        self._done_units.add(unit.unit_index)
+        missing = [m.name for m, g in zip(unit.param_metas, grads) if g is None]
+        if missing and not self.find_unused_parameters:
+            raise RuntimeError(
+                f"FSDP backward ended before every expected parameter gradient was accumulated: "
+                f"[{{'unit': {unit.unit_index}, 'missing_gradients': {missing}}}]")
+        if self.overlap_backward_reductions and not self.find_unused_parameters:
+            self._launch(unit, grads)
+        else:
+            self._deferred[unit.unit_index] = grads
+        unit.free_full_params()
+
+    def _launch(self, unit: DPParamUnit, grads: list) -> None:
+        while len(self._inflight) >= self._max_inflight:
+            self._inflight.pop(0).finish_gradient_reduction()
+        unit.reduce_gradients(grads)
+        self._inflight.append(unit)
+
+    def finalize_backward(self):
+        if not self.is_active:
+            return
+        if not self._backward_prepared:
+            raise RuntimeError("FSDP backward was not prepared before finalization")
+        # root units: gradients arrived through autograd on the full params
+        for u in self.root_units:
+            grads = [m.parameter.grad for m in u.param_metas]
+            for m in u.param_metas:
+                m.parameter.grad = None
+            if any(g is None for g in grads) and not self.find_unused_parameters and u.requires_grad:
+                missing = [m.name for m, g in zip(u.param_metas, grads) if g is None]
+                raise RuntimeError(
+                    f"FSDP backward ended before every expected parameter gradient was accumulated: "
+                    f"[{{'unit': {u.unit_index}, 'missing_gradients': {missing}}}]")
+            if u.requires_grad:
+                self._done_units.add(u.unit_index)
+                if self.overlap_backward_reductions and not self.find_unused_parameters:
+                    self._launch(u, grads)
+                else:
+                    self._deferred[u.unit_index] = grads
+        trainable = [u for u in self.units if u.requires_grad]
+        if not self.find_unused_parameters:
+            pending = [u.unit_index for u in trainable if u.unit_index not in self._done_units]
+            if pending:
+                raise RuntimeError(f"FSDP backward ended before every expected parameter gradient was "
+                                   f"accumulated: units {pending} never ran backward")
+            if not self.overlap_backward_reductions:
+                for u in reversed(trainable):
+                    self._launch(u, self._deferred.pop(u.unit_index))
+        else:
+            # fixed reverse order on every rank; zeros where nothing ran locally
+            for u in reversed(trainable):
+                grads = self._deferred.pop(u.unit_index, [None] * len(u.param_metas))
+                self._launch(u, grads)
+        for u in self._inflight:
+            u.finish_gradient_reduction()
+        self._inflight.clear()
+        participation = None
+        if self.find_unused_parameters:
+            bits = torch.tensor([int(p) for u in trainable for p in u._participation], dtype=torch.int32,
+                                device=self.device)
+            if bits.numel():
+                dist.all_reduce(bits, op=dist.ReduceOp.SUM, group=self.dp_shard_group)
+            flags = bits.gt(0).tolist()
+            participation, k = {}, 0
+            for u in trainable:
+                participation[u.unit_index] = flags[k:k + len(u.param_metas)]
+                k += len(u.param_metas)
+        for u in trainable:
+            u.attach_gradients(None if participation is None else participation[u.unit_index])
+        for u in self.units:
+            u.free_full_params()
+        self._backward_prepared = False
+        self._done_units.clear()
+
+    def zero_grad(self) -> None:
+        for u in self.units:
+            u.zero_grad()
+
+    # ------------------------------------------------------------------ params
+    def get_optimizer_params(self) -> list[nn.Parameter]:
+        if not self.units:
+            return [p for p in self.model.parameters() if p.requires_grad]
+        return [m.sharded_param for u in self.units if u.requires_grad for m in u.param_metas]
+
+    def get_sharded_params(self) -> list[nn.Parameter]:
+        return [m.sharded_param for u in self.units for m in u.param_metas]
+
+    def grad_buckets(self) -> list[torch.Tensor]:
+        """Reduced gradient shard buckets (one flat tensor per unit)."""
+        return [u.grad_shards() for u in self.units if u.requires_grad and u.grad_shards() is not None]
+
+    def clip_grad_norm_(self, max_norm: float) -> torch.Tensor:
+        """Clip by one norm shared by the shard group (no host synchronisation)."""
+        params = self.get_optimizer_params()
+        if not self.is_active:
+            return torch.nn.utils.clip_grad_norm_(params, max_norm)
+        sq = torch.zeros((), dtype=torch.float32, device=self.device)
+        for p in params:
+            if p.grad is not None:
+                sq += local_tensor(p.grad).detach().float().pow(2).sum().to(self.device)
+        dist.all_reduce(sq, op=dist.ReduceOp.SUM, group=self.dp_shard_group)
+        total = sq.sqrt()
+        coef = (max_norm / (total + 1e-6)).clamp(max=1.0)
+        for p in params:
+            if p.grad is not None:
+                g = local_tensor(p.grad)
+                g.mul_(coef.to(g.device, g.dtype))
+        return total
+
+    # ------------------------------------------------------------------ state dicts
+    @staticmethod
+    def _cpu_copy(v: Any) -> Any:
+        if isinstance(v, DTensor):
+            return v._local_tensor.detach().to(device="cpu", copy=True)
+        if isinstance(v, torch.Tensor):
+            return v.detach().to(device="cpu", copy=True)
+        return copy.deepcopy(v)
+
+    def _replicate_rank(self) -> int:
+        mesh = self.pconfig.device_mesh
+        if mesh is not None and Strategies.DP_REPLICATE.value in (mesh.mesh_dim_names or ()):
+            return mesh.get_local_rank(Strategies.DP_REPLICATE.value)
+        return 0
+
+    def _is_checkpoint_replica(self) -> bool:
+        return self._replicate_rank() == 0
+
+    def _full_state_root(self) -> bool:
+        if not self._is_checkpoint_replica():
+            return False
+        if self.is_active:
+            return dist.get_rank(self.dp_shard_group) == 0
+        return not dist.is_initialized() or dist.get_rank() == 0
+
+    def _non_parameter_state_dict(self) -> OrderedDict:
+        cur = self.model.state_dict(keep_vars=True)
+        out = OrderedDict((n, self._cpu_copy(v)) for n, v in cur.items() if n not in self._parameter_state_keys)
+        if hasattr(cur, "_metadata"):
+            out._metadata = copy.deepcopy(cur._metadata)
+        return out
+
+    def _copy_non_parameter_state(self, sd) -> None:
+        cur = self.model.state_dict(keep_vars=True)
+        for name, dst in cur.items():
+            if name in self._parameter_state_keys or name not in sd:
+                continue
+            if isinstance(dst, torch.Tensor):
+                dst.detach().copy_(sd[name])
+
+    def _sync_tensor(self, t: torch.Tensor, group) -> None:
+        src = dist.get_global_rank(group, 0)
+        v = local_tensor(t).detach()
+        if v.device.type == self.device.type:
+            dist.broadcast(v, src=src, group=group)
+            return
+        staged = v.to(self.device)
+        dist.broadcast(staged, src=src, group=group)
+        v.copy_(staged.to(v.device))
+
+    def _sync_replicated_state(self) -> None:
+        group = self.pconfig.group(Strategies.DP_REPLICATE)
+        if group is None:
+            return
+        tensors = list(self.model.buffers())
+        tensors += self.get_sharded_params() if self.is_active else list(self.model.parameters())
+        for t in tensors:
+            self._sync_tensor(t, group)
+
+    def full_state_dict(self) -> Optional[OrderedDict]:
+        """Full CPU state dict on the shard-group root (one unit gathered at a time)."""
+        if not self._state_dict_keys:
+            self._capture_state_dict_layout()
+        if not self._is_checkpoint_replica():
+            return None
+        if not self.is_active:
+            if not self._full_state_root():
+                return None
+            ms = self.model.state_dict(keep_vars=True)
+            out = OrderedDict((n, self._cpu_copy(v)) for n, v in ms.items())
+            if hasattr(ms, "_metadata"):
+                out._metadata = copy.deepcopy(ms._metadata)
+            return out
+        root = self._full_state_root()
+        values: dict[str, torch.Tensor] = {}
+        for u in self.units:
+            was = u.gathered
+            u.all_gather()
+            try:
+                if root:
+                    for m in u.param_metas:
+                        cpu = self._cpu_copy(m.parameter)
+                        for n in self._parameter_state_names[id(m.parameter)]:
+                            values[n] = cpu
+            finally:
+                if not was:
+                    u.free_full_params()
+        if not root:
+            return None
+        nps = self._non_parameter_state_dict()
+        out = OrderedDict((n, values[n] if n in values else nps[n]) for n in self._state_dict_keys)
+        if hasattr(nps, "_metadata"):
+            out._metadata = copy.deepcopy(nps._metadata)
+        return out
+
+    def _validate_full_state_dict(self, sd, strict: bool) -> dict:
+        expected = set(self._state_dict_keys)
+        actual = set(sd.keys())
+        missing = [n for n in self._state_dict_keys if n not in actual]
+        unexpected = [n for n in sd if n not in expected]
+        shapes: dict[str, torch.Size] = {}
+        for u in self.units:
+            for m in u.param_metas:
+                for n in self._parameter_state_names[id(m.parameter)]:
+                    shapes[n] = m.shape
+        for n, v in self.model.state_dict(keep_vars=True).items():
+            if isinstance(v, torch.Tensor) and n not in shapes:
+                shapes[n] = v.shape
+        errors = []
+        if strict and missing:
+            errors.append(f"Missing key(s): {missing}")
+        if strict and unexpected:
+            errors.append(f"Unexpected key(s): {unexpected}")
+        for n in expected & actual:
+            v = sd[n]
+            if n in shapes:
+                if not isinstance(v, torch.Tensor):
+                    errors.append(f"Expected tensor for {n}, got {type(v).__name__}")
+                elif v.shape != shapes[n]:
+                    errors.append(f"Shape mismatch for {n}: expected {tuple(shapes[n])}, got {tuple(v.shape)}")
+        return {"error": "; ".join(errors) if errors else None, "missing": missing, "unexpected": unexpected}
+
+    def _load_units_from(self, sd, is_group_root: bool, group_root: int) -> None:
+        for u in self.units:
+            was = u.gathered
+            u.all_gather()
+            try:
+                if is_group_root:
+                    by_name = {n: m for m in u.param_metas for n in self._parameter_state_names[id(m.parameter)]}
+                    for n in self._state_dict_keys:
+                        if n in by_name and n in sd:
+                            by_name[n].parameter.detach().copy_(sd[n])
+                dist.broadcast(u.full_buffer, src=group_root, group=self.dp_shard_group)
+                u.writeback_shards()
+            finally:
+                if not was:
+                    u.free_full_params()
+
+    def load_full_state_dict(self, state_dict, strict: bool = True):
+        if not self._state_dict_keys:
+            self._capture_state_dict_layout()
+        root = not dist.is_initialized() or dist.get_rank() == 0
+        if root:
+            validation = ({"error": "Global rank zero requires a full state dict", "missing": [], "unexpected": []}
+                          if state_dict is None else self._validate_full_state_dict(state_dict, strict))
+        else:
+            validation = None
+        if dist.is_initialized():
+            payload = [validation]
+            dist.broadcast_object_list(payload, src=0)
+            validation = payload[0]
+        if validation["error"] is not None:
+            raise RuntimeError(f"Error(s) in loading state_dict: {validation['error']}")
+        if self._is_checkpoint_replica():
+            if not self.is_active:
+                if self._full_state_root():
+                    self.model.load_state_dict(state_dict, strict=strict)
+            else:
+                gr = dist.get_global_rank(self.dp_shard_group, 0)
+                is_root = self._full_state_root()
+                self._load_units_from(state_dict, is_root, gr)
+                if is_root:
+                    self._copy_non_parameter_state(state_dict)
+                for b in self.model.buffers():
+                    self._sync_tensor(b, self.dp_shard_group)
+        self._sync_replicated_state()
+        return nn.modules.module._IncompatibleKeys(validation["missing"], validation["unexpected"])
+
+    def load_local_full_state_dict(self, state_dict, strict: bool = True):
+        """Load one full model-parallel-local state dict through the shard group."""
+        if not self.is_active:
+            return self.load_full_state_dict(state_dict, strict=strict)
+        if not self._state_dict_keys:
+            self._capture_state_dict_layout()
+        gr = dist.get_global_rank(self.dp_shard_group, 0)
+        is_root = dist.get_rank(self.dp_shard_group) == 0
+        if self._is_checkpoint_replica():
+            validation = self._validate_full_state_dict(state_dict, strict) if is_root else None
+            payload = [validation]
+            dist.broadcast_object_list(payload, src=gr, group=self.dp_shard_group)
+            validation = payload[0]
+            if validation["error"] is not None:
+                raise RuntimeError(f"Error(s) in loading local state_dict: {validation['error']}")
+            self._load_units_from(state_dict, is_root, gr)
+            if is_root:
+                self._copy_non_parameter_state(state_dict)
+            for b in self.model.buffers():
+                self._sync_tensor(b, self.dp_shard_group)
+        else:
+            validation = {"missing": [], "unexpected": []}
+        self._sync_replicated_state()
+        return nn.modules.module._IncompatibleKeys(validation["missing"], validation["unexpected"])
+
+    def checkpoint_layout(self) -> dict[str, Any]:
+        return {
+            "state_dict_keys": list(self._state_dict_keys),
+            "units": [
+                {
+                    "unit_index": u.unit_index,
+                    "parameters": [
+                        {
+                            "names": list(self._parameter_state_names[id(m.parameter)]),
+                            "shape": list(m.shape),
+                            "stride": list(m.stride),
+                            "numel": m.numel,
+                            "local_shape": list(m.sharded_param._local_tensor.shape),
+                            "placements": [str(pl) for pl in m.sharded_param.placements],
+                            "dtype": str(m.parameter.dtype),
+                            "requires_grad": m.parameter.requires_grad,
+                        }
+                        for m in u.param_metas
+                    ],
+                }
+                for u in self.units
+            ],
+        }
+
+    def sharded_state_dict(self) -> dict[str, Any]:
+        if not self._state_dict_keys:
+            self._capture_state_dict_layout()
+        if not self.is_active:
+            return {"layout": self.checkpoint_layout(), "full_state": self.full_state_dict()}
+        return {"layout": self.checkpoint_layout(),
+                "shards": [self._cpu_copy(p) for p in self.get_sharded_params()],
+                "non_parameter_state": self._non_parameter_state_dict()}
+
+    def load_sharded_state_dict(self, state_dict, strict: bool = True):
+        if not self._state_dict_keys:
+            self._capture_state_dict_layout()
+        if not isinstance(state_dict, dict):
+            raise TypeError("Sharded checkpoint state must be a dictionary")
+        if state_dict.get("layout") != self.checkpoint_layout():
+            raise RuntimeError("Sharded checkpoint layout does not match the current model")
+        if not self.is_active:
+            return self.model.load_state_dict(state_dict["full_state"], strict=strict)
+        shards = state_dict.get("shards", [])
+        params = self.get_sharded_params()
+        if len(shards) != len(params):
+            raise RuntimeError(f"Expected {len(params)} parameter shards, found {len(shards)}")
+        for i, (p, s) in enumerate(zip(params, shards)):
+            if not isinstance(s, torch.Tensor):
+                raise RuntimeError(f"Invalid parameter shard {i}: expected a tensor")
+            loc = p._local_tensor
+            if s.shape != loc.shape or s.dtype != loc.dtype:
+                raise RuntimeError(f"Invalid parameter shard {i}: expected shape/dtype {tuple(loc.shape)}/"
+                                   f"{loc.dtype}, got {tuple(s.shape)}/{s.dtype}")
+        nps = state_dict.get("non_parameter_state", {})
+        if not isinstance(nps, dict):
+            raise TypeError("Checkpoint non-parameter state must be a dictionary")
+        cur = self.model.state_dict(keep_vars=True)
+        expected = [n for n in cur if n not in self._parameter_state_keys]
+        missing = [n for n in expected if n not in nps]
+        unexpected = [n for n in nps if n not in set(expected)]
+        errors = []
+        if strict and missing:
+            errors.append(f"Missing non-parameter key(s): {missing}")
+        if strict and unexpected:
+            errors.append(f"Unexpected non-parameter key(s): {unexpected}")
+        for n in set(expected) & set(nps):
+            dst, src = cur[n], nps[n]
+            if isinstance(dst, torch.Tensor):
+                if not isinstance(src, torch.Tensor):
+                    errors.append(f"Expected tensor for non-parameter state {n}, got {type(src).__name__}")
+                elif src.shape != dst.shape or src.dtype != dst.dtype:
+                    errors.append(f"Invalid non-parameter state for {n}: expected shape/dtype "
+                                  f"{tuple(dst.shape)}/{dst.dtype}, got {tuple(src.shape)}/{src.dtype}")
+        if errors:
+            raise RuntimeError("; ".join(errors))
+        for p, s in zip(params, shards):
+            p._local_tensor.detach().copy_(s)
+        self._copy_non_parameter_state(nps)
+        return nn.modules.module._IncompatibleKeys(missing, unexpected)
+
+    def state_dict(self):
+        return self.full_state_dict()
+
+    def load_state_dict(self, state_dict, strict: bool = True):
+        return self.load_full_state_dict(state_dict, strict=strict)
+
+    @property
+    def is_active(self) -> bool:
+        return len(self.units) > 0
+
+    def remove_hooks(self):
+        for u in self.units:
+            u.all_gather()
+        for layer in get_fsdp_units(self.model):
+            if id(layer) in self._orig_forwards:
+                layer.forward = self._orig_forwards.pop(id(layer))
+        if self._root_hook is not None:
+            self._root_hook.remove()
+            self._root_hook = None

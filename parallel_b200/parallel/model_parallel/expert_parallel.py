@@ -1,0 +1,162 @@
+"""Expert parallelism folded onto the TP ranks.
+
+* ``ExpertPartition``: contiguous ownership ``owner = e // local_count`` and
+  route localisation (non-local routes get the sentinel index
+  ``local_count`` and score 0).
+* ``ReplicatedTokenExpertParallel`` (no SP): every rank routes all tokens,
+  runs its local experts, and the expert output is all-reduced (forward);
+  hidden-state and score gradients are all-reduced in backward.
+* ``SequenceParallelExpertParallel`` (SP): each rank's local tokens are
+  dispatched to the expert owners with variable all-to-alls and combined
+  back.
+
+Semantics: parallel/parallel/engine/model_parallel/expert_parallel.py.  The
+runtimes are callables the MoE block invokes as
+``runtime(experts, x, global_index, weights)``.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from ...profiling import collective_profile
+from .token_dispatch import TokenDispatcher
+
+
+@dataclass(frozen=True)
+class ExpertPartition:
+    num_experts: int
+    ep_size: int
+    ep_rank: int
+
+    def __post_init__(self):
+        if self.ep_size < 1:
+            raise ValueError("ep_size must be positive")
+        if not 0 <= self.ep_rank < self.ep_size:
+            raise ValueError("ep_rank is outside the expert-parallel group")
+        if self.num_experts % self.ep_size:
+            raise ValueError(f"num_experts ({self.num_experts}) must be divisible by ep_size ({self.ep_size})")
+
+    @property
+    def local_count(self) -> int:
+        return self.num_experts // self.ep_size
+
+    @property
+    def start(self) -> int:
+        return self.ep_rank * self.local_count
+
+    @property
+    def stop(self) -> int:
+        return self.start + self.local_count
+
+    @property
+    def global_experts(self) -> range:
+        return range(self.start, self.stop)
+
+    def owner(self, global_expert: torch.Tensor) -> torch.Tensor:
+        return torch.div(global_expert, self.local_count, rounding_mode="floor")
+
+    def localize_routes(self, global_indices: torch.Tensor, scores: torch.Tensor):
+        if global_indices.shape != scores.shape:
+            raise ValueError("Expert indices and scores must have the same shape")
+        local_mask = self.owner(global_indices) == self.ep_rank
+        local_idx = (global_indices - self.start).masked_fill(~local_mask, self.local_count)
+        return local_idx, scores.masked_fill(~local_mask, 0), local_mask
+
+
+def local_expert_range(num_experts: int, ep_size: int, ep_rank: int) -> range:
+    return ExpertPartition(num_experts, ep_size, ep_rank).global_experts
+
+
+def verify_expert_modules(model, partition: ExpertPartition) -> None:
+    mods = [(n, m) for n, m in model.named_modules() if n.endswith(".mlp.experts") and hasattr(m, "num_experts")]
+    if not mods:
+        raise RuntimeError("Expert-parallel plan found no expert modules")
+    bad = [f"{n}={m.num_experts}" for n, m in mods if m.num_experts != partition.local_count]
+    if bad:
+        raise RuntimeError(f"Expected {partition.local_count} local experts per rank, got " + ", ".join(bad))
+
+
+class _AllReduceBackward(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, value, group):
+        ctx.group = group
+        return value
+
+    @staticmethod
+    def backward(ctx, g):
+        g = g.contiguous().clone()
+        with collective_profile("ep_all_reduce", value=g, mode="replicated_token_grad", detail="expert_boundary"):
+            dist.all_reduce(g, op=dist.ReduceOp.SUM, group=ctx.group)
+        return g, None
+
+
+class _AllReduceForward(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, value, group):
+        out = value.contiguous().clone()
+        with collective_profile("ep_all_reduce", value=out, mode="replicated_token_output", detail="expert_boundary"):
+            dist.all_reduce(out, op=dist.ReduceOp.SUM, group=group)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        return g, None
+
+
+class ReplicatedTokenExpertParallel:
+    def __init__(self, partition: ExpertPartition, group):
+        self.partition = partition
+        self.group = group
+        self._model = None
+
+    def __call__(self, experts, x2, global_index, weights):
+        # localise after the backward all-reduce boundary (see reference note)
+        weights = _AllReduceBackward.apply(weights, self.group)
+        local_idx, local_w, _ = self.partition.localize_routes(global_index, weights)
+        h = _AllReduceBackward.apply(x2, self.group)
+        y = experts(h, local_idx, local_w)
+        return _AllReduceForward.apply(y, self.group)
+
+    def apply(self, model) -> None:
+        if self._model is not None:
+            raise RuntimeError("Expert parallel hooks are already installed")
+        ctx = model.ctx
+        ctx.expert_runtime = self
+        model.set_parallel_context(ctx)
+        self._model = model
+
+    def close(self) -> None:
+        if self._model is not None:
+            self._model.ctx.expert_runtime = None
+            self._model.set_parallel_context(self._model.ctx)
+            self._model = None
+
+
+class SequenceParallelExpertParallel:
+    def __init__(self, partition: ExpertPartition, group):
+        self.partition = partition
+        self.group = group
+        self.dispatcher = TokenDispatcher(partition, group)
+        self._model = None
+
+    def __call__(self, experts, x2, global_index, weights):
+        hidden, idx, w, state = self.dispatcher.dispatch(x2, global_index, weights)
+        y = experts(hidden, idx, w)
+        return self.dispatcher.combine(y, state)
+
+    def apply(self, model) -> None:
+        if self._model is not None:
+            raise RuntimeError("Expert parallel hooks are already installed")
+        ctx = model.ctx
+        ctx.expert_runtime = self
+        model.set_parallel_context(ctx)
+        self._model = model
+
+    def close(self) -> None:
+        if self._model is not None:
+            self._model.ctx.expert_runtime = None
+            self._model.set_parallel_context(self._model.ctx)
+            self._model = None
