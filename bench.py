@@ -262,20 +262,20 @@ def _install_omegaconf_stub():
     if "omegaconf" in sys.modules:
         return
     sys.path.insert(0, ROOT)
-    from parallel_b200.config import Config, from_dotlist, load_yaml, merge
+    from parallel_b200 import config as pbc
 
     mod = types.ModuleType("omegaconf")
 
     class OmegaConf:
-        load = staticmethod(load_yaml)
-        merge = staticmethod(lambda *cs: merge(*cs) if len(cs) == 2 else merge(cs[0], cs[1]))
-        from_dotlist = staticmethod(from_dotlist)
+        load = staticmethod(pbc.load_yaml)
+        merge = staticmethod(pbc.merge)
+        from_dotlist = staticmethod(pbc.from_dotlist)
 
         @staticmethod
         def to_container(c, resolve=True):
             return c.to_container()
 
-    mod.DictConfig = Config
+    mod.DictConfig = pbc.Config
     mod.OmegaConf = OmegaConf
     sys.modules["omegaconf"] = mod
 
