@@ -20,6 +20,9 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <cstdio>
+#include <exception>
+#include <mutex>
 
 #include "attention.cuh"
 #include "host_util.h"
@@ -430,3 +433,175 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
 }
 
 }  // namespace pb
+
+// ===========================================================================
+// Allocation-free entry point: pb_attention_bwd_noalloc
+//
+// This entry point has no counterpart in the reference.  It exists for callers
+// that cannot allocate device memory on their own: code running inside a
+// captured or externally owned stream with a fixed memory budget, plugins of
+// other runtimes that forbid cudaMalloc after start-up, and allocation-free
+// serving paths.  It computes the same dq / dk / dv as attention_bwd() (the
+// launcher above, used by the Python bindings) but keeps every scratch buffer
+// (the per-row delta, a padded copy of lse, the fp32 dq accumulator and the
+// kernel's error word) in one file-scope __device__ array of fixed size,
+// kNoAllocScratchBytes (8.5 MiB).  Every GPU that loads this library holds
+// that array until the process exits.
+//
+//  * The caller passes inputs (q, k, v, o, dout, lse) and outputs (dq, dk, dv)
+//    with the same layouts as attention_bwd(); lse needs no padding here.
+//  * Problems whose scratch would exceed the array are rejected: the function
+//    returns kNoAllocTooLarge and launches nothing.
+//  * No cudaMalloc / cudaFree or allocating library routine is called.  The
+//    first call on each device looks up the array's device address with
+//    cudaGetSymbolAddress while that device is current and caches it; make
+//    that first call outside any stream capture.
+//  * All calls share the array and it keeps the last call's contents; the
+//    parts that must start at zero are cleared on the caller's stream by each
+//    call.  Calls that overlap on the GPU (different streams without ordering,
+//    or different host threads on the same device) race on the array.
+// ===========================================================================
+namespace pb {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = (size_t)(8u << 20) + (256u << 10);
+static __device__ __align__(256) unsigned char g_attn_bwd_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocOk = 0;
+constexpr int kNoAllocTooLarge = 1;
+constexpr int kNoAllocBadArgs = 2;
+constexpr int kNoAllocCudaError = 3;
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_base[kMaxDevices] = {nullptr};
+bool g_noalloc_attr[kMaxDevices] = {false};
+thread_local char g_noalloc_msg[256] = "";
+
+void noalloc_set_msg(const char* m) {
+  snprintf(g_noalloc_msg, sizeof(g_noalloc_msg), "%s", m);
+}
+
+size_t round256(size_t n) { return (n + 255) & ~size_t(255); }
+
+}  // namespace
+}  // namespace pb
+
+extern "C" __attribute__((visibility("default"))) const char* pb_attention_bwd_noalloc_last_error() {
+  return pb::g_noalloc_msg;
+}
+
+extern "C" __attribute__((visibility("default"))) size_t pb_attention_bwd_noalloc_scratch_bytes() {
+  return pb::kNoAllocScratchBytes;
+}
+
+// Returns 0 on success, 1 if the problem needs more scratch than the fixed
+// array holds, 2 on invalid arguments, 3 on a CUDA error (message available
+// from pb_attention_bwd_noalloc_last_error()).
+extern "C" __attribute__((visibility("default"))) int pb_attention_bwd_noalloc(
+    const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse, void* dq,
+    void* dk, void* dv, int64_t ldq, int64_t ldk, int64_t ldv, int64_t ldo, int64_t lddo, int64_t lddq,
+    int64_t lddk, int64_t lddv, int B, int S, int nq, int nkv, int D, float scale, int causal,
+    cudaStream_t stream) {
+  using namespace pb;
+  if (!q || !k || !v || !o || !dout || !lse || !dq || !dk || !dv || B <= 0 || S <= 0 || nq <= 0 || nkv <= 0 ||
+      D != HD || nq % nkv != 0 || S % 8 != 0) {
+    noalloc_set_msg("pb_attention_bwd_noalloc: invalid arguments (need head_dim 128, nq % nkv == 0, S % 8 == 0)");
+    return kNoAllocBadArgs;
+  }
+  const int64_t T = (int64_t)B * S;
+  const int64_t rows = (int64_t)B * nq * S;
+  const int64_t ld_acc = (int64_t)nq * HD;
+  // scratch layout: [err word 256 B][delta (rows+128) f32][lse copy (rows+128) f32][dq_acc T*ld_acc f32]
+  const size_t off_delta = 256;
+  const size_t off_lse = off_delta + round256((size_t)(rows + 128) * sizeof(float));
+  const size_t off_acc = off_lse + round256((size_t)(rows + 128) * sizeof(float));
+  const size_t need = off_acc + (size_t)T * ld_acc * sizeof(float);
+  if (need > kNoAllocScratchBytes) {
+    char m[256];
+    snprintf(m, sizeof(m),
+             "pb_attention_bwd_noalloc: problem needs %zu scratch bytes, the fixed array holds %zu "
+             "(reduce B*S*nq)",
+             need, kNoAllocScratchBytes);
+    noalloc_set_msg(m);
+    return kNoAllocTooLarge;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    noalloc_set_msg("pb_attention_bwd_noalloc: cudaGetDevice failed");
+    return kNoAllocCudaError;
+  }
+  unsigned char* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_base[dev]) {
+      void* ptr = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&ptr, g_attn_bwd_scratch);
+      if (e != cudaSuccess || ptr == nullptr) {
+        char m[256];
+        snprintf(m, sizeof(m), "pb_attention_bwd_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+        noalloc_set_msg(m);
+        return kNoAllocCudaError;
+      }
+      g_noalloc_base[dev] = ptr;
+    }
+    if (!g_noalloc_attr[dev]) {
+      if (cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+          cudaSuccess) {
+        noalloc_set_msg("pb_attention_bwd_noalloc: cudaFuncSetAttribute failed");
+        return kNoAllocCudaError;
+      }
+      g_noalloc_attr[dev] = true;
+    }
+    base = static_cast<unsigned char*>(g_noalloc_base[dev]);
+  }
+  int* err = reinterpret_cast<int*>(base);
+  float* delta = reinterpret_cast<float*>(base + off_delta);
+  float* lse_pad = reinterpret_cast<float*>(base + off_lse);
+  float* dq_acc = reinterpret_cast<float*>(base + off_acc);
+  try {
+    // zero what must start at zero: error word, delta / lse padding, dq accumulator
+    PB_CUDA_CHECK(cudaMemsetAsync(err, 0, 256, stream));
+    PB_CUDA_CHECK(cudaMemsetAsync(delta + rows, 0, 128 * sizeof(float), stream));
+    PB_CUDA_CHECK(cudaMemcpyAsync(lse_pad, lse, (size_t)rows * sizeof(float), cudaMemcpyDeviceToDevice, stream));
+    PB_CUDA_CHECK(cudaMemsetAsync(lse_pad + rows, 0, 128 * sizeof(float), stream));
+    PB_CUDA_CHECK(cudaMemsetAsync(dq_acc, 0, (size_t)T * ld_acc * sizeof(float), stream));
+    const int items = (int)(T * nq);
+    attn_delta_kernel<<<(items + 7) / 8, 256, 0, stream>>>((const __nv_bfloat16*)o, ldo,
+                                                           (const __nv_bfloat16*)dout, lddo, delta, B, S, nq);
+    PB_CUDA_CHECK(cudaGetLastError());
+    const uint64_t uS = S, uB = B;
+    CUtensorMap tq = make_tmap_3d_bf16(q, (uint64_t)nq * HD, uS, uB, ldq, uS * ldq, 64, 128, 1);
+    CUtensorMap tk = make_tmap_3d_bf16(k, (uint64_t)nkv * HD, uS, uB, ldk, uS * ldk, 64, 128, 1);
+    CUtensorMap tv = make_tmap_3d_bf16(v, (uint64_t)nkv * HD, uS, uB, ldv, uS * ldv, 64, 128, 1);
+    CUtensorMap tdo = make_tmap_3d_bf16(dout, (uint64_t)nq * HD, uS, uB, lddo, uS * lddo, 64, 128, 1);
+    const int n_t = (S + BT - 1) / BT;
+    attn_bwd_kernel<<<B * nkv * n_t, kThreads, SMEM_BYTES, stream>>>(
+        tq, tk, tv, tdo, lse_pad, delta, dq_acc, ld_acc, (__nv_bfloat16*)dk, lddk, (__nv_bfloat16*)dv, lddv, B, S,
+        nq, nkv, scale, causal != 0, err);
+    PB_CUDA_CHECK(cudaGetLastError());
+    int sms = 0;
+    PB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int64_t cast_work = T * ld_acc / 4;
+    const int cgrid = (int)std::min<int64_t>((cast_work + 255) / 256, (int64_t)sms * 16);
+    cast_rows_kernel<<<cgrid, 256, 0, stream>>>(dq_acc, ld_acc, (__nv_bfloat16*)dq, lddq, (int)T, (int)ld_acc);
+    PB_CUDA_CHECK(cudaGetLastError());
+  } catch (const std::exception& ex) {
+    noalloc_set_msg(ex.what());
+    return kNoAllocCudaError;
+  }
+  noalloc_set_msg("");
+  return kNoAllocOk;
+}
+
+// Bounded-wait status of the last call on this device (reads the error word
+// kept in the scratch array; synchronises the device first).
+extern "C" __attribute__((visibility("default"))) int pb_attention_bwd_noalloc_device_status() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= pb::kMaxDevices || !pb::g_noalloc_base[dev])
+    return -1;
+  int v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  if (cudaMemcpy(&v, pb::g_noalloc_base[dev], sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  return v;
+}
