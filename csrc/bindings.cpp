@@ -72,6 +72,7 @@ void clear_error(int64_t device) { pb::clear_error((int)device); }
 }  // namespace
 
 void register_ops(pybind11::module& m);
+void register_comm(pybind11::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "parallel_b200 sm_100a kernels";
@@ -82,4 +83,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("read_error", &read_error);
   m.def("clear_error", &clear_error);
   register_ops(m);
+  register_comm(m);
 }

@@ -1,0 +1,165 @@
+// In-kernel NVLink peer-to-peer collectives over symmetric memory.
+//
+// Buffers are allocated symmetrically (every rank maps every peer's buffer
+// into its address space); these kernels read / write peers' memory with
+// ordinary loads and stores over NVLink 5 / NVSwitch.  No TMA multicast and
+// no library kernel ever touches a peer pointer.
+//
+//   signal_barrier   one block: publish `epoch` into every peer's signal pad
+//                    (release, system scope) and wait - bounded by limit_ns -
+//                    until every peer has published it into ours.  A timeout
+//                    records kErrPeerTimeout and returns (the host raises).
+//   multi_copy       gather of up to kMaxSegs (src, dst, bytes) segments with
+//                    16-byte vector loads; used for the FSDP all-gather, which
+//                    writes each peer's shard straight into the parameter-major
+//                    full buffer (no unpack pass).
+//   reduce_segments  reduce-scatter / all-reduce: out[i] = scale * sum over
+//                    peers of src_peer[i] (+ out[i] when accumulating), bf16 in
+//                    and out, fp32 sums.
+//   wait_flag        test hook: bounded wait on a flag that nobody sets.
+//
+// Reference counterpart: the NCCL all_gather_into_tensor / reduce_scatter_
+// tensor / all_reduce calls of parallel/parallel/engine/_dp_param_unit.py:
+// 18-37,350,477 and engine.py:239.
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "comm.cuh"
+#include "host_util.h"
+#include "ptx.cuh"
+
+namespace pb {
+namespace {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void signal_barrier_kernel(const uint64_t* __restrict__ peer_pads, int rank, int world, int slot_base,
+                                      uint32_t epoch, uint64_t limit_ns, int* err) {
+  const int i = threadIdx.x;
+  if (i >= world) return;
+  // make this rank's prior writes (earlier kernels on this stream) visible first
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  uint32_t* peer = reinterpret_cast<uint32_t*>(peer_pads[i]);
+  st_release_sys(peer + slot_base + rank, epoch);
+  const uint32_t* mine = reinterpret_cast<const uint32_t*>(peer_pads[rank]) + slot_base + i;
+  const uint64_t t0 = globaltimer();
+  uint32_t n = 0;
+  while ((int32_t)(ld_acquire_sys(mine) - epoch) < 0) {
+    if ((++n & 255u) == 0) {
+      if (*((volatile int*)err) != 0) return;
+      if (globaltimer() - t0 > limit_ns) {
+        record_error(err, kErrPeerTimeout);
+        return;
+      }
+    }
+  }
+}
+
+__global__ void multi_copy_kernel(CopySegments segs) {
+  // flatten all segments into 16-byte vectors; grid-stride
+  int64_t total = segs.vec_start[segs.n];
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
+    int s = 0;
+    while (s + 1 < segs.n && segs.vec_start[s + 1] <= v) ++s;
+    const int64_t off = (v - segs.vec_start[s]) * 16;
+    const uint4 val = *reinterpret_cast<const uint4*>(segs.src[s] + off);
+    *reinterpret_cast<uint4*>(segs.dst[s] + off) = val;
+  }
+}
+
+// out[i] = scale * sum_j src_j[i] (+ out[i]);  8 bf16 per thread per step
+__global__ void reduce_segments_kernel(ReduceSegments segs, int world, float scale, bool accumulate) {
+  int64_t total = segs.vec_start[segs.n];
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
+    int s = 0;
+    while (s + 1 < segs.n && segs.vec_start[s + 1] <= v) ++s;
+    const int64_t off = (v - segs.vec_start[s]) * 8;  // elements
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int j = 0; j < world; ++j) {
+      const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(segs.src[j][s]) + off;
+      uint4 u = *reinterpret_cast<const uint4*>(src);
+      const uint32_t* p = &u.x;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 f = unpack_bf16x2(p[q]);
+        acc[2 * q] += f.x;
+        acc[2 * q + 1] += f.y;
+      }
+    }
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(segs.dst[s]) + off;
+    if (accumulate) {
+      uint4 u = *reinterpret_cast<const uint4*>(dst);
+      const uint32_t* p = &u.x;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 f = unpack_bf16x2(p[q]);
+        acc[2 * q] = acc[2 * q] * scale + f.x;
+        acc[2 * q + 1] = acc[2 * q + 1] * scale + f.y;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] *= scale;
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(dst) = o;
+  }
+}
+
+__global__ void wait_flag_kernel(const uint32_t* flag, uint32_t target, uint64_t limit_ns, int* status) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const uint64_t t0 = globaltimer();
+  uint32_t n = 0;
+  while ((int32_t)(ld_acquire_sys(flag) - target) < 0) {
+    if ((++n & 255u) == 0 && globaltimer() - t0 > limit_ns) {
+      record_error(status, kErrPeerTimeout);
+      return;
+    }
+  }
+}
+
+int copy_grid(int64_t vecs) {
+  const int64_t cap = (int64_t)num_sms() * 8;
+  int64_t g = (vecs + 255) / 256;
+  return (int)std::max<int64_t>(1, std::min(g, cap));
+}
+
+}  // namespace
+
+void signal_barrier(const uint64_t* peer_pads_dev, int rank, int world, int slot_base, uint32_t epoch,
+                    uint64_t limit_ns, cudaStream_t s) {
+  PB_CHECK(world >= 1 && world <= kMaxPeers, "signal_barrier: world size");
+  signal_barrier_kernel<<<1, 32, 0, s>>>(peer_pads_dev, rank, world, slot_base, epoch, limit_ns, error_word());
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+void multi_copy(const CopySegments& segs, cudaStream_t s) {
+  if (segs.n == 0) return;
+  multi_copy_kernel<<<copy_grid(segs.vec_start[segs.n]), 256, 0, s>>>(segs);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+void reduce_segments(const ReduceSegments& segs, int world, float scale, bool accumulate, cudaStream_t s) {
+  if (segs.n == 0) return;
+  reduce_segments_kernel<<<copy_grid(segs.vec_start[segs.n]), 256, 0, s>>>(segs, world, scale, accumulate);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+void wait_flag(const uint32_t* flag, uint32_t target, uint64_t limit_ns, int* status, cudaStream_t s) {
+  wait_flag_kernel<<<1, 32, 0, s>>>(flag, target, limit_ns, status);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace pb

@@ -1,0 +1,196 @@
+"""NVLink peer-to-peer data plane for FSDP units (symmetric memory + own kernels).
+
+Every FSDP local bucket and the reduce-scatter staging slots are allocated
+as symmetric memory (``torch.distributed._symmetric_memory``: one mapping of
+every peer's buffer per process; used here only for allocation and handle
+exchange).  The data movement is done by this repository's kernels
+(``csrc/comm.cu``):
+
+* all-gather: one bounded signal barrier ("my shard is current"), then one
+  kernel that loads every peer's shard over NVLink and stores it straight
+  into the parameter-major full buffer (no rank-major staging, no unpack);
+* reduce-scatter: gradients are packed into a symmetric slot, one barrier
+  ("my gradients are staged"), one kernel that sums the rank's shard rows
+  from all peers in fp32 and writes (or accumulates into) the local bf16
+  gradient bucket scaled by 1/N, and a closing barrier so the slot can be
+  reused; it runs on a dedicated communication stream so it overlaps the
+  next unit's backward.
+
+Barriers are bounded (``PB_P2P_TIMEOUT_S``, default 60 s): a missing peer
+records an error word on the device instead of hanging; the engine reads it
+asynchronously and raises ``CollectiveTimeout``.
+"""
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+from ...ops._ext import ext
+from ...profiling import collective_profile
+from .unit_collectives import TorchUnitCollectives, unit_detail
+
+
+class CollectiveTimeout(RuntimeError):
+    pass
+
+
+def p2p_supported(group) -> bool:
+    if os.environ.get("PB_P2P", "1") == "0":
+        return False
+    if group is None or not torch.cuda.is_available():
+        return False
+    try:
+        import torch.distributed._symmetric_memory  # noqa: F401
+    except ImportError:
+        return False
+    return 1 < dist.get_world_size(group) <= 8
+
+
+class SymmBuffer:
+    """A symmetric allocation plus its peer addresses and signal pads."""
+
+    def __init__(self, numel: int, dtype, device, group):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.tensor = symm_mem.empty(max(numel, 64), dtype=dtype, device=device)
+        self.tensor.zero_()
+        self.handle = symm_mem.rendezvous(self.tensor, group)
+        self.rank = self.handle.rank
+        self.world = self.handle.world_size
+        base = list(self.handle.buffer_ptrs)
+        off = self.tensor.data_ptr() - base[self.rank]
+        self.peer_ptrs = [b + off for b in base]
+        self.pads_dev = int(self.handle.signal_pad_ptrs_dev)
+        self.epochs = [0] * 8
+        self.event = None
+
+    def barrier(self, channel: int, limit_s: float) -> None:
+        self.epochs[channel] += 1
+        ext().p2p_barrier(self.pads_dev, self.rank, self.world, channel * 8, self.epochs[channel], limit_s)
+
+
+@dataclass
+class _P2PHandle:
+    event: Any
+    profile: Any
+    torch_handle: Any = None
+
+
+class P2PUnitCollectives:
+    name = "p2p"
+
+    def __init__(self, group):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.limit_s = float(os.environ.get("PB_P2P_TIMEOUT_S", "60"))
+        self.slots: list[SymmBuffer] = []
+        self._slot_numel = 0
+        self._next_slot = 0
+        self.stream = None
+        self._fallback = TorchUnitCollectives()
+
+    # ------------------------------------------------------------ allocation
+    @staticmethod
+    def _aligned(unit) -> bool:
+        es = unit.param_metas[0].parameter.element_size()
+        return es == 2 and all((m.padded_numel * es) % 16 == 0 for m in unit.param_metas)
+
+    def alloc_local_bucket(self, unit, numel, dtype, device):
+        if not self._aligned(unit):
+            unit._p2p = None
+            return self._fallback.alloc_local_bucket(unit, numel, dtype, device)
+        buf = SymmBuffer(numel, dtype, device, self.group)
+        unit._p2p = buf
+        return buf.tensor[:numel]
+
+    def release_full(self, unit, full):
+        pass
+
+    # ------------------------------------------------------------ all-gather
+    def all_gather(self, unit, mode: str = "demand") -> torch.Tensor:
+        buf = getattr(unit, "_p2p", None)
+        if buf is None:
+            return self._fallback.all_gather(unit, mode)
+        es = 2
+        full = torch.empty(unit.full_numel, dtype=unit.local_bucket.dtype, device=unit.device)
+        src, dst, nb = [], [], []
+        fbase = full.data_ptr()
+        for r in range(self.world):
+            for m in unit.param_metas:
+                if m.padded_numel == 0:
+                    continue
+                src.append(buf.peer_ptrs[r] + m.bucket_offset * es)
+                dst.append(fbase + (m.full_offset + r * m.padded_numel) * es)
+                nb.append(m.padded_numel * es)
+        with collective_profile("fsdp_all_gather", value=unit.local_bucket, mode=mode, detail=unit_detail(unit)):
+            buf.barrier(0, self.limit_s)
+            ext().p2p_copy(src, dst, nb)
+        return full
+
+    # ------------------------------------------------------------ reduce-scatter
+    def _slot(self, unit) -> SymmBuffer:
+        if not self.slots:
+            raise RuntimeError("reduce-scatter slots not allocated")
+        s = self.slots[self._next_slot % len(self.slots)]
+        self._next_slot += 1
+        return s
+
+    def prepare(self, units) -> None:
+        """Allocate the reduce-scatter staging slots (collective; call once)."""
+        need = max((u.full_numel for u in units if getattr(u, "_p2p", None) is not None), default=0)
+        if need == 0 or self.slots:
+            return
+        dev = units[0].device
+        self._slot_numel = need
+        self.slots = [SymmBuffer(need, torch.bfloat16, dev, self.group) for _ in range(3)]
+        self.stream = torch.cuda.Stream(device=dev)
+
+    def reduce_scatter(self, unit, grads, grad_bucket, accumulate: bool, mode: str = "overlapped"):
+        buf = getattr(unit, "_p2p", None)
+        if buf is None or not self.slots:
+            return _P2PHandle(None, None, self._fallback.reduce_scatter(unit, grads, grad_bucket, accumulate, mode))
+        slot = self._slot(unit)
+        cur = torch.cuda.current_stream(unit.device)
+        if slot.event is not None:
+            cur.wait_event(slot.event)
+        N = self.world
+        st = slot.tensor
+        for g, m in zip(grads, unit.param_metas):
+            rows = N * m.padded_rows
+            view = st.narrow(0, m.full_offset, rows * m.row_numel).view(rows, -1)
+            if g is None:
+                view.zero_()
+                continue
+            g2 = g.reshape(m.shape[0], -1)
+            view[: m.shape[0]].copy_(g2)
+            if m.shape[0] < rows:
+                view[m.shape[0]:].zero_()
+        self.stream.wait_stream(cur)
+        es = 2
+        src = [[slot.peer_ptrs[r] + (m.full_offset + self.rank * m.padded_numel) * es for m in unit.param_metas]
+               for r in range(N)]
+        dst = [grad_bucket.data_ptr() + m.bucket_offset * es for m in unit.param_metas]
+        nel = [m.padded_numel for m in unit.param_metas]
+        prof = collective_profile("fsdp_reduce_scatter", payload_bytes=unit.full_numel * es, mode=mode,
+                                  detail=unit_detail(unit), device=unit.device, defer_cuda_end=True)
+        with torch.cuda.stream(self.stream):
+            with prof:
+                slot.barrier(1, self.limit_s)
+                ext().p2p_reduce(src, dst, nel, 1.0 / N, accumulate)
+                slot.barrier(2, self.limit_s)
+            ev = torch.cuda.Event()
+            ev.record(self.stream)
+        slot.event = ev
+        return _P2PHandle(ev, prof)
+
+    def wait(self, h: _P2PHandle) -> None:
+        if h.torch_handle is not None:
+            return self._fallback.wait(h.torch_handle)
+        torch.cuda.current_stream().wait_event(h.event)
+        if h.profile is not None:
+            h.profile.complete()

@@ -203,6 +203,8 @@ class FSDPWrapper:
             unit.shard()
             unit._layer_primary = primary
             self.units.append(unit)
+        if hasattr(self.coll, "prepare"):
+            self.coll.prepare(self.units)
         self.root_units = [u for u in self.units if u.module is self.model]
         for i, unit in enumerate(self.units):
             unit.next_fwd = self.units[i + 1] if i + 1 < len(self.units) else None

@@ -1,0 +1,69 @@
+"""Worker launched by tests/test_multigpu.py with torchrun (one process per GPU)."""
+import json
+import os
+import sys
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def run_engine(collectives, data, layers=2):
+    from parallel_b200.config import from_dotlist, load_cfg, merge
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.qwen3 import build_model
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    world = dist.get_world_size()
+    cfg = merge(load_cfg(argv=[]), from_dotlist([
+        "config.device_type=cuda", "model.learning_rate=1e-3", f"parallel.dp_shard={world}",
+        "engine.activation_checkpoint=true", f"engine.collectives={collectives}"]))
+    pc = ParallelConfig(cfg)
+    pc.set_device_mesh("cuda")
+    mcfg = resolve_config("Qwen/Qwen3-0.6B", num_hidden_layers=layers, vocab_size=4096)
+    m = build_model(mcfg, dtype=torch.bfloat16, seed=0)
+    eng = ParallelEngine(m, None, pc, cfg, pc.device)
+    losses = []
+    r = dist.get_rank()
+    for tok in data:
+        b = tok.shape[0] // world
+        mine = tok[r * b:(r + 1) * b].cuda()
+        loss = eng.forward(mine[:, :-1], mine[:, 1:]).loss
+        eng.backward(loss)
+        eng.step()
+        losses.append(eng.reduce_loss(loss).item())
+    state = eng.state_dict()
+    from parallel_b200.ops._ext import check_device_errors
+
+    torch.cuda.synchronize()
+    check_device_errors()
+    return losses, state, eng.fsdp_wrapper.coll.name
+
+
+def main():
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    world = dist.get_world_size()
+    g = torch.Generator().manual_seed(0)
+    data = [torch.randint(0, 4096, (2 * world, 257), generator=g) for _ in range(3)]
+    l_p2p, s_p2p, n1 = run_engine("p2p", data)
+    l_nccl, s_nccl, n2 = run_engine("nccl", data)
+    out = {"p2p": l_p2p, "nccl": l_nccl, "names": [n1, n2]}
+    if dist.get_rank() == 0:
+        worst = 0.0
+        for k in s_p2p:
+            a, b = s_p2p[k].float(), s_nccl[k].float()
+            worst = max(worst, ((a - b).norm() / (b.norm() + 1e-12)).item())
+        out["state_rel_diff"] = worst
+        with open(os.environ["PB_TEST_OUT"], "w") as f:
+            json.dump(out, f)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,41 @@
+"""Multi-GPU tests (NVLink P2P collectives vs NCCL) and the bounded-wait status path."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def test_bounded_wait_times_out_and_context_survives():
+    from parallel_b200.ops._ext import ext
+
+    C = ext()
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")   # nothing ever sets it
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    C.wait_flag(flag, 1, 0.5, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 2  # kErrPeerTimeout
+    a = torch.randn(256, 256, device="cuda").to(torch.bfloat16)
+    out = torch.empty(256, 256, device="cuda", dtype=torch.bfloat16)
+    C.gemm(a, a, out, False, False, 0, 1.0)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fsdp_p2p_collectives_match_nccl(tmp_path):
+    out = tmp_path / "res.json"
+    env = dict(os.environ, PB_TEST_OUT=str(out), NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+           "--master-port", "29533", os.path.join(HERE, "multigpu_worker.py")]
+    subprocess.run(cmd, env=env, check=True, timeout=600)
+    res = json.loads(out.read_text())
+    assert res["names"] == ["p2p", "nccl"]
+    for a, b in zip(res["p2p"], res["nccl"]):
+        assert abs(a - b) < 2e-2 * max(1.0, abs(b)), res
+    assert res["state_rel_diff"] < 2e-2, res
