@@ -325,6 +325,7 @@ def run_reference(args, rank, world, local):
     model.train()
     engine = RefEngine(model, None, pconfig, cfg, device, mp_plan=plan)
     B, S, V = args.batch, args.seq, model.config.vocab_size
+    deviation = None
     gen = torch.Generator(device="cpu").manual_seed(1000 + rank)
     nb = 4
     host = [torch.randint(0, V, (B, S + 1), generator=gen).pin_memory() for _ in range(nb)]
@@ -337,6 +338,28 @@ def run_reference(args, rank, world, local):
         engine.step()
         return loss
 
+    try:
+        step(dev[0])
+    except Exception as exc:
+        # HF's checkpointed recompute can take a different SDPA GQA branch than
+        # the forward on this image (transformers 5.5 vs the pinned 5.14) and
+        # torch.utils.checkpoint rejects it.  Rebuild with the reference's own
+        # engine.activation_checkpoint=false switch (less work per step, so
+        # any ratio against it is conservative) and say so in the JSON line.
+        if "CheckpointError" not in type(exc).__name__ or not cfg.engine.activation_checkpoint:
+            raise
+        deviation = (f"reference activation checkpointing raised {type(exc).__name__} on this image; "
+                     "reference measured with engine.activation_checkpoint=false")
+        del engine, model
+        torch.cuda.empty_cache()
+        cfg.engine.activation_checkpoint = False
+        pconfig.model_init_rngs(seed=42)
+        model, plan = ref_load(cfg, pconfig)
+        pconfig.model_train_rngs(seed=42)
+        if pconfig.dp_shard_size <= 1 and not pconfig.model_parallel_enabled:
+            model.to(device)
+        model.train()
+        engine = RefEngine(model, None, pconfig, cfg, device, mp_plan=plan)
     for i in range(args.warmup):
         step(dev[i % nb])
     clocks = ClockSampler(local)
@@ -363,7 +386,10 @@ def run_reference(args, rank, world, local):
         e2e = {"value": B * S * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": host[0].numel() * host[0].element_size(), "d2h_bytes_per_step": 4,
                "api": "reference ParallelEngine.forward/backward/step + loss.item()"}
-    return ms, clk, e2e, 0, {}
+    extra = {"reference_activation_checkpoint": bool(cfg.engine.activation_checkpoint)}
+    if deviation:
+        extra["deviation"] = deviation
+    return ms, clk, e2e, 0, extra
 
 
 def main():

@@ -22,6 +22,7 @@ asynchronously and raises ``CollectiveTimeout``.
 """
 from __future__ import annotations
 
+import importlib
 import os
 from dataclasses import dataclass
 from typing import Any
@@ -44,7 +45,7 @@ def p2p_supported(group) -> bool:
     if group is None or not torch.cuda.is_available():
         return False
     try:
-        import torch.distributed._symmetric_memory  # noqa: F401
+        importlib.import_module("torch.distributed._symmetric_memory")
     except ImportError:
         return False
     return 1 < dist.get_world_size(group) <= 8
@@ -54,8 +55,7 @@ class SymmBuffer:
     """A symmetric allocation plus its peer addresses and signal pads."""
 
     def __init__(self, numel: int, dtype, device, group):
-        import torch.distributed._symmetric_memory as symm_mem
-
+        symm_mem = importlib.import_module("torch.distributed._symmetric_memory")
         self.tensor = symm_mem.empty(max(numel, 64), dtype=dtype, device=device)
         self.tensor.zero_()
         self.handle = symm_mem.rendezvous(self.tensor, group)
