@@ -72,7 +72,8 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int64_t
                                    const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                    const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
                                    __nv_bfloat16* __restrict__ dx, int64_t lddx, float* __restrict__ dw,
-                                   int rows, int cols, int rows_per_block) {
+                                   int rows, int cols, int rows_per_block,
+                                   const __nv_bfloat16* __restrict__ dres, int64_t lddres) {
   extern __shared__ float sdw[];
   for (int c = threadIdx.x; c < cols; c += blockDim.x) sdw[c] = 0.f;
   __syncthreads();
@@ -106,6 +107,12 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int64_t
       load8(w + c, wv);
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = r * (gv[j] * wv[j] - xv[j] * r * dot);
+      if (dres) {
+        float rv[8];
+        load8(dres + (int64_t)row * lddres + c, rv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] += rv[j];
+      }
       store8(dxr + c, o);
     }
   }
@@ -114,8 +121,86 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int64_t
     for (int c = threadIdx.x; c < cols; c += blockDim.x) atomicAdd(&dw[c], sdw[c]);
 }
 
-// One warp per (token, head); D == 128: lane owns elements [4*lane, 4*lane+4).
-// RoPE pairs element i with i +- 64, i.e. lane l with lane l ^ 16.
+// Register-resident variant: cols == CH * 256; lane owns CH chunks of 8
+// columns; dw partials stay in registers until one shared-memory reduction
+// per warp.  Optionally adds a residual-stream gradient (dres) into dx, which
+// fuses the add autograd would otherwise run for "x -> norm(x) and x -> +".
+template <int CH>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(
+    const __nv_bfloat16* __restrict__ dy, int64_t lddy, const __nv_bfloat16* __restrict__ x, int64_t ldx,
+    const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dres,
+    int64_t lddres, __nv_bfloat16* __restrict__ dx, int64_t lddx, float* __restrict__ dw, int rows,
+    int rows_per_block) {
+  constexpr int cols = CH * 256;
+  extern __shared__ float sdw[];
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) sdw[c] = 0.f;
+  __syncthreads();
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  float acc[CH][8];
+#pragma unroll
+  for (int k = 0; k < CH; ++k)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[k][j] = 0.f;
+  const int r0 = blockIdx.x * rows_per_block;
+  const int r1 = min(rows, r0 + rows_per_block);
+  for (int row = r0 + (threadIdx.x >> 5); row < r1; row += warps) {
+    const float r = rstd[row];
+    const __nv_bfloat16* xr = x + (int64_t)row * ldx;
+    const __nv_bfloat16* gr = dy + (int64_t)row * lddy;
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < CH; ++k) {
+      const int c = k * 256 + lane * 8;
+      float xv[8], gv[8], wv[8];
+      load8(xr + c, xv);
+      load8(gr + c, gv);
+      load8(w + c, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float xh = xv[j] * r;
+        dot += gv[j] * wv[j] * xh;
+        acc[k][j] += gv[j] * bfr(xh);
+      }
+    }
+    dot = warp_sum(dot) / (float)cols;
+#pragma unroll
+    for (int k = 0; k < CH; ++k) {
+      const int c = k * 256 + lane * 8;
+      float xv[8], gv[8], wv[8], o[8];
+      load8(xr + c, xv);
+      load8(gr + c, gv);
+      load8(w + c, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = r * (gv[j] * wv[j] - xv[j] * r * dot);
+      if (dres) {
+        float rv[8];
+        load8(dres + (int64_t)row * lddres + c, rv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] += rv[j];
+      }
+      store8(dx + (int64_t)row * lddx + c, o);
+    }
+  }
+  if (dw) {
+#pragma unroll
+    for (int k = 0; k < CH; ++k)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) atomicAdd(&sdw[k * 256 + lane * 8 + j], acc[k][j]);
+    __syncthreads();
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) atomicAdd(&dw[c], sdw[c]);
+  }
+}
+
+// Half a warp per (token, head); D == 128: lane owns 8 consecutive elements
+// (16-byte accesses).  RoPE pairs element i with i +- 64, i.e. lane l with
+// lane l ^ 8 inside the same half warp.
+__device__ __forceinline__ float half_sum(float v) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
 __global__ void qknorm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ldqkv,
                                        const __nv_bfloat16* __restrict__ qw,
                                        const __nv_bfloat16* __restrict__ kw,
@@ -125,54 +210,44 @@ __global__ void qknorm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, in
                                        __nv_bfloat16* __restrict__ k_out, int64_t ldk,
                                        float* __restrict__ rstd, int T, int S, int nq, int nkv, float eps) {
   constexpr int D = 128;
-  const int warps = blockDim.x >> 5;
-  const int item = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  const int hl = lane & 15;
   const int nh = nq + nkv;
-  if (item >= T * nh) return;
-  const int t = item / nh, h = item % nh;
+  const int64_t total = (int64_t)T * nh;
+  int64_t item = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 2 + (lane >> 4);
+  const bool valid = item < total;
+  if (!valid) item = total - 1;  // keep all lanes in the shuffles
+  const int t = (int)(item / nh), h = (int)(item % nh);
   const bool is_q = h < nq;
-  const __nv_bfloat16* src = qkv + (int64_t)t * ldqkv + (int64_t)h * D + lane * 4;
-  const __nv_bfloat16* wgt = (is_q ? qw : kw) + lane * 4;
-  uint2 raw = *reinterpret_cast<const uint2*>(src);
-  float2 a = unpack_bf16x2(raw.x), b = unpack_bf16x2(raw.y);
-  float v[4] = {a.x, a.y, b.x, b.y};
-  float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
-  ss = warp_sum(ss);
+  float v[8], wv[8], cv[8], sv[8];
+  load8(qkv + (int64_t)t * ldqkv + (int64_t)h * D + hl * 8, v);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+  ss = half_sum(ss);
   const float r = rsqrtf(ss / (float)D + eps);
-  if (lane == 0) rstd[(int64_t)t * nh + h] = r;
-  uint2 wraw = *reinterpret_cast<const uint2*>(wgt);
-  float2 wa = unpack_bf16x2(wraw.x), wb = unpack_bf16x2(wraw.y);
-  float wv[4] = {wa.x, wa.y, wb.x, wb.y};
-  float n[4];
+  load8((is_q ? qw : kw) + hl * 8, wv);
+  float n[8], p[8];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) n[j] = bfr(wv[j] * bfr(v[j] * r));
-  // partner values (i +- 64)
-  float p[4];
+  for (int j = 0; j < 8; ++j) n[j] = bfr(wv[j] * bfr(v[j] * r));
 #pragma unroll
-  for (int j = 0; j < 4; ++j) p[j] = __shfl_xor_sync(0xffffffffu, n[j], 16);
+  for (int j = 0; j < 8; ++j) p[j] = __shfl_xor_sync(0xffffffffu, n[j], 8);
   const int pos = t % S;
-  const __nv_bfloat16* cr = cosb + (int64_t)pos * D + lane * 4;
-  const __nv_bfloat16* sr = sinb + (int64_t)pos * D + lane * 4;
-  uint2 craw = *reinterpret_cast<const uint2*>(cr);
-  uint2 sraw = *reinterpret_cast<const uint2*>(sr);
-  float2 ca = unpack_bf16x2(craw.x), cb = unpack_bf16x2(craw.y);
-  float2 sa = unpack_bf16x2(sraw.x), sb = unpack_bf16x2(sraw.y);
-  float cv[4] = {ca.x, ca.y, cb.x, cb.y}, sv[4] = {sa.x, sa.y, sb.x, sb.y};
-  const float sign = lane < 16 ? -1.f : 1.f;  // rotate_half: [-x2, x1]
-  float o[4];
+  load8(cosb + (int64_t)pos * D + hl * 8, cv);
+  load8(sinb + (int64_t)pos * D + hl * 8, sv);
+  const float sign = hl < 8 ? -1.f : 1.f;  // rotate_half: [-x2, x1]
+  float o[8];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) o[j] = bfr(bfr(n[j] * cv[j]) + bfr(sign * p[j] * sv[j]));
+  for (int j = 0; j < 8; ++j) o[j] = bfr(bfr(n[j] * cv[j]) + bfr(sign * p[j] * sv[j]));
+  if (!valid) return;
+  if (hl == 0) rstd[(int64_t)t * nh + h] = r;
   __nv_bfloat16* dst = is_q ? q_out + (int64_t)t * ldq + (int64_t)h * D
                             : k_out + (int64_t)t * ldk + (int64_t)(h - nq) * D;
-  uint2 out;
-  out.x = pack_bf16x2(o[0], o[1]);
-  out.y = pack_bf16x2(o[2], o[3]);
-  *reinterpret_cast<uint2*>(dst + lane * 4) = out;
+  store8(dst + hl * 8, o);
 }
 
-// Backward of the above.  Block = 8 warps; per-block smem partials for the
-// q/k norm weight grads (2 x 128 floats).
+// Backward of the above; q/k norm weight grads: per-lane registers, then one
+// shared-memory reduction per block.
 __global__ void qknorm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dq, int64_t lddq,
                                        const __nv_bfloat16* __restrict__ dk, int64_t lddk,
                                        const __nv_bfloat16* __restrict__ qkv, int64_t ldqkv,
@@ -188,64 +263,63 @@ __global__ void qknorm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dq, int
   __shared__ float sdw[2][D];
   for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) (&sdw[0][0])[i] = 0.f;
   __syncthreads();
-  const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int hl = lane & 15;
+  const int slots = (blockDim.x >> 5) * 2;
+  const int slot = (threadIdx.x >> 5) * 2 + (lane >> 4);
   const int nh = nq + nkv;
-  const int i0 = blockIdx.x * items_per_block;
-  const int i1 = min(T * nh, i0 + items_per_block);
-  float acc_q[4] = {0, 0, 0, 0}, acc_k[4] = {0, 0, 0, 0};
-  for (int item = i0 + (threadIdx.x >> 5); item < i1; item += warps) {
-    const int t = item / nh, h = item % nh;
+  const int64_t total = (int64_t)T * nh;
+  const int64_t i0 = (int64_t)blockIdx.x * items_per_block;
+  const int64_t i1 = min(total, i0 + items_per_block);
+  float qw_r[8], kw_r[8], acc_q[8], acc_k[8];
+  load8(qw + hl * 8, qw_r);
+  load8(kw + hl * 8, kw_r);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc_q[j] = acc_k[j] = 0.f;
+  // every lane iterates the same number of times so shuffles stay converged
+  const int64_t span = i1 - i0;
+  const int64_t iters = (span + slots - 1) / slots;
+  for (int64_t it = 0; it < iters; ++it) {
+    int64_t item = i0 + it * slots + slot;
+    const bool valid = item < i1;
+    if (!valid) item = i1 - 1;
+    const int t = (int)(item / nh), h = (int)(item % nh);
     const bool is_q = h < nq;
-    const __nv_bfloat16* g = is_q ? dq + (int64_t)t * lddq + (int64_t)h * D
-                                  : dk + (int64_t)t * lddk + (int64_t)(h - nq) * D;
-    uint2 graw = *reinterpret_cast<const uint2*>(g + lane * 4);
-    float2 ga = unpack_bf16x2(graw.x), gb = unpack_bf16x2(graw.y);
-    float gv[4] = {ga.x, ga.y, gb.x, gb.y};
+    float gv[8], cv[8], sv[8], xv[8];
+    load8(is_q ? dq + (int64_t)t * lddq + (int64_t)h * D + hl * 8
+               : dk + (int64_t)t * lddk + (int64_t)(h - nq) * D + hl * 8, gv);
     const int pos = t % S;
-    uint2 craw = *reinterpret_cast<const uint2*>(cosb + (int64_t)pos * D + lane * 4);
-    uint2 sraw = *reinterpret_cast<const uint2*>(sinb + (int64_t)pos * D + lane * 4);
-    float2 ca = unpack_bf16x2(craw.x), cb = unpack_bf16x2(craw.y);
-    float2 sa = unpack_bf16x2(sraw.x), sb = unpack_bf16x2(sraw.y);
-    float cv[4] = {ca.x, ca.y, cb.x, cb.y}, sv[4] = {sa.x, sa.y, sb.x, sb.y};
+    load8(cosb + (int64_t)pos * D + hl * 8, cv);
+    load8(sinb + (int64_t)pos * D + hl * 8, sv);
     // dn[i] = g[i]*c[i] + (i<64 ? g[i+64]*s[i+64] : -g[i-64]*s[i-64])
-    float gs[4];
+    float gs[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) gs[j] = __shfl_xor_sync(0xffffffffu, gv[j] * sv[j], 16);
-    const float sign = lane < 16 ? 1.f : -1.f;
-    float dn[4];
+    for (int j = 0; j < 8; ++j) gs[j] = __shfl_xor_sync(0xffffffffu, gv[j] * sv[j], 8);
+    const float sign = hl < 8 ? 1.f : -1.f;
+    float dn[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) dn[j] = gv[j] * cv[j] + sign * gs[j];
-    // norm backward
-    const __nv_bfloat16* src = qkv + (int64_t)t * ldqkv + (int64_t)h * D + lane * 4;
-    uint2 raw = *reinterpret_cast<const uint2*>(src);
-    float2 a = unpack_bf16x2(raw.x), b = unpack_bf16x2(raw.y);
-    float xv[4] = {a.x, a.y, b.x, b.y};
-    uint2 wraw = *reinterpret_cast<const uint2*>((is_q ? qw : kw) + lane * 4);
-    float2 wa = unpack_bf16x2(wraw.x), wb = unpack_bf16x2(wraw.y);
-    float wv[4] = {wa.x, wa.y, wb.x, wb.y};
+    for (int j = 0; j < 8; ++j) dn[j] = gv[j] * cv[j] + sign * gs[j];
+    load8(qkv + (int64_t)t * ldqkv + (int64_t)h * D + hl * 8, xv);
+    const float* wv = is_q ? qw_r : kw_r;
     const float r = rstd[(int64_t)t * nh + h];
     float dot = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) dot += dn[j] * wv[j] * xv[j] * r;
-    dot = warp_sum(dot) / (float)D;
-    float dx[4];
+    for (int j = 0; j < 8; ++j) dot += dn[j] * wv[j] * xv[j] * r;
+    dot = half_sum(dot) / (float)D;
+    if (!valid) continue;
+    float dx[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < 8; ++j) {
       dx[j] = r * (dn[j] * wv[j] - xv[j] * r * dot);
       const float contrib = dn[j] * bfr(xv[j] * r);
       if (is_q) acc_q[j] += contrib; else acc_k[j] += contrib;
     }
-    __nv_bfloat16* d = dqkv + (int64_t)t * lddqkv + (int64_t)h * D + lane * 4;
-    uint2 out;
-    out.x = pack_bf16x2(dx[0], dx[1]);
-    out.y = pack_bf16x2(dx[2], dx[3]);
-    *reinterpret_cast<uint2*>(d) = out;
+    store8(dqkv + (int64_t)t * lddqkv + (int64_t)h * D + hl * 8, dx);
   }
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    atomicAdd(&sdw[0][lane * 4 + j], acc_q[j]);
-    atomicAdd(&sdw[1][lane * 4 + j], acc_k[j]);
+  for (int j = 0; j < 8; ++j) {
+    atomicAdd(&sdw[0][hl * 8 + j], acc_q[j]);
+    atomicAdd(&sdw[1][hl * 8 + j], acc_k[j]);
   }
   __syncthreads();
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
@@ -268,15 +342,31 @@ void rmsnorm_fwd(const void* x, int64_t ldx, const void* w, void* y, int64_t ldy
 
 void rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const void* w,
                  const float* rstd, void* dx, int64_t lddx, float* dw_acc, int rows, int cols,
-                 cudaStream_t s) {
+                 cudaStream_t s, const void* dres, int64_t lddres) {
   PB_CHECK(cols % 8 == 0, "rmsnorm: cols must be a multiple of 8");
   const int blocks = num_sms() * 2;
   const int rpb = (rows + blocks - 1) / blocks;
   const int grid = (rows + rpb - 1) / rpb;
   const size_t smem = (size_t)cols * sizeof(float);
+  if (cols % 256 == 0 && cols <= 2048) {
+#define PB_RMS_BWD(CH)                                                                                     \
+  case CH:                                                                                                \
+    rmsnorm_bwd_reg_kernel<CH><<<grid, 256, smem, s>>>(                                                    \
+        (const __nv_bfloat16*)dy, lddy, (const __nv_bfloat16*)x, ldx, (const __nv_bfloat16*)w, rstd,      \
+        (const __nv_bfloat16*)dres, lddres, (__nv_bfloat16*)dx, lddx, dw_acc, rows, rpb);                 \
+    break;
+    switch (cols / 256) {
+      PB_RMS_BWD(1) PB_RMS_BWD(2) PB_RMS_BWD(3) PB_RMS_BWD(4) PB_RMS_BWD(5) PB_RMS_BWD(6) PB_RMS_BWD(7)
+      PB_RMS_BWD(8)
+    }
+#undef PB_RMS_BWD
+    PB_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   rmsnorm_bwd_kernel<<<grid, 256, smem, s>>>((const __nv_bfloat16*)dy, lddy, (const __nv_bfloat16*)x,
                                              ldx, (const __nv_bfloat16*)w, rstd, (__nv_bfloat16*)dx,
-                                             lddx, dw_acc, rows, cols, rpb);
+                                             lddx, dw_acc, rows, cols, rpb, (const __nv_bfloat16*)dres,
+                                             lddres);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -286,8 +376,8 @@ void qknorm_rope_fwd(const void* qkv, int64_t ldqkv, const void* qw, const void*
                      cudaStream_t s) {
   PB_CHECK(D == 128, "qknorm_rope: head_dim 128 only");
   const int items = T * (nq + nkv);
-  const int warps = 8;
-  qknorm_rope_fwd_kernel<<<(items + warps - 1) / warps, warps * 32, 0, s>>>(
+  const int per_block = 16;  // 8 warps x 2 items
+  qknorm_rope_fwd_kernel<<<(items + per_block - 1) / per_block, 256, 0, s>>>(
       (const __nv_bfloat16*)qkv, ldqkv, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw,
       (const __nv_bfloat16*)cos, (const __nv_bfloat16*)sin, (__nv_bfloat16*)q_out, ldq,
       (__nv_bfloat16*)k_out, ldk, rstd, T, S, nq, nkv, eps);

@@ -13,9 +13,11 @@ namespace pb {
 void rmsnorm_fwd(const void* x, int64_t ldx, const void* w, void* y, int64_t ldy, float* rstd,
                  int rows, int cols, float eps, cudaStream_t s);
 // dx = rstd * (w*dy - xhat * mean(w*dy*xhat)); dw_acc(f32) += sum_rows dy * bf16(xhat)
+// dres (optional, bf16 [rows, cols]) is added into dx: the residual-stream
+// gradient of "x feeds both norm(x) and a residual add".
 void rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const void* w,
                  const float* rstd, void* dx, int64_t lddx, float* dw_acc, int rows, int cols,
-                 cudaStream_t s);
+                 cudaStream_t s, const void* dres = nullptr, int64_t lddres = 0);
 
 // ---- per-head RMSNorm of q and k + rotate-half RoPE (norm.cu)
 // qkv: [T, (nq + 2*nkv) * D] (row stride ldqkv); writes q_out [T, nq*D],

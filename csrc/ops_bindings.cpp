@@ -33,11 +33,19 @@ void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const 
 }
 
 void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd,
-                 at::Tensor& dx, const c10::optional<at::Tensor>& dw) {
+                 at::Tensor& dx, const c10::optional<at::Tensor>& dw, const c10::optional<at::Tensor>& dres) {
   CHECK_BF16(dy); CHECK_BF16(x); CHECK_BF16(w); CHECK_BF16(dx); CHECK_F32(rstd);
   const c10::cuda::CUDAGuard g(x.device());
+  const void* rp = nullptr;
+  int64_t ldr = 0;
+  if (dres.has_value() && dres->defined()) {
+    CHECK_BF16(*dres);
+    TORCH_CHECK(dres->size(0) == x.size(0) && dres->size(1) == x.size(1), "rmsnorm_bwd: dres shape");
+    rp = dres->data_ptr();
+    ldr = dres->stride(0);
+  }
   pb::rmsnorm_bwd(dy.data_ptr(), dy.stride(0), x.data_ptr(), x.stride(0), w.data_ptr(), rstd.data_ptr<float>(),
-                  dx.data_ptr(), dx.stride(0), opt_f32(dw), x.size(0), x.size(1), cur_stream());
+                  dx.data_ptr(), dx.stride(0), opt_f32(dw), x.size(0), x.size(1), cur_stream(), rp, ldr);
 }
 
 void qknorm_rope_fwd(const at::Tensor& qkv, const at::Tensor& qw, const at::Tensor& kw, const at::Tensor& cos,
@@ -217,7 +225,7 @@ void register_ops(pybind11::module& m) {
   namespace py = pybind11;
   m.def("rmsnorm_fwd", &rmsnorm_fwd, py::arg("x"), py::arg("w"), py::arg("y"), py::arg("rstd"), py::arg("eps"));
   m.def("rmsnorm_bwd", &rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dx"),
-        py::arg("dw"));
+        py::arg("dw"), py::arg("dres") = py::none());
   m.def("qknorm_rope_fwd", &qknorm_rope_fwd);
   m.def("qknorm_rope_bwd", &qknorm_rope_bwd);
   m.def("swiglu_bwd", &swiglu_bwd);

@@ -21,7 +21,7 @@ namespace {
 
 constexpr int kMaxSegs = 48;
 constexpr int kThreads = 256;
-constexpr int kChunk = 4096;  // elements per block-chunk
+constexpr int kChunk = 8192;  // elements per block-chunk (multiple of 8 * kThreads)
 
 struct SegTable {
   AdamSeg seg[kMaxSegs];
@@ -56,6 +56,48 @@ __device__ __forceinline__ int find_seg(const int* starts, int nseg, int chunk) 
   return s;
 }
 
+template <typename T>
+__device__ __forceinline__ void ld8(const void* base, int64_t i, float* v) {
+  if constexpr (sizeof(T) == 4) {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i);
+    float4 a = p[0], b = p[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(base) + i);
+    const uint32_t* q = &u.x;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float2 f = unpack_bf16x2(q[k]);
+      v[2 * k] = f.x;
+      v[2 * k + 1] = f.y;
+    }
+  }
+}
+template <typename T>
+__device__ __forceinline__ void st8(void* base, int64_t i, const float* v) {
+  if constexpr (sizeof(T) == 4) {
+    float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + i);
+    p[0] = make_float4(v[0], v[1], v[2], v[3]);
+    p[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    uint4 u;
+    u.x = pack_bf16x2(v[0], v[1]);
+    u.y = pack_bf16x2(v[2], v[3]);
+    u.z = pack_bf16x2(v[4], v[5]);
+    u.w = pack_bf16x2(v[6], v[7]);
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(base) + i) = u;
+  }
+}
+
+__device__ __forceinline__ void adam_elem(float& p, float& m, float& v, float g, float lr, float wd, float beta1,
+                                          float beta2, float eps, float step_size, float bc2_sqrt) {
+  p *= 1.f - lr * wd;
+  m += (g - m) * (1.f - beta1);
+  v = v * beta2 + (1.f - beta2) * g * g;
+  const float denom = sqrtf(v) / bc2_sqrt + eps;
+  p -= step_size * m / denom;
+}
+
 template <typename GT, typename ST>
 __global__ void __launch_bounds__(kThreads) adamw_kernel(SegTable tab, float lr, float beta1,
                                                          float beta2, float eps, float wd,
@@ -70,19 +112,32 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(SegTable tab, float lr,
   const int64_t base = (int64_t)(chunk - tab.chunk_start[si]) * kChunk;
   const int64_t end = min(sg.n, base + kChunk);
   const float step_size = lr / bc1;
-  for (int64_t i = base + threadIdx.x; i < end; i += kThreads) {
-    const float g = ldf<GT>(sg.g, i) * gs;
-    float p = ldf<__nv_bfloat16>(sg.p, i);
-    float m = ldf<ST>(sg.m, i);
-    float v = ldf<ST>(sg.v, i);
-    p *= 1.f - lr * wd;
-    m += (g - m) * (1.f - beta1);
-    v = v * beta2 + (1.f - beta2) * g * g;
-    const float denom = sqrtf(v) / bc2_sqrt + eps;
-    p -= step_size * m / denom;
-    stf<__nv_bfloat16>(sg.p, i, p);
-    stf<ST>(sg.m, i, m);
-    stf<ST>(sg.v, i, v);
+  const bool vec = ((reinterpret_cast<uintptr_t>(sg.p) | reinterpret_cast<uintptr_t>(sg.g) |
+                     reinterpret_cast<uintptr_t>(sg.m) | reinterpret_cast<uintptr_t>(sg.v)) & 31) == 0;
+  int64_t i = base;
+  if (vec) {
+    // 8 elements per thread per step (kChunk is a multiple of 8 * kThreads)
+    const int64_t vend = base + ((end - base) / 8) * 8;
+    for (int64_t j = base + threadIdx.x * 8; j < vend; j += kThreads * 8) {
+      float g[8], p[8], m[8], v[8];
+      ld8<GT>(sg.g, j, g);
+      ld8<__nv_bfloat16>(sg.p, j, p);
+      ld8<ST>(sg.m, j, m);
+      ld8<ST>(sg.v, j, v);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) adam_elem(p[k], m[k], v[k], g[k] * gs, lr, wd, beta1, beta2, eps, step_size, bc2_sqrt);
+      st8<__nv_bfloat16>(sg.p, j, p);
+      st8<ST>(sg.m, j, m);
+      st8<ST>(sg.v, j, v);
+    }
+    i = vend;
+  }
+  for (int64_t j = i + threadIdx.x; j < end; j += kThreads) {
+    float p = ldf<__nv_bfloat16>(sg.p, j), m = ldf<ST>(sg.m, j), v = ldf<ST>(sg.v, j);
+    adam_elem(p, m, v, ldf<GT>(sg.g, j) * gs, lr, wd, beta1, beta2, eps, step_size, bc2_sqrt);
+    stf<__nv_bfloat16>(sg.p, j, p);
+    stf<ST>(sg.m, j, m);
+    stf<ST>(sg.v, j, v);
   }
 }
 

@@ -110,6 +110,14 @@ PRESETS: dict[str, dict[str, Any]] = {
                                num_key_value_heads=4, head_dim=128, num_experts=128, num_experts_per_tok=8,
                                moe_intermediate_size=768, norm_topk_prob=True, router_aux_loss_coef=0.001,
                                tie_word_embeddings=False, max_position_embeddings=40960),
+    # small configs with head_dim 128 (the attention kernels' head size) for GPU tests
+    "small-qwen3": dict(model_type="qwen3", vocab_size=2048, hidden_size=256, intermediate_size=512,
+                        num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2, head_dim=128,
+                        tie_word_embeddings=True),
+    "small-qwen3-moe": dict(model_type="qwen3_moe", vocab_size=2048, hidden_size=256, intermediate_size=512,
+                            num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2, head_dim=128,
+                            num_experts=8, num_experts_per_tok=2, moe_intermediate_size=128, norm_topk_prob=True,
+                            tie_word_embeddings=False, output_router_logits=True),
     # tiny configs for tests
     "tiny-qwen3": dict(model_type="qwen3", vocab_size=1024, hidden_size=256, intermediate_size=512,
                        num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2, head_dim=64,

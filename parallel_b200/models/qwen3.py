@@ -111,11 +111,11 @@ class Attention(nn.Module):
         self.q_norm = RMSNorm(D, cfg.rms_norm_eps)
         self.k_norm = RMSNorm(D, cfg.rms_norm_eps)
 
-    def core(self, h, inv_freq, B, S):
+    def core(self, h, inv_freq, B, S, stash=None):
         """Attention output before o_proj: [B*S, heads*D]."""
         return Fx.attention_block(h, self.q_proj.weight, self.k_proj.weight, self.v_proj.weight,
                                   self.q_norm.weight, self.k_norm.weight, inv_freq, B, S, self.num_heads,
-                                  self.num_kv_heads, self.head_dim, self.eps)
+                                  self.num_kv_heads, self.head_dim, self.eps, stash)
 
 
 class MLP(nn.Module):
@@ -198,17 +198,21 @@ class DecoderLayer(nn.Module):
         """x: [B, S_local, H] (S_local = S / tp under sequence parallelism)."""
         ctx = self._ctx
         B, S = self._seq
-        h = self.input_layernorm(x)
+        stash = getattr(self, "_attn_stash", None)
         if ctx.tp_size > 1:
+            h = self.input_layernorm(x)
             h = ctx.comm.gather_sequence(h, ctx) if ctx.sp else ctx.comm.copy_to_tp(h, ctx)
-        o = self.self_attn.core(h, self._inv_freq, B, S)
-        if ctx.tp_size > 1:
+            o = self.self_attn.core(h, self._inv_freq, B, S, stash)
             y = self.self_attn.o_proj(o).view(B, S, -1)
             y = ctx.comm.reduce_scatter_sequence(y, ctx) if ctx.sp else ctx.comm.reduce_from_tp(y, ctx)
             x = x + y
+            h = self.post_attention_layernorm(x)
         else:
-            x = self.self_attn.o_proj(o, residual=x)
-        h = self.post_attention_layernorm(x)
+            x_res, h = Fx.residual_rms_norm(x, self.input_layernorm.weight, self.input_layernorm.variance_epsilon)
+            o = self.self_attn.core(h, self._inv_freq, B, S, stash)
+            x = self.self_attn.o_proj(o, residual=x_res)
+            x, h = Fx.residual_rms_norm(x, self.post_attention_layernorm.weight,
+                                        self.post_attention_layernorm.variance_epsilon)
         if self.is_moe:
             return x + self.mlp(h, ctx, self._router_sink)
         if ctx.tp_size > 1:

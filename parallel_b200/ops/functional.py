@@ -128,13 +128,57 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     return _rms_ref(x, w, eps)
 
 
+class _ResidualRMSNormFn(torch.autograd.Function):
+    """(x, norm(x)) for a residual stream that feeds both a norm and a later
+    residual add; the backward sums both gradients inside the norm kernel."""
+
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        y = torch.empty_like(x2)
+        rstd = torch.empty(x2.shape[0], device=x.device, dtype=torch.float32)
+        ext().rmsnorm_fwd(x2, w, y, rstd, eps)
+        ctx.save_for_backward(x2, w, rstd)
+        ctx.shape = shape
+        return x.view_as(x), y.view(shape)
+
+    @staticmethod
+    def backward(ctx, dres, dy):
+        x2, w, rstd = ctx.saved_tensors
+        H = x2.shape[1]
+        dx = torch.empty_like(x2)
+        dw = torch.zeros(H, device=x2.device, dtype=torch.float32)
+        if dy is None:
+            return dres, None, None
+        dy2 = dy.reshape(-1, H)
+        if not dy2.is_contiguous():
+            dy2 = dy2.contiguous()
+        r2 = None
+        if dres is not None:
+            r2 = dres.reshape(-1, H)
+            if not r2.is_contiguous():
+                r2 = r2.contiguous()
+        ext().rmsnorm_bwd(dy2, x2, w, rstd, dx, dw, r2)
+        return dx.view(ctx.shape), dw.to(w.dtype), None
+
+
+def residual_rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float):
+    """Returns (x, norm(x)); use the first output for the residual add."""
+    if x.is_cuda:
+        return _ResidualRMSNormFn.apply(x, w, eps)
+    return x, _rms_ref(x, w, eps)
+
+
 # ----------------------------------------------------------------- attention block
 class _AttentionFn(torch.autograd.Function):
     """qkv = h W_qkv^T -> per-head q/k RMSNorm + RoPE -> causal GQA flash
     attention.  Returns the attention output [T, nq*D] (before o_proj)."""
 
     @staticmethod
-    def forward(ctx, h, wq, wk, wv, qw, kw, cos, sin, B, S, nq, nkv, D, eps):
+    def forward(ctx, h, wq, wk, wv, qw, kw, cos, sin, B, S, nq, nkv, D, eps, stash=None):
         T = B * S
         wqkv = fused_rows(wq, wk, wv)
         qkv = G.linear(h.reshape(T, -1), wqkv)
@@ -143,9 +187,16 @@ class _AttentionFn(torch.autograd.Function):
         rstd = torch.empty(T, nq + nkv, device=h.device, dtype=torch.float32)
         ext().qknorm_rope_fwd(qkv, qw, kw, cos, sin, q, k, rstd, S, nq, nkv, eps)
         v = qkv[:, (nq + nkv) * D:]
-        o = torch.empty(T, nq * D, device=h.device, dtype=h.dtype)
-        lse = torch.zeros(B * nq * S + 128, device=h.device, dtype=torch.float32)
-        ext().attn_fwd(q, k, v, o, lse, B, S, nq, nkv, 1.0 / math.sqrt(D), True)
+        if stash is not None and stash.get("mode") == "reuse" and "o" in stash:
+            # activation-checkpoint recompute: the attention output and its
+            # log-sum-exp were kept from the forward pass (same inputs, same result)
+            o, lse = stash.pop("o"), stash.pop("lse")
+        else:
+            o = torch.empty(T, nq * D, device=h.device, dtype=h.dtype)
+            lse = torch.zeros(B * nq * S + 128, device=h.device, dtype=torch.float32)
+            ext().attn_fwd(q, k, v, o, lse, B, S, nq, nkv, 1.0 / math.sqrt(D), True)
+            if stash is not None and stash.get("mode") == "save":
+                stash["o"], stash["lse"] = o, lse
         ctx.save_for_backward(h, wq, wk, wv, qw, kw, cos, sin, qkv, q, k, o, lse, rstd)
         ctx.dims = (B, S, nq, nkv, D)
         return o
@@ -172,14 +223,18 @@ class _AttentionFn(torch.autograd.Function):
         dh = G.linear_dgrad(dqkv, wqkv).view(h.shape)
         dw = G.linear_wgrad(dqkv, h2)
         gq, gk, gv = _split_rows(dw, (wq.shape[0], wk.shape[0], wv.shape[0]))
-        return dh, gq, gk, gv, dqw.to(qw.dtype), dkw.to(kw.dtype), None, None, None, None, None, None, None, None
+        return dh, gq, gk, gv, dqw.to(qw.dtype), dkw.to(kw.dtype), None, None, None, None, None, None, None, None, None
 
 
-def attention_block(h, wq, wk, wv, q_norm_w, k_norm_w, inv_freq, B, S, nq, nkv, D, eps):
-    """Self-attention up to (not including) o_proj: returns [B*S, nq*D]."""
+def attention_block(h, wq, wk, wv, q_norm_w, k_norm_w, inv_freq, B, S, nq, nkv, D, eps, stash=None):
+    """Self-attention up to (not including) o_proj: returns [B*S, nq*D].
+
+    ``stash`` (CUDA path): a dict with mode "save" keeps the attention output
+    and log-sum-exp; mode "reuse" consumes them instead of recomputing the
+    attention kernel (selective recompute under activation checkpointing)."""
     if h.is_cuda:
         cos, sin = rope_tables(inv_freq, S, h.dtype, h.device)
-        return _AttentionFn.apply(h, wq, wk, wv, q_norm_w, k_norm_w, cos, sin, B, S, nq, nkv, D, eps)
+        return _AttentionFn.apply(h, wq, wk, wv, q_norm_w, k_norm_w, cos, sin, B, S, nq, nkv, D, eps, stash)
     cos, sin = rope_tables(inv_freq, S, h.dtype, h.device)
     x = h.reshape(B, S, -1)
     q = F.linear(x, wq).view(B, S, nq, D)

@@ -66,8 +66,13 @@ class _UnitFn(torch.autograd.Function):
         if unit.next_fwd is not None:
             unit.next_fwd.prefetch()
         if unit.use_activation_checkpoint:
+            # selective recompute: the layer keeps its attention output from
+            # this pass and reuses it when it is recomputed in backward
+            unit.module._attn_stash = {"mode": "save"} if wrapper.keep_attention_output else None
             with torch.no_grad():
                 y, extras = _run_layer(unit, fwd, x, args)
+            ctx.stash = unit.module._attn_stash
+            unit.module._attn_stash = None
             ctx.save_for_backward(x)
             ctx.inner = None
         else:
@@ -92,8 +97,16 @@ class _UnitFn(torch.autograd.Function):
         if ctx.inner is None:
             (x,) = ctx.saved_tensors
             xi = x.detach().requires_grad_(True)
-            with torch.enable_grad():
-                y, extras = _run_layer(unit, ctx.fwd, xi, ctx.args)
+            stash = getattr(ctx, "stash", None)
+            if stash is not None:
+                stash["mode"] = "reuse"
+            unit.module._attn_stash = stash
+            try:
+                with torch.enable_grad():
+                    y, extras = _run_layer(unit, ctx.fwd, xi, ctx.args)
+            finally:
+                unit.module._attn_stash = None
+                ctx.stash = None
         else:
             xi, y, extras = ctx.inner
         ctx.inner = None
@@ -129,6 +142,9 @@ class FSDPWrapper:
         first = next(model.parameters(), None)
         self.device = device or (first.device if first is not None else torch.device("cpu"))
         self.collectives_kind = collectives
+        # under activation checkpointing keep each layer's attention output
+        # (and log-sum-exp) so the backward recompute skips the attention kernel
+        self.keep_attention_output = True
         self.units: list[DPParamUnit] = []
         self.root_units: list[DPParamUnit] = []
         self.dp_shard_group = None
