@@ -44,6 +44,7 @@ struct AttnBwdParams {
   int B, S, nq, nkv, D;
   float scale;
   bool causal;
+  long long* trace = nullptr;  // optional per-CTA phase timing [grid * 16]
 };
 
 void attention_bwd(const AttnBwdParams& p, cudaStream_t s);

@@ -53,7 +53,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float* __restrict__ LSE, const float* __restrict__ DELTA,
                     float* __restrict__ dq_acc, int64_t ld_dqacc, __nv_bfloat16* __restrict__ dK,
                     int64_t lddk, __nv_bfloat16* __restrict__ dV, int64_t lddv, int B, int S, int nq,
-                    int nkv, float scale, bool causal, int* err) {
+                    int nkv, float scale, bool causal, int* err, long long* trace) {
+  // optional per-CTA phase timing (clock64 cycles), slots documented at the use sites
+  long long tacc[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) tacc[i] = 0;
+  auto tw = [&](int slot, uint64_t* bar, uint32_t par) -> bool {
+    if (!trace) return mbar_wait(bar, par, err);
+    const long long t0 = clock64();
+    const bool r = mbar_wait(bar, par, err);
+    tacc[slot] += clock64() - t0;
+    return r;
+  };
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -146,14 +157,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int i = i0 + it % (n_t - i0);
         const int st = it & 1;
         const uint32_t ph = ((it >> 1) & 1) ^ 1;
-        if (!mbar_wait(&q_empty[st], ph, err)) break;
+        if (!tw(15, &q_empty[st], ph)) break;
         mbar_arrive_expect_tx(&q_full[st], TILE + 1024);
         for (int a = 0; a < 2; ++a)
           tma_load_3d(sQ + st * TILE + a * (TILE / 2), &tmQ, &q_full[st], h * HD + a * 64, i * BT, b);
         const int64_t row0 = ((int64_t)b * nq + h) * S + (int64_t)i * BT;  // 16B aligned: S % 8 == 0
         bulk_load(s_lse + st * 128, LSE + row0, 512, &q_full[st]);
         bulk_load(s_delta + st * 128, DELTA + row0, 512, &q_full[st]);
-        if (!mbar_wait(&do_empty[st], ph, err)) break;
+        if (!tw(15, &do_empty[st], ph)) break;
         mbar_arrive_expect_tx(&do_full[st], TILE);
         for (int a = 0; a < 2; ++a)
           tma_load_3d(sdO + st * TILE + a * (TILE / 2), &tmdO, &do_full[st], h * HD + a * 64, i * BT, b);
@@ -166,12 +177,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t id_mm = idesc_bf16(128, 128, true, true);    // both MN-major
       const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV), pds_base = smem_u32(sPdS);
       bool ok = mbar_wait(kv_full, 0, err);
+      const long long t_mma0 = clock64();
       for (int it = 0; it < n_iter && ok; ++it) {
         const int st = it & 1;
         const uint32_t ph = it & 1;
         const uint32_t q_base = smem_u32(sQ + st * TILE), do_base = smem_u32(sdO + st * TILE);
-        if (!mbar_wait(&q_full[st], (it >> 1) & 1, err) || !mbar_wait(&do_full[st], (it >> 1) & 1, err) ||
-            !mbar_wait(s_empty, ph ^ 1, err)) { ok = false; break; }
+        if (!tw(0, &q_full[st], (it >> 1) & 1) || !tw(0, &do_full[st], (it >> 1) & 1) ||
+            !tw(0, s_empty, ph ^ 1)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // S^T = K Q^T   (K = head dim)
@@ -180,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       id_kk, kk > 0);
         }
         mma_commit(s_full);
-        if (!mbar_wait(dq_empty, ph ^ 1, err)) { ok = false; break; }
+        if (!tw(1, dq_empty, ph ^ 1)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // dP^T = V dO^T
@@ -189,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       id_kk, kk > 0);
         }
         mma_commit(dp_full);
-        if (!mbar_wait(p_full, ph, err)) { ok = false; break; }
+        if (!tw(2, p_full, ph)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // dV += P^T dO   (K = queries)
@@ -198,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       smem_desc_sw128(do_base + kk * 2048, TILE / 2, 1024), id_km, (it > 0 || kk > 0));
         }
         mma_commit(dv_done);
-        if (!mbar_wait(ds_full, ph, err)) { ok = false; break; }
+        if (!tw(3, ds_full, ph)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // dK += dS^T Q   (K = queries)
@@ -216,6 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(pds_free);
         mma_commit(dq_full);
       }
+      if (trace) tacc[4] = clock64() - t_mma0;
       if (ok) mma_commit(kv_done);
       else {
         mma_commit(drain);
@@ -231,17 +244,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const float scale_log2 = scale * kLog2e;
     bool ok = true;
+    const long long t_loop0 = clock64();
+    long long tm = 0;
     for (int it = 0; it < n_iter; ++it) {
       const int h = kvh * G + it / (n_t - i0);
       const int i = i0 + it % (n_t - i0);
       const uint32_t ph = it & 1;
       const int st = it & 1;
       // lse / delta of query tile i arrive with Q_i (bulk copies on q_full)
-      if (!mbar_wait(&q_full[st], (it >> 1) & 1, err)) { ok = false; break; }
+      if (!tw(5, &q_full[st], (it >> 1) & 1)) { ok = false; break; }
       const float* lse_t = s_lse + st * 128;
       const float* delta_t = s_delta + st * 128;
-      if (!mbar_wait(s_full, ph, err)) { ok = false; break; }
+      if (!tw(6, s_full, ph)) { ok = false; break; }
       tc_fence_after();
+      if (trace) tm = clock64();
       float p[128];
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(tS + lane_off + c * 32, p + c * 32);
@@ -255,7 +271,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if ((diag && kpos > i * BT + c) || kpos >= S || i * BT + c >= S) x = 0.f;
         p[c] = x;
       }
-      if (!mbar_wait(pds_free, ph ^ 1, err)) { ok = false; break; }
+      if (trace) tacc[7] += clock64() - tm;
+      if (!tw(8, pds_free, ph ^ 1)) { ok = false; break; }
+      if (trace) tm = clock64();
       // P^T -> smem (row = key, 128 queries in two 64-wide swizzled atoms)
 #pragma unroll
       for (int a = 0; a < 2; ++a) {
@@ -274,8 +292,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
-      if (!mbar_wait(dp_full, ph, err) || !mbar_wait(dv_done, ph, err)) { ok = false; break; }
+      if (trace) tacc[9] += clock64() - tm;
+      if (!tw(10, dp_full, ph) || !tw(10, dv_done, ph)) { ok = false; break; }
       tc_fence_after();
+      if (trace) tm = clock64();
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float dp[32];
@@ -304,8 +324,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(ds_full);
-      if (!mbar_wait(dq_full, ph, err)) { ok = false; break; }
+      if (trace) tacc[11] += clock64() - tm;
+      if (!tw(12, dq_full, ph)) { ok = false; break; }
       tc_fence_after();
+      if (trace) tm = clock64();
       {
         const int q = i * BT + r;  // dQ lane = query row
         float* dst = dq_acc + ((int64_t)b * S + q) * ld_dqacc + (int64_t)h * HD;
@@ -323,7 +345,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(dq_empty);
+      if (trace) tacc[13] += clock64() - tm;
     }
+    if (trace) tacc[14] = clock64() - t_loop0;
     if (ok && mbar_wait(kv_done, 0, err)) {
       tc_fence_after();
       const bool valid = kpos < S;
@@ -349,6 +373,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+  }
+  if (trace && (threadIdx.x == 0 || threadIdx.x == 32 || threadIdx.x == 64)) {
+    long long* dst = trace + (int64_t)blockIdx.x * 16;
+    for (int i = 0; i < 16; ++i)
+      if (tacc[i]) atomicAdd(reinterpret_cast<unsigned long long*>(dst + i), (unsigned long long)tacc[i]);
   }
   tc_fence_before();
   __syncthreads();
@@ -424,7 +453,8 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   const int grid = p.B * p.nkv * n_t;
   attn_bwd_kernel<<<grid, kThreads, SMEM_BYTES, s>>>(tq, tk, tv, tdo, p.lse, p.delta, p.dq_acc, ld_acc,
                                                      (__nv_bfloat16*)p.dk, p.lddk, (__nv_bfloat16*)p.dv, p.lddv,
-                                                     p.B, p.S, p.nq, p.nkv, p.scale, p.causal, error_word());
+                                                     p.B, p.S, p.nq, p.nkv, p.scale, p.causal, error_word(),
+                                                     p.trace);
   PB_CUDA_CHECK(cudaGetLastError());
   const int64_t cast_work = (int64_t)T * ld_acc / 4;
   int cgrid = (int)std::min<int64_t>((cast_work + 255) / 256, (int64_t)num_sms() * 16);
@@ -578,7 +608,7 @@ extern "C" __attribute__((visibility("default"))) int pb_attention_bwd_noalloc(
     const int n_t = (S + BT - 1) / BT;
     attn_bwd_kernel<<<B * nkv * n_t, kThreads, SMEM_BYTES, stream>>>(
         tq, tk, tv, tdo, lse_pad, delta, dq_acc, ld_acc, (__nv_bfloat16*)dk, lddk, (__nv_bfloat16*)dv, lddv, B, S,
-        nq, nkv, scale, causal != 0, err);
+        nq, nkv, scale, causal != 0, err, nullptr);
     PB_CUDA_CHECK(cudaGetLastError());
     int sms = 0;
     PB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));

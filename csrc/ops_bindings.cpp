@@ -199,7 +199,7 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
 void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
               const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq_acc, at::Tensor& dq,
               at::Tensor& dk, at::Tensor& dv, int64_t B, int64_t S, int64_t nq, int64_t nkv, double scale,
-              bool causal) {
+              bool causal, const c10::optional<at::Tensor>& trace) {
   CHECK_BF16(q); CHECK_BF16(k); CHECK_BF16(v); CHECK_BF16(o); CHECK_BF16(dout); CHECK_BF16(dq); CHECK_BF16(dk);
   CHECK_BF16(dv); CHECK_F32(lse); CHECK_F32(delta); CHECK_F32(dq_acc);
   const int64_t D = q.size(1) / nq;
@@ -216,6 +216,10 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   p.lddq = dq.stride(0); p.lddk = dk.stride(0); p.lddv = dv.stride(0);
   p.B = (int)B; p.S = (int)S; p.nq = (int)nq; p.nkv = (int)nkv; p.D = (int)D; p.scale = (float)scale;
   p.causal = causal;
+  if (trace.has_value() && trace->defined()) {
+    TORCH_CHECK(trace->scalar_type() == at::kLong && trace->is_cuda(), "trace must be a CUDA int64 tensor");
+    p.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
+  }
   pb::attention_bwd(p, cur_stream());
 }
 
@@ -239,5 +243,8 @@ void register_ops(pybind11::module& m) {
   m.def("sumsq", &sumsq);
   m.def("clip_coef", &clip_coef);
   m.def("attn_fwd", &attn_fwd);
-  m.def("attn_bwd", &attn_bwd);
+  m.def("attn_bwd", &attn_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("dout"),
+        py::arg("lse"), py::arg("delta"), py::arg("dq_acc"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("B"),
+        py::arg("S"), py::arg("nq"), py::arg("nkv"), py::arg("scale"), py::arg("causal"),
+        py::arg("trace") = py::none());
 }
