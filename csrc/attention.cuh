@@ -35,8 +35,8 @@ struct AttnBwdParams {
   const void* o;
   const void* dout;
   const float* lse;
-  float* delta;  // [B*nq, S] scratch: rowsum(dO * O)
-  float* dq_acc; // [B*S, nq*D] fp32 scratch (zeroed by the launcher)
+  float* delta;   // scratch of 2 * (B*nq*S + 128) floats: delta*scale, lse*log2(e)
+  float* dq_acc;  // [B*S, nq*D] fp32 scratch (zeroed by the launcher), 16-byte aligned
   void* dq;
   void* dk;
   void* dv;
@@ -44,8 +44,10 @@ struct AttnBwdParams {
   int B, S, nq, nkv, D;
   float scale;
   bool causal;
-  long long* trace = nullptr;  // optional per-CTA phase timing [grid * 16]
+  long long* trace = nullptr;  // optional per-CTA phase timing [grid * kAttnBwdTraceSlots]
 };
+
+constexpr int kAttnBwdTraceSlots = 24;
 
 void attention_bwd(const AttnBwdParams& p, cudaStream_t s);
 

@@ -5,15 +5,26 @@
 // Per (head, i), with K_j / V_j resident in shared memory:
 //   S^T  = K_j Q_i^T            -> TMEM cols [  0,128)  (lane = key)
 //   dP^T = V_j dO_i^T           -> TMEM cols [128,256)
-//   P^T  = exp(S^T*scale - lse) -> smem (bf16)              [elementwise warps]
+//   P^T  = exp2(S^T*scale*log2e - lse*log2e) -> smem (bf16)   [element warps]
 //   dV  += P^T dO_i             -> TMEM cols [256,384)
-//   dS^T = P^T (dP^T - delta) * scale -> smem (same buffer, after dV read P)
-//   dK  += dS^T Q_i             -> TMEM cols [384,512)
+//   dS^T = P^T (dP^T*scale - delta*scale) -> smem (same buffer, after dV read P)
 //   dQ_i = dS K_j               -> TMEM cols [128,256)  (dP^T is consumed by then)
-// dQ_i is added into an fp32 accumulator with vector atomics; dK / dV leave
-// TMEM once at the end.  Every operand tile is loaded once in the K-major
-// 128B-swizzled layout and re-read as MN-major where a product needs its
-// transpose (same bytes, different descriptor strides).
+//   dK  += dS^T Q_i             -> TMEM cols [384,512)
+// dQ_i leaves TMEM through a shared staging buffer and a bulk tensor
+// reduce-add (the fp32 add happens in L2) issued by its own warpgroup; dK / dV
+// leave TMEM once at the end.  Every operand tile is loaded once in the
+// K-major 128B-swizzled layout and re-read as MN-major where a product needs
+// its transpose (same bytes, different descriptor strides).
+//
+// Warpgroups (512 threads): 0 = TMA producer (warp 0) and MMA issuer (warp 1);
+// 1 and 2 = element warps, warpgroup 1+g handling query columns [64g, 64g+64)
+// of S^T / dP^T; 3 = dQ drain (TMEM -> shared stage -> bulk reduce-add).  A
+// warp reads the TMEM lane quarter warp % 4.  setmaxnreg moves registers from
+// warpgroups 0 and 3 to the element warpgroups.
+//
+// A prep kernel computes delta*scale = rowsum(dO*O)*scale and lse*log2e into
+// one scratch array and zeroes the dQ accumulator; a cast kernel turns the
+// accumulator into bf16 dq afterwards.
 //
 // Replaces the autograd of HF's SDPA call in the reference
 // (parallel/parallel/engine/model_loading.py:22).
@@ -33,12 +44,18 @@ namespace {
 
 constexpr int BT = 128;   // tile rows (queries or keys)
 constexpr int HD = 128;
-constexpr int kThreads = 192;
-constexpr int TILE = 128 * HD * 2;  // 32 KB
-// 7 tiles + double-buffered lse/delta (2 x 1 KB) + 21 barriers + TMEM slot.
-constexpr int SMALL_BYTES = 2048 + 22 * 8;
+constexpr int kThreads = 512;  // 4 warpgroups
+// setmaxnreg split: 128 registers a thread at launch (65536 / 512); the sum
+// over the four warpgroups must stay 4 x 128.
+constexpr int kRegsCtl = 56, kRegsElem = 168, kRegsDq = 120;
+static_assert(kRegsCtl + 2 * kRegsElem + kRegsDq == 4 * 128, "attention bwd: register split");
+constexpr int TILE = 128 * HD * 2;   // 32 KB bf16 operand tile
+constexpr int STAGE = 128 * 32 * 4;  // 16 KB: one 128 x 32 fp32 dQ chunk
+// K, V, Q x2, dO, P/dS + two dQ stages + double-buffered lse2/delta (2 KB)
+// + barriers + TMEM slot.
+constexpr int SMALL_BYTES = 2048 + 24 * 8;
 constexpr int SMEM_BYTES = 232448;  // the sm_100 per-block maximum
-static_assert(7 * TILE + SMALL_BYTES <= SMEM_BYTES, "attention bwd: smem budget");
+static_assert(6 * TILE + 2 * STAGE + SMALL_BYTES <= SMEM_BYTES, "attention bwd: smem budget");
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ float ex2(float x) {
@@ -47,61 +64,71 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+template <bool kTrace>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
-                    const float* __restrict__ LSE, const float* __restrict__ DELTA,
-                    float* __restrict__ dq_acc, int64_t ld_dqacc, __nv_bfloat16* __restrict__ dK,
-                    int64_t lddk, __nv_bfloat16* __restrict__ dV, int64_t lddv, int B, int S, int nq,
-                    int nkv, float scale, bool causal, int* err, long long* trace) {
-  // optional per-CTA phase timing (clock64 cycles), slots documented at the use sites
-  long long tacc[16];
+                    const __grid_constant__ CUtensorMap tmdQ, const float* __restrict__ LSE2,
+                    const float* __restrict__ DELTA, __nv_bfloat16* __restrict__ dK, int64_t lddk,
+                    __nv_bfloat16* __restrict__ dV, int64_t lddv, int B, int S, int nq, int nkv, float scale,
+                    bool causal, int* err, long long* trace) {
+  // optional per-CTA phase timing (clock64 cycles, kTrace builds only); slots
+  // are documented at the use sites
+  constexpr int kSlots = kTrace ? kAttnBwdTraceSlots : 1;
+  long long tacc[kSlots];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) tacc[i] = 0;
+  for (int i = 0; i < kSlots; ++i) tacc[i] = 0;
   auto tw = [&](int slot, uint64_t* bar, uint32_t par) -> bool {
-    if (!trace) return mbar_wait(bar, par, err);
-    const long long t0 = clock64();
-    const bool r = mbar_wait(bar, par, err);
-    tacc[slot] += clock64() - t0;
-    return r;
+    if constexpr (!kTrace) {
+      return mbar_wait(bar, par, err);
+    } else {
+      const long long t0 = clock64();
+      const bool r = mbar_wait(bar, par, err);
+      tacc[slot] += clock64() - t0;
+      return r;
+    }
   };
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   // The 128B-swizzled tiles need 1024-byte alignment; the budget leaves
-  // SMEM_BYTES - 7*TILE - SMALL_BYTES bytes for it.  Bail out (uniformly,
-  // before any barrier or TMEM use) if the dynamic window is aligned worse.
-  if ((size_t)(smem - smem_raw) + 7 * TILE + SMALL_BYTES > (size_t)SMEM_BYTES) {
+  // SMEM_BYTES - 6*TILE - 2*STAGE - SMALL_BYTES bytes for it.  Bail out
+  // (uniformly, before any barrier or TMEM use) if the window is aligned worse.
+  if ((size_t)(smem - smem_raw) + 6 * TILE + 2 * STAGE + SMALL_BYTES > (size_t)SMEM_BYTES) {
     if (threadIdx.x == 0) record_error(err, kErrBadArg);
     return;
   }
   uint8_t* sK = smem;
   uint8_t* sV = smem + TILE;
-  uint8_t* sQ = smem + 2 * TILE;   // 2 stages
-  uint8_t* sdO = smem + 4 * TILE;  // 2 stages
-  uint8_t* sPdS = smem + 6 * TILE;
-  float* s_lse = reinterpret_cast<float*>(smem + 7 * TILE);  // [2][128]
-  float* s_delta = s_lse + 256;                               // [2][128]
+  uint8_t* sQ = smem + 2 * TILE;  // 2 stages
+  uint8_t* sdO = smem + 4 * TILE;
+  uint8_t* sPdS = smem + 5 * TILE;
+  uint8_t* sStage = smem + 6 * TILE;  // 2 dQ staging buffers
+  float* s_lse = reinterpret_cast<float*>(smem + 6 * TILE + 2 * STAGE);  // [2][128] lse * log2e
+  float* s_delta = s_lse + 256;                                          // [2][128] delta * scale
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_delta + 256);
   uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;    // [2]
-  uint64_t* q_empty = bars + 3;   // [2]
-  uint64_t* do_full = bars + 5;   // [2]
-  uint64_t* do_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;
-  uint64_t* s_empty = bars + 10;
-  uint64_t* dp_full = bars + 11;
-  uint64_t* p_full = bars + 12;
-  uint64_t* dv_done = bars + 13;
-  uint64_t* ds_full = bars + 14;
-  uint64_t* pds_free = bars + 15;
-  uint64_t* dq_full = bars + 16;
-  uint64_t* dq_empty = bars + 17;
-  uint64_t* kv_done = bars + 18;
-  uint64_t* drain = bars + 19;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* q_full = bars + 1;   // [2]
+  uint64_t* q_empty = bars + 3;  // [2]
+  uint64_t* do_full = bars + 5;
+  uint64_t* do_empty = bars + 6;
+  uint64_t* s_full = bars + 7;
+  uint64_t* s_empty = bars + 8;
+  uint64_t* dp_full = bars + 9;
+  uint64_t* p_full = bars + 10;
+  uint64_t* dv_done = bars + 11;
+  uint64_t* ds_full = bars + 12;
+  uint64_t* pds_free = bars + 13;
+  uint64_t* dq_full = bars + 14;
+  uint64_t* dq_empty = bars + 15;
+  uint64_t* kv_done = bars + 16;
+  uint64_t* drain = bars + 17;
+  uint64_t* stage_full = bars + 18;  // [2]
+  uint64_t* stage_free = bars + 20;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wg = warp >> 2;
   const int n_t = (S + BT - 1) / BT;
   const int G = nq / nkv;
   const int j = blockIdx.x / (B * nkv);  // smallest key tile (most work) first
@@ -109,21 +136,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int b = bk / nkv, kvh = bk % nkv;
   const int i0 = causal ? j : 0;
   const int n_iter = G * (n_t - i0);
+  constexpr int kElem = 256;  // two element warpgroups
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
-      mbar_init(&do_full[s], 1);
-      mbar_init(&do_empty[s], 1);
+      mbar_init(&stage_full[s], 128);
+      mbar_init(&stage_free[s], 1);
     }
+    mbar_init(do_full, 1);
+    mbar_init(do_empty, 1);
     mbar_init(s_full, 1);
-    mbar_init(s_empty, 128);
+    mbar_init(s_empty, kElem);
     mbar_init(dp_full, 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, kElem);
     mbar_init(dv_done, 1);
-    mbar_init(ds_full, 128);
+    mbar_init(ds_full, kElem);
     mbar_init(pds_free, 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 128);
@@ -141,8 +171,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 384;
 
-  if (warp == 0) {
-    if (lane == 0) {
+  if (wg == 0) {
+    // ---------------------------------------------------------------- warpgroup 0: TMA (warp 0), MMA (warp 1)
+    regs_decrease<kRegsCtl>();
+    if (warp == 0 && lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
@@ -156,43 +188,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int h = kvh * G + it / (n_t - i0);
         const int i = i0 + it % (n_t - i0);
         const int st = it & 1;
-        const uint32_t ph = ((it >> 1) & 1) ^ 1;
-        if (!tw(15, &q_empty[st], ph)) break;
+        // slot 15: producer waiting for free buffers
+        if (!tw(15, &q_empty[st], ((it >> 1) & 1) ^ 1)) break;
         mbar_arrive_expect_tx(&q_full[st], TILE + 1024);
         for (int a = 0; a < 2; ++a)
           tma_load_3d(sQ + st * TILE + a * (TILE / 2), &tmQ, &q_full[st], h * HD + a * 64, i * BT, b);
         const int64_t row0 = ((int64_t)b * nq + h) * S + (int64_t)i * BT;  // 16B aligned: S % 8 == 0
-        bulk_load(s_lse + st * 128, LSE + row0, 512, &q_full[st]);
+        bulk_load(s_lse + st * 128, LSE2 + row0, 512, &q_full[st]);
         bulk_load(s_delta + st * 128, DELTA + row0, 512, &q_full[st]);
-        if (!tw(15, &do_empty[st], ph)) break;
-        mbar_arrive_expect_tx(&do_full[st], TILE);
+        if (!tw(15, do_empty, (it & 1) ^ 1)) break;
+        mbar_arrive_expect_tx(do_full, TILE);
         for (int a = 0; a < 2; ++a)
-          tma_load_3d(sdO + st * TILE + a * (TILE / 2), &tmdO, &do_full[st], h * HD + a * 64, i * BT, b);
+          tma_load_3d(sdO + a * (TILE / 2), &tmdO, do_full, h * HD + a * 64, i * BT, b);
       }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
       constexpr uint32_t id_kk = idesc_bf16(128, 128, false, false);  // both K-major
       constexpr uint32_t id_km = idesc_bf16(128, 128, false, true);   // A K-major, B MN-major
       constexpr uint32_t id_mm = idesc_bf16(128, 128, true, true);    // both MN-major
       const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV), pds_base = smem_u32(sPdS);
-      bool ok = mbar_wait(kv_full, 0, err);
-      const long long t_mma0 = clock64();
-      for (int it = 0; it < n_iter && ok; ++it) {
+      const uint32_t do_base = smem_u32(sdO);
+      // S^T(it) = K Q_it^T into TMEM cols [0,128); slot 0 = waits for Q / S free
+      auto issue_s = [&](int it) -> bool {
         const int st = it & 1;
-        const uint32_t ph = it & 1;
-        const uint32_t q_base = smem_u32(sQ + st * TILE), do_base = smem_u32(sdO + st * TILE);
-        if (!tw(0, &q_full[st], (it >> 1) & 1) || !tw(0, &do_full[st], (it >> 1) & 1) ||
-            !tw(0, s_empty, ph ^ 1)) { ok = false; break; }
+        if (!tw(0, &q_full[st], (it >> 1) & 1) || !tw(0, s_empty, (it & 1) ^ 1)) return false;
         tc_fence_after();
+        const uint32_t q_base = smem_u32(sQ + st * TILE);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // S^T = K Q^T   (K = head dim)
+        for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * (TILE / 2) + (kk & 3) * 32;
           mma_bf16_ss(tS, smem_desc_sw128(k_base + off, 16, 1024), smem_desc_sw128(q_base + off, 16, 1024),
                       id_kk, kk > 0);
         }
         mma_commit(s_full);
-        if (!tw(1, dq_empty, ph ^ 1)) { ok = false; break; }
+        return true;
+      };
+      bool ok = mbar_wait(kv_full, 0, err) && (n_iter == 0 || issue_s(0));
+      const long long t_mma0 = clock64();
+      for (int it = 0; it < n_iter && ok; ++it) {
+        const int st = it & 1;
+        const uint32_t ph = it & 1;
+        const uint32_t q_base = smem_u32(sQ + st * TILE);
+        // slot 1: dQ(it-1) drained from TMEM, dO(it) loaded
+        if (!tw(1, dq_empty, ph ^ 1) || !tw(1, do_full, ph)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // dP^T = V dO^T
@@ -201,7 +238,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                       id_kk, kk > 0);
         }
         mma_commit(dp_full);
-        if (!tw(2, p_full, ph)) { ok = false; break; }
+        // S^T(it+1) as soon as the element warps hold S^T(it) in registers
+        if (it + 1 < n_iter && !issue_s(it + 1)) { ok = false; break; }
+        if (!tw(2, p_full, ph)) { ok = false; break; }  // slot 2: P written
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // dV += P^T dO   (K = queries)
@@ -210,25 +249,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                       smem_desc_sw128(do_base + kk * 2048, TILE / 2, 1024), id_km, (it > 0 || kk > 0));
         }
         mma_commit(dv_done);
-        if (!tw(3, ds_full, ph)) { ok = false; break; }
+        mma_commit(do_empty);
+        if (!tw(3, ds_full, ph)) { ok = false; break; }  // slot 3: dS written
         tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // dQ = dS K   (K = keys; dS read MN-major)
+          mma_bf16_ss(tdP, smem_desc_sw128(pds_base + kk * 2048, TILE / 2, 1024),
+                      smem_desc_sw128(k_base + kk * 2048, TILE / 2, 1024), id_mm, kk > 0);
+        }
+        mma_commit(dq_full);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // dK += dS^T Q   (K = queries)
           const uint32_t aoff = (kk >> 2) * (TILE / 2) + (kk & 3) * 32;
           mma_bf16_ss(tdK, smem_desc_sw128(pds_base + aoff, 16, 1024),
                       smem_desc_sw128(q_base + kk * 2048, TILE / 2, 1024), id_km, (it > 0 || kk > 0));
         }
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // dQ = dS K   (K = keys; dS read MN-major)
-          mma_bf16_ss(tdP, smem_desc_sw128(pds_base + kk * 2048, TILE / 2, 1024),
-                      smem_desc_sw128(k_base + kk * 2048, TILE / 2, 1024), id_mm, kk > 0);
-        }
         mma_commit(&q_empty[st]);
-        mma_commit(&do_empty[st]);
         mma_commit(pds_free);
-        mma_commit(dq_full);
       }
-      if (trace) tacc[4] = clock64() - t_mma0;
+      if (kTrace) tacc[4] = clock64() - t_mma0;  // slot 4: MMA loop total
       if (ok) mma_commit(kv_done);
       else {
         mma_commit(drain);
@@ -237,130 +276,115 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else {
+  } else if (wg <= 2) {
+    // ---------------------------------------------------------------- warpgroups 1, 2: softmax gradient
+    regs_increase<kRegsElem>();
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;        // key row within the tile (TMEM lane)
+    const int g = wg - 1;                     // element warpgroup
+    const int cg = g * 64;                    // its query-column block
+    const int r = quarter * 32 + lane;        // key row (S^T / dP^T TMEM lane)
     const int kpos = j * BT + r;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const float scale_log2 = scale * kLog2e;
+    uint8_t* pds_row = sPdS + g * (TILE / 2) + r * 128;  // this thread's row in atom g
     bool ok = true;
     const long long t_loop0 = clock64();
     long long tm = 0;
-    for (int it = 0; it < n_iter; ++it) {
-      const int h = kvh * G + it / (n_t - i0);
+    for (int it = 0; it < n_iter && ok; ++it) {
       const int i = i0 + it % (n_t - i0);
       const uint32_t ph = it & 1;
       const int st = it & 1;
-      // lse / delta of query tile i arrive with Q_i (bulk copies on q_full)
+      // lse2 / delta of query tile i arrive with Q_i (bulk copies on q_full); slot 5
       if (!tw(5, &q_full[st], (it >> 1) & 1)) { ok = false; break; }
-      const float* lse_t = s_lse + st * 128;
-      const float* delta_t = s_delta + st * 128;
-      if (!tw(6, s_full, ph)) { ok = false; break; }
+      const float* lse_t = s_lse + st * 128 + cg;
+      const float* delta_t = s_delta + st * 128 + cg;
+      if (!tw(6, s_full, ph)) { ok = false; break; }  // slot 6
       tc_fence_after();
-      if (trace) tm = clock64();
-      float p[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + lane_off + c * 32, p + c * 32);
+      if (kTrace) tm = clock64();
+      float p[64];
+      tmem_ld32(tS + lane_off + cg, p);
+      tmem_ld32(tS + lane_off + cg + 32, p + 32);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(s_empty);
-      const bool diag = causal && (i == j);
+      const bool masked = (causal && i == j) || (i + 1) * BT > S || (j + 1) * BT > S;
+      if (!masked) {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        float x = ex2(p[c] * scale_log2 - lse_t[c] * kLog2e);
-        if ((diag && kpos > i * BT + c) || kpos >= S || i * BT + c >= S) x = 0.f;
-        p[c] = x;
-      }
-      if (trace) tacc[7] += clock64() - tm;
-      if (!tw(8, pds_free, ph ^ 1)) { ok = false; break; }
-      if (trace) tm = clock64();
-      // P^T -> smem (row = key, 128 queries in two 64-wide swizzled atoms)
+        for (int c = 0; c < 64; c += 4) {
+          const float4 l = *reinterpret_cast<const float4*>(lse_t + c);
+          p[c + 0] = ex2(fmaf(p[c + 0], scale_log2, -l.x));
+          p[c + 1] = ex2(fmaf(p[c + 1], scale_log2, -l.y));
+          p[c + 2] = ex2(fmaf(p[c + 2], scale_log2, -l.z));
+          p[c + 3] = ex2(fmaf(p[c + 3], scale_log2, -l.w));
+        }
+      } else {
+        const int q0 = i * BT + cg;
 #pragma unroll
-      for (int a = 0; a < 2; ++a) {
-        uint8_t* rowp = sPdS + a * (TILE / 2) + r * 128;
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const float* pv = p + a * 64 + ch * 8;
-          uint4 u;
-          u.x = pack_bf16x2(pv[0], pv[1]);
-          u.y = pack_bf16x2(pv[2], pv[3]);
-          u.z = pack_bf16x2(pv[4], pv[5]);
-          u.w = pack_bf16x2(pv[6], pv[7]);
-          *reinterpret_cast<uint4*>(rowp + ((ch ^ (r & 7)) << 4)) = u;
+        for (int c = 0; c < 64; ++c) {
+          const float x = ex2(fmaf(p[c], scale_log2, -lse_t[c]));
+          const int q = q0 + c;
+          p[c] = ((causal && kpos > q) || kpos >= S || q >= S) ? 0.f : x;
         }
       }
+      // P^T -> smem (row = key; this warpgroup's 64 queries form swizzled atom g).
+      // The packed bf16 copy is also what dS uses below (the same rounding dV sees).
+      uint32_t pb[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) pb[e] = pack_bf16x2(p[2 * e], p[2 * e + 1]);
+      if (kTrace) tacc[7] += clock64() - tm;  // slot 7: S -> P
+      if (!tw(8, pds_free, ph ^ 1)) { ok = false; break; }  // slot 8
+      if (kTrace) tm = clock64();
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch)
+        *reinterpret_cast<uint4*>(pds_row + ((ch ^ (r & 7)) << 4)) =
+            make_uint4(pb[4 * ch], pb[4 * ch + 1], pb[4 * ch + 2], pb[4 * ch + 3]);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
-      if (trace) tacc[9] += clock64() - tm;
-      if (!tw(10, dp_full, ph) || !tw(10, dv_done, ph)) { ok = false; break; }
+      if (kTrace) tacc[9] += clock64() - tm;  // slot 9: P write
+      if (!tw(10, dp_full, ph)) { ok = false; break; }  // slot 10
       tc_fence_after();
-      if (trace) tm = clock64();
+      if (kTrace) tm = clock64();
+      uint32_t ds[32];  // dS^T row, packed bf16 pairs
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c2 = 0; c2 < 2; ++c2) {
         float dp[32];
-        tmem_ld32(tdP + lane_off + c * 32, dp);
+        tmem_ld32(tdP + lane_off + cg + c2 * 32, dp);
         tmem_wait_ld();
-        const int a = c >> 1;
-        uint8_t* rowp = sPdS + a * (TILE / 2) + r * 128;
 #pragma unroll
-        for (int ch4 = 0; ch4 < 4; ++ch4) {
-          const int ch = (c & 1) * 4 + ch4;  // 16-byte chunk within the 64-query atom
-          float d[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int q = c * 32 + ch4 * 8 + e;
-            const float dl = (i * BT + q < S) ? delta_t[q] : 0.f;
-            d[e] = p[q] * (dp[ch4 * 8 + e] - dl) * scale;
-          }
-          uint4 u;
-          u.x = pack_bf16x2(d[0], d[1]);
-          u.y = pack_bf16x2(d[2], d[3]);
-          u.z = pack_bf16x2(d[4], d[5]);
-          u.w = pack_bf16x2(d[6], d[7]);
-          *reinterpret_cast<uint4*>(rowp + ((ch ^ (r & 7)) << 4)) = u;
+        for (int e = 0; e < 32; e += 4) {
+          const float4 dl = *reinterpret_cast<const float4*>(delta_t + c2 * 32 + e);
+          const int w = (c2 * 32 + e) / 2;
+          const float2 p01 = unpack_bf16x2(pb[w]), p23 = unpack_bf16x2(pb[w + 1]);
+          ds[w] = pack_bf16x2(p01.x * fmaf(dp[e], scale, -dl.x), p01.y * fmaf(dp[e + 1], scale, -dl.y));
+          ds[w + 1] = pack_bf16x2(p23.x * fmaf(dp[e + 2], scale, -dl.z), p23.y * fmaf(dp[e + 3], scale, -dl.w));
         }
       }
+      tc_fence_before();
+      if (kTrace) tacc[11] += clock64() - tm;  // slot 11: dS compute
+      // dS overwrites P: the dV product must have read it; slot 12
+      if (!tw(12, dv_done, ph)) { ok = false; break; }
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch)
+        *reinterpret_cast<uint4*>(pds_row + ((ch ^ (r & 7)) << 4)) =
+            make_uint4(ds[4 * ch], ds[4 * ch + 1], ds[4 * ch + 2], ds[4 * ch + 3]);
       fence_proxy_async_smem();
-      tc_fence_before();
       mbar_arrive(ds_full);
-      if (trace) tacc[11] += clock64() - tm;
-      if (!tw(12, dq_full, ph)) { ok = false; break; }
-      tc_fence_after();
-      if (trace) tm = clock64();
-      {
-        const int q = i * BT + r;  // dQ lane = query row
-        float* dst = dq_acc + ((int64_t)b * S + q) * ld_dqacc + (int64_t)h * HD;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_ld32(tdP + lane_off + c * 32, v);
-          tmem_wait_ld();
-          if (q < S) {
-#pragma unroll
-            for (int e = 0; e < 32; e += 4)
-              atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + e), make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]));
-          }
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(dq_empty);
-      if (trace) tacc[13] += clock64() - tm;
     }
-    if (trace) tacc[14] = clock64() - t_loop0;
+    if (kTrace) tacc[14] = clock64() - t_loop0;  // slot 14: element loop total
     if (ok && mbar_wait(kv_done, 0, err)) {
       tc_fence_after();
       const bool valid = kpos < S;
-      __nv_bfloat16* dvr = dV + ((int64_t)b * S + kpos) * lddv + (int64_t)kvh * HD;
-      __nv_bfloat16* dkr = dK + ((int64_t)b * S + kpos) * lddk + (int64_t)kvh * HD;
+      __nv_bfloat16* dvr = dV + ((int64_t)b * S + kpos) * lddv + (int64_t)kvh * HD + cg;
+      __nv_bfloat16* dkr = dK + ((int64_t)b * S + kpos) * lddk + (int64_t)kvh * HD + cg;
 #pragma unroll 1
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         float v[32];
-        const uint32_t col = (c < 4 ? tdV : tdK) + (c & 3) * 32;
+        const uint32_t col = (c < 2 ? tdV : tdK) + cg + (c & 1) * 32;
         tmem_ld32(col + lane_off, v);
         tmem_wait_ld();
         if (valid) {
-          uint4* d4 = reinterpret_cast<uint4*>((c < 4 ? dvr : dkr) + (c & 3) * 32);
+          uint4* d4 = reinterpret_cast<uint4*>((c < 2 ? dvr : dkr) + (c & 1) * 32);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint4 u;
@@ -373,11 +397,68 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+  } else {
+    // ---------------------------------------------------------------- warpgroup 3: dQ drain
+    // TMEM dQ (lane = query row) -> two 16 KB swizzled fp32 stages -> bulk
+    // tensor reduce-add into the fp32 accumulator, 32 head-dim columns a time.
+    regs_decrease<kRegsDq>();
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const bool leader = threadIdx.x == 3 * 128;
+    bool ok = true;
+    int n = 0;  // chunks staged so far; chunk n uses stage n & 1
+    const long long t_loop0 = clock64();
+    for (int it = 0; it < n_iter && ok; ++it) {
+      const int h = kvh * G + it / (n_t - i0);
+      const int i = i0 + it % (n_t - i0);
+      if (!tw(16, dq_full, it & 1)) { ok = false; break; }  // slot 16
+      tc_fence_after();
+#pragma unroll 1
+      for (int hh = 0; hh < 2 && ok; ++hh) {
+        float v[64];
+        tmem_ld32(tdP + lane_off + hh * 64, v);
+        tmem_ld32(tdP + lane_off + hh * 64 + 32, v + 32);
+        tmem_wait_ld();
+        if (hh == 1) {  // all of dQ(it) is in registers: TMEM may take dP(it+1)
+          tc_fence_before();
+          mbar_arrive(dq_empty);
+        }
+#pragma unroll
+        for (int c = 0; c < 2; ++c, ++n) {
+          const int bb = n & 1, u = n >> 1;
+          uint8_t* stage = sStage + bb * STAGE;
+          if (leader && u > 0) {  // the reduce that last used this stage has read it
+            bulk_wait_group_read<1>();
+            mbar_arrive(&stage_free[bb]);
+          }
+          if (!tw(17, &stage_free[bb], (u & 1) ^ 1)) { ok = false; break; }  // slot 17
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            const float* vv = v + c * 32 + ch * 4;
+            *reinterpret_cast<float4*>(stage + r * 128 + ((ch ^ (r & 7)) << 4)) =
+                make_float4(vv[0], vv[1], vv[2], vv[3]);
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(&stage_full[bb]);
+          if (leader) {
+            if (!tw(18, &stage_full[bb], u & 1)) { ok = false; break; }  // slot 18
+            tma_reduce_add_3d(&tmdQ, stage, h * HD + hh * 64 + c * 32, i * BT, b);
+            bulk_commit_group();
+          }
+        }
+      }
+    }
+    if (leader) bulk_wait_group<0>();
+    if (kTrace) tacc[19] = clock64() - t_loop0;  // slot 19: dQ loop total
   }
-  if (trace && (threadIdx.x == 0 || threadIdx.x == 32 || threadIdx.x == 64)) {
-    long long* dst = trace + (int64_t)blockIdx.x * 16;
-    for (int i = 0; i < 16; ++i)
-      if (tacc[i]) atomicAdd(reinterpret_cast<unsigned long long*>(dst + i), (unsigned long long)tacc[i]);
+  if constexpr (kTrace) {
+    if (threadIdx.x == 0 || threadIdx.x == 32 || threadIdx.x == 128 || threadIdx.x == 384) {
+      long long* dst = trace + (int64_t)blockIdx.x * kAttnBwdTraceSlots;
+#pragma unroll
+      for (int i = 0; i < kSlots; ++i)
+        if (tacc[i]) atomicAdd(reinterpret_cast<unsigned long long*>(dst + i), (unsigned long long)tacc[i]);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -387,25 +468,43 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// delta[b, h, s] = sum_d dO * O   (one warp per (token, head))
-__global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ O, int64_t ldo,
-                                  const __nv_bfloat16* __restrict__ dO, int64_t lddo, float* __restrict__ delta,
-                                  int B, int S, int nq) {
-  const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+// One warp per (token, head):
+//   delta2[b, h, s] = scale * sum_d dO * O     (first half of `scratch`)
+//   lse2[b, h, s]   = lse * log2(e)            (second half)
+// and zero that (token, head)'s 128 fp32 dQ accumulator entries.  The two
+// halves are padded by 128 zeros so the kernel's 128-row bulk copies stay in
+// bounds and finite.
+__global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ O, int64_t ldo,
+                                     const __nv_bfloat16* __restrict__ dO, int64_t lddo,
+                                     const float* __restrict__ lse, float* __restrict__ scratch,
+                                     float* __restrict__ dq_acc, int64_t ld_acc, int B, int S, int nq, float scale) {
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t rows = (int64_t)B * nq * S;
+  float* delta2 = scratch;
+  float* lse2 = scratch + rows + 128;
+  if (gid < 128) {
+    delta2[rows + gid] = 0.f;
+    lse2[rows + gid] = 0.f;
+  }
+  const int64_t item = gid >> 5;
   const int lane = threadIdx.x & 31;
-  if (item >= B * S * nq) return;
-  const int t = item / nq, h = item % nq;
-  const __nv_bfloat16* o = O + (int64_t)t * ldo + h * HD + lane * 4;
-  const __nv_bfloat16* g = dO + (int64_t)t * lddo + h * HD + lane * 4;
+  if (item >= (int64_t)B * S * nq) return;
+  const int64_t t = item / nq;
+  const int h = (int)(item % nq);
+  const __nv_bfloat16* o = O + t * ldo + h * HD + lane * 4;
+  const __nv_bfloat16* g = dO + t * lddo + h * HD + lane * 4;
   uint2 ov = *reinterpret_cast<const uint2*>(o);
   uint2 gv = *reinterpret_cast<const uint2*>(g);
   float2 o0 = unpack_bf16x2(ov.x), o1 = unpack_bf16x2(ov.y), g0 = unpack_bf16x2(gv.x), g1 = unpack_bf16x2(gv.y);
   float acc = o0.x * g0.x + o0.y * g0.y + o1.x * g1.x + o1.y * g1.y;
+  *reinterpret_cast<float4*>(dq_acc + t * ld_acc + h * HD + lane * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   if (lane == 0) {
-    const int b = t / S, s = t % S;
-    delta[((int64_t)b * nq + h) * S + s] = acc;
+    const int64_t bb = t / S, s = t % S;
+    const int64_t idx = (bb * nq + h) * S + s;
+    delta2[idx] = acc * scale;
+    lse2[idx] = lse[idx] * kLog2e;
   }
 }
 
@@ -432,33 +531,36 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   PB_CHECK(p.S % 8 == 0, "attention bwd: sequence length must be a multiple of 8");
   static bool attr = false;
   if (!attr) {
-    PB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    PB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       SMEM_BYTES));
+    PB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        SMEM_BYTES));
     attr = true;
   }
-  const int T = p.B * p.S;
-  const int items = T * p.nq;
-  attn_delta_kernel<<<(items + 7) / 8, 256, 0, s>>>((const __nv_bfloat16*)p.o, p.ldo,
-                                                    (const __nv_bfloat16*)p.dout, p.lddo, p.delta, p.B, p.S,
-                                                    p.nq);
-  PB_CUDA_CHECK(cudaGetLastError());
+  const int64_t T = (int64_t)p.B * p.S;
+  const int64_t rows = (int64_t)p.B * p.nq * p.S;
   const int64_t ld_acc = (int64_t)p.nq * HD;
-  PB_CUDA_CHECK(cudaMemsetAsync(p.dq_acc, 0, (size_t)T * ld_acc * sizeof(float), s));
+  const int64_t prep_threads = std::max<int64_t>(T * p.nq * 32, 128);
+  attn_bwd_prep_kernel<<<(unsigned)((prep_threads + 255) / 256), 256, 0, s>>>(
+      (const __nv_bfloat16*)p.o, p.ldo, (const __nv_bfloat16*)p.dout, p.lddo, p.lse, p.delta, p.dq_acc, ld_acc,
+      p.B, p.S, p.nq, p.scale);
+  PB_CUDA_CHECK(cudaGetLastError());
   const uint64_t S = p.S, B = p.B;
   CUtensorMap tq = make_tmap_3d_bf16(p.q, (uint64_t)p.nq * HD, S, B, p.ldq, S * p.ldq, 64, 128, 1);
   CUtensorMap tk = make_tmap_3d_bf16(p.k, (uint64_t)p.nkv * HD, S, B, p.ldk, S * p.ldk, 64, 128, 1);
   CUtensorMap tv = make_tmap_3d_bf16(p.v, (uint64_t)p.nkv * HD, S, B, p.ldv, S * p.ldv, 64, 128, 1);
   CUtensorMap tdo = make_tmap_3d_bf16(p.dout, (uint64_t)p.nq * HD, S, B, p.lddo, S * p.lddo, 64, 128, 1);
+  CUtensorMap tdq = make_tmap_3d_f32(p.dq_acc, (uint64_t)ld_acc, S, B, ld_acc, S * ld_acc, 32, 128, 1, true);
   const int n_t = (p.S + BT - 1) / BT;
   const int grid = p.B * p.nkv * n_t;
-  attn_bwd_kernel<<<grid, kThreads, SMEM_BYTES, s>>>(tq, tk, tv, tdo, p.lse, p.delta, p.dq_acc, ld_acc,
-                                                     (__nv_bfloat16*)p.dk, p.lddk, (__nv_bfloat16*)p.dv, p.lddv,
-                                                     p.B, p.S, p.nq, p.nkv, p.scale, p.causal, error_word(),
-                                                     p.trace);
+  auto kern = p.trace ? attn_bwd_kernel<true> : attn_bwd_kernel<false>;
+  kern<<<grid, kThreads, SMEM_BYTES, s>>>(tq, tk, tv, tdo, tdq, p.delta + rows + 128, p.delta, (__nv_bfloat16*)p.dk,
+                                          p.lddk, (__nv_bfloat16*)p.dv, p.lddv, p.B, p.S, p.nq, p.nkv, p.scale,
+                                          p.causal, error_word(), p.trace);
   PB_CUDA_CHECK(cudaGetLastError());
-  const int64_t cast_work = (int64_t)T * ld_acc / 4;
+  const int64_t cast_work = T * ld_acc / 4;
   int cgrid = (int)std::min<int64_t>((cast_work + 255) / 256, (int64_t)num_sms() * 16);
-  cast_rows_kernel<<<cgrid, 256, 0, s>>>(p.dq_acc, ld_acc, (__nv_bfloat16*)p.dq, p.lddq, T, (int)ld_acc);
+  cast_rows_kernel<<<cgrid, 256, 0, s>>>(p.dq_acc, ld_acc, (__nv_bfloat16*)p.dq, p.lddq, (int)T, (int)ld_acc);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -473,7 +575,7 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
 // other runtimes that forbid cudaMalloc after start-up, and allocation-free
 // serving paths.  It computes the same dq / dk / dv as attention_bwd() (the
 // launcher above, used by the Python bindings) but keeps every scratch buffer
-// (the per-row delta, a padded copy of lse, the fp32 dq accumulator and the
+// (the per-row delta, lse rescaled to base 2, the fp32 dq accumulator and the
 // kernel's error word) in one file-scope __device__ array of fixed size,
 // kNoAllocScratchBytes (8.5 MiB).  Every GPU that loads this library holds
 // that array until the process exits.
@@ -542,10 +644,9 @@ extern "C" __attribute__((visibility("default"))) int pb_attention_bwd_noalloc(
   const int64_t T = (int64_t)B * S;
   const int64_t rows = (int64_t)B * nq * S;
   const int64_t ld_acc = (int64_t)nq * HD;
-  // scratch layout: [err word 256 B][delta (rows+128) f32][lse copy (rows+128) f32][dq_acc T*ld_acc f32]
+  // scratch layout: [err word 256 B][delta*scale, lse*log2e: 2 x (rows+128) f32][dq_acc T*ld_acc f32]
   const size_t off_delta = 256;
-  const size_t off_lse = off_delta + round256((size_t)(rows + 128) * sizeof(float));
-  const size_t off_acc = off_lse + round256((size_t)(rows + 128) * sizeof(float));
+  const size_t off_acc = off_delta + round256((size_t)2 * (rows + 128) * sizeof(float));
   const size_t need = off_acc + (size_t)T * ld_acc * sizeof(float);
   if (need > kNoAllocScratchBytes) {
     char m[256];
@@ -576,7 +677,7 @@ extern "C" __attribute__((visibility("default"))) int pb_attention_bwd_noalloc(
       g_noalloc_base[dev] = ptr;
     }
     if (!g_noalloc_attr[dev]) {
-      if (cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+      if (cudaFuncSetAttribute(attn_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
           cudaSuccess) {
         noalloc_set_msg("pb_attention_bwd_noalloc: cudaFuncSetAttribute failed");
         return kNoAllocCudaError;
@@ -587,27 +688,23 @@ extern "C" __attribute__((visibility("default"))) int pb_attention_bwd_noalloc(
   }
   int* err = reinterpret_cast<int*>(base);
   float* delta = reinterpret_cast<float*>(base + off_delta);
-  float* lse_pad = reinterpret_cast<float*>(base + off_lse);
   float* dq_acc = reinterpret_cast<float*>(base + off_acc);
   try {
-    // zero what must start at zero: error word, delta / lse padding, dq accumulator
+    // the prep kernel zeroes the dq accumulator and the scratch padding
     PB_CUDA_CHECK(cudaMemsetAsync(err, 0, 256, stream));
-    PB_CUDA_CHECK(cudaMemsetAsync(delta + rows, 0, 128 * sizeof(float), stream));
-    PB_CUDA_CHECK(cudaMemcpyAsync(lse_pad, lse, (size_t)rows * sizeof(float), cudaMemcpyDeviceToDevice, stream));
-    PB_CUDA_CHECK(cudaMemsetAsync(lse_pad + rows, 0, 128 * sizeof(float), stream));
-    PB_CUDA_CHECK(cudaMemsetAsync(dq_acc, 0, (size_t)T * ld_acc * sizeof(float), stream));
-    const int items = (int)(T * nq);
-    attn_delta_kernel<<<(items + 7) / 8, 256, 0, stream>>>((const __nv_bfloat16*)o, ldo,
-                                                           (const __nv_bfloat16*)dout, lddo, delta, B, S, nq);
+    const int64_t prep_threads = std::max<int64_t>(T * nq * 32, 128);
+    attn_bwd_prep_kernel<<<(unsigned)((prep_threads + 255) / 256), 256, 0, stream>>>(
+        (const __nv_bfloat16*)o, ldo, (const __nv_bfloat16*)dout, lddo, lse, delta, dq_acc, ld_acc, B, S, nq, scale);
     PB_CUDA_CHECK(cudaGetLastError());
     const uint64_t uS = S, uB = B;
     CUtensorMap tq = make_tmap_3d_bf16(q, (uint64_t)nq * HD, uS, uB, ldq, uS * ldq, 64, 128, 1);
     CUtensorMap tk = make_tmap_3d_bf16(k, (uint64_t)nkv * HD, uS, uB, ldk, uS * ldk, 64, 128, 1);
     CUtensorMap tv = make_tmap_3d_bf16(v, (uint64_t)nkv * HD, uS, uB, ldv, uS * ldv, 64, 128, 1);
     CUtensorMap tdo = make_tmap_3d_bf16(dout, (uint64_t)nq * HD, uS, uB, lddo, uS * lddo, 64, 128, 1);
+    CUtensorMap tdq = make_tmap_3d_f32(dq_acc, (uint64_t)ld_acc, uS, uB, ld_acc, uS * ld_acc, 32, 128, 1, true);
     const int n_t = (S + BT - 1) / BT;
-    attn_bwd_kernel<<<B * nkv * n_t, kThreads, SMEM_BYTES, stream>>>(
-        tq, tk, tv, tdo, lse_pad, delta, dq_acc, ld_acc, (__nv_bfloat16*)dk, lddk, (__nv_bfloat16*)dv, lddv, B, S,
+    attn_bwd_kernel<false><<<B * nkv * n_t, kThreads, SMEM_BYTES, stream>>>(
+        tq, tk, tv, tdo, tdq, delta + rows + 128, delta, (__nv_bfloat16*)dk, lddk, (__nv_bfloat16*)dv, lddv, B, S,
         nq, nkv, scale, causal != 0, err, nullptr);
     PB_CUDA_CHECK(cudaGetLastError());
     int sms = 0;

@@ -110,4 +110,23 @@ CUtensorMap make_tmap_3d_bf16(const void* base, uint64_t d0, uint64_t d1, uint64
   return m;
 }
 
+CUtensorMap make_tmap_3d_f32(void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_elems,
+                             uint64_t stride2_elems, uint32_t b0, uint32_t b1, uint32_t b2, bool swizzle128) {
+  PB_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
+  PB_CHECK((stride1_elems * 4) % 16 == 0 && (stride2_elems * 4) % 16 == 0,
+           "TMA strides must be multiples of 16 bytes");
+  PB_CHECK(!swizzle128 || b0 * 4 <= 128, "128B swizzle needs an inner box of at most 128 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_elems * 4, stride2_elems * 4};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  PB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (3d f32) failed: code " + std::to_string(r));
+  return m;
+}
+
 }  // namespace pb

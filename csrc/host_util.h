@@ -46,4 +46,9 @@ CUtensorMap make_tmap_3d_bf16(const void* base, uint64_t d0, uint64_t d1, uint64
                               uint64_t stride1_elems, uint64_t stride2_elems, uint32_t b0,
                               uint32_t b1, uint32_t b2);
 
+// Encode a 3-D fp32 tiled tensor map (used as the destination of bulk
+// reduce-adds); swizzle128 needs b0 * 4 <= 128.
+CUtensorMap make_tmap_3d_f32(void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_elems,
+                             uint64_t stride2_elems, uint32_t b0, uint32_t b1, uint32_t b2, bool swizzle128);
+
 }  // namespace pb

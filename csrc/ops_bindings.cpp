@@ -203,9 +203,10 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   CHECK_BF16(q); CHECK_BF16(k); CHECK_BF16(v); CHECK_BF16(o); CHECK_BF16(dout); CHECK_BF16(dq); CHECK_BF16(dk);
   CHECK_BF16(dv); CHECK_F32(lse); CHECK_F32(delta); CHECK_F32(dq_acc);
   const int64_t D = q.size(1) / nq;
-  // lse / delta are read in 128-row blocks: they must be padded by 128 entries
-  TORCH_CHECK(lse.numel() >= B * nq * S + 128 && delta.numel() >= B * nq * S + 128,
-              "attn bwd: lse/delta need 128 floats of padding");
+  // delta is the kernel's scratch: delta*scale and lse*log2(e), each padded by 128 entries
+  TORCH_CHECK(lse.numel() >= B * nq * S, "attn bwd: lse too small");
+  TORCH_CHECK(delta.numel() >= 2 * (B * nq * S + 128), "attn bwd: delta scratch needs 2 * (B*nq*S + 128) floats");
+  TORCH_CHECK(delta.is_contiguous() && dq_acc.is_contiguous(), "attn bwd: scratch must be contiguous");
   TORCH_CHECK(dq_acc.numel() >= B * S * nq * D, "attn bwd: dq_acc too small");
   const c10::cuda::CUDAGuard g(q.device());
   pb::AttnBwdParams p{};
@@ -218,6 +219,8 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   p.causal = causal;
   if (trace.has_value() && trace->defined()) {
     TORCH_CHECK(trace->scalar_type() == at::kLong && trace->is_cuda(), "trace must be a CUDA int64 tensor");
+    TORCH_CHECK(trace->numel() >= B * nkv * ((S + 127) / 128) * pb::kAttnBwdTraceSlots,
+                "trace needs kAttnBwdTraceSlots int64 entries per CTA");
     p.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
   }
   pb::attention_bwd(p, cur_stream());

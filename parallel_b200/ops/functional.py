@@ -212,7 +212,7 @@ class _AttentionFn(torch.autograd.Function):
         dk = torch.empty_like(k)
         dv = dqkv[:, (nq + nkv) * D:]
         v = qkv[:, (nq + nkv) * D:]
-        delta = torch.zeros(B * nq * S + 128, device=h.device, dtype=torch.float32)
+        delta = torch.empty(2 * (B * nq * S + 128), device=h.device, dtype=torch.float32)
         dq_acc = torch.empty(T, nq * D, device=h.device, dtype=torch.float32)
         ext().attn_bwd(q, k, v, o, do, lse, delta, dq_acc, dq, dk, dv, B, S, nq, nkv, 1.0 / math.sqrt(D), True)
         dqw = torch.zeros(D, device=h.device, dtype=torch.float32)

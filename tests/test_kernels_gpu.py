@@ -287,7 +287,7 @@ def test_attention_fwd_bwd(B, S, nq, nkv):
         return
     do = torch.randn(T, nq * D, device="cuda").to(torch.bfloat16)
     o_ref.backward(do.float())
-    delta = torch.zeros(B * nq * S + 128, device="cuda")
+    delta = torch.empty(2 * (B * nq * S + 128), device="cuda")
     dq_acc = torch.empty(T, nq * D, device="cuda")
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)

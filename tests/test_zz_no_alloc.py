@@ -56,7 +56,7 @@ def test_noalloc_matches_allocating_entry_point():
     C.attn_fwd(q, k, v, o, lse, B, S, nq, nkv, scale, True)
     do = torch.randn_like(q)
     # regular (allocating) entry point
-    delta = torch.zeros(B * nq * S + 128, device="cuda")
+    delta = torch.empty(2 * (B * nq * S + 128), device="cuda")
     acc = torch.empty(T, nq * D, device="cuda")
     ref_dq, ref_dk, ref_dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     C.attn_bwd(q, k, v, o, do, lse, delta, acc, ref_dq, ref_dk, ref_dv, B, S, nq, nkv, scale, True)
