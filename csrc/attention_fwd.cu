@@ -1,15 +1,24 @@
 // Causal GQA flash-attention forward on tcgen05.
 //
-// One CTA computes a 128-query tile of one (batch, head).  Roles (192 thr):
-//   warp 0     : TMA producer - Q once, then K_j / V_j into 2-deep rings
-//   warp 1     : TMEM allocator + MMA issuer:  S_j = Q K_j^T (TMEM, double
-//                buffered), O += P_j V_j (TMEM accumulator)
-//   warps 2..5 : softmax - one query row per thread; reads S_j from TMEM,
-//                keeps the running max / sum in registers, writes P_j (bf16,
-//                128B-swizzled) to shared memory for the PV MMA, and rescales
-//                O in TMEM only when a row's max grew by more than 2^8
-//                (exact: the final O / l does not depend on the reference max)
-// S_{j+1} is issued before PV_j so the tensor core overlaps the softmax.
+// One CTA computes one 128-query tile for a pair of query heads that share a
+// kv head (GQA groups of even size; one head per CTA otherwise), so every K / V
+// tile it loads feeds two tiles of work.  Roles (384 threads, 3 warpgroups):
+//   warpgroup 0, warp 0 : TMA producer - Q (both heads) once, K_j / V_j rings
+//   warpgroup 0, warp 1 : TMEM allocator + MMA issuer
+//   warpgroup 1 + t     : softmax of query tile t, one query row per thread
+// TMEM (512 columns): S_t in [128t, 128t+128), O_t in [256 + 128t, ...).
+// Per key tile j and query tile t:
+//   S_t  = Q_t K_j^T            (A, B from shared memory)
+//   P_t  = exp2(S_t*scale*log2e - m_t), packed bf16 into the first 64
+//          columns of S_t by the softmax warps (tcgen05.st)
+//   O_t += P_t V_j              (A = P_t read from TMEM, B = V_j from shared)
+// The MMA warp alternates the two tiles (PV_0(j), S_0(j+1), PV_1(j),
+// S_1(j+1)) so the tensor core works on one tile while the other tile's
+// softmax runs, and P never touches shared memory.  MMAs of one thread run in
+// issue order, so S_t(j+1) (which overwrites P_t(j)) follows PV_t(j) safely,
+// and observing S_t(j+1) complete implies PV_t(j) is complete.
+// The running max moves lazily (only when a row's max grew by more than 2^8);
+// the final O / l does not depend on the reference max, so the result is exact.
 //
 // Replaces the SDPA call HF makes for every layer in the reference
 // (attn_implementation="sdpa", parallel/parallel/engine/model_loading.py:22).
@@ -24,10 +33,14 @@
 namespace pb {
 namespace {
 
-constexpr int BQ = 128;       // queries per CTA
-constexpr int BKV = 128;      // keys per tile
-constexpr int HD = 128;       // head dim
-constexpr int kThreads = 192;
+constexpr int BQ = 128;   // queries per tile
+constexpr int BKV = 128;  // keys per tile
+constexpr int HD = 128;   // head dim
+constexpr int kThreads = 384;
+// setmaxnreg split: 168 registers a thread at launch (65536 / 384, rounded
+// down to a multiple of 8); the sum over the three warpgroups stays 3 x 168.
+constexpr int kRegsCtl = 56, kRegsSoftmax = 224;
+static_assert(kRegsCtl + 2 * kRegsSoftmax == 3 * 168, "attention fwd: register split");
 constexpr int TILE_BYTES = 128 * HD * 2;  // 32 KB: 128 rows x 128 bf16
 constexpr int SMEM_BYTES = TILE_BYTES * 6 + 1024 + 256;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -47,31 +60,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + TILE_BYTES;       // 2 stages
-  uint8_t* sV = smem + 3 * TILE_BYTES;   // 2 stages
-  uint8_t* sP = smem + 5 * TILE_BYTES;
+  uint8_t* sQ = smem;                    // [2 tiles]
+  uint8_t* sK = smem + 2 * TILE_BYTES;   // 2 stages
+  uint8_t* sV = smem + 4 * TILE_BYTES;   // 2 stages
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * TILE_BYTES);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* s_empty = bars + 11; // [2]
-  uint64_t* p_full = bars + 13;
-  uint64_t* p_empty = bars + 14;
-  uint64_t* o_full = bars + 15;
-  uint64_t* drain = bars + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* k_full = bars + 1;   // [2 stages]
+  uint64_t* k_empty = bars + 3;  // [2 stages]
+  uint64_t* v_full = bars + 5;   // [2 stages]
+  uint64_t* v_empty = bars + 7;  // [2 stages]
+  uint64_t* s_full = bars + 9;   // [2 tiles]
+  uint64_t* p_full = bars + 11;  // [2 tiles]
+  uint64_t* o_full = bars + 13;
+  uint64_t* drain = bars + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wg = warp >> 2;
+  const int G = nq / nkv;
+  const int tpc = (G % 2 == 0) ? 2 : 1;  // query tiles (heads) per CTA
+  const int n_hg = nq / tpc;
   const int n_qt = (S + BQ - 1) / BQ;
-  const int bh = blockIdx.x % (B * nq);
-  const int qi = n_qt - 1 - blockIdx.x / (B * nq);  // heaviest tiles first
-  const int b = bh / nq, h = bh % nq;
-  const int kvh = h / (nq / nkv);
-  const int n_kv = causal ? min(qi + 1, (S + BKV - 1) / BKV) : (S + BKV - 1) / BKV;
+  const int n_kt = (S + BKV - 1) / BKV;
+  const int qi = n_qt - 1 - blockIdx.x / (B * n_hg);  // heaviest tiles first
+  const int rem = blockIdx.x % (B * n_hg);
+  const int b = rem / n_hg;
+  const int h0 = (rem % n_hg) * tpc;
+  const int kvh = h0 / G;
+  const int n_kv = causal ? min(qi + 1, n_kt) : n_kt;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -81,10 +97,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(p_empty, 1);
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -97,17 +111,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem;        // 2 x 128 columns
-  const uint32_t tO = tmem + 256;  // 128 columns
 
-  if (warp == 0) {
-    if (lane == 0) {
+  if (wg == 0) {
+    regs_decrease<kRegsCtl>();
+    if (warp == 0 && lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(q_full, TILE_BYTES);
-      tma_load_3d(sQ, &tmQ, q_full, h * HD, qi * BQ, b);
-      tma_load_3d(sQ + TILE_BYTES / 2, &tmQ, q_full, h * HD + 64, qi * BQ, b);
+      mbar_arrive_expect_tx(q_full, tpc * TILE_BYTES);
+      for (int t = 0; t < tpc; ++t)
+        for (int a = 0; a < 2; ++a)
+          tma_load_3d(sQ + t * TILE_BYTES + a * (TILE_BYTES / 2), &tmQ, q_full, (h0 + t) * HD + a * 64, qi * BQ, b);
       for (int j = 0; j < n_kv; ++j) {
         const int st = j & 1;
         const uint32_t ph = ((j >> 1) & 1) ^ 1;
@@ -125,47 +139,44 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_3d(vd + db * 16384 + kb * 8192, &tmV, &v_full[st], kvh * HD + db * 64,
                         j * BKV + kb * 64, b);
       }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16(128, 128, false, false);
       constexpr uint32_t idesc_o = idesc_bf16(128, 128, false, true);
-      const uint32_t q_base = smem_u32(sQ);
-      const uint32_t p_base = smem_u32(sP);
       bool ok = mbar_wait(q_full, 0, err);
-      auto issue_s = [&](int j) -> bool {
+      // S_t(j) = Q_t K_j^T
+      auto issue_s = [&](int t, int j) -> bool {
         const int st = j & 1;
         if (!mbar_wait(&k_full[st], (j >> 1) & 1, err)) return false;
-        if (!mbar_wait(&s_empty[st], ((j >> 1) & 1) ^ 1, err)) return false;
         tc_fence_after();
+        const uint32_t q_base = smem_u32(sQ + t * TILE_BYTES);
         const uint32_t k_base = smem_u32(sK + st * TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (TILE_BYTES / 2) + (kk & 3) * 32;
-          mma_bf16_ss(tS + st * 128, smem_desc_sw128(q_base + off, 16, 1024),
+          mma_bf16_ss(tmem + t * 128, smem_desc_sw128(q_base + off, 16, 1024),
                       smem_desc_sw128(k_base + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         }
-        mma_commit(&k_empty[st]);
-        mma_commit(&s_full[st]);
+        mma_commit(&s_full[t]);
         return true;
       };
-      if (ok) ok = issue_s(0);
+      for (int t = 0; t < tpc && ok; ++t) ok = issue_s(t, 0);
+      if (ok) mma_commit(&k_empty[0]);
       for (int j = 0; j < n_kv && ok; ++j) {
-        if (j + 1 < n_kv && !issue_s(j + 1)) { ok = false; break; }
         const int st = j & 1;
-        if (!mbar_wait(p_full, j & 1, err)) { ok = false; break; }
         if (!mbar_wait(&v_full[st], (j >> 1) & 1, err)) { ok = false; break; }
-        tc_fence_after();
         const uint32_t v_base = smem_u32(sV + st * TILE_BYTES);
+        for (int t = 0; t < tpc; ++t) {
+          if (!mbar_wait(&p_full[t], j & 1, err)) { ok = false; break; }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint32_t poff = (kk >> 2) * (TILE_BYTES / 2) + (kk & 3) * 32;
-          mma_bf16_ss(tO, smem_desc_sw128(p_base + poff, 16, 1024),
-                      smem_desc_sw128(v_base + kk * 2048, 16384, 1024), idesc_o,
-                      (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BKV / 16; ++kk)  // O_t += P_t V_j, P_t from TMEM
+            mma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                        smem_desc_sw128(v_base + kk * 2048, 16384, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          if (j + 1 < n_kv && !issue_s(t, j + 1)) { ok = false; break; }
         }
+        if (!ok) break;
         mma_commit(&v_empty[st]);
-        mma_commit(p_empty);
+        if (j + 1 < n_kv) mma_commit(&k_empty[(j + 1) & 1]);
       }
       if (ok) mma_commit(o_full);
       else {
@@ -176,110 +187,111 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // softmax warps: thread owns query row `row` of the tile
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const int qpos = qi * BQ + row;
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    float m_ref = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int st = j & 1;
-      if (!mbar_wait(&s_full[st], (j >> 1) & 1, err)) { ok = false; break; }
-      tc_fence_after();
-      float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + lane_off + st * 128 + c * 32, s + c * 32);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&s_empty[st]);
-      const int kbase = j * BKV;
-      const bool diag = (causal && kbase + BKV - 1 > qi * BQ) || kbase + BKV > S;
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        float x = s[c] * scale_log2;
-        if (diag) {
-          const int kpos = kbase + c;
-          if ((causal && kpos > qpos) || kpos >= S) x = -INFINITY;
-        }
-        s[c] = x;
-        mx = fmaxf(mx, x);
-      }
-      // lazy rescale: move the reference max only when it grew by > 2^8
-      const bool need = mx > m_ref + kRescaleThreshold;
-      float alpha = 1.f;
-      if (need) {
-        alpha = (m_ref == -INFINITY) ? 0.f : ex2(m_ref - mx);
-        m_ref = mx;
-      }
-      const float mu = (m_ref == -INFINITY) ? 0.f : m_ref;
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        s[c] = ex2(s[c] - mu);
-        rs += s[c];
-      }
-      l = l * alpha + rs;
-      if (j > 0) {
-        if (!mbar_wait(p_empty, (j - 1) & 1, err)) { ok = false; break; }
+    regs_increase<kRegsSoftmax>();
+    const int t = wg - 1;  // query tile (head h0 + t)
+    if (t < tpc) {
+      const int h = h0 + t;
+      const int quarter = warp & 3;
+      const int row = quarter * 32 + lane;
+      const int qpos = qi * BQ + row;
+      const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+      const uint32_t tS = tmem + t * 128 + lane_off;
+      const uint32_t tO = tmem + 256 + t * 128 + lane_off;
+      float m_ref = -INFINITY, l = 0.f;
+      bool ok = true;
+      for (int j = 0; j < n_kv; ++j) {
+        if (!mbar_wait(&s_full[t], j & 1, err)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, need)) {
+        float s[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s + c * 32);
+        tmem_wait_ld();
+        const int kbase = j * BKV;
+        const bool diag = (causal && kbase + BKV - 1 > qi * BQ) || kbase + BKV > S;
+        if (diag) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c) {
+            const int kpos = kbase + c;
+            if ((causal && kpos > qpos) || kpos >= S) s[c] = -INFINITY;
+          }
+        }
+        float mx = s[0];
+#pragma unroll
+        for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
+        mx *= scale_log2;
+        // lazy rescale: move the reference max only when it grew by > 2^8
+        const bool need = mx > m_ref + kRescaleThreshold;
+        float alpha = 1.f;
+        if (need) {
+          alpha = (m_ref == -INFINITY) ? 0.f : ex2(m_ref - mx);
+          m_ref = mx;
+        }
+        const float mu = (m_ref == -INFINITY) ? 0.f : m_ref;
+        const uint64_t sc2 = f2_pack(scale_log2, scale_log2), nmu2 = f2_pack(-mu, -mu);
+        uint64_t acc[4] = {0, 0, 0, 0};
+        uint32_t pk[64];
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const float2 x = f2_unpack(ffma2(f2_pack(s[2 * c], s[2 * c + 1]), sc2, nmu2));
+          float a0, a1;
+          // 5 of every 16 pairs on the FMA pipe (masked tiles need exact zeros: all MUFU)
+          if (!diag && (c & 15) >= 11) {
+            exp2_poly_pair(x.x, x.y, a0, a1);
+          } else {
+            a0 = ex2(x.x);
+            a1 = ex2(x.y);
+          }
+          acc[c & 3] = fadd2(acc[c & 3], f2_pack(a0, a1));
+          pk[c] = pack_bf16x2(a0, a1);
+        }
+        const float2 r01 = f2_unpack(fadd2(acc[0], acc[1])), r23 = f2_unpack(fadd2(acc[2], acc[3]));
+        const float rs = (r01.x + r01.y) + (r23.x + r23.y);
+        l = l * alpha + rs;
+        // O_t rescale: PV_t(j-1) is complete (S_t(j) was issued after it)
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             float o[32];
-            tmem_ld32(tO + lane_off + c * 32, o);
+            tmem_ld32(tO + c * 32, o);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(tO + lane_off + c * 32, o);
+            tmem_st32(tO + c * 32, o);
           }
-          tmem_wait_st();
         }
+        // P_t (bf16 pairs) over the first 64 columns of S_t
+        tmem_st32(tS, reinterpret_cast<const float*>(pk));
+        tmem_st32(tS + 32, reinterpret_cast<const float*>(pk + 32));
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[t]);
       }
-      // P (bf16) -> smem, K-major 128B swizzle: atom (64 keys) x row x 16B chunk
-#pragma unroll
-      for (int a = 0; a < 2; ++a) {
-        uint8_t* rowp = sP + a * (TILE_BYTES / 2) + row * 128;
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const float* pv = s + a * 64 + ch * 8;
-          uint4 u;
-          u.x = pack_bf16x2(pv[0], pv[1]);
-          u.y = pack_bf16x2(pv[2], pv[3]);
-          u.z = pack_bf16x2(pv[4], pv[5]);
-          u.w = pack_bf16x2(pv[6], pv[7]);
-          *reinterpret_cast<uint4*>(rowp + ((ch ^ (row & 7)) << 4)) = u;
-        }
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(p_full);
-    }
-    if (ok && mbar_wait(o_full, 0, err)) {
-      tc_fence_after();
-      const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      const bool valid = qpos < S;
-      __nv_bfloat16* orow = O + ((int64_t)b * S + qpos) * ldo + (int64_t)h * HD;
+      if (ok && mbar_wait(o_full, 0, err)) {
+        tc_fence_after();
+        const float inv_l = l > 0.f ? 1.f / l : 0.f;
+        const bool valid = qpos < S;
+        __nv_bfloat16* orow = O + ((int64_t)b * S + qpos) * ldo + (int64_t)h * HD;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float o[32];
-        tmem_ld32(tO + lane_off + c * 32, o);
-        tmem_wait_ld();
-        if (valid) {
-          uint4* d4 = reinterpret_cast<uint4*>(orow + c * 32);
+        for (int c = 0; c < 4; ++c) {
+          float o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld();
+          if (valid) {
+            uint4* d4 = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 u;
-            u.x = pack_bf16x2(o[q * 8 + 0] * inv_l, o[q * 8 + 1] * inv_l);
-            u.y = pack_bf16x2(o[q * 8 + 2] * inv_l, o[q * 8 + 3] * inv_l);
-            u.z = pack_bf16x2(o[q * 8 + 4] * inv_l, o[q * 8 + 5] * inv_l);
-            u.w = pack_bf16x2(o[q * 8 + 6] * inv_l, o[q * 8 + 7] * inv_l);
-            d4[q] = u;
+            for (int q = 0; q < 4; ++q) {
+              uint4 u;
+              u.x = pack_bf16x2(o[q * 8 + 0] * inv_l, o[q * 8 + 1] * inv_l);
+              u.y = pack_bf16x2(o[q * 8 + 2] * inv_l, o[q * 8 + 3] * inv_l);
+              u.z = pack_bf16x2(o[q * 8 + 4] * inv_l, o[q * 8 + 5] * inv_l);
+              u.w = pack_bf16x2(o[q * 8 + 6] * inv_l, o[q * 8 + 7] * inv_l);
+              d4[q] = u;
+            }
           }
         }
+        if (valid && LSE)
+          LSE[((int64_t)b * nq + h) * S + qpos] = (m_ref + __log2f(l)) * 0.6931471805599453f;
       }
-      if (valid && LSE) LSE[(int64_t)bh * S + qpos] = (m_ref + __log2f(l)) * 0.6931471805599453f;
     }
   }
   tc_fence_before();
@@ -305,8 +317,10 @@ void attention_fwd(const AttnParams& p, cudaStream_t s) {
   CUtensorMap tq = make_tmap_3d_bf16(p.q, (uint64_t)p.nq * HD, S, B, p.ldq, S * p.ldq, 64, 128, 1);
   CUtensorMap tk = make_tmap_3d_bf16(p.k, (uint64_t)p.nkv * HD, S, B, p.ldk, S * p.ldk, 64, 128, 1);
   CUtensorMap tv = make_tmap_3d_bf16(p.v, (uint64_t)p.nkv * HD, S, B, p.ldv, S * p.ldv, 64, 64, 1);
+  const int G = p.nq / p.nkv;
+  const int tpc = (G % 2 == 0) ? 2 : 1;
   const int n_qt = (p.S + BQ - 1) / BQ;
-  const int grid = p.B * p.nq * n_qt;
+  const int grid = p.B * (p.nq / tpc) * n_qt;
   attn_fwd_kernel<<<grid, kThreads, SMEM_BYTES, s>>>(tq, tk, tv, (__nv_bfloat16*)p.o, p.ldo, p.lse, p.B,
                                                      p.S, p.nq, p.nkv, p.scale * kLog2e, p.causal,
                                                      error_word());

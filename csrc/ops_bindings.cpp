@@ -121,6 +121,13 @@ void ce_row_stats(const at::Tensor& logits, at::Tensor& row_max, at::Tensor& row
                    row_sumexp.data_ptr<float>(), cur_stream());
 }
 
+void exp2_emulated(const at::Tensor& x, at::Tensor& y) {
+  CHECK_F32(x); CHECK_F32(y);
+  TORCH_CHECK(x.numel() == y.numel(), "exp2_emulated: size mismatch");
+  const c10::cuda::CUDAGuard g(x.device());
+  pb::exp2_emulated(x.data_ptr<float>(), y.data_ptr<float>(), x.numel(), cur_stream());
+}
+
 void cast_f32_to_bf16(const at::Tensor& src, at::Tensor& dst) {
   CHECK_F32(src);
   TORCH_CHECK(dst.is_contiguous() && dst.scalar_type() == at::kBFloat16 && dst.numel() == src.numel(), "cast: dst");
@@ -242,6 +249,7 @@ void register_ops(pybind11::module& m) {
   m.def("ce_fwd_bwd", &ce_fwd_bwd);
   m.def("ce_row_stats", &ce_row_stats);
   m.def("cast_f32_to_bf16", &cast_f32_to_bf16);
+  m.def("exp2_emulated", &exp2_emulated);
   m.def("adamw", &adamw);
   m.def("sumsq", &sumsq);
   m.def("clip_coef", &clip_coef);
