@@ -22,7 +22,7 @@ cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 //   b: [N, K] (b_mn=False) or [K, N] (b_mn=True), unit inner stride
 //   out: [M, N] bf16 or fp32 depending on epi
 void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, bool b_mn, int64_t epi,
-          double alpha, const c10::optional<at::Tensor>& r, int64_t b_up_offset, int64_t n_out) {
+          double alpha, const c10::optional<at::Tensor>& r, int64_t b_up_offset, int64_t n_out, int64_t kernel) {
   CHECK_CUDA_BF16(a);
   CHECK_CUDA_BF16(b);
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm: 2-D operands expected");
@@ -45,6 +45,8 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, 
   p.epi = (int)epi;
   p.alpha = (float)alpha;
   p.max_ctas = 0;
+  TORCH_CHECK(kernel >= 0 && kernel <= 2, "gemm: kernel must be 0 (choose), 1 (one CTA) or 2 (CTA pair)");
+  p.kernel = (int)kernel;
   p.b_up_offset = b_up_offset;
   if (epi == pb::kEpiSwiGLU) {
     p.N = (int)n_out;
@@ -79,7 +81,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM with fused epilogues", pybind11::arg("a"),
         pybind11::arg("b"), pybind11::arg("out"), pybind11::arg("a_mn"), pybind11::arg("b_mn"),
         pybind11::arg("epi"), pybind11::arg("alpha"), pybind11::arg("r") = pybind11::none(),
-        pybind11::arg("b_up_offset") = 0, pybind11::arg("n_out") = 0);
+        pybind11::arg("b_up_offset") = 0, pybind11::arg("n_out") = 0, pybind11::arg("kernel") = 0);
   m.def("read_error", &read_error);
   m.def("clear_error", &clear_error);
   register_ops(m);

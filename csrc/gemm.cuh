@@ -36,8 +36,11 @@ struct GemmParams {
   float alpha;
   int64_t b_up_offset;  // kEpiSwiGLU: row offset (in N units) of the "up" half of B
   int max_ctas;         // 0 = one CTA per SM
+  int kernel = 0;       // 0 = choose, 1 = one-CTA kernel, 2 = CTA-pair kernel
 };
 
+// Dispatches to the one-CTA (gemm.cu) or the CTA-pair (gemm_pair.cu) kernel.
 void gemm_bf16(const GemmParams& p, cudaStream_t stream);
+void gemm_bf16_pair(const GemmParams& p, cudaStream_t stream);
 
 }  // namespace pb

@@ -1,0 +1,146 @@
+// Fused GEMM epilogues shared by the one-CTA and CTA-pair GEMM kernels: one
+// thread owns one output row of a tile and reads its accumulator row from
+// TMEM 32 columns at a time.
+#pragma once
+#include <cuda_bf16.h>
+
+#include "gemm.cuh"
+#include "ptx.cuh"
+
+namespace pb {
+namespace gemm_detail {
+
+struct EpiArgs {
+  void* C;
+  const void* R;
+  int64_t ldc, ldr;
+  float alpha;
+  int epi;
+  int64_t up_col;  // kEpiSwiGLU: column of the "up" half inside R
+};
+
+// silu(g) = g * sigmoid(g) with the fast reciprocal-based division.
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
+template <typename Fn>
+__device__ __forceinline__ void for_cols(int n0, int N, Fn fn) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (n0 + j < N) fn(j);
+}
+
+// Store 32 consecutive values of one output row (vectorised when all 32
+// columns are inside [0, N)).
+__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float* v, int n0, int N) {
+  if (n0 + 32 <= N) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 u;
+      u.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+      u.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+      u.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+      u.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+      d4[q] = u;
+    }
+  } else {
+    for_cols(n0, N, [&](int j) { dst[j] = __float2bfloat16(v[j]); });
+  }
+}
+
+__device__ __forceinline__ void load_row_bf16(const __nv_bfloat16* src, float* v, int n0, int N) {
+  if (n0 + 32 <= N) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 u = s4[q];
+      float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+      v[q * 8 + 0] = a.x; v[q * 8 + 1] = a.y; v[q * 8 + 2] = b.x; v[q * 8 + 3] = b.y;
+      v[q * 8 + 4] = c.x; v[q * 8 + 5] = c.y; v[q * 8 + 6] = d.x; v[q * 8 + 7] = d.y;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (n0 + j < N) ? __bfloat162float(src[j]) : 0.f;
+  }
+}
+
+// Epilogue of one accumulator row: t_row = TMEM address of the row's first
+// accumulator column, m = output row, n_base = first output column of the
+// tile.  BN = accumulator columns (SwiGLU: [gate BN/2 | up BN/2]).
+template <int BN, bool SWIGLU>
+__device__ __forceinline__ void epilogue_row(const EpiArgs& ep, uint32_t t_row, int m, int M, int N, int n_base) {
+  constexpr int BN_OUT = SWIGLU ? BN / 2 : BN;
+  if (SWIGLU) {
+#pragma unroll 1
+    for (int c = 0; c < BN_OUT; c += 32) {
+      float g[32], u[32];
+      tmem_ld32(t_row + c, g);
+      tmem_ld32(t_row + BN_OUT + c, u);
+      tmem_wait_ld();
+      const int n0 = n_base + c;
+      if (m < M) {
+        if (ep.R) {
+          __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(ep.R)) + (int64_t)m * ep.ldr;
+          store_row_bf16(gu + n0, g, n0, N);
+          store_row_bf16(gu + ep.up_col + n0, u, n0, N);
+        }
+        float h[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          // round the pre-activations to bf16 first so the forward matches a
+          // bf16 gate/up GEMM followed by silu(g)*u
+          const float gb = __bfloat162float(__float2bfloat16(g[j]));
+          const float ub = __bfloat162float(__float2bfloat16(u[j]));
+          h[j] = silu_f(gb) * ub;
+        }
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ep.C) + (int64_t)m * ep.ldc + n0;
+        store_row_bf16(dst, h, n0, N);
+      }
+    }
+    return;
+  }
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    float v[32];
+    tmem_ld32(t_row + c, v);
+    tmem_wait_ld();
+    const int n0 = n_base + c;
+    if (m < M && n0 < N) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= ep.alpha;
+      if (ep.epi == kEpiStoreBf16) {
+        store_row_bf16(reinterpret_cast<__nv_bfloat16*>(ep.C) + (int64_t)m * ep.ldc + n0, v, n0, N);
+      } else if (ep.epi == kEpiResidualBf16 || ep.epi == kEpiAccumBf16) {
+        const __nv_bfloat16* src =
+            ep.epi == kEpiResidualBf16
+                ? reinterpret_cast<const __nv_bfloat16*>(ep.R) + (int64_t)m * ep.ldr + n0
+                : reinterpret_cast<const __nv_bfloat16*>(ep.C) + (int64_t)m * ep.ldc + n0;
+        float r[32];
+        load_row_bf16(src, r, n0, N);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += r[j];
+        store_row_bf16(reinterpret_cast<__nv_bfloat16*>(ep.C) + (int64_t)m * ep.ldc + n0, v, n0, N);
+      } else {
+        float* dst = reinterpret_cast<float*>(ep.C) + (int64_t)m * ep.ldc + n0;
+        const bool accum = ep.epi == kEpiAccumF32;
+        if (n0 + 32 <= N) {
+          float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            float4 o = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+            if (accum) {
+              float4 p = d4[q];
+              o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+            }
+            d4[q] = o;
+          }
+        } else {
+          for_cols(n0, N, [&](int j) { dst[j] = accum ? dst[j] + v[j] : v[j]; });
+        }
+      }
+    }
+  }
+}
+
+}  // namespace gemm_detail
+}  // namespace pb

@@ -1,0 +1,270 @@
+// CTA-pair (2-SM) persistent bf16 GEMM on tcgen05.
+//
+// A cluster of two CTAs computes 256 x BN output tiles with
+// tcgen05.mma.cta_group::2: each CTA stages its own 128 rows of A and half of
+// B's BN columns, the MMA (issued by the even CTA) reads both CTAs' shared
+// memory and writes each CTA's 128 accumulator rows into its own TMEM.  Per
+// 64-deep k-step a CTA moves 32 KB through shared memory instead of the 48 KB
+// of a one-CTA 128 x 256 tile, which keeps the shared-memory traffic (TMA
+// writes + MMA reads) under the 128 B/clk the SM provides while the tensor
+// core runs at full rate.
+//
+// Roles per CTA (192 threads): warp 0 = TMA producer (both CTAs, each for its
+// own halves; completion bytes go to the even CTA's barrier), warp 1 = TMEM
+// allocator (both) + MMA issuer (even CTA), warps 2..5 = epilogue (both, one
+// output row per thread, the same fused epilogues as the one-CTA kernel).
+// The accumulator is double buffered in TMEM (2 x BN columns).  No load uses
+// cluster multicast; only MMA completion is multicast to both CTAs.
+//
+// Same products as gemm.cu (the nn.Linear GEMMs of the reference's HF
+// modules, parallel/parallel/engine/model_loading.py:17-35).
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "gemm.cuh"
+#include "gemm_epi.cuh"
+#include "host_util.h"
+#include "ptx.cuh"
+
+namespace pb {
+namespace {
+
+using gemm_detail::EpiArgs;
+
+constexpr int BM_CTA = 128;  // rows of A per CTA (tile M = 256)
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct PairCfg {
+  static constexpr int B_HALF = BN / 2;  // B rows (N) staged per CTA
+  static constexpr int A_BYTES = BM_CTA * BK * 2;
+  static constexpr int B_BYTES = B_HALF * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+template <int BN, bool A_MN, bool B_MN, bool SWIGLU>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiArgs ep,
+                     int M, int N, int K, int b_up_row, int* err) {
+  using Cfg = PairCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int B_HALF = Cfg::B_HALF;
+  constexpr int BN_OUT = SWIGLU ? BN / 2 : BN;
+  static_assert(!SWIGLU || B_HALF == BN_OUT, "SwiGLU: the even CTA stages gate rows, the odd CTA up rows");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;  // used on the even CTA (256 arrivals: both epilogues)
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull_bar[i], 1);
+      mbar_init(&tempty_bar[i], 2 * 128);
+    }
+    mbar_init(drain_bar, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before any cross-CTA use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles_m = (M + 2 * BM_CTA - 1) / (2 * BM_CTA);
+  const int tiles_n = (N + BN_OUT - 1) / BN_OUT;
+  const int num_tiles = tiles_m * tiles_n;
+  const int num_kb = (K + BK - 1) / BK;
+  const int n_clusters = gridDim.x >> 1;
+  const int cid = blockIdx.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = cid; tile < num_tiles && ok; tile += n_clusters) {
+        const int tm = tile % tiles_m, tn = tile / tiles_m;
+        const int a_row = tm * 2 * BM_CTA + (int)rank * BM_CTA;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, err)) { ok = false; break; }
+          const uint32_t full_even = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::STAGE_BYTES);
+          uint8_t* a_dst = sA + stage * Cfg::A_BYTES;
+          uint8_t* b_dst = sB + stage * Cfg::B_BYTES;
+          if (!A_MN) {
+            tma_load_2d_pair(a_dst, &tmA, full_even, kb * BK, a_row);
+          } else {
+#pragma unroll
+            for (int i = 0; i < BM_CTA / 64; ++i)
+              tma_load_2d_pair(a_dst + i * 64 * BK * 2, &tmA, full_even, a_row + i * 64, kb * BK);
+          }
+          if (SWIGLU) {
+            // even CTA: gate rows, odd CTA: up rows (B K-major)
+            tma_load_2d_pair(b_dst, &tmB, full_even, kb * BK, (leader ? 0 : b_up_row) + tn * BN_OUT);
+          } else if (!B_MN) {
+            tma_load_2d_pair(b_dst, &tmB, full_even, kb * BK, tn * BN + (int)rank * B_HALF);
+          } else {
+#pragma unroll
+            for (int i = 0; i < B_HALF / 64; ++i)
+              tma_load_2d_pair(b_dst + i * 64 * BK * 2, &tmB, full_even, tn * BN + (int)rank * B_HALF + i * 64,
+                               kb * BK);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(2 * BM_CTA, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = cid; tile < num_tiles && ok; tile += n_clusters, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * Cfg::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t adesc = A_MN ? smem_desc_sw128(a_base + kk * 2048, 64 * BK * 2, 1024)
+                                        : smem_desc_sw128(a_base + kk * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? smem_desc_sw128(b_base + kk * 2048, 64 * BK * 2, 1024)
+                                        : smem_desc_sw128(b_base + kk * 32, 16, 1024);
+            mma_bf16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit_pair(&empty_bar[stage], 0x3);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (ok) mma_commit_pair(&tfull_bar[acc], 0x3);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    int local = 0;
+    for (int tile = cid; tile < num_tiles; tile += n_clusters, ++local) {
+      const int tm = tile % tiles_m, tn = tile / tiles_m;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, err)) break;
+      tc_fence_after();
+      const int m = tm * 2 * BM_CTA + (int)rank * BM_CTA + row;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      gemm_detail::epilogue_row<BN, SWIGLU>(ep, t_row, m, M, N, tn * BN_OUT);
+      tc_fence_before();
+      mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
+    }
+  }
+
+  // On an error path the MMA issuer may have left MMAs in flight: drain them
+  // (bounded) before the accumulator columns are released.
+  if (warp == 1 && lane == 0 && leader && *((volatile int*)err) != 0) {
+    mma_commit_pair(drain_bar, 0x1);
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(smem_u32(drain_bar), 0) && globaltimer() - t0 < 100000000ull) {
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the pair MMA may still read its shared memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, bool SWIGLU>
+void launch_pair(const GemmParams& p, cudaStream_t stream) {
+  using Cfg = PairCfg<BN>;
+  auto kern = gemm_pair_kernel<BN, A_MN, B_MN, SWIGLU>;
+  static std::mutex mu;
+  static int max_clusters[64] = {0};
+  int dev = 0;
+  PB_CUDA_CHECK(cudaGetDevice(&dev));
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = stream;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (max_clusters[dev & 63] == 0) {
+      PB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+      cfg.gridDim = dim3(2 * num_sms(dev) / 2, 1, 1);
+      int n = 0;
+      PB_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+      PB_CHECK(n > 0, "gemm pair: no cluster of two CTAs fits on this GPU");
+      max_clusters[dev & 63] = n;
+    }
+  }
+  CUtensorMap ta = A_MN ? make_tmap_2d_bf16(p.A, p.M, p.K, p.lda, 64, BK)
+                        : make_tmap_2d_bf16(p.A, p.K, p.M, p.lda, BK, BM_CTA);
+  CUtensorMap tb;
+  if (SWIGLU)
+    tb = make_tmap_2d_bf16(p.B, p.K, p.b_up_offset + p.N, p.ldb, BK, Cfg::B_HALF);
+  else
+    tb = B_MN ? make_tmap_2d_bf16(p.B, p.N, p.K, p.ldb, 64, BK)
+              : make_tmap_2d_bf16(p.B, p.K, p.N, p.ldb, BK, Cfg::B_HALF);
+  EpiArgs ep{p.C, p.R, p.ldc, p.ldr, p.alpha, p.epi, SWIGLU ? p.b_up_offset : 0};
+  const int bn_out = SWIGLU ? BN / 2 : BN;
+  const int tiles = ((p.M + 2 * BM_CTA - 1) / (2 * BM_CTA)) * ((p.N + bn_out - 1) / bn_out);
+  int clusters = max_clusters[dev & 63];
+  if (p.max_ctas > 0) clusters = std::min(clusters, std::max(1, p.max_ctas / 2));
+  clusters = std::max(1, std::min(clusters, tiles));
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  PB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, ep, p.M, p.N, p.K, (int)p.b_up_offset, error_word(dev)));
+}
+
+}  // namespace
+
+void gemm_bf16_pair(const GemmParams& p, cudaStream_t stream) {
+  if (p.epi == kEpiSwiGLU) return launch_pair<256, false, false, true>(p, stream);
+  if (!p.a_mn && !p.b_mn) return launch_pair<256, false, false, false>(p, stream);
+  if (!p.a_mn && p.b_mn) return launch_pair<256, false, true, false>(p, stream);
+  if (p.a_mn && !p.b_mn) return launch_pair<256, true, false, false>(p, stream);
+  return launch_pair<256, true, true, false>(p, stream);
+}
+
+}  // namespace pb

@@ -41,6 +41,53 @@ def test_gemm_layouts(M, N, K, a_mn, b_mn):
     assert _rel_err(out, ref) < 1e-2
 
 
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (512, 512, 256), (304, 200, 136), (1000, 1536, 1024),
+                                   (8192, 1024, 1024), (1024, 3072, 2048)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+def test_gemm_pair_layouts(M, N, K, a_mn, b_mn):
+    """The CTA-pair (cta_group::2) kernel, forced, against fp32 PyTorch."""
+    C = _ext()
+    torch.manual_seed(0)
+    A = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    B = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    a_arg = A.t().contiguous() if a_mn else A
+    b_arg = B.t().contiguous() if b_mn else B
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm(a_arg, b_arg, out, a_mn, b_mn, 0, 1.0, kernel=2)
+    _check_no_device_error()
+    ref = A.float() @ B.float().t()
+    assert _rel_err(out, ref) < 1e-2
+
+
+def test_gemm_pair_epilogues():
+    C = _ext()
+    torch.manual_seed(1)
+    M, N, K = 640, 384, 320
+    A = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    B = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    R = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+    ref = A.float() @ B.float().t()
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm(A, B, out, False, False, 1, 1.0, R, kernel=2)
+    assert _rel_err(out, ref + R.float()) < 1e-2
+    out32 = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    C.gemm(A, B, out32, False, False, 2, 0.5, kernel=2)
+    assert _rel_err(out32, 0.5 * ref) < 1e-3
+    C.gemm(A, B, out32, False, False, 4, 0.5, kernel=2)
+    assert _rel_err(out32, ref) < 1e-3
+    # SwiGLU: B rows [0, I) gate, [I, 2I) up
+    T, I, H = 768, 384, 256
+    x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(2 * I, H, device="cuda", dtype=torch.bfloat16) / math.sqrt(H)
+    h = torch.empty(T, I, device="cuda", dtype=torch.bfloat16)
+    gu = torch.empty(T, 2 * I, device="cuda", dtype=torch.bfloat16)
+    C.gemm(x, w, h, False, False, 5, 1.0, gu, I, I, kernel=2)
+    _check_no_device_error()
+    gu_ref = x.float() @ w.float().t()
+    assert _rel_err(gu, gu_ref) < 1e-2
+    assert _rel_err(h, torch.nn.functional.silu(gu_ref[:, :I]) * gu_ref[:, I:]) < 2e-2
+
+
 def test_gemm_epilogues():
     C = _ext()
     torch.manual_seed(1)
