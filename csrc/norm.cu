@@ -126,69 +126,96 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int64_t
 // per warp.  Optionally adds a residual-stream gradient (dres) into dx, which
 // fuses the add autograd would otherwise run for "x -> norm(x) and x -> +".
 template <int CH>
-__global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(
+__global__ void __launch_bounds__(256, 2) rmsnorm_bwd_reg_kernel(
     const __nv_bfloat16* __restrict__ dy, int64_t lddy, const __nv_bfloat16* __restrict__ x, int64_t ldx,
     const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dres,
     int64_t lddres, __nv_bfloat16* __restrict__ dx, int64_t lddx, float* __restrict__ dw, int rows,
     int rows_per_block) {
+  // One warp per row, all of the row's loads (x, dy, dres) issued before the
+  // reduction and kept packed in registers, so a row costs one DRAM round
+  // trip.  Weight-grad partials live in a per-warp shared-memory slice (each
+  // lane owns its columns: no atomics) and are summed once per block.
   constexpr int cols = CH * 256;
-  extern __shared__ float sdw[];
-  for (int c = threadIdx.x; c < cols; c += blockDim.x) sdw[c] = 0.f;
-  __syncthreads();
+  extern __shared__ float sdw[];  // [warps][cols]
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
-  float acc[CH][8];
+  float* mine = sdw + (threadIdx.x >> 5) * cols;
+  if (dw) {
 #pragma unroll
-  for (int k = 0; k < CH; ++k)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[k][j] = 0.f;
+    for (int k = 0; k < CH; ++k) {
+      float4* d4 = reinterpret_cast<float4*>(mine + k * 256 + lane * 8);
+      d4[0] = d4[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
   const int r0 = blockIdx.x * rows_per_block;
   const int r1 = min(rows, r0 + rows_per_block);
   for (int row = r0 + (threadIdx.x >> 5); row < r1; row += warps) {
     const float r = rstd[row];
-    const __nv_bfloat16* xr = x + (int64_t)row * ldx;
-    const __nv_bfloat16* gr = dy + (int64_t)row * lddy;
-    float dot = 0.f;
+    uint4 xp[CH], gp[CH], rp[CH];
 #pragma unroll
     for (int k = 0; k < CH; ++k) {
       const int c = k * 256 + lane * 8;
-      float xv[8], gv[8], wv[8];
-      load8(xr + c, xv);
-      load8(gr + c, gv);
-      load8(w + c, wv);
+      xp[k] = *reinterpret_cast<const uint4*>(x + (int64_t)row * ldx + c);
+      gp[k] = *reinterpret_cast<const uint4*>(dy + (int64_t)row * lddy + c);
+      if (dres) rp[k] = *reinterpret_cast<const uint4*>(dres + (int64_t)row * lddres + c);
+    }
+    float dot = 0.f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float xh = xv[j] * r;
-        dot += gv[j] * wv[j] * xh;
-        acc[k][j] += gv[j] * bfr(xh);
+    for (int k = 0; k < CH; ++k) {
+      const uint32_t* xu = &xp[k].x;
+      const uint32_t* gu = &gp[k].x;
+      const uint4 wq = __ldg(reinterpret_cast<const uint4*>(w + k * 256 + lane * 8));  // L1-resident
+      const uint32_t* wu = &wq.x;
+      float a[8];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 xv = unpack_bf16x2(xu[q]), gv = unpack_bf16x2(gu[q]), wv = unpack_bf16x2(wu[q]);
+        const float xh0 = xv.x * r, xh1 = xv.y * r;
+        dot += gv.x * wv.x * xh0 + gv.y * wv.y * xh1;
+        a[2 * q] = gv.x * bfr(xh0);
+        a[2 * q + 1] = gv.y * bfr(xh1);
+      }
+      if (dw) {
+        float4* d4 = reinterpret_cast<float4*>(mine + k * 256 + lane * 8);
+        float4 u0 = d4[0], u1 = d4[1];
+        u0.x += a[0]; u0.y += a[1]; u0.z += a[2]; u0.w += a[3];
+        u1.x += a[4]; u1.y += a[5]; u1.z += a[6]; u1.w += a[7];
+        d4[0] = u0;
+        d4[1] = u1;
       }
     }
     dot = warp_sum(dot) / (float)cols;
 #pragma unroll
     for (int k = 0; k < CH; ++k) {
       const int c = k * 256 + lane * 8;
-      float xv[8], gv[8], wv[8], o[8];
-      load8(xr + c, xv);
-      load8(gr + c, gv);
-      load8(w + c, wv);
+      const uint32_t* xu = &xp[k].x;
+      const uint32_t* gu = &gp[k].x;
+      const uint4 wq = __ldg(reinterpret_cast<const uint4*>(w + c));
+      const uint32_t* wu = &wq.x;
+      const uint32_t* ru = &rp[k].x;
+      uint4 o;
+      uint32_t* ou = &o.x;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = r * (gv[j] * wv[j] - xv[j] * r * dot);
-      if (dres) {
-        float rv[8];
-        load8(dres + (int64_t)row * lddres + c, rv);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] += rv[j];
+      for (int q = 0; q < 4; ++q) {
+        const float2 xv = unpack_bf16x2(xu[q]), gv = unpack_bf16x2(gu[q]), wv = unpack_bf16x2(wu[q]);
+        float o0 = r * (gv.x * wv.x - xv.x * r * dot), o1 = r * (gv.y * wv.y - xv.y * r * dot);
+        if (dres) {
+          const float2 rv = unpack_bf16x2(ru[q]);
+          o0 += rv.x;
+          o1 += rv.y;
+        }
+        ou[q] = pack_bf16x2(o0, o1);
       }
-      store8(dx + (int64_t)row * lddx + c, o);
+      *reinterpret_cast<uint4*>(dx + (int64_t)row * lddx + c) = o;
     }
   }
   if (dw) {
-#pragma unroll
-    for (int k = 0; k < CH; ++k)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) atomicAdd(&sdw[k * 256 + lane * 8 + j], acc[k][j]);
     __syncthreads();
-    for (int c = threadIdx.x; c < cols; c += blockDim.x) atomicAdd(&dw[c], sdw[c]);
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+      float t = 0.f;
+      for (int w8 = 0; w8 < warps; ++w8) t += sdw[w8 * cols + c];
+      atomicAdd(&dw[c], t);
+    }
   }
 }
 
@@ -209,6 +236,9 @@ __global__ void qknorm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, in
                                        __nv_bfloat16* __restrict__ q_out, int64_t ldq,
                                        __nv_bfloat16* __restrict__ k_out, int64_t ldk,
                                        float* __restrict__ rstd, int T, int S, int nq, int nkv, float eps) {
+  // The bf16 products / sums of the reference's op-by-op bf16 arithmetic run
+  // as packed bf16x2 instructions: a product of two bf16 values is exact in
+  // fp32, so the packed multiply rounds exactly like fp32-multiply-then-round.
   constexpr int D = 128;
   const int lane = threadIdx.x & 31;
   const int hl = lane & 15;
@@ -219,36 +249,53 @@ __global__ void qknorm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, in
   if (!valid) item = total - 1;  // keep all lanes in the shuffles
   const int t = (int)(item / nh), h = (int)(item % nh);
   const bool is_q = h < nq;
-  float v[8], wv[8], cv[8], sv[8];
-  load8(qkv + (int64_t)t * ldqkv + (int64_t)h * D + hl * 8, v);
+  const int pos = t % S;
+  // every load issued before the reduction (one round trip per item)
+  const uint4 xv = *reinterpret_cast<const uint4*>(qkv + (int64_t)t * ldqkv + (int64_t)h * D + hl * 8);
+  const uint4 wv = __ldg(reinterpret_cast<const uint4*>((is_q ? qw : kw) + hl * 8));
+  const uint4 cv = __ldg(reinterpret_cast<const uint4*>(cosb + (int64_t)pos * D + hl * 8));
+  uint4 sv = __ldg(reinterpret_cast<const uint4*>(sinb + (int64_t)pos * D + hl * 8));
+  const uint32_t* x32 = &xv.x;
+  float xf[8];
   float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+  for (int q = 0; q < 4; ++q) {
+    const float2 f = unpack_bf16x2(x32[q]);
+    xf[2 * q] = f.x;
+    xf[2 * q + 1] = f.y;
+    ss += f.x * f.x + f.y * f.y;
+  }
   ss = half_sum(ss);
   const float r = rsqrtf(ss / (float)D + eps);
-  load8((is_q ? qw : kw) + hl * 8, wv);
-  float n[8], p[8];
+  // rotate_half: [-x2, x1] -> the first half of the lanes takes -sin
+  if (hl < 8) {
+    sv.x ^= 0x80008000u; sv.y ^= 0x80008000u; sv.z ^= 0x80008000u; sv.w ^= 0x80008000u;
+  }
+  const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv);
+  const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&cv);
+  const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(&sv);
+  uint4 ov;
+  uint32_t* o32 = &ov.x;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) n[j] = bfr(wv[j] * bfr(v[j] * r));
-#pragma unroll
-  for (int j = 0; j < 8; ++j) p[j] = __shfl_xor_sync(0xffffffffu, n[j], 8);
-  const int pos = t % S;
-  load8(cosb + (int64_t)pos * D + hl * 8, cv);
-  load8(sinb + (int64_t)pos * D + hl * 8, sv);
-  const float sign = hl < 8 ? -1.f : 1.f;  // rotate_half: [-x2, x1]
-  float o[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) o[j] = bfr(bfr(n[j] * cv[j]) + bfr(sign * p[j] * sv[j]));
+  for (int q = 0; q < 4; ++q) {
+    const __nv_bfloat162 xh = __floats2bfloat162_rn(xf[2 * q] * r, xf[2 * q + 1] * r);
+    const __nv_bfloat162 n = __hmul2(w2[q], xh);
+    const uint32_t nu = *reinterpret_cast<const uint32_t*>(&n);
+    const uint32_t pu = __shfl_xor_sync(0xffffffffu, nu, 8);
+    const __nv_bfloat162 pn = *reinterpret_cast<const __nv_bfloat162*>(&pu);
+    const __nv_bfloat162 o = __hadd2(__hmul2(n, c2[q]), __hmul2(pn, s2[q]));
+    o32[q] = *reinterpret_cast<const uint32_t*>(&o);
+  }
   if (!valid) return;
   if (hl == 0) rstd[(int64_t)t * nh + h] = r;
   __nv_bfloat16* dst = is_q ? q_out + (int64_t)t * ldq + (int64_t)h * D
                             : k_out + (int64_t)t * ldk + (int64_t)(h - nq) * D;
-  store8(dst + hl * 8, o);
+  *reinterpret_cast<uint4*>(dst + hl * 8) = ov;
 }
 
 // Backward of the above; q/k norm weight grads: per-lane registers, then one
 // shared-memory reduction per block.
-__global__ void qknorm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dq, int64_t lddq,
+__global__ void __launch_bounds__(256, 2) qknorm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dq, int64_t lddq,
                                        const __nv_bfloat16* __restrict__ dk, int64_t lddk,
                                        const __nv_bfloat16* __restrict__ qkv, int64_t ldqkv,
                                        const __nv_bfloat16* __restrict__ qw,
@@ -259,7 +306,11 @@ __global__ void qknorm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dq, int
                                        __nv_bfloat16* __restrict__ dqkv, int64_t lddqkv,
                                        float* __restrict__ dqw, float* __restrict__ dkw, int T, int S,
                                        int nq, int nkv, int items_per_block) {
+  // A half warp per (token, head) item, two items per iteration with every
+  // load (gradient, input row, rstd, cos/sin) issued before the first
+  // shuffle, so an iteration costs one DRAM round trip for two items.
   constexpr int D = 128;
+  constexpr int U = 2;
   __shared__ float sdw[2][D];
   for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) (&sdw[0][0])[i] = 0.f;
   __syncthreads();
@@ -276,45 +327,69 @@ __global__ void qknorm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dq, int
   load8(kw + hl * 8, kw_r);
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc_q[j] = acc_k[j] = 0.f;
+  const float sign = hl < 8 ? 1.f : -1.f;
   // every lane iterates the same number of times so shuffles stay converged
   const int64_t span = i1 - i0;
-  const int64_t iters = (span + slots - 1) / slots;
+  const int64_t iters = (span + slots * U - 1) / (slots * U);
   for (int64_t it = 0; it < iters; ++it) {
-    int64_t item = i0 + it * slots + slot;
-    const bool valid = item < i1;
-    if (!valid) item = i1 - 1;
-    const int t = (int)(item / nh), h = (int)(item % nh);
-    const bool is_q = h < nq;
-    float gv[8], cv[8], sv[8], xv[8];
-    load8(is_q ? dq + (int64_t)t * lddq + (int64_t)h * D + hl * 8
-               : dk + (int64_t)t * lddk + (int64_t)(h - nq) * D + hl * 8, gv);
-    const int pos = t % S;
-    load8(cosb + (int64_t)pos * D + hl * 8, cv);
-    load8(sinb + (int64_t)pos * D + hl * 8, sv);
-    // dn[i] = g[i]*c[i] + (i<64 ? g[i+64]*s[i+64] : -g[i-64]*s[i-64])
-    float gs[8];
+    uint4 gp[U], xp[U], cp[U], sp[U];
+    float rr[U];
+    int hh[U], tt[U];
+    bool valid[U];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) gs[j] = __shfl_xor_sync(0xffffffffu, gv[j] * sv[j], 8);
-    const float sign = hl < 8 ? 1.f : -1.f;
-    float dn[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) dn[j] = gv[j] * cv[j] + sign * gs[j];
-    load8(qkv + (int64_t)t * ldqkv + (int64_t)h * D + hl * 8, xv);
-    const float* wv = is_q ? qw_r : kw_r;
-    const float r = rstd[(int64_t)t * nh + h];
-    float dot = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) dot += dn[j] * wv[j] * xv[j] * r;
-    dot = half_sum(dot) / (float)D;
-    if (!valid) continue;
-    float dx[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      dx[j] = r * (dn[j] * wv[j] - xv[j] * r * dot);
-      const float contrib = dn[j] * bfr(xv[j] * r);
-      if (is_q) acc_q[j] += contrib; else acc_k[j] += contrib;
+    for (int u = 0; u < U; ++u) {
+      int64_t item = i0 + (it * U + u) * slots + slot;
+      valid[u] = item < i1;
+      if (!valid[u]) item = i1 - 1;
+      const int t = (int)(item / nh), h = (int)(item % nh);
+      tt[u] = t;
+      hh[u] = h;
+      const bool is_q = h < nq;
+      gp[u] = *reinterpret_cast<const uint4*>(is_q ? dq + (int64_t)t * lddq + (int64_t)h * D + hl * 8
+                                                   : dk + (int64_t)t * lddk + (int64_t)(h - nq) * D + hl * 8);
+      xp[u] = *reinterpret_cast<const uint4*>(qkv + (int64_t)t * ldqkv + (int64_t)h * D + hl * 8);
+      const int pos = t % S;
+      cp[u] = *reinterpret_cast<const uint4*>(cosb + (int64_t)pos * D + hl * 8);
+      sp[u] = *reinterpret_cast<const uint4*>(sinb + (int64_t)pos * D + hl * 8);
+      rr[u] = rstd[(int64_t)t * nh + h];
     }
-    store8(dqkv + (int64_t)t * lddqkv + (int64_t)h * D + hl * 8, dx);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const bool is_q = hh[u] < nq;
+      float gv[8], cv[8], sv[8], xv[8];
+      const uint32_t* g32 = &gp[u].x;
+      const uint32_t* x32 = &xp[u].x;
+      const uint32_t* c32 = &cp[u].x;
+      const uint32_t* s32 = &sp[u].x;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 a = unpack_bf16x2(g32[q]), b = unpack_bf16x2(x32[q]), c = unpack_bf16x2(c32[q]),
+                     d = unpack_bf16x2(s32[q]);
+        gv[2 * q] = a.x; gv[2 * q + 1] = a.y;
+        xv[2 * q] = b.x; xv[2 * q + 1] = b.y;
+        cv[2 * q] = c.x; cv[2 * q + 1] = c.y;
+        sv[2 * q] = d.x; sv[2 * q + 1] = d.y;
+      }
+      // dn[i] = g[i]*c[i] + (i<64 ? g[i+64]*s[i+64] : -g[i-64]*s[i-64])
+      float dn[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dn[j] = gv[j] * cv[j] + sign * __shfl_xor_sync(0xffffffffu, gv[j] * sv[j], 8);
+      const float* wv = is_q ? qw_r : kw_r;
+      const float r = rr[u];
+      float dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dot += dn[j] * wv[j] * xv[j] * r;
+      dot = half_sum(dot) / (float)D;
+      if (!valid[u]) continue;
+      float dx[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        dx[j] = r * (dn[j] * wv[j] - xv[j] * r * dot);
+        const float contrib = dn[j] * bfr(xv[j] * r);
+        if (is_q) acc_q[j] += contrib; else acc_k[j] += contrib;
+      }
+      store8(dqkv + (int64_t)tt[u] * lddqkv + (int64_t)hh[u] * D + hl * 8, dx);
+    }
   }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -344,20 +419,20 @@ void rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const
                  const float* rstd, void* dx, int64_t lddx, float* dw_acc, int rows, int cols,
                  cudaStream_t s, const void* dres, int64_t lddres) {
   PB_CHECK(cols % 8 == 0, "rmsnorm: cols must be a multiple of 8");
-  const int blocks = num_sms() * 2;
+  const int blocks = num_sms() * 2;  // one wave: two 256-thread blocks per SM
   const int rpb = (rows + blocks - 1) / blocks;
   const int grid = (rows + rpb - 1) / rpb;
   const size_t smem = (size_t)cols * sizeof(float);
-  if (cols % 256 == 0 && cols <= 2048) {
+  const size_t smem_reg = (size_t)8 * cols * sizeof(float);  // per-warp partials (<= 48 KB)
+  if (cols % 256 == 0 && cols <= 1536) {  // wider rows would spill: generic kernel
 #define PB_RMS_BWD(CH)                                                                                     \
   case CH:                                                                                                \
-    rmsnorm_bwd_reg_kernel<CH><<<grid, 256, smem, s>>>(                                                    \
+    rmsnorm_bwd_reg_kernel<CH><<<grid, 256, smem_reg, s>>>(                                                \
         (const __nv_bfloat16*)dy, lddy, (const __nv_bfloat16*)x, ldx, (const __nv_bfloat16*)w, rstd,      \
         (const __nv_bfloat16*)dres, lddres, (__nv_bfloat16*)dx, lddx, dw_acc, rows, rpb);                 \
     break;
     switch (cols / 256) {
-      PB_RMS_BWD(1) PB_RMS_BWD(2) PB_RMS_BWD(3) PB_RMS_BWD(4) PB_RMS_BWD(5) PB_RMS_BWD(6) PB_RMS_BWD(7)
-      PB_RMS_BWD(8)
+      PB_RMS_BWD(1) PB_RMS_BWD(2) PB_RMS_BWD(3) PB_RMS_BWD(4) PB_RMS_BWD(5) PB_RMS_BWD(6)
     }
 #undef PB_RMS_BWD
     PB_CUDA_CHECK(cudaGetLastError());
@@ -391,7 +466,7 @@ void qknorm_rope_bwd(const void* dq, int64_t lddq, const void* dk, int64_t lddk,
                      cudaStream_t s) {
   PB_CHECK(D == 128, "qknorm_rope: head_dim 128 only");
   const int items = T * (nq + nkv);
-  const int blocks = num_sms() * 4;
+  const int blocks = num_sms() * 2;  // one wave
   const int ipb = (items + blocks - 1) / blocks;
   const int grid = (items + ipb - 1) / ipb;
   qknorm_rope_bwd_kernel<<<grid, 256, 0, s>>>(

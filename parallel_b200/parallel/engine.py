@@ -74,6 +74,10 @@ class ParallelEngine:
         configure_collective_profiling(enabled=_cfg_get(eng, "collective_profiling", False), device=device)
         self.sync_finite_check = bool(_cfg_get(eng, "sync_finite_check", False))
         self._pending_nonfinite: torch.Tensor | None = None
+        # asynchronous read-back of the non-finite flag: copied into pinned
+        # host memory behind an event at the end of step k, read at step k+1
+        self._flag_host: torch.Tensor | None = None
+        self._flag_event = None
         self._last_grad_norm: torch.Tensor | None = None
         self.reset_step_memory_stats()
 
@@ -174,11 +178,28 @@ class ParallelEngine:
             self._step_impl()
 
     def _check_pending_nonfinite(self):
-        if self._pending_nonfinite is not None:
+        if self._pending_nonfinite is None:
+            return
+        if self._flag_event is not None:
+            # waits only for the end of the previous optimizer step, which the
+            # GPU has normally passed long ago (no pipeline drain)
+            self._flag_event.synchronize()
+            bad = bool(self._flag_host[0].item())
+            self._flag_event = None
+        else:
             bad = bool(self._pending_nonfinite.item())
-            self._pending_nonfinite = None
-            if bad:
-                raise FloatingPointError("Non-finite gradients encountered")
+        self._pending_nonfinite = None
+        if bad:
+            raise FloatingPointError("Non-finite gradients encountered")
+
+    def _defer_nonfinite_check(self, flag: torch.Tensor):
+        self._pending_nonfinite = flag
+        if flag.is_cuda:
+            if self._flag_host is None:
+                self._flag_host = torch.zeros(1, dtype=flag.dtype, pin_memory=True)
+            self._flag_host.copy_(flag.reshape(1), non_blocking=True)
+            self._flag_event = torch.cuda.Event()
+            self._flag_event.record()
 
     def _grad_lists(self):
         """(grad tensors, weights) for the norm: replicated TP params count once."""
@@ -239,7 +260,7 @@ class ParallelEngine:
                 self._pending_nonfinite = flag
                 self._check_pending_nonfinite()
             else:
-                self._pending_nonfinite = flag
+                self._defer_nonfinite_check(flag)
             return
         # generic path (CPU / fp16 scaler): reference semantics with host syncs
         finite = self._grads_are_finite()
