@@ -25,7 +25,7 @@ import sys
 import tempfile
 import time
 import types
-from datetime import timedelta
+from datetime import datetime, timedelta
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "train tokens/s (device-timed, max over ranks) @1/2/4/8 B200 vs ref NCCL build"
@@ -50,27 +50,42 @@ def parse():
 
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """One nvidia-smi poller per node (local rank 0) over every local GPU of
+    the job, started before the warm-up so its start-up cost stays out of the
+    timed region; only samples whose timestamps fall inside the marked timed
+    window are reported."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu_index = gpu_index
+    def __init__(self, local_rank: int, local_world: int):
+        self.active = local_rank == 0
+        self.gpus = ",".join(str(i) for i in range(max(1, local_world)))
         self.proc = None
         self.path = None
+        self.window = None
 
     def start(self):
+        if not self.active:
+            return
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.gpu_index), "-f", self.path],
+                 "-i", self.gpus, "-f", self.path],
                 stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
+    def mark(self, t0: float, t1: float):
+        """Host wall-clock bounds of the timed region."""
+        self.window = (t0, t1)
+
     def stop(self) -> dict:
+        if not self.active:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["sampled on local rank 0"]}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         self.proc.terminate()
@@ -78,26 +93,36 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = []
         try:
             for line in open(self.path):
                 parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9:
+                if len(parts) < 10:
                     continue
                 try:
-                    sm.append(float(parts[1]))
-                    mx.append(float(parts[2]))
+                    ts = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                    rows.append((ts, float(parts[2]), float(parts[3]), parts[6:10]))
                 except ValueError:
                     continue
-                for n, v in zip(names, parts[5:9]):
-                    if v.lower() == "active":
-                        reasons.add(n)
             os.unlink(self.path)
         except Exception:
             pass
+        inside = rows
+        if self.window is not None:
+            inside = [r for r in rows if self.window[0] <= r[0] <= self.window[1]]
+            if not inside and rows:  # region shorter than the poll period: nearest samples
+                mid = 0.5 * (self.window[0] + self.window[1])
+                inside = sorted(rows, key=lambda r: abs(r[0] - mid))[: max(1, len(self.gpus.split(",")))]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in inside:
+            for n, v in zip(names, r[3]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        sm = [r[1] for r in inside]
+        mx = [r[2] for r in inside]
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "gpus": self.gpus}
 
 
 # --------------------------------------------------------------------------- timing helpers
@@ -217,13 +242,15 @@ def run_ours(args, rank, world, local):
         engine.step()
         return loss
 
+    clocks = ClockSampler(local, int(os.environ.get("LOCAL_WORLD_SIZE", world)))
+    clocks.start()
     for i in range(args.warmup):
         step(dev[i % nb])
     torch.cuda.synchronize()
     check_device_errors()
-    clocks = ClockSampler(local)
-    clocks.start()
+    t_wall0 = time.time()
     ms = time_steps(step, dev, args.steps)
+    clocks.mark(t_wall0, time.time())
     clk = clocks.stop()
     ms = max_over_ranks(ms)
     check_device_errors()
@@ -360,11 +387,13 @@ def run_reference(args, rank, world, local):
             model.to(device)
         model.train()
         engine = RefEngine(model, None, pconfig, cfg, device, mp_plan=plan)
+    clocks = ClockSampler(local, int(os.environ.get("LOCAL_WORLD_SIZE", world)))
+    clocks.start()
     for i in range(args.warmup):
         step(dev[i % nb])
-    clocks = ClockSampler(local)
-    clocks.start()
+    t_wall0 = time.time()
     ms = time_steps(step, dev, args.steps)
+    clocks.mark(t_wall0, time.time())
     clk = clocks.stop()
     ms = max_over_ranks(ms)
     e2e = None
