@@ -10,8 +10,8 @@ parallel/parallel/engine/model_parallel/sequence_parallel.py:48-158):
 * ``reduce_scatter_sequence`` reduce-scatter(dim 1) fwd / all-gather bwd
 * ``scatter_sequence``       split(dim 1) fwd / all-gather bwd
 
-Each takes the model's ``ParallelContext``; the data plane is the context's
-collectives object (NCCL/gloo by default, the NVLink P2P kernels on B200).
+Each takes the model's ``ParallelContext``; the data plane is torch.distributed
+(NCCL on GPUs, gloo on CPU).
 """
 from __future__ import annotations
 
