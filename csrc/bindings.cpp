@@ -68,6 +68,104 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, 
   pb::gemm_bf16(p, cur_stream());
 }
 
+// gemm_ag: out = gather(A shards) @ B^T (or @ B when b_mn) with the
+// sequence-parallel all-gather inside the GEMM kernel.  `dst` [T, K] receives
+// the gathered A (kept for the weight gradient); src_ptrs[r] are the ranks'
+// shards [batch*seq_local, K] (peer pointers of a symmetric buffer); flags is
+// an int32 tensor with one counter per 256-row block of dst, bumped by
+// 256/16 per block and call; `target` = that count after this call.
+void gemm_ag(at::Tensor& dst, const std::vector<int64_t>& src_ptrs, int64_t src_ld, at::Tensor& flags,
+             int64_t target, int64_t seq, int64_t seq_local, int64_t batch, const std::vector<int64_t>& m_order,
+             const at::Tensor& b, at::Tensor& out, bool b_mn, int64_t epi, double alpha,
+             const c10::optional<at::Tensor>& r, int64_t b_up_offset, int64_t n_out) {
+  CHECK_CUDA_BF16(dst);
+  CHECK_CUDA_BF16(b);
+  TORCH_CHECK(dst.is_contiguous() && flags.is_cuda() && flags.scalar_type() == at::kInt, "gemm_ag: dst / flags");
+  TORCH_CHECK(src_ptrs.size() >= 1 && src_ptrs.size() <= 8, "gemm_ag: 1..8 shards");
+  TORCH_CHECK(m_order.size() == (size_t)((dst.size(0) + 255) / 256) && m_order.size() <= 64, "gemm_ag: m_order");
+  TORCH_CHECK(flags.numel() >= (int64_t)m_order.size(), "gemm_ag: flags too small");
+  const c10::cuda::CUDAGuard guard(dst.device());
+  pb::GatherArgs g{};
+  for (size_t i = 0; i < src_ptrs.size(); ++i) g.src[i] = reinterpret_cast<const void*>(src_ptrs[i]);
+  g.dst = dst.data_ptr();
+  g.flags = flags.data_ptr<int>();
+  g.target = (int)target;
+  g.nranks = (int)src_ptrs.size();
+  g.seq = (int)seq;
+  g.seq_local = (int)seq_local;
+  g.batch = (int)batch;
+  g.src_ld = src_ld;
+  g.n_blocks = (int)m_order.size();
+  for (size_t i = 0; i < m_order.size(); ++i) g.m_order[i] = (int)m_order[i];
+  TORCH_CHECK(seq == seq_local * (int64_t)src_ptrs.size() && dst.size(0) == batch * seq, "gemm_ag: sizes");
+  pb::GemmParams p{};
+  p.A = dst.data_ptr();
+  p.B = b.data_ptr();
+  p.C = out.data_ptr();
+  p.lda = dst.stride(0);
+  p.ldb = b.stride(0);
+  p.ldc = out.stride(0);
+  p.a_mn = false;
+  p.b_mn = b_mn;
+  p.M = dst.size(0);
+  p.K = dst.size(1);
+  p.N = b_mn ? b.size(1) : b.size(0);
+  p.epi = (int)epi;
+  p.alpha = (float)alpha;
+  p.b_up_offset = b_up_offset;
+  if (epi == pb::kEpiSwiGLU) {
+    p.N = (int)n_out;
+    TORCH_CHECK(b_up_offset + n_out <= b.size(0), "gemm_ag: swiglu B too small");
+  }
+  TORCH_CHECK(out.size(0) == p.M && out.size(1) == p.N && out.scalar_type() == at::kBFloat16, "gemm_ag: out");
+  if (r.has_value() && r->defined()) {
+    CHECK_CUDA_BF16(*r);
+    p.R = r->data_ptr();
+    p.ldr = r->stride(0);
+  }
+  TORCH_CHECK(epi == pb::kEpiStoreBf16 || epi == pb::kEpiSwiGLU, "gemm_ag: store or SwiGLU epilogue");
+  p.gather = &g;
+  pb::gemm_bf16(p, cur_stream());
+}
+
+// gemm_rs: partial = A @ B^T (or A @ B when b_mn) over the full sequence, each
+// output row stored as bf16 into its owner's receive buffer (peer_ptrs[owner])
+// at slot `slot`: row (slot*slot_rows + b*seq_local + s % seq_local), stride ldc.
+void gemm_rs(const at::Tensor& a, const at::Tensor& b, bool b_mn, double alpha, const std::vector<int64_t>& peer_ptrs,
+             int64_t ldc, int64_t seq, int64_t seq_local, int64_t slot, int64_t slot_rows) {
+  CHECK_CUDA_BF16(a);
+  CHECK_CUDA_BF16(b);
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1, "gemm_rs: unit inner strides");
+  TORCH_CHECK(peer_ptrs.size() >= 1 && peer_ptrs.size() <= 8 && seq == seq_local * (int64_t)peer_ptrs.size(),
+              "gemm_rs: ranks / sequence");
+  const c10::cuda::CUDAGuard guard(a.device());
+  pb::ScatterArgs sc{};
+  for (size_t i = 0; i < peer_ptrs.size(); ++i) sc.peer[i] = reinterpret_cast<void*>(peer_ptrs[i]);
+  sc.nranks = (int)peer_ptrs.size();
+  sc.seq = (int)seq;
+  sc.seq_local = (int)seq_local;
+  sc.slot = (int)slot;
+  sc.slot_rows = slot_rows;
+  pb::GemmParams p{};
+  p.A = a.data_ptr();
+  p.B = b.data_ptr();
+  p.C = reinterpret_cast<void*>(peer_ptrs[0]);
+  p.lda = a.stride(0);
+  p.ldb = b.stride(0);
+  p.ldc = ldc;
+  p.a_mn = false;
+  p.b_mn = b_mn;
+  p.M = a.size(0);
+  p.K = a.size(1);
+  p.N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == p.K, "gemm_rs: K mismatch");
+  TORCH_CHECK(p.M % seq == 0, "gemm_rs: rows must be whole sequences");
+  p.epi = pb::kEpiStoreBf16;
+  p.alpha = (float)alpha;
+  p.scatter = &sc;
+  pb::gemm_bf16(p, cur_stream());
+}
+
 int64_t read_error(int64_t device) { return pb::read_error((int)device); }
 void clear_error(int64_t device) { pb::clear_error((int)device); }
 
@@ -82,6 +180,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("b"), pybind11::arg("out"), pybind11::arg("a_mn"), pybind11::arg("b_mn"),
         pybind11::arg("epi"), pybind11::arg("alpha"), pybind11::arg("r") = pybind11::none(),
         pybind11::arg("b_up_offset") = 0, pybind11::arg("n_out") = 0, pybind11::arg("kernel") = 0);
+  m.def("gemm_ag", &gemm_ag, "GEMM with the sequence-parallel all-gather of A in the same kernel",
+        pybind11::arg("dst"), pybind11::arg("src_ptrs"), pybind11::arg("src_ld"), pybind11::arg("flags"),
+        pybind11::arg("target"), pybind11::arg("seq"), pybind11::arg("seq_local"), pybind11::arg("batch"),
+        pybind11::arg("m_order"), pybind11::arg("b"), pybind11::arg("out"), pybind11::arg("b_mn"),
+        pybind11::arg("epi"), pybind11::arg("alpha"), pybind11::arg("r") = pybind11::none(),
+        pybind11::arg("b_up_offset") = 0, pybind11::arg("n_out") = 0);
+  m.def("gemm_rs", &gemm_rs, "GEMM whose epilogue stores rows into their sequence-parallel owners' buffers",
+        pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("b_mn"), pybind11::arg("alpha"),
+        pybind11::arg("peer_ptrs"), pybind11::arg("ldc"), pybind11::arg("seq"), pybind11::arg("seq_local"),
+        pybind11::arg("slot"), pybind11::arg("slot_rows"));
   m.def("read_error", &read_error);
   m.def("clear_error", &clear_error);
   register_ops(m);

@@ -24,6 +24,34 @@ enum GemmEpilogue : int {
                           // raw [g | u] pre-activations (ldr) for the backward.
 };
 
+// Sequence-parallel reduce-scatter epilogue: output row m = b*seq + s (a row
+// of the full-sequence partial product) is stored, as bf16, into the receive
+// buffer of its owner rank s / seq_local, in the sender's slot:
+//   peer[owner] + (slot * slot_rows + b*seq_local + s % seq_local) * ldc.
+// The owner later sums its nranks slots.
+struct ScatterArgs {
+  void* peer[8];
+  int nranks = 0, seq = 0, seq_local = 0, slot = 0;
+  int64_t slot_rows = 0;
+};
+
+// Sequence-parallel all-gather fused into the GEMM's A operand: rank r holds
+// rows [b*seq_local, (b+1)*seq_local) of batch b in src[r]; the kernel's copy
+// warps assemble dst (row b*seq + r*seq_local + sl) one 256-row block at a
+// time, bump flags[block] per finished piece, and the TMA producer starts a
+// tile only once its A block reached `target`.  M tiles run in m_order.
+struct GatherArgs {
+  const void* src[8];
+  void* dst;
+  int* flags;
+  int target = 0;  // flag value of a complete block for this call
+  int nranks = 0, seq = 0, seq_local = 0, batch = 0;
+  int64_t src_ld = 0;  // row stride of the shards (elements)
+  int n_blocks = 0;
+  int m_order[64];
+};
+constexpr int kGatherRowsPerPiece = 16;
+
 struct GemmParams {
   const void* A;
   const void* B;
@@ -37,6 +65,8 @@ struct GemmParams {
   int64_t b_up_offset;  // kEpiSwiGLU: row offset (in N units) of the "up" half of B
   int max_ctas;         // 0 = one CTA per SM
   int kernel = 0;       // 0 = choose, 1 = one-CTA kernel, 2 = CTA-pair kernel
+  const ScatterArgs* scatter = nullptr;  // kEpiStoreBf16 rows to their sequence-parallel owners
+  const GatherArgs* gather = nullptr;    // A assembled from sequence-parallel shards in-kernel
 };
 
 // Dispatches to the one-CTA (gemm.cu) or the CTA-pair (gemm_pair.cu) kernel.

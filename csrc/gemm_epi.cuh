@@ -17,7 +17,17 @@ struct EpiArgs {
   float alpha;
   int epi;
   int64_t up_col;  // kEpiSwiGLU: column of the "up" half inside R
+  ScatterArgs sc;  // sc.nranks > 0: kEpiStoreBf16 rows go to their owners
 };
+
+// Output row pointer of row m for the bf16 store epilogue.
+__device__ __forceinline__ __nv_bfloat16* out_row_bf16(const EpiArgs& ep, int m) {
+  if (ep.sc.nranks == 0) return reinterpret_cast<__nv_bfloat16*>(ep.C) + (int64_t)m * ep.ldc;
+  const int b = m / ep.sc.seq, s = m % ep.sc.seq;
+  const int owner = s / ep.sc.seq_local;
+  const int64_t local = (int64_t)b * ep.sc.seq_local + s % ep.sc.seq_local;
+  return reinterpret_cast<__nv_bfloat16*>(ep.sc.peer[owner]) + (ep.sc.slot * ep.sc.slot_rows + local) * ep.ldc;
+}
 
 // silu(g) = g * sigmoid(g) with the fast reciprocal-based division.
 __device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
@@ -109,7 +119,7 @@ __device__ __forceinline__ void epilogue_row(const EpiArgs& ep, uint32_t t_row, 
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] *= ep.alpha;
       if (ep.epi == kEpiStoreBf16) {
-        store_row_bf16(reinterpret_cast<__nv_bfloat16*>(ep.C) + (int64_t)m * ep.ldc + n0, v, n0, N);
+        store_row_bf16(out_row_bf16(ep, m) + n0, v, n0, N);
       } else if (ep.epi == kEpiResidualBf16 || ep.epi == kEpiAccumBf16) {
         const __nv_bfloat16* src =
             ep.epi == kEpiResidualBf16

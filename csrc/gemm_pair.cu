@@ -48,10 +48,50 @@ struct PairCfg {
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 };
 
-template <int BN, bool A_MN, bool B_MN, bool SWIGLU>
-__global__ void __launch_bounds__(kThreads, 1)
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Copy warps of the gather variant: piece q of the pieces_per_block pieces of
+// block `blk` (kGatherRowsPerPiece rows of K elements, contiguous in both the
+// source shard and the gathered buffer), then publish it on flags[blk].
+__device__ __forceinline__ void gather_piece(const GatherArgs& g, int K, int blk, int q, int lane) {
+  const int64_t m0 = (int64_t)blk * 256 + (int64_t)q * kGatherRowsPerPiece;
+  const int b = (int)(m0 / g.seq), s = (int)(m0 % g.seq);
+  const int r = s / g.seq_local, sl = s % g.seq_local;
+  const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(g.src[r]) +
+                                                    ((int64_t)b * g.seq_local + sl) * g.src_ld);
+  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(g.dst) + m0 * K);
+  const int64_t vecs_per_row = K / 8;
+  const int64_t n = (int64_t)kGatherRowsPerPiece * vecs_per_row;
+  if (g.src_ld == K) {
+    constexpr int U = 8;
+    for (int64_t i = lane; i < n; i += 32 * U) {
+      uint4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (i + u * 32 < n) v[u] = src[i + u * 32];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (i + u * 32 < n) dst[i + u * 32] = v[u];
+    }
+  } else {
+    for (int64_t i = lane; i < n; i += 32) {
+      const int64_t row = i / vecs_per_row, c = i % vecs_per_row;
+      dst[i] = src[row * (g.src_ld / 8) + c];
+    }
+  }
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) atomicAdd(&g.flags[blk], 1);
+}
+
+template <int BN, bool A_MN, bool B_MN, bool SWIGLU, bool GATHER>
+__global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiArgs ep,
-                     int M, int N, int K, int b_up_row, int* err) {
+                     int M, int N, int K, int b_up_row, int* err, const __grid_constant__ GatherArgs ga) {
   using Cfg = PairCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int B_HALF = Cfg::B_HALF;
@@ -112,8 +152,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = cid; tile < num_tiles && ok; tile += n_clusters) {
-        const int tm = tile % tiles_m, tn = tile / tiles_m;
+        const int tm = GATHER ? ga.m_order[tile % tiles_m] : tile % tiles_m, tn = tile / tiles_m;
         const int a_row = tm * 2 * BM_CTA + (int)rank * BM_CTA;
+        if constexpr (GATHER) {
+          // the A block of this tile must have been assembled by the copy warps
+          const uint64_t t0 = globaltimer();
+          uint32_t it = 0;
+          while (ld_acquire_gpu(&ga.flags[tm]) - ga.target < 0) {
+            if ((++it & 255u) == 0 && (*((volatile int*)err) != 0 || globaltimer() - t0 > PB_SPIN_LIMIT_NS)) {
+              record_error(err, kErrPeerTimeout);
+              ok = false;
+              break;
+            }
+          }
+          if (!ok) break;
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, err)) { ok = false; break; }
           const uint32_t full_even = mapa_shared(smem_u32(&full_bar[stage]), 0);
@@ -174,12 +228,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) mma_commit_pair(&tfull_bar[acc], 0x3);
       }
     }
+  } else if (GATHER && warp >= 6) {
+    // copy warps: pieces of the blocks in the order the tiles need them
+    const int pieces = 256 / kGatherRowsPerPiece;
+    const int cw = (int)blockIdx.x * 2 + (warp - 6);
+    for (int pi = cw; pi < ga.n_blocks * pieces; pi += (int)gridDim.x * 2)
+      gather_piece(ga, K, ga.m_order[pi / pieces], pi % pieces, lane);
   } else {
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     int local = 0;
     for (int tile = cid; tile < num_tiles; tile += n_clusters, ++local) {
-      const int tm = tile % tiles_m, tn = tile / tiles_m;
+      const int tm = GATHER ? ga.m_order[tile % tiles_m] : tile % tiles_m, tn = tile / tiles_m;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull_bar[acc], acc_phase, err)) break;
@@ -209,10 +269,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, bool SWIGLU>
+template <int BN, bool A_MN, bool B_MN, bool SWIGLU, bool GATHER = false>
 void launch_pair(const GemmParams& p, cudaStream_t stream) {
   using Cfg = PairCfg<BN>;
-  auto kern = gemm_pair_kernel<BN, A_MN, B_MN, SWIGLU>;
+  auto kern = gemm_pair_kernel<BN, A_MN, B_MN, SWIGLU, GATHER>;
   static std::mutex mu;
   static int max_clusters[64] = {0};
   int dev = 0;
@@ -225,7 +285,7 @@ void launch_pair(const GemmParams& p, cudaStream_t stream) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(GATHER ? kThreads + 64 : kThreads, 1, 1);
   cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
   cfg.stream = stream;
   {
@@ -248,18 +308,32 @@ void launch_pair(const GemmParams& p, cudaStream_t stream) {
     tb = B_MN ? make_tmap_2d_bf16(p.B, p.N, p.K, p.ldb, 64, BK)
               : make_tmap_2d_bf16(p.B, p.K, p.N, p.ldb, BK, Cfg::B_HALF);
   EpiArgs ep{p.C, p.R, p.ldc, p.ldr, p.alpha, p.epi, SWIGLU ? p.b_up_offset : 0};
+  if (p.scatter) ep.sc = *p.scatter;
+  GatherArgs ga{};
+  if (GATHER) ga = *p.gather;
   const int bn_out = SWIGLU ? BN / 2 : BN;
   const int tiles = ((p.M + 2 * BM_CTA - 1) / (2 * BM_CTA)) * ((p.N + bn_out - 1) / bn_out);
   int clusters = max_clusters[dev & 63];
   if (p.max_ctas > 0) clusters = std::min(clusters, std::max(1, p.max_ctas / 2));
   clusters = std::max(1, std::min(clusters, tiles));
   cfg.gridDim = dim3(2 * clusters, 1, 1);
-  PB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, ep, p.M, p.N, p.K, (int)p.b_up_offset, error_word(dev)));
+  PB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, ep, p.M, p.N, p.K, (int)p.b_up_offset, error_word(dev), ga));
 }
 
 }  // namespace
 
 void gemm_bf16_pair(const GemmParams& p, cudaStream_t stream) {
+  if (p.gather) {
+    // A (the gathered activations) is K-major by construction
+    PB_CHECK(!p.a_mn, "gemm: the gathered A operand is K-major");
+    PB_CHECK(p.gather->seq_local % 256 == 0 && p.gather->n_blocks == (p.M + 255) / 256 && p.M % 256 == 0 &&
+                 p.gather->n_blocks <= 64 && p.K % 8 == 0 && p.gather->nranks <= 8,
+             "gemm: gather needs 256-row aligned shards, M % 256 == 0 and at most 64 blocks");
+    if (p.epi == kEpiSwiGLU) return launch_pair<256, false, false, true, true>(p, stream);
+    if (!p.b_mn) return launch_pair<256, false, false, false, true>(p, stream);
+    return launch_pair<256, false, true, false, true>(p, stream);
+  }
+  if (p.scatter) PB_CHECK(p.epi == kEpiStoreBf16 && p.scatter->nranks <= 8, "gemm: scatter needs the bf16 store epilogue");
   if (p.epi == kEpiSwiGLU) return launch_pair<256, false, false, true>(p, stream);
   if (!p.a_mn && !p.b_mn) return launch_pair<256, false, false, false>(p, stream);
   if (!p.a_mn && p.b_mn) return launch_pair<256, false, true, false>(p, stream);

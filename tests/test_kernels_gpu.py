@@ -364,3 +364,64 @@ def test_exp2_emulation_error_bound():
     w = torch.empty_like(z)
     C.exp2_emulated(z, w)
     assert torch.isfinite(w).all() and (w >= 0).all() and (w < 1e-37).all()
+
+
+@pytest.mark.parametrize("b_mn,swiglu", [(False, False), (True, False), (False, True)])
+def test_gemm_allgather_fused_emulated_ranks(b_mn, swiglu):
+    """gemm_ag with 4 emulated ranks whose shards are local tensors: the kernel
+    assembles the gathered operand (checked row for row) and multiplies it."""
+    C = _ext()
+    torch.manual_seed(5)
+    R, Bt, SL, K = 4, 2, 256, 512
+    S = R * SL
+    shards = [torch.randn(Bt * SL, K, device="cuda").to(torch.bfloat16) for _ in range(R)]
+    full_ref = torch.cat([torch.stack([sh[b * SL:(b + 1) * SL] for sh in shards]).reshape(S, K)
+                          for b in range(Bt)])  # row b*S + r*SL + sl
+    dst = torch.empty(Bt * S, K, device="cuda", dtype=torch.bfloat16)
+    flags = torch.zeros(64, device="cuda", dtype=torch.int32)
+    order = list(range(Bt * S // 256))[::-1]
+    if swiglu:
+        I = 384
+        w = (torch.randn(2 * I, K, device="cuda") / math.sqrt(K)).to(torch.bfloat16)
+        h = torch.empty(Bt * S, I, device="cuda", dtype=torch.bfloat16)
+        gu = torch.empty(Bt * S, 2 * I, device="cuda", dtype=torch.bfloat16)
+        for call in (1, 2):  # flags are monotonic across calls
+            C.gemm_ag(dst, [t.data_ptr() for t in shards], K, flags, 16 * call, S, SL, Bt, order, w, h,
+                      False, 5, 1.0, gu, I, I)
+        _check_no_device_error()
+        assert torch.equal(dst, full_ref)
+        g_ref = full_ref.float() @ w.float().t()
+        assert _rel_err(gu, g_ref) < 1e-2
+        assert _rel_err(h, torch.nn.functional.silu(g_ref[:, :I]) * g_ref[:, I:]) < 2e-2
+        return
+    N = 768
+    W = torch.randn(N, K, device="cuda").to(torch.bfloat16)
+    b = W.t().contiguous() if b_mn else W
+    out = torch.empty(Bt * S, N, device="cuda", dtype=torch.bfloat16)
+    for call in (1, 2):
+        C.gemm_ag(dst, [t.data_ptr() for t in shards], K, flags, 16 * call, S, SL, Bt, order, b, out, b_mn, 0, 1.0)
+    _check_no_device_error()
+    assert torch.equal(dst, full_ref)
+    assert _rel_err(out, full_ref.float() @ W.float().t()) < 1e-2
+
+
+@pytest.mark.parametrize("b_mn", [False, True])
+def test_gemm_reducescatter_fused_emulated_ranks(b_mn):
+    """gemm_rs with 4 emulated ranks: every rank's partial product rows land in
+    the owner's slot; summing the slots gives the reduce-scatter."""
+    C = _ext()
+    torch.manual_seed(6)
+    R, Bt, SL, K, N = 4, 2, 256, 384, 512
+    S = R * SL
+    recv = [torch.full((R * Bt * SL, N), float("nan"), device="cuda").to(torch.bfloat16) for _ in range(R)]
+    W = torch.randn(N, K, device="cuda").to(torch.bfloat16)
+    b = W.t().contiguous() if b_mn else W
+    parts = [torch.randn(Bt * S, K, device="cuda").to(torch.bfloat16) for _ in range(R)]
+    for src in range(R):
+        C.gemm_rs(parts[src], b, b_mn, 1.0, [t.data_ptr() for t in recv], N, S, SL, src, Bt * SL)
+    _check_no_device_error()
+    total = sum(p.float() @ W.float().t() for p in parts)  # [Bt*S, N]
+    for r in range(R):
+        mine = torch.cat([total[bb * S + r * SL: bb * S + (r + 1) * SL] for bb in range(Bt)])
+        got = recv[r].view(R, Bt * SL, N).float().sum(0)
+        assert _rel_err(got, mine) < 1e-2
