@@ -40,6 +40,7 @@ class ParallelContext:
     ep_rank: int = 0
     expert_runtime: Any = None  # ReplicatedTokenExpertParallel / SequenceParallelExpertParallel
     comm: Any = None  # model_parallel.comm_ops module (set by the wrapper)
+    fused_sp: Any = None  # FusedSequenceParallel (NVLink GEMM+collective kernels) or None
 
     @property
     def active(self) -> bool:
@@ -111,11 +112,13 @@ class Attention(nn.Module):
         self.q_norm = RMSNorm(D, cfg.rms_norm_eps)
         self.k_norm = RMSNorm(D, cfg.rms_norm_eps)
 
-    def core(self, h, inv_freq, B, S, stash=None):
-        """Attention output before o_proj: [B*S, heads*D]."""
+    def core(self, h, inv_freq, B, S, stash=None, sp=None):
+        """Attention output before o_proj: [B*S, heads*D].  With ``sp`` (fused
+        sequence parallel), h is this rank's sequence shard and the all-gather
+        runs inside the QKV GEMM."""
         return Fx.attention_block(h, self.q_proj.weight, self.k_proj.weight, self.v_proj.weight,
                                   self.q_norm.weight, self.k_norm.weight, inv_freq, B, S, self.num_heads,
-                                  self.num_kv_heads, self.head_dim, self.eps, stash)
+                                  self.num_kv_heads, self.head_dim, self.eps, stash, sp)
 
 
 class MLP(nn.Module):
@@ -199,6 +202,22 @@ class DecoderLayer(nn.Module):
         ctx = self._ctx
         B, S = self._seq
         stash = getattr(self, "_attn_stash", None)
+        fsp = ctx.fused_sp if (ctx.sp and ctx.fused_sp is not None and x.is_cuda
+                               and ctx.fused_sp.supports(B, S, x.shape[-1])) else None
+        if fsp is not None:
+            # sequence parallel on the fused NVLink kernels: the gathers run inside
+            # the column-parallel GEMMs, the reduce-scatters inside the row-parallel ones
+            from ..parallel.model_parallel.fused_sp import linear_reduce_scatter, sp_swiglu_mlp
+
+            h = self.input_layernorm(x)
+            o = self.self_attn.core(h, self._inv_freq, B, S, stash, sp=fsp)
+            y = linear_reduce_scatter(o, self.self_attn.o_proj.weight, fsp, B, S)
+            x = x + y.view(x.shape)
+            h = self.post_attention_layernorm(x)
+            if self.is_moe:
+                return x + self.mlp(h, ctx, self._router_sink)
+            return x + sp_swiglu_mlp(h, self.mlp.gate_proj.weight, self.mlp.up_proj.weight,
+                                     self.mlp.down_proj.weight, fsp, B, S)
         if ctx.tp_size > 1:
             h = self.input_layernorm(x)
             h = ctx.comm.gather_sequence(h, ctx) if ctx.sp else ctx.comm.copy_to_tp(h, ctx)

@@ -178,10 +178,18 @@ class _AttentionFn(torch.autograd.Function):
     attention.  Returns the attention output [T, nq*D] (before o_proj)."""
 
     @staticmethod
-    def forward(ctx, h, wq, wk, wv, qw, kw, cos, sin, B, S, nq, nkv, D, eps, stash=None):
+    def forward(ctx, h, wq, wk, wv, qw, kw, cos, sin, B, S, nq, nkv, D, eps, stash=None, sp=None):
         T = B * S
         wqkv = fused_rows(wq, wk, wv)
-        qkv = G.linear(h.reshape(T, -1), wqkv)
+        ctx.sp = sp
+        ctx.h_shape = h.shape
+        if sp is not None:
+            # sequence parallel: h is this rank's [B*S/tp, H] shard; the gather
+            # runs inside the QKV GEMM and the gathered rows are kept for dW
+            h_local = h.reshape(-1, h.shape[-1])
+            qkv, h = sp.all_gather_gemm(h_local if h_local.is_contiguous() else h_local.contiguous(), wqkv, B, S)
+        else:
+            qkv = G.linear(h.reshape(T, -1), wqkv)
         q = torch.empty(T, nq * D, device=h.device, dtype=h.dtype)
         k = torch.empty(T, nkv * D, device=h.device, dtype=h.dtype)
         rstd = torch.empty(T, nq + nkv, device=h.device, dtype=torch.float32)
@@ -220,13 +228,16 @@ class _AttentionFn(torch.autograd.Function):
         ext().qknorm_rope_bwd(dq, dk, qkv, qw, kw, cos, sin, rstd, dqkv, dqw, dkw, S, nq, nkv)
         wqkv = fused_rows(wq, wk, wv)
         h2 = h.reshape(T, -1)
-        dh = G.linear_dgrad(dqkv, wqkv).view(h.shape)
+        if ctx.sp is not None:
+            dh = ctx.sp.gemm_reduce_scatter(dqkv, wqkv, B, S, b_mn=True).view(ctx.h_shape)
+        else:
+            dh = G.linear_dgrad(dqkv, wqkv).view(h.shape)
         dw = G.linear_wgrad(dqkv, h2)
         gq, gk, gv = _split_rows(dw, (wq.shape[0], wk.shape[0], wv.shape[0]))
-        return dh, gq, gk, gv, dqw.to(qw.dtype), dkw.to(kw.dtype), None, None, None, None, None, None, None, None, None
+        return dh, gq, gk, gv, dqw.to(qw.dtype), dkw.to(kw.dtype), None, None, None, None, None, None, None, None, None, None
 
 
-def attention_block(h, wq, wk, wv, q_norm_w, k_norm_w, inv_freq, B, S, nq, nkv, D, eps, stash=None):
+def attention_block(h, wq, wk, wv, q_norm_w, k_norm_w, inv_freq, B, S, nq, nkv, D, eps, stash=None, sp=None):
     """Self-attention up to (not including) o_proj: returns [B*S, nq*D].
 
     ``stash`` (CUDA path): a dict with mode "save" keeps the attention output
@@ -234,7 +245,7 @@ def attention_block(h, wq, wk, wv, q_norm_w, k_norm_w, inv_freq, B, S, nq, nkv, 
     attention kernel (selective recompute under activation checkpointing)."""
     if h.is_cuda:
         cos, sin = rope_tables(inv_freq, S, h.dtype, h.device)
-        return _AttentionFn.apply(h, wq, wk, wv, q_norm_w, k_norm_w, cos, sin, B, S, nq, nkv, D, eps, stash)
+        return _AttentionFn.apply(h, wq, wk, wv, q_norm_w, k_norm_w, cos, sin, B, S, nq, nkv, D, eps, stash, sp)
     cos, sin = rope_tables(inv_freq, S, h.dtype, h.device)
     x = h.reshape(B, S, -1)
     q = F.linear(x, wq).view(B, S, nq, D)

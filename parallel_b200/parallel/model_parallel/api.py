@@ -14,6 +14,7 @@ import torch
 
 from ...models.qwen3 import ParallelContext
 from . import comm_ops
+from .fused_sp import FusedSequenceParallel
 from .checkpoint import ComposedModelParallelCheckpoint, ModelParallelCheckpoint
 from .expert_parallel import (ExpertPartition, ReplicatedTokenExpertParallel, SequenceParallelExpertParallel,
                               verify_expert_modules)
@@ -30,6 +31,7 @@ class ModelParallelWrapper:
         self.pconfig = pconfig
         self.device = device
         self.plan = plan
+        self.collectives = collectives
         self.mesh = None
         self.group = None
         self.experts = None
@@ -60,6 +62,11 @@ class ModelParallelWrapper:
             self.sequence_runtime = SequenceParallelRuntime(self.group,
                                                             dense_mlp=not self.plan.capabilities.expert_parallel)
             self.sequence_runtime.apply(model)
+            # NVLink data plane: all-gather / reduce-scatter fused into the GEMMs
+            if self.collectives != "nccl" and FusedSequenceParallel.available(self.group, device):
+                ctx = model.ctx
+                ctx.fused_sp = FusedSequenceParallel(self.group, device)
+                model.set_parallel_context(ctx)
         if self.plan.capabilities.expert_parallel:
             self.experts = ExpertPartition(model.config.num_experts, self.plan.expert_parallel_size,
                                            self.mesh.get_local_rank())

@@ -1,0 +1,216 @@
+"""Sequence-parallel collectives fused with their GEMMs over NVLink.
+
+Megatron-style sequence parallelism surrounds every column-parallel GEMM with
+an all-gather of the sequence-sharded activations and every row-parallel GEMM
+with a reduce-scatter of its partial output (the reference issues both through
+NCCL around HF's Linear layers: parallel/parallel/engine/model_parallel/
+sequence_parallel.py:19-46,178-213, tensor_parallel.py:31-35).  Here each pair
+is one kernel (``csrc/gemm_pair.cu``):
+
+* all-gather -> GEMM (``gemm_ag``): every rank's shard sits in a symmetric
+  buffer; copy warps inside the GEMM kernel pull the peers' shards over
+  NVLink into a local gathered buffer one 256-row block at a time and publish
+  per-block counters, and the GEMM starts each tile as soon as its block is
+  in (local shard first, then the peers in rotation).  The gathered buffer is
+  kept for the weight gradient.
+* GEMM -> reduce-scatter (``gemm_rs``): the epilogue stores every output row
+  of the partial product straight into its owner's symmetric receive buffer
+  (one slot per sender); after a signal barrier the owner sums its slots.
+
+Buffers rotate between two sets, so one signal barrier per call orders reuse:
+when a rank passes the barrier of call k every rank has finished call k-1,
+hence nobody still reads the set that call k+1 overwrites.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.distributed as dist
+
+from ...ops._ext import ext
+from ...ops.gemm import EPI_STORE_BF16, EPI_SWIGLU
+from ...profiling import collective_profile
+from ..comm.p2p import SymmBuffer, p2p_supported
+
+_PIECES_PER_BLOCK = 256 // 16  # kGatherRowsPerPiece = 16 rows per copy piece
+
+
+class FusedSequenceParallel:
+    """NVLink data plane of one TP/SP group (all ranks call in the same order)."""
+
+    def __init__(self, group, device: torch.device):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = device
+        self.limit_s = float(os.environ.get("PB_P2P_TIMEOUT_S", "60"))
+        self._rows = 0
+        self._cols = 0
+        self.ag = []  # 2 x SymmBuffer [rows_local, cols] (this rank's shard)
+        self.rs = []  # 2 x SymmBuffer [world * rows_local, cols] (one slot per sender)
+        self.flags = []
+        self.flag_calls = [0, 0]
+        self.n_ag = 0
+        self.n_rs = 0
+
+    # ------------------------------------------------------------------ support
+    @staticmethod
+    def available(group, device) -> bool:
+        return device.type == "cuda" and p2p_supported(group)
+
+    def supports(self, batch: int, seq: int, cols: int) -> bool:
+        """Shapes the fused kernels take: 256-row aligned local shards, <= 64 row blocks."""
+        if seq % self.world:
+            return False
+        sl = seq // self.world
+        return sl % 256 == 0 and (batch * seq) // 256 <= 64 and cols % 8 == 0
+
+    def _ensure(self, rows_local: int, cols: int) -> None:
+        if self.ag and rows_local <= self._rows and cols <= self._cols:
+            return
+        if self.ag:
+            raise RuntimeError("fused sequence parallel: buffers are sized by the first call; shapes grew "
+                               f"({self._rows}x{self._cols} -> {rows_local}x{cols})")
+        self._rows, self._cols = rows_local, cols
+        n = rows_local * cols
+        self.ag = [SymmBuffer(n, torch.bfloat16, self.device, self.group) for _ in range(2)]
+        self.rs = [SymmBuffer(self.world * n, torch.bfloat16, self.device, self.group) for _ in range(2)]
+        self.flags = [torch.zeros(64, dtype=torch.int32, device=self.device) for _ in range(2)]
+
+    def _block_order(self, batch: int, seq: int) -> list[int]:
+        sl = seq // self.world
+        blocks = list(range(batch * seq // 256))
+        owner = [((b * 256) % seq) // sl for b in blocks]
+        return sorted(blocks, key=lambda b: ((owner[b] - self.rank) % self.world, b))
+
+    # ------------------------------------------------------------------ all-gather -> GEMM
+    def all_gather_gemm(self, x_local: torch.Tensor, b: torch.Tensor, batch: int, seq: int, *, b_mn: bool = False,
+                        swiglu_inter: int = 0, gu_out: torch.Tensor | None = None):
+        """Returns (out, x_full): out = gather(x) @ b^T (or @ b when b_mn), or for
+        swiglu_inter > 0 the SwiGLU of the gate/up product (gu_out receives the
+        pre-activations); x_full [batch*seq, K] is the gathered input."""
+        rows_local, K = x_local.shape
+        self._ensure(rows_local, K)
+        k = self.n_ag % 2
+        buf = self.ag[k]
+        shard = buf.tensor[: rows_local * K].view(rows_local, K)
+        shard.copy_(x_local)
+        T = batch * seq
+        x_full = torch.empty(T, K, device=x_local.device, dtype=torch.bfloat16)
+        if swiglu_inter:
+            out = torch.empty(T, swiglu_inter, device=x_local.device, dtype=torch.bfloat16)
+            epi, n_out, up = EPI_SWIGLU, swiglu_inter, swiglu_inter
+        else:
+            N = b.shape[1] if b_mn else b.shape[0]
+            out = torch.empty(T, N, device=x_local.device, dtype=torch.bfloat16)
+            epi, n_out, up = EPI_STORE_BF16, 0, 0
+        self.flag_calls[k] += 1
+        target = self.flag_calls[k] * _PIECES_PER_BLOCK
+        with collective_profile("sp_all_gather_gemm", value=x_local, mode="fused"):
+            buf.barrier(0, self.limit_s)
+            ext().gemm_ag(x_full, buf.peer_ptrs, K, self.flags[k], target, seq, seq // self.world, batch,
+                          self._block_order(batch, seq), b, out, b_mn, epi, 1.0, gu_out, up, n_out)
+        self.n_ag += 1
+        return out, x_full
+
+    # ------------------------------------------------------------------ GEMM -> reduce-scatter
+    def gemm_reduce_scatter(self, a_full: torch.Tensor, b: torch.Tensor, batch: int, seq: int, *,
+                            b_mn: bool = False) -> torch.Tensor:
+        """y_local [batch*seq/world, N] = reduce_scatter(a_full @ b^T (or @ b))."""
+        N = b.shape[1] if b_mn else b.shape[0]
+        rows_local = batch * seq // self.world
+        self._ensure(rows_local, N)  # receive slots are rows_local x N (N <= buffer width)
+        k = self.n_rs % 2
+        buf = self.rs[k]
+        y = torch.empty(rows_local, N, device=a_full.device, dtype=torch.bfloat16)
+        slot_elems = rows_local * N
+        with collective_profile("sp_gemm_reduce_scatter", payload_bytes=a_full.shape[0] * N * 2, mode="fused"):
+            ext().gemm_rs(a_full, b, b_mn, 1.0, buf.peer_ptrs, N, seq, seq // self.world, self.rank, rows_local)
+            buf.barrier(0, self.limit_s)
+            base = buf.tensor.data_ptr()
+            ext().p2p_reduce([[base + s * slot_elems * 2] for s in range(self.world)], [y.data_ptr()],
+                             [slot_elems], 1.0, False)
+        self.n_rs += 1
+        return y
+
+
+# ---------------------------------------------------------------------------- autograd
+class _LinearRSFn(torch.autograd.Function):
+    """Row-parallel linear with the sequence reduce-scatter fused (forward) and
+    the all-gather of the output gradient fused into the dgrad GEMM (backward)."""
+
+    @staticmethod
+    def forward(ctx, a, w, sp, batch, seq):
+        a2 = a.reshape(-1, a.shape[-1])
+        if not a2.is_contiguous():
+            a2 = a2.contiguous()
+        y = sp.gemm_reduce_scatter(a2, w, batch, seq)
+        ctx.save_for_backward(a2, w)
+        ctx.sp, ctx.batch, ctx.seq = sp, batch, seq
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        from ...ops import gemm as G
+
+        a2, w = ctx.saved_tensors
+        g2 = g.reshape(-1, w.shape[0])
+        if not g2.is_contiguous():
+            g2 = g2.contiguous()
+        da, g_full = ctx.sp.all_gather_gemm(g2, w, ctx.batch, ctx.seq, b_mn=True)
+        dw = G.linear_wgrad(g_full, a2)
+        return da, dw, None, None, None
+
+
+def linear_reduce_scatter(a, w, sp: FusedSequenceParallel, batch: int, seq: int):
+    """reduce_scatter_seq(a @ w.T) -> [batch*seq/world, out]."""
+    return _LinearRSFn.apply(a, w, sp, batch, seq)
+
+
+class _SPMLPFn(torch.autograd.Function):
+    """Dense SwiGLU MLP under sequence parallelism: gather -> gate/up (SwiGLU
+    epilogue) in one kernel, down -> reduce-scatter in one kernel; the backward
+    mirrors it (gather of dy fused into the down dgrad, reduce-scatter of dx
+    fused into the gate/up dgrad)."""
+
+    @staticmethod
+    def forward(ctx, x_local, wg, wu, wd, sp, batch, seq):
+        from ...ops.functional import fused_rows
+
+        I = wg.shape[0]
+        x2 = x_local.reshape(-1, x_local.shape[-1])
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        wgu = fused_rows(wg, wu)
+        T = batch * seq
+        gu = torch.empty(T, 2 * I, device=x2.device, dtype=torch.bfloat16)
+        h, x_full = sp.all_gather_gemm(x2, wgu, batch, seq, swiglu_inter=I, gu_out=gu)
+        y = sp.gemm_reduce_scatter(h, wd, batch, seq)
+        ctx.save_for_backward(x_full, wg, wu, wd, gu, h)
+        ctx.sp, ctx.batch, ctx.seq = sp, batch, seq
+        ctx.in_shape = x_local.shape
+        return y.view(*x_local.shape[:-1], wd.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        from ...ops import gemm as G
+        from ...ops.functional import fused_rows
+
+        x_full, wg, wu, wd, gu, h = ctx.saved_tensors
+        I = wg.shape[0]
+        dy2 = dy.reshape(-1, wd.shape[0])
+        if not dy2.is_contiguous():
+            dy2 = dy2.contiguous()
+        dh, dy_full = ctx.sp.all_gather_gemm(dy2, wd, ctx.batch, ctx.seq, b_mn=True)
+        dwd = G.linear_wgrad(dy_full, h)
+        dgu = torch.empty_like(gu)
+        ext().swiglu_bwd(dh, gu, dgu)
+        wgu = fused_rows(wg, wu)
+        dx = ctx.sp.gemm_reduce_scatter(dgu, wgu, ctx.batch, ctx.seq, b_mn=True).view(ctx.in_shape)
+        dwgu = G.linear_wgrad(dgu, x_full)
+        return dx, dwgu[:I], dwgu[I:], dwd, None, None, None
+
+
+def sp_swiglu_mlp(x_local, wg, wu, wd, sp: FusedSequenceParallel, batch: int, seq: int):
+    return _SPMLPFn.apply(x_local, wg, wu, wd, sp, batch, seq)

@@ -43,7 +43,77 @@ def run_engine(collectives, data, layers=2):
     return losses, state, eng.fsdp_wrapper.coll.name
 
 
+def run_sp(collectives, data, steps_grads):
+    """Qwen3 (head_dim 128) with tp = sp = world: the fused NVLink sequence-parallel
+    kernels (collectives != nccl) against the NCCL path.  Returns losses and
+    the local gradient shards after one backward."""
+    from parallel_b200.config import from_dotlist, load_cfg, merge
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.qwen3 import build_model
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    from parallel_b200.models.loading import load_causal_lm, save_pretrained
+
+    world = dist.get_world_size()
+    path = os.path.join(os.environ.get("PB_TEST_TMP", "/tmp"), "sp_ckpt")
+    if dist.get_rank() == 0:
+        mcfg = resolve_config("small-qwen3", num_hidden_layers=2, vocab_size=2048, hidden_size=512,
+                              intermediate_size=1024)
+        save_pretrained(build_model(mcfg, dtype=torch.bfloat16, seed=0), path)
+    dist.barrier()
+    cfg = merge(load_cfg(argv=[]), from_dotlist([
+        "config.device_type=cuda", "model.learning_rate=1e-3", f"model.name={path}", f"parallel.tp={world}",
+        f"parallel.sp={world}", "engine.activation_checkpoint=false", f"engine.collectives={collectives}"]))
+    pc = ParallelConfig(cfg)
+    pc.set_device_mesh("cuda")
+    m, plan = load_causal_lm(cfg, pc, dtype=torch.bfloat16)
+    m.to(pc.device)
+    eng = ParallelEngine(m, None, pc, cfg, pc.device, mp_plan=plan)
+    fused = eng.model.model.layers[0]._ctx.fused_sp is not None
+    losses, grads = [], {}
+    for i, tok in enumerate(data):
+        tok = tok.cuda()
+        loss = eng.forward(tok[:, :-1], tok[:, 1:]).loss
+        eng.backward(loss)
+        if i == 0:
+            for n, p in eng.model.named_parameters():
+                if p.grad is not None:
+                    grads[n] = p.grad.detach().float().cpu()
+        eng.step()
+        losses.append(eng.reduce_loss(loss).item())
+    from parallel_b200.ops._ext import check_device_errors
+
+    torch.cuda.synchronize()
+    check_device_errors()
+    return losses, grads, fused
+
+
+def main_sp():
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    world = dist.get_world_size()
+    g = torch.Generator().manual_seed(0)
+    data = [torch.randint(0, 2048, (2, 256 * world + 1), generator=g) for _ in range(3)]
+    l_f, g_f, fused = run_sp("p2p", data, 1)
+    l_n, g_n, fused_n = run_sp("nccl", data, 1)
+    worst = 0.0
+    for k in g_n:
+        a, b = g_f[k], g_n[k]
+        worst = max(worst, ((a - b).norm() / (b.norm() + 1e-12)).item())
+    t = torch.tensor([worst], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    if dist.get_rank() == 0:
+        with open(os.environ["PB_TEST_OUT"], "w") as f:
+            json.dump({"fused": l_f, "nccl": l_n, "used_fused": [fused, fused_n], "grad_rel_diff": t.item()}, f)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
+    if os.environ.get("PB_TEST_MODE") == "sp":
+        return main_sp()
     local = int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
