@@ -45,10 +45,14 @@ struct AttnBwdParams {
   float scale;
   bool causal;
   long long* trace = nullptr;  // optional per-CTA phase timing [grid * kAttnBwdTraceSlots]
+  // dS tile buffer (attention_bwd_ds_elems bf16 elements): when set, dQ is
+  // computed from stored dS tiles by a second kernel (no fp32 accumulator)
+  void* ds_buf = nullptr;
 };
 
 constexpr int kAttnBwdTraceSlots = 24;
 
 void attention_bwd(const AttnBwdParams& p, cudaStream_t s);
+int64_t attention_bwd_ds_elems(int B, int S, int nq, bool causal);
 
 }  // namespace pb

@@ -50,7 +50,8 @@ constexpr int kThreads = 512;  // 4 warpgroups
 constexpr int kRegsCtl = 56, kRegsElem = 168, kRegsDq = 120;
 static_assert(kRegsCtl + 2 * kRegsElem + kRegsDq == 4 * 128, "attention bwd: register split");
 constexpr int TILE = 128 * HD * 2;   // 32 KB bf16 operand tile
-constexpr int STAGE = 128 * 32 * 4;  // 16 KB: one 128 x 32 fp32 dQ chunk
+constexpr int STAGE = 128 * 32 * 4;  // 16 KB of dQ staging per buffer (2 buffers)
+constexpr int DQ_BOX = 32 * 32 * 4;  // 4 KB: one warp's 32 rows x 32 fp32 columns
 // K, V, Q x2, dO, P/dS + two dQ stages + double-buffered lse2/delta (2 KB)
 // + barriers + TMEM slot.
 constexpr int SMALL_BYTES = 2048 + 24 * 8;
@@ -64,14 +65,16 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-template <bool kTrace>
+// DS_STORE: instead of producing dQ, every dS^T tile (the bf16 shared-memory
+// image, already swizzled for the MMA) is stored to ds_buf for the dQ kernel.
+template <bool kTrace, bool DS_STORE>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                     const __grid_constant__ CUtensorMap tmdQ, const float* __restrict__ LSE2,
                     const float* __restrict__ DELTA, __nv_bfloat16* __restrict__ dK, int64_t lddk,
                     __nv_bfloat16* __restrict__ dV, int64_t lddv, int B, int S, int nq, int nkv, float scale,
-                    bool causal, int* err, long long* trace) {
+                    bool causal, int* err, long long* trace, __nv_bfloat16* __restrict__ ds_buf) {
   // optional per-CTA phase timing (clock64 cycles, kTrace builds only); slots
   // are documented at the use sites
   constexpr int kSlots = kTrace ? kAttnBwdTraceSlots : 1;
@@ -104,7 +107,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sdO = smem + 4 * TILE;
   uint8_t* sPdS = smem + 5 * TILE;
   uint8_t* sStage = smem + 6 * TILE;  // 2 dQ staging buffers
-  float* s_lse = reinterpret_cast<float*>(smem + 6 * TILE + 2 * STAGE);  // [2][128] lse * log2e
+  float* s_lse = reinterpret_cast<float*>(smem + 6 * TILE + 2 * STAGE);  // [2][128] -lse * log2e
   float* s_delta = s_lse + 256;                                          // [2][128] delta * scale
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_delta + 256);
   uint64_t* kv_full = bars + 0;
@@ -123,9 +126,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* dq_empty = bars + 15;
   uint64_t* kv_done = bars + 16;
   uint64_t* drain = bars + 17;
-  uint64_t* stage_full = bars + 18;  // [2]
-  uint64_t* stage_free = bars + 20;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wg = warp >> 2;
@@ -143,8 +144,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
-      mbar_init(&stage_full[s], 128);
-      mbar_init(&stage_free[s], 1);
     }
     mbar_init(do_full, 1);
     mbar_init(do_empty, 1);
@@ -154,7 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(p_full, kElem);
     mbar_init(dv_done, 1);
     mbar_init(ds_full, kElem);
-    mbar_init(pds_free, 1);
+    mbar_init(pds_free, DS_STORE ? 2 : 1);  // dK product done (+ dS tile stored)
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 128);
     mbar_init(kv_done, 1);
@@ -229,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = it & 1;
         const uint32_t q_base = smem_u32(sQ + st * TILE);
         // slot 1: dQ(it-1) drained from TMEM, dO(it) loaded
-        if (!tw(1, dq_empty, ph ^ 1) || !tw(1, do_full, ph)) { ok = false; break; }
+        if ((!DS_STORE && !tw(1, dq_empty, ph ^ 1)) || !tw(1, do_full, ph)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // dP^T = V dO^T
@@ -252,12 +251,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(do_empty);
         if (!tw(3, ds_full, ph)) { ok = false; break; }  // slot 3: dS written
         tc_fence_after();
+        if constexpr (!DS_STORE) {
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // dQ = dS K   (K = keys; dS read MN-major)
-          mma_bf16_ss(tdP, smem_desc_sw128(pds_base + kk * 2048, TILE / 2, 1024),
-                      smem_desc_sw128(k_base + kk * 2048, TILE / 2, 1024), id_mm, kk > 0);
+          for (int kk = 0; kk < 8; ++kk) {  // dQ = dS K   (K = keys; dS read MN-major)
+            mma_bf16_ss(tdP, smem_desc_sw128(pds_base + kk * 2048, TILE / 2, 1024),
+                        smem_desc_sw128(k_base + kk * 2048, TILE / 2, 1024), id_mm, kk > 0);
+          }
+          mma_commit(dq_full);
         }
-        mma_commit(dq_full);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // dK += dS^T Q   (K = queries)
           const uint32_t aoff = (kk >> 2) * (TILE / 2) + (kk & 3) * 32;
@@ -309,19 +310,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(s_empty);
       const bool masked = (causal && i == j) || (i + 1) * BT > S || (j + 1) * BT > S;
       if (!masked) {
+        const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
 #pragma unroll
         for (int c = 0; c < 64; c += 4) {
-          const float4 l = *reinterpret_cast<const float4*>(lse_t + c);
-          p[c + 0] = ex2(fmaf(p[c + 0], scale_log2, -l.x));
-          p[c + 1] = ex2(fmaf(p[c + 1], scale_log2, -l.y));
-          p[c + 2] = ex2(fmaf(p[c + 2], scale_log2, -l.z));
-          p[c + 3] = ex2(fmaf(p[c + 3], scale_log2, -l.w));
+          const float4 l = *reinterpret_cast<const float4*>(lse_t + c);  // -lse * log2(e)
+          const float2 x01 = f2_unpack(ffma2(f2_pack(p[c], p[c + 1]), sc2, f2_pack(l.x, l.y)));
+          const float2 x23 = f2_unpack(ffma2(f2_pack(p[c + 2], p[c + 3]), sc2, f2_pack(l.z, l.w)));
+          // 5 of every 16 pairs on the FMA pipe, the rest on the special-function unit
+          if (((c >> 1) & 15) >= 11) exp2_poly_pair(x01.x, x01.y, p[c], p[c + 1]);
+          else { p[c] = ex2(x01.x); p[c + 1] = ex2(x01.y); }
+          if ((((c >> 1) + 1) & 15) >= 11) exp2_poly_pair(x23.x, x23.y, p[c + 2], p[c + 3]);
+          else { p[c + 2] = ex2(x23.x); p[c + 3] = ex2(x23.y); }
         }
       } else {
         const int q0 = i * BT + cg;
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const float x = ex2(fmaf(p[c], scale_log2, -lse_t[c]));
+          const float x = ex2(fmaf(p[c], scale_log2, lse_t[c]));
           const int q = q0 + c;
           p[c] = ((causal && kpos > q) || kpos >= S || q >= S) ? 0.f : x;
         }
@@ -397,17 +402,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+  } else if (DS_STORE) {
+    // ---------------------------------------------------------------- warpgroup 3: dS tile store
+    regs_decrease<kRegsDq>();
+    if (threadIdx.x == 3 * 128) {
+      const int tiles_bh = causal ? n_t * (n_t + 1) / 2 : n_t * n_t;
+      bool ok = true;
+      for (int it = 0; it < n_iter && ok; ++it) {
+        const int h = kvh * G + it / (n_t - i0);
+        const int i = i0 + it % (n_t - i0);
+        if (!tw(16, ds_full, it & 1)) { ok = false; break; }
+        const int64_t tile = ((int64_t)b * nq + h) * tiles_bh + (causal ? (int64_t)i * (i + 1) / 2 : (int64_t)i * n_t) + j;
+        bulk_store(ds_buf + tile * (TILE / 2), sPdS, TILE);
+        bulk_commit_group();
+        bulk_wait_group_read<0>();  // the P/dS buffer may be overwritten after this
+        mbar_arrive(pds_free);
+      }
+      bulk_wait_group<0>();
+    }
   } else {
     // ---------------------------------------------------------------- warpgroup 3: dQ drain
-    // TMEM dQ (lane = query row) -> two 16 KB swizzled fp32 stages -> bulk
-    // tensor reduce-add into the fp32 accumulator, 32 head-dim columns a time.
+    // TMEM dQ (lane = query row) -> shared staging -> bulk tensor reduce-add
+    // into the fp32 accumulator.  Each warp owns its 32 rows end to end: a
+    // private ring of two 32 x 32 fp32 boxes (4 KB each), its own bulk groups,
+    // no cross-warp handshakes; TMEM is released once all four column chunks
+    // of every warp are in registers / staged.
     regs_decrease<kRegsDq>();
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const bool leader = threadIdx.x == 3 * 128;
+    uint8_t* ring = sStage + quarter * (2 * DQ_BOX);  // this warp's two boxes
     bool ok = true;
-    int n = 0;  // chunks staged so far; chunk n uses stage n & 1
+    int n = 0;  // chunks staged by this warp so far; chunk n uses box n & 1
     const long long t_loop0 = clock64();
     for (int it = 0; it < n_iter && ok; ++it) {
       const int h = kvh * G + it / (n_t - i0);
@@ -415,41 +440,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!tw(16, dq_full, it & 1)) { ok = false; break; }  // slot 16
       tc_fence_after();
 #pragma unroll 1
-      for (int hh = 0; hh < 2 && ok; ++hh) {
-        float v[64];
-        tmem_ld32(tdP + lane_off + hh * 64, v);
-        tmem_ld32(tdP + lane_off + hh * 64 + 32, v + 32);
+      for (int c = 0; c < 4; ++c, ++n) {
+        float v[32];
+        tmem_ld32(tdP + lane_off + c * 32, v);
         tmem_wait_ld();
-        if (hh == 1) {  // all of dQ(it) is in registers: TMEM may take dP(it+1)
+        if (c == 3) {  // all of this warp's dQ(it) columns are out of TMEM
           tc_fence_before();
           mbar_arrive(dq_empty);
         }
+        uint8_t* box = ring + (n & 1) * DQ_BOX;
+        if (lane == 0 && n >= 2) bulk_wait_group_read<1>();  // box n-2 has been read
+        __syncwarp();
 #pragma unroll
-        for (int c = 0; c < 2; ++c, ++n) {
-          const int bb = n & 1, u = n >> 1;
-          uint8_t* stage = sStage + bb * STAGE;
-          if (leader && u > 0) {  // the reduce that last used this stage has read it
-            bulk_wait_group_read<1>();
-            mbar_arrive(&stage_free[bb]);
-          }
-          if (!tw(17, &stage_free[bb], (u & 1) ^ 1)) { ok = false; break; }  // slot 17
-#pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
-            const float* vv = v + c * 32 + ch * 4;
-            *reinterpret_cast<float4*>(stage + r * 128 + ((ch ^ (r & 7)) << 4)) =
-                make_float4(vv[0], vv[1], vv[2], vv[3]);
-          }
-          fence_proxy_async_smem();
-          mbar_arrive(&stage_full[bb]);
-          if (leader) {
-            if (!tw(18, &stage_full[bb], u & 1)) { ok = false; break; }  // slot 18
-            tma_reduce_add_3d(&tmdQ, stage, h * HD + hh * 64 + c * 32, i * BT, b);
-            bulk_commit_group();
-          }
+        for (int ch = 0; ch < 8; ++ch)
+          *reinterpret_cast<float4*>(box + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
+              make_float4(v[ch * 4], v[ch * 4 + 1], v[ch * 4 + 2], v[ch * 4 + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_3d(&tmdQ, box, h * HD + c * 32, i * BT + quarter * 32, b);
+          bulk_commit_group();
         }
       }
     }
-    if (leader) bulk_wait_group<0>();
+    if (lane == 0) bulk_wait_group<0>();
     if (kTrace) tacc[19] = clock64() - t_loop0;  // slot 19: dQ loop total
   }
   if constexpr (kTrace) {
@@ -468,16 +482,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// One warp per (token, head):
-//   delta2[b, h, s] = scale * sum_d dO * O     (first half of `scratch`)
-//   lse2[b, h, s]   = lse * log2(e)            (second half)
-// and zero that (token, head)'s 128 fp32 dQ accumulator entries.  The two
-// halves are padded by 128 zeros so the kernel's 128-row bulk copies stay in
-// bounds and finite.
+// delta2[b, h, s] = scale * sum_d dO * O     (first half of `scratch`)
+// nlse2[b, h, s]  = -lse * log2(e)           (second half)
+// and, when dq_acc is given, zero the fp32 dQ accumulator.  A warp handles 16
+// consecutive tokens of one (batch, head): a half warp per token row (16-byte
+// loads, all issued before the reductions), contiguous delta / lse accesses.
+// The two halves are padded by 128 zeros so the main kernel's 128-row bulk
+// copies stay in bounds and finite.
 __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ O, int64_t ldo,
                                      const __nv_bfloat16* __restrict__ dO, int64_t lddo,
                                      const float* __restrict__ lse, float* __restrict__ scratch,
                                      float* __restrict__ dq_acc, int64_t ld_acc, int B, int S, int nq, float scale) {
+  constexpr int kTok = 16;  // tokens per warp
   const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t rows = (int64_t)B * nq * S;
   float* delta2 = scratch;
@@ -486,25 +502,207 @@ __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ O, int64_
     delta2[rows + gid] = 0.f;
     lse2[rows + gid] = 0.f;
   }
-  const int64_t item = gid >> 5;
-  const int lane = threadIdx.x & 31;
-  if (item >= (int64_t)B * S * nq) return;
-  const int64_t t = item / nq;
-  const int h = (int)(item % nq);
-  const __nv_bfloat16* o = O + t * ldo + h * HD + lane * 4;
-  const __nv_bfloat16* g = dO + t * lddo + h * HD + lane * 4;
-  uint2 ov = *reinterpret_cast<const uint2*>(o);
-  uint2 gv = *reinterpret_cast<const uint2*>(g);
-  float2 o0 = unpack_bf16x2(ov.x), o1 = unpack_bf16x2(ov.y), g0 = unpack_bf16x2(gv.x), g1 = unpack_bf16x2(gv.y);
-  float acc = o0.x * g0.x + o0.y * g0.y + o1.x * g1.x + o1.y * g1.y;
-  *reinterpret_cast<float4*>(dq_acc + t * ld_acc + h * HD + lane * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4;
+  const int64_t wid = gid >> 5;
+  const int groups = (S + kTok - 1) / kTok;
+  if (wid >= (int64_t)B * nq * groups) return;
+  const int bh = (int)(wid / groups);
+  const int s0 = (int)(wid % groups) * kTok;
+  const int b = bh / nq, h = bh % nq;
+  uint4 ov[kTok / 2], gv[kTok / 2];
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) {
-    const int64_t bb = t / S, s = t % S;
-    const int64_t idx = (bb * nq + h) * S + s;
-    delta2[idx] = acc * scale;
-    lse2[idx] = lse[idx] * kLog2e;
+  for (int k = 0; k < kTok / 2; ++k) {
+    const int s = min(s0 + 2 * k + half, S - 1);
+    const int64_t t = (int64_t)b * S + s;
+    ov[k] = *reinterpret_cast<const uint4*>(O + t * ldo + h * HD + hl * 8);
+    gv[k] = *reinterpret_cast<const uint4*>(dO + t * lddo + h * HD + hl * 8);
+  }
+  float mine = 0.f;  // lane 2k+half (k < 8) ends up holding token s0 + 2k + half
+#pragma unroll
+  for (int k = 0; k < kTok / 2; ++k) {
+    const uint32_t* o32 = &ov[k].x;
+    const uint32_t* g32 = &gv[k].x;
+    float acc = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 a = unpack_bf16x2(o32[e]), c = unpack_bf16x2(g32[e]);
+      acc += a.x * c.x + a.y * c.y;
+    }
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    // acc: half-0 lanes hold token 2k, half-1 lanes token 2k+1; lanes 0..15
+    // also receive the half-1 value
+    const float other = __shfl_down_sync(0xffffffffu, acc, 16);
+    if (lane == 2 * k) mine = acc;
+    if (lane == 2 * k + 1) mine = other;
+  }
+  if (dq_acc) {
+#pragma unroll
+    for (int k = 0; k < kTok / 2; ++k) {
+      const int s = s0 + 2 * k + half;
+      if (s < S) {
+        float4* z = reinterpret_cast<float4*>(dq_acc + ((int64_t)b * S + s) * ld_acc + h * HD + hl * 8);
+        z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+        z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  }
+  const int s = s0 + lane;
+  if (lane < kTok && s < S) {
+    const int64_t idx = (int64_t)bh * S + s;
+    delta2[idx] = mine * scale;
+    lse2[idx] = -lse[idx] * kLog2e;
+  }
+}
+
+// dQ from the stored dS tiles: persistent CTAs walk the (query tile i, batch,
+// head) items, heavy tiles first; dQ_i = sum_j dS_ij K_j accumulates in TMEM
+// (double buffered, so the epilogue of one item overlaps the next item's
+// products) and leaves as bf16 (dS already carries the softmax scale).  Warp
+// 0 streams the dS tiles (1-D bulk copies of the stored shared-memory images)
+// and the K tiles (TMA) through a 3-stage ring, warp 1 issues the MMAs, warps
+// 2..5 write dq.
+constexpr int DQ_STAGES = 3;
+constexpr int DQ_SMEM = DQ_STAGES * 2 * TILE + 1024 + 256;
+
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmK, const __nv_bfloat16* __restrict__ ds_buf,
+                       __nv_bfloat16* __restrict__ dq, int64_t lddq, int B, int S, int nq, int nkv, bool causal,
+                       int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sDS = smem;                     // [stages][TILE]
+  uint8_t* sKt = smem + DQ_STAGES * TILE;  // [stages][TILE]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * DQ_STAGES * TILE);
+  uint64_t* full = bars;                // [stages]
+  uint64_t* empty = bars + DQ_STAGES;   // [stages]
+  uint64_t* tfull = bars + 2 * DQ_STAGES;  // [2] accumulator ready
+  uint64_t* tempty = tfull + 2;            // [2] accumulator drained
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_t = (S + BT - 1) / BT;
+  const int n_items = B * nq * n_t;
+  const int tiles_bh = causal ? n_t * (n_t + 1) / 2 : n_t * n_t;
+  auto decode = [&](int w, int& qi, int& b, int& h) {
+    qi = n_t - 1 - w / (B * nq);  // heaviest query tiles first
+    const int rem = w % (B * nq);
+    b = rem / nq;
+    h = rem % nq;
+  };
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < DQ_STAGES; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmK);
+      int n = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+        int qi, b, h;
+        decode(w, qi, b, h);
+        const int kvh = h / (nq / nkv);
+        const int n_j = causal ? qi + 1 : n_t;
+        const int64_t tile0 = ((int64_t)b * nq + h) * tiles_bh + (causal ? (int64_t)qi * (qi + 1) / 2 : (int64_t)qi * n_t);
+        for (int jj = 0; jj < n_j; ++jj, ++n) {
+          const int st = n % DQ_STAGES;
+          if (!mbar_wait(&empty[st], ((n / DQ_STAGES) & 1) ^ 1, err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[st], 2 * TILE);
+          bulk_load(sDS + st * TILE, ds_buf + (tile0 + jj) * (TILE / 2), TILE, &full[st]);
+          for (int a = 0; a < 2; ++a)
+            tma_load_3d(sKt + st * TILE + a * (TILE / 2), &tmK, &full[st], kvh * HD + a * 64, jj * BT, b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_mm = idesc_bf16(128, 128, true, true);  // both MN-major
+      bool ok = true;
+      int n = 0, local = 0;
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++local) {
+        int qi, b, h;
+        decode(w, qi, b, h);
+        const int n_j = causal ? qi + 1 : n_t;
+        const int acc = local & 1;
+        if (!mbar_wait(&tempty[acc], ((local >> 1) & 1) ^ 1, err)) { ok = false; break; }
+        tc_fence_after();
+        for (int jj = 0; jj < n_j; ++jj, ++n) {
+          const int st = n % DQ_STAGES;
+          if (!mbar_wait(&full[st], (n / DQ_STAGES) & 1, err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t ds_base = smem_u32(sDS + st * TILE), k_base = smem_u32(sKt + st * TILE);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)  // dQ += dS K_j   (K = keys; dS^T image read MN-major)
+            mma_bf16_ss(tmem + acc * 128, smem_desc_sw128(ds_base + kk * 2048, TILE / 2, 1024),
+                        smem_desc_sw128(k_base + kk * 2048, TILE / 2, 1024), id_mm, (jj > 0 || kk > 0));
+          mma_commit(&empty[st]);
+        }
+        if (ok) mma_commit(&tfull[acc]);
+      }
+      if (!ok) {
+        mma_commit(drain);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(smem_u32(drain), 0) && globaltimer() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    int local = 0;
+    for (int w = blockIdx.x; w < n_items; w += gridDim.x, ++local) {
+      int qi, b, h;
+      decode(w, qi, b, h);
+      const int acc = local & 1;
+      if (!mbar_wait(&tfull[acc], (local >> 1) & 1, err)) break;
+      tc_fence_after();
+      const int q = qi * BT + r;
+      __nv_bfloat16* dst = dq + ((int64_t)b * S + q) * lddq + (int64_t)h * HD;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(tmem + acc * 128 + ((uint32_t)(quarter * 32) << 16) + c * 32, v);
+        tmem_wait_ld();
+        if (q < S) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint4 o;
+            o.x = pack_bf16x2(v[u * 8 + 0], v[u * 8 + 1]);
+            o.y = pack_bf16x2(v[u * 8 + 2], v[u * 8 + 3]);
+            o.z = pack_bf16x2(v[u * 8 + 4], v[u * 8 + 5]);
+            o.w = pack_bf16x2(v[u * 8 + 6], v[u * 8 + 7]);
+            d4[u] = o;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
   }
 }
 
@@ -531,37 +729,53 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   PB_CHECK(p.S % 8 == 0, "attention bwd: sequence length must be a multiple of 8");
   static bool attr = false;
   if (!attr) {
-    PB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       SMEM_BYTES));
-    PB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       SMEM_BYTES));
+    for (auto k : {attn_bwd_kernel<false, false>, attn_bwd_kernel<true, false>, attn_bwd_kernel<false, true>,
+                   attn_bwd_kernel<true, true>})
+      PB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    PB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DQ_SMEM));
     attr = true;
   }
+  const bool ds_path = p.ds_buf != nullptr;
+  PB_CHECK(ds_path || p.dq_acc != nullptr, "attention bwd: needs a dS tile buffer or a dQ accumulator");
   const int64_t T = (int64_t)p.B * p.S;
   const int64_t rows = (int64_t)p.B * p.nq * p.S;
   const int64_t ld_acc = (int64_t)p.nq * HD;
-  const int64_t prep_threads = std::max<int64_t>(T * p.nq * 32, 128);
+  const int64_t prep_threads = std::max<int64_t>((int64_t)p.B * p.nq * ((p.S + 15) / 16) * 32, 128);
   attn_bwd_prep_kernel<<<(unsigned)((prep_threads + 255) / 256), 256, 0, s>>>(
-      (const __nv_bfloat16*)p.o, p.ldo, (const __nv_bfloat16*)p.dout, p.lddo, p.lse, p.delta, p.dq_acc, ld_acc,
-      p.B, p.S, p.nq, p.scale);
+      (const __nv_bfloat16*)p.o, p.ldo, (const __nv_bfloat16*)p.dout, p.lddo, p.lse, p.delta,
+      ds_path ? nullptr : p.dq_acc, ld_acc, p.B, p.S, p.nq, p.scale);
   PB_CUDA_CHECK(cudaGetLastError());
   const uint64_t S = p.S, B = p.B;
   CUtensorMap tq = make_tmap_3d_bf16(p.q, (uint64_t)p.nq * HD, S, B, p.ldq, S * p.ldq, 64, 128, 1);
   CUtensorMap tk = make_tmap_3d_bf16(p.k, (uint64_t)p.nkv * HD, S, B, p.ldk, S * p.ldk, 64, 128, 1);
   CUtensorMap tv = make_tmap_3d_bf16(p.v, (uint64_t)p.nkv * HD, S, B, p.ldv, S * p.ldv, 64, 128, 1);
   CUtensorMap tdo = make_tmap_3d_bf16(p.dout, (uint64_t)p.nq * HD, S, B, p.lddo, S * p.lddo, 64, 128, 1);
-  CUtensorMap tdq = make_tmap_3d_f32(p.dq_acc, (uint64_t)ld_acc, S, B, ld_acc, S * ld_acc, 32, 128, 1, true);
+  CUtensorMap tdq{};
+  if (!ds_path) tdq = make_tmap_3d_f32(p.dq_acc, (uint64_t)ld_acc, S, B, ld_acc, S * ld_acc, 32, 32, 1, true);
   const int n_t = (p.S + BT - 1) / BT;
   const int grid = p.B * p.nkv * n_t;
-  auto kern = p.trace ? attn_bwd_kernel<true> : attn_bwd_kernel<false>;
+  auto kern = ds_path ? (p.trace ? attn_bwd_kernel<true, true> : attn_bwd_kernel<false, true>)
+                      : (p.trace ? attn_bwd_kernel<true, false> : attn_bwd_kernel<false, false>);
   kern<<<grid, kThreads, SMEM_BYTES, s>>>(tq, tk, tv, tdo, tdq, p.delta + rows + 128, p.delta, (__nv_bfloat16*)p.dk,
                                           p.lddk, (__nv_bfloat16*)p.dv, p.lddv, p.B, p.S, p.nq, p.nkv, p.scale,
-                                          p.causal, error_word(), p.trace);
+                                          p.causal, error_word(), p.trace, (__nv_bfloat16*)p.ds_buf);
   PB_CUDA_CHECK(cudaGetLastError());
+  if (ds_path) {
+    attn_bwd_dq_kernel<<<std::min(num_sms(), p.B * p.nq * n_t), 192, DQ_SMEM, s>>>(tk, (const __nv_bfloat16*)p.ds_buf,
+                                                              (__nv_bfloat16*)p.dq, p.lddq, p.B, p.S, p.nq, p.nkv,
+                                                              p.causal, error_word());
+    PB_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const int64_t cast_work = T * ld_acc / 4;
   int cgrid = (int)std::min<int64_t>((cast_work + 255) / 256, (int64_t)num_sms() * 16);
   cast_rows_kernel<<<cgrid, 256, 0, s>>>(p.dq_acc, ld_acc, (__nv_bfloat16*)p.dq, p.lddq, (int)T, (int)ld_acc);
   PB_CUDA_CHECK(cudaGetLastError());
+}
+
+int64_t attention_bwd_ds_elems(int B, int S, int nq, bool causal) {
+  const int64_t n_t = (S + BT - 1) / BT;
+  return (int64_t)B * nq * (causal ? n_t * (n_t + 1) / 2 : n_t * n_t) * (TILE / 2);
 }
 
 }  // namespace pb
@@ -677,7 +891,7 @@ extern "C" __attribute__((visibility("default"))) int pb_attention_bwd_noalloc(
       g_noalloc_base[dev] = ptr;
     }
     if (!g_noalloc_attr[dev]) {
-      if (cudaFuncSetAttribute(attn_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+      if (cudaFuncSetAttribute(attn_bwd_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
           cudaSuccess) {
         noalloc_set_msg("pb_attention_bwd_noalloc: cudaFuncSetAttribute failed");
         return kNoAllocCudaError;
@@ -692,7 +906,7 @@ extern "C" __attribute__((visibility("default"))) int pb_attention_bwd_noalloc(
   try {
     // the prep kernel zeroes the dq accumulator and the scratch padding
     PB_CUDA_CHECK(cudaMemsetAsync(err, 0, 256, stream));
-    const int64_t prep_threads = std::max<int64_t>(T * nq * 32, 128);
+    const int64_t prep_threads = std::max<int64_t>((int64_t)B * nq * ((S + 15) / 16) * 32, 128);
     attn_bwd_prep_kernel<<<(unsigned)((prep_threads + 255) / 256), 256, 0, stream>>>(
         (const __nv_bfloat16*)o, ldo, (const __nv_bfloat16*)dout, lddo, lse, delta, dq_acc, ld_acc, B, S, nq, scale);
     PB_CUDA_CHECK(cudaGetLastError());
@@ -701,11 +915,11 @@ extern "C" __attribute__((visibility("default"))) int pb_attention_bwd_noalloc(
     CUtensorMap tk = make_tmap_3d_bf16(k, (uint64_t)nkv * HD, uS, uB, ldk, uS * ldk, 64, 128, 1);
     CUtensorMap tv = make_tmap_3d_bf16(v, (uint64_t)nkv * HD, uS, uB, ldv, uS * ldv, 64, 128, 1);
     CUtensorMap tdo = make_tmap_3d_bf16(dout, (uint64_t)nq * HD, uS, uB, lddo, uS * lddo, 64, 128, 1);
-    CUtensorMap tdq = make_tmap_3d_f32(dq_acc, (uint64_t)ld_acc, uS, uB, ld_acc, uS * ld_acc, 32, 128, 1, true);
+    CUtensorMap tdq = make_tmap_3d_f32(dq_acc, (uint64_t)ld_acc, uS, uB, ld_acc, uS * ld_acc, 32, 32, 1, true);
     const int n_t = (S + BT - 1) / BT;
-    attn_bwd_kernel<false><<<B * nkv * n_t, kThreads, SMEM_BYTES, stream>>>(
+    attn_bwd_kernel<false, false><<<B * nkv * n_t, kThreads, SMEM_BYTES, stream>>>(
         tq, tk, tv, tdo, tdq, delta + rows + 128, delta, (__nv_bfloat16*)dk, lddk, (__nv_bfloat16*)dv, lddv, B, S,
-        nq, nkv, scale, causal != 0, err, nullptr);
+        nq, nkv, scale, causal != 0, err, nullptr, nullptr);
     PB_CUDA_CHECK(cudaGetLastError());
     int sms = 0;
     PB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));

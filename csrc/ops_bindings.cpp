@@ -206,7 +206,7 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
 void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
               const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq_acc, at::Tensor& dq,
               at::Tensor& dk, at::Tensor& dv, int64_t B, int64_t S, int64_t nq, int64_t nkv, double scale,
-              bool causal, const c10::optional<at::Tensor>& trace) {
+              bool causal, const c10::optional<at::Tensor>& trace, const c10::optional<at::Tensor>& ds_buf) {
   CHECK_BF16(q); CHECK_BF16(k); CHECK_BF16(v); CHECK_BF16(o); CHECK_BF16(dout); CHECK_BF16(dq); CHECK_BF16(dk);
   CHECK_BF16(dv); CHECK_F32(lse); CHECK_F32(delta); CHECK_F32(dq_acc);
   const int64_t D = q.size(1) / nq;
@@ -214,7 +214,8 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   TORCH_CHECK(lse.numel() >= B * nq * S, "attn bwd: lse too small");
   TORCH_CHECK(delta.numel() >= 2 * (B * nq * S + 128), "attn bwd: delta scratch needs 2 * (B*nq*S + 128) floats");
   TORCH_CHECK(delta.is_contiguous() && dq_acc.is_contiguous(), "attn bwd: scratch must be contiguous");
-  TORCH_CHECK(dq_acc.numel() >= B * S * nq * D, "attn bwd: dq_acc too small");
+  const bool use_ds = ds_buf.has_value() && ds_buf->defined();
+  TORCH_CHECK(use_ds || dq_acc.numel() >= B * S * nq * D, "attn bwd: dq_acc too small");
   const c10::cuda::CUDAGuard g(q.device());
   pb::AttnBwdParams p{};
   p.q = q.data_ptr(); p.k = k.data_ptr(); p.v = v.data_ptr(); p.o = o.data_ptr(); p.dout = dout.data_ptr();
@@ -230,7 +231,17 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
                 "trace needs kAttnBwdTraceSlots int64 entries per CTA");
     p.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
   }
+  if (use_ds) {
+    CHECK_BF16(*ds_buf);
+    TORCH_CHECK(ds_buf->is_contiguous() && ds_buf->numel() >= pb::attention_bwd_ds_elems((int)B, (int)S, (int)nq, causal),
+                "attn bwd: ds_buf too small (attn_bwd_ds_elems)");
+    p.ds_buf = ds_buf->data_ptr();
+  }
   pb::attention_bwd(p, cur_stream());
+}
+
+int64_t attn_bwd_ds_elems(int64_t B, int64_t S, int64_t nq, bool causal) {
+  return pb::attention_bwd_ds_elems((int)B, (int)S, (int)nq, causal);
 }
 
 }  // namespace
@@ -257,5 +268,6 @@ void register_ops(pybind11::module& m) {
   m.def("attn_bwd", &attn_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("dout"),
         py::arg("lse"), py::arg("delta"), py::arg("dq_acc"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("B"),
         py::arg("S"), py::arg("nq"), py::arg("nkv"), py::arg("scale"), py::arg("causal"),
-        py::arg("trace") = py::none());
+        py::arg("trace") = py::none(), py::arg("ds_buf") = py::none());
+  m.def("attn_bwd_ds_elems", &attn_bwd_ds_elems);
 }

@@ -136,6 +136,14 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
       : "memory");
 }
 
+// Untiled bulk copy shared -> global (bulk-group completion); addresses
+// 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_store(void* gdst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(gdst)),
+               "r"(smem_u32(smem_src)), "r"(bytes)
+               : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 // TMEM allocation: executed by one full warp; the base address is written to
 // `*dst_smem`.  ncols must be a power of two >= 32.

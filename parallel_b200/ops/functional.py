@@ -17,6 +17,7 @@ cross-entropy over labels != -100.
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 import torch.nn.functional as F
@@ -173,6 +174,9 @@ def residual_rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float):
 
 
 # ----------------------------------------------------------------- attention block
+# Upper bound of the attention backward's dS tile buffer (bf16, causal tiles of
+# every head); larger problems use the fp32 dQ accumulator instead.
+_ATTN_DS_LIMIT_BYTES = int(os.environ.get("PB_ATTN_DS_LIMIT_BYTES", str(4 << 30)))
 class _AttentionFn(torch.autograd.Function):
     """qkv = h W_qkv^T -> per-head q/k RMSNorm + RoPE -> causal GQA flash
     attention.  Returns the attention output [T, nq*D] (before o_proj)."""
@@ -221,8 +225,16 @@ class _AttentionFn(torch.autograd.Function):
         dv = dqkv[:, (nq + nkv) * D:]
         v = qkv[:, (nq + nkv) * D:]
         delta = torch.empty(2 * (B * nq * S + 128), device=h.device, dtype=torch.float32)
-        dq_acc = torch.empty(T, nq * D, device=h.device, dtype=torch.float32)
-        ext().attn_bwd(q, k, v, o, do, lse, delta, dq_acc, dq, dk, dv, B, S, nq, nkv, 1.0 / math.sqrt(D), True)
+        ds_elems = ext().attn_bwd_ds_elems(B, S, nq, True)
+        if ds_elems * 2 <= _ATTN_DS_LIMIT_BYTES:
+            # dS tiles stored once, dQ from a second tcgen05 kernel (no fp32 accumulator)
+            ds_buf = torch.empty(ds_elems, device=h.device, dtype=torch.bfloat16)
+            dq_acc = torch.empty(0, device=h.device, dtype=torch.float32)
+        else:  # very long sequences: dQ reduced into an fp32 accumulator in place
+            ds_buf = None
+            dq_acc = torch.empty(T, nq * D, device=h.device, dtype=torch.float32)
+        ext().attn_bwd(q, k, v, o, do, lse, delta, dq_acc, dq, dk, dv, B, S, nq, nkv, 1.0 / math.sqrt(D), True,
+                       None, ds_buf)
         dqw = torch.zeros(D, device=h.device, dtype=torch.float32)
         dkw = torch.zeros(D, device=h.device, dtype=torch.float32)
         ext().qknorm_rope_bwd(dq, dk, qkv, qw, kw, cos, sin, rstd, dqkv, dqw, dkw, S, nq, nkv)

@@ -334,16 +334,20 @@ def test_attention_fwd_bwd(B, S, nq, nkv):
         return
     do = torch.randn(T, nq * D, device="cuda").to(torch.bfloat16)
     o_ref.backward(do.float())
-    delta = torch.empty(2 * (B * nq * S + 128), device="cuda")
-    dq_acc = torch.empty(T, nq * D, device="cuda")
-    dq = torch.empty_like(q)
-    dk = torch.empty_like(k)
-    dv = torch.empty(T, nkv * D, device="cuda", dtype=torch.bfloat16)
-    C.attn_bwd(q, k, v, o, do, lse, delta, dq_acc, dq, dk, dv, B, S, nq, nkv, 1 / math.sqrt(D), True)
-    _check_no_device_error()
-    assert _rel_err(dv, vf.grad) < 3e-2
-    assert _rel_err(dk, kf.grad) < 3e-2
-    assert _rel_err(dq, qf.grad) < 3e-2
+    for use_ds in (False, True):  # fp32 dQ accumulator path, stored-dS + dQ-kernel path
+        delta = torch.empty(2 * (B * nq * S + 128), device="cuda")
+        dq_acc = torch.empty(T, nq * D, device="cuda")
+        ds_buf = (torch.empty(C.attn_bwd_ds_elems(B, S, nq, True), device="cuda", dtype=torch.bfloat16)
+                  if use_ds else None)
+        dq = torch.empty_like(q)
+        dk = torch.empty_like(k)
+        dv = torch.empty(T, nkv * D, device="cuda", dtype=torch.bfloat16)
+        C.attn_bwd(q, k, v, o, do, lse, delta, dq_acc, dq, dk, dv, B, S, nq, nkv, 1 / math.sqrt(D), True, None,
+                   ds_buf)
+        _check_no_device_error()
+        assert _rel_err(dv, vf.grad) < 3e-2, use_ds
+        assert _rel_err(dk, kf.grad) < 3e-2, use_ds
+        assert _rel_err(dq, qf.grad) < 3e-2, use_ds
 
 
 @pytest.mark.gpu
