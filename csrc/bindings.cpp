@@ -22,7 +22,8 @@ cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 //   b: [N, K] (b_mn=False) or [K, N] (b_mn=True), unit inner stride
 //   out: [M, N] bf16 or fp32 depending on epi
 void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, bool b_mn, int64_t epi,
-          double alpha, const c10::optional<at::Tensor>& r, int64_t b_up_offset, int64_t n_out, int64_t kernel) {
+          double alpha, const c10::optional<at::Tensor>& r, int64_t b_up_offset, int64_t n_out, int64_t kernel,
+          int64_t splits) {
   CHECK_CUDA_BF16(a);
   CHECK_CUDA_BF16(b);
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm: 2-D operands expected");
@@ -47,13 +48,15 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, 
   p.max_ctas = 0;
   TORCH_CHECK(kernel >= 0 && kernel <= 2, "gemm: kernel must be 0 (choose), 1 (one CTA) or 2 (CTA pair)");
   p.kernel = (int)kernel;
+  TORCH_CHECK(splits >= 1 && splits <= 16, "gemm: splits in [1, 16]");
+  p.splits = (int)splits;
   p.b_up_offset = b_up_offset;
   if (epi == pb::kEpiSwiGLU) {
     p.N = (int)n_out;
     TORCH_CHECK(b_up_offset + n_out <= b.size(0), "gemm: swiglu B too small");
   }
   TORCH_CHECK(out.size(0) == p.M && out.size(1) == p.N, "gemm: output shape mismatch");
-  const bool f32 = epi == pb::kEpiStoreF32 || epi == pb::kEpiAccumF32;
+  const bool f32 = epi == pb::kEpiStoreF32 || epi == pb::kEpiAccumF32 || epi == pb::kEpiAtomicF32;
   TORCH_CHECK(out.scalar_type() == (f32 ? at::kFloat : at::kBFloat16), "gemm: output dtype mismatch");
   if (r.has_value() && r->defined()) {
     CHECK_CUDA_BF16(*r);
@@ -179,7 +182,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM with fused epilogues", pybind11::arg("a"),
         pybind11::arg("b"), pybind11::arg("out"), pybind11::arg("a_mn"), pybind11::arg("b_mn"),
         pybind11::arg("epi"), pybind11::arg("alpha"), pybind11::arg("r") = pybind11::none(),
-        pybind11::arg("b_up_offset") = 0, pybind11::arg("n_out") = 0, pybind11::arg("kernel") = 0);
+        pybind11::arg("b_up_offset") = 0, pybind11::arg("n_out") = 0, pybind11::arg("kernel") = 0,
+        pybind11::arg("splits") = 1);
   m.def("gemm_ag", &gemm_ag, "GEMM with the sequence-parallel all-gather of A in the same kernel",
         pybind11::arg("dst"), pybind11::arg("src_ptrs"), pybind11::arg("src_ld"), pybind11::arg("flags"),
         pybind11::arg("target"), pybind11::arg("seq"), pybind11::arg("seq_local"), pybind11::arg("batch"),

@@ -22,6 +22,7 @@ enum GemmEpilogue : int {
   kEpiSwiGLU = 5,         // B rows [0,N) are gate, [N,2N) are up (same ldb, "b_up_offset" rows
                           // apart): C(bf16) = silu(g)*u, and if R != null, R(bf16) receives the
                           // raw [g | u] pre-activations (ldr) for the backward.
+  kEpiAtomicF32 = 6,      // C(f32) += alpha*acc with atomic adds (split-K partial sums)
 };
 
 // Sequence-parallel reduce-scatter epilogue: output row m = b*seq + s (a row
@@ -65,6 +66,7 @@ struct GemmParams {
   int64_t b_up_offset;  // kEpiSwiGLU: row offset (in N units) of the "up" half of B
   int max_ctas;         // 0 = one CTA per SM
   int kernel = 0;       // 0 = choose, 1 = one-CTA kernel, 2 = CTA-pair kernel
+  int splits = 1;       // split-K slices (CTA-pair kernel, kEpiAtomicF32 only)
   const ScatterArgs* scatter = nullptr;  // kEpiStoreBf16 rows to their sequence-parallel owners
   const GatherArgs* gather = nullptr;    // A assembled from sequence-parallel shards in-kernel
 };

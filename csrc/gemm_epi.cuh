@@ -130,6 +130,15 @@ __device__ __forceinline__ void epilogue_row(const EpiArgs& ep, uint32_t t_row, 
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] += r[j];
         store_row_bf16(reinterpret_cast<__nv_bfloat16*>(ep.C) + (int64_t)m * ep.ldc + n0, v, n0, N);
+      } else if (ep.epi == kEpiAtomicF32) {
+        float* dst = reinterpret_cast<float*>(ep.C) + (int64_t)m * ep.ldc + n0;
+        if (n0 + 32 <= N) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            atomicAdd(reinterpret_cast<float4*>(dst) + q, make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]));
+        } else {
+          for_cols(n0, N, [&](int j) { atomicAdd(dst + j, v[j]); });
+        }
       } else {
         float* dst = reinterpret_cast<float*>(ep.C) + (int64_t)m * ep.ldc + n0;
         const bool accum = ep.epi == kEpiAccumF32;

@@ -91,7 +91,8 @@ __device__ __forceinline__ void gather_piece(const GatherArgs& g, int K, int blk
 template <int BN, bool A_MN, bool B_MN, bool SWIGLU, bool GATHER>
 __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiArgs ep,
-                     int M, int N, int K, int b_up_row, int* err, const __grid_constant__ GatherArgs ga) {
+                     int M, int N, int K, int b_up_row, int* err, const __grid_constant__ GatherArgs ga,
+                     int splits) {
   using Cfg = PairCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int B_HALF = Cfg::B_HALF;
@@ -143,6 +144,9 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
   const int tiles_n = (N + BN_OUT - 1) / BN_OUT;
   const int num_tiles = tiles_m * tiles_n;
   const int num_kb = (K + BK - 1) / BK;
+  // work item w = (tile, K slice): tile = w % num_tiles, slice = w / num_tiles
+  const int kb_per = (num_kb + splits - 1) / splits;
+  const int num_work = num_tiles * splits;
   const int n_clusters = gridDim.x >> 1;
   const int cid = blockIdx.x >> 1;
 
@@ -151,7 +155,9 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = cid; tile < num_tiles && ok; tile += n_clusters) {
+      for (int w = cid; w < num_work && ok; w += n_clusters) {
+        const int tile = w % num_tiles;
+        const int kb0 = (w / num_tiles) * kb_per, kb1 = min(num_kb, kb0 + kb_per);
         const int tm = GATHER ? ga.m_order[tile % tiles_m] : tile % tiles_m, tn = tile / tiles_m;
         const int a_row = tm * 2 * BM_CTA + (int)rank * BM_CTA;
         if constexpr (GATHER) {
@@ -168,7 +174,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
           if (!ok) break;
           asm volatile("fence.proxy.async.global;" ::: "memory");
         }
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, err)) { ok = false; break; }
           const uint32_t full_even = mapa_shared(smem_u32(&full_bar[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::STAGE_BYTES);
@@ -203,13 +209,14 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = cid; tile < num_tiles && ok; tile += n_clusters, ++local) {
+      for (int w = cid; w < num_work && ok; w += n_clusters, ++local) {
+        const int kb0 = (w / num_tiles) * kb_per, kb1 = min(num_kb, kb0 + kb_per);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, err)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, err)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_base = smem_u32(sA + stage * Cfg::A_BYTES);
@@ -220,7 +227,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
                                         : smem_desc_sw128(a_base + kk * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? smem_desc_sw128(b_base + kk * 2048, 64 * BK * 2, 1024)
                                         : smem_desc_sw128(b_base + kk * 32, 16, 1024);
-            mma_bf16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            mma_bf16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
           }
           mma_commit_pair(&empty_bar[stage], 0x3);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -238,7 +245,8 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     int local = 0;
-    for (int tile = cid; tile < num_tiles; tile += n_clusters, ++local) {
+    for (int w = cid; w < num_work; w += n_clusters, ++local) {
+      const int tile = w % num_tiles;
       const int tm = GATHER ? ga.m_order[tile % tiles_m] : tile % tiles_m, tn = tile / tiles_m;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
@@ -312,12 +320,13 @@ void launch_pair(const GemmParams& p, cudaStream_t stream) {
   GatherArgs ga{};
   if (GATHER) ga = *p.gather;
   const int bn_out = SWIGLU ? BN / 2 : BN;
-  const int tiles = ((p.M + 2 * BM_CTA - 1) / (2 * BM_CTA)) * ((p.N + bn_out - 1) / bn_out);
+  const int tiles = ((p.M + 2 * BM_CTA - 1) / (2 * BM_CTA)) * ((p.N + bn_out - 1) / bn_out) * std::max(1, p.splits);
   int clusters = max_clusters[dev & 63];
   if (p.max_ctas > 0) clusters = std::min(clusters, std::max(1, p.max_ctas / 2));
   clusters = std::max(1, std::min(clusters, tiles));
   cfg.gridDim = dim3(2 * clusters, 1, 1);
-  PB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, ep, p.M, p.N, p.K, (int)p.b_up_offset, error_word(dev), ga));
+  PB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, ep, p.M, p.N, p.K, (int)p.b_up_offset, error_word(dev), ga,
+                                   std::max(1, p.splits)));
 }
 
 }  // namespace
@@ -334,6 +343,8 @@ void gemm_bf16_pair(const GemmParams& p, cudaStream_t stream) {
     return launch_pair<256, false, true, false, true>(p, stream);
   }
   if (p.scatter) PB_CHECK(p.epi == kEpiStoreBf16 && p.scatter->nranks <= 8, "gemm: scatter needs the bf16 store epilogue");
+  PB_CHECK(p.splits <= 1 || (p.epi == kEpiAtomicF32 && !p.gather && !p.scatter),
+           "gemm: split-K needs the atomic fp32 epilogue");
   if (p.epi == kEpiSwiGLU) return launch_pair<256, false, false, true>(p, stream);
   if (!p.a_mn && !p.b_mn) return launch_pair<256, false, false, false>(p, stream);
   if (!p.a_mn && p.b_mn) return launch_pair<256, false, true, false>(p, stream);

@@ -22,6 +22,35 @@ EPI_STORE_F32 = 2
 EPI_ACCUM_BF16 = 3
 EPI_ACCUM_F32 = 4
 EPI_SWIGLU = 5
+EPI_ATOMIC_F32 = 6
+
+# Split-K for long-K products with few CTA-pair tiles (the weight gradients
+# reduce over all tokens): pick the slice count that minimises waves per unit
+# of K on the SM pairs, and only when it saves at least 15%.
+_SPLITK_MIN_K = 2048
+
+
+def _pair_slots() -> int:
+    try:
+        return max(1, torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count // 2)
+    except Exception:
+        return 74
+
+
+def _splitk(M: int, N: int, K: int, slots: int | None = None) -> int:
+    if M < 256 or K < 2 * _SPLITK_MIN_K:
+        return 1
+    slots = slots or _pair_slots()
+    tiles = ((M + 255) // 256) * ((N + 255) // 256)
+
+    def cost(s):
+        return -(-tiles * s // slots) / s
+
+    best = 1
+    for s in (2, 3, 4):
+        if K // s >= _SPLITK_MIN_K and cost(s) < cost(best) and cost(s) <= 0.85 * cost(1):
+            best = s
+    return best
 
 
 def _rows(t: torch.Tensor) -> torch.Tensor:
@@ -107,6 +136,19 @@ def linear_wgrad(g: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = No
     if out is None:
         out = torch.empty(g2.shape[1], x2.shape[1], dtype=out_dtype, device=g.device)
         accumulate = False
+    M, N, K = g2.shape[1], x2.shape[1], g2.shape[0]
+    splits = _splitk(M, N, K)
+    if splits > 1:
+        # split-K over the tokens: slices add into an fp32 target with atomics
+        if out.dtype == torch.float32:
+            if not accumulate:
+                out.zero_()
+            ext().gemm(g2, x2, out, True, True, EPI_ATOMIC_F32, 1.0, splits=splits)
+            return out
+        ws = out.float() if accumulate else torch.zeros(M, N, dtype=torch.float32, device=g.device)
+        ext().gemm(g2, x2, ws, True, True, EPI_ATOMIC_F32, 1.0, splits=splits)
+        ext().cast_f32_to_bf16(ws, out)
+        return out
     if out.dtype == torch.float32:
         epi = EPI_ACCUM_F32 if accumulate else EPI_STORE_F32
     else:

@@ -429,3 +429,33 @@ def test_gemm_reducescatter_fused_emulated_ranks(b_mn):
         mine = torch.cat([total[bb * S + r * SL: bb * S + (r + 1) * SL] for bb in range(Bt)])
         got = recv[r].view(R, Bt * SL, N).float().sum(0)
         assert _rel_err(got, mine) < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K,splits", [(1024, 3072, 8192, 3), (1000, 520, 4096, 2), (2048, 1024, 8192, 4)])
+def test_gemm_splitk_atomic(M, N, K, splits):
+    """Split-K slices of the CTA-pair kernel adding into an fp32 target."""
+    C = _ext()
+    torch.manual_seed(7)
+    g = torch.randn(K, M, device="cuda").to(torch.bfloat16)  # wgrad layout: A MN-major
+    x = torch.randn(K, N, device="cuda").to(torch.bfloat16)
+    out = torch.full((M, N), 0.5, device="cuda")
+    C.gemm(g, x, out, True, True, 6, 1.0, splits=splits)
+    _check_no_device_error()
+    ref = g.float().t() @ x.float() + 0.5
+    assert _rel_err(out, ref) < 1e-3
+
+
+def test_linear_wgrad_splitk_policy():
+    from parallel_b200.ops.gemm import _splitk, linear_wgrad
+
+    torch.manual_seed(8)
+    T, N, K = 8192, 1024, 3072
+    g = torch.randn(T, N, device="cuda").to(torch.bfloat16)
+    x = torch.randn(T, K, device="cuda").to(torch.bfloat16)
+    assert _splitk(N, K, T) > 1
+    w = linear_wgrad(g, x)
+    _check_no_device_error()
+    assert w.dtype == torch.bfloat16 and _rel_err(w, g.float().t() @ x.float()) < 1e-2
+    acc = torch.ones(N, K, device="cuda", dtype=torch.float32)
+    linear_wgrad(g, x, out=acc, accumulate=True)
+    assert _rel_err(acc, g.float().t() @ x.float() + 1.0) < 1e-3
