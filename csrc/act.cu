@@ -196,24 +196,4 @@ void add_bf16_inplace(void* dst, const void* src, int64_t n, float alpha, cudaSt
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
-namespace {
-__global__ void exp2_emulated_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
-  for (int64_t i = 2 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x); i < n;
-       i += 2 * (int64_t)gridDim.x * blockDim.x) {
-    if (i + 1 < n) {
-      exp2_poly_pair(x[i], x[i + 1], y[i], y[i + 1]);
-    } else {
-      float dummy;
-      exp2_poly_pair(x[i], 0.f, y[i], dummy);
-    }
-  }
-}
-}  // namespace
-
-// Test hook for the FMA-pipe exp2 used by the attention softmax.
-void exp2_emulated(const float* x, float* y, int64_t n, cudaStream_t s) {
-  exp2_emulated_kernel<<<grid_for((n + 1) / 2, 256), 256, 0, s>>>(x, y, n);
-  PB_CUDA_CHECK(cudaGetLastError());
-}
-
 }  // namespace pb

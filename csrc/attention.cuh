@@ -24,6 +24,7 @@ struct AttnParams {
   int B, S, nq, nkv, D;
   float scale;  // softmax scale (1/sqrt(D))
   bool causal;
+  long long* trace = nullptr;  // optional per-CTA phase timing [grid * 16]
 };
 
 void attention_fwd(const AttnParams& p, cudaStream_t s);

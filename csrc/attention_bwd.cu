@@ -315,17 +315,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(s_empty);
       const bool masked = (causal && i == j) || (i + 1) * BT > S || (j + 1) * BT > S;
       if (!masked) {
-        const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
 #pragma unroll
         for (int c = 0; c < 64; c += 4) {
           const float4 l = *reinterpret_cast<const float4*>(lse_t + c);  // -lse * log2(e)
-          const float2 x01 = f2_unpack(ffma2(f2_pack(p[c], p[c + 1]), sc2, f2_pack(l.x, l.y)));
-          const float2 x23 = f2_unpack(ffma2(f2_pack(p[c + 2], p[c + 3]), sc2, f2_pack(l.z, l.w)));
-          // 5 of every 16 pairs on the FMA pipe, the rest on the special-function unit
-          if (((c >> 1) & 15) >= 11) exp2_poly_pair(x01.x, x01.y, p[c], p[c + 1]);
-          else { p[c] = ex2(x01.x); p[c + 1] = ex2(x01.y); }
-          if ((((c >> 1) + 1) & 15) >= 11) exp2_poly_pair(x23.x, x23.y, p[c + 2], p[c + 3]);
-          else { p[c + 2] = ex2(x23.x); p[c + 3] = ex2(x23.y); }
+          p[c] = ex2(fmaf(p[c], scale_log2, l.x));
+          p[c + 1] = ex2(fmaf(p[c + 1], scale_log2, l.y));
+          p[c + 2] = ex2(fmaf(p[c + 2], scale_log2, l.z));
+          p[c + 3] = ex2(fmaf(p[c + 3], scale_log2, l.w));
         }
       } else {
         const int q0 = i * BT + cg;

@@ -52,11 +52,27 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+template <bool kTrace>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int64_t ldo,
                     float* __restrict__ LSE, int B, int S, int nq, int nkv, float scale_log2, bool causal,
-                    int* err) {
+                    int* err, long long* trace) {
+  // optional per-CTA phase timing (clock64 cycles, kTrace builds only)
+  constexpr int kSlots = kTrace ? 16 : 1;
+  long long tacc[kSlots];
+#pragma unroll
+  for (int i = 0; i < kSlots; ++i) tacc[i] = 0;
+  auto tw = [&](int slot, uint64_t* bar, uint32_t par) -> bool {
+    if constexpr (!kTrace) {
+      return mbar_wait(bar, par, err);
+    } else {
+      const long long t0 = clock64();
+      const bool r = mbar_wait(bar, par, err);
+      tacc[slot] += clock64() - t0;
+      return r;
+    }
+  };
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -125,12 +141,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < n_kv; ++j) {
         const int st = j & 1;
         const uint32_t ph = ((j >> 1) & 1) ^ 1;
-        if (!mbar_wait(&k_empty[st], ph, err)) break;
+        if (!tw(0, &k_empty[st], ph)) break;
         mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
         uint8_t* kd = sK + st * TILE_BYTES;
         tma_load_3d(kd, &tmK, &k_full[st], kvh * HD, j * BKV, b);
         tma_load_3d(kd + TILE_BYTES / 2, &tmK, &k_full[st], kvh * HD + 64, j * BKV, b);
-        if (!mbar_wait(&v_empty[st], ph, err)) break;
+        if (!tw(0, &v_empty[st], ph)) break;
         mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
         uint8_t* vd = sV + st * TILE_BYTES;
         // MN-major V: [d-block (16 KB)][key-block (8 KB)] of {64 d x 64 keys}
@@ -146,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // S_t(j) = Q_t K_j^T
       auto issue_s = [&](int t, int j) -> bool {
         const int st = j & 1;
-        if (!mbar_wait(&k_full[st], (j >> 1) & 1, err)) return false;
+        if (!tw(1, &k_full[st], (j >> 1) & 1)) return false;
         tc_fence_after();
         const uint32_t q_base = smem_u32(sQ + t * TILE_BYTES);
         const uint32_t k_base = smem_u32(sK + st * TILE_BYTES);
@@ -159,14 +175,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&s_full[t]);
         return true;
       };
+      const long long t_mma0 = clock64();
       for (int t = 0; t < tpc && ok; ++t) ok = issue_s(t, 0);
       if (ok) mma_commit(&k_empty[0]);
       for (int j = 0; j < n_kv && ok; ++j) {
         const int st = j & 1;
-        if (!mbar_wait(&v_full[st], (j >> 1) & 1, err)) { ok = false; break; }
+        if (!tw(2, &v_full[st], (j >> 1) & 1)) { ok = false; break; }
         const uint32_t v_base = smem_u32(sV + st * TILE_BYTES);
         for (int t = 0; t < tpc; ++t) {
-          if (!mbar_wait(&p_full[t], j & 1, err)) { ok = false; break; }
+          if (!tw(3, &p_full[t], j & 1)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < BKV / 16; ++kk)  // O_t += P_t V_j, P_t from TMEM
@@ -178,6 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&v_empty[st]);
         if (j + 1 < n_kv) mma_commit(&k_empty[(j + 1) & 1]);
       }
+      if (kTrace) tacc[4] = clock64() - t_mma0;  // slot 4: MMA loop total
       if (ok) mma_commit(o_full);
       else {
         mma_commit(drain);
@@ -199,13 +217,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tO = tmem + 256 + t * 128 + lane_off;
       float m_ref = -INFINITY, l = 0.f;
       bool ok = true;
+      const long long t_sm0 = clock64();
+      long long tm = 0;
       for (int j = 0; j < n_kv; ++j) {
-        if (!mbar_wait(&s_full[t], j & 1, err)) { ok = false; break; }
+        if (!tw(5, &s_full[t], j & 1)) { ok = false; break; }  // slot 5
         tc_fence_after();
+        if (kTrace) tm = clock64();
         float s[128];
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s + c * 32);
         tmem_wait_ld();
+        if (kTrace) { tacc[9] += clock64() - tm; tm = clock64(); }  // slot 9: S load
         const int kbase = j * BKV;
         const bool diag = (causal && kbase + BKV - 1 > qi * BQ) || kbase + BKV > S;
         if (diag) {
@@ -215,9 +237,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             if ((causal && kpos > qpos) || kpos >= S) s[c] = -INFINITY;
           }
         }
-        float mx = s[0];
+        // row max as 8 independent chains (a single 127-deep chain is latency bound)
+        float m8[8];
 #pragma unroll
-        for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
+        for (int u = 0; u < 8; ++u) m8[u] = s[u];
+#pragma unroll
+        for (int c = 8; c < 128; c += 8)
+#pragma unroll
+          for (int u = 0; u < 8; ++u) m8[u] = fmaxf(m8[u], s[c + u]);
+        float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
         mx *= scale_log2;
         // lazy rescale: move the reference max only when it grew by > 2^8
         const bool need = mx > m_ref + kRescaleThreshold;
@@ -227,26 +255,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           m_ref = mx;
         }
         const float mu = (m_ref == -INFINITY) ? 0.f : m_ref;
-        const uint64_t sc2 = f2_pack(scale_log2, scale_log2), nmu2 = f2_pack(-mu, -mu);
-        uint64_t acc[4] = {0, 0, 0, 0};
+        float r4[4] = {0.f, 0.f, 0.f, 0.f};
         uint32_t pk[64];
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const float2 x = f2_unpack(ffma2(f2_pack(s[2 * c], s[2 * c + 1]), sc2, nmu2));
-          float a0, a1;
-          // 5 of every 16 pairs on the FMA pipe (masked tiles need exact zeros: all MUFU)
-          if (!diag && (c & 15) >= 11) {
-            exp2_poly_pair(x.x, x.y, a0, a1);
-          } else {
-            a0 = ex2(x.x);
-            a1 = ex2(x.y);
-          }
-          acc[c & 3] = fadd2(acc[c & 3], f2_pack(a0, a1));
+          const float a0 = ex2(fmaf(s[2 * c], scale_log2, -mu)), a1 = ex2(fmaf(s[2 * c + 1], scale_log2, -mu));
+          r4[c & 3] += a0 + a1;
           pk[c] = pack_bf16x2(a0, a1);
         }
-        const float2 r01 = f2_unpack(fadd2(acc[0], acc[1])), r23 = f2_unpack(fadd2(acc[2], acc[3]));
-        const float rs = (r01.x + r01.y) + (r23.x + r23.y);
+        const float rs = (r4[0] + r4[1]) + (r4[2] + r4[3]);
         l = l * alpha + rs;
+        if (kTrace) { tacc[10] += clock64() - tm; tm = clock64(); }  // slot 10: max + exp
         // O_t rescale: PV_t(j-1) is complete (S_t(j) was issued after it)
         if (j > 0 && __any_sync(0xffffffffu, need)) {
 #pragma unroll 1
@@ -259,13 +278,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st32(tO + c * 32, o);
           }
         }
+        if (kTrace) { tacc[7] += clock64() - tm; tm = clock64(); }  // slot 7: O rescale
         // P_t (bf16 pairs) over the first 64 columns of S_t
         tmem_st32(tS, reinterpret_cast<const float*>(pk));
         tmem_st32(tS + 32, reinterpret_cast<const float*>(pk + 32));
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&p_full[t]);
+        if (kTrace) tacc[11] += clock64() - tm;  // slot 11: P store
       }
+      if (kTrace) tacc[8] = clock64() - t_sm0;  // slot 8: softmax loop total
       if (ok && mbar_wait(o_full, 0, err)) {
         tc_fence_after();
         const float inv_l = l > 0.f ? 1.f / l : 0.f;
@@ -294,6 +316,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+  if constexpr (kTrace) {
+    if (threadIdx.x == 0 || threadIdx.x == 32 || threadIdx.x == 128) {
+      long long* dst = trace + (int64_t)blockIdx.x * 16;
+#pragma unroll
+      for (int i = 0; i < kSlots; ++i)
+        if (tacc[i]) atomicAdd(reinterpret_cast<unsigned long long*>(dst + i), (unsigned long long)tacc[i]);
+    }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -309,7 +339,9 @@ void attention_fwd(const AttnParams& p, cudaStream_t s) {
   PB_CHECK(p.nq % p.nkv == 0, "attention: nq must be a multiple of nkv");
   static bool attr = false;
   if (!attr) {
-    PB_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    PB_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       SMEM_BYTES));
+    PB_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        SMEM_BYTES));
     attr = true;
   }
@@ -321,9 +353,9 @@ void attention_fwd(const AttnParams& p, cudaStream_t s) {
   const int tpc = (G % 2 == 0) ? 2 : 1;
   const int n_qt = (p.S + BQ - 1) / BQ;
   const int grid = p.B * (p.nq / tpc) * n_qt;
-  attn_fwd_kernel<<<grid, kThreads, SMEM_BYTES, s>>>(tq, tk, tv, (__nv_bfloat16*)p.o, p.ldo, p.lse, p.B,
-                                                     p.S, p.nq, p.nkv, p.scale * kLog2e, p.causal,
-                                                     error_word());
+  auto kern = p.trace ? attn_fwd_kernel<true> : attn_fwd_kernel<false>;
+  kern<<<grid, kThreads, SMEM_BYTES, s>>>(tq, tk, tv, (__nv_bfloat16*)p.o, p.ldo, p.lse, p.B, p.S, p.nq, p.nkv,
+                                          p.scale * kLog2e, p.causal, error_word(), p.trace);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -66,7 +66,6 @@ void ce_row_stats(const void* logits, int64_t ld, int T, int V, float* row_max, 
 
 // ---- casts / elementwise helpers (act.cu)
 void cast_f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t s);
-void exp2_emulated(const float* x, float* y, int64_t n, cudaStream_t s);
 void add_bf16_inplace(void* dst, const void* src, int64_t n, float alpha, cudaStream_t s);
 
 // ---- optimizer (optim.cu)

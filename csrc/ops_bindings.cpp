@@ -121,13 +121,6 @@ void ce_row_stats(const at::Tensor& logits, at::Tensor& row_max, at::Tensor& row
                    row_sumexp.data_ptr<float>(), cur_stream());
 }
 
-void exp2_emulated(const at::Tensor& x, at::Tensor& y) {
-  CHECK_F32(x); CHECK_F32(y);
-  TORCH_CHECK(x.numel() == y.numel(), "exp2_emulated: size mismatch");
-  const c10::cuda::CUDAGuard g(x.device());
-  pb::exp2_emulated(x.data_ptr<float>(), y.data_ptr<float>(), x.numel(), cur_stream());
-}
-
 void cast_f32_to_bf16(const at::Tensor& src, at::Tensor& dst) {
   CHECK_F32(src);
   TORCH_CHECK(dst.is_contiguous() && dst.scalar_type() == at::kBFloat16 && dst.numel() == src.numel(), "cast: dst");
@@ -192,7 +185,8 @@ void clip_coef(const at::Tensor& total, double max_norm, at::Tensor& out) {
 }
 
 void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
-              int64_t B, int64_t S, int64_t nq, int64_t nkv, double scale, bool causal) {
+              int64_t B, int64_t S, int64_t nq, int64_t nkv, double scale, bool causal,
+              const c10::optional<at::Tensor>& trace) {
   CHECK_BF16(q); CHECK_BF16(k); CHECK_BF16(v); CHECK_BF16(o); CHECK_F32(lse);
   TORCH_CHECK(q.size(0) == B * S && k.size(0) == B * S && v.size(0) == B * S, "attn: token count");
   TORCH_CHECK(lse.numel() >= B * nq * S, "attn: lse too small");
@@ -200,6 +194,10 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
   pb::AttnParams p{q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(),
                    q.stride(0), k.stride(0), v.stride(0), o.stride(0), (int)B, (int)S, (int)nq, (int)nkv,
                    (int)(q.size(1) / nq), (float)scale, causal};
+  if (trace.has_value() && trace->defined()) {
+    TORCH_CHECK(trace->scalar_type() == at::kLong && trace->is_cuda(), "trace must be a CUDA int64 tensor");
+    p.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
+  }
   pb::attention_fwd(p, cur_stream());
 }
 
@@ -260,11 +258,12 @@ void register_ops(pybind11::module& m) {
   m.def("ce_fwd_bwd", &ce_fwd_bwd);
   m.def("ce_row_stats", &ce_row_stats);
   m.def("cast_f32_to_bf16", &cast_f32_to_bf16);
-  m.def("exp2_emulated", &exp2_emulated);
   m.def("adamw", &adamw);
   m.def("sumsq", &sumsq);
   m.def("clip_coef", &clip_coef);
-  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_fwd", &attn_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("B"),
+        py::arg("S"), py::arg("nq"), py::arg("nkv"), py::arg("scale"), py::arg("causal"),
+        py::arg("trace") = py::none());
   m.def("attn_bwd", &attn_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("dout"),
         py::arg("lse"), py::arg("delta"), py::arg("dq_acc"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("B"),
         py::arg("S"), py::arg("nq"), py::arg("nkv"), py::arg("scale"), py::arg("causal"),

@@ -375,56 +375,6 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t* bar, uint16_t cta_mask
       : "memory");
 }
 
-// ---------------------------------------------------------------- packed fp32 pairs
-// sm_100 executes add / fma on two fp32 lanes packed in a 64-bit register
-// with one instruction.
-__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
-  float a, b;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
-  return make_float2(a, b);
-}
-__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
-// 2^x for a pair on the FMA pipe (offloads the special-function unit).
-// Method: Cody-Waite range reduction (W. J. Cody and W. Waite, "Software
-// Manual for the Elementary Functions", 1980) with round-to-nearest by the
-// 1.5 * 2^23 addition trick, so x = j + f with j integer and |f| <= 1/2;
-// 2^f is a degree-3 polynomial whose coefficients were fitted for this file
-// with the Remez exchange algorithm (max relative error 7.5e-5 in fp32,
-// far below bf16 rounding); 2^j is added into the exponent field.  Inputs
-// are clamped to >= -125 so the exponent never underflows (the result is
-// then ~2^-125 instead of 0).
-__device__ __forceinline__ void exp2_poly_pair(float x0, float x1, float& e0, float& e1) {
-  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-  constexpr float c0 = 0.99992807f, c1 = 0.69326097f, c2 = 0.24261112f, c3 = 0.05517167f;
-  x0 = fmaxf(x0, -125.f);
-  x1 = fmaxf(x1, -125.f);
-  const uint64_t x = f2_pack(x0, x1);
-  const uint64_t t = fadd2(x, f2_pack(kMagic, kMagic));
-  const uint64_t jf = fadd2(t, f2_pack(-kMagic, -kMagic));
-  const uint64_t f = ffma2(jf, f2_pack(-1.f, -1.f), x);
-  uint64_t p = ffma2(f2_pack(c3, c3), f, f2_pack(c2, c2));
-  p = ffma2(p, f, f2_pack(c1, c1));
-  p = ffma2(p, f, f2_pack(c0, c0));
-  const float2 pv = f2_unpack(p), tv = f2_unpack(t);
-  e0 = __int_as_float(__float_as_int(pv.x) + (__float_as_int(tv.x) << 23));
-  e1 = __int_as_float(__float_as_int(pv.y) + (__float_as_int(tv.y) << 23));
-}
-
 // Warpgroup register re-balancing.  Every warp of a warpgroup executes the
 // same call; the increases of all warpgroups must fit in what the decreases
 // and the launch allocation (threads x registers at launch) provide.
