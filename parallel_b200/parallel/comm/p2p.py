@@ -92,6 +92,8 @@ class P2PUnitCollectives:
         self._slot_numel = 0
         self._next_slot = 0
         self.stream = None
+        self._need_barrier = True
+        self._prev_slot = None
         self._fallback = TorchUnitCollectives()
 
     # ------------------------------------------------------------ allocation
@@ -111,6 +113,15 @@ class P2PUnitCollectives:
     def release_full(self, unit, full):
         pass
 
+    def begin_forward(self) -> None:
+        """A forward pass starts: the shards may have changed since the last
+        one (optimizer step, checkpoint load), so the first all-gather waits
+        for every rank once.  Within the pass the shards are read-only, and
+        every rank finishes its reads of pass k before it can update its shard
+        (the optimizer step follows the gradient-norm all-reduce), so the
+        later gathers need no barrier."""
+        self._need_barrier = True
+
     # ------------------------------------------------------------ all-gather
     def all_gather(self, unit, mode: str = "demand") -> torch.Tensor:
         buf = getattr(unit, "_p2p", None)
@@ -128,7 +139,9 @@ class P2PUnitCollectives:
                 dst.append(fbase + (m.full_offset + r * m.padded_numel) * es)
                 nb.append(m.padded_numel * es)
         with collective_profile("fsdp_all_gather", value=unit.local_bucket, mode=mode, detail=unit_detail(unit)):
-            buf.barrier(0, self.limit_s)
+            if self._need_barrier:
+                buf.barrier(0, self.limit_s)
+                self._need_barrier = False
             ext().p2p_copy(src, dst, nb)
         return full
 
@@ -156,7 +169,7 @@ class P2PUnitCollectives:
             return _P2PHandle(None, None, self._fallback.reduce_scatter(unit, grads, grad_bucket, accumulate, mode))
         slot = self._slot(unit)
         cur = torch.cuda.current_stream(unit.device)
-        if slot.event is not None:
+        if slot.event is not None:  # every rank is done reading this slot's previous contents
             cur.wait_event(slot.event)
         N = self.world
         st = slot.tensor
@@ -180,12 +193,20 @@ class P2PUnitCollectives:
                                   detail=unit_detail(unit), device=unit.device, defer_cuda_end=True)
         with torch.cuda.stream(self.stream):
             with prof:
+                # every rank has staged its gradients into its slot
                 slot.barrier(1, self.limit_s)
+                # ...which also means every rank finished the previous reduction
+                # (issued before this barrier on its side stream), so the
+                # previous slot may be restaged
+                if self._prev_slot is not None:
+                    freed = torch.cuda.Event()
+                    freed.record(self.stream)
+                    self._prev_slot.event = freed
                 ext().p2p_reduce(src, dst, nel, 1.0 / N, accumulate)
-                slot.barrier(2, self.limit_s)
             ev = torch.cuda.Event()
             ev.record(self.stream)
-        slot.event = ev
+        slot.event = None  # set when the next reduction's barrier passes
+        self._prev_slot = slot
         return _P2PHandle(ev, prof)
 
     def wait(self, h: _P2PHandle) -> None:

@@ -262,6 +262,9 @@ class FSDPWrapper:
         layer.forward = forward
 
     def _root_pre_forward(self, module, args):
+        begin = getattr(self.coll, "begin_forward", None) if self.coll is not None else None
+        if begin is not None:
+            begin()
         for u in self.root_units:
             u.all_gather()
         nxt = self.root_units[-1].next_fwd if self.root_units else None

@@ -260,14 +260,22 @@ class DPParamUnit:
         if not self._grad_valid:
             return
         part = participation or [True] * len(self.param_metas)
+        key = self.grad_bucket.data_ptr()
         for keep, m in zip(part, self.param_metas):
             if not keep:
                 m.sharded_param.grad = None
                 continue
-            g = self.grad_bucket.narrow(0, m.bucket_offset, m.padded_numel).view(m.padded_rows, *m.shape[1:])
-            local = g.narrow(0, 0, m.local_rows)
-            m.sharded_param.grad = DTensor.from_local(local, device_mesh=self.mesh, placements=(Shard(0),),
-                                                      run_check=False, shape=m.shape, stride=m.stride)
+            # the bucket is persistent, so the DTensor views over it are built once
+            # (DTensor construction costs tens of microseconds of host time per call)
+            cached = getattr(m, "_grad_view", None)
+            if cached is None or cached[0] != key:
+                g = self.grad_bucket.narrow(0, m.bucket_offset, m.padded_numel).view(m.padded_rows, *m.shape[1:])
+                local = g.narrow(0, 0, m.local_rows)
+                dt = DTensor.from_local(local, device_mesh=self.mesh, placements=(Shard(0),), run_check=False,
+                                        shape=m.shape, stride=m.stride)
+                cached = (key, dt)
+                m._grad_view = cached
+            m.sharded_param.grad = cached[1]
 
     def zero_grad(self) -> None:
         """Start a new accumulation window (the bucket is reused, not freed)."""
