@@ -1,0 +1,120 @@
+"""Micro-benchmarks of the sm_100a kernels at the Qwen3-0.6B training shapes.
+
+    python -m parallel_b200.ops.kernel_bench attn_fwd|attn_bwd|gemm|rmsnorm_bwd|qknorm [--iters N]
+
+Each case runs a few warm-up launches, then times ``--iters`` launches with
+CUDA events on the current stream and prints the time per launch and the
+achieved TF/s or GB/s.  With ``--iters 1`` and ``--warmup 3`` the same command
+is the small case used for ``ncu --set full`` captures (select the kernel with
+``-k`` and skip the warm-up launches with ``-s 3``).
+"""
+from __future__ import annotations
+
+import argparse
+import math
+
+import torch
+
+from ._ext import check_device_errors, ext
+
+B, S, NQ, NKV, D, H, I = 4, 2048, 16, 8, 128, 1024, 3072
+
+
+def _time(fn, warmup: int, iters: int) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    check_device_errors()
+    return s.elapsed_time(e) / iters * 1e3  # us
+
+
+def _attn_inputs():
+    T = B * S
+    q = torch.randn(T, NQ * D, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(T, NKV * D, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(T, NKV * D, device="cuda", dtype=torch.bfloat16)
+    o = torch.empty_like(q)
+    lse = torch.zeros(B * NQ * S + 128, device="cuda")
+    return q, k, v, o, lse
+
+
+def case_attn_fwd(warmup, iters):
+    C = ext()
+    q, k, v, o, lse = _attn_inputs()
+    us = _time(lambda: C.attn_fwd(q, k, v, o, lse, B, S, NQ, NKV, 1 / math.sqrt(D), True), warmup, iters)
+    flops = 4 * B * NQ * S * S * D / 2
+    return f"attention fwd B={B} S={S} heads={NQ}/{NKV} D={D} causal: {us:.1f} us, {flops / us / 1e6:.0f} TF/s"
+
+
+def case_attn_bwd(warmup, iters):
+    C = ext()
+    q, k, v, o, lse = _attn_inputs()
+    C.attn_fwd(q, k, v, o, lse, B, S, NQ, NKV, 1 / math.sqrt(D), True)
+    do = torch.randn_like(q)
+    delta = torch.empty(2 * lse.numel(), device="cuda")
+    acc = torch.empty(0, device="cuda")
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    ds = torch.empty(C.attn_bwd_ds_elems(B, S, NQ, True), device="cuda", dtype=torch.bfloat16)
+    us = _time(lambda: C.attn_bwd(q, k, v, o, do, lse, delta, acc, dq, dk, dv, B, S, NQ, NKV, 1 / math.sqrt(D), True,
+                                  None, ds), warmup, iters)
+    flops = 2.5 * 4 * B * NQ * S * S * D / 2
+    return f"attention bwd (prep + main + dQ kernels) B={B} S={S} heads={NQ}/{NKV}: {us:.1f} us, {flops / us / 1e6:.0f} TF/s"
+
+
+def case_gemm(warmup, iters):
+    C = ext()
+    M, N, K = B * S, (NQ + 2 * NKV) * D, H  # the fused QKV projection
+    a = (torch.randn(M, K, device="cuda") * 0.05).to(torch.bfloat16)
+    b = (torch.randn(N, K, device="cuda") * 0.05).to(torch.bfloat16)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    us = _time(lambda: C.gemm(a, b, out, False, False, 0, 1.0), warmup, iters)
+    return f"gemm (CTA pair) {M}x{N}x{K}: {us:.1f} us, {2 * M * N * K / us / 1e6:.0f} TF/s"
+
+
+def case_rmsnorm_bwd(warmup, iters):
+    C = ext()
+    T = B * S
+    x, dy, dres = (torch.randn(T, H, device="cuda", dtype=torch.bfloat16) for _ in range(3))
+    w = torch.randn(H, device="cuda", dtype=torch.bfloat16)
+    rstd = torch.rand(T, device="cuda") + 0.5
+    dx, dw = torch.empty_like(x), torch.zeros(H, device="cuda")
+    us = _time(lambda: C.rmsnorm_bwd(dy, x, w, rstd, dx, dw, dres), warmup, iters)
+    return f"rmsnorm bwd (+ residual grad) {T}x{H}: {us:.1f} us, {4 * T * H * 2 / us / 1e3:.0f} GB/s"
+
+
+def case_qknorm(warmup, iters):
+    C = ext()
+    T = B * S
+    qkv = torch.randn(T, (NQ + 2 * NKV) * D, device="cuda", dtype=torch.bfloat16)
+    cos, sin = (torch.randn(S, D, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    qw, kw = (torch.randn(D, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    q = torch.empty(T, NQ * D, device="cuda", dtype=torch.bfloat16)
+    k = torch.empty(T, NKV * D, device="cuda", dtype=torch.bfloat16)
+    rstd = torch.empty(T * (NQ + NKV), device="cuda")
+    us = _time(lambda: C.qknorm_rope_fwd(qkv, qw, kw, cos, sin, q, k, rstd, S, NQ, NKV, 1e-6), warmup, iters)
+    return f"qk-norm + RoPE fwd {T} tokens x {NQ + NKV} heads: {us:.1f} us, {2 * T * (NQ + NKV) * D * 2 / us / 1e3:.0f} GB/s"
+
+
+CASES = {"attn_fwd": case_attn_fwd, "attn_bwd": case_attn_bwd, "gemm": case_gemm, "rmsnorm_bwd": case_rmsnorm_bwd,
+         "qknorm": case_qknorm}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("case", choices=sorted(CASES) + ["all"])
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args(argv)
+    torch.manual_seed(0)
+    for name in (sorted(CASES) if args.case == "all" else [args.case]):
+        print(CASES[name](args.warmup, args.iters), flush=True)
+
+
+if __name__ == "__main__":
+    main()
