@@ -136,6 +136,68 @@ int copy_grid(int64_t vecs) {
   return (int)std::max<int64_t>(1, std::min(g, cap));
 }
 
+// One warp per row: copy row_bytes from the local source row to the peer row.
+__global__ void row_scatter_kernel(const uint8_t* __restrict__ src, int64_t ld_src, const int64_t* __restrict__ src_row,
+                                   const int32_t* __restrict__ dst_rank, const int64_t* __restrict__ dst_row,
+                                   PeerBases peers, int64_t ld_dst, int64_t vecs, int64_t n) {
+  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= n) return;
+  const int r = dst_rank[i];
+  if (r < 0 || r >= kMaxPeers) return;
+  const uint4* s4 = reinterpret_cast<const uint4*>(src + src_row[i] * ld_src);
+  uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(peers.p[r]) + dst_row[i] * ld_dst);
+  for (int64_t v = lane; v < vecs; v += 32) d4[v] = s4[v];
+}
+
+// One warp per token: fp32 sum of its k_per routes' bf16 rows read from the owners.
+__global__ void row_gather_sum_kernel(__nv_bfloat16* __restrict__ dst, int64_t ld_dst, int64_t n_tokens, int k_per,
+                                      const int32_t* __restrict__ rank, const int64_t* __restrict__ row,
+                                      PeerBases peers, int64_t ld_src, int64_t vecs) {
+  const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= n_tokens) return;
+  for (int64_t v = lane; v < vecs; v += 32) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < k_per; ++k) {
+      const int r = rank[t * k_per + k];
+      if (r < 0 || r >= kMaxPeers) continue;
+      const uint4 u = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(peers.p[r]) +
+                                                     row[t * k_per + k] * ld_src)[v];
+      const uint32_t* w = &u.x;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = unpack_bf16x2(w[q]);
+        acc[2 * q] += f.x;
+        acc[2 * q + 1] += f.y;
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(dst + t * ld_dst)[v] = o;
+  }
+}
+
+// One warp per row: pull row_bytes from a peer row (zeros for rank < 0).
+__global__ void row_gather_kernel(uint8_t* __restrict__ dst, int64_t ld_dst, const int32_t* __restrict__ rank,
+                                  const int64_t* __restrict__ row, PeerBases peers, int64_t ld_src, int64_t vecs,
+                                  int64_t n) {
+  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= n) return;
+  const int r = rank[i];
+  uint4* d4 = reinterpret_cast<uint4*>(dst + i * ld_dst);
+  if (r < 0 || r >= kMaxPeers) {
+    for (int64_t v = lane; v < vecs; v += 32) d4[v] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint4* s4 = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(peers.p[r]) + row[i] * ld_src);
+  for (int64_t v = lane; v < vecs; v += 32) d4[v] = s4[v];
+}
+
 }  // namespace
 
 void signal_barrier(const uint64_t* peer_pads_dev, int rank, int world, int slot_base, uint32_t epoch,
@@ -159,6 +221,38 @@ void reduce_segments(const ReduceSegments& segs, int world, float scale, bool ac
 
 void wait_flag(const uint32_t* flag, uint32_t target, uint64_t limit_ns, int* status, cudaStream_t s) {
   wait_flag_kernel<<<1, 32, 0, s>>>(flag, target, limit_ns, status);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+void row_scatter(const void* src, int64_t ld_src_bytes, const int64_t* src_row, const int32_t* dst_rank,
+                 const int64_t* dst_row, const PeerBases& peers, int64_t ld_dst_bytes, int64_t row_bytes, int64_t n,
+                 cudaStream_t s) {
+  PB_CHECK(row_bytes % 16 == 0 && ld_src_bytes % 16 == 0 && ld_dst_bytes % 16 == 0, "row_scatter: 16-byte rows");
+  if (n == 0) return;
+  const int64_t threads = n * 32;
+  row_scatter_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+      reinterpret_cast<const uint8_t*>(src), ld_src_bytes, src_row, dst_rank, dst_row, peers, ld_dst_bytes,
+      row_bytes / 16, n);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+void row_gather_sum(void* dst, int64_t ld_dst, int64_t n_tokens, int k_per, const int32_t* rank, const int64_t* row,
+                    const PeerBases& peers, int64_t ld_src, int64_t cols, cudaStream_t s) {
+  PB_CHECK(cols % 8 == 0 && ld_dst % 8 == 0 && ld_src % 8 == 0, "row_gather_sum: 16-byte rows");
+  if (n_tokens == 0) return;
+  const int64_t threads = n_tokens * 32;
+  row_gather_sum_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+      reinterpret_cast<__nv_bfloat16*>(dst), ld_dst, n_tokens, k_per, rank, row, peers, ld_src, cols / 8);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+void row_gather(void* dst, int64_t ld_dst_bytes, const int32_t* rank, const int64_t* row, const PeerBases& peers,
+                int64_t ld_src_bytes, int64_t row_bytes, int64_t n, cudaStream_t s) {
+  PB_CHECK(row_bytes % 16 == 0 && ld_src_bytes % 16 == 0 && ld_dst_bytes % 16 == 0, "row_gather: 16-byte rows");
+  if (n == 0) return;
+  const int64_t threads = n * 32;
+  row_gather_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(reinterpret_cast<uint8_t*>(dst), ld_dst_bytes, rank,
+                                                                      row, peers, ld_src_bytes, row_bytes / 16, n);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -31,4 +31,21 @@ void multi_copy(const CopySegments& segs, cudaStream_t s);
 void reduce_segments(const ReduceSegments& segs, int world, float scale, bool accumulate, cudaStream_t s);
 void wait_flag(const uint32_t* flag, uint32_t target, uint64_t limit_ns, int* status, cudaStream_t s);
 
+// Expert-parallel row exchange over peer memory (one warp per row, 16-byte
+// vectors; row_bytes and all strides multiples of 16 bytes).
+//   row_scatter:    peer[dst_rank[i]] + dst_row[i]*ld_dst  <-  src + src_row[i]*ld_src   (i < n)
+//   row_gather_sum: dst[t] = sum_k peer[rank[t*k_per+k]] + row[t*k_per+k]*ld_src  (bf16 rows,
+//                   fp32 sums; rank < 0 skips the route)
+struct PeerBases {
+  void* p[kMaxPeers];
+};
+void row_scatter(const void* src, int64_t ld_src_bytes, const int64_t* src_row, const int32_t* dst_rank,
+                 const int64_t* dst_row, const PeerBases& peers, int64_t ld_dst_bytes, int64_t row_bytes, int64_t n,
+                 cudaStream_t s);
+void row_gather_sum(void* dst, int64_t ld_dst, int64_t n_tokens, int k_per, const int32_t* rank, const int64_t* row,
+                    const PeerBases& peers, int64_t ld_src, int64_t cols, cudaStream_t s);
+//   row_gather:     dst + i*ld_dst  <-  peer[rank[i]] + row[i]*ld_src   (row_bytes; rank < 0 writes zeros)
+void row_gather(void* dst, int64_t ld_dst_bytes, const int32_t* rank, const int64_t* row, const PeerBases& peers,
+                int64_t ld_src_bytes, int64_t row_bytes, int64_t n, cudaStream_t s);
+
 }  // namespace pb

@@ -91,10 +91,67 @@ void error_word_copy_async(at::Tensor& pinned) {
 
 }  // namespace
 
+pb::PeerBases peer_bases(const std::vector<int64_t>& ptrs) {
+  TORCH_CHECK(ptrs.size() >= 1 && ptrs.size() <= (size_t)pb::kMaxPeers, "1..8 peer pointers");
+  pb::PeerBases b{};
+  for (size_t i = 0; i < ptrs.size(); ++i) b.p[i] = reinterpret_cast<void*>(ptrs[i]);
+  return b;
+}
+
+// row_scatter(src [rows, cols] any dtype, src_row int64 [n], dst_rank int32 [n], dst_row int64 [n],
+//             peer_ptrs, ld_dst_bytes): src rows -> rows of the peers' buffers.
+void row_scatter(const at::Tensor& src, const at::Tensor& src_row, const at::Tensor& dst_rank,
+                 const at::Tensor& dst_row, const std::vector<int64_t>& peer_ptrs, int64_t ld_dst_bytes) {
+  TORCH_CHECK(src.is_cuda() && src.dim() == 2 && src.stride(1) == 1, "row_scatter: src 2-D CUDA, unit inner stride");
+  TORCH_CHECK(src_row.scalar_type() == at::kLong && dst_row.scalar_type() == at::kLong &&
+                  dst_rank.scalar_type() == at::kInt && src_row.is_contiguous() && dst_row.is_contiguous() &&
+                  dst_rank.is_contiguous(),
+              "row_scatter: index dtypes");
+  const int64_t n = src_row.numel();
+  TORCH_CHECK(dst_rank.numel() == n && dst_row.numel() == n, "row_scatter: index lengths");
+  const c10::cuda::CUDAGuard g(src.device());
+  pb::row_scatter(src.data_ptr(), src.stride(0) * src.element_size(), src_row.data_ptr<int64_t>(),
+                  dst_rank.data_ptr<int32_t>(), dst_row.data_ptr<int64_t>(), peer_bases(peer_ptrs), ld_dst_bytes,
+                  src.size(1) * src.element_size(), n, at::cuda::getCurrentCUDAStream().stream());
+}
+
+// row_gather_sum(dst bf16 [tokens, cols], rank int32 [tokens*k], row int64 [tokens*k], peer_ptrs, ld_src):
+// dst[t] = sum_k peer[rank][row] (rank < 0 skips).
+void row_gather_sum(at::Tensor& dst, const at::Tensor& rank, const at::Tensor& row,
+                    const std::vector<int64_t>& peer_ptrs, int64_t ld_src) {
+  TORCH_CHECK(dst.is_cuda() && dst.scalar_type() == at::kBFloat16 && dst.dim() == 2 && dst.stride(1) == 1,
+              "row_gather_sum: dst 2-D bf16");
+  TORCH_CHECK(rank.scalar_type() == at::kInt && row.scalar_type() == at::kLong && rank.is_contiguous() &&
+                  row.is_contiguous() && rank.numel() == row.numel(),
+              "row_gather_sum: index tensors");
+  const int64_t n_tokens = dst.size(0);
+  TORCH_CHECK(n_tokens == 0 || rank.numel() % n_tokens == 0, "row_gather_sum: routes per token");
+  const int k_per = n_tokens ? (int)(rank.numel() / n_tokens) : 0;
+  const c10::cuda::CUDAGuard g(dst.device());
+  pb::row_gather_sum(dst.data_ptr(), dst.stride(0), n_tokens, k_per, rank.data_ptr<int32_t>(), row.data_ptr<int64_t>(),
+                     peer_bases(peer_ptrs), ld_src, dst.size(1), at::cuda::getCurrentCUDAStream().stream());
+}
+
+// row_gather(dst [n, cols] (16-byte rows), rank int32 [n], row int64 [n], peer_ptrs, ld_src_bytes)
+void row_gather(at::Tensor& dst, const at::Tensor& rank, const at::Tensor& row, const std::vector<int64_t>& peer_ptrs,
+                int64_t ld_src_bytes) {
+  TORCH_CHECK(dst.is_cuda() && dst.dim() == 2 && dst.stride(1) == 1, "row_gather: dst 2-D CUDA");
+  TORCH_CHECK(rank.scalar_type() == at::kInt && row.scalar_type() == at::kLong && rank.is_contiguous() &&
+                  row.is_contiguous() && rank.numel() == dst.size(0) && row.numel() == dst.size(0),
+              "row_gather: index tensors");
+  const c10::cuda::CUDAGuard g(dst.device());
+  pb::row_gather(dst.data_ptr(), dst.stride(0) * dst.element_size(), rank.data_ptr<int32_t>(), row.data_ptr<int64_t>(),
+                 peer_bases(peer_ptrs), ld_src_bytes, dst.size(1) * dst.element_size(), dst.size(0),
+                 at::cuda::getCurrentCUDAStream().stream());
+}
+
 void register_comm(pybind11::module& m) {
   m.def("p2p_barrier", &p2p_barrier);
   m.def("p2p_copy", &p2p_copy);
   m.def("p2p_reduce", &p2p_reduce);
   m.def("wait_flag", &wait_flag);
+  m.def("row_scatter", &row_scatter);
+  m.def("row_gather_sum", &row_gather_sum);
+  m.def("row_gather", &row_gather);
   m.def("error_word_copy_async", &error_word_copy_async);
 }

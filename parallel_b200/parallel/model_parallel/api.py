@@ -71,9 +71,11 @@ class ModelParallelWrapper:
             self.experts = ExpertPartition(model.config.num_experts, self.plan.expert_parallel_size,
                                            self.mesh.get_local_rank())
             verify_expert_modules(model, self.experts)
-            rt = (SequenceParallelExpertParallel if self.plan.capabilities.sequence_parallel
-                  else ReplicatedTokenExpertParallel)
-            self.expert_runtime = rt(self.experts, self.group)
+            if self.plan.capabilities.sequence_parallel:
+                self.expert_runtime = SequenceParallelExpertParallel(self.experts, self.group, device=device,
+                                                                     collectives=self.collectives)
+            else:
+                self.expert_runtime = ReplicatedTokenExpertParallel(self.experts, self.group)
             self.expert_runtime.apply(model)
         self.checkpoint = ModelParallelCheckpoint(model, pconfig, self.plan, self.mesh, device)
 

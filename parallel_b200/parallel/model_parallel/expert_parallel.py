@@ -136,10 +136,16 @@ class ReplicatedTokenExpertParallel:
 
 
 class SequenceParallelExpertParallel:
-    def __init__(self, partition: ExpertPartition, group):
+    def __init__(self, partition: ExpertPartition, group, device=None, collectives: str = "auto"):
         self.partition = partition
         self.group = group
-        self.dispatcher = TokenDispatcher(partition, group)
+        # NVLink peer-memory dispatch / combine on CUDA (<= 8 ranks), NCCL / gloo otherwise
+        from .p2p_dispatch import P2PTokenDispatcher
+
+        if device is not None and collectives != "nccl" and P2PTokenDispatcher.available(group, device):
+            self.dispatcher = P2PTokenDispatcher(partition, group, device)
+        else:
+            self.dispatcher = TokenDispatcher(partition, group)
         self._model = None
 
     def __call__(self, experts, x2, global_index, weights):

@@ -43,7 +43,7 @@ def run_engine(collectives, data, layers=2):
     return losses, state, eng.fsdp_wrapper.coll.name
 
 
-def run_sp(collectives, data, steps_grads):
+def run_sp(collectives, data, steps_grads, moe=False):
     """Qwen3 (head_dim 128) with tp = sp = world: the fused NVLink sequence-parallel
     kernels (collectives != nccl) against the NCCL path.  Returns losses and
     the local gradient shards after one backward."""
@@ -58,19 +58,27 @@ def run_sp(collectives, data, steps_grads):
     world = dist.get_world_size()
     path = os.path.join(os.environ.get("PB_TEST_TMP", "/tmp"), "sp_ckpt")
     if dist.get_rank() == 0:
-        mcfg = resolve_config("small-qwen3", num_hidden_layers=2, vocab_size=2048, hidden_size=512,
-                              intermediate_size=1024)
+        if moe:
+            mcfg = resolve_config("small-qwen3-moe", num_hidden_layers=2, vocab_size=2048)
+        else:
+            mcfg = resolve_config("small-qwen3", num_hidden_layers=2, vocab_size=2048, hidden_size=512,
+                                  intermediate_size=1024)
         save_pretrained(build_model(mcfg, dtype=torch.bfloat16, seed=0), path)
     dist.barrier()
+    par = [f"parallel.tp={world}", f"parallel.sp={world}"] + ([f"parallel.ep={world}"] if moe else [])
     cfg = merge(load_cfg(argv=[]), from_dotlist([
-        "config.device_type=cuda", "model.learning_rate=1e-3", f"model.name={path}", f"parallel.tp={world}",
-        f"parallel.sp={world}", "engine.activation_checkpoint=false", f"engine.collectives={collectives}"]))
+        "config.device_type=cuda", "model.learning_rate=1e-3", f"model.name={path}",
+        "engine.activation_checkpoint=false", f"engine.collectives={collectives}"] + par))
     pc = ParallelConfig(cfg)
     pc.set_device_mesh("cuda")
     m, plan = load_causal_lm(cfg, pc, dtype=torch.bfloat16)
     m.to(pc.device)
     eng = ParallelEngine(m, None, pc, cfg, pc.device, mp_plan=plan)
-    fused = eng.model.model.layers[0]._ctx.fused_sp is not None
+    ctx0 = eng.model.model.layers[0]._ctx
+    if moe:
+        fused = type(ctx0.expert_runtime.dispatcher).__name__ == "P2PTokenDispatcher"
+    else:
+        fused = ctx0.fused_sp is not None
     losses, grads = [], {}
     for i, tok in enumerate(data):
         tok = tok.cuda()
@@ -96,8 +104,9 @@ def main_sp():
     world = dist.get_world_size()
     g = torch.Generator().manual_seed(0)
     data = [torch.randint(0, 2048, (2, 256 * world + 1), generator=g) for _ in range(3)]
-    l_f, g_f, fused = run_sp("p2p", data, 1)
-    l_n, g_n, fused_n = run_sp("nccl", data, 1)
+    moe = os.environ.get("PB_TEST_MOE") == "1"
+    l_f, g_f, fused = run_sp("p2p", data, 1, moe)
+    l_n, g_n, fused_n = run_sp("nccl", data, 1, moe)
     worst = 0.0
     for k in g_n:
         a, b = g_f[k], g_n[k]

@@ -56,3 +56,20 @@ def test_fused_sequence_parallel_matches_nccl(tmp_path):
     for a, b in zip(res["fused"], res["nccl"]):
         assert abs(a - b) < 2e-2 * max(1.0, abs(b)), res
     assert res["grad_rel_diff"] < 3e-2, res
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_p2p_expert_dispatch_matches_nccl(tmp_path):
+    """Qwen3-MoE with tp = sp = ep = 2: token dispatch / combine over NVLink peer
+    memory give the same losses and gradients as the NCCL all-to-all path."""
+    out = tmp_path / "res_moe.json"
+    env = dict(os.environ, PB_TEST_OUT=str(out), PB_TEST_MODE="sp", PB_TEST_MOE="1", PB_TEST_TMP=str(tmp_path),
+               NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+           "--master-port", "29535", os.path.join(HERE, "multigpu_worker.py")]
+    subprocess.run(cmd, env=env, check=True, timeout=600)
+    res = json.loads(out.read_text())
+    assert res["used_fused"] == [True, False], res
+    for a, b in zip(res["fused"], res["nccl"]):
+        assert abs(a - b) < 2e-2 * max(1.0, abs(b)), res
+    assert res["grad_rel_diff"] < 5e-2, res
