@@ -169,6 +169,70 @@ void gemm_rs(const at::Tensor& a, const at::Tensor& b, bool b_mn, double alpha, 
   pb::gemm_bf16(p, cur_stream());
 }
 
+// gemm_grouped(mode, a, b, out, work int32 [n, 4], krange int32 [E, 2] or None, E, b_mn, epi, alpha,
+//              r=None, b_up_offset=0, n_out=0)
+//   mode 1: a [M_pad, K], b [E, b_rows, K] (or [E, K, N] with b_mn), out [M_pad, N]
+//   mode 2: a [rows, M_group], b [rows, N], out [E, M_group, N]
+void gemm_grouped(int64_t mode, const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const at::Tensor& work,
+                  const c10::optional<at::Tensor>& krange, bool b_mn, int64_t epi, double alpha,
+                  const c10::optional<at::Tensor>& r, int64_t b_up_offset, int64_t n_out) {
+  CHECK_CUDA_BF16(a);
+  CHECK_CUDA_BF16(b);
+  TORCH_CHECK(a.is_contiguous() && b.is_contiguous() && out.is_contiguous(), "gemm_grouped: contiguous operands");
+  TORCH_CHECK(work.is_cuda() && work.scalar_type() == at::kInt && work.dim() == 2 && work.size(1) == 4 &&
+                  work.is_contiguous(),
+              "gemm_grouped: work must be int32 [n, 4]");
+  const c10::cuda::CUDAGuard guard(a.device());
+  pb::GroupedGemmParams p;
+  p.mode = (int)mode;
+  p.A = a.data_ptr();
+  p.B = b.data_ptr();
+  p.C = out.data_ptr();
+  p.b_mn = b_mn;
+  p.epi = (int)epi;
+  p.alpha = (float)alpha;
+  p.b_up_offset = b_up_offset;
+  p.work = reinterpret_cast<const int4*>(work.data_ptr<int>());
+  p.n_work = (int)work.size(0);
+  if (mode == 1) {
+    TORCH_CHECK(a.dim() == 2 && b.dim() == 3 && out.dim() == 2, "gemm_grouped rows: a 2-D, b 3-D, out 2-D");
+    p.E = (int)b.size(0);
+    p.M_total = (int)a.size(0);
+    p.K = (int)a.size(1);
+    p.lda = a.stride(0);
+    p.ldb = b.stride(1);
+    p.b_rows = b_mn ? b.size(1) : b.size(1);
+    p.N = epi == pb::kEpiSwiGLU ? (int)n_out : (int)(b_mn ? b.size(2) : b.size(1));
+    TORCH_CHECK((b_mn ? b.size(1) : b.size(2)) == p.K, "gemm_grouped rows: K mismatch");
+    TORCH_CHECK(out.size(0) == p.M_total && out.size(1) == p.N, "gemm_grouped rows: out shape");
+  } else {
+    TORCH_CHECK(mode == 2 && krange.has_value() && krange->defined(), "gemm_grouped: mode 2 needs krange");
+    TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 3 && a.size(0) == b.size(0), "gemm_grouped k: shapes");
+    TORCH_CHECK(krange->is_cuda() && krange->scalar_type() == at::kInt && krange->is_contiguous() &&
+                    krange->numel() == 2 * out.size(0),
+                "gemm_grouped k: krange int32 [E, 2]");
+    p.E = (int)out.size(0);
+    p.M_group = (int)out.size(1);
+    p.N = (int)out.size(2);
+    p.rows = (int)a.size(0);
+    p.K = (int)a.size(0);
+    p.M_total = p.E * p.M_group;
+    p.lda = a.stride(0);
+    p.ldb = b.stride(0);
+    TORCH_CHECK(a.size(1) == p.M_group && b.size(1) == p.N, "gemm_grouped k: operand widths");
+    p.krange = reinterpret_cast<const int2*>(krange->data_ptr<int>());
+  }
+  const bool f32 = epi == pb::kEpiStoreF32 || epi == pb::kEpiAccumF32;
+  TORCH_CHECK(out.scalar_type() == (f32 ? at::kFloat : at::kBFloat16), "gemm_grouped: output dtype");
+  p.ldc = mode == 1 ? out.stride(0) : out.stride(1);
+  if (r.has_value() && r->defined()) {
+    CHECK_CUDA_BF16(*r);
+    p.R = r->data_ptr();
+    p.ldr = r->stride(0);
+  }
+  pb::gemm_grouped(p, cur_stream());
+}
+
 int64_t read_error(int64_t device) { return pb::read_error((int)device); }
 void clear_error(int64_t device) { pb::clear_error((int)device); }
 
@@ -194,6 +258,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("b_mn"), pybind11::arg("alpha"),
         pybind11::arg("peer_ptrs"), pybind11::arg("ldc"), pybind11::arg("seq"), pybind11::arg("seq_local"),
         pybind11::arg("slot"), pybind11::arg("slot_rows"));
+  m.def("gemm_grouped", &gemm_grouped, "grouped (mixture-of-experts) GEMM driven by a device work table",
+        pybind11::arg("mode"), pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("out"), pybind11::arg("work"),
+        pybind11::arg("krange"), pybind11::arg("b_mn"), pybind11::arg("epi"), pybind11::arg("alpha"),
+        pybind11::arg("r") = pybind11::none(), pybind11::arg("b_up_offset") = 0, pybind11::arg("n_out") = 0);
   m.def("read_error", &read_error);
   m.def("clear_error", &clear_error);
   register_ops(m);

@@ -71,6 +71,33 @@ struct GemmParams {
   const GatherArgs* gather = nullptr;    // A assembled from sequence-parallel shards in-kernel
 };
 
+// Grouped (mixture-of-experts) products, gemm_grouped.cu.  work: int4 per
+// tile {expert, M tile, N tile, 0}; rows of one expert start at a 128-row
+// aligned offset of A / C and are separated by zero rows.
+//   mode 1 (rows): C[M_total, N] = A[M_total, K] x B_e, B stacked [E][b_rows][K]
+//     (K-major) or [E][K][N] (b_mn); SwiGLU takes gate rows [0, N) and up rows
+//     [b_up_offset, b_up_offset + N) of B_e.
+//   mode 2 (k): C[E][M_group][N] = A_e^T B_e over rows krange[e] of
+//     A [rows, M_group] and B [rows, N].
+struct GroupedGemmParams {
+  int mode = 1;
+  const void* A = nullptr;
+  const void* B = nullptr;
+  void* C = nullptr;
+  const void* R = nullptr;
+  int64_t lda = 0, ldb = 0, ldc = 0, ldr = 0;
+  int E = 0, M_total = 0, M_group = 0, rows = 0, N = 0, K = 0;
+  int64_t b_rows = 0;
+  bool b_mn = false;
+  int epi = kEpiStoreBf16;
+  float alpha = 1.f;
+  int64_t b_up_offset = 0;
+  const int4* work = nullptr;
+  int n_work = 0;
+  const int2* krange = nullptr;
+};
+void gemm_grouped(const GroupedGemmParams& p, cudaStream_t stream);
+
 // Dispatches to the one-CTA (gemm.cu) or the CTA-pair (gemm_pair.cu) kernel.
 void gemm_bf16(const GemmParams& p, cudaStream_t stream);
 void gemm_bf16_pair(const GemmParams& p, cudaStream_t stream);

@@ -16,8 +16,8 @@ replicated-token expert parallelism uses for experts owned by other ranks,
 parallel/parallel/engine/model_parallel/expert_parallel.py:50-60) are
 skipped explicitly.
 
-On CUDA the expert MLPs run the tcgen05 SwiGLU GEMM per expert on rows
-sorted by expert; on CPU the plain PyTorch loop runs.
+On CUDA the expert MLPs run as grouped tcgen05 GEMMs (csrc/gemm_grouped.cu,
+one launch per product for all experts); on CPU the plain PyTorch loop runs.
 """
 from __future__ import annotations
 
@@ -45,60 +45,94 @@ def _gemm_ok(x2, w) -> bool:
             and w.is_contiguous() and x2.shape[0] > 0)
 
 
+def _padded_layout(counts: list, device):
+    """Rows of expert e at a 128-aligned offset: (offsets list, padded total, index of each sorted row)."""
+    offs, o = [], 0
+    for n in counts:
+        offs.append(o)
+        o += -(-n // 128) * 128
+    pos = torch.cat([torch.arange(n, device=device) + off for n, off in zip(counts, offs) if n > 0]) \
+        if any(counts) else torch.zeros(0, dtype=torch.int64, device=device)
+    return offs, max(o, 128), pos
+
+
+def _rows_work(counts, offs, n_tiles: int, device) -> torch.Tensor:
+    """Grouped-GEMM rows-mode work table {expert, M tile, N tile, 0}."""
+    items = [(e, off // 128 + t, tn, 0) for e, (n, off) in enumerate(zip(counts, offs)) if n > 0
+             for t in range(-(-n // 128)) for tn in range(n_tiles)]
+    return torch.tensor(items or [(0, 0, 0, 0)], dtype=torch.int32, device=device)[: len(items)]
+
+
+def _k_work(counts, m_group: int, n: int, device):
+    """Grouped-GEMM k-mode work table and per-expert row ranges (64-row multiples)."""
+    items = [(e, tm, tn, 0) for e, c in enumerate(counts) if c > 0
+             for tm in range(-(-m_group // 128)) for tn in range(-(-n // 128))]
+    return torch.tensor(items or [(0, 0, 0, 0)], dtype=torch.int32, device=device)[: len(items)]
+
+
 class _ExpertsFn(torch.autograd.Function):
-    """Expert SwiGLU MLPs over expert-sorted rows.
+    """Expert SwiGLU MLPs over expert-sorted rows, as grouped tcgen05 GEMMs.
 
     xs: [N, H] rows sorted by expert; counts: python list of rows per expert;
     scores: [N] routing weights (fp32); w_gu [E, 2I, H]; w_d [E, H, I].
-    Returns ys [N, H] = score * down(silu(g) * u).
+    Returns ys [N, H] = score * down(silu(g) * u).  Rows are laid out per
+    expert at 128-row aligned offsets with zero rows in between (one launch
+    per product: gate/up + SwiGLU, down; backward: down input-grad, down
+    weight-grad, SwiGLU backward, gate/up input-grad, gate/up weight-grad).
     """
 
     @staticmethod
     def forward(ctx, xs, scores, w_gu, w_d, counts):
         N, H = xs.shape
-        I = w_d.shape[2]
-        ys = torch.empty_like(xs)
-        y_raw = torch.empty_like(xs)
-        gu_all = torch.empty(N, 2 * I, device=xs.device, dtype=xs.dtype)
-        h_all = torch.empty(N, I, device=xs.device, dtype=xs.dtype)
-        r = 0
-        for e, n in enumerate(counts):
-            if n == 0:
-                continue
-            xe = xs[r:r + n]
-            ext().gemm(xe, w_gu[e], h_all[r:r + n], False, False, G.EPI_SWIGLU, 1.0, gu_all[r:r + n], I, I)
-            ext().gemm(h_all[r:r + n], w_d[e], y_raw[r:r + n], False, False, G.EPI_STORE_BF16, 1.0)
-            r += n
-        ys.copy_(y_raw * scores[:, None].to(y_raw.dtype))
-        ctx.save_for_backward(xs, scores, w_gu, w_d, gu_all, h_all, y_raw)
-        ctx.counts = counts
+        E, I = w_d.shape[0], w_d.shape[2]
+        offs, n_pad, pos = _padded_layout(counts, xs.device)
+        x_pad = torch.zeros(n_pad, H, device=xs.device, dtype=xs.dtype)
+        x_pad[pos] = xs
+        gu_pad = torch.empty(n_pad, 2 * I, device=xs.device, dtype=xs.dtype)
+        h_pad = torch.empty(n_pad, I, device=xs.device, dtype=xs.dtype)
+        w_gu = w_gu.contiguous()
+        w_d = w_d.contiguous()
+        C = ext()
+        C.gemm_grouped(1, x_pad, w_gu, h_pad, _rows_work(counts, offs, -(-I // 128), xs.device), None, False,
+                       G.EPI_SWIGLU, 1.0, gu_pad, I, I)
+        y_pad = torch.empty(n_pad, H, device=xs.device, dtype=xs.dtype)
+        C.gemm_grouped(1, h_pad, w_d, y_pad, _rows_work(counts, offs, -(-H // 128), xs.device), None, False,
+                       G.EPI_STORE_BF16, 1.0)
+        y_raw = y_pad[pos]
+        ys = y_raw * scores[:, None].to(y_raw.dtype)
+        ctx.save_for_backward(x_pad, scores, w_gu, w_d, gu_pad, h_pad, y_raw, pos)
+        ctx.counts, ctx.offs = counts, offs
         return ys
 
     @staticmethod
     def backward(ctx, dys):
-        xs, scores, w_gu, w_d, gu_all, h_all, y_raw = ctx.saved_tensors
-        counts = ctx.counts
-        I = w_d.shape[2]
+        x_pad, scores, w_gu, w_d, gu_pad, h_pad, y_raw, pos = ctx.saved_tensors
+        counts, offs = ctx.counts, ctx.offs
+        E, H, I = w_d.shape
+        n_pad = x_pad.shape[0]
+        dev = x_pad.device
         dys = dys.contiguous()
         dscores = (dys.float() * y_raw.float()).sum(-1)
-        dy_s = (dys * scores[:, None].to(dys.dtype)).contiguous()
-        dxs = torch.zeros_like(xs)
-        dw_gu = torch.zeros_like(w_gu)
+        dy_pad = torch.zeros(n_pad, H, device=dev, dtype=dys.dtype)
+        dy_pad[pos] = dys * scores[:, None].to(dys.dtype)
+        krange = torch.tensor([[off, off + -(-n // 64) * 64] for n, off in zip(counts, offs)], dtype=torch.int32,
+                              device=dev)
+        C = ext()
+        # down projection: dh = dy W_d (rows), dW_d[e] = dy_e^T h_e (k)
+        dh_pad = torch.empty(n_pad, I, device=dev, dtype=dys.dtype)
+        C.gemm_grouped(1, dy_pad, w_d, dh_pad, _rows_work(counts, offs, -(-I // 128), dev), None, True,
+                       G.EPI_STORE_BF16, 1.0)
         dw_d = torch.zeros_like(w_d)
-        dh = torch.empty(xs.shape[0], I, device=xs.device, dtype=xs.dtype)
-        dgu = torch.empty_like(gu_all)
-        r = 0
-        for e, n in enumerate(counts):
-            if n == 0:
-                continue
-            sl = slice(r, r + n)
-            G.linear_dgrad(dy_s[sl], w_d[e], out=dh[sl])
-            G.linear_wgrad(dy_s[sl], h_all[sl], out=dw_d[e])
-            ext().swiglu_bwd(dh[sl], gu_all[sl], dgu[sl])
-            G.linear_dgrad(dgu[sl], w_gu[e], out=dxs[sl])
-            G.linear_wgrad(dgu[sl], xs[sl], out=dw_gu[e])
-            r += n
-        return dxs, dscores.to(scores.dtype), dw_gu, dw_d, None
+        C.gemm_grouped(2, dy_pad, h_pad, dw_d, _k_work(counts, H, I, dev), krange, True, G.EPI_STORE_BF16, 1.0)
+        dgu = torch.empty_like(gu_pad)
+        C.swiglu_bwd(dh_pad, gu_pad, dgu)
+        # gate/up projection: dx = dgu W_gu (rows), dW_gu[e] = dgu_e^T x_e (k)
+        dx_pad = torch.empty(n_pad, H, device=dev, dtype=dys.dtype)
+        C.gemm_grouped(1, dgu, w_gu, dx_pad, _rows_work(counts, offs, -(-H // 128), dev), None, True,
+                       G.EPI_STORE_BF16, 1.0)
+        dw_gu = torch.zeros_like(w_gu)
+        C.gemm_grouped(2, dgu, x_pad, dw_gu, _k_work(counts, 2 * I, H, dev), krange, True, G.EPI_STORE_BF16, 1.0)
+        return dx_pad[pos], dscores.to(scores.dtype), dw_gu, dw_d, None
 
 
 def experts_forward(x2: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: torch.Tensor,
