@@ -126,9 +126,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* dq_empty = bars + 15;
   uint64_t* kv_done = bars + 16;
   uint64_t* drain = bars + 17;
-  uint64_t* p_free = bars + 18;  // DS_STORE: P has its own buffer (the dQ staging area)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
-  uint8_t* sP = DS_STORE ? sStage : sPdS;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wg = warp >> 2;
@@ -156,7 +154,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(dv_done, 1);
     mbar_init(ds_full, kElem);
     mbar_init(pds_free, DS_STORE ? 2 : 1);  // dK product done (+ dS tile stored)
-    mbar_init(p_free, 1);                   // DS_STORE: dV product done with P
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 128);
     mbar_init(kv_done, 1);
@@ -208,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t id_km = idesc_bf16(128, 128, false, true);   // A K-major, B MN-major
       constexpr uint32_t id_mm = idesc_bf16(128, 128, true, true);    // both MN-major
       const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV), pds_base = smem_u32(sPdS);
-      const uint32_t do_base = smem_u32(sdO), p_base = smem_u32(sP);
+      const uint32_t do_base = smem_u32(sdO);
       // S^T(it) = K Q_it^T into TMEM cols [0,128); slot 0 = waits for Q / S free
       auto issue_s = [&](int it) -> bool {
         const int st = it & 1;
@@ -240,19 +237,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                       id_kk, kk > 0);
         }
         mma_commit(dp_full);
-        // S^T(it+1) as soon as the element warps hold S^T(it) in registers
-        if (it + 1 < n_iter && !issue_s(it + 1)) { ok = false; break; }
-        if (!tw(2, p_full, ph)) { ok = false; break; }  // slot 2: P written
+        if (!tw(2, p_full, ph)) { ok = false; break; }  // slot 2: P written into TMEM
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // dV += P^T dO   (K = queries)
-          const uint32_t aoff = (kk >> 2) * (TILE / 2) + (kk & 3) * 32;
-          mma_bf16_ss(tdV, smem_desc_sw128(p_base + aoff, 16, 1024),
-                      smem_desc_sw128(do_base + kk * 2048, TILE / 2, 1024), id_km, (it > 0 || kk > 0));
+        for (int kk = 0; kk < 8; ++kk) {  // dV += P^T dO   (K = queries; P^T read from TMEM)
+          // element warpgroup g stored queries [64g, 64g+64) as 32 packed columns at 64g
+          const uint32_t a_col = (kk >> 2) * 64 + (kk & 3) * 8;
+          mma_bf16_ts(tdV, tS + a_col, smem_desc_sw128(do_base + kk * 2048, TILE / 2, 1024), id_km,
+                      (it > 0 || kk > 0));
         }
         mma_commit(dv_done);
         mma_commit(do_empty);
-        if (DS_STORE) mma_commit(p_free);
+        // S^T(it+1) overwrites P^T(it): issued after dV(it) (MMAs run in order)
+        if (it + 1 < n_iter && !issue_s(it + 1)) { ok = false; break; }
         if (!tw(3, ds_full, ph)) { ok = false; break; }  // slot 3: dS written
         tc_fence_after();
         if constexpr (!DS_STORE) {
@@ -292,7 +289,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const float scale_log2 = scale * kLog2e;
     uint8_t* pds_row = sPdS + g * (TILE / 2) + r * 128;  // this thread's row in atom g (dS)
-    uint8_t* p_row = sP + g * (TILE / 2) + r * 128;      // (P; the same buffer unless DS_STORE)
     bool ok = true;
     const long long t_loop0 = clock64();
     long long tm = 0;
@@ -332,20 +328,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           p[c] = ((causal && kpos > q) || kpos >= S || q >= S) ? 0.f : x;
         }
       }
-      // P^T -> smem (row = key; this warpgroup's 64 queries form swizzled atom g).
-      // The packed bf16 copy is also what dS uses below (the same rounding dV sees).
+      // P^T packed to bf16 pairs (row = key, this warpgroup's 64 queries); the
+      // packed copy is also what dS uses below (the same rounding dV sees).
       uint32_t pb[32];
 #pragma unroll
       for (int e = 0; e < 32; ++e) pb[e] = pack_bf16x2(p[2 * e], p[2 * e + 1]);
       if (kTrace) tacc[7] += clock64() - tm;  // slot 7: S -> P
-      // slot 8: the P buffer is free (dV(it-1) read it; without DS_STORE also dK / dQ)
-      if (!tw(8, DS_STORE ? p_free : pds_free, ph ^ 1)) { ok = false; break; }
       if (kTrace) tm = clock64();
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch)
-        *reinterpret_cast<uint4*>(p_row + ((ch ^ (r & 7)) << 4)) =
-            make_uint4(pb[4 * ch], pb[4 * ch + 1], pb[4 * ch + 2], pb[4 * ch + 3]);
-      fence_proxy_async_smem();
+      // P^T (packed bf16 pairs) over the first 32 of this warpgroup's own S^T
+      // columns, which this thread has already read: the dV product's A operand
+      tmem_st32(tS + lane_off + cg, reinterpret_cast<const float*>(pb));
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(p_full);
       if (kTrace) tacc[9] += clock64() - tm;  // slot 9: P write
@@ -369,9 +362,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       if (kTrace) tacc[11] += clock64() - tm;  // slot 11: dS compute
-      // slot 12: dS overwrites P unless DS_STORE, so the dV product must have read
-      // it; with DS_STORE the dS buffer must be free (dK(it-1) done, dS(it-1) stored)
-      if (!tw(12, DS_STORE ? pds_free : dv_done, DS_STORE ? (ph ^ 1) : ph)) { ok = false; break; }
+      // slot 12: the dS buffer is free (dQ / dK of the previous tile read it and,
+      // with DS_STORE, it has been stored)
+      if (!tw(12, pds_free, ph ^ 1)) { ok = false; break; }
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch)
         *reinterpret_cast<uint4*>(pds_row + ((ch ^ (r & 7)) << 4)) =
