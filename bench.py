@@ -45,6 +45,7 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalidates the metric)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--collectives", default="auto")
+    ap.add_argument("--no-graph", action="store_true", help="eager steps instead of the captured CUDA-graph step")
     return ap.parse_args()
 
 
@@ -236,16 +237,18 @@ def run_ours(args, rank, world, local):
     dev = [h.to(device) for h in host]
 
     def step(tok):
-        x, y = tok[:, :-1], tok[:, 1:]
-        loss = engine.forward(x, y).loss
-        engine.backward(loss)
-        engine.step()
-        return loss
+        # the public whole-step API: forward + backward + optimizer (a CUDA-graph
+        # replay once captured)
+        return engine.train_step(tok[:, :-1], tok[:, 1:])
 
     clocks = ClockSampler(local, int(os.environ.get("LOCAL_WORLD_SIZE", world)))
     clocks.start()
     for i in range(args.warmup):
         step(dev[i % nb])
+    use_graph = not args.no_graph and os.environ.get("PB_GRAPH", "1") != "0"
+    if use_graph:
+        # one more eager step on the capture stream, then the capture (untimed)
+        engine.capture_train_step(dev[0][:, :-1], dev[0][:, 1:], warmup=1)
     torch.cuda.synchronize()
     check_device_errors()
     t_wall0 = time.time()
@@ -275,11 +278,15 @@ def run_ours(args, rank, world, local):
         e2e_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
         e2e = {"value": B * S * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": host[0].numel() * host[0].element_size(),
-               "d2h_bytes_per_step": 4, "api": "ParallelEngine.forward/backward/step + loss.item()",
+               "d2h_bytes_per_step": 4, "api": "ParallelEngine.train_step + loss.item()",
                "last_loss": losses[-1]}
     launches = count_our_launches(step, dev[0]) * args.steps
     check_device_errors()
-    return ms, clk, e2e, launches, {"collectives": getattr(engine.fsdp_wrapper.coll, "name", "none")}
+    # the graph holds NCCL work: release it before the process group goes
+    engine.release_graph()
+    torch.cuda.synchronize()
+    return ms, clk, e2e, launches, {"collectives": getattr(engine.fsdp_wrapper.coll, "name", "none"),
+                                    "cuda_graph": use_graph}
 
 
 # --------------------------------------------------------------------------- reference arm

@@ -98,25 +98,72 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids,
   }
 }
 
-__global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids,
+// Embedding gradient from token ids sorted by value: one warp per run of
+// equal ids sums that run's dY rows in fp32 (in the stable-sort order, so the
+// result is deterministic) and writes - or adds into - one bf16 gradient row.
+// No full-vocabulary fp32 accumulator and no atomics.
+__global__ void embedding_bwd_kernel(const int64_t* __restrict__ sid, const int64_t* __restrict__ perm,
                                      const __nv_bfloat16* __restrict__ dy, int64_t lddy,
-                                     float* __restrict__ grad, int64_t ldg, int T, int H, int64_t v0,
-                                     int64_t vrows) {
-  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+                                     __nv_bfloat16* __restrict__ grad, int64_t ldg, int T, int H, int64_t v0,
+                                     int64_t vrows, bool accumulate) {
+  const int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (t >= T) return;
-  const int64_t row = ids[t] - v0;
+  if (p >= T) return;
+  const int64_t id = sid[p];
+  if (p > 0 && sid[p - 1] == id) return;  // not the head of its run
+  const int64_t row = id - v0;
   if (row < 0 || row >= vrows) return;
-  const __nv_bfloat16* g = dy + (int64_t)t * lddy;
-  float* dst = grad + row * ldg;
+  int end = p + 1;
+  while (end < T && sid[end] == id) ++end;
+  __nv_bfloat16* dst = grad + row * ldg;
   for (int c = lane * 8; c < H; c += 256) {
-    uint4 raw = *reinterpret_cast<const uint4*>(g + c);
-    const uint32_t* p = &raw.x;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int q = p; q < end; ++q) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(dy + perm[q] * lddy + c);
+      const uint32_t* w = &raw.x;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float2 f = unpack_bf16x2(p[q]);
-      atomicAdd(dst + c + 2 * q, f.x);
-      atomicAdd(dst + c + 2 * q + 1, f.y);
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_bf16x2(w[e]);
+        acc[2 * e] += f.x;
+        acc[2 * e + 1] += f.y;
+      }
+    }
+    uint4 o;
+    uint32_t* ow = &o.x;
+    if (accumulate) {
+      const uint4 old = *reinterpret_cast<const uint4*>(dst + c);
+      const uint32_t* w = &old.x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_bf16x2(w[e]);
+        ow[e] = pack_bf16x2(acc[2 * e] + f.x, acc[2 * e + 1] + f.y);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ow[e] = pack_bf16x2(acc[2 * e], acc[2 * e + 1]);
+    }
+    *reinterpret_cast<uint4*>(dst + c) = o;
+  }
+}
+
+// x *= *s in place (bf16), skipped entirely when *s == 1: the incoming
+// gradient of a loss is almost always exactly one, and the check costs no host sync.
+__global__ void scale_by_scalar_kernel(__nv_bfloat16* __restrict__ x, int64_t n, const float* __restrict__ s) {
+  const float a = *s;
+  if (a == 1.f) return;
+  for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 8; i < n;
+       i += (int64_t)gridDim.x * blockDim.x * 8) {
+    if (i + 8 <= n) {
+      uint4 raw = *reinterpret_cast<const uint4*>(x + i);
+      uint32_t* w = &raw.x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_bf16x2(w[e]);
+        w[e] = pack_bf16x2(f.x * a, f.y * a);
+      }
+      *reinterpret_cast<uint4*>(x + i) = raw;
+    } else {
+      for (int64_t j = i; j < n; ++j) x[j] = __float2bfloat16(__bfloat162float(x[j]) * a);
     }
   }
 }
@@ -177,11 +224,20 @@ void embedding_fwd(const int64_t* ids, const void* table, int64_t ldt, void* out
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
-void embedding_bwd(const int64_t* ids, const void* dy, int64_t lddy, float* grad, int64_t ldg,
-                   int T, int H, int64_t vocab_start, int64_t vocab_rows, cudaStream_t s) {
-  PB_CHECK(H % 8 == 0, "embedding: H must be a multiple of 8");
-  embedding_bwd_kernel<<<(T + 7) / 8, 256, 0, s>>>(ids, (const __nv_bfloat16*)dy, lddy, grad, ldg,
-                                                   T, H, vocab_start, vocab_rows);
+void embedding_bwd(const int64_t* sorted_ids, const int64_t* perm, const void* dy, int64_t lddy, void* grad,
+                   int64_t ldg, int T, int H, int64_t vocab_start, int64_t vocab_rows, bool accumulate,
+                   cudaStream_t s) {
+  PB_CHECK(H % 8 == 0 && lddy % 8 == 0 && ldg % 8 == 0, "embedding: H and strides must be multiples of 8");
+  if (T == 0) return;
+  embedding_bwd_kernel<<<(T + 7) / 8, 256, 0, s>>>(sorted_ids, perm, (const __nv_bfloat16*)dy, lddy,
+                                                   (__nv_bfloat16*)grad, ldg, T, H, vocab_start, vocab_rows,
+                                                   accumulate);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+void scale_by_scalar(void* x, int64_t n, const float* s_dev, cudaStream_t s) {
+  if (n == 0) return;
+  scale_by_scalar_kernel<<<grid_for(n / 8 + 1, 256), 256, 0, s>>>((__nv_bfloat16*)x, n, s_dev);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -5,7 +5,8 @@
 // ordinary loads and stores over NVLink 5 / NVSwitch.  No TMA multicast and
 // no library kernel ever touches a peer pointer.
 //
-//   signal_barrier   one block: publish `epoch` into every peer's signal pad
+//   signal_barrier   one warp: bump this buffer's device epoch counter, publish
+//                    the new epoch into every peer's signal pad
 //                    (release, system scope) and wait - bounded by limit_ns -
 //                    until every peer has published it into ours.  A timeout
 //                    records kErrPeerTimeout and returns (the host raises).
@@ -43,8 +44,13 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 __global__ void signal_barrier_kernel(const uint64_t* __restrict__ peer_pads, int rank, int world, int slot_base,
-                                      uint32_t epoch, uint64_t limit_ns, int* err) {
+                                      uint32_t* __restrict__ epoch_ctr, uint64_t limit_ns, int* err) {
   const int i = threadIdx.x;
+  // the epoch lives on the device (one counter per buffer and channel, bumped
+  // here), so a captured CUDA graph replays a fresh epoch every time
+  const uint32_t epoch = *((volatile uint32_t*)epoch_ctr) + 1u;
+  __syncwarp();
+  if (i == 0) *epoch_ctr = epoch;
   if (i >= world) return;
   // make this rank's prior writes (earlier kernels on this stream) visible first
   asm volatile("fence.acq_rel.sys;" ::: "memory");
@@ -200,10 +206,10 @@ __global__ void row_gather_kernel(uint8_t* __restrict__ dst, int64_t ld_dst, con
 
 }  // namespace
 
-void signal_barrier(const uint64_t* peer_pads_dev, int rank, int world, int slot_base, uint32_t epoch,
+void signal_barrier(const uint64_t* peer_pads_dev, int rank, int world, int slot_base, uint32_t* epoch_ctr,
                     uint64_t limit_ns, cudaStream_t s) {
   PB_CHECK(world >= 1 && world <= kMaxPeers, "signal_barrier: world size");
-  signal_barrier_kernel<<<1, 32, 0, s>>>(peer_pads_dev, rank, world, slot_base, epoch, limit_ns, error_word());
+  signal_barrier_kernel<<<1, 32, 0, s>>>(peer_pads_dev, rank, world, slot_base, epoch_ctr, limit_ns, error_word());
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

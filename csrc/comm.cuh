@@ -25,7 +25,7 @@ struct ReduceSegments {
 
 // peer_pads_dev: device array of `world` signal-pad pointers (uint32 words).
 // Slot words used: [slot_base + r] for r in [0, world).
-void signal_barrier(const uint64_t* peer_pads_dev, int rank, int world, int slot_base, uint32_t epoch,
+void signal_barrier(const uint64_t* peer_pads_dev, int rank, int world, int slot_base, uint32_t* epoch_ctr,
                     uint64_t limit_ns, cudaStream_t s);
 void multi_copy(const CopySegments& segs, cudaStream_t s);
 void reduce_segments(const ReduceSegments& segs, int world, float scale, bool accumulate, cudaStream_t s);

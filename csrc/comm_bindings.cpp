@@ -14,11 +14,16 @@ namespace {
 
 cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
-void p2p_barrier(int64_t peer_pads_dev, int64_t rank, int64_t world, int64_t slot_base, int64_t epoch,
-                 double limit_s) {
+// epochs: int32 CUDA tensor of per-channel counters owned by this buffer; the
+// kernel bumps epochs[channel] on the device (CUDA-graph replay safe).
+void p2p_barrier(int64_t peer_pads_dev, int64_t rank, int64_t world, int64_t slot_base, at::Tensor& epochs,
+                 int64_t channel, double limit_s) {
   TORCH_CHECK(world >= 1 && world <= pb::kMaxPeers && rank >= 0 && rank < world, "p2p_barrier: bad rank/world");
+  TORCH_CHECK(epochs.is_cuda() && epochs.scalar_type() == at::kInt && channel >= 0 && channel < epochs.numel(),
+              "p2p_barrier: epochs must be an int32 CUDA tensor with one counter per channel");
   pb::signal_barrier(reinterpret_cast<const uint64_t*>(peer_pads_dev), (int)rank, (int)world, (int)slot_base,
-                     (uint32_t)epoch, (uint64_t)(limit_s * 1e9), cur_stream());
+                     reinterpret_cast<uint32_t*>(epochs.data_ptr<int>()) + channel, (uint64_t)(limit_s * 1e9),
+                     cur_stream());
 }
 
 // Copy segments (src_ptr -> dst_ptr, nbytes); all 16-byte aligned multiples.

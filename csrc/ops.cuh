@@ -46,8 +46,11 @@ void swiglu_fwd(const void* gu, int64_t ldgu, void* h, int64_t ldh, int T, int I
 void embedding_fwd(const int64_t* ids, const void* table, int64_t ldt, void* out, int64_t ldo,
                    int T, int H, int64_t vocab_start, int64_t vocab_rows, cudaStream_t s);
 // grad_f32[ids[t]-vocab_start, :] += dy[t, :] (fp32 atomics, rows outside skipped)
-void embedding_bwd(const int64_t* ids, const void* dy, int64_t lddy, float* grad, int64_t ldg,
-                   int T, int H, int64_t vocab_start, int64_t vocab_rows, cudaStream_t s);
+void embedding_bwd(const int64_t* sorted_ids, const int64_t* perm, const void* dy, int64_t lddy, void* grad,
+                   int64_t ldg, int T, int H, int64_t vocab_start, int64_t vocab_rows, bool accumulate,
+                   cudaStream_t s);
+// x (bf16, n elements) *= *s_dev unless *s_dev == 1
+void scale_by_scalar(void* x, int64_t n, const float* s_dev, cudaStream_t s);
 
 // ---- cross entropy over a [T, V] bf16 logits block (ce.cu)
 // Row t's label is labels[t]; labels < 0 are ignored.  This rank holds vocab
@@ -81,7 +84,7 @@ struct AdamSeg {
   int64_t n;
 };
 void adamw_multi(const AdamSeg* segs_host, int nseg, float lr, float beta1, float beta2, float eps,
-                 float wd, int step, const float* grad_scale_dev, const int* skip_dev,
+                 float wd, int step, const float* grad_scale_dev, const int* skip_dev, const float* hyper_dev,
                  bool grad_f32, bool state_f32, cudaStream_t s);
 // Sum of squares of all segments into out[0] (f32, accumulated) and sets
 // out_flag[0] = 1 if any element is non-finite.

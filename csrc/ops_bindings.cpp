@@ -94,12 +94,25 @@ void embedding_fwd(const at::Tensor& ids, const at::Tensor& table, at::Tensor& o
                     ids.numel(), table.size(1), v0, table.size(0), cur_stream());
 }
 
-void embedding_bwd(const at::Tensor& ids, const at::Tensor& dy, at::Tensor& grad, int64_t v0) {
-  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "ids must be contiguous int64");
-  CHECK_BF16(dy); CHECK_F32(grad);
+// sorted_ids / perm: torch.sort(ids, stable=True); grad bf16 [vocab rows, H]
+void embedding_bwd(const at::Tensor& sorted_ids, const at::Tensor& perm, const at::Tensor& dy, at::Tensor& grad,
+                   int64_t v0, bool accumulate) {
+  TORCH_CHECK(sorted_ids.scalar_type() == at::kLong && sorted_ids.is_contiguous() &&
+              perm.scalar_type() == at::kLong && perm.is_contiguous() && perm.numel() == sorted_ids.numel(),
+              "embedding_bwd: sorted ids and permutation must be contiguous int64 of one length");
+  CHECK_BF16(dy); CHECK_BF16(grad);
+  TORCH_CHECK(dy.size(0) == sorted_ids.numel() && dy.size(1) == grad.size(1), "embedding_bwd: shapes");
   const c10::cuda::CUDAGuard g(dy.device());
-  pb::embedding_bwd(ids.data_ptr<int64_t>(), dy.data_ptr(), dy.stride(0), grad.data_ptr<float>(), grad.stride(0),
-                    ids.numel(), dy.size(1), v0, grad.size(0), cur_stream());
+  pb::embedding_bwd(sorted_ids.data_ptr<int64_t>(), perm.data_ptr<int64_t>(), dy.data_ptr(), dy.stride(0),
+                    grad.data_ptr(), grad.stride(0), sorted_ids.numel(), dy.size(1), v0, grad.size(0), accumulate,
+                    cur_stream());
+}
+
+void scale_by_scalar(at::Tensor& x, const at::Tensor& s) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "scale_by_scalar: bf16 x");
+  TORCH_CHECK(s.is_cuda() && s.scalar_type() == at::kFloat && s.numel() == 1, "scale_by_scalar: fp32 scalar");
+  const c10::cuda::CUDAGuard g(x.device());
+  pb::scale_by_scalar(x.data_ptr(), x.numel(), s.data_ptr<float>(), cur_stream());
 }
 
 void ce_fwd_bwd(at::Tensor& logits, const at::Tensor& labels, int64_t v0, const c10::optional<at::Tensor>& scale,
@@ -132,7 +145,8 @@ void cast_f32_to_bf16(const at::Tensor& src, at::Tensor& dst) {
 void adamw(const std::vector<at::Tensor>& params, const std::vector<at::Tensor>& grads,
            const std::vector<at::Tensor>& exp_avgs, const std::vector<at::Tensor>& exp_avg_sqs, double lr,
            double beta1, double beta2, double eps, double wd, int64_t step,
-           const c10::optional<at::Tensor>& grad_scale, const c10::optional<at::Tensor>& skip) {
+           const c10::optional<at::Tensor>& grad_scale, const c10::optional<at::Tensor>& skip,
+           const c10::optional<at::Tensor>& hyper) {
   TORCH_CHECK(params.size() == grads.size() && params.size() == exp_avgs.size() &&
               params.size() == exp_avg_sqs.size(), "adamw: list sizes differ");
   if (params.empty()) return;
@@ -158,7 +172,7 @@ void adamw(const std::vector<at::Tensor>& params, const std::vector<at::Tensor>&
     skip_ptr = skip->data_ptr<int>();
   }
   pb::adamw_multi(segs.data(), (int)segs.size(), (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd,
-                  (int)step, opt_f32(grad_scale), skip_ptr, grad_f32, state_f32, cur_stream());
+                  (int)step, opt_f32(grad_scale), skip_ptr, opt_f32(hyper), grad_f32, state_f32, cur_stream());
 }
 
 void sumsq(const std::vector<at::Tensor>& grads, const std::vector<double>& weights, at::Tensor& out,
@@ -255,10 +269,13 @@ void register_ops(pybind11::module& m) {
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
+  m.def("scale_by_scalar", &scale_by_scalar);
   m.def("ce_fwd_bwd", &ce_fwd_bwd);
   m.def("ce_row_stats", &ce_row_stats);
   m.def("cast_f32_to_bf16", &cast_f32_to_bf16);
-  m.def("adamw", &adamw);
+  m.def("adamw", &adamw, py::arg("params"), py::arg("grads"), py::arg("exp_avgs"), py::arg("exp_avg_sqs"),
+        py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("wd"), py::arg("step"),
+        py::arg("grad_scale") = py::none(), py::arg("skip") = py::none(), py::arg("hyper") = py::none());
   m.def("sumsq", &sumsq);
   m.def("clip_coef", &clip_coef);
   m.def("attn_fwd", &attn_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("B"),

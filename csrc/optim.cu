@@ -103,9 +103,15 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(SegTable tab, float lr,
                                                          float beta2, float eps, float wd,
                                                          float bc1, float bc2_sqrt,
                                                          const float* __restrict__ gscale,
-                                                         const int* __restrict__ skip) {
+                                                         const int* __restrict__ skip,
+                                                         const float* __restrict__ hyper) {
   if (skip && *skip) return;
   const float gs = gscale ? *gscale : 1.f;
+  if (hyper) {  // {lr, 1 - beta1^t, sqrt(1 - beta2^t)} from the device (CUDA-graph replays)
+    lr = hyper[0];
+    bc1 = hyper[1];
+    bc2_sqrt = hyper[2];
+  }
   const int chunk = blockIdx.x;
   const int si = find_seg(tab.chunk_start, tab.nseg, chunk);
   const AdamSeg sg = tab.seg[si];
@@ -184,8 +190,8 @@ __global__ void clip_coef_kernel(const float* total, float max_norm, float* out)
 }  // namespace
 
 void adamw_multi(const AdamSeg* segs, int nseg, float lr, float beta1, float beta2, float eps,
-                 float wd, int step, const float* grad_scale_dev, const int* skip_dev, bool grad_f32,
-                 bool state_f32, cudaStream_t s) {
+                 float wd, int step, const float* grad_scale_dev, const int* skip_dev, const float* hyper_dev,
+                 bool grad_f32, bool state_f32, cudaStream_t s) {
   const float bc1 = 1.f - powf(beta1, (float)step);
   const float bc2_sqrt = sqrtf(1.f - powf(beta2, (float)step));
   for (int off = 0; off < nseg; off += kMaxSegs) {
@@ -201,16 +207,16 @@ void adamw_multi(const AdamSeg* segs, int nseg, float lr, float beta1, float bet
     if (chunks == 0) continue;
     if (grad_f32 && state_f32)
       adamw_kernel<float, float><<<chunks, kThreads, 0, s>>>(tab, lr, beta1, beta2, eps, wd, bc1,
-                                                             bc2_sqrt, grad_scale_dev, skip_dev);
+                                                             bc2_sqrt, grad_scale_dev, skip_dev, hyper_dev);
     else if (grad_f32)
       adamw_kernel<float, __nv_bfloat16><<<chunks, kThreads, 0, s>>>(
-          tab, lr, beta1, beta2, eps, wd, bc1, bc2_sqrt, grad_scale_dev, skip_dev);
+          tab, lr, beta1, beta2, eps, wd, bc1, bc2_sqrt, grad_scale_dev, skip_dev, hyper_dev);
     else if (state_f32)
       adamw_kernel<__nv_bfloat16, float><<<chunks, kThreads, 0, s>>>(
-          tab, lr, beta1, beta2, eps, wd, bc1, bc2_sqrt, grad_scale_dev, skip_dev);
+          tab, lr, beta1, beta2, eps, wd, bc1, bc2_sqrt, grad_scale_dev, skip_dev, hyper_dev);
     else
       adamw_kernel<__nv_bfloat16, __nv_bfloat16><<<chunks, kThreads, 0, s>>>(
-          tab, lr, beta1, beta2, eps, wd, bc1, bc2_sqrt, grad_scale_dev, skip_dev);
+          tab, lr, beta1, beta2, eps, wd, bc1, bc2_sqrt, grad_scale_dev, skip_dev, hyper_dev);
     PB_CUDA_CHECK(cudaGetLastError());
   }
 }

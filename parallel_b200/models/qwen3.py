@@ -83,8 +83,8 @@ class Embedding(nn.Module):
         super().__init__()
         self.weight = nn.Parameter(torch.empty(num, dim))
 
-    def forward(self, ids, vocab_start: int = 0):
-        return Fx.embedding(ids, self.weight, vocab_start)
+    def forward(self, ids, vocab_start: int = 0, tied=None):
+        return Fx.embedding(ids, self.weight, vocab_start, tied)
 
 
 class RotaryEmbedding(nn.Module):
@@ -316,7 +316,11 @@ class Qwen3ForCausalLM(nn.Module):
             layer._seq = (B, S)
             layer._inv_freq = inv_freq
             layer._router_sink = []
-        x = self.model.embed_tokens(input_ids, self.vocab_start)
+        # tied embedding / LM head on the fused CE path: the embedding backward
+        # updates the LM head's weight gradient in place
+        tied = (Fx.TiedGrad() if self.config.tie_word_embeddings and ctx.tp_size == 1 and labels is not None
+                and input_ids.is_cuda else None)
+        x = self.model.embed_tokens(input_ids, self.vocab_start, tied)
         if ctx.tp_size > 1:
             x = ctx.comm.reduce_from_tp(x, ctx)
             if ctx.sp:
@@ -341,7 +345,7 @@ class Qwen3ForCausalLM(nn.Module):
             return out
         if labels is not None:
             y = Fx.shift_labels(labels) if shift_labels else labels
-            out.loss = Fx.lm_head_cross_entropy(x.reshape(B * S, -1), self.lm_head.weight, y)
+            out.loss = Fx.lm_head_cross_entropy(x.reshape(B * S, -1), self.lm_head.weight, y, tied=tied)
             if self.config.is_moe and (self.config.output_router_logits if output_router_logits is None
                                        else output_router_logits) and router_logits:
                 out.aux_loss = MoE.load_balancing_loss(router_logits, self.config.num_experts,

@@ -12,9 +12,10 @@ exchange).  The data movement is done by this repository's kernels
 * reduce-scatter: gradients are packed into a symmetric slot, one barrier
   ("my gradients are staged"), one kernel that sums the rank's shard rows
   from all peers in fp32 and writes (or accumulates into) the local bf16
-  gradient bucket scaled by 1/N, and a closing barrier so the slot can be
-  reused; it runs on a dedicated communication stream so it overlaps the
-  next unit's backward.
+  gradient bucket scaled by 1/N; it runs on a dedicated communication stream
+  so it overlaps the next unit's backward.  A slot is restaged only after the
+  barrier of the following reduction has passed (every rank finished reading
+  it), which needs no closing barrier.
 
 Barriers are bounded (``PB_P2P_TIMEOUT_S``, default 60 s): a missing peer
 records an error word on the device instead of hanging; the engine reads it
@@ -65,12 +66,13 @@ class SymmBuffer:
         off = self.tensor.data_ptr() - base[self.rank]
         self.peer_ptrs = [b + off for b in base]
         self.pads_dev = int(self.handle.signal_pad_ptrs_dev)
-        self.epochs = [0] * 8
+        # per-channel epoch counters live on the device: the barrier kernel bumps
+        # them, so a captured CUDA graph that contains barriers replays correctly
+        self.epochs = torch.zeros(8, dtype=torch.int32, device=device)
         self.event = None
 
     def barrier(self, channel: int, limit_s: float) -> None:
-        self.epochs[channel] += 1
-        ext().p2p_barrier(self.pads_dev, self.rank, self.world, channel * 8, self.epochs[channel], limit_s)
+        ext().p2p_barrier(self.pads_dev, self.rank, self.world, channel * 8, self.epochs, channel, limit_s)
 
 
 @dataclass
@@ -112,6 +114,15 @@ class P2PUnitCollectives:
 
     def release_full(self, unit, full):
         pass
+
+    def reset_step_events(self) -> None:
+        """Forget the slot-reuse events of finished steps.  Valid between steps:
+        the gradient-norm all-reduce that ends a step follows every rank's
+        reductions, so every slot is free when the next step starts (needed
+        before a CUDA-graph capture, which cannot wait on earlier events)."""
+        for s in self.slots:
+            s.event = None
+        self._prev_slot = None
 
     def begin_forward(self) -> None:
         """A forward pass starts: the shards may have changed since the last

@@ -79,6 +79,8 @@ class ParallelEngine:
         self._flag_host: torch.Tensor | None = None
         self._flag_event = None
         self._last_grad_norm: torch.Tensor | None = None
+        self._graph = None
+        self._captured_flag: torch.Tensor | None = None
         self.reset_step_memory_stats()
 
     # ------------------------------------------------------------------ init
@@ -177,6 +179,37 @@ class ParallelEngine:
         with collective_phase("optimizer"):
             self._step_impl()
 
+    # ------------------------------------------------------------------ whole step
+    def train_step(self, x, y):
+        """Forward, backward and optimizer step on one batch; returns the loss
+        as a device tensor (no host synchronisation).  After
+        ``capture_train_step`` this replays the captured CUDA graph instead
+        (the returned tensor is then the graph's static loss, overwritten by
+        the next call)."""
+        if self._graph is not None:
+            return self._graph.replay(x, y)
+        outputs = self.forward(x, y)
+        self.backward(outputs.loss)
+        self.step()
+        return outputs.loss.detach()
+
+    def capture_train_step(self, x, y, warmup: int = 3):
+        """Run ``warmup`` eager steps on (x, y) (they train on it), then capture
+        one whole training step - forward, backward, reductions, optimizer - as
+        a CUDA graph that ``train_step`` replays from then on.  Every rank must
+        call this at the same point.  See ``parallel_b200/parallel/graph_step.py``."""
+        from .graph_step import GraphedTrainStep
+
+        self._graph = None
+        self._graph = GraphedTrainStep(self, x, y, warmup=warmup)
+        return self._graph
+
+    def release_graph(self):
+        """Drop the captured step (call before destroying the process group)."""
+        if self._graph is not None:
+            self._graph.release()
+        self._graph = None
+
     def _check_pending_nonfinite(self):
         if self._pending_nonfinite is None:
             return
@@ -225,7 +258,9 @@ class ParallelEngine:
         return groups
 
     def _step_impl(self):
-        self._check_pending_nonfinite()
+        capturing = self.device.type == "cuda" and torch.cuda.is_current_stream_capturing()
+        if not capturing:
+            self._check_pending_nonfinite()
         self._average_gradients()
         if self.grad_scaler.is_enabled():
             self.grad_scaler.unscale_(self.optimizer)
@@ -256,12 +291,16 @@ class ParallelEngine:
             self.optimizer.step(grad_scale=scale, skip=flag)
             self.optimizer.zero_grad(set_to_none=True)
             self.fsdp_wrapper.zero_grad()
-            if self.sync_finite_check:
+            if capturing:  # read back after each replay by the graph runner
+                self._captured_flag = flag
+            elif self.sync_finite_check:
                 self._pending_nonfinite = flag
                 self._check_pending_nonfinite()
             else:
                 self._defer_nonfinite_check(flag)
             return
+        if capturing:
+            raise RuntimeError("Only the CUDA step without a gradient scaler can be captured in a CUDA graph")
         # generic path (CPU / fp16 scaler): reference semantics with host syncs
         finite = self._grads_are_finite()
         if finite and max_norm > 0.0:

@@ -265,6 +265,13 @@ def test_adamw_and_sumsq():
         opt.step()
         C.adamw([p], [g], [m], [v], 1e-2, 0.9, 0.95, 1e-8, 0.1, step, None, None)
     assert _rel_err(p, opt.param_groups[0]["params"][0].detach()) < 1e-2
+    # step 4 with lr and bias corrections read from a device tensor (the CUDA-graph
+    # path); the scalar lr / step given alongside must be ignored
+    opt.param_groups[0]["params"][0].grad = g.float()
+    opt.step()
+    hyper = torch.tensor([1e-2, 1 - 0.9 ** 4, (1 - 0.95 ** 4) ** 0.5], device="cuda")
+    C.adamw([p], [g], [m], [v], 0.0, 0.9, 0.95, 1e-8, 0.1, 1, None, None, hyper)
+    assert _rel_err(p, opt.param_groups[0]["params"][0].detach()) < 1e-2
     out = torch.zeros(1, device="cuda")
     flag = torch.zeros(1, device="cuda", dtype=torch.int32)
     C.sumsq([g, g[:100]], [1.0, 0.0], out, flag)
@@ -289,10 +296,24 @@ def test_embedding():
     ref[(ids < 200) | (ids >= 600)] = 0
     assert torch.equal(out, ref)
     dy = torch.randn(T, H, device="cuda").to(torch.bfloat16)
-    grad = torch.zeros(V, H, device="cuda")
-    C.embedding_bwd(ids, dy, grad, 0)
+    ids[:40] = 7  # a long run of one id
+    sid, perm = torch.sort(ids, stable=True)
+    grad = torch.zeros(V, H, device="cuda", dtype=torch.bfloat16)
+    C.embedding_bwd(sid, perm, dy, grad, 0, False)
     ref_g = torch.zeros(V, H, device="cuda").index_add_(0, ids, dy.float())
-    assert _rel_err(grad, ref_g) < 1e-5
+    assert _rel_err(grad, ref_g) < 4e-3
+    # accumulate into an existing gradient, vocabulary slice [200, 600)
+    base = torch.randn(400, H, device="cuda").to(torch.bfloat16)
+    acc = base.clone()
+    C.embedding_bwd(sid, perm, dy, acc, 200, True)
+    assert _rel_err(acc, base.float() + ref_g[200:600]) < 4e-3
+    # in-place scale by a device scalar; a scale of exactly 1 leaves x untouched
+    x = torch.randn(1000, device="cuda").to(torch.bfloat16)
+    y = x.clone()
+    C.scale_by_scalar(y, torch.tensor([1.0], device="cuda"))
+    assert torch.equal(x, y)
+    C.scale_by_scalar(y, torch.tensor([0.5], device="cuda"))
+    assert torch.equal(y, (x.float() * 0.5).to(torch.bfloat16))
     _check_no_device_error()
 
 

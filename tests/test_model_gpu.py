@@ -67,3 +67,45 @@ def test_engine_trains_on_gpu():
     check_device_errors()
     assert losses[-1] < losses[0] - 0.5, losses
     assert eng.last_grad_norm is not None and torch.isfinite(eng.last_grad_norm).all()
+
+
+def test_cuda_graph_step_matches_eager():
+    """A captured-and-replayed training step follows the eager trajectory
+    (same kernels in the same order; lr and bias corrections read from the
+    device), including an lr change between replays."""
+    from parallel_b200.config import from_dotlist, load_cfg, merge
+    from parallel_b200.ops._ext import check_device_errors
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    c = merge(load_cfg(argv=[]), from_dotlist(["config.device_type=cuda", "model.learning_rate=3e-3"]))
+    engines = []
+    for _ in range(2):
+        cfg, _, gpu = _pair("small-qwen3")
+        pc = ParallelConfig(c)
+        pc.set_device_mesh("cuda")
+        engines.append(ParallelEngine(gpu, None, pc, c, torch.device("cuda", 0)))
+    eager, graphed = engines
+    g = torch.Generator().manual_seed(3)
+    toks = [torch.randint(0, cfg.vocab_size, (4, 129), generator=g).cuda() for _ in range(5)]
+    # the capture runs its warm-up steps eagerly on the capture batch
+    graphed.capture_train_step(toks[0][:, :-1], toks[0][:, 1:], warmup=2)
+    for _ in range(2):
+        eager.train_step(toks[0][:, :-1], toks[0][:, 1:])
+    le, lg = [], []
+    for i in range(1, 5):
+        if i == 3:
+            for e in engines:
+                e.optimizer.param_groups[0]["lr"] = 1e-3
+        le.append(float(eager.train_step(toks[i][:, :-1], toks[i][:, 1:])))
+        lg.append(float(graphed.train_step(toks[i][:, :-1], toks[i][:, 1:])))
+    torch.cuda.synchronize()
+    check_device_errors()
+    assert max(abs(a - b) for a, b in zip(le, lg)) < 2e-2, (le, lg)
+    pe, pg = dict(eager.model.named_parameters()), dict(graphed.model.named_parameters())
+    for n, p in pe.items():
+        assert _rel(pg[n].detach(), p.detach()) < 2e-2, n
+    se = eager.optimizer.state[next(iter(eager.optimizer.state))]["step"]
+    sg = graphed.optimizer.state[next(iter(graphed.optimizer.state))]["step"]
+    assert float(se) == float(sg) == 6.0
+    graphed.release_graph()
