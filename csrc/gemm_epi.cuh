@@ -18,7 +18,16 @@ struct EpiArgs {
   int epi;
   int64_t up_col;  // kEpiSwiGLU: column of the "up" half inside R
   ScatterArgs sc;  // sc.nranks > 0: kEpiStoreBf16 rows go to their owners
+  int tma;         // CTA-pair kernel: stage tiles in shared memory and store them with TMA
 };
+
+// TMA-store epilogue staging, per epilogue warp: three 32 x 32 bf16 boxes of
+// 64-byte rows with the 64-byte swizzle (16-byte chunk q of row r sits at
+// chunk q ^ ((r >> 1) & 3)), which keeps the row-per-thread writes of a warp
+// free of bank conflicts.
+constexpr int kEpiBox = 32;
+constexpr int kEpiBoxBytes = kEpiBox * kEpiBox * 2;
+constexpr int kEpiWarpBytes = 3 * kEpiBoxBytes;
 
 // Output row pointer of row m for the bf16 store epilogue.
 __device__ __forceinline__ __nv_bfloat16* out_row_bf16(const EpiArgs& ep, int m) {
@@ -158,6 +167,83 @@ __device__ __forceinline__ void epilogue_row(const EpiArgs& ep, uint32_t t_row, 
         }
       }
     }
+  }
+}
+
+__device__ __forceinline__ void stage_row_swz64(uint8_t* box, int r, const float* v) {
+  uint8_t* row = box + r * 64;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 u;
+    u.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+    u.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+    u.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+    u.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+    *reinterpret_cast<uint4*>(row + ((q ^ ((r >> 1) & 3)) << 4)) = u;
+  }
+}
+
+// TMA-store epilogue of one warp's 32 accumulator rows of a tile (the bf16
+// store and SwiGLU epilogues): each 32-column chunk is read from TMEM,
+// converted, written into this warp's staging boxes and stored with one TMA
+// tile store per array (coalesced full lines, asynchronous).  `release` runs
+// right after the tile's last TMEM read, so the MMA can reuse the
+// accumulator while the stores drain.  y0 = the warp's first output row,
+// n_base = the tile's first output column, N = output columns.
+template <int BN, bool SWIGLU, typename Release>
+__device__ __forceinline__ void epilogue_warp_tma(const EpiArgs& ep, const CUtensorMap* tmC, const CUtensorMap* tmR,
+                                                  uint32_t t_row, uint8_t* stage, int lane, int y0, int M, int N,
+                                                  int n_base, Release release) {
+  constexpr int BN_OUT = SWIGLU ? BN / 2 : BN;
+  const bool rows_in = y0 < M;
+#pragma unroll 1
+  for (int c = 0; c < BN_OUT; c += 32) {
+    float a[32], b[32];
+    tmem_ld32(t_row + c, a);
+    if (SWIGLU) tmem_ld32(t_row + BN_OUT + c, b);
+    tmem_wait_ld();
+    if (c + 32 >= BN_OUT) release();
+    const int n0 = n_base + c;
+    const bool store = rows_in && n0 < N;
+    uint8_t* box0;
+    if (SWIGLU) {
+      float h[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        // the pre-activations are stored as bf16: silu(g) * u of the rounded values
+        a[j] = __bfloat162float(__float2bfloat16(a[j]));
+        b[j] = __bfloat162float(__float2bfloat16(b[j]));
+        h[j] = silu_f(a[j]) * b[j];
+      }
+      if (lane == 0) bulk_wait_group_read<0>();  // the previous chunk's stores have read the boxes
+      __syncwarp();
+      box0 = stage;
+      if (store) {
+        stage_row_swz64(stage, lane, h);
+        if (ep.R) {
+          stage_row_swz64(stage + kEpiBoxBytes, lane, a);
+          stage_row_swz64(stage + 2 * kEpiBoxBytes, lane, b);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) a[j] *= ep.alpha;
+      // two boxes alternate: chunk c may be staged while chunk c - 1 drains
+      box0 = stage + ((c >> 5) & 1) * kEpiBoxBytes;
+      if (lane == 0) bulk_wait_group_read<1>();
+      __syncwarp();
+      if (store) stage_row_swz64(box0, lane, a);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && store) {
+      tma_store_2d(tmC, box0, n0, y0);
+      if (SWIGLU && ep.R) {
+        tma_store_2d(tmR, stage + kEpiBoxBytes, n0, y0);
+        tma_store_2d(tmR, stage + 2 * kEpiBoxBytes, (int)ep.up_col + n0, y0);
+      }
+    }
+    if (lane == 0) bulk_commit_group();
   }
 }
 

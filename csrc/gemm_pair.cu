@@ -45,7 +45,8 @@ struct PairCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int EPI_BYTES = 4 * gemm_detail::kEpiWarpBytes;  // TMA-store staging of the 4 epilogue warps
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
 };
 
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
@@ -92,7 +93,7 @@ template <int BN, bool A_MN, bool B_MN, bool SWIGLU, bool GATHER>
 __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiArgs ep,
                      int M, int N, int K, int b_up_row, int* err, const __grid_constant__ GatherArgs ga,
-                     int splits) {
+                     int splits, const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR) {
   using Cfg = PairCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int B_HALF = Cfg::B_HALF;
@@ -104,7 +105,8 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
                                              ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint8_t* sEpi = sB + STAGES * Cfg::B_BYTES;  // 1024-byte aligned (stage sizes are multiples of 1 KB)
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sEpi + Cfg::EPI_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;  // used on the even CTA (256 arrivals: both epilogues)
@@ -244,6 +246,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
   } else {
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
+    uint8_t* stage = sEpi + quarter * gemm_detail::kEpiWarpBytes;
     int local = 0;
     for (int w = cid; w < num_work; w += n_clusters, ++local) {
       const int tile = w % num_tiles;
@@ -254,10 +257,21 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
       tc_fence_after();
       const int m = tm * 2 * BM_CTA + (int)rank * BM_CTA + row;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      gemm_detail::epilogue_row<BN, SWIGLU>(ep, t_row, m, M, N, tn * BN_OUT);
-      tc_fence_before();
-      mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
+      const uint32_t tempty = mapa_shared(smem_u32(&tempty_bar[acc]), 0);
+      if (ep.tma) {
+        gemm_detail::epilogue_warp_tma<BN, SWIGLU>(ep, &tmC, &tmR, t_row, stage, lane, m - lane, M, N, tn * BN_OUT,
+                                                   [&] {
+                                                     tc_fence_before();
+                                                     mbar_arrive_cluster(tempty);
+                                                   });
+      } else {
+        gemm_detail::epilogue_row<BN, SWIGLU>(ep, t_row, m, M, N, tn * BN_OUT);
+        tc_fence_before();
+        mbar_arrive_cluster(tempty);
+      }
     }
+    // the tile stores must have finished before the kernel's shared memory goes
+    if (ep.tma && lane == 0) bulk_wait_group<0>();
   }
 
   // On an error path the MMA issuer may have left MMAs in flight: drain them
@@ -317,6 +331,21 @@ void launch_pair(const GemmParams& p, cudaStream_t stream) {
               : make_tmap_2d_bf16(p.B, p.K, p.N, p.ldb, BK, Cfg::B_HALF);
   EpiArgs ep{p.C, p.R, p.ldc, p.ldr, p.alpha, p.epi, SWIGLU ? p.b_up_offset : 0};
   if (p.scatter) ep.sc = *p.scatter;
+  // TMA-store epilogue for the bf16 store and SwiGLU epilogues into local memory
+  // (16-byte aligned bases and row strides; SwiGLU: whole 32-column chunks so a
+  // gate store can never spill into the up half)
+  auto al16 = [](const void* ptr, int64_t ld) {
+    return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && (ld * 2) % 16 == 0;
+  };
+  CUtensorMap tc{}, tr{};
+  if (!p.scatter && p.C && al16(p.C, p.ldc) &&
+      ((SWIGLU && p.N % 32 == 0 && (!p.R || al16(p.R, p.ldr))) || (!SWIGLU && p.epi == kEpiStoreBf16))) {
+    tc = make_tmap_2d_bf16_swz(p.C, p.N, p.M, p.ldc, gemm_detail::kEpiBox, gemm_detail::kEpiBox, 64);
+    if (SWIGLU && p.R)
+      tr = make_tmap_2d_bf16_swz(p.R, p.b_up_offset + p.N, p.M, p.ldr, gemm_detail::kEpiBox, gemm_detail::kEpiBox,
+                                 64);
+    ep.tma = 1;
+  }
   GatherArgs ga{};
   if (GATHER) ga = *p.gather;
   const int bn_out = SWIGLU ? BN / 2 : BN;
@@ -326,7 +355,7 @@ void launch_pair(const GemmParams& p, cudaStream_t stream) {
   clusters = std::max(1, std::min(clusters, tiles));
   cfg.gridDim = dim3(2 * clusters, 1, 1);
   PB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, ep, p.M, p.N, p.K, (int)p.b_up_offset, error_word(dev), ga,
-                                   std::max(1, p.splits)));
+                                   std::max(1, p.splits), tc, tr));
 }
 
 }  // namespace

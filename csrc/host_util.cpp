@@ -91,6 +91,27 @@ CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t inner, uint64_t outer,
   return m;
 }
 
+CUtensorMap make_tmap_2d_bf16_swz(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                                  uint32_t box_inner, uint32_t box_outer, int swizzle_bytes) {
+  PB_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
+  PB_CHECK((row_stride_elems * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+  if (swizzle_bytes == 32) sw = CU_TENSOR_MAP_SWIZZLE_32B;
+  else if (swizzle_bytes == 64) sw = CU_TENSOR_MAP_SWIZZLE_64B;
+  else if (swizzle_bytes == 128) sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  else PB_CHECK(swizzle_bytes == 0, "TMA swizzle must be 0, 32, 64 or 128 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  PB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (2d, swizzled store) failed: code " + std::to_string(r));
+  return m;
+}
+
 CUtensorMap make_tmap_3d_bf16(const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                               uint64_t stride1_elems, uint64_t stride2_elems, uint32_t b0,
                               uint32_t b1, uint32_t b2) {

@@ -41,6 +41,11 @@ CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t inner, uint64_t outer,
                               uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
                               bool swizzle128 = true);
 
+// 2-D bf16 tensor map with a chosen swizzle span (0 = none, 32, 64 or 128 bytes);
+// used for epilogue tile stores.
+CUtensorMap make_tmap_2d_bf16_swz(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                                  uint32_t box_inner, uint32_t box_outer, int swizzle_bytes);
+
 // Encode a 3-D bf16 tiled tensor map with 128-byte swizzle.
 CUtensorMap make_tmap_3d_bf16(const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                               uint64_t stride1_elems, uint64_t stride2_elems, uint32_t b0,

@@ -289,6 +289,13 @@ __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const 
       : "memory");
 }
 
+// TMA tile store (shared -> global) into the bulk group of this thread.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Wait until at most N committed bulk groups still read their shared source.

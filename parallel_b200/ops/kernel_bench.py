@@ -1,6 +1,6 @@
 """Micro-benchmarks of the sm_100a kernels at the Qwen3-0.6B training shapes.
 
-    python -m parallel_b200.ops.kernel_bench attn_fwd|attn_bwd|gemm|rmsnorm_bwd|qknorm [--iters N]
+    python -m parallel_b200.ops.kernel_bench attn_fwd|attn_bwd|gemm|gemm_swiglu|gemm_residual|rmsnorm_bwd|qknorm|all [--iters N]
 
 Each case runs a few warm-up launches, then times ``--iters`` launches with
 CUDA events on the current stream and prints the time per launch and the
@@ -77,6 +77,28 @@ def case_gemm(warmup, iters):
     return f"gemm (CTA pair) {M}x{N}x{K}: {us:.1f} us, {2 * M * N * K / us / 1e6:.0f} TF/s"
 
 
+def case_gemm_swiglu(warmup, iters):
+    C = ext()
+    M, N, K = B * S, 2 * I, H  # gate/up projection with the SwiGLU epilogue (training: saves gate/up)
+    a = (torch.randn(M, K, device="cuda") * 0.05).to(torch.bfloat16)
+    b = (torch.randn(N, K, device="cuda") * 0.05).to(torch.bfloat16)
+    h = torch.empty(M, I, device="cuda", dtype=torch.bfloat16)
+    gu = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    us = _time(lambda: C.gemm(a, b, h, False, False, 5, 1.0, gu, I, I), warmup, iters)
+    return f"gemm + SwiGLU epilogue (CTA pair) {M}x{N}x{K}: {us:.1f} us, {2 * M * N * K / us / 1e6:.0f} TF/s"
+
+
+def case_gemm_residual(warmup, iters):
+    C = ext()
+    M, N, K = B * S, H, I  # down projection + residual
+    a = (torch.randn(M, K, device="cuda") * 0.05).to(torch.bfloat16)
+    b = (torch.randn(N, K, device="cuda") * 0.05).to(torch.bfloat16)
+    r = torch.randn(M, N, device="cuda").to(torch.bfloat16)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    us = _time(lambda: C.gemm(a, b, out, False, False, 1, 1.0, r), warmup, iters)
+    return f"gemm + residual epilogue (CTA pair) {M}x{N}x{K}: {us:.1f} us, {2 * M * N * K / us / 1e6:.0f} TF/s"
+
+
 def case_rmsnorm_bwd(warmup, iters):
     C = ext()
     T = B * S
@@ -101,8 +123,8 @@ def case_qknorm(warmup, iters):
     return f"qk-norm + RoPE fwd {T} tokens x {NQ + NKV} heads: {us:.1f} us, {2 * T * (NQ + NKV) * D * 2 / us / 1e3:.0f} GB/s"
 
 
-CASES = {"attn_fwd": case_attn_fwd, "attn_bwd": case_attn_bwd, "gemm": case_gemm, "rmsnorm_bwd": case_rmsnorm_bwd,
-         "qknorm": case_qknorm}
+CASES = {"attn_fwd": case_attn_fwd, "attn_bwd": case_attn_bwd, "gemm": case_gemm, "gemm_swiglu": case_gemm_swiglu,
+         "gemm_residual": case_gemm_residual, "rmsnorm_bwd": case_rmsnorm_bwd, "qknorm": case_qknorm}
 
 
 def main(argv=None):

@@ -110,7 +110,9 @@ def test_gemm_epilogues():
     _check_no_device_error()
 
 
-@pytest.mark.parametrize("T,I,H", [(256, 384, 256), (1024, 3072, 1024)])
+# (1000, 320): ragged rows on the TMA-store epilogue; (512, 200): columns not a
+# multiple of 32, which takes the row-store epilogue
+@pytest.mark.parametrize("T,I,H", [(256, 384, 256), (1024, 3072, 1024), (1000, 320, 256), (512, 200, 128)])
 def test_gemm_swiglu(T, I, H):
     from parallel_b200.ops.gemm import linear_swiglu
 
