@@ -98,4 +98,15 @@ void sumsq_multi(const NormSeg* segs_host, int nseg, bool f32, float* out, int* 
 // scale = min(max_norm / (sqrt(total) + 1e-6), 1)  written to scale_out[0]
 void clip_coef(const float* total_sumsq, float max_norm, float* scale_out, cudaStream_t s);
 
+// Mixture-of-experts router (csrc/router.cu): softmax + top-k + renormalisation
+// + route histogram of bf16 logits [T, E] (row stride ld); and its backward.
+void router_fwd(const void* logits, int64_t ld, int T, int E, int K, bool renorm, float* probs, float* topv,
+                int64_t* topi, int* counts, cudaStream_t s);
+void router_bwd(const float* probs, const float* dprobs, const float* dtopv, const int64_t* topi, int T, int E, int K,
+                bool renorm, void* dlogits, int64_t ld, cudaStream_t s);
+// Load-balancing loss statistics over probabilities [R, E]: per-expert top-k
+// counts and sums of the second softmax (accumulated into counts / ssum).
+void aux_stats(const float* probs, int R, int E, int K, float* counts, float* ssum, cudaStream_t s);
+void aux_stats_bwd(const float* probs, const float* gsum, int R, int E, float* dprobs, cudaStream_t s);
+
 }  // namespace pb

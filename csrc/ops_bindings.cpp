@@ -115,6 +115,58 @@ void scale_by_scalar(at::Tensor& x, const at::Tensor& s) {
   pb::scale_by_scalar(x.data_ptr(), x.numel(), s.data_ptr<float>(), cur_stream());
 }
 
+// ---------------------------------------------------------------- MoE router
+void router_fwd(const at::Tensor& logits, int64_t top_k, bool renorm, at::Tensor& probs, at::Tensor& topv,
+                at::Tensor& topi, const c10::optional<at::Tensor>& counts) {
+  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == at::kBFloat16 && logits.dim() == 2 &&
+              logits.stride(1) == 1, "router_fwd: bf16 [T, E] logits with unit inner stride");
+  const int64_t T = logits.size(0), E = logits.size(1);
+  CHECK_F32(probs); CHECK_F32(topv);
+  TORCH_CHECK(probs.numel() == T * E && topv.numel() == T * top_k, "router_fwd: output sizes");
+  TORCH_CHECK(topi.scalar_type() == at::kLong && topi.is_contiguous() && topi.numel() == T * top_k,
+              "router_fwd: int64 [T, k] indices");
+  int* cnt = nullptr;
+  if (counts.has_value() && counts->defined()) {
+    TORCH_CHECK(counts->scalar_type() == at::kInt && counts->numel() == E, "router_fwd: int32 [E] counts");
+    cnt = counts->data_ptr<int>();
+  }
+  const c10::cuda::CUDAGuard g(logits.device());
+  pb::router_fwd(logits.data_ptr(), logits.stride(0), (int)T, (int)E, (int)top_k, renorm, probs.data_ptr<float>(),
+                 topv.data_ptr<float>(), topi.data_ptr<int64_t>(), cnt, cur_stream());
+}
+
+void router_bwd(const at::Tensor& probs, const c10::optional<at::Tensor>& dprobs, const at::Tensor& dtopv,
+                const at::Tensor& topi, bool renorm, at::Tensor& dlogits) {
+  CHECK_F32(probs); CHECK_F32(dtopv); CHECK_BF16(dlogits);
+  TORCH_CHECK(probs.dim() == 2 && topi.dim() == 2 && topi.scalar_type() == at::kLong && topi.is_contiguous(),
+              "router_bwd: probs [T, E], topi int64 [T, k]");
+  const int64_t T = probs.size(0), E = probs.size(1), K = topi.size(1);
+  const float* dp = opt_f32(dprobs);
+  if (dp) TORCH_CHECK(dprobs->numel() == T * E, "router_bwd: dprobs size");
+  TORCH_CHECK(dtopv.numel() == T * K && dlogits.size(0) == T && dlogits.size(1) == E, "router_bwd: sizes");
+  const c10::cuda::CUDAGuard g(probs.device());
+  pb::router_bwd(probs.data_ptr<float>(), dp, dtopv.data_ptr<float>(), topi.data_ptr<int64_t>(), (int)T, (int)E,
+                 (int)K, renorm, dlogits.data_ptr(), dlogits.stride(0), cur_stream());
+}
+
+void aux_stats(const at::Tensor& probs, int64_t top_k, at::Tensor& counts, at::Tensor& ssum) {
+  CHECK_F32(probs); CHECK_F32(counts); CHECK_F32(ssum);
+  TORCH_CHECK(probs.dim() == 2 && counts.numel() == probs.size(1) && ssum.numel() == probs.size(1),
+              "aux_stats: probs [R, E], counts / sums [E]");
+  const c10::cuda::CUDAGuard g(probs.device());
+  pb::aux_stats(probs.data_ptr<float>(), (int)probs.size(0), (int)probs.size(1), (int)top_k,
+                counts.data_ptr<float>(), ssum.data_ptr<float>(), cur_stream());
+}
+
+void aux_stats_bwd(const at::Tensor& probs, const at::Tensor& gsum, at::Tensor& dprobs) {
+  CHECK_F32(probs); CHECK_F32(gsum); CHECK_F32(dprobs);
+  TORCH_CHECK(probs.dim() == 2 && gsum.numel() == probs.size(1) && dprobs.numel() == probs.numel(),
+              "aux_stats_bwd: sizes");
+  const c10::cuda::CUDAGuard g(probs.device());
+  pb::aux_stats_bwd(probs.data_ptr<float>(), gsum.data_ptr<float>(), (int)probs.size(0), (int)probs.size(1),
+                    dprobs.data_ptr<float>(), cur_stream());
+}
+
 void ce_fwd_bwd(at::Tensor& logits, const at::Tensor& labels, int64_t v0, const c10::optional<at::Tensor>& scale,
                 const c10::optional<at::Tensor>& row_lse, bool lse_given, const c10::optional<at::Tensor>& row_target,
                 const c10::optional<at::Tensor>& loss_sum, bool write_grad) {
@@ -270,6 +322,10 @@ void register_ops(pybind11::module& m) {
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("scale_by_scalar", &scale_by_scalar);
+  m.def("router_fwd", &router_fwd);
+  m.def("router_bwd", &router_bwd);
+  m.def("aux_stats", &aux_stats);
+  m.def("aux_stats_bwd", &aux_stats_bwd);
   m.def("ce_fwd_bwd", &ce_fwd_bwd);
   m.def("ce_row_stats", &ce_row_stats);
   m.def("cast_f32_to_bf16", &cast_f32_to_bf16);

@@ -16,8 +16,10 @@ replicated-token expert parallelism uses for experts owned by other ranks,
 parallel/parallel/engine/model_parallel/expert_parallel.py:50-60) are
 skipped explicitly.
 
-On CUDA the expert MLPs run as grouped tcgen05 GEMMs (csrc/gemm_grouped.cu,
-one launch per product for all experts); on CPU the plain PyTorch loop runs.
+On CUDA the router's softmax / top-k / renormalisation / histogram and the
+loss statistics are fused kernels (csrc/router.cu) and the expert MLPs run as
+grouped tcgen05 GEMMs (csrc/gemm_grouped.cu, one launch per product for all
+experts); on CPU the plain PyTorch code runs.
 """
 from __future__ import annotations
 
@@ -28,11 +30,50 @@ from . import gemm as G
 from ._ext import ext
 
 
-def route(x2: torch.Tensor, w: torch.Tensor, top_k: int, norm_topk_prob: bool):
-    """Returns (probs [T, E] fp32 softmax, top-k weights [T, k], top-k index [T, k])."""
+class _RouterFn(torch.autograd.Function):
+    """Softmax + top-k + renormalisation (+ route histogram) of bf16 router
+    logits in one kernel (csrc/router.cu); the backward folds the gradients of
+    the probabilities (auxiliary loss) and of the selected weights."""
+
+    @staticmethod
+    def forward(ctx, logits, top_k, renorm, counts):
+        T, E = logits.shape
+        probs = torch.empty(T, E, device=logits.device, dtype=torch.float32)
+        topv = torch.empty(T, top_k, device=logits.device, dtype=torch.float32)
+        topi = torch.empty(T, top_k, device=logits.device, dtype=torch.int64)
+        ext().router_fwd(logits, top_k, renorm, probs, topv, topi, counts)
+        ctx.save_for_backward(probs, topi)
+        ctx.renorm = renorm
+        ctx.mark_non_differentiable(topi)
+        return probs, topv, topi
+
+    @staticmethod
+    def backward(ctx, dprobs, dtopv, _):
+        probs, topi = ctx.saved_tensors
+        T, E = probs.shape
+        if dtopv is None:
+            dtopv = torch.zeros_like(topi, dtype=torch.float32)
+        dtopv = dtopv.float().contiguous()
+        if dprobs is not None:
+            dprobs = dprobs.float().contiguous()
+        dl = torch.empty(T, E, device=probs.device, dtype=torch.bfloat16)
+        ext().router_bwd(probs, dprobs, dtopv, topi, ctx.renorm, dl)
+        return dl, None, None, None
+
+
+def _router_kernel_ok(logits: torch.Tensor, top_k: int) -> bool:
+    return (logits.is_cuda and logits.dtype == torch.bfloat16 and logits.dim() == 2 and logits.stride(1) == 1
+            and 1 <= logits.shape[1] <= 256 and 1 <= top_k <= min(16, logits.shape[1]))
+
+
+def route(x2: torch.Tensor, w: torch.Tensor, top_k: int, norm_topk_prob: bool, counts: torch.Tensor | None = None):
+    """Returns (probs [T, E] fp32 softmax, top-k weights [T, k], top-k index [T, k]).
+    On CUDA ``counts`` (int32 [E]), when given, accumulates the route histogram."""
     from .functional import linear as _linear
 
     logits = _linear(x2.contiguous(), w) if (x2.is_cuda and _gemm_ok(x2, w)) else F.linear(x2, w)
+    if _router_kernel_ok(logits, top_k):
+        return _RouterFn.apply(logits, top_k, bool(norm_topk_prob), counts)
     probs = torch.softmax(logits, dim=-1, dtype=torch.float32)
     top_v, top_i = torch.topk(probs, top_k, dim=-1)
     if norm_topk_prob:
@@ -165,9 +206,49 @@ def experts_forward(x2: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: 
     return out.index_add(0, tok, ys)
 
 
+class _AuxStatsFn(torch.autograd.Function):
+    """Per-expert statistics of the load-balancing loss over recorded router
+    probabilities p [R, E]: (top-k selection counts of s = softmax(p), sums of s
+    over the rows); differentiable in the sums (csrc/router.cu)."""
+
+    @staticmethod
+    def forward(ctx, probs, top_k):
+        E = probs.shape[1]
+        counts = torch.zeros(E, device=probs.device, dtype=torch.float32)
+        ssum = torch.zeros(E, device=probs.device, dtype=torch.float32)
+        ext().aux_stats(probs, top_k, counts, ssum)
+        ctx.save_for_backward(probs)
+        ctx.mark_non_differentiable(counts)
+        return counts, ssum
+
+    @staticmethod
+    def backward(ctx, _, gsum):
+        (probs,) = ctx.saved_tensors
+        dp = torch.empty_like(probs)
+        ext().aux_stats_bwd(probs, gsum.float().contiguous(), dp)
+        return dp, None
+
+
+def aux_loss_stats(probs: torch.Tensor, top_k: int):
+    """(counts [E], sums [E]) of the double-softmax load-balancing loss; the
+    counts sum the top-k selections of softmax(probs) over rows and slots."""
+    E = probs.shape[-1]
+    if probs.is_cuda and probs.dtype == torch.float32 and probs.dim() == 2 and 1 <= E <= 256 \
+            and 1 <= top_k <= min(16, E):
+        return _AuxStatsFn.apply(probs.contiguous(), top_k)
+    s = torch.softmax(probs, dim=-1)
+    selected = torch.topk(s, top_k, dim=-1).indices
+    counts = F.one_hot(selected, probs.shape[1]).float().sum(dim=(0, 1))
+    return counts, s.sum(dim=0)
+
+
 def load_balancing_loss(router_probs: tuple, num_experts: int, top_k: int) -> torch.Tensor:
     """HF load_balancing_loss_func (no attention mask), double softmax included."""
     cat = torch.cat([p.to(router_probs[0].device) for p in router_probs], dim=0)
+    if cat.is_cuda:
+        counts, ssum = aux_loss_stats(cat.float(), top_k)
+        R = cat.shape[0]
+        return torch.sum((counts / R) * (ssum / R)) * num_experts
     routing_weights = torch.softmax(cat, dim=-1)
     _, selected = torch.topk(routing_weights, top_k, dim=-1)
     expert_mask = F.one_hot(selected, num_experts)

@@ -76,16 +76,15 @@ def sequence_parallel_load_balancing_loss(router_logits, *, num_experts: int, to
     """Switch aux loss over the SP-global token population."""
     if not router_logits:
         return None
+    from ...ops.moe import aux_loss_stats
+
     logits = torch.cat(tuple(router_logits), dim=0)
-    probs = torch.softmax(logits, dim=-1)
-    selected = torch.topk(probs, top_k, dim=-1).indices
-    assign = torch.nn.functional.one_hot(selected, num_experts).float()
-    counts = assign.sum(dim=0)
-    prob_sum = probs.sum(dim=0)
+    # per-expert top-k counts and sums of softmax(probs) (one fused kernel on CUDA)
+    counts, prob_sum = aux_loss_stats(logits.float(), top_k)
     ntok = torch.tensor(logits.shape[0], dtype=torch.float32, device=logits.device)
     with collective_profile("sp_all_reduce", value=counts, mode="router_counts", detail="load_balancing_loss"):
         dist.all_reduce(counts, group=group)
     with collective_profile("sp_all_reduce", value=ntok, mode="token_count", detail="load_balancing_loss"):
         dist.all_reduce(ntok, group=group)
     prob_sum = _AllReduceForwardIdentityBackward.apply(prob_sum, group)
-    return num_experts * torch.sum((counts / ntok) * (prob_sum / ntok).unsqueeze(0))
+    return num_experts * torch.sum((counts / ntok) * (prob_sum / ntok))

@@ -498,3 +498,54 @@ def test_grouped_expert_gemms_match_fp32():
     assert _rel_err(w_gu.grad, guf.grad) < 3e-2
     assert _rel_err(w_d.grad, df.grad) < 3e-2
     assert w_gu.grad[0].abs().max().item() == 0 and w_d.grad[4].abs().max().item() == 0  # empty experts
+
+
+@pytest.mark.parametrize("T,E,K,renorm", [(1000, 128, 8, True), (333, 60, 4, False), (64, 256, 16, True)])
+def test_router_matches_torch(T, E, K, renorm):
+    """Fused softmax / top-k / renorm / histogram and its backward against fp32 PyTorch."""
+    from parallel_b200.ops.moe import _RouterFn
+
+    torch.manual_seed(11)
+    logits = (torch.randn(T, E, device="cuda") * 2).to(torch.bfloat16).requires_grad_(True)
+    counts = torch.zeros(E, device="cuda", dtype=torch.int32)
+    probs, topv, topi = _RouterFn.apply(logits, K, renorm, counts)
+    ref_l = logits.detach().float().requires_grad_(True)
+    ref_p = torch.softmax(ref_l, dim=-1)
+    top_ref, _ = torch.topk(ref_p.detach(), K, dim=-1)
+    assert torch.allclose(probs, ref_p, atol=1e-6, rtol=1e-5)
+    # bf16 logits tie often; the order among equal probabilities is unspecified,
+    # so check that the chosen experts carry the top-k probabilities (largest first)
+    assert all(len(set(r)) == K for r in topi.tolist())
+    assert torch.allclose(ref_p.detach().gather(1, topi), top_ref, atol=1e-6, rtol=1e-5)
+    ref_v = ref_p.gather(1, topi)
+    if renorm:
+        ref_v = ref_v / ref_v.sum(dim=-1, keepdim=True)
+    assert torch.allclose(topv, ref_v, atol=1e-6, rtol=1e-5)
+    assert torch.equal(counts.long(), torch.bincount(topi.reshape(-1), minlength=E))
+    wv, wp = torch.randn(T, K, device="cuda"), torch.randn(T, E, device="cuda")
+    ((topv * wv).sum() + (probs * wp).sum()).backward()
+    ((ref_v * wv).sum() + (ref_p * wp).sum()).backward()
+    assert _rel_err(logits.grad, ref_l.grad) < 1e-2
+    _check_no_device_error()
+
+
+def test_aux_loss_stats_match_torch():
+    """Double-softmax load-balancing loss statistics and their gradient."""
+    from parallel_b200.ops.moe import load_balancing_loss
+
+    torch.manual_seed(12)
+    E, K = 128, 8
+    probs = [torch.softmax(torch.randn(500, E, device="cuda") * 3, dim=-1).requires_grad_(True) for _ in range(3)]
+    loss = load_balancing_loss(tuple(probs), E, K)
+    ref_probs = [p.detach().clone().requires_grad_(True) for p in probs]
+    cat = torch.cat(ref_probs, dim=0)
+    rw = torch.softmax(cat, dim=-1)
+    _, sel = torch.topk(rw, K, dim=-1)
+    tpe = torch.nn.functional.one_hot(sel, E).float().mean(dim=0)
+    ref = torch.sum(tpe * rw.mean(dim=0).unsqueeze(0)) * E
+    assert abs(loss.item() - ref.item()) < 1e-5 * max(1.0, abs(ref.item()))
+    loss.backward()
+    ref.backward()
+    for p, r in zip(probs, ref_probs):
+        assert _rel_err(p.grad, r.grad) < 1e-4
+    _check_no_device_error()
