@@ -204,6 +204,84 @@ __global__ void row_gather_kernel(uint8_t* __restrict__ dst, int64_t ld_dst, con
   for (int64_t v = lane; v < vecs; v += 32) d4[v] = s4[v];
 }
 
+// Sliced small all-reduce: block b owns units [lo, hi).  It bumps its own
+// epoch counter, stores its slice of `in` into slot `rank` of parity
+// (epoch & 1) in every peer's region, publishes the epoch in each peer's flag
+// [b][rank] (release, system scope), waits - bounded - for every peer's flag
+// [b][j], then combines the `world` slots of its slice from its own region.
+// The grid is the same for every call, so all blocks share the call's epoch.
+// A peer raises its call-k flag only from its kernel k, which starts after its
+// kernel k-1 - every read of the parity that call k+1 overwrites - has
+// finished: two parities make the exchange safe without a closing barrier.
+__global__ void small_ar_kernel(const float* __restrict__ in, float* __restrict__ out, int64_t units, int op,
+                                PeerBases bases, int rank, int world, int64_t cap, uint32_t* __restrict__ epochs,
+                                uint64_t limit_ns, int* err) {
+  const int b = blockIdx.x;
+  const int uf = op == kArLse3 ? 3 : 1;  // floats per unit
+  const int64_t per = (units + gridDim.x - 1) / gridDim.x;
+  const int64_t lo = (int64_t)b * per, hi = min(units, lo + per);
+  __shared__ uint32_t s_epoch;
+  if (threadIdx.x == 0) {
+    s_epoch = epochs[b] + 1u;
+    epochs[b] = s_epoch;
+  }
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  const int par = epoch & 1;
+  const int64_t slot_floats = cap * uf;
+  const int64_t flags_off = 2 * (int64_t)world * slot_floats;  // in floats (uint32 flags follow the data)
+  // push this rank's slice into every peer (planar layout: plane q of unit u at q * cap + u)
+  for (int j = 0; j < world; ++j) {
+    float* dst = reinterpret_cast<float*>(bases.p[j]) + ((int64_t)par * world + rank) * slot_floats;
+    for (int q = 0; q < uf; ++q)
+      for (int64_t u = lo + threadIdx.x; u < hi; u += blockDim.x) dst[q * cap + u] = in[q * units + u];
+  }
+  __syncthreads();
+  if (threadIdx.x < world) {
+    const int j = threadIdx.x;
+    __threadfence_system();
+    uint32_t* flag = reinterpret_cast<uint32_t*>(reinterpret_cast<float*>(bases.p[j]) + flags_off) +
+                     b * world + rank;
+    st_release_sys(flag, epoch);
+    const uint32_t* mine =
+        reinterpret_cast<const uint32_t*>(reinterpret_cast<const float*>(bases.p[rank]) + flags_off) + b * world + j;
+    const uint64_t t0 = globaltimer();
+    uint32_t n = 0;
+    while ((int32_t)(ld_acquire_sys(mine) - epoch) < 0) {
+      if ((++n & 255u) == 0) {
+        if (*((volatile int*)err) != 0) break;
+        if (globaltimer() - t0 > limit_ns) {
+          record_error(err, kErrPeerTimeout);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const float* base = reinterpret_cast<const float*>(bases.p[rank]) + (int64_t)par * world * slot_floats;
+  for (int64_t u = lo + threadIdx.x; u < hi; u += blockDim.x) {
+    if (op == kArLse3) {
+      float m = -INFINITY;
+      for (int j = 0; j < world; ++j) m = fmaxf(m, base[j * slot_floats + u]);
+      float se = 0.f, t = 0.f;
+      for (int j = 0; j < world; ++j) {
+        const float* sl = base + j * slot_floats;
+        se += sl[cap + u] * __expf(sl[u] - m);
+        t += sl[2 * cap + u];
+      }
+      out[u] = m + __logf(se);
+      out[units + u] = t;
+    } else {
+      float acc = op == kArMax ? -INFINITY : 0.f;
+      for (int j = 0; j < world; ++j) {
+        const float v = base[j * slot_floats + u];
+        acc = op == kArMax ? fmaxf(acc, v) : acc + v;
+      }
+      out[u] = acc;
+    }
+  }
+}
+
 }  // namespace
 
 void signal_barrier(const uint64_t* peer_pads_dev, int rank, int world, int slot_base, uint32_t* epoch_ctr,
@@ -259,6 +337,27 @@ void row_gather(void* dst, int64_t ld_dst_bytes, const int32_t* rank, const int6
   const int64_t threads = n * 32;
   row_gather_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(reinterpret_cast<uint8_t*>(dst), ld_dst_bytes, rank,
                                                                       row, peers, ld_src_bytes, row_bytes / 16, n);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace pb
+
+namespace pb {
+
+int64_t small_ar_region_floats(int world, int64_t cap_units, int op_unit_floats) {
+  return 2 * (int64_t)world * cap_units * op_unit_floats + (int64_t)kSmallArMaxBlocks * world;
+}
+
+void small_all_reduce(const float* in, float* out, int64_t units, int op, const PeerBases& bases, int rank, int world,
+                      int64_t cap_units, uint32_t* block_epochs, uint64_t limit_ns, cudaStream_t s) {
+  PB_CHECK(world >= 1 && world <= kMaxPeers && rank >= 0 && rank < world, "small_all_reduce: rank / world");
+  PB_CHECK(units <= cap_units, "small_all_reduce: more units than the buffer holds");
+  PB_CHECK(op == kArSum || op == kArMax || op == kArLse3, "small_all_reduce: op");
+  if (units == 0) return;
+  // a fixed grid: every block takes part in every call, so all block epochs
+  // (and the parity of the data slots) stay equal from call to call
+  small_ar_kernel<<<kSmallArBlocks, 256, 0, s>>>(in, out, units, op, bases, rank, world, cap_units, block_epochs, limit_ns,
+                                         error_word());
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -48,4 +48,17 @@ void row_gather_sum(void* dst, int64_t ld_dst, int64_t n_tokens, int k_per, cons
 void row_gather(void* dst, int64_t ld_dst_bytes, const int32_t* rank, const int64_t* row, const PeerBases& peers,
                 int64_t ld_src_bytes, int64_t row_bytes, int64_t n, cudaStream_t s);
 
+// Small all-reduce of fp32 data over symmetric buffers (grad-norm partials,
+// finite flags, loss statistics, the vocab-parallel log-sum-exp merge).
+// Every rank's region (at bases.p[r]) holds two parities of `world` source
+// slots of `cap` units, then the block flags: uint32 [kSmallArMaxBlocks][world].
+// A unit is one float (SUM / MAX) or one row of three planes (LSE3: max,
+// sum-exp, target -> out = [lse | target sum], rows planes each).
+constexpr int kSmallArMaxBlocks = 64;
+constexpr int kSmallArBlocks = 16;  // the grid of every call (<= kSmallArMaxBlocks)
+enum SmallArOp { kArSum = 0, kArMax = 1, kArLse3 = 2 };
+int64_t small_ar_region_floats(int world, int64_t cap_units, int op_unit_floats);
+void small_all_reduce(const float* in, float* out, int64_t units, int op, const PeerBases& bases, int rank, int world,
+                      int64_t cap_units, uint32_t* block_epochs, uint64_t limit_ns, cudaStream_t s);
+
 }  // namespace pb

@@ -79,6 +79,33 @@ void p2p_reduce(const std::vector<std::vector<int64_t>>& src, const std::vector<
   }
 }
 
+int64_t small_ar_region_floats(int64_t world, int64_t cap_units) {
+  return pb::small_ar_region_floats((int)world, cap_units, 3);
+}
+
+// op: 0 sum, 1 max (fp32 [units]); 2 lse3 (in [3, units]: max, sum-exp,
+// target; out [2, units]: log-sum-exp, target sum).  bases: every rank's
+// region (symmetric, small_ar_region_floats(world, cap) floats); epochs: int32
+// [kSmallArMaxBlocks] device counters of this region.
+void small_all_reduce(const at::Tensor& in, at::Tensor& out, int64_t units, int64_t op,
+                      const std::vector<int64_t>& bases, int64_t rank, int64_t cap_units, at::Tensor& epochs,
+                      double limit_s) {
+  TORCH_CHECK(in.is_cuda() && in.scalar_type() == at::kFloat && in.is_contiguous() && out.is_cuda() &&
+              out.scalar_type() == at::kFloat && out.is_contiguous(), "small_all_reduce: contiguous fp32 CUDA");
+  const int64_t uf = op == pb::kArLse3 ? 3 : 1, of = op == pb::kArLse3 ? 2 : 1;
+  TORCH_CHECK(in.numel() >= units * uf && out.numel() >= units * of, "small_all_reduce: tensor sizes");
+  TORCH_CHECK(epochs.is_cuda() && epochs.scalar_type() == at::kInt && epochs.numel() >= pb::kSmallArMaxBlocks,
+              "small_all_reduce: int32 epoch counters");
+  TORCH_CHECK(bases.size() >= 1 && bases.size() <= (size_t)pb::kMaxPeers, "small_all_reduce: world");
+  pb::PeerBases pb_{};
+  for (size_t i = 0; i < bases.size(); ++i) pb_.p[i] = reinterpret_cast<void*>(bases[i]);
+  const c10::cuda::CUDAGuard g(in.device());
+  // slot capacity in units of this op: the region was sized for cap_units rows of 3 floats
+  pb::small_all_reduce(in.data_ptr<float>(), out.data_ptr<float>(), units, (int)op, pb_, (int)rank,
+                       (int)bases.size(), op == pb::kArLse3 ? cap_units : 3 * cap_units,
+                       reinterpret_cast<uint32_t*>(epochs.data_ptr<int>()), (uint64_t)(limit_s * 1e9), cur_stream());
+}
+
 void wait_flag(const at::Tensor& flag, int64_t target, double limit_s, at::Tensor& status) {
   TORCH_CHECK(flag.is_cuda() && flag.scalar_type() == at::kInt && status.is_cuda() &&
               status.scalar_type() == at::kInt, "wait_flag: int32 CUDA tensors");
@@ -155,6 +182,8 @@ void register_comm(pybind11::module& m) {
   m.def("p2p_copy", &p2p_copy);
   m.def("p2p_reduce", &p2p_reduce);
   m.def("wait_flag", &wait_flag);
+  m.def("small_ar_region_floats", &small_ar_region_floats);
+  m.def("small_all_reduce", &small_all_reduce);
   m.def("row_scatter", &row_scatter);
   m.def("row_gather_sum", &row_gather_sum);
   m.def("row_gather", &row_gather);

@@ -75,6 +75,64 @@ class SymmBuffer:
         ext().p2p_barrier(self.pads_dev, self.rank, self.world, channel * 8, self.epochs, channel, limit_s)
 
 
+class P2PSmallAllReduce:
+    """All-reduce of small fp32 vectors over NVLink peer memory in one kernel
+    (``csrc/comm.cu``: each block pushes its slice into every peer's symmetric
+    region, raises a per-block device epoch flag and sums its slice locally;
+    two parities of slots, no closing barrier, CUDA-graph safe).  Used for the
+    gradient-norm / finite-flag reductions, the load-balancing-loss statistics
+    and the vocab-parallel log-sum-exp merge instead of NCCL all-reduces.
+
+    ``get(group, device)`` returns the instance of a group (creating it is
+    collective: every rank of the group must make the first call together)."""
+
+    _instances: dict = {}
+    MAX_BLOCKS = 64
+
+    def __init__(self, group, device, cap_units: int = 16384):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.cap = cap_units
+        self.limit_s = float(os.environ.get("PB_P2P_TIMEOUT_S", "60"))
+        self.buf = SymmBuffer(ext().small_ar_region_floats(self.world, cap_units), torch.float32, device, group)
+        self.bases = list(self.buf.peer_ptrs)
+        self.epochs = torch.zeros(self.MAX_BLOCKS, dtype=torch.int32, device=device)
+
+    @classmethod
+    def get(cls, group, device):
+        if not (device.type == "cuda" and p2p_supported(group)):
+            return None
+        key = (id(group), device.index)
+        inst = cls._instances.get(key)
+        if inst is None:
+            inst = cls._instances[key] = cls(group, device)
+        return inst
+
+    def _run(self, x: torch.Tensor, out: torch.Tensor, units: int, op: int) -> None:
+        ext().small_all_reduce(x, out, units, op, self.bases, self.rank, self.cap, self.epochs, self.limit_s)
+
+    def all_reduce_(self, t: torch.Tensor, op: str = "sum") -> torch.Tensor:
+        """In-place SUM / MAX of an fp32 CUDA tensor (at most 3 x cap elements)."""
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise TypeError("P2PSmallAllReduce works on contiguous fp32 tensors")
+        if t.numel() > 3 * self.cap:
+            raise ValueError(f"{t.numel()} elements exceed the {3 * self.cap}-element buffer")
+        self._run(t, t, t.numel(), {"sum": 0, "max": 1}[op])
+        return t
+
+    def lse_merge(self, row_max: torch.Tensor, row_sumexp: torch.Tensor, row_target: torch.Tensor):
+        """Global (log-sum-exp, target) per row from every rank's local row max,
+        sum of exp(x - local max) and target-logit contribution."""
+        rows = row_max.numel()
+        if rows > self.cap:
+            raise ValueError(f"{rows} rows exceed the {self.cap}-row buffer")
+        packed = torch.stack([row_max.float(), row_sumexp.float(), row_target.float()]).contiguous()
+        out = torch.empty(2, rows, device=packed.device, dtype=torch.float32)
+        self._run(packed, out, rows, 2)
+        return out[0], out[1]
+
+
 @dataclass
 class _P2PHandle:
     event: Any

@@ -277,12 +277,7 @@ class ParallelEngine:
                 by_dtype[g.dtype][1].append(w)
             for gs, ws in by_dtype.values():
                 ext().sumsq(gs, ws, sq, flag)
-            for group in self._norm_groups():
-                dist.all_reduce(sq, op=dist.ReduceOp.SUM, group=group)
-            for dim in (Strategies.DP_REPLICATE, Strategies.TP, Strategies.DP_SHARD):
-                group = self.pconfig.group(dim)
-                if group is not None:
-                    dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
+            sq, flag = self._reduce_norm_and_flag(sq, flag)
             scale = None
             if max_norm > 0.0:
                 scale = torch.empty(1, dtype=torch.float32, device=self.device)
@@ -322,6 +317,40 @@ class ParallelEngine:
                 self.optimizer.step()
         self.optimizer.zero_grad(set_to_none=True)
         self.fsdp_wrapper.zero_grad()
+
+    def _reduce_norm_and_flag(self, sq: torch.Tensor, flag: torch.Tensor):
+        """Sum the squared-gradient partial over the norm groups (TP, then the
+        shard group) and the non-finite flag over every data / model group.
+        On CUDA with NVLink peer access both travel in one peer-memory kernel
+        per group ([sq, flag] summed; flag > 0 means non-finite anywhere);
+        otherwise NCCL all-reduces (SUM, MAX)."""
+        norm_groups = self._norm_groups()
+        flag_groups = [g for dim in (Strategies.DP_REPLICATE, Strategies.TP, Strategies.DP_SHARD)
+                       if (g := self.pconfig.group(dim)) is not None]
+        groups = []
+        for g in norm_groups + flag_groups:
+            if all(g is not h for h in groups) and dist.get_world_size(g) > 1:
+                groups.append(g)
+        small = None
+        if groups and self.device.type == "cuda" and _cfg_get(self.cfg.engine, "collectives", "auto") != "nccl":
+            from .comm.p2p import P2PSmallAllReduce
+
+            small = [P2PSmallAllReduce.get(g, self.device) for g in groups]
+            if any(x is None for x in small):
+                small = None
+        if small is None:
+            for group in norm_groups:
+                dist.all_reduce(sq, op=dist.ReduceOp.SUM, group=group)
+            for group in flag_groups:
+                dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
+            return sq, flag
+        packed = torch.cat([sq.reshape(1), flag.reshape(1).to(torch.float32)])
+        for g, ar in zip(groups, small):
+            if any(g is h for h in norm_groups):
+                ar.all_reduce_(packed, "sum")
+            else:  # replicas hold the same gradients: only the flag is combined
+                ar.all_reduce_(packed[1:], "sum")
+        return packed[:1], (packed[1:] > 0).to(torch.int32)
 
     def _average_gradients(self):
         """All-reduce mean of gradients over the replicate group."""

@@ -98,7 +98,7 @@ class ModelParallelWrapper:
         h = getattr(outputs, "hidden_states", None)
         if outputs.logits is None and h is not None and h.is_cuda:
             loss = vocab_parallel_lm_head_ce(h, self.model.lm_head.weight, labels, self.group,
-                                             self.model.vocab_start)
+                                             self.model.vocab_start, collectives=self.collectives)
         else:
             logits = outputs.logits if outputs.logits is not None else self.model.lm_head(h)
             loss = self.token_loss(logits, labels)
@@ -108,7 +108,8 @@ class ModelParallelWrapper:
             if self.plan.capabilities.sequence_parallel and self.plan.capabilities.expert_parallel:
                 aux = sequence_parallel_load_balancing_loss(getattr(outputs, "router_logits", None),
                                                             num_experts=cfg.num_experts,
-                                                            top_k=cfg.num_experts_per_tok, group=self.group)
+                                                            top_k=cfg.num_experts_per_tok, group=self.group,
+                                                            collectives=self.collectives)
             else:
                 from ...ops.moe import load_balancing_loss
 

@@ -95,7 +95,7 @@ def vocab_parallel_cross_entropy(local_logits, labels, *, tp_mesh, vocab_size: i
 
 class _VocabParallelLMHeadCE(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, h, w, labels, group, v0, block_bytes):
+    def forward(ctx, h, w, labels, group, v0, block_bytes, small):
         T, H = h.shape
         V = w.shape[0]
         labels = labels.reshape(-1).contiguous()
@@ -113,14 +113,22 @@ class _VocabParallelLMHeadCE(torch.autograd.Function):
             mx = torch.empty(r1 - r0, device=h.device)
             se = torch.empty(r1 - r0, device=h.device)
             ext().ce_row_stats(logits, mx, se)
-            gm = mx.clone()
-            dist.all_reduce(gm, op=dist.ReduceOp.MAX, group=group)
-            se = se * torch.exp(mx - gm)
-            dist.all_reduce(se, op=dist.ReduceOp.SUM, group=group)
-            lse = gm + torch.log(se)
-            tgt = torch.empty(r1 - r0, device=h.device)
-            ext().ce_fwd_bwd(logits, lb, v0, inv, lse, True, tgt, None, True)
-            dist.all_reduce(tgt, op=dist.ReduceOp.SUM, group=group)
+            if small is not None:
+                # one peer-memory kernel merges (max, sum-exp, target) of every rank
+                local = lb - v0
+                inside = (lb != IGNORE) & (local >= 0) & (local < V)
+                tl = logits.gather(1, local.clamp(0, V - 1)[:, None])[:, 0].float()
+                lse, tgt = small.lse_merge(mx, se, torch.where(inside, tl, torch.zeros_like(tl)))
+                ext().ce_fwd_bwd(logits, lb, v0, inv, lse, True, None, None, True)
+            else:
+                gm = mx.clone()
+                dist.all_reduce(gm, op=dist.ReduceOp.MAX, group=group)
+                se = se * torch.exp(mx - gm)
+                dist.all_reduce(se, op=dist.ReduceOp.SUM, group=group)
+                lse = gm + torch.log(se)
+                tgt = torch.empty(r1 - r0, device=h.device)
+                ext().ce_fwd_bwd(logits, lb, v0, inv, lse, True, tgt, None, True)
+                dist.all_reduce(tgt, op=dist.ReduceOp.SUM, group=group)
             valid = lb != IGNORE
             loss_sum += torch.where(valid, lse - tgt, torch.zeros_like(lse)).sum()
             G.linear_dgrad(logits, w, out=dh[r0:r1])
@@ -134,14 +142,24 @@ class _VocabParallelLMHeadCE(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         dh, dw = ctx.saved_tensors
-        return dh * g.to(dh.dtype), dw * g.to(dw.dtype), None, None, None, None
+        return dh * g.to(dh.dtype), dw * g.to(dw.dtype), None, None, None, None, None
 
 
-def vocab_parallel_lm_head_ce(h, w_local, labels, group, vocab_start: int, block_bytes: int = 4 << 30):
+def vocab_parallel_lm_head_ce(h, w_local, labels, group, vocab_start: int, block_bytes: int = 4 << 30,
+                              collectives: str = "auto"):
     """Mean CE of ``h @ w_local.T`` whose vocab is sharded over ``group`` (CUDA).
 
     ``h`` [T, H] (the gathered hidden states, identical on every TP rank);
     the returned gradient of ``h`` is this rank's partial, to be summed over
-    the TP group by the caller's ``copy_to_tp`` boundary."""
+    the TP group by the caller's ``copy_to_tp`` boundary.  With NVLink peer
+    access (``collectives`` not "nccl") the per-block statistics of all ranks
+    are merged by one peer-memory kernel instead of three NCCL all-reduces."""
+    small = None
+    if collectives != "nccl":
+        from ..comm.p2p import P2PSmallAllReduce
+
+        small = P2PSmallAllReduce.get(group, h.device)
+        if small is not None and h.reshape(-1, h.shape[-1]).shape[0] > small.cap:
+            small = None
     return _VocabParallelLMHeadCE.apply(h.reshape(-1, h.shape[-1]).contiguous(), w_local, labels, group,
-                                        vocab_start, block_bytes)
+                                        vocab_start, block_bytes, small)

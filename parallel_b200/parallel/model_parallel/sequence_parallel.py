@@ -60,20 +60,31 @@ class SequenceParallelRuntime:
 
 
 class _AllReduceForwardIdentityBackward(torch.autograd.Function):
+    """SUM over the group in forward, identity in backward (the reference's
+    semantics for the SP router-probability sums).  ``small`` (a
+    P2PSmallAllReduce) runs it as one peer-memory kernel instead of NCCL."""
+
     @staticmethod
-    def forward(ctx, value, group):
+    def forward(ctx, value, group, small=None):
         out = value.contiguous().clone()
-        with collective_profile("sp_all_reduce", value=out, mode="router_probability", detail="load_balancing_loss"):
-            dist.all_reduce(out, group=group)
+        with collective_profile("sp_all_reduce", value=out, mode="router_statistics", detail="load_balancing_loss"):
+            if small is not None:
+                small.all_reduce_(out, "sum")
+            else:
+                dist.all_reduce(out, group=group)
         return out
 
     @staticmethod
     def backward(ctx, g):
-        return g, None
+        return g, None, None
 
 
-def sequence_parallel_load_balancing_loss(router_logits, *, num_experts: int, top_k: int, group):
-    """Switch aux loss over the SP-global token population."""
+def sequence_parallel_load_balancing_loss(router_logits, *, num_experts: int, top_k: int, group,
+                                          collectives: str = "auto"):
+    """Switch aux loss over the SP-global token population.  The per-expert
+    top-k counts, the sums of softmax(probs) and the token count travel in
+    one all-reduce (one peer-memory kernel on CUDA with NVLink), where the
+    reference issues three (sequence_parallel.py:239-280)."""
     if not router_logits:
         return None
     from ...ops.moe import aux_loss_stats
@@ -81,10 +92,13 @@ def sequence_parallel_load_balancing_loss(router_logits, *, num_experts: int, to
     logits = torch.cat(tuple(router_logits), dim=0)
     # per-expert top-k counts and sums of softmax(probs) (one fused kernel on CUDA)
     counts, prob_sum = aux_loss_stats(logits.float(), top_k)
-    ntok = torch.tensor(logits.shape[0], dtype=torch.float32, device=logits.device)
-    with collective_profile("sp_all_reduce", value=counts, mode="router_counts", detail="load_balancing_loss"):
-        dist.all_reduce(counts, group=group)
-    with collective_profile("sp_all_reduce", value=ntok, mode="token_count", detail="load_balancing_loss"):
-        dist.all_reduce(ntok, group=group)
-    prob_sum = _AllReduceForwardIdentityBackward.apply(prob_sum, group)
-    return num_experts * torch.sum((counts / ntok) * (prob_sum / ntok))
+    ntok = torch.full((1,), float(logits.shape[0]), dtype=torch.float32, device=logits.device)
+    small = None
+    if collectives != "nccl" and logits.is_cuda:
+        from ..comm.p2p import P2PSmallAllReduce
+
+        small = P2PSmallAllReduce.get(group, logits.device)
+    E = counts.numel()
+    packed = _AllReduceForwardIdentityBackward.apply(torch.cat([counts.detach(), prob_sum, ntok]), group, small)
+    counts, prob_sum, ntok = packed[:E], packed[E:2 * E], packed[2 * E]
+    return num_experts * torch.sum((counts.detach() / ntok.detach()) * (prob_sum / ntok.detach()))

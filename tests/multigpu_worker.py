@@ -120,9 +120,80 @@ def main_sp():
     dist.destroy_process_group()
 
 
+def main_small():
+    """P2P small all-reduce (sum / max / log-sum-exp merge) against NCCL, over
+    varying sizes (both slot parities) and inside a replayed CUDA graph."""
+    from parallel_b200.ops._ext import check_device_errors
+    from parallel_b200.parallel.comm.p2p import P2PSmallAllReduce
+
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    rank = dist.get_rank()
+    group = dist.group.WORLD
+    ar = P2PSmallAllReduce.get(group, dev)
+    worst = 0.0
+    g = torch.Generator(device="cpu").manual_seed(100 + rank)
+    for n in (1, 2, 1000, 37, 40000, 5, 16384 * 3):
+        x = torch.randn(n, generator=g).to(dev)
+        for op, red in (("sum", dist.ReduceOp.SUM), ("max", dist.ReduceOp.MAX)):
+            ref = x.clone()
+            dist.all_reduce(ref, op=red)
+            got = ar.all_reduce_(x.clone(), op)
+            worst = max(worst, ((got - ref).abs().max() / (ref.abs().max() + 1e-12)).item())
+    for rows in (7, 2048, 8192):
+        m = torch.randn(rows, generator=g).to(dev) * 4
+        se = torch.rand(rows, generator=g).to(dev) + 0.5
+        tg = torch.randn(rows, generator=g).to(dev)
+        lse, tsum = ar.lse_merge(m, se, tg)
+        gm = m.clone()
+        dist.all_reduce(gm, op=dist.ReduceOp.MAX)
+        gs = se * torch.exp(m - gm)
+        dist.all_reduce(gs)
+        ref_lse = gm + torch.log(gs)
+        ref_t = tg.clone()
+        dist.all_reduce(ref_t)
+        worst = max(worst, ((lse - ref_lse).abs().max() / ref_lse.abs().max()).item(),
+                    ((tsum - ref_t).abs().max() / ref_t.abs().max()).item())
+    # graph replay: the epochs live on the device
+    x = torch.ones(300, device=dev) * (rank + 1)
+    y = torch.empty_like(x)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        y.copy_(x)
+        ar.all_reduce_(y, "sum")
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        y.copy_(x)
+        ar.all_reduce_(y, "sum")
+        ar.all_reduce_(y, "sum")
+    W = dist.get_world_size()
+    for i in range(3):
+        x.fill_(rank + 1 + i)
+        graph.replay()
+        torch.cuda.synchronize()
+        expect = W * sum(r + 1 + i for r in range(W))
+        worst = max(worst, abs(float(y[0]) - expect) / expect)
+    graph.reset()
+    check_device_errors()
+    t = torch.tensor([worst], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        with open(os.environ["PB_TEST_OUT"], "w") as f:
+            json.dump({"worst": t.item()}, f)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     if os.environ.get("PB_TEST_MODE") == "sp":
         return main_sp()
+    if os.environ.get("PB_TEST_MODE") == "small":
+        return main_small()
     local = int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))

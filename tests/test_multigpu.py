@@ -73,3 +73,16 @@ def test_p2p_expert_dispatch_matches_nccl(tmp_path):
     for a, b in zip(res["fused"], res["nccl"]):
         assert abs(a - b) < 2e-2 * max(1.0, abs(b)), res
     assert res["grad_rel_diff"] < 5e-2, res
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_p2p_small_all_reduce_matches_nccl(tmp_path):
+    """Peer-memory small all-reduce (sum, max, log-sum-exp merge) equals NCCL,
+    across sizes and inside a replayed CUDA graph."""
+    out = tmp_path / "res_small.json"
+    env = dict(os.environ, PB_TEST_OUT=str(out), PB_TEST_MODE="small", NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+           "--master-port", "29536", os.path.join(HERE, "multigpu_worker.py")]
+    subprocess.run(cmd, env=env, check=True, timeout=600)
+    res = json.loads(out.read_text())
+    assert res["worst"] < 1e-5, res
