@@ -70,57 +70,104 @@ __global__ void signal_barrier_kernel(const uint64_t* __restrict__ peer_pads, in
   }
 }
 
-__global__ void multi_copy_kernel(CopySegments segs) {
-  // flatten all segments into 16-byte vectors; grid-stride
-  int64_t total = segs.vec_start[segs.n];
-  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
-    int s = 0;
-    while (s + 1 < segs.n && segs.vec_start[s + 1] <= v) ++s;
-    const int64_t off = (v - segs.vec_start[s]) * 16;
-    const uint4 val = *reinterpret_cast<const uint4*>(segs.src[s] + off);
-    *reinterpret_cast<uint4*>(segs.dst[s] + off) = val;
+// Segment of vector v: the last s with vec_start[s] <= v (binary search over
+// the kernel-parameter table).
+template <typename Segs>
+__device__ __forceinline__ int find_seg(const Segs& segs, int64_t v) {
+  int lo = 0, hi = segs.n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (segs.vec_start[mid] <= v) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+constexpr int kCopyChunkVecs = 4096;  // 64 KB of 16-byte vectors per chunk
+constexpr int kCopyUnroll = 4;
+
+// Chunked gather: one block per 64 KB chunk (short-lived blocks: a copy that
+// overlaps compute never holds an SM for long, so the compute kernels' CTAs
+// find room as soon as they need it), the chunk's first segment found once,
+// and kCopyUnroll independent 16-byte loads in flight per thread (remote
+// NVLink loads need many outstanding requests).
+__global__ void __launch_bounds__(512) multi_copy_kernel(CopySegments segs) {
+  const int64_t total = segs.vec_start[segs.n];
+  {
+    const int64_t c = blockIdx.x;
+    const int64_t v0 = c * kCopyChunkVecs, v1 = min(total, v0 + kCopyChunkVecs);
+    int seg = find_seg(segs, v0 + threadIdx.x < v1 ? v0 + threadIdx.x : v0);
+    for (int64_t base = v0 + threadIdx.x; base < v1; base += kCopyUnroll * blockDim.x) {
+      uint4 val[kCopyUnroll];
+      uint8_t* dst[kCopyUnroll];
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u) {
+        const int64_t v = base + (int64_t)u * blockDim.x;
+        dst[u] = nullptr;
+        if (v < v1) {
+          while (seg + 1 < segs.n && segs.vec_start[seg + 1] <= v) ++seg;
+          const int64_t off = (v - segs.vec_start[seg]) * 16;
+          val[u] = *reinterpret_cast<const uint4*>(segs.src[seg] + off);
+          dst[u] = segs.dst[seg] + off;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u)
+        if (dst[u]) *reinterpret_cast<uint4*>(dst[u]) = val[u];
+    }
   }
 }
 
-// out[i] = scale * sum_j src_j[i] (+ out[i]);  8 bf16 per thread per step
-__global__ void reduce_segments_kernel(ReduceSegments segs, int world, float scale, bool accumulate) {
-  int64_t total = segs.vec_start[segs.n];
-  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
-    int s = 0;
-    while (s + 1 < segs.n && segs.vec_start[s + 1] <= v) ++s;
-    const int64_t off = (v - segs.vec_start[s]) * 8;  // elements
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int j = 0; j < world; ++j) {
-      const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(segs.src[j][s]) + off;
-      uint4 u = *reinterpret_cast<const uint4*>(src);
-      const uint32_t* p = &u.x;
+// out[i] = scale * sum_j src_j[i] (+ out[i]);  8 bf16 per vector, one block
+// per chunk as multi_copy (one segment search per chunk, monotone advance).
+__global__ void __launch_bounds__(512) reduce_segments_kernel(ReduceSegments segs, int world, float scale,
+                                                              bool accumulate) {
+  const int64_t total = segs.vec_start[segs.n];
+  {
+    const int64_t c = blockIdx.x;
+    const int64_t v0 = c * kCopyChunkVecs, v1 = min(total, v0 + kCopyChunkVecs);
+    int seg = find_seg(segs, v0 + threadIdx.x < v1 ? v0 + threadIdx.x : v0);
+    for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
+      while (seg + 1 < segs.n && segs.vec_start[seg + 1] <= v) ++seg;
+      const int64_t off = (v - segs.vec_start[seg]) * 8;  // elements
+      uint4 in[kMaxPeers];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float2 f = unpack_bf16x2(p[q]);
-        acc[2 * q] += f.x;
-        acc[2 * q + 1] += f.y;
+      for (int j = 0; j < kMaxPeers; ++j)
+        if (j < world) in[j] = *reinterpret_cast<const uint4*>(
+                           reinterpret_cast<const __nv_bfloat16*>(segs.src[j][seg]) + off);
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+      for (int j = 0; j < kMaxPeers; ++j) {
+        if (j >= world) break;
+        const uint32_t* p = &in[j].x;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(p[q]);
+          acc[2 * q] += f.x;
+          acc[2 * q + 1] += f.y;
+        }
       }
-    }
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(segs.dst[s]) + off;
-    if (accumulate) {
-      uint4 u = *reinterpret_cast<const uint4*>(dst);
-      const uint32_t* p = &u.x;
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(segs.dst[seg]) + off;
+      if (accumulate) {
+        const uint4 u = *reinterpret_cast<const uint4*>(dst);
+        const uint32_t* p = &u.x;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float2 f = unpack_bf16x2(p[q]);
-        acc[2 * q] = acc[2 * q] * scale + f.x;
-        acc[2 * q + 1] = acc[2 * q + 1] * scale + f.y;
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(p[q]);
+          acc[2 * q] = acc[2 * q] * scale + f.x;
+          acc[2 * q + 1] = acc[2 * q + 1] * scale + f.y;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] *= scale;
       }
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] *= scale;
+      uint4 o;
+      o.x = pack_bf16x2(acc[0], acc[1]);
+      o.y = pack_bf16x2(acc[2], acc[3]);
+      o.z = pack_bf16x2(acc[4], acc[5]);
+      o.w = pack_bf16x2(acc[6], acc[7]);
+      *reinterpret_cast<uint4*>(dst) = o;
     }
-    uint4 o;
-    o.x = pack_bf16x2(acc[0], acc[1]);
-    o.y = pack_bf16x2(acc[2], acc[3]);
-    o.z = pack_bf16x2(acc[4], acc[5]);
-    o.w = pack_bf16x2(acc[6], acc[7]);
-    *reinterpret_cast<uint4*>(dst) = o;
   }
 }
 
@@ -136,11 +183,6 @@ __global__ void wait_flag_kernel(const uint32_t* flag, uint32_t target, uint64_t
   }
 }
 
-int copy_grid(int64_t vecs) {
-  const int64_t cap = (int64_t)num_sms() * 8;
-  int64_t g = (vecs + 255) / 256;
-  return (int)std::max<int64_t>(1, std::min(g, cap));
-}
 
 // One warp per row: copy row_bytes from the local source row to the peer row.
 __global__ void row_scatter_kernel(const uint8_t* __restrict__ src, int64_t ld_src, const int64_t* __restrict__ src_row,
@@ -291,15 +333,21 @@ void signal_barrier(const uint64_t* peer_pads_dev, int rank, int world, int slot
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
+unsigned chunk_grid(int64_t vecs) {
+  const int64_t g = (vecs + kCopyChunkVecs - 1) / kCopyChunkVecs;
+  PB_CHECK(g < (int64_t)1 << 31, "p2p copy: too many chunks");
+  return (unsigned)std::max<int64_t>(1, g);
+}
+
 void multi_copy(const CopySegments& segs, cudaStream_t s) {
   if (segs.n == 0) return;
-  multi_copy_kernel<<<copy_grid(segs.vec_start[segs.n]), 256, 0, s>>>(segs);
+  multi_copy_kernel<<<chunk_grid(segs.vec_start[segs.n]), 512, 0, s>>>(segs);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
 void reduce_segments(const ReduceSegments& segs, int world, float scale, bool accumulate, cudaStream_t s) {
   if (segs.n == 0) return;
-  reduce_segments_kernel<<<copy_grid(segs.vec_start[segs.n]), 256, 0, s>>>(segs, world, scale, accumulate);
+  reduce_segments_kernel<<<chunk_grid(segs.vec_start[segs.n]), 512, 0, s>>>(segs, world, scale, accumulate);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

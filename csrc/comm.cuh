@@ -27,6 +27,8 @@ struct ReduceSegments {
 // Slot words used: [slot_base + r] for r in [0, world).
 void signal_barrier(const uint64_t* peer_pads_dev, int rank, int world, int slot_base, uint32_t* epoch_ctr,
                     uint64_t limit_ns, cudaStream_t s);
+// One short-lived 512-thread block per 64 KB chunk (they interleave with the
+// CTAs of concurrent compute kernels).
 void multi_copy(const CopySegments& segs, cudaStream_t s);
 void reduce_segments(const ReduceSegments& segs, int world, float scale, bool accumulate, cudaStream_t s);
 void wait_flag(const uint32_t* flag, uint32_t target, uint64_t limit_ns, int* status, cudaStream_t s);

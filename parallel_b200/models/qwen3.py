@@ -84,7 +84,10 @@ class Embedding(nn.Module):
         self.weight = nn.Parameter(torch.empty(num, dim))
 
     def forward(self, ids, vocab_start: int = 0, tied=None):
-        return Fx.embedding(ids, self.weight, vocab_start, tied)
+        # an FSDP wrapper may install a one-shot reader that fetches the rows of
+        # this batch from the row shards while the full table is still being gathered
+        reader = self.__dict__.pop("_sharded_lookup", None)
+        return Fx.embedding(ids, self.weight, vocab_start, tied, reader=reader)
 
 
 class RotaryEmbedding(nn.Module):

@@ -376,12 +376,16 @@ class TiedGrad:
 
 class _EmbeddingFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, ids, w, v0, tied):
+    def forward(ctx, ids, w, v0, tied, reader):
         flat = ids.reshape(-1)
         if not flat.is_contiguous():
             flat = flat.contiguous()
-        out = torch.empty(flat.numel(), w.shape[1], device=w.device, dtype=w.dtype)
-        ext().embedding_fwd(flat, w, out, v0)
+        if reader is not None:
+            # rows fetched by the caller's reader (FSDP: from the peers' row shards)
+            out = reader(flat)
+        else:
+            out = torch.empty(flat.numel(), w.shape[1], device=w.device, dtype=w.dtype)
+            ext().embedding_fwd(flat, w, out, v0)
         ctx.save_for_backward(flat)
         ctx.v0 = v0
         ctx.wshape = w.shape
@@ -407,16 +411,19 @@ class _EmbeddingFn(torch.autograd.Function):
                 pending = None
         if pending is not None:
             ext().embedding_bwd(sid, perm, dy2, pending, ctx.v0, True)
-            return None, None, None, None
+            return None, None, None, None, None
         gb = torch.zeros(ctx.wshape, device=dy.device, dtype=torch.bfloat16)
         ext().embedding_bwd(sid, perm, dy2, gb, ctx.v0, False)
-        return None, gb.to(ctx.wdtype), None, None
+        return None, gb.to(ctx.wdtype), None, None, None
 
 
-def embedding(ids: torch.Tensor, w: torch.Tensor, vocab_start: int = 0, tied: TiedGrad | None = None) -> torch.Tensor:
-    """Rows of ``w`` for ids in [vocab_start, vocab_start + len(w)), zeros elsewhere."""
+def embedding(ids: torch.Tensor, w: torch.Tensor, vocab_start: int = 0, tied: TiedGrad | None = None,
+              reader=None) -> torch.Tensor:
+    """Rows of ``w`` for ids in [vocab_start, vocab_start + len(w)), zeros elsewhere.
+    ``reader(flat_ids) -> rows`` (CUDA only) supplies the forward rows instead
+    of ``w``; the gradient still goes to ``w``."""
     if w.is_cuda:
-        return _EmbeddingFn.apply(ids, w, vocab_start, tied)
+        return _EmbeddingFn.apply(ids, w, vocab_start, tied, reader)
     if vocab_start == 0 and (ids.numel() == 0 or int(ids.max()) < w.shape[0]):
         return F.embedding(ids, w)
     local = ids - vocab_start

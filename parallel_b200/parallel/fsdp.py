@@ -27,6 +27,7 @@ Execution model (B200-first):
 from __future__ import annotations
 
 import copy
+import os
 from collections import OrderedDict
 from typing import Any, Optional
 
@@ -261,12 +262,66 @@ class FSDPWrapper:
 
         layer.forward = forward
 
+    def _deferred_root(self):
+        """(root unit, embedding meta, embedding module, final norm module) when
+        the root unit can be gathered in the background of the forward pass:
+        one root unit on the NVLink data plane holding the token embedding, no
+        tensor parallelism.  The embedding rows of the batch are then read
+        straight from the owners' shards (the table is row-sharded exactly as
+        a vocabulary-parallel embedding) and the full gather is waited for only
+        before the final norm / LM head."""
+        if getattr(self, "_deferred_root_info", 0) != 0:
+            return self._deferred_root_info
+        info = None
+        inner = getattr(self.model, "model", None)
+        emb = getattr(inner, "embed_tokens", None)
+        norm = getattr(inner, "norm", None)
+        ctx = getattr(self.model, "ctx", None)
+        if (os.environ.get("PB_DEFER_ROOT_GATHER", "1") != "0"
+                and len(self.root_units) == 1 and emb is not None and norm is not None and self.device.type == "cuda"
+                and getattr(self.root_units[0], "_p2p", None) is not None and getattr(ctx, "tp_size", 1) == 1
+                and getattr(self.coll, "name", "") == "p2p"):
+            root = self.root_units[0]
+            metas = [m for m in root.param_metas if m.parameter is emb.weight]
+            if metas and metas[0].parameter.dtype == torch.bfloat16 and (metas[0].shape[1] * 2) % 16 == 0:
+                info = (root, metas[0], emb, norm)
+                self._norm_hook = norm.register_forward_pre_hook(lambda mod, args: root.wait_for_prefetch())
+        self._deferred_root_info = info
+        return info
+
+    def _sharded_embedding_reader(self, root, meta):
+        buf = root._p2p
+        bases = [p + meta.bucket_offset * 2 for p in buf.peer_ptrs]
+        pr, H = meta.padded_rows, meta.shape[1]
+
+        def read(flat_ids):
+            from ..ops._ext import ext
+
+            rank = torch.div(flat_ids, pr, rounding_mode="floor")
+            row = flat_ids - rank * pr
+            out = torch.empty(flat_ids.numel(), H, device=flat_ids.device, dtype=torch.bfloat16)
+            ext().row_gather(out, rank.to(torch.int32), row.contiguous(), bases, H * 2)
+            return out
+
+        return read
+
     def _root_pre_forward(self, module, args):
         begin = getattr(self.coll, "begin_forward", None) if self.coll is not None else None
         if begin is not None:
             begin()
-        for u in self.root_units:
-            u.all_gather()
+        deferred = self._deferred_root()
+        if deferred is not None:
+            root, meta, emb, _ = deferred
+            # every rank's shards are current (its optimizer step is done) ...
+            root._p2p.barrier(0, self.coll.limit_s)
+            self.coll._need_barrier = False
+            # ... so the gather runs in the background and the batch's rows are
+            # read from the shards directly
+            root.prefetch()
+            emb._sharded_lookup = self._sharded_embedding_reader(root, meta)
+        else:
+            for u in self.root_units:
+                u.all_gather()
         nxt = self.root_units[-1].next_fwd if self.root_units else None
         if nxt is not None:
             nxt.prefetch()
@@ -688,3 +743,7 @@ class FSDPWrapper:
         if self._root_hook is not None:
             self._root_hook.remove()
             self._root_hook = None
+        if getattr(self, "_norm_hook", None) is not None:
+            self._norm_hook.remove()
+            self._norm_hook = None
+        self._deferred_root_info = 0
