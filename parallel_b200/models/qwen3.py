@@ -40,7 +40,9 @@ class ParallelContext:
     ep_rank: int = 0
     expert_runtime: Any = None  # ReplicatedTokenExpertParallel / SequenceParallelExpertParallel
     comm: Any = None  # model_parallel.comm_ops module (set by the wrapper)
-    fused_sp: Any = None  # FusedSequenceParallel (NVLink GEMM+collective kernels) or None
+    # NVLink GEMM + collective data plane of the TP group: FusedSequenceParallel
+    # under sequence parallelism, FusedTensorParallel without it, or None
+    fused_tp: Any = None
 
     @property
     def active(self) -> bool:
@@ -205,11 +207,12 @@ class DecoderLayer(nn.Module):
         ctx = self._ctx
         B, S = self._seq
         stash = getattr(self, "_attn_stash", None)
-        fsp = ctx.fused_sp if (ctx.sp and ctx.fused_sp is not None and x.is_cuda
-                               and ctx.fused_sp.supports(B, S, x.shape[-1])) else None
+        fsp = ctx.fused_tp if (ctx.tp_size > 1 and ctx.fused_tp is not None and x.is_cuda
+                               and ctx.fused_tp.supports(B, S, x.shape[-1])) else None
         if fsp is not None:
-            # sequence parallel on the fused NVLink kernels: the gathers run inside
-            # the column-parallel GEMMs, the reduce-scatters inside the row-parallel ones
+            # tensor / sequence parallel on the fused NVLink kernels: the gathers run
+            # inside the column-parallel GEMMs, the reduce-scatters (all-reduces
+            # without SP) inside the row-parallel ones
             from ..parallel.model_parallel.fused_sp import linear_reduce_scatter, sp_swiglu_mlp
 
             h = self.input_layernorm(x)

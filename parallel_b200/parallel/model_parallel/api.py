@@ -14,7 +14,7 @@ import torch
 
 from ...models.qwen3 import ParallelContext
 from . import comm_ops
-from .fused_sp import FusedSequenceParallel
+from .fused_sp import FusedSequenceParallel, FusedTensorParallel
 from .checkpoint import ComposedModelParallelCheckpoint, ModelParallelCheckpoint
 from .expert_parallel import (ExpertPartition, ReplicatedTokenExpertParallel, SequenceParallelExpertParallel,
                               verify_expert_modules)
@@ -65,8 +65,14 @@ class ModelParallelWrapper:
             # NVLink data plane: all-gather / reduce-scatter fused into the GEMMs
             if self.collectives != "nccl" and FusedSequenceParallel.available(self.group, device):
                 ctx = model.ctx
-                ctx.fused_sp = FusedSequenceParallel(self.group, device)
+                ctx.fused_tp = FusedSequenceParallel(self.group, device)
                 model.set_parallel_context(ctx)
+        elif self.collectives != "nccl" and FusedTensorParallel.available(self.group, device):
+            # TP without SP: GEMM -> all-reduce over NVLink for the row-parallel outputs
+            # and the column-parallel input gradients
+            ctx = model.ctx
+            ctx.fused_tp = FusedTensorParallel(self.group, device)
+            model.set_parallel_context(ctx)
         if self.plan.capabilities.expert_parallel:
             self.experts = ExpertPartition(model.config.num_experts, self.plan.expert_parallel_size,
                                            self.mesh.get_local_rank())

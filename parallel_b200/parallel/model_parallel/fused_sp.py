@@ -1,4 +1,4 @@
-"""Sequence-parallel collectives fused with their GEMMs over NVLink.
+"""Tensor- and sequence-parallel collectives fused with their GEMMs over NVLink.
 
 Megatron-style sequence parallelism surrounds every column-parallel GEMM with
 an all-gather of the sequence-sharded activations and every row-parallel GEMM
@@ -132,6 +132,87 @@ class FusedSequenceParallel:
             ext().p2p_reduce([[base + s * slot_elems * 2] for s in range(self.world)], [y.data_ptr()],
                              [slot_elems], 1.0, False)
         self.n_rs += 1
+        return y
+
+
+class FusedTensorParallel:
+    """The same data-plane interface for tensor parallelism WITHOUT sequence
+    parallelism, so the fused autograd Functions below serve both modes.  The
+    reference's non-SP TP all-reduces the row-parallel outputs in forward and
+    the column-parallel input gradients in backward (HF Rowwise / Colwise
+    styles, hf/integrations/tensor_parallel.py:702,845).  Here:
+
+    * ``all_gather_gemm``: the input is replicated, so the "gather" is the
+      identity and this is a plain GEMM (optionally with the SwiGLU epilogue);
+    * ``gemm_reduce_scatter`` is a GEMM -> all-reduce: the GEMM epilogue stores
+      every row of the partial product into its row owner's symmetric slot
+      over NVLink (the reduce-scatter's transfer rides inside the GEMM), the
+      owner sums its slots into a symmetric block, and every rank gathers the
+      reduced blocks of all owners.  Two signal barriers; buffers rotate over
+      two sets (a rank passing call k's barriers knows every rank finished
+      call k-1, so the set call k+1 overwrites is free)."""
+
+    def __init__(self, group, device: torch.device):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = device
+        self.limit_s = float(os.environ.get("PB_P2P_TIMEOUT_S", "60"))
+        self._rows = 0
+        self._cols = 0
+        self.rs = []   # 2 x SymmBuffer [world * rows_local, cols]: one receive slot per sender
+        self.red = []  # 2 x SymmBuffer [rows_local, cols]: this rank's reduced row block
+        self.n = 0
+
+    available = staticmethod(FusedSequenceParallel.available)
+
+    def supports(self, batch: int, seq: int, cols: int) -> bool:
+        return (batch * seq) % self.world == 0 and cols % 8 == 0
+
+    def _ensure(self, rows_local: int, cols: int) -> None:
+        if self.rs and rows_local <= self._rows and cols <= self._cols:
+            return
+        if self.rs:
+            raise RuntimeError("fused tensor parallel: buffers are sized by the first call; shapes grew "
+                               f"({self._rows}x{self._cols} -> {rows_local}x{cols})")
+        self._rows, self._cols = rows_local, cols
+        n = rows_local * cols
+        self.rs = [SymmBuffer(self.world * n, torch.bfloat16, self.device, self.group) for _ in range(2)]
+        self.red = [SymmBuffer(n, torch.bfloat16, self.device, self.group) for _ in range(2)]
+
+    def all_gather_gemm(self, x: torch.Tensor, b: torch.Tensor, batch: int, seq: int, *, b_mn: bool = False,
+                        swiglu_inter: int = 0, gu_out: torch.Tensor | None = None):
+        T = x.shape[0]
+        if swiglu_inter:
+            out = torch.empty(T, swiglu_inter, device=x.device, dtype=torch.bfloat16)
+            ext().gemm(x, b, out, False, False, EPI_SWIGLU, 1.0, gu_out, swiglu_inter, swiglu_inter)
+        else:
+            N = b.shape[1] if b_mn else b.shape[0]
+            out = torch.empty(T, N, device=x.device, dtype=torch.bfloat16)
+            ext().gemm(x, b, out, False, b_mn, EPI_STORE_BF16, 1.0)
+        return out, x
+
+    def gemm_reduce_scatter(self, a: torch.Tensor, b: torch.Tensor, batch: int, seq: int, *,
+                            b_mn: bool = False) -> torch.Tensor:
+        """y [M, N] = all_reduce(a @ b^T (or @ b)) over the group (see the class docstring)."""
+        M = a.shape[0]
+        N = b.shape[1] if b_mn else b.shape[0]
+        rows_local = M // self.world
+        self._ensure(rows_local, N)
+        k = self.n % 2
+        rs, red = self.rs[k], self.red[k]
+        slot = rows_local * N
+        y = torch.empty(M, N, device=a.device, dtype=torch.bfloat16)
+        with collective_profile("tp_gemm_all_reduce", payload_bytes=M * N * 2, mode="fused"):
+            ext().gemm_rs(a, b, b_mn, 1.0, rs.peer_ptrs, N, M, rows_local, self.rank, rows_local)
+            rs.barrier(0, self.limit_s)
+            base = rs.tensor.data_ptr()
+            ext().p2p_reduce([[base + s * slot * 2] for s in range(self.world)], [red.tensor.data_ptr()], [slot],
+                             1.0, False)
+            red.barrier(0, self.limit_s)
+            ext().p2p_copy(list(red.peer_ptrs), [y.data_ptr() + r * slot * 2 for r in range(self.world)],
+                           [slot * 2] * self.world)
+        self.n += 1
         return y
 
 

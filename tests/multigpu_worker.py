@@ -43,7 +43,7 @@ def run_engine(collectives, data, layers=2):
     return losses, state, eng.fsdp_wrapper.coll.name
 
 
-def run_sp(collectives, data, steps_grads, moe=False):
+def run_sp(collectives, data, steps_grads, moe=False, sp=True):
     """Qwen3 (head_dim 128) with tp = sp = world: the fused NVLink sequence-parallel
     kernels (collectives != nccl) against the NCCL path.  Returns losses and
     the local gradient shards after one backward."""
@@ -65,7 +65,8 @@ def run_sp(collectives, data, steps_grads, moe=False):
                                   intermediate_size=1024)
         save_pretrained(build_model(mcfg, dtype=torch.bfloat16, seed=0), path)
     dist.barrier()
-    par = [f"parallel.tp={world}", f"parallel.sp={world}"] + ([f"parallel.ep={world}"] if moe else [])
+    par = [f"parallel.tp={world}"] + ([f"parallel.sp={world}"] if sp else []) + \
+        ([f"parallel.ep={world}"] if moe else [])
     cfg = merge(load_cfg(argv=[]), from_dotlist([
         "config.device_type=cuda", "model.learning_rate=1e-3", f"model.name={path}",
         "engine.activation_checkpoint=false", f"engine.collectives={collectives}"] + par))
@@ -78,7 +79,7 @@ def run_sp(collectives, data, steps_grads, moe=False):
     if moe:
         fused = type(ctx0.expert_runtime.dispatcher).__name__ == "P2PTokenDispatcher"
     else:
-        fused = ctx0.fused_sp is not None
+        fused = ctx0.fused_tp is not None
     losses, grads = [], {}
     for i, tok in enumerate(data):
         tok = tok.cuda()
@@ -105,8 +106,9 @@ def main_sp():
     g = torch.Generator().manual_seed(0)
     data = [torch.randint(0, 2048, (2, 256 * world + 1), generator=g) for _ in range(3)]
     moe = os.environ.get("PB_TEST_MOE") == "1"
-    l_f, g_f, fused = run_sp("p2p", data, 1, moe)
-    l_n, g_n, fused_n = run_sp("nccl", data, 1, moe)
+    sp = os.environ.get("PB_TEST_SP", "1") == "1"
+    l_f, g_f, fused = run_sp("p2p", data, 1, moe, sp)
+    l_n, g_n, fused_n = run_sp("nccl", data, 1, moe, sp)
     worst = 0.0
     for k in g_n:
         a, b = g_f[k], g_n[k]
