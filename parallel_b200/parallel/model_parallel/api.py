@@ -81,7 +81,9 @@ class ModelParallelWrapper:
                 self.expert_runtime = SequenceParallelExpertParallel(self.experts, self.group, device=device,
                                                                      collectives=self.collectives)
             else:
-                self.expert_runtime = ReplicatedTokenExpertParallel(self.experts, self.group)
+                fused = getattr(model.ctx, "fused_tp", None)
+                self.expert_runtime = ReplicatedTokenExpertParallel(
+                    self.experts, self.group, fused=fused if hasattr(fused, "try_all_reduce") else None)
             self.expert_runtime.apply(model)
         self.checkpoint = ModelParallelCheckpoint(model, pconfig, self.plan, self.mesh, device)
 

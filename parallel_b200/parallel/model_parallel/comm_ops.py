@@ -11,7 +11,9 @@ parallel/parallel/engine/model_parallel/sequence_parallel.py:48-158):
 * ``scatter_sequence``       split(dim 1) fwd / all-gather bwd
 
 Each takes the model's ``ParallelContext``; the data plane is torch.distributed
-(NCCL on GPUs, gloo on CPU).
+(NCCL on GPUs, gloo on CPU), except that the all-reduces of non-SP tensor
+parallelism go over NVLink peer memory when the context carries a
+``FusedTensorParallel`` (bf16 tensors whose rows divide over the group).
 """
 from __future__ import annotations
 
@@ -56,7 +58,14 @@ def reduce_scatter_dim(value: torch.Tensor, group, dim: int, op_name: str = "sp_
     return _back(out, dim, value.ndim)
 
 
-def all_reduce_sum(value: torch.Tensor, group, op_name: str = "tp_all_reduce", mode: str = "") -> torch.Tensor:
+def all_reduce_sum(value: torch.Tensor, group, op_name: str = "tp_all_reduce", mode: str = "",
+                   fused=None) -> torch.Tensor:
+    """SUM over ``group``; ``fused`` (a FusedTensorParallel) runs it over NVLink
+    peer memory when the tensor fits its buffers, NCCL / gloo otherwise."""
+    if fused is not None:
+        out = fused.try_all_reduce(value)
+        if out is not None:
+            return out
     out = value.contiguous().clone()
     with collective_profile(op_name, value=out, mode=mode):
         dist.all_reduce(out, op=dist.ReduceOp.SUM, group=group)
@@ -65,23 +74,29 @@ def all_reduce_sum(value: torch.Tensor, group, op_name: str = "tp_all_reduce", m
 
 class _CopyToTP(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, group):
-        ctx.group = group
+    def forward(ctx, x, group, fused):
+        ctx.group, ctx.fused = group, fused
         return x
 
     @staticmethod
     def backward(ctx, g):
-        return all_reduce_sum(g, ctx.group, mode="colwise_input_grad"), None
+        return all_reduce_sum(g, ctx.group, mode="colwise_input_grad", fused=ctx.fused), None, None
 
 
 class _ReduceFromTP(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, group):
-        return all_reduce_sum(x, group, mode="rowwise_output")
+    def forward(ctx, x, group, fused):
+        return all_reduce_sum(x, group, mode="rowwise_output", fused=fused)
 
     @staticmethod
     def backward(ctx, g):
-        return g, None
+        return g, None, None
+
+
+def _p2p_all_reduce(ctx):
+    """The context's NVLink all-reduce (FusedTensorParallel, non-SP TP) or None."""
+    f = getattr(ctx, "fused_tp", None)
+    return f if f is not None and hasattr(f, "try_all_reduce") else None
 
 
 class _GatherSeq(torch.autograd.Function):
@@ -123,11 +138,11 @@ class _ScatterSeq(torch.autograd.Function):
 
 
 def copy_to_tp(x, ctx):
-    return _CopyToTP.apply(x, ctx.tp_group)
+    return _CopyToTP.apply(x, ctx.tp_group, _p2p_all_reduce(ctx))
 
 
 def reduce_from_tp(x, ctx):
-    return _ReduceFromTP.apply(x, ctx.tp_group)
+    return _ReduceFromTP.apply(x, ctx.tp_group, _p2p_all_reduce(ctx))
 
 
 def gather_sequence(x, ctx, dim: int = 1):

@@ -79,46 +79,56 @@ def verify_expert_modules(model, partition: ExpertPartition) -> None:
         raise RuntimeError(f"Expected {partition.local_count} local experts per rank, got " + ", ".join(bad))
 
 
+def _sum(value, group, fused, mode):
+    """SUM over the group: NVLink peer memory through ``fused`` (a
+    FusedTensorParallel) when the tensor fits it, NCCL / gloo otherwise."""
+    if fused is not None:
+        out = fused.try_all_reduce(value)
+        if out is not None:
+            return out
+    out = value.contiguous().clone()
+    with collective_profile("ep_all_reduce", value=out, mode=mode, detail="expert_boundary"):
+        dist.all_reduce(out, op=dist.ReduceOp.SUM, group=group)
+    return out
+
+
 class _AllReduceBackward(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, value, group):
-        ctx.group = group
+    def forward(ctx, value, group, fused=None):
+        ctx.group, ctx.fused = group, fused
         return value
 
     @staticmethod
     def backward(ctx, g):
-        g = g.contiguous().clone()
-        with collective_profile("ep_all_reduce", value=g, mode="replicated_token_grad", detail="expert_boundary"):
-            dist.all_reduce(g, op=dist.ReduceOp.SUM, group=ctx.group)
-        return g, None
+        return _sum(g, ctx.group, ctx.fused, "replicated_token_grad"), None, None
 
 
 class _AllReduceForward(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, value, group):
-        out = value.contiguous().clone()
-        with collective_profile("ep_all_reduce", value=out, mode="replicated_token_output", detail="expert_boundary"):
-            dist.all_reduce(out, op=dist.ReduceOp.SUM, group=group)
-        return out
+    def forward(ctx, value, group, fused=None):
+        return _sum(value, group, fused, "replicated_token_output")
 
     @staticmethod
     def backward(ctx, g):
-        return g, None
+        return g, None, None
 
 
 class ReplicatedTokenExpertParallel:
-    def __init__(self, partition: ExpertPartition, group):
+    def __init__(self, partition: ExpertPartition, group, fused=None):
         self.partition = partition
         self.group = group
+        # FusedTensorParallel of the TP group (NVLink all-reduces of the bf16
+        # hidden states / expert outputs) or None
+        self.fused = fused
         self._model = None
 
     def __call__(self, experts, x2, global_index, weights):
         # localise after the backward all-reduce boundary (see reference note)
         weights = _AllReduceBackward.apply(weights, self.group)
         local_idx, local_w, _ = self.partition.localize_routes(global_index, weights)
-        h = _AllReduceBackward.apply(x2, self.group)
+        h = _AllReduceBackward.apply(x2, self.group, self.fused)
         y = experts(h, local_idx, local_w)
-        return _AllReduceForward.apply(y, self.group)
+        return _AllReduceForward.apply(y, self.group, self.fused)
 
     def apply(self, model) -> None:
         if self._model is not None:

@@ -167,7 +167,10 @@ class FusedTensorParallel:
     available = staticmethod(FusedSequenceParallel.available)
 
     def supports(self, batch: int, seq: int, cols: int) -> bool:
-        return (batch * seq) % self.world == 0 and cols % 8 == 0
+        rows = batch * seq
+        if rows % self.world or cols % 8:
+            return False
+        return not self.rs or (rows // self.world <= self._rows and cols <= self._cols)
 
     def _ensure(self, rows_local: int, cols: int) -> None:
         if self.rs and rows_local <= self._rows and cols <= self._cols:
@@ -192,6 +195,42 @@ class FusedTensorParallel:
             ext().gemm(x, b, out, False, b_mn, EPI_STORE_BF16, 1.0)
         return out, x
 
+    def _reduce_and_gather(self, rs, red, y: torch.Tensor, slot: int) -> None:
+        rs.barrier(0, self.limit_s)
+        base = rs.tensor.data_ptr()
+        ext().p2p_reduce([[base + s * slot * 2] for s in range(self.world)], [red.tensor.data_ptr()], [slot],
+                         1.0, False)
+        red.barrier(0, self.limit_s)
+        ext().p2p_copy(list(red.peer_ptrs), [y.data_ptr() + r * slot * 2 for r in range(self.world)],
+                       [slot * 2] * self.world)
+
+    def try_all_reduce(self, x: torch.Tensor):
+        """SUM of a bf16 CUDA tensor over the group on the same buffers (row
+        blocks pushed to their owners, owner reduce, gather); None when the
+        shape does not fit (rows % world, or larger than the buffers sized by
+        the first call), so the caller falls back to NCCL."""
+        if not (x.is_cuda and x.dtype == torch.bfloat16 and x.dim() >= 1 and x.shape[-1] % 8 == 0):
+            return None
+        x2 = x.reshape(-1, x.shape[-1])
+        M, N = x2.shape
+        if M % self.world:
+            return None
+        rows_local = M // self.world
+        if self.rs and (rows_local > self._rows or N > self._cols):
+            return None
+        self._ensure(rows_local, N)
+        x2 = x2.contiguous()
+        k = self.n % 2
+        rs, red = self.rs[k], self.red[k]
+        slot = rows_local * N
+        y = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
+        with collective_profile("tp_all_reduce", value=x2, mode="p2p"):
+            ext().p2p_copy([x2.data_ptr() + r * slot * 2 for r in range(self.world)],
+                           [rs.peer_ptrs[r] + self.rank * slot * 2 for r in range(self.world)], [slot * 2] * self.world)
+            self._reduce_and_gather(rs, red, y, slot)
+        self.n += 1
+        return y.view(x.shape)
+
     def gemm_reduce_scatter(self, a: torch.Tensor, b: torch.Tensor, batch: int, seq: int, *,
                             b_mn: bool = False) -> torch.Tensor:
         """y [M, N] = all_reduce(a @ b^T (or @ b)) over the group (see the class docstring)."""
@@ -205,13 +244,7 @@ class FusedTensorParallel:
         y = torch.empty(M, N, device=a.device, dtype=torch.bfloat16)
         with collective_profile("tp_gemm_all_reduce", payload_bytes=M * N * 2, mode="fused"):
             ext().gemm_rs(a, b, b_mn, 1.0, rs.peer_ptrs, N, M, rows_local, self.rank, rows_local)
-            rs.barrier(0, self.limit_s)
-            base = rs.tensor.data_ptr()
-            ext().p2p_reduce([[base + s * slot * 2] for s in range(self.world)], [red.tensor.data_ptr()], [slot],
-                             1.0, False)
-            red.barrier(0, self.limit_s)
-            ext().p2p_copy(list(red.peer_ptrs), [y.data_ptr() + r * slot * 2 for r in range(self.world)],
-                           [slot * 2] * self.world)
+            self._reduce_and_gather(rs, red, y, slot)
         self.n += 1
         return y
 

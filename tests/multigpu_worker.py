@@ -76,8 +76,10 @@ def run_sp(collectives, data, steps_grads, moe=False, sp=True):
     m.to(pc.device)
     eng = ParallelEngine(m, None, pc, cfg, pc.device, mp_plan=plan)
     ctx0 = eng.model.model.layers[0]._ctx
-    if moe:
+    if moe and sp:
         fused = type(ctx0.expert_runtime.dispatcher).__name__ == "P2PTokenDispatcher"
+    elif moe:
+        fused = getattr(ctx0.expert_runtime, "fused", None) is not None
     else:
         fused = ctx0.fused_tp is not None
     losses, grads = [], {}

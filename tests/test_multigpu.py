@@ -89,13 +89,15 @@ def test_p2p_small_all_reduce_matches_nccl(tmp_path):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_fused_tensor_parallel_matches_nccl(tmp_path):
+@pytest.mark.parametrize("moe", ["0", "1"])
+def test_fused_tensor_parallel_matches_nccl(tmp_path, moe):
     """tp = 2 without sequence parallelism: GEMM -> all-reduce over NVLink for
-    the row-parallel outputs and the column-parallel input gradients gives the
-    NCCL path's losses and gradients."""
+    the row-parallel outputs and the column-parallel input gradients, the
+    embedding all-reduce and (MoE) the replicated-token expert all-reduces on
+    peer memory give the NCCL path's losses and gradients."""
     out = tmp_path / "res_tp.json"
-    env = dict(os.environ, PB_TEST_OUT=str(out), PB_TEST_MODE="sp", PB_TEST_SP="0", PB_TEST_TMP=str(tmp_path),
-               NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, PB_TEST_OUT=str(out), PB_TEST_MODE="sp", PB_TEST_SP="0", PB_TEST_MOE=moe,
+               PB_TEST_TMP=str(tmp_path), NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
            "--master-port", "29537", os.path.join(HERE, "multigpu_worker.py")]
     subprocess.run(cmd, env=env, check=True, timeout=600)
