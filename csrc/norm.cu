@@ -236,61 +236,74 @@ __global__ void qknorm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, in
                                        __nv_bfloat16* __restrict__ q_out, int64_t ldq,
                                        __nv_bfloat16* __restrict__ k_out, int64_t ldk,
                                        float* __restrict__ rstd, int T, int S, int nq, int nkv, float eps) {
-  // The bf16 products / sums of the reference's op-by-op bf16 arithmetic run
-  // as packed bf16x2 instructions: a product of two bf16 values is exact in
-  // fp32, so the packed multiply rounds exactly like fp32-multiply-then-round.
+  // A half warp per unit = (token, U consecutive heads): the token's cos / sin
+  // rows are loaded once and all U input rows are issued before the first
+  // reduction (one DRAM round trip per unit).  The bf16 products / sums of the
+  // reference's op-by-op bf16 arithmetic run as packed bf16x2 instructions: a
+  // product of two bf16 values is exact in fp32, so the packed multiply rounds
+  // exactly like fp32-multiply-then-round.
   constexpr int D = 128;
+  constexpr int U = 4;
   const int lane = threadIdx.x & 31;
   const int hl = lane & 15;
   const int nh = nq + nkv;
-  const int64_t total = (int64_t)T * nh;
-  int64_t item = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 2 + (lane >> 4);
-  const bool valid = item < total;
-  if (!valid) item = total - 1;  // keep all lanes in the shuffles
-  const int t = (int)(item / nh), h = (int)(item % nh);
-  const bool is_q = h < nq;
+  const int groups = (nh + U - 1) / U;
+  const int64_t total = (int64_t)T * groups;
+  int64_t unit = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 2 + (lane >> 4);
+  const bool unit_ok = unit < total;
+  if (!unit_ok) unit = total - 1;  // keep all lanes in the shuffles
+  const int t = (int)(unit / groups), h0 = (int)(unit % groups) * U;
   const int pos = t % S;
-  // every load issued before the reduction (one round trip per item)
-  const uint4 xv = *reinterpret_cast<const uint4*>(qkv + (int64_t)t * ldqkv + (int64_t)h * D + hl * 8);
-  const uint4 wv = __ldg(reinterpret_cast<const uint4*>((is_q ? qw : kw) + hl * 8));
+  uint4 xv[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u)
+    xv[u] = *reinterpret_cast<const uint4*>(qkv + (int64_t)t * ldqkv + (int64_t)min(h0 + u, nh - 1) * D + hl * 8);
+  const uint4 qwv = __ldg(reinterpret_cast<const uint4*>(qw + hl * 8));
+  const uint4 kwv = __ldg(reinterpret_cast<const uint4*>(kw + hl * 8));
   const uint4 cv = __ldg(reinterpret_cast<const uint4*>(cosb + (int64_t)pos * D + hl * 8));
   uint4 sv = __ldg(reinterpret_cast<const uint4*>(sinb + (int64_t)pos * D + hl * 8));
-  const uint32_t* x32 = &xv.x;
-  float xf[8];
-  float ss = 0.f;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const float2 f = unpack_bf16x2(x32[q]);
-    xf[2 * q] = f.x;
-    xf[2 * q + 1] = f.y;
-    ss += f.x * f.x + f.y * f.y;
-  }
-  ss = half_sum(ss);
-  const float r = rsqrtf(ss / (float)D + eps);
   // rotate_half: [-x2, x1] -> the first half of the lanes takes -sin
   if (hl < 8) {
     sv.x ^= 0x80008000u; sv.y ^= 0x80008000u; sv.z ^= 0x80008000u; sv.w ^= 0x80008000u;
   }
-  const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv);
   const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&cv);
   const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(&sv);
-  uint4 ov;
-  uint32_t* o32 = &ov.x;
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const __nv_bfloat162 xh = __floats2bfloat162_rn(xf[2 * q] * r, xf[2 * q + 1] * r);
-    const __nv_bfloat162 n = __hmul2(w2[q], xh);
-    const uint32_t nu = *reinterpret_cast<const uint32_t*>(&n);
-    const uint32_t pu = __shfl_xor_sync(0xffffffffu, nu, 8);
-    const __nv_bfloat162 pn = *reinterpret_cast<const __nv_bfloat162*>(&pu);
-    const __nv_bfloat162 o = __hadd2(__hmul2(n, c2[q]), __hmul2(pn, s2[q]));
-    o32[q] = *reinterpret_cast<const uint32_t*>(&o);
+  for (int u = 0; u < U; ++u) {
+    const int h = h0 + u;
+    const bool valid = unit_ok && h < nh;
+    const bool is_q = h < nq;
+    const uint32_t* x32 = &xv[u].x;
+    float xf[8];
+    float ss = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = unpack_bf16x2(x32[q]);
+      xf[2 * q] = f.x;
+      xf[2 * q + 1] = f.y;
+      ss += f.x * f.x + f.y * f.y;
+    }
+    ss = half_sum(ss);
+    const float r = rsqrtf(ss / (float)D + eps);
+    const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(is_q ? &qwv : &kwv);
+    uint4 ov;
+    uint32_t* o32 = &ov.x;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const __nv_bfloat162 xh = __floats2bfloat162_rn(xf[2 * q] * r, xf[2 * q + 1] * r);
+      const __nv_bfloat162 n = __hmul2(w2[q], xh);
+      const uint32_t nu = *reinterpret_cast<const uint32_t*>(&n);
+      const uint32_t pu = __shfl_xor_sync(0xffffffffu, nu, 8);
+      const __nv_bfloat162 pn = *reinterpret_cast<const __nv_bfloat162*>(&pu);
+      const __nv_bfloat162 o = __hadd2(__hmul2(n, c2[q]), __hmul2(pn, s2[q]));
+      o32[q] = *reinterpret_cast<const uint32_t*>(&o);
+    }
+    if (!valid) continue;
+    if (hl == 0) rstd[(int64_t)t * nh + h] = r;
+    __nv_bfloat16* dst = is_q ? q_out + (int64_t)t * ldq + (int64_t)h * D
+                              : k_out + (int64_t)t * ldk + (int64_t)(h - nq) * D;
+    *reinterpret_cast<uint4*>(dst + hl * 8) = ov;
   }
-  if (!valid) return;
-  if (hl == 0) rstd[(int64_t)t * nh + h] = r;
-  __nv_bfloat16* dst = is_q ? q_out + (int64_t)t * ldq + (int64_t)h * D
-                            : k_out + (int64_t)t * ldk + (int64_t)(h - nq) * D;
-  *reinterpret_cast<uint4*>(dst + hl * 8) = ov;
 }
 
 // Backward of the above; q/k norm weight grads: per-lane registers, then one
@@ -305,12 +318,13 @@ __global__ void __launch_bounds__(256, 2) qknorm_rope_bwd_kernel(const __nv_bflo
                                        const float* __restrict__ rstd,
                                        __nv_bfloat16* __restrict__ dqkv, int64_t lddqkv,
                                        float* __restrict__ dqw, float* __restrict__ dkw, int T, int S,
-                                       int nq, int nkv, int items_per_block) {
-  // A half warp per (token, head) item, two items per iteration with every
-  // load (gradient, input row, rstd, cos/sin) issued before the first
-  // shuffle, so an iteration costs one DRAM round trip for two items.
+                                       int nq, int nkv, int units_per_block) {
+  // A half warp per unit = (token, group of U consecutive heads): the token's
+  // cos / sin rows are loaded once per unit and every head's gradient and
+  // input rows (2 x 16 bytes per lane per head) are issued before the first
+  // shuffle, so a unit costs one DRAM round trip with 2U + 2 loads in flight.
   constexpr int D = 128;
-  constexpr int U = 2;
+  constexpr int U = 4;
   __shared__ float sdw[2][D];
   for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) (&sdw[0][0])[i] = 0.f;
   __syncthreads();
@@ -319,9 +333,10 @@ __global__ void __launch_bounds__(256, 2) qknorm_rope_bwd_kernel(const __nv_bflo
   const int slots = (blockDim.x >> 5) * 2;
   const int slot = (threadIdx.x >> 5) * 2 + (lane >> 4);
   const int nh = nq + nkv;
-  const int64_t total = (int64_t)T * nh;
-  const int64_t i0 = (int64_t)blockIdx.x * items_per_block;
-  const int64_t i1 = min(total, i0 + items_per_block);
+  const int groups = (nh + U - 1) / U;
+  const int64_t total = (int64_t)T * groups;
+  const int64_t u0 = (int64_t)blockIdx.x * units_per_block;
+  const int64_t u1 = min(total, u0 + units_per_block);
   float qw_r[8], kw_r[8], acc_q[8], acc_k[8];
   load8(qw + hl * 8, qw_r);
   load8(kw + hl * 8, kw_r);
@@ -329,46 +344,50 @@ __global__ void __launch_bounds__(256, 2) qknorm_rope_bwd_kernel(const __nv_bflo
   for (int j = 0; j < 8; ++j) acc_q[j] = acc_k[j] = 0.f;
   const float sign = hl < 8 ? 1.f : -1.f;
   // every lane iterates the same number of times so shuffles stay converged
-  const int64_t span = i1 - i0;
-  const int64_t iters = (span + slots * U - 1) / (slots * U);
+  const int64_t iters = (u1 - u0 + slots - 1) / slots;
   for (int64_t it = 0; it < iters; ++it) {
-    uint4 gp[U], xp[U], cp[U], sp[U];
+    int64_t unit = u0 + it * slots + slot;
+    const bool unit_ok = unit < u1;
+    if (!unit_ok) unit = u1 - 1;
+    const int t = (int)(unit / groups), h0 = (int)(unit % groups) * U;
+    const int pos = t % S;
+    const uint4 cp = *reinterpret_cast<const uint4*>(cosb + (int64_t)pos * D + hl * 8);
+    const uint4 sp = *reinterpret_cast<const uint4*>(sinb + (int64_t)pos * D + hl * 8);
+    uint4 gp[U], xp[U];
     float rr[U];
-    int hh[U], tt[U];
-    bool valid[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      int64_t item = i0 + (it * U + u) * slots + slot;
-      valid[u] = item < i1;
-      if (!valid[u]) item = i1 - 1;
-      const int t = (int)(item / nh), h = (int)(item % nh);
-      tt[u] = t;
-      hh[u] = h;
+      const int h = min(h0 + u, nh - 1);
       const bool is_q = h < nq;
       gp[u] = *reinterpret_cast<const uint4*>(is_q ? dq + (int64_t)t * lddq + (int64_t)h * D + hl * 8
                                                    : dk + (int64_t)t * lddk + (int64_t)(h - nq) * D + hl * 8);
       xp[u] = *reinterpret_cast<const uint4*>(qkv + (int64_t)t * ldqkv + (int64_t)h * D + hl * 8);
-      const int pos = t % S;
-      cp[u] = *reinterpret_cast<const uint4*>(cosb + (int64_t)pos * D + hl * 8);
-      sp[u] = *reinterpret_cast<const uint4*>(sinb + (int64_t)pos * D + hl * 8);
       rr[u] = rstd[(int64_t)t * nh + h];
+    }
+    float cv[8], sv[8];
+    {
+      const uint32_t* c32 = &cp.x;
+      const uint32_t* s32 = &sp.x;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 c = unpack_bf16x2(c32[q]), d = unpack_bf16x2(s32[q]);
+        cv[2 * q] = c.x; cv[2 * q + 1] = c.y;
+        sv[2 * q] = d.x; sv[2 * q + 1] = d.y;
+      }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const bool is_q = hh[u] < nq;
-      float gv[8], cv[8], sv[8], xv[8];
+      const int h = h0 + u;
+      const bool valid = unit_ok && h < nh;
+      const bool is_q = h < nq;
+      float gv[8], xv[8];
       const uint32_t* g32 = &gp[u].x;
       const uint32_t* x32 = &xp[u].x;
-      const uint32_t* c32 = &cp[u].x;
-      const uint32_t* s32 = &sp[u].x;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const float2 a = unpack_bf16x2(g32[q]), b = unpack_bf16x2(x32[q]), c = unpack_bf16x2(c32[q]),
-                     d = unpack_bf16x2(s32[q]);
+        const float2 a = unpack_bf16x2(g32[q]), b = unpack_bf16x2(x32[q]);
         gv[2 * q] = a.x; gv[2 * q + 1] = a.y;
         xv[2 * q] = b.x; xv[2 * q + 1] = b.y;
-        cv[2 * q] = c.x; cv[2 * q + 1] = c.y;
-        sv[2 * q] = d.x; sv[2 * q + 1] = d.y;
       }
       // dn[i] = g[i]*c[i] + (i<64 ? g[i+64]*s[i+64] : -g[i-64]*s[i-64])
       float dn[8];
@@ -380,7 +399,7 @@ __global__ void __launch_bounds__(256, 2) qknorm_rope_bwd_kernel(const __nv_bflo
 #pragma unroll
       for (int j = 0; j < 8; ++j) dot += dn[j] * wv[j] * xv[j] * r;
       dot = half_sum(dot) / (float)D;
-      if (!valid[u]) continue;
+      if (!valid) continue;
       float dx[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -388,7 +407,7 @@ __global__ void __launch_bounds__(256, 2) qknorm_rope_bwd_kernel(const __nv_bflo
         const float contrib = dn[j] * bfr(xv[j] * r);
         if (is_q) acc_q[j] += contrib; else acc_k[j] += contrib;
       }
-      store8(dqkv + (int64_t)tt[u] * lddqkv + (int64_t)hh[u] * D + hl * 8, dx);
+      store8(dqkv + (int64_t)t * lddqkv + (int64_t)h * D + hl * 8, dx);
     }
   }
 #pragma unroll
@@ -450,9 +469,9 @@ void qknorm_rope_fwd(const void* qkv, int64_t ldqkv, const void* qw, const void*
                      int64_t ldk, float* rstd, int T, int S, int nq, int nkv, int D, float eps,
                      cudaStream_t s) {
   PB_CHECK(D == 128, "qknorm_rope: head_dim 128 only");
-  const int items = T * (nq + nkv);
-  const int per_block = 16;  // 8 warps x 2 items
-  qknorm_rope_fwd_kernel<<<(items + per_block - 1) / per_block, 256, 0, s>>>(
+  const int units = T * ((nq + nkv + 3) / 4);  // (token, 4 heads) units
+  const int per_block = 16;                    // 8 warps x 2 half-warps
+  qknorm_rope_fwd_kernel<<<(units + per_block - 1) / per_block, 256, 0, s>>>(
       (const __nv_bfloat16*)qkv, ldqkv, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw,
       (const __nv_bfloat16*)cos, (const __nv_bfloat16*)sin, (__nv_bfloat16*)q_out, ldq,
       (__nv_bfloat16*)k_out, ldk, rstd, T, S, nq, nkv, eps);
@@ -465,10 +484,10 @@ void qknorm_rope_bwd(const void* dq, int64_t lddq, const void* dk, int64_t lddk,
                      float* dqw_acc, float* dkw_acc, int T, int S, int nq, int nkv, int D,
                      cudaStream_t s) {
   PB_CHECK(D == 128, "qknorm_rope: head_dim 128 only");
-  const int items = T * (nq + nkv);
-  const int blocks = num_sms() * 2;  // one wave
-  const int ipb = (items + blocks - 1) / blocks;
-  const int grid = (items + ipb - 1) / ipb;
+  const int units = T * ((nq + nkv + 3) / 4);  // (token, 4 heads) units
+  const int blocks = num_sms() * 2;            // one wave
+  const int ipb = (units + blocks - 1) / blocks;
+  const int grid = (units + ipb - 1) / ipb;
   qknorm_rope_bwd_kernel<<<grid, 256, 0, s>>>(
       (const __nv_bfloat16*)dq, lddq, (const __nv_bfloat16*)dk, lddk, (const __nv_bfloat16*)qkv,
       ldqkv, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw, (const __nv_bfloat16*)cos,

@@ -1,6 +1,6 @@
 """Micro-benchmarks of the sm_100a kernels at the Qwen3-0.6B training shapes.
 
-    python -m parallel_b200.ops.kernel_bench attn_fwd|attn_bwd|gemm|gemm_swiglu|gemm_residual|rmsnorm_bwd|qknorm|all [--iters N]
+    python -m parallel_b200.ops.kernel_bench attn_fwd|attn_bwd|gemm|gemm_swiglu|gemm_residual|rmsnorm_bwd|qknorm|qknorm_bwd|all [--iters N]
 
 Each case runs a few warm-up launches, then times ``--iters`` launches with
 CUDA events on the current stream and prints the time per launch and the
@@ -123,8 +123,27 @@ def case_qknorm(warmup, iters):
     return f"qk-norm + RoPE fwd {T} tokens x {NQ + NKV} heads: {us:.1f} us, {2 * T * (NQ + NKV) * D * 2 / us / 1e3:.0f} GB/s"
 
 
+def case_qknorm_bwd(warmup, iters):
+    C = ext()
+    T = B * S
+    nh = NQ + NKV
+    qkv = torch.randn(T, (NQ + 2 * NKV) * D, device="cuda", dtype=torch.bfloat16)
+    dq = torch.randn(T, NQ * D, device="cuda", dtype=torch.bfloat16)
+    dk = torch.randn(T, NKV * D, device="cuda", dtype=torch.bfloat16)
+    cos, sin = (torch.randn(S, D, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    qw, kw = (torch.randn(D, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    rstd = torch.rand(T * nh, device="cuda") + 0.5
+    dqkv = torch.empty_like(qkv)
+    dqw, dkw = torch.zeros(D, device="cuda"), torch.zeros(D, device="cuda")
+    us = _time(lambda: C.qknorm_rope_bwd(dq, dk, qkv, qw, kw, cos, sin, rstd, dqkv, dqw, dkw, S, NQ, NKV),
+               warmup, iters)
+    moved = 3 * T * nh * D * 2  # gradient in, input rows in, input gradient out
+    return f"qk-norm + RoPE bwd {T} tokens x {nh} heads: {us:.1f} us, {moved / us / 1e3:.0f} GB/s"
+
+
 CASES = {"attn_fwd": case_attn_fwd, "attn_bwd": case_attn_bwd, "gemm": case_gemm, "gemm_swiglu": case_gemm_swiglu,
-         "gemm_residual": case_gemm_residual, "rmsnorm_bwd": case_rmsnorm_bwd, "qknorm": case_qknorm}
+         "gemm_residual": case_gemm_residual, "rmsnorm_bwd": case_rmsnorm_bwd, "qknorm": case_qknorm,
+         "qknorm_bwd": case_qknorm_bwd}
 
 
 def main(argv=None):
