@@ -363,16 +363,24 @@ class ParallelEngine:
                     dist.all_reduce(bucket, op=dist.ReduceOp.SUM, group=group)
                 bucket.div_(self.pconfig.dp_replicate_size)
             return
-        for p in self.optimizer_params:
-            has = torch.tensor(int(p.grad is not None), dtype=torch.int32, device=self.device)
+        # one participation bitmap for all parameters (one all-reduce, one
+        # read-back) instead of the reference's per-parameter flag and sync
+        # (parallel/parallel/engine/engine.py:224-247); replicas without a local
+        # gradient contribute zeros, globally unused parameters keep grad=None
+        params = list(self.optimizer_params)
+        has = torch.tensor([int(p.grad is not None) for p in params], dtype=torch.int32, device=self.device)
+        if has.numel():
             dist.all_reduce(has, op=dist.ReduceOp.MAX, group=group)
+        used = has.tolist()
+        for p, u in zip(params, used):
+            if not u:
+                p.grad = None
+                continue
             if p.grad is None:
                 p.grad = torch.zeros_like(p)
             g = local_tensor(p.grad)
             dist.all_reduce(g, op=dist.ReduceOp.SUM, group=group)
             g.div_(self.pconfig.dp_replicate_size)
-            if not has.item():
-                p.grad = None
 
     def _grads_are_finite(self) -> bool:
         finite = torch.ones((), dtype=torch.int32, device=self.device)

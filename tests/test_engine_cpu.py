@@ -1,0 +1,56 @@
+"""Host-side pieces of the engine that need no GPU: the whole-step API, the
+CUDA-graph refusals and the optimizer step-count bookkeeping of graph replays."""
+import pytest
+import torch
+
+from dist_utils import cpu_cfg
+
+
+def _engine():
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.qwen3 import build_model
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    cfg = cpu_cfg()
+    pc = ParallelConfig(cfg)
+    pc.set_device_mesh("cpu")
+    m = build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0)
+    return ParallelEngine(m, None, pc, cfg, torch.device("cpu")), m
+
+
+def test_train_step_equals_forward_backward_step():
+    a, ma = _engine()
+    b, mb = _engine()
+    tok = torch.randint(0, 1024, (2, 33), generator=torch.Generator().manual_seed(1))
+    la = a.train_step(tok[:, :-1], tok[:, 1:])
+    out = b.forward(tok[:, :-1], tok[:, 1:])
+    b.backward(out.loss)
+    b.step()
+    assert abs(float(la) - float(out.loss.detach())) < 1e-6
+    for (n, p), q in zip(ma.named_parameters(), mb.parameters()):
+        torch.testing.assert_close(p, q, rtol=0, atol=0, msg=n)
+
+
+def test_graph_capture_refused_on_cpu():
+    eng, _ = _engine()
+    tok = torch.randint(0, 1024, (2, 17))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        eng.capture_train_step(tok[:, :-1], tok[:, 1:])
+    assert eng._graph is None
+
+
+def test_graph_step_count_bookkeeping():
+    """A capture advances the host step counters without running: they are
+    restored afterwards; each replay advances them once."""
+    from parallel_b200.parallel.optim import FusedAdamW
+
+    p = torch.nn.Parameter(torch.randn(8))
+    opt = FusedAdamW([p], lr=1e-2)
+    p.grad = torch.randn(8)
+    opt.step()
+    counts = opt.graph_step_counts()
+    assert float(counts[id(p)]) == 1.0
+    opt.state[p]["step"] += 1  # what a capture does on the host
+    opt.restore_step_counts(counts)
+    assert float(opt.state[p]["step"]) == 1.0

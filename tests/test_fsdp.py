@@ -111,3 +111,42 @@ def test_fsdp_units_and_layout(tmp_path):
     run_ranks(_layout_worker, 2, out)
     lay = torch.load(out, weights_only=False)
     assert lay["state_dict_keys"][0] == "model.embed_tokens.weight"
+
+
+def _replicate_worker(rank, world, data, out_q):
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.qwen3 import build_model
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    cfg = cpu_cfg(**{"parallel.dp_replicate": world})
+    pc = ParallelConfig(cfg)
+    pc.set_device_mesh("cpu")
+    m = build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0)
+    eng = ParallelEngine(m, None, pc, cfg, torch.device("cpu"))
+    losses = []
+    for tok in data:
+        B = tok.shape[0] // world
+        mine = tok[rank * B:(rank + 1) * B]
+        loss = eng.forward(mine[:, :-1], mine[:, 1:]).loss
+        eng.backward(loss)
+        eng.step()
+        losses.append(eng.reduce_loss(loss.detach()).item())
+    if rank == 0:
+        torch.save({"losses": losses, "state": {k: v.detach().clone() for k, v in m.state_dict().items()}}, out_q)
+
+
+def test_dp_replicate_matches_single_process(tmp_path):
+    """Replicated data parallelism (gradient all-reduce mean, one participation
+    bitmap per step) equals single-process training on the global batch."""
+    world = 2
+    data = _tokens(world)[:4]
+    out = str(tmp_path / "rep.pt")
+    run_ranks(_replicate_worker, world, data, out)
+    got = torch.load(out, weights_only=False)
+    ref_losses, ref_model = _single_process_losses(data)
+    for a, b in zip(got["losses"], ref_losses):
+        assert abs(a - b) < 1e-5, (got["losses"], ref_losses)
+    ref_sd = ref_model.state_dict()
+    for k, v in got["state"].items():
+        torch.testing.assert_close(v, ref_sd[k], rtol=1e-3, atol=2e-4)
