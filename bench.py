@@ -30,7 +30,7 @@ from datetime import datetime, timedelta
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "train tokens/s (device-timed, max over ranks) @1/2/4/8 B200 vs ref NCCL build"
 MODEL = "Qwen/Qwen3-0.6B"
-BASELINE_VALUE = None  # BASELINE.md publishes no number for this metric
+BASELINE_VALUE = None  # no published number exists for this metric on this config
 
 
 def parse():
