@@ -150,3 +150,148 @@ def test_dp_replicate_matches_single_process(tmp_path):
     ref_sd = ref_model.state_dict()
     for k, v in got["state"].items():
         torch.testing.assert_close(v, ref_sd[k], rtol=1e-3, atol=2e-4)
+
+
+class _ToyLayer(torch.nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.a = torch.nn.Linear(16, 16, bias=False)
+        self.b = torch.nn.Linear(16, 16, bias=False)
+        self.never = torch.nn.Linear(16, 16, bias=False)  # unused on every rank
+        self.use_b = True
+
+    def forward(self, x):
+        y = x + self.a(x)
+        return y + self.b(torch.tanh(y)) if self.use_b else y
+
+
+class _Toy(torch.nn.Module):
+    """Rank-divergent graph: layer 0's ``b`` runs only where ``use_b`` is set."""
+
+    def __init__(self, seed=0):
+        super().__init__()
+        torch.manual_seed(seed)
+        self.embed = torch.nn.Embedding(64, 16)
+        self.layers = torch.nn.ModuleList([_ToyLayer(), _ToyLayer()])
+        self.head = torch.nn.Linear(16, 64, bias=False)
+
+    def forward(self, input_ids, labels=None):
+        from types import SimpleNamespace
+
+        x = self.embed(input_ids)
+        for layer in self.layers:
+            x = layer(x)
+        logits = self.head(x)
+        loss = torch.nn.functional.cross_entropy(logits.reshape(-1, 64), labels.reshape(-1))
+        return SimpleNamespace(loss=loss, logits=logits)
+
+
+def _unused_data(world, steps=3):
+    g = torch.Generator().manual_seed(5)
+    return [torch.randint(0, 64, (world * 2, 9), generator=g) for _ in range(steps)]
+
+
+def _unused_worker(rank, world, data, out):
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    cfg = cpu_cfg(**{"parallel.dp_shard": world, "engine.find_unused_parameters": "true",
+                     "engine.activation_checkpoint": "false", "model.learning_rate": 1e-2})
+    pc = ParallelConfig(cfg)
+    pc.set_device_mesh("cpu")
+    m = _Toy()
+    m.layers[0].use_b = rank == 0
+    eng = ParallelEngine(m, None, pc, cfg, torch.device("cpu"))
+    for tok in data:
+        mine = tok[rank * 2:(rank + 1) * 2]
+        loss = eng.forward(mine[:, :-1], mine[:, 1:]).loss
+        eng.backward(loss)
+        eng.step()
+    full = eng.state_dict()
+    if rank == 0:
+        torch.save(full, out)
+
+
+def test_fsdp_rank_divergent_unused_parameters(tmp_path):
+    """find_unused_parameters: a parameter used on some ranks gets the mean over
+    all ranks (zeros where unused); one unused everywhere keeps grad=None and is
+    left untouched by AdamW (no weight decay either)."""
+    from parallel_b200.parallel.optim import FusedAdamW
+
+    world = 2
+    data = _unused_data(world)
+    out = str(tmp_path / "unused.pt")
+    run_ranks(_unused_worker, world, data, out)
+    got = torch.load(out, weights_only=False)
+    ref = _Toy()
+    init_never = ref.layers[1].never.weight.detach().clone()
+    opt = FusedAdamW(list(ref.parameters()), lr=1e-2, betas=(0.9, 0.999), weight_decay=0.01)
+    for tok in data:
+        grads = []
+        for r in range(world):
+            ref.layers[0].use_b = r == 0
+            ref.zero_grad(set_to_none=True)
+            mine = tok[r * 2:(r + 1) * 2]
+            ref(mine[:, :-1], labels=mine[:, 1:]).loss.backward()
+            grads.append({n: (p.grad.clone() if p.grad is not None else None) for n, p in ref.named_parameters()})
+        for n, p in ref.named_parameters():
+            gs = [g[n] for g in grads]
+            if all(g is None for g in gs):
+                p.grad = None
+            else:
+                p.grad = sum(g if g is not None else torch.zeros_like(p) for g in gs) / world
+        torch.nn.utils.clip_grad_norm_([p for p in ref.parameters() if p.grad is not None], 1.0)
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+    sd = ref.state_dict()
+    for k, v in got.items():
+        torch.testing.assert_close(v, sd[k], rtol=1e-4, atol=1e-5, msg=k)
+    torch.testing.assert_close(got["layers.1.never.weight"], init_never, rtol=0, atol=0)
+
+
+def _order_worker(rank, world, out):
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.qwen3 import build_model
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.parallel.param_unit import DPParamUnit
+    from parallel_b200.state import ParallelConfig
+
+    events = []
+    orig_reduce, orig_finish = DPParamUnit.reduce_gradients, DPParamUnit.finish_gradient_reduction
+
+    def reduce(self, grads):
+        events.append(("start", self.unit_index, sum(u.reduction_in_flight for u in units) + 1))
+        return orig_reduce(self, grads)
+
+    def finish(self):
+        if self.reduction_in_flight:
+            events.append(("finish", self.unit_index, None))
+        return orig_finish(self)
+
+    DPParamUnit.reduce_gradients, DPParamUnit.finish_gradient_reduction = reduce, finish
+    cfg = cpu_cfg(**{"parallel.dp_shard": world, "engine.overlap_backward_reductions": "true"})
+    pc = ParallelConfig(cfg)
+    pc.set_device_mesh("cpu")
+    cfg_m = resolve_config("tiny-qwen3", num_hidden_layers=4)
+    m = build_model(cfg_m, dtype=torch.float32, seed=0)
+    eng = ParallelEngine(m, None, pc, cfg, torch.device("cpu"))
+    units = eng.fsdp_wrapper.units
+    tok = torch.randint(0, 1024, (2, 33), generator=torch.Generator().manual_seed(rank))
+    loss = eng.forward(tok[:, :-1], tok[:, 1:]).loss
+    eng.backward(loss)
+    if rank == 0:
+        torch.save(events, out)
+
+
+def test_fsdp_reductions_reverse_order_at_most_two_in_flight(tmp_path):
+    """Overlapped backward: every unit's reduce-scatter starts in strict reverse
+    unit order (layers last-to-first, then the root unit at the end), with at
+    most two in flight, and each is drained before the backward returns (the
+    reference's schedule, dp_sharded.py:305-321)."""
+    out = str(tmp_path / "order.pt")
+    run_ranks(_order_worker, 2, out)
+    events = torch.load(out, weights_only=False)
+    starts = [u for kind, u, _ in events if kind == "start"]
+    assert starts == [4, 3, 2, 1, 0], events  # unit 0 = root (embedding, final norm), 1..4 = layers
+    assert max(n for kind, _, n in events if kind == "start") <= 2, events
+    assert sorted(u for kind, u, _ in events if kind == "finish") == [0, 1, 2, 3, 4], events
