@@ -178,6 +178,44 @@ def time_steps(step_fn, batches, K):
     return s.elapsed_time(e) / K
 
 
+def e2e_loop(step_fn, host, K, device, warm=2):
+    """End-to-end steps through the public API: each step copies its tokens
+    from pinned host memory to the device and reads its loss back to the host.
+    The read-back is pipelined one step behind, as a training loop that logs
+    every step does: the loss goes to pinned memory by an async copy right
+    after the step, and the host reads it after launching the next step.
+    Device-timed (CUDA events around the K steps, max over ranks); returns
+    (ms per step, losses)."""
+    import torch
+
+    pinned = [torch.zeros(1, dtype=torch.float32).pin_memory() for _ in range(2)]
+    events = [torch.cuda.Event(), torch.cuda.Event()]
+
+    def run(n):
+        out = []
+        for i in range(n):
+            loss = step_fn(host[i % len(host)].to(device, non_blocking=True))
+            k = i % 2
+            pinned[k].copy_(loss.detach().reshape(1).float(), non_blocking=True)
+            events[k].record()
+            if i > 0:
+                events[1 - k].synchronize()
+                out.append(float(pinned[1 - k][0]))
+        events[(n - 1) % 2].synchronize()
+        out.append(float(pinned[(n - 1) % 2][0]))
+        return out
+
+    run(warm)
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    losses = run(K)
+    t1.record()
+    barrier()
+    return max_over_ranks(t0.elapsed_time(t1) / K), losses
+
+
 def count_our_launches(step_fn, batch) -> int:
     """Kernels of this repo launched by one step (torch profiler, untimed)."""
     import torch
@@ -259,26 +297,11 @@ def run_ours(args, rank, world, local):
     check_device_errors()
     e2e = None
     if not args.no_e2e:
-        def e2e_step(h):
-            tok = h.to(device, non_blocking=True)
-            loss = step(tok)
-            return loss.item()
-
-        for i in range(2):
-            e2e_step(host[i % nb])
-        barrier()
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record()
-        losses = []
-        for i in range(args.steps):
-            losses.append(e2e_step(host[i % nb]))
-        t1.record()
-        barrier()
-        e2e_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+        e2e_ms, losses = e2e_loop(step, host, args.steps, device)
         e2e = {"value": B * S * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": host[0].numel() * host[0].element_size(),
-               "d2h_bytes_per_step": 4, "api": "ParallelEngine.train_step + loss.item()",
+               "d2h_bytes_per_step": 4,
+               "api": "ParallelEngine.train_step; pinned async loss read-back, read one step behind",
                "last_loss": losses[-1]}
     launches = count_our_launches(step, dev[0]) * args.steps
     check_device_errors()
@@ -405,23 +428,11 @@ def run_reference(args, rank, world, local):
     ms = max_over_ranks(ms)
     e2e = None
     if not args.no_e2e:
-        def e2e_step(h):
-            return step(h.to(device, non_blocking=True)).item()
-
-        for i in range(2):
-            e2e_step(host[i % nb])
-        barrier()
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record()
-        for i in range(args.steps):
-            e2e_step(host[i % nb])
-        t1.record()
-        barrier()
-        e2e_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+        e2e_ms, _ = e2e_loop(step, host, args.steps, device)
         e2e = {"value": B * S * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": host[0].numel() * host[0].element_size(), "d2h_bytes_per_step": 4,
-               "api": "reference ParallelEngine.forward/backward/step + loss.item()"}
+               "api": "reference ParallelEngine.forward/backward/step; pinned async loss read-back, "
+                      "read one step behind (the same loop as ours)"}
     extra = {"reference_activation_checkpoint": bool(cfg.engine.activation_checkpoint)}
     if deviation:
         extra["deviation"] = deviation
