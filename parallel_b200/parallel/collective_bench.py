@@ -1,0 +1,227 @@
+"""Fused-collective micro-benchmarks: this repository's NVLink kernels against
+the reference's composition (NCCL collective + cuBLAS GEMM), one process per GPU.
+
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 -m parallel_b200.parallel.collective_bench \
+        [--cases ag_gemm,gemm_rs,fsdp_ag,fsdp_rs,ep,ce] [--quick] [--iters 10]
+
+Cases (bf16 N(0,1) inputs from a fixed seed):
+
+* ``ag_gemm``  all-gather of the sequence shard -> column-parallel GEMM
+  (``FusedSequenceParallel.all_gather_gemm`` vs ``all_gather_into_tensor`` + ``torch.matmul``);
+* ``gemm_rs``  row-parallel GEMM -> reduce-scatter (``gemm_reduce_scatter`` vs
+  ``torch.matmul`` + ``reduce_scatter_tensor``);
+* ``fsdp_ag`` / ``fsdp_rs``  flat-buffer all-gather / reduce-scatter (peer gather / N-peer
+  reduce kernels vs NCCL);
+* ``ep``  expert dispatch + combine of top-8 routes over 128 experts (peer row kernels
+  vs NCCL variable all-to-all);
+* ``ce``  vocabulary-parallel LM head + cross-entropy (peer log-sum-exp merge vs NCCL
+  all-reduces).
+
+Every time is device time with CUDA events after warm-up, the max over ranks.
+``roofline`` is the slower of the FLOPs at the measured bf16 GEMM peak and the
+bytes each GPU must receive over NVLink at the measured 770 GB/s peer copy;
+``frac`` = roofline / achieved time.  Rank 0 prints one JSON line per case.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+GEMM_PEAK = 1.70e15   # measured cuBLAS bf16 burst on this pool (FLOP/s)
+LINK_BW = 770e9       # measured peer copy per direction (B/s)
+
+
+def _time(fn, warmup, iters):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([s.elapsed_time(e) / iters * 1e3], device="cuda")  # us
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t)
+
+
+def _report(case, shape, ours_us, base_us, flops, link_bytes):
+    roof = max(flops / GEMM_PEAK, link_bytes / LINK_BW) * 1e6
+    return {"case": case, "shape": shape, "ours_us": round(ours_us, 1), "nccl_cublas_us": round(base_us, 1),
+            "speedup": round(base_us / ours_us, 3), "roofline_us": round(roof, 1),
+            "frac_of_roofline": round(roof / ours_us, 3)}
+
+
+def case_ag_gemm(W, rank, dev, M, K, N, warmup, iters):
+    from .model_parallel.fused_sp import FusedSequenceParallel
+
+    g = torch.Generator(device="cpu").manual_seed(rank)
+    x = torch.randn(M // W, K, generator=g).to(dev, torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) / K ** 0.5).to(dev, torch.bfloat16)
+    sp = FusedSequenceParallel(dist.group.WORLD, dev)
+    if not sp.supports(1, M, K):
+        return None
+    ours = _time(lambda: sp.all_gather_gemm(x, w, 1, M), warmup, iters)
+    full = torch.empty(M, K, device=dev, dtype=torch.bfloat16)
+
+    def base():
+        dist.all_gather_into_tensor(full, x)
+        torch.matmul(full, w.t())
+
+    return _report("ag_gemm", [M, K, N], ours, _time(base, warmup, iters), 2 * M * K * N, (W - 1) * (M // W) * K * 2)
+
+
+def case_gemm_rs(W, rank, dev, M, K, N, warmup, iters):
+    from .model_parallel.fused_sp import FusedSequenceParallel
+
+    g = torch.Generator(device="cpu").manual_seed(rank)
+    a = torch.randn(M, K, generator=g).to(dev, torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) / K ** 0.5).to(dev, torch.bfloat16)
+    sp = FusedSequenceParallel(dist.group.WORLD, dev)
+    if not sp.supports(1, M, N):
+        return None
+    ours = _time(lambda: sp.gemm_reduce_scatter(a, w, 1, M), warmup, iters)
+    out = torch.empty(M // W, N, device=dev, dtype=torch.bfloat16)
+
+    def base():
+        dist.reduce_scatter_tensor(out, torch.matmul(a, w.t()))
+
+    return _report("gemm_rs", [M, K, N], ours, _time(base, warmup, iters), 2 * M * K * N, (W - 1) * (M // W) * N * 2)
+
+
+def _flat_buffers(W, dev, nbytes):
+    from .comm.p2p import SymmBuffer
+
+    n = nbytes // 2 // (8 * W) * (8 * W)
+    buf = SymmBuffer(n, torch.bfloat16, dev, dist.group.WORLD)
+    buf.tensor[:n].normal_()
+    return buf, n
+
+
+def case_fsdp_ag(W, rank, dev, nbytes, warmup, iters):
+    from ..ops._ext import ext
+
+    buf, n = _flat_buffers(W, dev, nbytes)
+    shard = n // W
+    full = torch.empty(n, device=dev, dtype=torch.bfloat16)
+    src = [p for p in buf.peer_ptrs]
+    dst = [full.data_ptr() + r * shard * 2 for r in range(W)]
+
+    def ours():
+        buf.barrier(0, 60.0)
+        ext().p2p_copy(src, dst, [shard * 2] * W)
+
+    local = buf.tensor[:shard]
+    t_ours = _time(ours, warmup, iters)
+    t_base = _time(lambda: dist.all_gather_into_tensor(full, local), warmup, iters)
+    return _report("fsdp_ag", [n * 2 // (1 << 20), "MB"], t_ours, t_base, 0, (W - 1) * shard * 2)
+
+
+def case_fsdp_rs(W, rank, dev, nbytes, warmup, iters):
+    from ..ops._ext import ext
+
+    buf, n = _flat_buffers(W, dev, nbytes)
+    shard = n // W
+    out = torch.empty(shard, device=dev, dtype=torch.bfloat16)
+    src = [[p + rank * shard * 2] for p in buf.peer_ptrs]
+
+    def ours():
+        buf.barrier(1, 60.0)
+        ext().p2p_reduce(src, [out.data_ptr()], [shard], 1.0 / W, False)
+
+    t_ours = _time(ours, warmup, iters)
+    full = buf.tensor[:n]
+    t_base = _time(lambda: dist.reduce_scatter_tensor(out, full), warmup, iters)
+    return _report("fsdp_rs", [n * 2 // (1 << 20), "MB"], t_ours, t_base, 0, (W - 1) * shard * 2)
+
+
+def case_ep(W, rank, dev, tokens, hidden, experts, top_k, warmup, iters):
+    from .model_parallel.expert_parallel import ExpertPartition
+    from .model_parallel.p2p_dispatch import P2PTokenDispatcher
+    from .model_parallel.token_dispatch import TokenDispatcher
+
+    g = torch.Generator(device="cpu").manual_seed(rank)
+    x = torch.randn(tokens, hidden, generator=g).to(dev, torch.bfloat16)
+    idx = torch.stack([torch.randperm(experts, generator=g)[:top_k] for _ in range(tokens)]).to(dev)
+    sc = torch.rand(tokens, top_k, generator=g).to(dev)
+    part = ExpertPartition(experts, W, rank)
+    p2p = P2PTokenDispatcher(part, dist.group.WORLD, dev)
+    nccl = TokenDispatcher(part, dist.group.WORLD)
+
+    def run(d):
+        h, _, _, st = d.dispatch(x, idx, sc)
+        d.combine(h, st)
+
+    t_ours = _time(lambda: run(p2p), warmup, iters)
+    t_base = _time(lambda: run(nccl), warmup, iters)
+    # each route's row crosses the link to its owner and back (uniform routing)
+    link = 2 * tokens * top_k * hidden * 2 * (W - 1) / W
+    return _report("ep_dispatch_combine", [tokens, hidden, experts, top_k], t_ours, t_base, 0, link)
+
+
+def case_ce(W, rank, dev, tokens, hidden, vocab, warmup, iters):
+    from .model_parallel.loss_parallel import vocab_parallel_lm_head_ce
+
+    g = torch.Generator(device="cpu").manual_seed(0)
+    h = torch.randn(tokens, hidden, generator=g).to(dev, torch.bfloat16)
+    w = (torch.randn(vocab // W, hidden, generator=torch.Generator().manual_seed(rank)) * 0.02).to(dev, torch.bfloat16)
+    labels = torch.randint(0, vocab, (tokens,), generator=g).to(dev)
+    v0 = rank * (vocab // W)
+    grp = dist.group.WORLD
+    t_ours = _time(lambda: vocab_parallel_lm_head_ce(h, w, labels, grp, v0, collectives="p2p"), warmup, iters)
+    t_base = _time(lambda: vocab_parallel_lm_head_ce(h, w, labels, grp, v0, collectives="nccl"), warmup, iters)
+    flops = 3 * 2 * tokens * hidden * (vocab // W)  # logits, dh, dW
+    return _report("vocab_parallel_ce", [tokens, hidden, vocab], t_ours, t_base, flops, 3 * tokens * 4 * (W - 1))
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--cases", default="ag_gemm,gemm_rs,fsdp_ag,fsdp_rs,ep,ce")
+    ap.add_argument("--quick", action="store_true", help="one shape per case")
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--iters", type=int, default=10)
+    args = ap.parse_args(argv)
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    W, rank = dist.get_world_size(), dist.get_rank()
+    cases = args.cases.split(",")
+    gemm_shapes = [(8192, 4096, 4096)] if args.quick else [(4096, 4096, 4096), (16384, 4096, 4096),
+                                                          (32768, 4096, 4096), (16384, 4096, 12288)]
+    flat = [64 << 20] if args.quick else [8 << 20, 64 << 20, 512 << 20]
+    results = []
+    for M, K, N in gemm_shapes:
+        if "ag_gemm" in cases:
+            results.append(case_ag_gemm(W, rank, dev, M, K, N, args.warmup, args.iters))
+        if "gemm_rs" in cases:
+            results.append(case_gemm_rs(W, rank, dev, M, K, N, args.warmup, args.iters))
+    for nb in flat:
+        if "fsdp_ag" in cases:
+            results.append(case_fsdp_ag(W, rank, dev, nb, args.warmup, args.iters))
+        if "fsdp_rs" in cases:
+            results.append(case_fsdp_rs(W, rank, dev, nb, args.warmup, args.iters))
+    if "ep" in cases:
+        for tokens in ([8192] if args.quick else [8192, 32768]):
+            results.append(case_ep(W, rank, dev, tokens, 2048, 128, 8, args.warmup, args.iters))
+    if "ce" in cases:
+        results.append(case_ce(W, rank, dev, 16384 if not args.quick else 8192, 1024, 151936, args.warmup,
+                               args.iters))
+    if rank == 0:
+        for r in results:
+            if r is not None:
+                print(json.dumps(dict(r, n_gpus=W)), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
