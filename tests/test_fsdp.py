@@ -295,3 +295,54 @@ def test_fsdp_reductions_reverse_order_at_most_two_in_flight(tmp_path):
     assert starts == [4, 3, 2, 1, 0], events  # unit 0 = root (embedding, final norm), 1..4 = layers
     assert max(n for kind, _, n in events if kind == "start") <= 2, events
     assert sorted(u for kind, u, _ in events if kind == "finish") == [0, 1, 2, 3, 4], events
+
+
+def _collective_count_worker(rank, world, ckpt, out):
+    import torch.distributed as dist
+
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.qwen3 import build_model
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    calls = {"all_gather": [], "reduce_scatter": []}
+    real_ag, real_rs = dist.all_gather_into_tensor, dist.reduce_scatter_tensor
+
+    def ag(*a, **k):
+        calls["all_gather"].append(a[1].numel())
+        return real_ag(*a, **k)
+
+    def rs(*a, **k):
+        calls["reduce_scatter"].append(a[1].numel())
+        return real_rs(*a, **k)
+
+    cfg = cpu_cfg(**{"parallel.dp_shard": world, "engine.activation_checkpoint": str(ckpt).lower()})
+    pc = ParallelConfig(cfg)
+    pc.set_device_mesh("cpu")
+    m = build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0)
+    eng = ParallelEngine(m, None, pc, cfg, torch.device("cpu"))
+    buckets = [u.bucket_numel for u in eng.fsdp_wrapper.units]
+    tok = torch.randint(0, 1024, (2, 33), generator=torch.Generator().manual_seed(rank))
+    dist.all_gather_into_tensor, dist.reduce_scatter_tensor = ag, rs
+    try:
+        loss = eng.forward(tok[:, :-1], tok[:, 1:]).loss
+        eng.backward(loss)
+    finally:
+        dist.all_gather_into_tensor, dist.reduce_scatter_tensor = real_ag, real_rs
+    if rank == 0:
+        torch.save({"calls": calls, "buckets": buckets}, out)
+
+
+@pytest.mark.parametrize("ckpt", [False, True])
+def test_fsdp_one_packed_collective_per_unit_each_way(tmp_path, ckpt):
+    """Every unit moves its whole flat bucket in ONE all-gather per gather and
+    ONE reduce-scatter per backward: the root unit (embedding, final norm) is
+    gathered once and kept; each layer is gathered for the forward and again
+    for its backward (resharded in between)."""
+    out = str(tmp_path / "calls.pt")
+    run_ranks(_collective_count_worker, 2, ckpt, out)
+    got = torch.load(out, weights_only=False)
+    buckets, calls = got["buckets"], got["calls"]
+    root, layers = buckets[0], buckets[1:]
+    assert sorted(calls["all_gather"]) == sorted([root] + 2 * layers), calls
+    assert sorted(calls["reduce_scatter"]) == sorted(2 * b for b in buckets), calls
