@@ -34,3 +34,30 @@ def _dispatch_worker(rank, world):
 
 def test_dispatch_combine_identity_and_grads():
     run_ranks(_dispatch_worker, 2)
+
+
+def _empty_receiver_worker(rank, world):
+    import torch.distributed as dist
+
+    from parallel_b200.parallel.model_parallel import ExpertPartition, TokenDispatcher
+
+    part = ExpertPartition(num_experts=4, ep_size=2, ep_rank=rank)
+    disp = TokenDispatcher(part, dist.group.WORLD)
+    T, K, H = 4, 2, 3
+    torch.manual_seed(10 + rank)
+    hidden = torch.randn(T, H, requires_grad=True)
+    idx = torch.tensor([[2, 3]] * T)  # every route of both ranks goes to rank 1's experts
+    scores = torch.rand(T, K)
+    h, e, s, state = disp.dispatch(hidden, idx, scores)
+    if rank == 0:
+        assert h.shape[0] == 0 and e.numel() == 0  # rank 0 receives nothing
+    else:
+        assert h.shape[0] == 2 * T * K
+    out = disp.combine(h * 2, state)
+    torch.testing.assert_close(out, hidden * 2 * K)
+    out.sum().backward()
+    torch.testing.assert_close(hidden.grad, torch.full_like(hidden, 2.0 * K))
+
+
+def test_dispatch_with_a_rank_receiving_no_tokens():
+    run_ranks(_empty_receiver_worker, 2)
