@@ -46,6 +46,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--collectives", default="auto")
     ap.add_argument("--no-graph", action="store_true", help="eager steps instead of the captured CUDA-graph step")
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor-parallel size (model-parallel configs; dp_shard = gpus / tp; eager steps)")
+    ap.add_argument("--sp", action="store_true", help="sequence parallelism over the TP group")
+    ap.add_argument("--ep", action="store_true", help="expert parallelism over the TP group (MoE models)")
     return ap.parse_args()
 
 
@@ -136,6 +140,8 @@ def dist_setup(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if args.tp < 1 or world % args.tp:
+        raise SystemExit(f"--tp {args.tp} must divide the {world} GPUs")
     torch.cuda.set_device(local)
     if world > 1 and not dist.is_initialized():
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
@@ -239,8 +245,18 @@ def make_cfg(args, world):
             f"model.max_seq_length={args.seq}", "model.learning_rate=1e-5", "model.clip_grad_norm=1.0",
             "config.device_type=cuda", "config.backend=nccl", "config.grad_accum_steps=1",
             "engine.activation_checkpoint=true", "engine.overlap_backward_reductions=true",
-            f"engine.collectives={args.collectives}", f"parallel.dp_shard={world}", "data.synthetic=true"]
+            f"engine.collectives={args.collectives}", f"parallel.dp_shard={world // args.tp}", "data.synthetic=true"]
+    if args.tp > 1:
+        over += [f"parallel.tp={args.tp}"] + ([f"parallel.sp={args.tp}"] if args.sp else []) + \
+            ([f"parallel.ep={args.tp}"] if args.ep else [])
     return merge(cfg, from_dotlist(over))
+
+
+def parallelism_name(args, world):
+    if args.tp > 1:
+        mp = f"tp{args.tp}" + (f"_sp{args.tp}" if args.sp else "") + (f"_ep{args.tp}" if args.ep else "")
+        return mp + (f"_dp_shard{world // args.tp}" if world // args.tp > 1 else "")
+    return f"dp_shard{world}" if world > 1 else "single"
 
 
 def run_ours(args, rank, world, local):
@@ -261,15 +277,25 @@ def run_ours(args, rank, world, local):
     if args.layers:
         mcfg.num_hidden_layers = args.layers
     pconfig.model_init_rngs(seed=42)
-    model = build_model(mcfg, dtype=torch.bfloat16, seed=1234)
-    if world == 1:
+    if args.tp > 1:
+        # model-parallel configs: each rank builds only its local shards (random init)
+        from parallel_b200.models.loading import load_causal_lm
+
+        model, plan = load_causal_lm(cfg, pconfig, dtype=torch.bfloat16, seed=1234)
         model.to(device)
-        model._layout_fused_weights()
-    model.train()
-    engine = ParallelEngine(model, None, pconfig, cfg, device)
+        model.train()
+        engine = ParallelEngine(model, None, pconfig, cfg, device, mp_plan=plan)
+    else:
+        model = build_model(mcfg, dtype=torch.bfloat16, seed=1234)
+        if world == 1:
+            model.to(device)
+            model._layout_fused_weights()
+        model.train()
+        engine = ParallelEngine(model, None, pconfig, cfg, device)
     pconfig.model_train_rngs(seed=42)
     B, S, V = args.batch, args.seq, mcfg.vocab_size
-    gen = torch.Generator(device="cpu").manual_seed(1000 + rank)
+    # ranks of one TP group train on the same batch (data parallelism is across groups)
+    gen = torch.Generator(device="cpu").manual_seed(1000 + rank // args.tp)
     nb = 4
     host = [torch.randint(0, V, (B, S + 1), generator=gen).pin_memory() for _ in range(nb)]
     dev = [h.to(device) for h in host]
@@ -283,7 +309,8 @@ def run_ours(args, rank, world, local):
     clocks.start()
     for i in range(args.warmup):
         step(dev[i % nb])
-    use_graph = not args.no_graph and os.environ.get("PB_GRAPH", "1") != "0"
+    # (the captured step covers data parallelism; model-parallel steps run eagerly)
+    use_graph = not args.no_graph and args.tp == 1 and os.environ.get("PB_GRAPH", "1") != "0"
     if use_graph:
         # one more eager step on the capture stream, then the capture (untimed)
         engine.capture_train_step(dev[0][:, :-1], dev[0][:, 1:], warmup=1)
@@ -298,7 +325,7 @@ def run_ours(args, rank, world, local):
     e2e = None
     if not args.no_e2e:
         e2e_ms, losses = e2e_loop(step, host, args.steps, device)
-        e2e = {"value": B * S * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+        e2e = {"value": B * S * (world // args.tp) / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": host[0].numel() * host[0].element_size(),
                "d2h_bytes_per_step": 4,
                "api": "ParallelEngine.train_step; pinned async loss read-back, read one step behind",
@@ -429,7 +456,7 @@ def run_reference(args, rank, world, local):
     e2e = None
     if not args.no_e2e:
         e2e_ms, _ = e2e_loop(step, host, args.steps, device)
-        e2e = {"value": B * S * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+        e2e = {"value": B * S * (world // args.tp) / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": host[0].numel() * host[0].element_size(), "d2h_bytes_per_step": 4,
                "api": "reference ParallelEngine.forward/backward/step; pinned async loss read-back, "
                       "read one step behind (the same loop as ours)"}
@@ -460,7 +487,7 @@ def main():
     else:
         ms, clk, e2e, launches, extra = run_ours(args, rank, world, local)
     B, S = args.batch, args.seq
-    tokens_per_step = B * S * world
+    tokens_per_step = B * S * (world // args.tp)  # one batch per data-parallel replica
     value = tokens_per_step / (ms / 1e3)
     line = {
         "metric": METRIC,
@@ -475,8 +502,8 @@ def main():
         "vs_baseline": (value / BASELINE_VALUE) if BASELINE_VALUE else None,
         "dtype": "bf16",
         "data": "synthetic (uniform random token ids, random-init weights)",
-        "config": {"model": args.model, "global_batch": B * world, "per_device_batch": B, "seq_len": S,
-                   "parallelism": f"dp_shard{world}" if world > 1 else "single",
+        "config": {"model": args.model, "global_batch": B * (world // args.tp), "per_device_batch": B, "seq_len": S,
+                   "parallelism": parallelism_name(args, world),
                    "activation_checkpoint": world > 1, "overlap_backward_reductions": True,
                    "l2": "working set (weights + activations, several GB) exceeds the 126 MB L2; no flush",
                    **extra},
