@@ -168,8 +168,10 @@ class Experts(nn.Module):
 class SparseMoeBlock(nn.Module):
     def __init__(self, cfg: ModelConfig, ep: int = 1):
         super().__init__()
-        self.gate = TopKRouter(cfg)
+        # registration order = HF's (experts, then the router): the FSDP bucket
+        # layout follows parameter order, so exact-topology checkpoints depend on it
         self.experts = Experts(cfg, cfg.num_experts // ep)
+        self.gate = TopKRouter(cfg)
         self.num_experts = cfg.num_experts
         self.top_k = cfg.num_experts_per_tok
 

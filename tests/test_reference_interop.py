@@ -78,7 +78,7 @@ def _train(engine, data, rank, world, steps):
     return losses
 
 
-def _worker(rank, world, tmp, out):
+def _worker(rank, world, tmp, out, name="tiny-qwen3"):
     import torch.distributed as dist
 
     from parallel_b200.models.config import resolve_config
@@ -87,7 +87,7 @@ def _worker(rank, world, tmp, out):
 
     path = os.path.join(tmp, "init")
     if rank == 0:
-        save_pretrained(build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0), path)
+        save_pretrained(build_model(resolve_config(name), dtype=torch.float32, seed=0), path)
     dist.barrier()
     g = torch.Generator().manual_seed(3)
     data = [torch.randint(0, 1024, (2 * world, 65), generator=g) for _ in range(STEPS + 1)]
@@ -104,18 +104,38 @@ def _worker(rank, world, tmp, out):
     ours_b.load_checkpoint(os.path.join(tmp, "ref"))
     ref_b = _ref_engine(path, world)
     ref_b.load_checkpoint(os.path.join(tmp, "ours"))
+    # portable full-model files, each loaded by the other implementation: the
+    # loaded weights equal the writer's weights exactly
+    ours.save_full_model(os.path.join(tmp, "ours_full.pt"))
+    ref.save_full_model(os.path.join(tmp, "ref_full.pt"))
+    dist.barrier()
+    ours_c = _our_engine(path, world)
+    ours_c.load_full_model(os.path.join(tmp, "ref_full.pt"))
+    ref_c = _ref_engine(path, world)
+    ref_c.load_full_model(os.path.join(tmp, "ours_full.pt"))
+    # state_dict() is collective; the full dicts land on rank 0
+    pairs = [(ours_c.state_dict(), ref.state_dict()), (ref_c.state_dict(), ours.state_dict())]
+    worst, same_keys = 0.0, True
+    if rank == 0:
+        for got, src in pairs:
+            same_keys = same_keys and sorted(got) == sorted(src)
+            worst = max([worst] + [(got[k].float() - v.float()).abs().max().item() for k, v in src.items() if k in got])
     nxt = data[STEPS:]
     cont = {"ours": _train(ours, nxt, rank, world, 1), "ref": _train(ref, nxt, rank, world, 1),
             "ours_from_ref": _train(ours_b, nxt, rank, world, 1), "ref_from_ours": _train(ref_b, nxt, rank, world, 1)}
     if rank == 0:
-        torch.save({"ours": l_ours, "ref": l_ref, "cont": cont}, out)
+        torch.save({"ours": l_ours, "ref": l_ref, "cont": cont, "full_worst": worst, "full_keys": same_keys}, out)
     dist.barrier()
 
 
-def test_losses_and_checkpoints_interchange_with_the_reference(tmp_path):
+@pytest.mark.parametrize("name", ["tiny-qwen3", "tiny-qwen3-moe"])
+def test_losses_and_checkpoints_interchange_with_the_reference(tmp_path, name):
     out = str(tmp_path / "res.pt")
-    run_ranks(_worker, 2, str(tmp_path), out)
+    run_ranks(_worker, 2, str(tmp_path), out, name)
     res = torch.load(out, weights_only=False)
+    # portable full-model files: same keys, and after loading the other
+    # implementation's file both hold the same trained weights
+    assert res["full_keys"] and res["full_worst"] == 0.0, res
     # fp32 on CPU: the same losses step by step (bit-identical on this image)
     for a, b in zip(res["ours"], res["ref"]):
         assert abs(a - b) < 1e-5 * max(1.0, abs(b)), res
