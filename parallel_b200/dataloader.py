@@ -164,9 +164,7 @@ def dist_data_loader(tokenizer, B, T, split, tokenizer_batch_size=128, device="c
 
     use_cuda = torch.device(device).type == "cuda"
     rows = torch.empty((B, cap), dtype=torch.long)
-    cpu = torch.empty(2 * B * T, dtype=torch.long, pin_memory=use_cuda)
     dev = torch.empty(2 * B * T, dtype=torch.long, device=device)
-    cpu_x, cpu_y = cpu[:B * T].view(B, T), cpu[B * T:].view(B, T)
     x, y = dev[:B * T].view(B, T), dev[B * T:].view(B, T)
     while True:
         for r in range(B):
@@ -183,8 +181,12 @@ def dist_data_loader(tokenizer, B, T, split, tokenizer_batch_size=128, device="c
                     doc = buf.pop_shortest()
                     rows[r, pos:pos + rem] = torch.tensor(doc[:rem], dtype=torch.long)
                     pos += rem
-        cpu_x.copy_(rows[:, :-1])
-        cpu_y.copy_(rows[:, 1:])
+        # a fresh pinned staging tensor per batch (from the caching host allocator,
+        # which keeps it alive until its asynchronous copy has run): refilling one
+        # reused buffer could overwrite a batch whose copy is still queued
+        cpu = torch.empty(2 * B * T, dtype=torch.long, pin_memory=use_cuda)
+        cpu[:B * T].view(B, T).copy_(rows[:, :-1])
+        cpu[B * T:].view(B, T).copy_(rows[:, 1:])
         state = {**pos_state, "doc_buffer": buf.docs, "dataset": identity, "loader_config": loader_config}
         dev.copy_(cpu, non_blocking=use_cuda)
         yield x, y, state
@@ -195,10 +197,12 @@ def synthetic_data_loader(B, T, vocab_size, device="cuda", seed: int = 0, pconfi
     rank = pconfig.data_rank if pconfig is not None else 0
     step = int(resume_state_dict.get("step", 0)) if resume_state_dict else 0
     use_cuda = torch.device(device).type == "cuda"
-    cpu = torch.empty((B, T + 1), dtype=torch.long, pin_memory=use_cuda)
     while True:
         g = torch.Generator().manual_seed(seed * 1_000_003 + rank * 7919 + step)
-        cpu.copy_(torch.randint(0, vocab_size, (B, T + 1), generator=g))
-        tok = cpu.to(device, non_blocking=use_cuda)
+        # a fresh host tensor per batch: a reused buffer would alias the previous
+        # batch on CPU and could be refilled before its asynchronous copy ran on
+        # CUDA (the pinned block is kept alive by the host allocator until then)
+        host = torch.randint(0, vocab_size, (B, T + 1), generator=g)
+        tok = host.pin_memory().to(device, non_blocking=True) if use_cuda else host
         step += 1
         yield tok[:, :-1], tok[:, 1:], {"step": step, "synthetic": True, "seed": seed, "data_rank": rank}

@@ -1,0 +1,40 @@
+"""The training entry point end to end on CPU (synthetic data): logging,
+checkpoint cadence, and an exact resume of model, optimizer, RNG and data
+stream from a saved checkpoint."""
+import os
+import re
+import subprocess
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _run(tmp, extra):
+    env = dict(os.environ, PYTHONPATH=ROOT, WANDB_MODE="disabled")
+    args = [sys.executable, "-m", "parallel_b200.train", f"model.name={tmp}/init", "config.device_type=cpu",
+            "config.backend=gloo", "config.use_amp=false", "data.synthetic=true", "config.max_steps=4",
+            "config.eval_interval=100", "config.eval_steps=1", "config.grad_accum_steps=2",
+            "config.checkpoint_interval=2", f"config.checkpoint_dir={tmp}/ckpt", "model.per_device_batch_size=2",
+            "model.max_seq_length=32", "model.learning_rate=1e-3"] + extra
+    out = subprocess.run(args, env=env, cwd=tmp, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-3000:]
+    return {int(m.group(1)): float(m.group(2))
+            for m in re.finditer(r"step\s+(\d+) \| loss ([0-9.]+)", out.stdout + out.stderr)}
+
+
+def test_train_cli_checkpoint_and_exact_resume(tmp_path):
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.loading import save_pretrained
+    from parallel_b200.models.qwen3 import build_model
+
+    tmp = str(tmp_path)
+    save_pretrained(build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0), f"{tmp}/init")
+    full = _run(tmp, [])
+    assert sorted(full) == [1, 2, 3, 4], full
+    assert os.path.isdir(f"{tmp}/ckpt/step-00000002") and os.path.isdir(f"{tmp}/ckpt/step-00000004")
+    resumed = _run(tmp, [f"config.resume_from={tmp}/ckpt/step-00000002", f"config.checkpoint_dir={tmp}/ckpt2"])
+    assert sorted(resumed) == [3, 4], resumed
+    for s in (3, 4):
+        assert resumed[s] == full[s], (full, resumed)
