@@ -107,7 +107,9 @@ class FusedSequenceParallel:
             epi, n_out, up = EPI_STORE_BF16, 0, 0
         self.flag_calls[k] += 1
         target = self.flag_calls[k] * _PIECES_PER_BLOCK
-        with collective_profile("sp_all_gather_gemm", value=x_local, mode="fused"):
+        n_cols = 2 * swiglu_inter if swiglu_inter else out.shape[1]
+        with collective_profile("sp_all_gather_gemm", value=x_local, mode="fused", flops=2.0 * T * K * n_cols,
+                                link_bytes=(self.world - 1) * rows_local * K * 2):
             buf.barrier(0, self.limit_s)
             ext().gemm_ag(x_full, buf.peer_ptrs, K, self.flags[k], target, seq, seq // self.world, batch,
                           self._block_order(batch, seq), b, out, b_mn, epi, 1.0, gu_out, up, n_out)
@@ -125,7 +127,9 @@ class FusedSequenceParallel:
         buf = self.rs[k]
         y = torch.empty(rows_local, N, device=a_full.device, dtype=torch.bfloat16)
         slot_elems = rows_local * N
-        with collective_profile("sp_gemm_reduce_scatter", payload_bytes=a_full.shape[0] * N * 2, mode="fused"):
+        with collective_profile("sp_gemm_reduce_scatter", payload_bytes=a_full.shape[0] * N * 2, mode="fused",
+                                flops=2.0 * a_full.shape[0] * a_full.shape[1] * N,
+                                link_bytes=(self.world - 1) * rows_local * N * 2):
             ext().gemm_rs(a_full, b, b_mn, 1.0, buf.peer_ptrs, N, seq, seq // self.world, self.rank, rows_local)
             buf.barrier(0, self.limit_s)
             base = buf.tensor.data_ptr()
@@ -242,7 +246,8 @@ class FusedTensorParallel:
         rs, red = self.rs[k], self.red[k]
         slot = rows_local * N
         y = torch.empty(M, N, device=a.device, dtype=torch.bfloat16)
-        with collective_profile("tp_gemm_all_reduce", payload_bytes=M * N * 2, mode="fused"):
+        with collective_profile("tp_gemm_all_reduce", payload_bytes=M * N * 2, mode="fused",
+                                flops=2.0 * M * a.shape[1] * N, link_bytes=2 * (self.world - 1) * slot * 2):
             ext().gemm_rs(a, b, b_mn, 1.0, rs.peer_ptrs, N, M, rows_local, self.rank, rows_local)
             self._reduce_and_gather(rs, red, y, slot)
         self.n += 1

@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import logging
 import math
+import os
 from collections import defaultdict
 from contextlib import ContextDecorator, contextmanager
 from dataclasses import dataclass
@@ -44,6 +45,14 @@ class CollectiveRecord:
     ev_start: Any = None
     ev_end: Any = None
     cuda_ms: float | None = None
+    link_bytes: int = 0
+
+
+def _roofline_peaks() -> tuple[float, float]:
+    """(bf16 GEMM FLOP/s, NVLink peer bytes/s) used for roofline fractions."""
+    tf = float(os.environ.get("PB_ROOFLINE_TFLOPS", "1700"))
+    gbps = float(os.environ.get("PB_ROOFLINE_LINK_GBPS", "770"))
+    return tf * 1e12, gbps * 1e9
 
 
 def _nbytes(t: Any) -> int:
@@ -101,7 +110,8 @@ class CollectiveProfiler:
 
         rank = dist.get_rank() if dist.is_initialized() else 0
         mine = [dict(rank=rank, operation=r.operation, phase=r.phase, mode=r.mode, detail=r.detail,
-                     payload_bytes=r.payload_bytes, cpu_ms=r.cpu_ms, cuda_ms=r.cuda_ms, flops=r.flops)
+                     payload_bytes=r.payload_bytes, cpu_ms=r.cpu_ms, cuda_ms=r.cuda_ms, flops=r.flops,
+                     link_bytes=r.link_bytes)
                 for r in self.records]
         if dist.is_initialized():
             everyone: list[Any] = [None] * dist.get_world_size()
@@ -131,6 +141,10 @@ class CollectiveProfiler:
             fl = sum(r["flops"] for r in recs)
             if fl and total > 0:
                 line += f" tflops/rank={fl / len(per_rank) / (total * 1e-3) / 1e12:.1f}"
+                peak_flops, link_bw = _roofline_peaks()
+                lb = sum(r.get("link_bytes", 0) for r in recs)
+                roof_ms = max(fl / peak_flops, lb / link_bw) / len(per_rank) * 1e3
+                line += f" roofline={roof_ms:.3f}ms frac={roof_ms / total:.2f}"
             lines.append(line)
         self.records.clear()
         return lines
@@ -183,7 +197,8 @@ class _CollectiveScope:
         if self._rf is not None:
             self._rf.__exit__(*exc)
         self._rec = CollectiveRecord(self.operation, self.phase, self.mode, self.detail, self.payload_bytes,
-                                     cpu_ms, self.flops, self._ev0, self._ev1)
+                                     cpu_ms, self.flops, self._ev0, self._ev1,
+                                     link_bytes=getattr(self, "link_bytes", 0))
         if not self.defer_cuda_end:
             _COLLECTIVE_PROFILER.add(self._rec)
         return False
@@ -228,13 +243,20 @@ def collective_phase(phase: str):
 
 def collective_profile(operation: str, *, value: Any = None, payload_bytes: int | None = None, mode: str = "",
                        detail: str = "", device: Any = None, defer_cuda_end: bool = False,
-                       flops: float = 0.0) -> _CollectiveScope:
+                       flops: float = 0.0, link_bytes: int = 0) -> _CollectiveScope:
+    """``flops`` / ``link_bytes`` (fused GEMM + collective ops): the step line then
+    adds the achieved TF/s and the fraction of the op's roofline, the slower of
+    the FLOPs at the bf16 GEMM peak and the bytes this rank receives over NVLink
+    at the peer-copy bandwidth (``PB_ROOFLINE_TFLOPS`` / ``PB_ROOFLINE_LINK_GBPS``,
+    defaults: the measured 1700 TF/s and 770 GB/s of this B200 pool)."""
     if payload_bytes is None:
         payload_bytes = _nbytes(value) if value is not None else 0
     if device is None and value is not None:
         device = value.device
-    return _CollectiveScope(operation, mode=mode, detail=detail, payload_bytes=payload_bytes, device=device,
-                            defer_cuda_end=defer_cuda_end, flops=flops)
+    scope = _CollectiveScope(operation, mode=mode, detail=detail, payload_bytes=payload_bytes, device=device,
+                             defer_cuda_end=defer_cuda_end, flops=flops)
+    scope.link_bytes = link_bytes
+    return scope
 
 
 def scheduled_torch_profiler(*, enabled: bool, trace_dir: str | Path, rank: int, warmup_steps: int = 1,

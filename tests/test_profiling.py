@@ -57,6 +57,24 @@ def test_collective_aggregation_line():
     P.configure_collective_profiling(enabled=False)
 
 
+def test_fused_op_line_reports_tflops_and_roofline_fraction(monkeypatch):
+    monkeypatch.setenv("PB_ROOFLINE_TFLOPS", "1000")
+    monkeypatch.setenv("PB_ROOFLINE_LINK_GBPS", "500")
+    P.configure_collective_profiling(enabled=True, device=None)
+    P.start_collective_profile_step()
+    times = iter([0.0, 0.004])
+    with mock.patch.object(P, "perf_counter", side_effect=lambda: next(times)):
+        with P.collective_phase("forward"):
+            # 2 TFLOP and 1 GB over the link in 4 ms: roofline = max(2 ms, 2 ms) = 2 ms
+            with P.collective_profile("sp_all_gather_gemm", payload_bytes=1 << 20, mode="fused", flops=2e12,
+                                      link_bytes=1_000_000_000):
+                pass
+    (line,) = P.finish_collective_profile_step()
+    assert "op=sp_all_gather_gemm mode=fused" in line
+    assert "tflops/rank=500.0" in line and "roofline=2.000ms frac=0.50" in line, line
+    P.configure_collective_profiling(enabled=False)
+
+
 def test_deferred_completion_records_only_after_complete():
     P.configure_collective_profiling(enabled=True)
     P.start_collective_profile_step()
