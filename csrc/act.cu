@@ -57,29 +57,6 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dh, int64_t 
   }
 }
 
-__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, int64_t ldgu,
-                                  __nv_bfloat16* __restrict__ h, int64_t ldh, int T, int I) {
-  const int vec_per_row = I / 8;
-  const int64_t total = (int64_t)T * vec_per_row;
-  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int t = (int)(idx / vec_per_row);
-    const int c = (int)(idx % vec_per_row) * 8;
-    uint4 graw = *reinterpret_cast<const uint4*>(gu + (int64_t)t * ldgu + c);
-    uint4 uraw = *reinterpret_cast<const uint4*>(gu + (int64_t)t * ldgu + I + c);
-    const uint32_t* gp = &graw.x;
-    const uint32_t* up = &uraw.x;
-    uint4 o;
-    uint32_t* op = &o.x;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float2 g2 = unpack_bf16x2(gp[q]), u2 = unpack_bf16x2(up[q]);
-      op[q] = pack_bf16x2(g2.x * sigmoid_f(g2.x) * u2.x, g2.y * sigmoid_f(g2.y) * u2.y);
-    }
-    *reinterpret_cast<uint4*>(h + (int64_t)t * ldh + c) = o;
-  }
-}
-
 // One warp per token; H % 8 == 0.
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids,
                                      const __nv_bfloat16* __restrict__ table, int64_t ldt,
@@ -184,13 +161,6 @@ __global__ void cast_f32_bf16_kernel(const float* __restrict__ src, __nv_bfloat1
   }
 }
 
-__global__ void add_bf16_kernel(__nv_bfloat16* __restrict__ dst, const __nv_bfloat16* __restrict__ src,
-                                int64_t n, float alpha) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x)
-    dst[i] = __float2bfloat16(__bfloat162float(dst[i]) + alpha * __bfloat162float(src[i]));
-}
-
 int grid_for(int64_t work, int threads) {
   int64_t g = (work + threads - 1) / threads;
   const int64_t cap = (int64_t)num_sms() * 16;
@@ -205,13 +175,6 @@ void swiglu_bwd(const void* dh, int64_t lddh, const void* gu, int64_t ldgu, void
   PB_CHECK(I % 8 == 0, "swiglu: I must be a multiple of 8");
   swiglu_bwd_kernel<<<grid_for((int64_t)T * I / 8, 256), 256, 0, s>>>(
       (const __nv_bfloat16*)dh, lddh, (const __nv_bfloat16*)gu, ldgu, (__nv_bfloat16*)dgu, lddgu, T, I);
-  PB_CUDA_CHECK(cudaGetLastError());
-}
-
-void swiglu_fwd(const void* gu, int64_t ldgu, void* h, int64_t ldh, int T, int I, cudaStream_t s) {
-  PB_CHECK(I % 8 == 0, "swiglu: I must be a multiple of 8");
-  swiglu_fwd_kernel<<<grid_for((int64_t)T * I / 8, 256), 256, 0, s>>>(
-      (const __nv_bfloat16*)gu, ldgu, (__nv_bfloat16*)h, ldh, T, I);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -243,12 +206,6 @@ void scale_by_scalar(void* x, int64_t n, const float* s_dev, cudaStream_t s) {
 
 void cast_f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t s) {
   cast_f32_bf16_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, s>>>(src, (__nv_bfloat16*)dst, n);
-  PB_CUDA_CHECK(cudaGetLastError());
-}
-
-void add_bf16_inplace(void* dst, const void* src, int64_t n, float alpha, cudaStream_t s) {
-  add_bf16_kernel<<<grid_for(n, 256), 256, 0, s>>>((__nv_bfloat16*)dst, (const __nv_bfloat16*)src, n,
-                                                   alpha);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

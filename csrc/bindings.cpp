@@ -235,6 +235,12 @@ void gemm_grouped(int64_t mode, const at::Tensor& a, const at::Tensor& b, at::Te
 
 int64_t read_error(int64_t device) { return pb::read_error((int)device); }
 void clear_error(int64_t device) { pb::clear_error((int)device); }
+// Test hook: write an error code into the device's error word from the host
+// (what a bounded device wait that gave up would leave there).
+void set_error_for_test(int64_t device, int64_t code) {
+  const int c = (int)code;
+  PB_CUDA_CHECK(cudaMemcpy(pb::error_word((int)device), &c, sizeof(int), cudaMemcpyHostToDevice));
+}
 
 }  // namespace
 
@@ -264,6 +270,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("r") = pybind11::none(), pybind11::arg("b_up_offset") = 0, pybind11::arg("n_out") = 0);
   m.def("read_error", &read_error);
   m.def("clear_error", &clear_error);
+  m.def("set_error_for_test", &set_error_for_test);
   register_ops(m);
   register_comm(m);
 }

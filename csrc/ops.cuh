@@ -40,7 +40,6 @@ void qknorm_rope_bwd(const void* dq, int64_t lddq, const void* dk, int64_t lddk,
 void swiglu_bwd(const void* dh, int64_t lddh, const void* gu, int64_t ldgu, void* dgu,
                 int64_t lddgu, int T, int I, cudaStream_t s);
 // h = silu(g) * u (used on the CPU-parity path and by the MoE experts)
-void swiglu_fwd(const void* gu, int64_t ldgu, void* h, int64_t ldh, int T, int I, cudaStream_t s);
 
 // ---- embedding (act.cu)
 void embedding_fwd(const int64_t* ids, const void* table, int64_t ldt, void* out, int64_t ldo,
@@ -69,7 +68,6 @@ void ce_row_stats(const void* logits, int64_t ld, int T, int V, float* row_max, 
 
 // ---- casts / elementwise helpers (act.cu)
 void cast_f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t s);
-void add_bf16_inplace(void* dst, const void* src, int64_t n, float alpha, cudaStream_t s);
 
 // ---- optimizer (optim.cu)
 // Multi-tensor AdamW over `n` segments.  Each segment: param (bf16),

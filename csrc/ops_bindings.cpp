@@ -80,12 +80,6 @@ void swiglu_bwd(const at::Tensor& dh, const at::Tensor& gu, at::Tensor& dgu) {
                  dh.size(0), dh.size(1), cur_stream());
 }
 
-void swiglu_fwd(const at::Tensor& gu, at::Tensor& h) {
-  CHECK_BF16(gu); CHECK_BF16(h);
-  const c10::cuda::CUDAGuard g(gu.device());
-  pb::swiglu_fwd(gu.data_ptr(), gu.stride(0), h.data_ptr(), h.stride(0), h.size(0), h.size(1), cur_stream());
-}
-
 void embedding_fwd(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int64_t v0) {
   TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "ids must be contiguous int64");
   CHECK_BF16(table); CHECK_BF16(out);
@@ -318,7 +312,6 @@ void register_ops(pybind11::module& m) {
   m.def("qknorm_rope_fwd", &qknorm_rope_fwd);
   m.def("qknorm_rope_bwd", &qknorm_rope_bwd);
   m.def("swiglu_bwd", &swiglu_bwd);
-  m.def("swiglu_fwd", &swiglu_fwd);
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("scale_by_scalar", &scale_by_scalar);

@@ -41,6 +41,11 @@ def use_kernels(t: torch.Tensor) -> bool:
     return False
 
 
+def clear_device_errors(device: int | None = None) -> None:
+    if _C is not None:
+        _C.clear_error(torch.cuda.current_device() if device is None else device)
+
+
 def check_device_errors(device: int | None = None) -> None:
     """Raise if any kernel on ``device`` recorded a bounded-wait timeout."""
     if _C is None:

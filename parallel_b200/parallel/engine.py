@@ -77,6 +77,7 @@ class ParallelEngine:
         # asynchronous read-back of the non-finite flag: copied into pinned
         # host memory behind an event at the end of step k, read at step k+1
         self._flag_host: torch.Tensor | None = None
+        self._err_host: torch.Tensor | None = None
         self._flag_event = None
         self._last_grad_norm: torch.Tensor | None = None
         self._graph = None
@@ -213,15 +214,26 @@ class ParallelEngine:
     def _check_pending_nonfinite(self):
         if self._pending_nonfinite is None:
             return
+        err = 0
         if self._flag_event is not None:
             # waits only for the end of the previous optimizer step, which the
             # GPU has normally passed long ago (no pipeline drain)
             self._flag_event.synchronize()
             bad = bool(self._flag_host[0].item())
+            err = int(self._err_host[0]) if self._err_host is not None else 0
             self._flag_event = None
         else:
             bad = bool(self._pending_nonfinite.item())
         self._pending_nonfinite = None
+        if err:
+            # a bounded device wait gave up during that step (its results are not
+            # trustworthy): clear the word and fail on every rank that saw it
+            from ..ops._ext import clear_device_errors
+            from .comm.p2p import CollectiveTimeout
+
+            clear_device_errors(self.device.index)
+            msg = f"device error code {err} during the previous step (1 = pipeline wait, 2 = peer wait timeout)"
+            raise CollectiveTimeout(msg) if err == 2 else RuntimeError(msg)
         if bad:
             raise FloatingPointError("Non-finite gradients encountered")
 
@@ -230,7 +242,10 @@ class ParallelEngine:
         if flag.is_cuda:
             if self._flag_host is None:
                 self._flag_host = torch.zeros(1, dtype=flag.dtype, pin_memory=True)
+                self._err_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
             self._flag_host.copy_(flag.reshape(1), non_blocking=True)
+            # the device error word (bounded waits that timed out) travels with the flag
+            ext().error_word_copy_async(self._err_host)
             self._flag_event = torch.cuda.Event()
             self._flag_event.record()
 
@@ -260,7 +275,14 @@ class ParallelEngine:
     def _step_impl(self):
         capturing = self.device.type == "cuda" and torch.cuda.is_current_stream_capturing()
         if not capturing:
-            self._check_pending_nonfinite()
+            try:
+                self._check_pending_nonfinite()
+            except (FloatingPointError, RuntimeError):
+                # the previous step failed (reported one step late): this step is
+                # abandoned too, like the synchronous check's failing step
+                self.optimizer.zero_grad(set_to_none=True)
+                self.fsdp_wrapper.zero_grad()
+                raise
         self._average_gradients()
         if self.grad_scaler.is_enabled():
             self.grad_scaler.unscale_(self.optimizer)

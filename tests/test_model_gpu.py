@@ -109,3 +109,30 @@ def test_cuda_graph_step_matches_eager():
     sg = graphed.optimizer.state[next(iter(graphed.optimizer.state))]["step"]
     assert float(se) == float(sg) == 6.0
     graphed.release_graph()
+
+
+def test_device_error_word_surfaces_as_collective_timeout():
+    """A bounded device wait that gave up (its error word, written here from the
+    host) is read back asynchronously with the step's finite flag and raised at
+    the next step as CollectiveTimeout; the word is cleared."""
+    from parallel_b200.config import from_dotlist, load_cfg, merge
+    from parallel_b200.ops._ext import ext
+    from parallel_b200.parallel.comm.p2p import CollectiveTimeout
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    cfg, _, gpu = _pair("small-qwen3")
+    c = merge(load_cfg(argv=[]), from_dotlist(["config.device_type=cuda"]))
+    pc = ParallelConfig(c)
+    pc.set_device_mesh("cuda")
+    eng = ParallelEngine(gpu, None, pc, c, torch.device("cuda", 0))
+    tok = torch.randint(0, cfg.vocab_size, (2, 65), device="cuda")
+    eng.train_step(tok[:, :-1], tok[:, 1:])
+    torch.cuda.synchronize()
+    ext().set_error_for_test(0, 2)
+    eng.train_step(tok[:, :-1], tok[:, 1:])  # its read-back carries the error
+    with pytest.raises(CollectiveTimeout):
+        eng.train_step(tok[:, :-1], tok[:, 1:])
+    assert ext().read_error(0) == 0
+    eng.train_step(tok[:, :-1], tok[:, 1:])  # the engine keeps working
+    torch.cuda.synchronize()
