@@ -182,3 +182,30 @@ def test_route_localization():
     assert li.tolist() == [[4, 1], [3, 4]]
     assert ls.tolist() == [[0.0, 0.25], [0.125, 0.0]]
     assert mask.tolist() == [[False, True], [True, False]]
+
+
+@pytest.mark.parametrize("name,tp,sp,ep", [("Qwen/Qwen3-8B", 4, 4, 1), ("Qwen/Qwen3-30B-A3B", 4, 4, 4),
+                                         ("Qwen/Qwen3-0.6B", 2, 2, 1)])
+def test_benchmark_configurations_have_valid_plans(name, tp, sp, ep):
+    """The model-parallel configurations of the benchmarks (8B tp=sp=4, 30B-A3B
+    tp=sp=ep=4) build plans that cover every parameter of the local-shape model
+    with the expected shard shapes."""
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.qwen3 import Qwen3ForCausalLM
+    from parallel_b200.parallel.model_parallel import build_model_parallel_plan
+
+    cfg = resolve_config(name, num_hidden_layers=1)
+
+    class PC:
+        tp_size, sp_size, ep_size, expert_tp_size, dp_shard_size = tp, sp, ep, 1, 2
+
+    plan = build_model_parallel_plan(cfg, PC())
+    with torch.device("meta"):
+        local = Qwen3ForCausalLM(cfg, tp=tp, ep=ep)
+    params = dict(local.named_parameters())
+    plan.validate_parameter_coverage(params)
+    q = params["model.layers.0.self_attn.q_proj.weight"]
+    assert q.shape == (cfg.num_attention_heads * cfg.head_dim // tp, cfg.hidden_size)
+    if ep > 1:
+        gu = params["model.layers.0.mlp.experts.gate_up_proj"]
+        assert gu.shape[0] == cfg.num_experts // ep
