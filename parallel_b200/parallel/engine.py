@@ -284,6 +284,7 @@ class ParallelEngine:
                 self.fsdp_wrapper.zero_grad()
                 raise
         self._average_gradients()
+        self.fsdp_wrapper.stage_offloaded_gradients()
         if self.grad_scaler.is_enabled():
             self.grad_scaler.unscale_(self.optimizer)
         cuda = self.device.type == "cuda" and all(local_tensor(p).is_cuda for p in self.optimizer_params)

@@ -186,7 +186,9 @@ class FSDPWrapper:
             raise RuntimeError("FSDPWrapper.shard_model() can only be called once")
         self.dp_shard_mesh = self.pconfig.device_mesh[Strategies.DP_SHARD.value]
         self.dp_shard_group = self.dp_shard_mesh.get_group()
-        self.coll = make_unit_collectives(self.collectives_kind, self.device, self.dp_shard_group)
+        # host-resident shards cannot live in symmetric device memory
+        self.coll = make_unit_collectives("nccl" if self.cpu_offload else self.collectives_kind, self.device,
+                                          self.dp_shard_group)
         for buf in self.model.buffers():
             buf.data = buf.data.to(self.device)
         layers = get_fsdp_units(self.model)
@@ -419,6 +421,12 @@ class FSDPWrapper:
     def zero_grad(self) -> None:
         for u in self.units:
             u.zero_grad()
+
+    def stage_offloaded_gradients(self) -> None:
+        """cpu_offload: bring the reduced gradients to the host shards (no-op otherwise)."""
+        if self.cpu_offload:
+            for u in self.units:
+                u.stage_offloaded_gradients()
 
     # ------------------------------------------------------------------ params
     def get_optimizer_params(self) -> list[nn.Parameter]:

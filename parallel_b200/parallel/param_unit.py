@@ -134,7 +134,14 @@ class DPParamUnit:
         self.bucket_numel = off
         self.full_numel = foff
         dtype = self.param_metas[0].parameter.dtype
-        self.local_bucket = self.coll.alloc_local_bucket(self, self.bucket_numel, dtype, self.device)
+        if self.cpu_offload:
+            # shards (and, via the optimizer, its state) live in pinned host memory;
+            # the all-gather copies them to the device (the reference's cpu_offload,
+            # parallel/parallel/engine/_dp_param_unit.py:205-214,518-533)
+            self.local_bucket = torch.zeros(self.bucket_numel, dtype=dtype,
+                                            pin_memory=torch.cuda.is_available() and self.device.type == "cuda")
+        else:
+            self.local_bucket = self.coll.alloc_local_bucket(self, self.bucket_numel, dtype, self.device)
         self.local_bucket.zero_()
         root = dist.get_global_rank(self.group, 0)
         for m in self.param_metas:
@@ -260,7 +267,15 @@ class DPParamUnit:
         if not self._grad_valid:
             return
         part = participation or [True] * len(self.param_metas)
-        key = self.grad_bucket.data_ptr()
+        bucket = self.grad_bucket
+        if self.cpu_offload:
+            # gradients are exposed on the host next to the shards; the device
+            # bucket is copied in by stage_offloaded_gradients() before the step
+            if getattr(self, "_host_grad_bucket", None) is None:
+                self._host_grad_bucket = torch.zeros(self.bucket_numel, dtype=bucket.dtype,
+                                                     pin_memory=torch.cuda.is_available() and bucket.is_cuda)
+            bucket = self._host_grad_bucket
+        key = bucket.data_ptr()
         for keep, m in zip(part, self.param_metas):
             if not keep:
                 m.sharded_param.grad = None
@@ -269,13 +284,19 @@ class DPParamUnit:
             # (DTensor construction costs tens of microseconds of host time per call)
             cached = getattr(m, "_grad_view", None)
             if cached is None or cached[0] != key:
-                g = self.grad_bucket.narrow(0, m.bucket_offset, m.padded_numel).view(m.padded_rows, *m.shape[1:])
+                g = bucket.narrow(0, m.bucket_offset, m.padded_numel).view(m.padded_rows, *m.shape[1:])
                 local = g.narrow(0, 0, m.local_rows)
                 dt = DTensor.from_local(local, device_mesh=self.mesh, placements=(Shard(0),), run_check=False,
                                         shape=m.shape, stride=m.stride)
                 cached = (key, dt)
                 m._grad_view = cached
             m.sharded_param.grad = cached[1]
+
+    def stage_offloaded_gradients(self) -> None:
+        """cpu_offload: copy the reduced (and replica-averaged) device gradients
+        into the host bucket the ``.grad`` views cover."""
+        if self.cpu_offload and self._grad_valid and getattr(self, "_host_grad_bucket", None) is not None:
+            self._host_grad_bucket.copy_(self.grad_bucket)
 
     def zero_grad(self) -> None:
         """Start a new accumulation window (the bucket is reused, not freed)."""

@@ -37,14 +37,15 @@ def _single_process_losses(data, accum=1, clip=1.0):
     return losses, m
 
 
-def _fsdp_worker(rank, world, data, ckpt, overlap, accum, out_q):
+def _fsdp_worker(rank, world, data, ckpt, overlap, accum, out_q, offload=False):
     from parallel_b200.models.config import resolve_config
     from parallel_b200.models.qwen3 import build_model
     from parallel_b200.parallel.engine import ParallelEngine
     from parallel_b200.state import ParallelConfig
 
     cfg = cpu_cfg(**{"parallel.dp_shard": world, "engine.activation_checkpoint": str(ckpt).lower(),
-                     "engine.overlap_backward_reductions": str(overlap).lower(), "config.grad_accum_steps": accum})
+                     "engine.overlap_backward_reductions": str(overlap).lower(), "config.grad_accum_steps": accum,
+                     "engine.cpu_offload": str(offload).lower()})
     pc = ParallelConfig(cfg)
     pc.set_device_mesh("cpu")
     m = build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0)
@@ -65,13 +66,15 @@ def _fsdp_worker(rank, world, data, ckpt, overlap, accum, out_q):
         torch.save({"losses": losses, "state": full}, out_q)
 
 
-@pytest.mark.parametrize("ckpt,overlap,accum", [(True, True, 1), (False, True, 2), (True, False, 1)])
-def test_fsdp_matches_single_process(tmp_path, ckpt, overlap, accum):
-    """tiny Qwen3, dp_shard=2, fp32, 10 AdamW steps; loss equal to 1e-5."""
+@pytest.mark.parametrize("ckpt,overlap,accum,offload", [(True, True, 1, False), (False, True, 2, False),
+                                                        (True, False, 1, False), (False, True, 2, True)])
+def test_fsdp_matches_single_process(tmp_path, ckpt, overlap, accum, offload):
+    """tiny Qwen3, dp_shard=2, fp32, 10 AdamW steps; loss equal to 1e-5
+    (also with the shards and their gradients kept in host memory: cpu_offload)."""
     world = 2
     data = _tokens(world)
     out = str(tmp_path / "out.pt")
-    run_ranks(_fsdp_worker, world, data, ckpt, overlap, accum, out)
+    run_ranks(_fsdp_worker, world, data, ckpt, overlap, accum, out, offload)
     got = torch.load(out, weights_only=False)
     ref_losses, ref_model = _single_process_losses([t for t in data], accum=accum)
     for a, b in zip(got["losses"], ref_losses):
