@@ -21,13 +21,13 @@ pytestmark = pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "parallel", 
 STEPS = 3
 
 
-def _cfg(path, world):
-    cfg = cpu_cfg(**{"parallel.dp_shard": world, "model.name": path, "engine.activation_checkpoint": "false",
+def _cfg(path, world, dp="dp_shard"):
+    cfg = cpu_cfg(**{f"parallel.{dp}": world, "model.name": path, "engine.activation_checkpoint": "false",
                      "model.learning_rate": 1e-3})
     return cfg
 
 
-def _ref_engine(path, world):
+def _ref_engine(path, world, dp="dp_shard"):
     import sys
 
     sys.path.insert(0, REF)
@@ -39,7 +39,7 @@ def _ref_engine(path, world):
     from parallel.parallel.engine.model_loading import load_causal_lm as ref_load
     from parallel.parallel.state import ParallelConfig as RefPConfig
 
-    cfg = _cfg(path, world)
+    cfg = _cfg(path, world, dp)
     for key in ("collectives", "optimizer_state_dtype", "sync_finite_check"):
         cfg.engine.pop(key, None)
     cfg.data.pop("synthetic", None)
@@ -52,12 +52,12 @@ def _ref_engine(path, world):
     return RefEngine(model, None, pc, cfg, torch.device("cpu"), mp_plan=plan)
 
 
-def _our_engine(path, world):
+def _our_engine(path, world, dp="dp_shard"):
     from parallel_b200.models.loading import load_causal_lm
     from parallel_b200.parallel.engine import ParallelEngine
     from parallel_b200.state import ParallelConfig
 
-    cfg = _cfg(path, world)
+    cfg = _cfg(path, world, dp)
     pc = ParallelConfig(cfg)
     pc.set_device_mesh("cpu")
     pc.model_init_rngs(seed=42)
@@ -78,7 +78,7 @@ def _train(engine, data, rank, world, steps):
     return losses
 
 
-def _worker(rank, world, tmp, out, name="tiny-qwen3"):
+def _worker(rank, world, tmp, out, name="tiny-qwen3", dp="dp_shard"):
     import torch.distributed as dist
 
     from parallel_b200.models.config import resolve_config
@@ -92,26 +92,26 @@ def _worker(rank, world, tmp, out, name="tiny-qwen3"):
     g = torch.Generator().manual_seed(3)
     data = [torch.randint(0, 1024, (2 * world, 65), generator=g) for _ in range(STEPS + 1)]
 
-    ours = _our_engine(path, world)
-    ref = _ref_engine(path, world)
+    ours = _our_engine(path, world, dp)
+    ref = _ref_engine(path, world, dp)
     l_ours = _train(ours, data, rank, world, STEPS)
     l_ref = _train(ref, data, rank, world, STEPS)
 
     # exact-topology checkpoints, each loaded by the other implementation
     ours.save_checkpoint(os.path.join(tmp, "ours"), step=STEPS)
     ref.save_checkpoint(os.path.join(tmp, "ref"), step=STEPS)
-    ours_b = _our_engine(path, world)
+    ours_b = _our_engine(path, world, dp)
     ours_b.load_checkpoint(os.path.join(tmp, "ref"))
-    ref_b = _ref_engine(path, world)
+    ref_b = _ref_engine(path, world, dp)
     ref_b.load_checkpoint(os.path.join(tmp, "ours"))
     # portable full-model files, each loaded by the other implementation: the
     # loaded weights equal the writer's weights exactly
     ours.save_full_model(os.path.join(tmp, "ours_full.pt"))
     ref.save_full_model(os.path.join(tmp, "ref_full.pt"))
     dist.barrier()
-    ours_c = _our_engine(path, world)
+    ours_c = _our_engine(path, world, dp)
     ours_c.load_full_model(os.path.join(tmp, "ref_full.pt"))
-    ref_c = _ref_engine(path, world)
+    ref_c = _ref_engine(path, world, dp)
     ref_c.load_full_model(os.path.join(tmp, "ours_full.pt"))
     # state_dict() is collective; the full dicts land on rank 0
     pairs = [(ours_c.state_dict(), ref.state_dict()), (ref_c.state_dict(), ours.state_dict())]
@@ -128,10 +128,11 @@ def _worker(rank, world, tmp, out, name="tiny-qwen3"):
     dist.barrier()
 
 
-@pytest.mark.parametrize("name", ["tiny-qwen3", "tiny-qwen3-moe"])
-def test_losses_and_checkpoints_interchange_with_the_reference(tmp_path, name):
+@pytest.mark.parametrize("name,dp", [("tiny-qwen3", "dp_shard"), ("tiny-qwen3-moe", "dp_shard"),
+                                     ("tiny-qwen3", "dp_replicate")])
+def test_losses_and_checkpoints_interchange_with_the_reference(tmp_path, name, dp):
     out = str(tmp_path / "res.pt")
-    run_ranks(_worker, 2, str(tmp_path), out, name)
+    run_ranks(_worker, 2, str(tmp_path), out, name, dp)
     res = torch.load(out, weights_only=False)
     # portable full-model files: same keys, and after loading the other
     # implementation's file both hold the same trained weights
