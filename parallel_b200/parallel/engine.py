@@ -81,6 +81,7 @@ class ParallelEngine:
         self._flag_event = None
         self._last_grad_norm: torch.Tensor | None = None
         self._graph = None
+        self._graph_pending = None
         self._captured_flag: torch.Tensor | None = None
         self.reset_step_memory_stats()
 
@@ -189,10 +190,50 @@ class ParallelEngine:
         the next call)."""
         if self._graph is not None:
             return self._graph.replay(x, y)
+        if self._graph_pending is not None:
+            return self._pending_graph_step(x, y)
         outputs = self.forward(x, y)
         self.backward(outputs.loss)
         self.step()
         return outputs.loss.detach()
+
+    def enable_graph_capture(self, warmup_steps: int = 2):
+        """From the next ``train_step`` on: run ``warmup_steps`` ordinary steps
+        (each on its own batch) on the capture stream, then capture the step
+        at the following call and replay it from then on.  Unlike
+        ``capture_train_step`` no batch is trained on more than once, so a
+        training run's trajectory is the eager one.  This is what
+        ``engine.compile=true`` selects: the reference compiles the model with
+        ``torch.compile`` there (parallel/parallel/train.py:60-66); here the
+        kernels are already hand-written and the remaining cost is launch
+        overhead, which the graph removes."""
+        if self.device.type != "cuda":
+            raise NotImplementedError("engine.compile captures the training step as a CUDA graph; it needs a "
+                                      "CUDA device")
+        if warmup_steps < 1:
+            raise ValueError("at least one eager step must run on the capture stream before the capture")
+        self._graph = None
+        self._graph_pending = {"stream": torch.cuda.Stream(device=self.device), "left": int(warmup_steps)}
+
+    def _pending_graph_step(self, x, y):
+        from .graph_step import GraphedTrainStep
+
+        st = self._graph_pending
+        cur = torch.cuda.current_stream(self.device)
+        if st["left"] > 0:
+            st["left"] -= 1
+            st["stream"].wait_stream(cur)
+            with torch.cuda.stream(st["stream"]):
+                outputs = self.forward(x, y)
+                self.backward(outputs.loss)
+                self.step()
+                loss = outputs.loss.detach()
+            cur.wait_stream(st["stream"])
+            loss.record_stream(cur)
+            return loss
+        self._graph_pending = None
+        self._graph = GraphedTrainStep(self, x, y, warmup=0, stream=st["stream"])
+        return self._graph.replay(x, y)
 
     def capture_train_step(self, x, y, warmup: int = 3):
         """Run ``warmup`` eager steps on (x, y) (they train on it), then capture
@@ -201,7 +242,7 @@ class ParallelEngine:
         call this at the same point.  See ``parallel_b200/parallel/graph_step.py``."""
         from .graph_step import GraphedTrainStep
 
-        self._graph = None
+        self._graph = self._graph_pending = None
         self._graph = GraphedTrainStep(self, x, y, warmup=warmup)
         return self._graph
 
@@ -209,7 +250,7 @@ class ParallelEngine:
         """Drop the captured step (call before destroying the process group)."""
         if self._graph is not None:
             self._graph.release()
-        self._graph = None
+        self._graph = self._graph_pending = None
 
     def _check_pending_nonfinite(self):
         if self._pending_nonfinite is None:

@@ -40,7 +40,10 @@ import torch.distributed as dist
 
 
 class GraphedTrainStep:
-    def __init__(self, engine, x: torch.Tensor, y: torch.Tensor, warmup: int = 3):
+    def __init__(self, engine, x: torch.Tensor, y: torch.Tensor, warmup: int = 3, stream=None):
+        """``warmup`` eager steps on (x, y) run on the capture stream first.  With
+        ``warmup=0`` the caller passes the ``stream`` on which its own eager
+        steps already ran (``ParallelEngine.enable_graph_capture``)."""
         if engine.device.type != "cuda":
             raise RuntimeError("CUDA-graph steps need a CUDA device")
         if engine.grad_scaler.is_enabled():
@@ -58,10 +61,12 @@ class GraphedTrainStep:
         # warm-up on the stream the capture will use: lazy initialisation of
         # optimizer state, kernel attributes, NCCL communicators and symmetric
         # buffers happens here, outside the capture
-        self.stream = torch.cuda.Stream(device=dev)
+        if warmup < 1 and stream is None:
+            raise ValueError("warmup=0 needs the stream on which the eager warm-up steps ran")
+        self.stream = stream if stream is not None else torch.cuda.Stream(device=dev)
         self.stream.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(self.stream):
-            for _ in range(max(1, warmup)):
+            for _ in range(warmup):
                 engine.train_step(self.x, self.y)
         torch.cuda.current_stream(dev).wait_stream(self.stream)
         torch.cuda.synchronize(dev)

@@ -70,10 +70,17 @@ def main(argv=None):
         logger.info("Collecting token bytes...")
         token_bytes = get_token_bytes(tokenizer)
     pconfig.model_train_rngs(seed=seed)
-    if cfg.engine.compile and pconfig.dp_shard_size > 1:
-        raise NotImplementedError("torch.compile is not yet supported with the custom FSDP implementation")
-    if cfg.engine.compile and pconfig.model_parallel_enabled:
-        raise NotImplementedError("torch.compile is not yet supported with folded model parallelism")
+    # engine.compile: the whole training step is captured as a CUDA graph
+    # (ParallelEngine.enable_graph_capture) - FSDP and DP-replicate included,
+    # which the reference's torch.compile path refuses (train.py:45-48)
+    graph_step = bool(cfg.engine.compile)
+    if graph_step and pconfig.model_parallel_enabled:
+        raise NotImplementedError("engine.compile is not yet supported with folded model parallelism")
+    if graph_step and cfg.config.grad_accum_steps != 1:
+        raise NotImplementedError("engine.compile captures one whole step; it needs config.grad_accum_steps=1")
+    if graph_step and cfg.engine.get("collective_profiling", False):
+        raise NotImplementedError("engine.compile replays the step as one graph; per-collective profiling needs "
+                                  "eager steps")
     if pconfig.dp_shard_size <= 1 and not pconfig.model_parallel_enabled:
         model.to(device)
         model._layout_fused_weights()
@@ -82,6 +89,8 @@ def main(argv=None):
         model._layout_fused_weights()
     model.train()
     engine = ParallelEngine(model, tokenizer, pconfig, cfg, device, mp_plan=mp_plan)
+    if graph_step:
+        engine.enable_graph_capture(warmup_steps=2)
     resume = None
     if cfg.config.resume_from:
         logger.info(f"Loading checkpoint from {cfg.config.resume_from}")
@@ -119,12 +128,16 @@ def main(argv=None):
         engine.reset_step_memory_stats()
         total = torch.tensor(0.0, device=device)
         dl_state = None
-        for _ in range(accum):
+        if graph_step:
             x, y, dl_state = next(train_loader)
-            loss = engine.forward(x, y).loss / accum
-            engine.backward(loss)
-            total += loss.detach()
-        engine.step()
+            total += engine.train_step(x, y)
+        else:
+            for _ in range(accum):
+                x, y, dl_state = next(train_loader)
+                loss = engine.forward(x, y).loss / accum
+                engine.backward(loss)
+                total += loss.detach()
+            engine.step()
         if cuda:
             ev1.record()
         if prof is not None:
@@ -170,6 +183,7 @@ def main(argv=None):
             engine.save_checkpoint(path, step=step, dataloader_state=dl_state, eval_dataloader_state=eval_state)
     if prof is not None:
         prof.__exit__(None, None, None)
+    engine.release_graph()
     wandb.finish()
     dist_cleanup()
 

@@ -111,6 +111,43 @@ def test_cuda_graph_step_matches_eager():
     graphed.release_graph()
 
 
+def test_deferred_graph_capture_follows_the_eager_trajectory():
+    """engine.compile's mode: two eager steps on the capture stream, then the
+    capture, then replays - each batch trained on exactly once, so the losses
+    and weights follow a plain eager run."""
+    from parallel_b200.config import from_dotlist, load_cfg, merge
+    from parallel_b200.ops._ext import check_device_errors
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    c = merge(load_cfg(argv=[]), from_dotlist(["config.device_type=cuda", "model.learning_rate=3e-3"]))
+    engines = []
+    for _ in range(2):
+        cfg, _, gpu = _pair("small-qwen3")
+        pc = ParallelConfig(c)
+        pc.set_device_mesh("cuda")
+        engines.append(ParallelEngine(gpu, None, pc, c, torch.device("cuda", 0)))
+    eager, graphed = engines
+    graphed.enable_graph_capture(warmup_steps=2)
+    g = torch.Generator().manual_seed(5)
+    toks = [torch.randint(0, cfg.vocab_size, (4, 129), generator=g).cuda() for _ in range(6)]
+    le, lg = [], []
+    for i, t in enumerate(toks):
+        le.append(float(eager.train_step(t[:, :-1], t[:, 1:])))
+        lg.append(float(graphed.train_step(t[:, :-1], t[:, 1:])))
+        assert (graphed._graph is not None) == (i >= 2)
+    torch.cuda.synchronize()
+    check_device_errors()
+    assert max(abs(a - b) for a, b in zip(le, lg)) < 2e-2, (le, lg)
+    pe, pg = dict(eager.model.named_parameters()), dict(graphed.model.named_parameters())
+    for n, p in pe.items():
+        assert _rel(pg[n].detach(), p.detach()) < 2e-2, n
+    se = eager.optimizer.state[next(iter(eager.optimizer.state))]["step"]
+    sg = graphed.optimizer.state[next(iter(graphed.optimizer.state))]["step"]
+    assert float(se) == float(sg) == 6.0
+    graphed.release_graph()
+
+
 def test_device_error_word_surfaces_as_collective_timeout():
     """A bounded device wait that gave up (its error word, written here from the
     host) is read back asynchronously with the step's finite flag and raised at

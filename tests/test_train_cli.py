@@ -38,3 +38,28 @@ def test_train_cli_checkpoint_and_exact_resume(tmp_path):
     assert sorted(resumed) == [3, 4], resumed
     for s in (3, 4):
         assert resumed[s] == full[s], (full, resumed)
+
+
+def _run_fail(tmp, extra):
+    env = dict(os.environ, PYTHONPATH=ROOT, WANDB_MODE="disabled")
+    args = [sys.executable, "-m", "parallel_b200.train", f"model.name={tmp}/init", "config.device_type=cpu",
+            "config.backend=gloo", "config.use_amp=false", "data.synthetic=true", "config.max_steps=1",
+            "model.per_device_batch_size=2", "model.max_seq_length=32"] + extra
+    out = subprocess.run(args, env=env, cwd=tmp, capture_output=True, text=True, timeout=300)
+    assert out.returncode != 0
+    return out.stderr
+
+
+def test_train_cli_compile_selects_the_graph_step_and_refuses_what_it_cannot_capture(tmp_path):
+    """engine.compile=true captures the training step as a CUDA graph: it is
+    refused with gradient accumulation and on a CPU device, with a clear error."""
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.loading import save_pretrained
+    from parallel_b200.models.qwen3 import build_model
+
+    tmp = str(tmp_path)
+    save_pretrained(build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0), f"{tmp}/init")
+    err = _run_fail(tmp, ["engine.compile=true", "config.grad_accum_steps=2"])
+    assert "grad_accum_steps=1" in err, err[-2000:]
+    err = _run_fail(tmp, ["engine.compile=true", "config.grad_accum_steps=1"])
+    assert "needs a CUDA device" in err, err[-2000:]
