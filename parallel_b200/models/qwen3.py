@@ -203,9 +203,18 @@ class DecoderLayer(nn.Module):
         self._router_sink: list = []
         self._inv_freq = None
         self._seq = None
+        # model parallelism: the layer's TP-summed parameters, their gradients
+        # reduced in one collective (set by the model-parallel wrapper)
+        self._tp_grad_pack = None
 
     def forward(self, x):
         """x: [B, S_local, H] (S_local = S / tp under sequence parallelism)."""
+        pack = self._tp_grad_pack
+        if pack is not None and torch.is_grad_enabled():
+            return pack.run(self._forward, x)
+        return self._forward(x)
+
+    def _forward(self, x):
         ctx = self._ctx
         B, S = self._seq
         stash = getattr(self, "_attn_stash", None)

@@ -2,7 +2,8 @@
 
 Same responsibilities and public methods as the reference wrapper
 (parallel/parallel/engine/model_parallel/api.py:26-163): verify the model
-against its plan, install SUM_TP gradient hooks, switch on the sequence-
+against its plan, install the SUM_TP gradient reductions (one packed
+all-reduce per decoder layer instead of one per parameter), switch on the sequence-
 parallel runtime and the expert-parallel runtime, provide the vocab-parallel
 token loss / training loss (+ router aux loss) and MP gradient clipping, and
 own the checkpoint adapter (replaced by the composed one once FSDP is
@@ -22,7 +23,8 @@ from .grad_norm import clip_grad_norm_
 from .loss_parallel import loss_parallel_context, vocab_parallel_cross_entropy, vocab_parallel_lm_head_ce
 from .registry import build_model_parallel_plan
 from .sequence_parallel import SequenceParallelRuntime, sequence_parallel_load_balancing_loss
-from .tensor_parallel import install_tensor_parallel_gradient_hooks, tensor_parallel_mesh, verify_tensor_parallel_model
+from .tensor_parallel import (install_layer_gradient_packs, install_tensor_parallel_gradient_hooks,
+                              tensor_parallel_mesh, verify_tensor_parallel_model)
 
 
 class ModelParallelWrapper:
@@ -54,7 +56,16 @@ class ModelParallelWrapper:
                               tp_group=self.group, sp=False, ep_size=self.plan.expert_parallel_size,
                               ep_rank=self.mesh.get_local_rank(), comm=comm_ops)
         model.set_parallel_context(ctx)
-        self._tp_gradient_hook_handles = install_tensor_parallel_gradient_hooks(model, self.plan, self.mesh)
+        # SUM_TP gradients: one packed reduction per decoder layer, per-param
+        # hooks for the rest (the final norm under sequence parallelism)
+        small = None
+        if self.collectives != "nccl" and device is not None and torch.device(device).type == "cuda":
+            from ..comm.p2p import P2PSmallAllReduce
+
+            small = P2PSmallAllReduce.get(self.group, torch.device(device))
+        packed = install_layer_gradient_packs(model, self.plan, self.mesh, small)
+        self._tp_gradient_hook_handles = install_tensor_parallel_gradient_hooks(model, self.plan, self.mesh,
+                                                                                exclude=packed)
         for name, p in model.named_parameters():
             if self.plan.placement_for_parameter(name).shard_dim is None:
                 self._replicated_ids.add(id(p))

@@ -209,3 +209,63 @@ def test_benchmark_configurations_have_valid_plans(name, tp, sp, ep):
     if ep > 1:
         gu = params["model.layers.0.mlp.experts.gate_up_proj"]
         assert gu.shape[0] == cfg.num_experts // ep
+
+
+def _pack_worker(rank, world, path, sp, out):
+    import torch.distributed as dist
+
+    from parallel_b200.models.loading import load_causal_lm
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    cfg = cpu_cfg(**{"model.name": path, "parallel.tp": 2, "parallel.sp": sp})
+    pc = ParallelConfig(cfg)
+    pc.set_device_mesh("cpu")
+    model, plan = load_causal_lm(cfg, pc, dtype=torch.float32)
+    eng = ParallelEngine(model, None, pc, cfg, torch.device("cpu"), mp_plan=plan)
+    packs = [l._tp_grad_pack for l in model.model.layers]
+    calls = []
+    real = dist.all_reduce
+
+    def counting(t, *a, **k):
+        calls.append(t.numel())
+        return real(t, *a, **k)
+
+    tok = _data(steps=1)[0]
+    loss = eng.forward(tok[:, :-1], tok[:, 1:]).loss
+    dist.all_reduce = counting
+    try:
+        eng.backward(loss)
+    finally:
+        dist.all_reduce = real
+    grads = {n: p.grad.clone() for n, p in model.named_parameters()
+             if p.grad is not None and plan.placement_for_parameter(n).shard_dim is None}
+    torch.save({"numels": [p.numel for p in packs], "names": [p.rel_names for p in packs], "calls": calls,
+                "hooks": len(eng.mp_wrapper._tp_gradient_hook_handles), "grads": grads},
+               out.replace(".pt", f"-{rank}.pt"))
+
+
+@pytest.mark.parametrize("sp", [1, 2])
+def test_sum_tp_gradients_are_reduced_once_per_layer(tmp_path, sp):
+    """Each decoder layer's TP-summed parameters (q/k-norm; + both layer norms
+    under SP) are reduced in one packed all-reduce in the backward instead of
+    one per parameter; only the final norm (SP) keeps a per-parameter hook.
+    The reduced gradients are identical on both TP ranks (their correctness
+    against single-process training is the parity tests' job)."""
+    path = str(tmp_path / "model")
+    cfg = _save_ref_model(path, "tiny-qwen3").config
+    out = str(tmp_path / "res.pt")
+    run_ranks(_pack_worker, 2, path, sp, out)
+    res = [torch.load(out.replace(".pt", f"-{r}.pt"), weights_only=False) for r in range(2)]
+    H, D, L = cfg.hidden_size, cfg.head_dim, cfg.num_hidden_layers
+    want = 2 * D + (2 * H if sp > 1 else 0)
+    r0 = res[0]
+    assert r0["numels"] == [want] * L
+    expect = {"self_attn.q_norm.weight", "self_attn.k_norm.weight"}
+    if sp > 1:
+        expect |= {"input_layernorm.weight", "post_attention_layernorm.weight"}
+    assert all(set(n) == expect for n in r0["names"])
+    assert r0["calls"].count(want) == L
+    assert r0["hooks"] == (1 if sp > 1 else 0)
+    for n, g in r0["grads"].items():
+        torch.testing.assert_close(res[1]["grads"][n], g, rtol=0, atol=0)
