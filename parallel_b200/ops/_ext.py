@@ -19,14 +19,25 @@ except Exception as exc:  # pragma: no cover - depends on the build
     _err = exc
 
 
+_resolved = None
+
+
 def ext():
-    """Return the compiled module, raising loudly if it is unavailable."""
+    """Return the compiled module, raising loudly if it is unavailable.  With
+    ``PB_COMM_DEBUG=1`` (read once per process) the peer-memory launches go
+    through the span and guard-word checks of ``parallel_b200.parallel.comm.debug``."""
+    global _resolved
+    if _resolved is not None:
+        return _resolved
     if _C is None:
         raise RuntimeError(
             "parallel_b200._C (sm_100a kernels) is not built or failed to load: "
             f"{_err!r}. Build it with `python setup.py build_ext --inplace`."
         )
-    return _C
+    from ..parallel.comm import debug
+
+    _resolved = debug.checked_extension(_C) if debug.enabled() else _C
+    return _resolved
 
 
 def available() -> bool:

@@ -33,6 +33,7 @@ import torch.distributed as dist
 
 from ...ops._ext import ext
 from ...profiling import collective_profile
+from . import debug as comm_debug
 from .unit_collectives import TorchUnitCollectives, unit_detail
 
 
@@ -55,16 +56,25 @@ def p2p_supported(group) -> bool:
 class SymmBuffer:
     """A symmetric allocation plus its peer addresses and signal pads."""
 
-    def __init__(self, numel: int, dtype, device, group):
+    def __init__(self, numel: int, dtype, device, group, name: str = "symm"):
         symm_mem = importlib.import_module("torch.distributed._symmetric_memory")
-        self.tensor = symm_mem.empty(max(numel, 64), dtype=dtype, device=device)
+        numel = max(numel, 64)
+        # debug mode: guard words on both sides of the payload (same on every rank)
+        total, guard = comm_debug.guarded_numel(numel, dtype) if comm_debug.enabled() else (numel, 0)
+        self._alloc = symm_mem.empty(total, dtype=dtype, device=device)
+        self.tensor = self._alloc[guard:guard + numel]
         self.tensor.zero_()
-        self.handle = symm_mem.rendezvous(self.tensor, group)
+        self.handle = symm_mem.rendezvous(self._alloc, group)
         self.rank = self.handle.rank
         self.world = self.handle.world_size
         base = list(self.handle.buffer_ptrs)
         off = self.tensor.data_ptr() - base[self.rank]
         self.peer_ptrs = [b + off for b in base]
+        self.guard = None
+        if guard:
+            es = self.tensor.element_size()
+            self.guard = comm_debug.register(comm_debug.GuardedRegion(
+                name, self._alloc.view(torch.uint8), guard * es, numel * es, list(self.peer_ptrs)))
         self.pads_dev = int(self.handle.signal_pad_ptrs_dev)
         # per-channel epoch counters live on the device: the barrier kernel bumps
         # them, so a captured CUDA graph that contains barriers replays correctly
@@ -95,7 +105,8 @@ class P2PSmallAllReduce:
         self.rank = dist.get_rank(group)
         self.cap = cap_units
         self.limit_s = float(os.environ.get("PB_P2P_TIMEOUT_S", "60"))
-        self.buf = SymmBuffer(ext().small_ar_region_floats(self.world, cap_units), torch.float32, device, group)
+        self.buf = SymmBuffer(ext().small_ar_region_floats(self.world, cap_units), torch.float32, device, group,
+                              "small_all_reduce")
         self.bases = list(self.buf.peer_ptrs)
         self.epochs = torch.zeros(self.MAX_BLOCKS, dtype=torch.int32, device=device)
 
@@ -166,7 +177,7 @@ class P2PUnitCollectives:
         if not self._aligned(unit):
             unit._p2p = None
             return self._fallback.alloc_local_bucket(unit, numel, dtype, device)
-        buf = SymmBuffer(numel, dtype, device, self.group)
+        buf = SymmBuffer(numel, dtype, device, self.group, "fsdp_bucket")
         unit._p2p = buf
         return buf.tensor[:numel]
 
@@ -229,7 +240,7 @@ class P2PUnitCollectives:
             return
         dev = units[0].device
         self._slot_numel = need
-        self.slots = [SymmBuffer(need, torch.bfloat16, dev, self.group) for _ in range(3)]
+        self.slots = [SymmBuffer(need, torch.bfloat16, dev, self.group, "fsdp_rs_slot") for _ in range(3)]
         self.stream = torch.cuda.Stream(device=dev)
 
     def reduce_scatter(self, unit, grads, grad_bucket, accumulate: bool, mode: str = "overlapped"):

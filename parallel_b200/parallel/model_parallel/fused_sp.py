@@ -74,8 +74,9 @@ class FusedSequenceParallel:
                                f"({self._rows}x{self._cols} -> {rows_local}x{cols})")
         self._rows, self._cols = rows_local, cols
         n = rows_local * cols
-        self.ag = [SymmBuffer(n, torch.bfloat16, self.device, self.group) for _ in range(2)]
-        self.rs = [SymmBuffer(self.world * n, torch.bfloat16, self.device, self.group) for _ in range(2)]
+        self.ag = [SymmBuffer(n, torch.bfloat16, self.device, self.group, "sp_gather") for _ in range(2)]
+        self.rs = [SymmBuffer(self.world * n, torch.bfloat16, self.device, self.group, "tp_partials")
+                   for _ in range(2)]
         self.flags = [torch.zeros(64, dtype=torch.int32, device=self.device) for _ in range(2)]
 
     def _block_order(self, batch: int, seq: int) -> list[int]:
@@ -184,8 +185,9 @@ class FusedTensorParallel:
                                f"({self._rows}x{self._cols} -> {rows_local}x{cols})")
         self._rows, self._cols = rows_local, cols
         n = rows_local * cols
-        self.rs = [SymmBuffer(self.world * n, torch.bfloat16, self.device, self.group) for _ in range(2)]
-        self.red = [SymmBuffer(n, torch.bfloat16, self.device, self.group) for _ in range(2)]
+        self.rs = [SymmBuffer(self.world * n, torch.bfloat16, self.device, self.group, "tp_partials")
+                   for _ in range(2)]
+        self.red = [SymmBuffer(n, torch.bfloat16, self.device, self.group, "tp_reduced") for _ in range(2)]
 
     def all_gather_gemm(self, x: torch.Tensor, b: torch.Tensor, batch: int, seq: int, *, b_mn: bool = False,
                         swiglu_inter: int = 0, gu_out: torch.Tensor | None = None):

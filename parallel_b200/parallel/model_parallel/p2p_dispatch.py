@@ -38,8 +38,8 @@ class _Pool:
 
     def __init__(self, group, device, cap: int, hidden: int):
         self.cap, self.hidden = cap, hidden
-        self.rows = [SymmBuffer(cap * hidden, torch.bfloat16, device, group) for _ in range(2)]
-        self.recs = [SymmBuffer(cap * 4, torch.int32, device, group) for _ in range(2)]
+        self.rows = [SymmBuffer(cap * hidden, torch.bfloat16, device, group, "ep_rows") for _ in range(2)]
+        self.recs = [SymmBuffer(cap * 4, torch.int32, device, group, "ep_records") for _ in range(2)]
         self.n = 0
 
     def next(self):
