@@ -177,6 +177,8 @@ def residual_rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float):
 # Upper bound of the attention backward's dS tile buffer (bf16, causal tiles of
 # every head); larger problems use the fp32 dQ accumulator instead.
 _ATTN_DS_LIMIT_BYTES = int(os.environ.get("PB_ATTN_DS_LIMIT_BYTES", str(4 << 30)))
+
+
 class _AttentionFn(torch.autograd.Function):
     """qkv = h W_qkv^T -> per-head q/k RMSNorm + RoPE -> causal GQA flash
     attention.  Returns the attention output [T, nq*D] (before o_proj)."""
