@@ -62,7 +62,7 @@ class SymmBuffer:
         # debug mode: guard words on both sides of the payload (same on every rank)
         total, guard = comm_debug.guarded_numel(numel, dtype) if comm_debug.enabled() else (numel, 0)
         self._alloc = symm_mem.empty(total, dtype=dtype, device=device)
-        self.tensor = self._alloc[guard:guard + numel]
+        self.tensor = self._alloc[guard:guard + numel] if guard else self._alloc
         self.tensor.zero_()
         self.handle = symm_mem.rendezvous(self._alloc, group)
         self.rank = self.handle.rank
