@@ -7,9 +7,11 @@ the reference's composition (NCCL collective + cuBLAS GEMM), one process per GPU
 Cases (bf16 N(0,1) inputs from a fixed seed):
 
 * ``ag_gemm``  all-gather of the sequence shard -> column-parallel GEMM
-  (``FusedSequenceParallel.all_gather_gemm`` vs ``all_gather_into_tensor`` + ``torch.matmul``);
+  (``FusedSequenceParallel.all_gather_gemm`` vs ``all_gather_into_tensor`` + ``torch.matmul``;
+  ``pull_us``: the same in pull mode, peer gather kernel then plain GEMM);
 * ``gemm_rs``  row-parallel GEMM -> reduce-scatter (``gemm_reduce_scatter`` vs
-  ``torch.matmul`` + ``reduce_scatter_tensor``);
+  ``torch.matmul`` + ``reduce_scatter_tensor``; ``pull_us``: GEMM into the local
+  symmetric buffer, then each owner pulls and sums its rows);
 * ``fsdp_ag`` / ``fsdp_rs``  flat-buffer all-gather / reduce-scatter (peer gather / N-peer
   reduce kernels vs NCCL);
 * ``ep``  expert dispatch + combine of top-8 routes over 128 experts (peer row kernels
@@ -53,11 +55,17 @@ def _time(fn, warmup, iters):
     return float(t)
 
 
-def _report(case, shape, ours_us, base_us, flops, link_bytes):
+def _report(case, shape, ours_us, base_us, flops, link_bytes, pull_us=None):
     roof = max(flops / GEMM_PEAK, link_bytes / LINK_BW) * 1e6
-    return {"case": case, "shape": shape, "ours_us": round(ours_us, 1), "nccl_cublas_us": round(base_us, 1),
-            "speedup": round(base_us / ours_us, 3), "roofline_us": round(roof, 1),
-            "frac_of_roofline": round(roof / ours_us, 3)}
+    out = {"case": case, "shape": shape, "ours_us": round(ours_us, 1), "nccl_cublas_us": round(base_us, 1),
+           "speedup": round(base_us / ours_us, 3), "roofline_us": round(roof, 1),
+           "frac_of_roofline": round(roof / ours_us, 3)}
+    if pull_us is not None:
+        # the same operation in pull mode (collective kernel + plain GEMM, no
+        # communication inside the GEMM)
+        out.update(pull_us=round(pull_us, 1), pull_speedup=round(base_us / pull_us, 3),
+                   pull_frac_of_roofline=round(roof / pull_us, 3))
+    return out
 
 
 def case_ag_gemm(W, rank, dev, M, K, N, warmup, iters):
@@ -70,13 +78,16 @@ def case_ag_gemm(W, rank, dev, M, K, N, warmup, iters):
     if not sp.supports(1, M, K):
         return None
     ours = _time(lambda: sp.all_gather_gemm(x, w, 1, M), warmup, iters)
+    pull = FusedSequenceParallel(dist.group.WORLD, dev, mode="pull")
+    t_pull = _time(lambda: pull.all_gather_gemm(x, w, 1, M), warmup, iters)
     full = torch.empty(M, K, device=dev, dtype=torch.bfloat16)
 
     def base():
         dist.all_gather_into_tensor(full, x)
         torch.matmul(full, w.t())
 
-    return _report("ag_gemm", [M, K, N], ours, _time(base, warmup, iters), 2 * M * K * N, (W - 1) * (M // W) * K * 2)
+    return _report("ag_gemm", [M, K, N], ours, _time(base, warmup, iters), 2 * M * K * N, (W - 1) * (M // W) * K * 2,
+                   t_pull)
 
 
 def case_gemm_rs(W, rank, dev, M, K, N, warmup, iters):
@@ -89,12 +100,15 @@ def case_gemm_rs(W, rank, dev, M, K, N, warmup, iters):
     if not sp.supports(1, M, N):
         return None
     ours = _time(lambda: sp.gemm_reduce_scatter(a, w, 1, M), warmup, iters)
+    pull = FusedSequenceParallel(dist.group.WORLD, dev, mode="pull")
+    t_pull = _time(lambda: pull.gemm_reduce_scatter(a, w, 1, M), warmup, iters)
     out = torch.empty(M // W, N, device=dev, dtype=torch.bfloat16)
 
     def base():
         dist.reduce_scatter_tensor(out, torch.matmul(a, w.t()))
 
-    return _report("gemm_rs", [M, K, N], ours, _time(base, warmup, iters), 2 * M * K * N, (W - 1) * (M // W) * N * 2)
+    return _report("gemm_rs", [M, K, N], ours, _time(base, warmup, iters), 2 * M * K * N, (W - 1) * (M // W) * N * 2,
+                   t_pull)
 
 
 def _flat_buffers(W, dev, nbytes):

@@ -20,6 +20,16 @@ is one kernel (``csrc/gemm_pair.cu``):
 Buffers rotate between two sets, so one signal barrier per call orders reuse:
 when a rank passes the barrier of call k every rank has finished call k-1,
 hence nobody still reads the set that call k+1 overwrites.
+
+``mode="pull"`` (``PB_SP_MODE=pull``) runs the same two operations as a
+collective followed / preceded by a plain GEMM, with no communication inside
+the GEMM kernel: the all-gather is one peer-gather kernel (every rank pulls
+the peers' shards into the gathered buffer), the reduce-scatter writes the
+whole partial product into this rank's symmetric buffer with the GEMM's
+TMA-store epilogue and each owner then pulls and sums its rows from every
+peer with the N-peer reduce kernel.  It trades the overlap of the fused
+kernels for bulk transfers (no per-row peer stores from the epilogue); the
+address plans are ``pull_gather_plan`` / ``pull_reduce_plan``.
 """
 from __future__ import annotations
 
@@ -36,14 +46,45 @@ from ..comm.p2p import SymmBuffer, p2p_supported
 _PIECES_PER_BLOCK = 256 // 16  # kGatherRowsPerPiece = 16 rows per copy piece
 
 
+def pull_gather_plan(peer_ptrs: list[int], dst_ptr: int, batch: int, seq: int, cols: int, es: int = 2):
+    """Peer-gather arguments (src, dst, nbytes) that assemble the gathered
+    [batch*seq, cols] activation from every rank's [batch*seq/world, cols]
+    shard: rank j holds positions [j*sl, (j+1)*sl) of every sequence."""
+    world = len(peer_ptrs)
+    sl = seq // world
+    seg = sl * cols * es
+    src, dst = [], []
+    for j, p in enumerate(peer_ptrs):
+        for b in range(batch):
+            src.append(p + b * seg)
+            dst.append(dst_ptr + (b * seq + j * sl) * cols * es)
+    return src, dst, [seg] * len(src)
+
+
+def pull_reduce_plan(peer_ptrs: list[int], dst_ptr: int, rank: int, batch: int, seq: int, cols: int, es: int = 2):
+    """N-peer reduce arguments (src per peer, dst, nelem) that sum this rank's
+    rows - positions [rank*sl, (rank+1)*sl) of every sequence - out of every
+    peer's full [batch*seq, cols] partial product into the local
+    [batch*seq/world, cols] output."""
+    world = len(peer_ptrs)
+    sl = seq // world
+    rows = [(b * seq + rank * sl) * cols * es for b in range(batch)]
+    src = [[p + r for r in rows] for p in peer_ptrs]
+    dst = [dst_ptr + b * sl * cols * es for b in range(batch)]
+    return src, dst, [sl * cols] * batch
+
+
 class FusedSequenceParallel:
     """NVLink data plane of one TP/SP group (all ranks call in the same order)."""
 
-    def __init__(self, group, device: torch.device):
+    def __init__(self, group, device: torch.device, mode: str | None = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.device = device
+        self.mode = mode or os.environ.get("PB_SP_MODE", "fused")
+        if self.mode not in ("fused", "pull"):
+            raise ValueError(f"unknown sequence-parallel mode {self.mode!r} (fused / pull)")
         self.limit_s = float(os.environ.get("PB_P2P_TIMEOUT_S", "60"))
         self._rows = 0
         self._cols = 0
@@ -106,9 +147,20 @@ class FusedSequenceParallel:
             N = b.shape[1] if b_mn else b.shape[0]
             out = torch.empty(T, N, device=x_local.device, dtype=torch.bfloat16)
             epi, n_out, up = EPI_STORE_BF16, 0, 0
+        n_cols = 2 * swiglu_inter if swiglu_inter else out.shape[1]
+        if self.mode == "pull":
+            with collective_profile("sp_all_gather_gemm", value=x_local, mode="pull", flops=2.0 * T * K * n_cols,
+                                    link_bytes=(self.world - 1) * rows_local * K * 2):
+                buf.barrier(0, self.limit_s)
+                ext().p2p_copy(*pull_gather_plan(buf.peer_ptrs, x_full.data_ptr(), batch, seq, K))
+                if swiglu_inter:
+                    ext().gemm(x_full, b, out, False, False, EPI_SWIGLU, 1.0, gu_out, up, n_out)
+                else:
+                    ext().gemm(x_full, b, out, False, b_mn, EPI_STORE_BF16, 1.0)
+            self.n_ag += 1
+            return out, x_full
         self.flag_calls[k] += 1
         target = self.flag_calls[k] * _PIECES_PER_BLOCK
-        n_cols = 2 * swiglu_inter if swiglu_inter else out.shape[1]
         with collective_profile("sp_all_gather_gemm", value=x_local, mode="fused", flops=2.0 * T * K * n_cols,
                                 link_bytes=(self.world - 1) * rows_local * K * 2):
             buf.barrier(0, self.limit_s)
@@ -128,6 +180,18 @@ class FusedSequenceParallel:
         buf = self.rs[k]
         y = torch.empty(rows_local, N, device=a_full.device, dtype=torch.bfloat16)
         slot_elems = rows_local * N
+        if self.mode == "pull":
+            T = a_full.shape[0]
+            part = buf.tensor[: T * N].view(T, N)
+            with collective_profile("sp_gemm_reduce_scatter", payload_bytes=T * N * 2, mode="pull",
+                                    flops=2.0 * T * a_full.shape[1] * N,
+                                    link_bytes=(self.world - 1) * rows_local * N * 2):
+                ext().gemm(a_full, b, part, False, b_mn, EPI_STORE_BF16, 1.0)
+                buf.barrier(0, self.limit_s)
+                ext().p2p_reduce(*pull_reduce_plan(buf.peer_ptrs, y.data_ptr(), self.rank, batch, seq, N), 1.0,
+                                 False)
+            self.n_rs += 1
+            return y
         with collective_profile("sp_gemm_reduce_scatter", payload_bytes=a_full.shape[0] * N * 2, mode="fused",
                                 flops=2.0 * a_full.shape[0] * a_full.shape[1] * N,
                                 link_bytes=(self.world - 1) * rows_local * N * 2):
