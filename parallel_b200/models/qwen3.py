@@ -15,13 +15,11 @@ tensor_parallel.py, sequence_parallel.py, expert_parallel.py).
 """
 from __future__ import annotations
 
-import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from typing import Any, Optional
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from ..ops import functional as Fx
 from ..ops import moe as MoE

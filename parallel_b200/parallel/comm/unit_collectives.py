@@ -10,7 +10,7 @@ symmetric memory and writes the parameter-major layout directly.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Any, Optional
+from typing import Any
 
 import torch
 import torch.distributed as dist
