@@ -194,12 +194,12 @@ def _unused_data(world, steps=3):
     return [torch.randint(0, 64, (world * 2, 9), generator=g) for _ in range(steps)]
 
 
-def _unused_worker(rank, world, data, out):
+def _unused_worker(rank, world, data, out, ckpt="false"):
     from parallel_b200.parallel.engine import ParallelEngine
     from parallel_b200.state import ParallelConfig
 
     cfg = cpu_cfg(**{"parallel.dp_shard": world, "engine.find_unused_parameters": "true",
-                     "engine.activation_checkpoint": "false", "model.learning_rate": 1e-2})
+                     "engine.activation_checkpoint": ckpt, "model.learning_rate": 1e-2})
     pc = ParallelConfig(cfg)
     pc.set_device_mesh("cpu")
     m = _Toy()
@@ -215,16 +215,18 @@ def _unused_worker(rank, world, data, out):
         torch.save(full, out)
 
 
-def test_fsdp_rank_divergent_unused_parameters(tmp_path):
-    """find_unused_parameters: a parameter used on some ranks gets the mean over
-    all ranks (zeros where unused); one unused everywhere keeps grad=None and is
-    left untouched by AdamW (no weight decay either)."""
+@pytest.mark.parametrize("ckpt", ["false", "true"])
+def test_fsdp_rank_divergent_unused_parameters(tmp_path, ckpt):
+    """find_unused_parameters (with and without activation checkpointing): a
+    parameter used on some ranks gets the mean over all ranks (zeros where
+    unused); one unused everywhere keeps grad=None and is left untouched by
+    AdamW (no weight decay either)."""
     from parallel_b200.parallel.optim import FusedAdamW
 
     world = 2
     data = _unused_data(world)
     out = str(tmp_path / "unused.pt")
-    run_ranks(_unused_worker, world, data, out)
+    run_ranks(_unused_worker, world, data, out, ckpt)
     got = torch.load(out, weights_only=False)
     ref = _Toy()
     init_never = ref.layers[1].never.weight.detach().clone()
