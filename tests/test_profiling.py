@@ -97,3 +97,57 @@ def test_scheduled_profiler_validation(tmp_path):
         P.scheduled_torch_profiler(enabled=True, trace_dir=tmp_path, rank=0, active_steps=0)
     prof = P.scheduled_torch_profiler(enabled=True, trace_dir=tmp_path / "t", rank=3)
     assert prof is not None and (tmp_path / "t").is_dir()
+
+
+def test_profile_logs_when_the_block_raises():
+    log = mock.Mock()
+    with mock.patch.object(P, "perf_counter", side_effect=[2.0, 2.5]):
+        with pytest.raises(KeyError):
+            with P.profile("failing", logger=log):
+                raise KeyError("x")
+    log.log.assert_called_once_with(logging.INFO, "[PROFILE] %s: %.3f ms", "failing", 500.0)
+
+
+def test_profile_cuda_events_interval_is_logged():
+    """use_cuda_events records an event pair on the current stream and logs
+    their elapsed time (CUDA mocked: the test needs no device)."""
+    log = mock.Mock()
+    ev0, ev1 = mock.Mock(), mock.Mock()
+    ev0.elapsed_time.return_value = 7.5
+    stream = object()
+    with mock.patch.object(torch.cuda, "is_available", return_value=True), \
+            mock.patch.object(torch.cuda, "Event", side_effect=[ev0, ev1]), \
+            mock.patch.object(torch.cuda, "current_stream", return_value=stream), \
+            mock.patch.object(P, "perf_counter", side_effect=[0.0, 0.01]):
+        with P.profile("kernel", logger=log, use_cuda_events=True):
+            pass
+    ev0.record.assert_called_once_with(stream)
+    ev1.record.assert_called_once_with(stream)
+    ev1.synchronize.assert_called_once()
+    ev0.elapsed_time.assert_called_once_with(ev1)
+    assert log.log.call_args_list[-1] == mock.call(logging.INFO, "[PROFILE] %s CUDA event: %.3f ms", "kernel", 7.5)
+    with pytest.raises(ValueError):
+        with P.profile("cpu", logger=log, device="cpu", use_cuda_events=True):
+            pass
+
+
+def test_profile_torch_profiler_table_on_cpu():
+    log = mock.Mock()
+    with mock.patch.object(torch.cuda, "is_available", return_value=False):
+        with P.profile("matmul", logger=log, use_torch_profiler=True):
+            torch.ones(64, 64) @ torch.ones(64, 64)
+    msgs = [c.args for c in log.log.call_args_list]
+    assert msgs[0][1] == "[PROFILE] %s: %.3f ms"
+    assert msgs[1][1] == "[PROFILE] %s torch profiler:\n%s" and "aten::" in msgs[1][3]
+
+
+def test_scheduled_profiler_warms_up_then_writes_one_trace_per_rank(tmp_path):
+    with mock.patch.object(torch.cuda, "is_available", return_value=False):
+        prof = P.scheduled_torch_profiler(enabled=True, trace_dir=tmp_path, rank=5, warmup_steps=1, active_steps=1)
+    prof.__enter__()
+    for _ in range(3):
+        torch.ones(32, 32) @ torch.ones(32, 32)
+        prof.step()
+    prof.__exit__(None, None, None)
+    traces = list(tmp_path.glob("rank5*.pt.trace.json.gz"))
+    assert len(traces) == 1, list(tmp_path.iterdir())
