@@ -62,13 +62,14 @@ def _reference(path, name, data, dp=1):
     return losses, grads, norms, {k: v.clone() for k, v in m.state_dict().items()}
 
 
-def _mp_worker(rank, world, path, data, par, out):
+def _mp_worker(rank, world, path, data, par, out, extra=None):
     from parallel_b200.models.loading import load_causal_lm
     from parallel_b200.parallel.engine import ParallelEngine
     from parallel_b200.state import ParallelConfig
 
     over = {"model.name": path, "model.output_router_logits": "true"}
     over.update({f"parallel.{k}": v for k, v in par.items()})
+    over.update(extra or {})
     cfg = cpu_cfg(**over)
     pc = ParallelConfig(cfg)
     pc.set_device_mesh("cpu")
@@ -100,13 +101,13 @@ def _mp_worker(rank, world, path, data, par, out):
                 "step": info["step"]}, out.replace(".pt", f"-{rank}.pt"))
 
 
-def _check(tmp_path, name, par, world):
+def _check(tmp_path, name, par, world, extra=None):
     path = str(tmp_path / "model")
     _save_ref_model(path, name)
     dp = par.get("dp_shard", 1) * par.get("dp_replicate", 1)
     data = _data(world=dp)
     out = str(tmp_path / "res.pt")
-    run_ranks(_mp_worker, world, path, data, par, out)
+    run_ranks(_mp_worker, world, path, data, par, out, extra)
     ref_losses, ref_grads, ref_norms, ref_state = _reference(path, name, data, dp)
     res = [torch.load(out.replace(".pt", f"-{r}.pt"), weights_only=False) for r in range(world)]
     for r in res:
@@ -152,6 +153,13 @@ def test_moe_tp_ep(tmp_path, sp):
 @pytest.mark.parametrize("sp", [1, 2])
 def test_moe_tp_ep_fsdp_composition(tmp_path, sp):
     _check(tmp_path, "tiny-qwen3-moe", {"tp": 2, "ep": 2, "sp": sp, "dp_shard": 2}, 4)
+
+
+def test_moe_tp_ep_sp_fsdp_composition_with_activation_checkpointing(tmp_path):
+    """The recomputed layer forward in the backward routes the layer's TP-summed
+    parameters (norms, q/k-norm, router) through the packed reduction too."""
+    _check(tmp_path, "tiny-qwen3-moe", {"tp": 2, "ep": 2, "sp": 2, "dp_shard": 2}, 4,
+           {"engine.activation_checkpoint": "true"})
 
 
 def test_plan_validation():
