@@ -155,6 +155,12 @@ def test_moe_tp_ep_fsdp_composition(tmp_path, sp):
     _check(tmp_path, "tiny-qwen3-moe", {"tp": 2, "ep": 2, "sp": sp, "dp_shard": 2}, 4)
 
 
+@pytest.mark.parametrize("sp", [1, 2])
+def test_dense_tp_fsdp_composition(tmp_path, sp):
+    """The dense benchmark layout (Qwen3-8B: tp = sp over FSDP) at tp=2 x dp_shard=2."""
+    _check(tmp_path, "tiny-qwen3", {"tp": 2, "sp": sp, "dp_shard": 2}, 4)
+
+
 def test_moe_tp_ep_sp_fsdp_composition_with_activation_checkpointing(tmp_path):
     """The recomputed layer forward in the backward routes the layer's TP-summed
     parameters (norms, q/k-norm, router) through the packed reduction too."""
