@@ -83,7 +83,8 @@ def _mp_worker(rank, world, path, data, par, out, extra=None):
         mine = tok[drank * b:(drank + 1) * b]
         loss = eng.forward(mine[:, :-1], mine[:, 1:]).loss
         eng.backward(loss)
-        if not eng.fsdp_wrapper.is_active:
+        if not eng.fsdp_wrapper.is_active and dp == 1:
+            # (with data-parallel replicas the grads are averaged in step(), not here)
             local_grads.append({n: p.grad.clone() for n, p in model.named_parameters() if p.grad is not None})
         eng.step()
         norms.append(float(eng.last_grad_norm))
@@ -159,6 +160,12 @@ def test_moe_tp_ep_fsdp_composition(tmp_path, sp):
 def test_dense_tp_fsdp_composition(tmp_path, sp):
     """The dense benchmark layout (Qwen3-8B: tp = sp over FSDP) at tp=2 x dp_shard=2."""
     _check(tmp_path, "tiny-qwen3", {"tp": 2, "sp": sp, "dp_shard": 2}, 4)
+
+
+def test_dense_tp_sp_with_dp_replicate(tmp_path):
+    """TP+SP with replicated data parallelism (gradient all-reduce over the
+    replicas, no FSDP) at tp=2 x dp_replicate=2."""
+    _check(tmp_path, "tiny-qwen3", {"tp": 2, "sp": 2, "dp_replicate": 2}, 4)
 
 
 def test_moe_tp_ep_sp_fsdp_composition_with_activation_checkpointing(tmp_path):
