@@ -168,11 +168,13 @@ def test_dense_tp_sp_with_dp_replicate(tmp_path):
     _check(tmp_path, "tiny-qwen3", {"tp": 2, "sp": 2, "dp_replicate": 2}, 4)
 
 
-def test_moe_tp_ep_sp_fsdp_composition_with_activation_checkpointing(tmp_path):
+@pytest.mark.parametrize("overlap", ["true", "false"])
+def test_moe_tp_ep_sp_fsdp_composition_with_activation_checkpointing(tmp_path, overlap):
     """The recomputed layer forward in the backward routes the layer's TP-summed
-    parameters (norms, q/k-norm, router) through the packed reduction too."""
+    parameters (norms, q/k-norm, router) through the packed reduction too; with
+    the FSDP reductions overlapped with the backward or deferred to its end."""
     _check(tmp_path, "tiny-qwen3-moe", {"tp": 2, "ep": 2, "sp": 2, "dp_shard": 2}, 4,
-           {"engine.activation_checkpoint": "true"})
+           {"engine.activation_checkpoint": "true", "engine.overlap_backward_reductions": overlap})
 
 
 def test_plan_validation():
