@@ -97,9 +97,19 @@ def _mp_worker(rank, world, path, data, par, out, extra=None):
     eng2 = ParallelEngine(model2, None, pc, cfg, torch.device("cpu"), mp_plan=plan2)
     info = eng2.load_checkpoint(ck)
     full2 = eng2.state_dict()
+    # both continue with one more step on the same batch: the resumed engine
+    # (weights, optimizer moments and step count) takes the original's step
+    cont = []
+    for e in (eng, eng2):
+        mine = data[0][drank * b:(drank + 1) * b]
+        loss = e.forward(mine[:, :-1], mine[:, 1:]).loss
+        e.backward(loss)
+        e.step()
+        cont.append(e.reduce_loss(loss).item())
+    after = [eng.state_dict(), eng2.state_dict()]
     torch.save({"rank": rank, "losses": losses, "grads": local_grads, "norms": norms, "tp_rank":
                 pc._mesh_rank("tp"), "plan": plan.checkpoint_metadata(), "full": full, "full2": full2,
-                "step": info["step"]}, out.replace(".pt", f"-{rank}.pt"))
+                "step": info["step"], "cont": cont, "after": after}, out.replace(".pt", f"-{rank}.pt"))
 
 
 def _check(tmp_path, name, par, world, extra=None):
@@ -119,6 +129,10 @@ def _check(tmp_path, name, par, world, extra=None):
     for k, v in root["full"].items():
         torch.testing.assert_close(v, ref_state[k], rtol=1e-3, atol=2e-4)
         torch.testing.assert_close(root["full2"][k], v, rtol=0, atol=0)
+    # the resumed engine continues exactly like the original
+    assert root["cont"][0] == root["cont"][1], root["cont"]
+    for k, v in root["after"][0].items():
+        torch.testing.assert_close(root["after"][1][k], v, rtol=0, atol=0)
     # per-shard gradients (model-parallel without FSDP)
     if root["grads"]:
         from parallel_b200.parallel.model_parallel.plan import ParameterPlacement  # noqa: F401
