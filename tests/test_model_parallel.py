@@ -176,6 +176,11 @@ def test_dense_tp_fsdp_composition(tmp_path, sp):
     _check(tmp_path, "tiny-qwen3", {"tp": 2, "sp": sp, "dp_shard": 2}, 4)
 
 
+def test_dense_tp_sp_fsdp_cpu_offload(tmp_path):
+    """FSDP shards in host memory under TP+SP (engine.cpu_offload)."""
+    _check(tmp_path, "tiny-qwen3", {"tp": 2, "sp": 2, "dp_shard": 2}, 4, {"engine.cpu_offload": "true"})
+
+
 def test_dense_tp_sp_with_dp_replicate(tmp_path):
     """TP+SP with replicated data parallelism (gradient all-reduce over the
     replicas, no FSDP) at tp=2 x dp_replicate=2."""
