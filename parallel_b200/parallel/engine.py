@@ -184,18 +184,33 @@ class ParallelEngine:
     # ------------------------------------------------------------------ whole step
     def train_step(self, x, y):
         """Forward, backward and optimizer step on one batch; returns the loss
-        as a device tensor (no host synchronisation).  After
-        ``capture_train_step`` this replays the captured CUDA graph instead
-        (the returned tensor is then the graph's static loss, overwritten by
-        the next call)."""
+        as a device tensor (no host synchronisation).  ``x`` / ``y`` are token
+        ids [B, S], or [A, B, S] for A micro-batches accumulated into one
+        optimizer step (each micro-batch loss scaled by 1/A, as the training
+        loop does with ``config.grad_accum_steps``; the returned loss is their
+        sum).  After ``capture_train_step`` this replays the captured CUDA
+        graph instead (the returned tensor is then the graph's static loss,
+        overwritten by the next call)."""
         if self._graph is not None:
             return self._graph.replay(x, y)
         if self._graph_pending is not None:
             return self._pending_graph_step(x, y)
-        outputs = self.forward(x, y)
-        self.backward(outputs.loss)
+        return self._eager_step(x, y)
+
+    def _eager_step(self, x, y):
+        if x.dim() == 2:
+            outputs = self.forward(x, y)
+            self.backward(outputs.loss)
+            self.step()
+            return outputs.loss.detach()
+        A = x.shape[0]
+        total = None
+        for a in range(A):
+            loss = self.forward(x[a], y[a]).loss / A
+            self.backward(loss)
+            total = loss.detach() if total is None else total + loss.detach()
         self.step()
-        return outputs.loss.detach()
+        return total
 
     def enable_graph_capture(self, warmup_steps: int = 2):
         """From the next ``train_step`` on: run ``warmup_steps`` ordinary steps
@@ -224,10 +239,7 @@ class ParallelEngine:
             st["left"] -= 1
             st["stream"].wait_stream(cur)
             with torch.cuda.stream(st["stream"]):
-                outputs = self.forward(x, y)
-                self.backward(outputs.loss)
-                self.step()
-                loss = outputs.loss.detach()
+                loss = self._eager_step(x, y)
             cur.wait_stream(st["stream"])
             loss.record_stream(cur)
             return loss

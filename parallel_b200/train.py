@@ -76,8 +76,6 @@ def main(argv=None):
     graph_step = bool(cfg.engine.compile)
     if graph_step and pconfig.model_parallel_enabled:
         raise NotImplementedError("engine.compile is not yet supported with folded model parallelism")
-    if graph_step and cfg.config.grad_accum_steps != 1:
-        raise NotImplementedError("engine.compile captures one whole step; it needs config.grad_accum_steps=1")
     if graph_step and cfg.engine.get("collective_profiling", False):
         raise NotImplementedError("engine.compile replays the step as one graph; per-collective profiling needs "
                                   "eager steps")
@@ -129,7 +127,14 @@ def main(argv=None):
         total = torch.tensor(0.0, device=device)
         dl_state = None
         if graph_step:
-            x, y, dl_state = next(train_loader)
+            # the micro-batches of the step stacked [accum, B, T]: one captured
+            # step accumulates them and runs the optimizer
+            batches = [next(train_loader) for _ in range(accum)]
+            dl_state = batches[-1][2]
+            if accum == 1:
+                x, y = batches[0][0], batches[0][1]
+            else:
+                x, y = torch.stack([b[0] for b in batches]), torch.stack([b[1] for b in batches])
             total += engine.train_step(x, y)
         else:
             for _ in range(accum):

@@ -32,6 +32,24 @@ def test_train_step_equals_forward_backward_step():
         torch.testing.assert_close(p, q, rtol=0, atol=0, msg=n)
 
 
+def test_train_step_accumulates_stacked_micro_batches():
+    """train_step on [A, B, S] equals the training loop's accumulation: each
+    micro-batch loss scaled by 1/A, backward per micro-batch, one step."""
+    a, ma = _engine()
+    b, mb = _engine()
+    tok = torch.randint(0, 1024, (3, 2, 33), generator=torch.Generator().manual_seed(2))
+    la = a.train_step(tok[..., :-1], tok[..., 1:])
+    total = 0.0
+    for i in range(3):
+        loss = b.forward(tok[i, :, :-1], tok[i, :, 1:]).loss / 3
+        b.backward(loss)
+        total += float(loss.detach())
+    b.step()
+    assert abs(float(la) - total) < 1e-6
+    for (n, p), q in zip(ma.named_parameters(), mb.parameters()):
+        torch.testing.assert_close(p, q, rtol=0, atol=0, msg=n)
+
+
 def test_graph_capture_refused_on_cpu():
     eng, _ = _engine()
     tok = torch.randint(0, 1024, (2, 17))

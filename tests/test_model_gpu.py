@@ -148,6 +148,45 @@ def test_deferred_graph_capture_follows_the_eager_trajectory():
     graphed.release_graph()
 
 
+def test_graph_step_accumulates_micro_batches():
+    """A captured step over two stacked micro-batches [2, B, S] follows the
+    eager accumulation (loss / 2 per micro-batch, one optimizer step)."""
+    from parallel_b200.config import from_dotlist, load_cfg, merge
+    from parallel_b200.ops._ext import check_device_errors
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    c = merge(load_cfg(argv=[]), from_dotlist(["config.device_type=cuda", "model.learning_rate=3e-3"]))
+    engines = []
+    for _ in range(2):
+        cfg, _, gpu = _pair("small-qwen3")
+        pc = ParallelConfig(c)
+        pc.set_device_mesh("cuda")
+        engines.append(ParallelEngine(gpu, None, pc, c, torch.device("cuda", 0)))
+    eager, graphed = engines
+    graphed.enable_graph_capture(warmup_steps=1)
+    g = torch.Generator().manual_seed(7)
+    toks = [torch.randint(0, cfg.vocab_size, (2, 2, 129), generator=g).cuda() for _ in range(4)]
+    le, lg = [], []
+    for t in toks:
+        total = 0.0
+        for a in range(2):
+            loss = eager.forward(t[a, :, :-1], t[a, :, 1:]).loss / 2
+            eager.backward(loss)
+            total += float(loss.detach())
+        eager.step()
+        le.append(total)
+        lg.append(float(graphed.train_step(t[..., :-1], t[..., 1:])))
+    assert graphed._graph is not None
+    torch.cuda.synchronize()
+    check_device_errors()
+    assert max(abs(a - b) for a, b in zip(le, lg)) < 2e-2, (le, lg)
+    pe, pg = dict(eager.model.named_parameters()), dict(graphed.model.named_parameters())
+    for n, p in pe.items():
+        assert _rel(pg[n].detach(), p.detach()) < 2e-2, n
+    graphed.release_graph()
+
+
 def test_device_error_word_surfaces_as_collective_timeout():
     """A bounded device wait that gave up (its error word, written here from the
     host) is read back asynchronously with the step's finite flag and raised at

@@ -52,14 +52,13 @@ def _run_fail(tmp, extra):
 
 def test_train_cli_compile_selects_the_graph_step_and_refuses_what_it_cannot_capture(tmp_path):
     """engine.compile=true captures the training step as a CUDA graph: it is
-    refused with gradient accumulation and on a CPU device, with a clear error."""
+    refused on a CPU device, with a clear error."""
     from parallel_b200.models.config import resolve_config
     from parallel_b200.models.loading import save_pretrained
     from parallel_b200.models.qwen3 import build_model
 
     tmp = str(tmp_path)
     save_pretrained(build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0), f"{tmp}/init")
-    err = _run_fail(tmp, ["engine.compile=true", "config.grad_accum_steps=2"])
-    assert "grad_accum_steps=1" in err, err[-2000:]
-    err = _run_fail(tmp, ["engine.compile=true", "config.grad_accum_steps=1"])
-    assert "needs a CUDA device" in err, err[-2000:]
+    for accum in (1, 2):
+        err = _run_fail(tmp, ["engine.compile=true", f"config.grad_accum_steps={accum}"])
+        assert "needs a CUDA device" in err, err[-2000:]
