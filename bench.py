@@ -309,8 +309,10 @@ def run_ours(args, rank, world, local):
     clocks.start()
     for i in range(args.warmup):
         step(dev[i % nb])
-    # (the captured step covers data parallelism; model-parallel steps run eagerly)
-    use_graph = not args.no_graph and args.tp == 1 and os.environ.get("PB_GRAPH", "1") != "0"
+    # (the captured step covers dense data parallelism; model-parallel and MoE
+    # steps run eagerly: MoE routing sizes its grouped GEMMs on the host)
+    use_graph = (not args.no_graph and args.tp == 1 and not engine.model.config.is_moe
+                 and os.environ.get("PB_GRAPH", "1") != "0")
     if use_graph:
         # one more eager step on the capture stream, then the capture (untimed)
         engine.capture_train_step(dev[0][:, :-1], dev[0][:, 1:], warmup=1)

@@ -29,9 +29,10 @@ reuse of a reduce-scatter slot or of a shard comes after the previous
 step's gradient-norm all-reduce, which no rank passes before every rank's
 reductions and gathers of that step have finished.
 
-Not capturable (the runner refuses them): model parallelism (MoE routing
-sends the route counts to the host; the fused sequence-parallel kernels use
-host-side flag targets), fp16 loss scaling (host decisions), CPU devices.
+Not capturable (the runner refuses them): MoE models (the routing sends the
+route counts to the host to size the grouped expert GEMMs), model
+parallelism (the fused sequence-parallel kernels use host-side flag
+targets), fp16 loss scaling (host decisions), CPU devices.
 """
 from __future__ import annotations
 
@@ -50,6 +51,9 @@ class GraphedTrainStep:
             raise RuntimeError("CUDA-graph steps do not support fp16 loss scaling")
         if engine.mp_wrapper.is_active:
             raise NotImplementedError("CUDA-graph steps support data parallelism (FSDP / replicate) only")
+        if getattr(getattr(engine.model, "config", None), "is_moe", False):
+            raise NotImplementedError("CUDA-graph steps do not support MoE models yet: the routing sizes the "
+                                      "grouped expert GEMMs on the host")
         if not hasattr(engine.optimizer, "enable_graph_hyper"):
             raise RuntimeError("CUDA-graph steps need FusedAdamW")
         self.engine = engine

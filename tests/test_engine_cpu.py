@@ -50,6 +50,22 @@ def test_train_step_accumulates_stacked_micro_batches():
         torch.testing.assert_close(p, q, rtol=0, atol=0, msg=n)
 
 
+def test_graph_capture_refuses_moe_models():
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.qwen3 import build_model
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    cfg = cpu_cfg()
+    pc = ParallelConfig(cfg)
+    pc.set_device_mesh("cpu")
+    m = build_model(resolve_config("tiny-qwen3-moe"), dtype=torch.float32, seed=0)
+    eng = ParallelEngine(m, None, pc, cfg, torch.device("cpu"))
+    with pytest.raises(NotImplementedError, match="MoE"):
+        eng.enable_graph_capture()
+    assert eng._graph_pending is None
+
+
 def test_graph_capture_refused_on_cpu():
     eng, _ = _engine()
     tok = torch.randint(0, 1024, (2, 17))
