@@ -222,9 +222,11 @@ class ParallelEngine:
         ``torch.compile`` there (parallel/parallel/train.py:60-66); here the
         kernels are already hand-written and the remaining cost is launch
         overhead, which the graph removes."""
-        if getattr(getattr(self.model, "config", None), "is_moe", False):
-            raise NotImplementedError("engine.compile (CUDA-graph step) does not support MoE models yet: the "
-                                      "routing sizes the grouped expert GEMMs on the host")
+        from .graph_step import capture_unsupported
+
+        why = capture_unsupported(self)
+        if why is not None:
+            raise NotImplementedError(f"engine.compile (CUDA-graph step) does not support {why}")
         if self.device.type != "cuda":
             raise NotImplementedError("engine.compile captures the training step as a CUDA graph; it needs a "
                                       "CUDA device")

@@ -29,15 +29,38 @@ reuse of a reduce-scatter slot or of a shard comes after the previous
 step's gradient-norm all-reduce, which no rank passes before every rank's
 reductions and gathers of that step have finished.
 
-Not capturable (the runner refuses them): MoE models (the routing sends the
-route counts to the host to size the grouped expert GEMMs), model
-parallelism (the fused sequence-parallel kernels use host-side flag
-targets), fp16 loss scaling (host decisions), CPU devices.
+Not capturable (the runner refuses them, ``capture_unsupported``): MoE
+models (the routing sends the route counts to the host to size the grouped
+expert GEMMs), model parallelism (the fused sequence-parallel kernels use
+host-side flag targets), fp16 loss scaling (host decisions), CPU offload
+(host optimizer), usage bitmaps read on the host (FSDP with
+find_unused_parameters, DP-replicate without FSDP), CPU devices.
 """
 from __future__ import annotations
 
 import torch
 import torch.distributed as dist
+
+
+def capture_unsupported(engine) -> str | None:
+    """Why the engine's training step cannot be captured (each of these makes
+    a host decision or a host read inside the step), or None."""
+    fsdp = engine.fsdp_wrapper
+    if getattr(getattr(engine.model, "config", None), "is_moe", False):
+        return "MoE models yet: the routing sizes the grouped expert GEMMs on the host"
+    if engine.mp_wrapper.is_active:
+        return "model parallelism (the fused sequence-parallel kernels take host-side flag targets)"
+    if engine.grad_scaler.is_enabled():
+        return "fp16 loss scaling (its skip / rescale decisions are taken on the host)"
+    if fsdp.is_active and fsdp.cpu_offload:
+        return "engine.cpu_offload (the optimizer steps on host memory)"
+    if fsdp.is_active and fsdp.find_unused_parameters:
+        return "engine.find_unused_parameters (the usage bitmap is read on the host)"
+    if not fsdp.is_active and engine.pconfig.dp_replicate_size > 1:
+        return "DP-replicate without FSDP (the gradient participation bitmap is read on the host)"
+    if not hasattr(engine.optimizer, "enable_graph_hyper"):
+        return "optimizers other than FusedAdamW"
+    return None
 
 
 class GraphedTrainStep:
@@ -47,15 +70,9 @@ class GraphedTrainStep:
         steps already ran (``ParallelEngine.enable_graph_capture``)."""
         if engine.device.type != "cuda":
             raise RuntimeError("CUDA-graph steps need a CUDA device")
-        if engine.grad_scaler.is_enabled():
-            raise RuntimeError("CUDA-graph steps do not support fp16 loss scaling")
-        if engine.mp_wrapper.is_active:
-            raise NotImplementedError("CUDA-graph steps support data parallelism (FSDP / replicate) only")
-        if getattr(getattr(engine.model, "config", None), "is_moe", False):
-            raise NotImplementedError("CUDA-graph steps do not support MoE models yet: the routing sizes the "
-                                      "grouped expert GEMMs on the host")
-        if not hasattr(engine.optimizer, "enable_graph_hyper"):
-            raise RuntimeError("CUDA-graph steps need FusedAdamW")
+        why = capture_unsupported(engine)
+        if why is not None:
+            raise NotImplementedError(f"CUDA-graph steps do not support {why}")
         self.engine = engine
         dev = engine.device
         self.x = torch.empty(x.shape, dtype=x.dtype, device=dev)

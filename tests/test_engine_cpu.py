@@ -88,3 +88,27 @@ def test_graph_step_count_bookkeeping():
     opt.state[p]["step"] += 1  # what a capture does on the host
     opt.restore_step_counts(counts)
     assert float(opt.state[p]["step"]) == 1.0
+
+
+def test_capture_unsupported_names_each_host_side_decision():
+    from types import SimpleNamespace as NS
+
+    from parallel_b200.parallel.graph_step import capture_unsupported
+
+    def eng(moe=False, mp=False, scaler=False, fsdp=True, offload=False, unused=False, rep=1, fused=True):
+        opt = NS(enable_graph_hyper=lambda d: None) if fused else NS()
+        return NS(model=NS(config=NS(is_moe=moe)), mp_wrapper=NS(is_active=mp),
+                  grad_scaler=NS(is_enabled=lambda: scaler),
+                  fsdp_wrapper=NS(is_active=fsdp, cpu_offload=offload, find_unused_parameters=unused),
+                  pconfig=NS(dp_replicate_size=rep), optimizer=opt)
+
+    assert capture_unsupported(eng()) is None
+    assert capture_unsupported(eng(fsdp=True, rep=2)) is None          # hybrid: bucket all-reduce, capturable
+    assert capture_unsupported(eng(fsdp=False)) is None                 # single device
+    assert "MoE" in capture_unsupported(eng(moe=True))
+    assert "model parallelism" in capture_unsupported(eng(mp=True))
+    assert "fp16" in capture_unsupported(eng(scaler=True))
+    assert "cpu_offload" in capture_unsupported(eng(offload=True))
+    assert "find_unused" in capture_unsupported(eng(unused=True))
+    assert "DP-replicate" in capture_unsupported(eng(fsdp=False, rep=2))
+    assert "FusedAdamW" in capture_unsupported(eng(fused=False))
