@@ -62,3 +62,37 @@ def test_train_cli_compile_selects_the_graph_step_and_refuses_what_it_cannot_cap
     for accum in (1, 2):
         err = _run_fail(tmp, ["engine.compile=true", f"config.grad_accum_steps={accum}"])
         assert "needs a CUDA device" in err, err[-2000:]
+
+
+def _run_dist(tmp, extra, port):
+    env = dict(os.environ, PYTHONPATH=ROOT, WANDB_MODE="disabled")
+    args = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+            "--master-port", str(port), "-m", "parallel_b200.train", f"model.name={tmp}/init",
+            "config.device_type=cpu", "config.backend=gloo", "config.use_amp=false", "data.synthetic=true",
+            "config.max_steps=4", "config.eval_interval=100", "config.eval_steps=1", "parallel.dp_shard=2",
+            "config.checkpoint_interval=2", "model.per_device_batch_size=2", "model.max_seq_length=32",
+            "model.learning_rate=1e-3"] + extra
+    out = subprocess.run(args, env=env, cwd=tmp, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-3000:]
+    return {int(m.group(1)): float(m.group(2))
+            for m in re.finditer(r"step\s+(\d+) \| loss ([0-9.]+)", out.stdout + out.stderr)}
+
+
+def test_train_cli_two_ranks_fsdp_checkpoint_and_exact_resume(tmp_path):
+    """The entry point under torchrun (2 gloo ranks, FSDP): sharded
+    checkpoint at step 2, and a resumed run repeats steps 3-4 exactly."""
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.loading import save_pretrained
+    from parallel_b200.models.qwen3 import build_model
+
+    tmp = str(tmp_path)
+    save_pretrained(build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0), f"{tmp}/init")
+    full = _run_dist(tmp, [f"config.checkpoint_dir={tmp}/ckpt"], 29631)
+    assert sorted(full) == [1, 2, 3, 4], full
+    manifest = f"{tmp}/ckpt/step-00000002/manifest.json"
+    assert os.path.isfile(manifest)
+    resumed = _run_dist(tmp, [f"config.resume_from={tmp}/ckpt/step-00000002", f"config.checkpoint_dir={tmp}/c2"],
+                        29632)
+    assert sorted(resumed) == [3, 4], resumed
+    for s in (3, 4):
+        assert resumed[s] == full[s], (full, resumed)
