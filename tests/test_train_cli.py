@@ -6,6 +6,7 @@ import re
 import subprocess
 import sys
 
+import pytest
 import torch
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -69,7 +70,7 @@ def _run_dist(tmp, extra, port):
     args = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
             "--master-port", str(port), "-m", "parallel_b200.train", f"model.name={tmp}/init",
             "config.device_type=cpu", "config.backend=gloo", "config.use_amp=false", "data.synthetic=true",
-            "config.max_steps=4", "config.eval_interval=100", "config.eval_steps=1", "parallel.dp_shard=2",
+            "config.max_steps=4", "config.eval_interval=100", "config.eval_steps=1",
             "config.checkpoint_interval=2", "model.per_device_batch_size=2", "model.max_seq_length=32",
             "model.learning_rate=1e-3"] + extra
     out = subprocess.run(args, env=env, cwd=tmp, capture_output=True, text=True, timeout=300)
@@ -78,21 +79,23 @@ def _run_dist(tmp, extra, port):
             for m in re.finditer(r"step\s+(\d+) \| loss ([0-9.]+)", out.stdout + out.stderr)}
 
 
-def test_train_cli_two_ranks_fsdp_checkpoint_and_exact_resume(tmp_path):
-    """The entry point under torchrun (2 gloo ranks, FSDP): sharded
-    checkpoint at step 2, and a resumed run repeats steps 3-4 exactly."""
+@pytest.mark.parametrize("topo,port", [(["parallel.dp_shard=2"], 29631), (["parallel.tp=2", "parallel.sp=2"], 29641)])
+def test_train_cli_two_ranks_checkpoint_and_exact_resume(tmp_path, topo, port):
+    """The entry point under torchrun (2 gloo ranks; FSDP, or TP + SP):
+    exact-topology checkpoint at step 2, and a resumed run repeats steps 3-4
+    exactly."""
     from parallel_b200.models.config import resolve_config
     from parallel_b200.models.loading import save_pretrained
     from parallel_b200.models.qwen3 import build_model
 
     tmp = str(tmp_path)
     save_pretrained(build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0), f"{tmp}/init")
-    full = _run_dist(tmp, [f"config.checkpoint_dir={tmp}/ckpt"], 29631)
+    full = _run_dist(tmp, topo + [f"config.checkpoint_dir={tmp}/ckpt"], port)
     assert sorted(full) == [1, 2, 3, 4], full
     manifest = f"{tmp}/ckpt/step-00000002/manifest.json"
     assert os.path.isfile(manifest)
-    resumed = _run_dist(tmp, [f"config.resume_from={tmp}/ckpt/step-00000002", f"config.checkpoint_dir={tmp}/c2"],
-                        29632)
+    resumed = _run_dist(tmp, topo + [f"config.resume_from={tmp}/ckpt/step-00000002",
+                                     f"config.checkpoint_dir={tmp}/c2"], port + 1)
     assert sorted(resumed) == [3, 4], resumed
     for s in (3, 4):
         assert resumed[s] == full[s], (full, resumed)
