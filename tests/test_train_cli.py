@@ -99,3 +99,43 @@ def test_train_cli_two_ranks_checkpoint_and_exact_resume(tmp_path, topo, port):
     assert sorted(resumed) == [3, 4], resumed
     for s in (3, 4):
         assert resumed[s] == full[s], (full, resumed)
+
+
+def test_train_cli_real_data_path_with_local_tokenizer_and_parquet(tmp_path):
+    """data.synthetic=false end to end: a tokenizer saved next to the model
+    (built offline), parquet shards in data.dir (the last one is validation),
+    best-fit packed batches, eval in bits per byte, and an exact resume of
+    the data stream from a checkpoint."""
+    import pyarrow as pa
+    import pyarrow.parquet as pq
+    from tokenizers import Tokenizer, models, pre_tokenizers, trainers
+    from transformers import PreTrainedTokenizerFast
+
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.loading import save_pretrained
+    from parallel_b200.models.qwen3 import build_model
+
+    tmp = str(tmp_path)
+    words = ["alpha", "beta", "gamma", "delta", "epsilon", "zeta", "eta", "theta", "iota", "kappa"]
+    g = torch.Generator().manual_seed(0)
+    texts = [" ".join(words[int(i)] for i in torch.randint(0, 10, (int(n),), generator=g))
+             for n in torch.randint(3, 40, (400,), generator=g)]
+    tok = Tokenizer(models.BPE(unk_token="<unk>"))
+    tok.pre_tokenizer = pre_tokenizers.ByteLevel(add_prefix_space=False)
+    tok.train_from_iterator(texts, trainers.BpeTrainer(vocab_size=300, special_tokens=["<unk>", "<bos>"],
+                                                       initial_alphabet=pre_tokenizers.ByteLevel.alphabet()))
+    save_pretrained(build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0), f"{tmp}/init")
+    PreTrainedTokenizerFast(tokenizer_object=tok, bos_token="<bos>", unk_token="<unk>").save_pretrained(f"{tmp}/init")
+    os.makedirs(f"{tmp}/data")
+    for i, part in enumerate((texts[:300], texts[300:])):
+        pq.write_table(pa.table({"text": part}), f"{tmp}/data/shard_{i:05d}.parquet", row_group_size=50)
+    common = ["data.synthetic=false", f"data.dir={tmp}/data", "config.grad_accum_steps=1",
+              "config.eval_interval=2", "config.eval_steps=2"]
+    out_full = _run(tmp, common)
+    assert sorted(out_full) == [1, 2, 3, 4], out_full
+    state = torch.load(f"{tmp}/ckpt/step-00000002/rank-state-00000.pt", weights_only=False)
+    dl = state["dataloader"]
+    assert "pq_idx" in dl and "doc_buffer" in dl and not dl.get("synthetic"), dl.keys()
+    resumed = _run(tmp, common + [f"config.resume_from={tmp}/ckpt/step-00000002", f"config.checkpoint_dir={tmp}/c2"])
+    for s in (3, 4):
+        assert resumed[s] == out_full[s], (out_full, resumed)
