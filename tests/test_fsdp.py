@@ -139,6 +139,47 @@ def _replicate_worker(rank, world, data, out_q):
         torch.save({"losses": losses, "state": {k: v.detach().clone() for k, v in m.state_dict().items()}}, out_q)
 
 
+def _hybrid_worker(rank, world, data, out_q):
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.qwen3 import build_model
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    cfg = cpu_cfg(**{"parallel.dp_replicate": 2, "parallel.dp_shard": 2})
+    pc = ParallelConfig(cfg)
+    pc.set_device_mesh("cpu")
+    m = build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0)
+    eng = ParallelEngine(m, None, pc, cfg, torch.device("cpu"))
+    losses = []
+    r = pc.data_rank
+    for tok in data:
+        B = tok.shape[0] // world
+        mine = tok[r * B:(r + 1) * B]
+        loss = eng.forward(mine[:, :-1], mine[:, 1:]).loss
+        eng.backward(loss)
+        eng.step()
+        losses.append(eng.reduce_loss(loss.detach()).item())
+    state = eng.state_dict()
+    if rank == 0:
+        torch.save({"losses": losses, "state": state}, out_q)
+
+
+def test_hybrid_replicate_over_fsdp_matches_single_process(tmp_path):
+    """dp_replicate=2 x dp_shard=2: FSDP inside each replica, the reduced shard
+    gradients averaged over the replicas, equals single-process training."""
+    world = 4
+    data = _tokens(world)[:3]
+    out = str(tmp_path / "hsdp.pt")
+    run_ranks(_hybrid_worker, world, data, out)
+    got = torch.load(out, weights_only=False)
+    ref_losses, ref_model = _single_process_losses(data)
+    for a, b in zip(got["losses"], ref_losses):
+        assert abs(a - b) < 1e-5, (got["losses"], ref_losses)
+    ref_sd = ref_model.state_dict()
+    for k, v in got["state"].items():
+        torch.testing.assert_close(v, ref_sd[k], rtol=1e-3, atol=2e-4)
+
+
 def test_dp_replicate_matches_single_process(tmp_path):
     """Replicated data parallelism (gradient all-reduce mean, one participation
     bitmap per step) equals single-process training on the global batch."""
