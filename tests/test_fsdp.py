@@ -160,8 +160,26 @@ def _hybrid_worker(rank, world, data, out_q):
         eng.step()
         losses.append(eng.reduce_loss(loss.detach()).item())
     state = eng.state_dict()
+    # exact-topology checkpoint (shard files written by replica 0 only), then
+    # a fresh engine continues exactly like this one
+    import os
+
+    ck = os.path.join(os.path.dirname(out_q), "hsdp_ckpt")
+    eng.save_checkpoint(ck, step=len(data))
+    m2 = build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=1)
+    eng2 = ParallelEngine(m2, None, pc, cfg, torch.device("cpu"))
+    eng2.load_checkpoint(ck)
+    nxt = data[0][r * (data[0].shape[0] // world):(r + 1) * (data[0].shape[0] // world)]
+    cont = []
+    for e in (eng, eng2):
+        loss = e.forward(nxt[:, :-1], nxt[:, 1:]).loss
+        e.backward(loss)
+        e.step()
+        cont.append(e.reduce_loss(loss.detach()).item())
+    after = [eng.state_dict(), eng2.state_dict()]
     if rank == 0:
-        torch.save({"losses": losses, "state": state}, out_q)
+        files = sorted(f for f in os.listdir(ck) if f.startswith("model-"))
+        torch.save({"losses": losses, "state": state, "cont": cont, "after": after, "files": files}, out_q)
 
 
 def test_hybrid_replicate_over_fsdp_matches_single_process(tmp_path):
@@ -178,6 +196,10 @@ def test_hybrid_replicate_over_fsdp_matches_single_process(tmp_path):
     ref_sd = ref_model.state_dict()
     for k, v in got["state"].items():
         torch.testing.assert_close(v, ref_sd[k], rtol=1e-3, atol=2e-4)
+    assert got["files"] == ["model-shard-00000.pt", "model-shard-00001.pt"], got["files"]
+    assert got["cont"][0] == got["cont"][1], got["cont"]
+    for k, v in got["after"][0].items():
+        torch.testing.assert_close(got["after"][1][k], v, rtol=0, atol=0)
 
 
 def test_dp_replicate_matches_single_process(tmp_path):
