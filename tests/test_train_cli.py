@@ -139,3 +139,31 @@ def test_train_cli_real_data_path_with_local_tokenizer_and_parquet(tmp_path):
     resumed = _run(tmp, common + [f"config.resume_from={tmp}/ckpt/step-00000002", f"config.checkpoint_dir={tmp}/c2"])
     for s in (3, 4):
         assert resumed[s] == out_full[s], (out_full, resumed)
+
+
+def test_train_cli_torch_profiler_and_collective_lines(tmp_path):
+    """engine.torch_profiler writes one gzip trace for the rank after its
+    warm-up / active steps; engine.collective_profiling logs [COLLECTIVE] lines
+    for every step (2 gloo ranks, FSDP)."""
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.loading import save_pretrained
+    from parallel_b200.models.qwen3 import build_model
+
+    tmp = str(tmp_path)
+    save_pretrained(build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0), f"{tmp}/init")
+    env = dict(os.environ, PYTHONPATH=ROOT, WANDB_MODE="disabled")
+    args = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+            "--master-port", "29651", "-m", "parallel_b200.train", f"model.name={tmp}/init",
+            "config.device_type=cpu", "config.backend=gloo", "config.use_amp=false", "data.synthetic=true",
+            "config.max_steps=3", "config.eval_interval=100", "config.eval_steps=1", "parallel.dp_shard=2",
+            "config.checkpoint_interval=0", "model.per_device_batch_size=2", "model.max_seq_length=32",
+            "engine.torch_profiler=true", f"engine.torch_profiler_trace_dir={tmp}/traces",
+            "engine.torch_profiler_warmup_steps=1", "engine.torch_profiler_active_steps=1",
+            "engine.collective_profiling=true"]
+    out = subprocess.run(args, env=env, cwd=tmp, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-3000:]
+    text = out.stdout + out.stderr
+    traces = sorted(os.listdir(f"{tmp}/traces"))
+    assert [t for t in traces if t.startswith("rank0")] and [t for t in traces if t.startswith("rank1")], traces
+    lines = [l for l in text.splitlines() if "[COLLECTIVE]" in l]
+    assert any("fsdp_all_gather" in l for l in lines) and any("fsdp_reduce_scatter" in l for l in lines), lines[:5]
