@@ -112,3 +112,33 @@ def test_capture_unsupported_names_each_host_side_decision():
     assert "find_unused" in capture_unsupported(eng(unused=True))
     assert "DP-replicate" in capture_unsupported(eng(fsdp=False, rep=2))
     assert "FusedAdamW" in capture_unsupported(eng(fused=False))
+
+
+def test_fp16_loss_scaling_halves_the_scale_on_non_finite_gradients():
+    """config.amp_dtype=fp16: the GradScaler path (the reference's
+    engine.py:201-221 semantics): a non-finite step leaves the parameters
+    untouched and halves the scale instead of raising; finite steps update."""
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.qwen3 import build_model
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    cfg = cpu_cfg(**{"config.use_amp": "true", "config.amp_dtype": "fp16"})
+    pc = ParallelConfig(cfg)
+    pc.set_device_mesh("cpu")
+    m = build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0)
+    eng = ParallelEngine(m, None, pc, cfg, torch.device("cpu"))
+    assert eng.grad_scaler.is_enabled()
+    tok = torch.randint(0, 1024, (2, 33), generator=torch.Generator().manual_seed(4))
+    before = {n: p.detach().clone() for n, p in m.named_parameters()}
+    eng.backward(eng.forward(tok[:, :-1], tok[:, 1:]).loss)
+    next(p for p in m.parameters() if p.grad is not None).grad.view(-1)[0] = float("inf")
+    scale = eng.grad_scaler.get_scale()
+    eng.step()                                     # no FloatingPointError with a scaler
+    assert eng.grad_scaler.get_scale() == scale / 2
+    for n, p in m.named_parameters():
+        torch.testing.assert_close(p.detach(), before[n], rtol=0, atol=0, msg=n)
+        assert p.grad is None
+    eng.backward(eng.forward(tok[:, :-1], tok[:, 1:]).loss)
+    eng.step()
+    assert any(not torch.equal(p.detach(), before[n]) for n, p in m.named_parameters())
