@@ -37,7 +37,7 @@ def _single_process_losses(data, accum=1, clip=1.0):
     return losses, m
 
 
-def _fsdp_worker(rank, world, data, ckpt, overlap, accum, out_q, offload=False):
+def _fsdp_worker(rank, world, data, ckpt, overlap, accum, out_q, offload=False, every_n=1):
     from parallel_b200.models.config import resolve_config
     from parallel_b200.models.qwen3 import build_model
     from parallel_b200.parallel.engine import ParallelEngine
@@ -45,7 +45,7 @@ def _fsdp_worker(rank, world, data, ckpt, overlap, accum, out_q, offload=False):
 
     cfg = cpu_cfg(**{"parallel.dp_shard": world, "engine.activation_checkpoint": str(ckpt).lower(),
                      "engine.overlap_backward_reductions": str(overlap).lower(), "config.grad_accum_steps": accum,
-                     "engine.cpu_offload": str(offload).lower()})
+                     "engine.cpu_offload": str(offload).lower(), "engine.checkpoint_every_n": every_n})
     pc = ParallelConfig(cfg)
     pc.set_device_mesh("cpu")
     m = build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0)
@@ -62,8 +62,28 @@ def _fsdp_worker(rank, world, data, ckpt, overlap, accum, out_q, offload=False):
         eng.step()
         losses.append(eng.reduce_loss(total).item())
     full = eng.state_dict()
+    roots = {id(u) for u in eng.fsdp_wrapper.root_units}
+    recompute = [u.use_activation_checkpoint for u in eng.fsdp_wrapper.units if id(u) not in roots]
     if rank == 0:
-        torch.save({"losses": losses, "state": full}, out_q)
+        torch.save({"losses": losses, "state": full, "recompute": recompute}, out_q)
+
+
+def test_fsdp_checkpoint_every_n_layers(tmp_path):
+    """engine.checkpoint_every_n=2: only every second layer unit recomputes its
+    forward in the backward; training still equals single-process training."""
+    world = 2
+    data = _tokens(world)[:3]
+    out = str(tmp_path / "every_n.pt")
+    run_ranks(_fsdp_worker, world, data, True, True, 1, out, False, 2)
+    got = torch.load(out, weights_only=False)
+    n = len(got["recompute"])
+    assert n >= 2 and got["recompute"] == [i % 2 == 0 for i in range(n)], got["recompute"]
+    ref_losses, ref_model = _single_process_losses(data)
+    for a, b in zip(got["losses"], ref_losses):
+        assert abs(a - b) < 1e-5, (got["losses"], ref_losses)
+    ref_sd = ref_model.state_dict()
+    for k, v in got["state"].items():
+        torch.testing.assert_close(v, ref_sd[k], rtol=1e-3, atol=2e-4)
 
 
 @pytest.mark.parametrize("ckpt,overlap,accum,offload", [(True, True, 1, False), (False, True, 2, False),
