@@ -434,3 +434,35 @@ def test_fsdp_one_packed_collective_per_unit_each_way(tmp_path, ckpt):
     root, layers = buckets[0], buckets[1:]
     assert sorted(calls["all_gather"]) == sorted([root] + 2 * layers), calls
     assert sorted(calls["reduce_scatter"]) == sorted(2 * b for b in buckets), calls
+
+
+def _buffer_worker(rank, world, out_q):
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.qwen3 import build_model
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    cfg = cpu_cfg(**{"parallel.dp_replicate": 2, "parallel.dp_shard": 2})
+    pc = ParallelConfig(cfg)
+    pc.set_device_mesh("cpu")
+    m = build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0)
+    eng = ParallelEngine(m, None, pc, cfg, torch.device("cpu"))
+    buf = m.model.rotary_emb.inv_freq
+    buf.add_(float(rank))  # diverge on purpose
+    eng.sync_buffers()
+    got = [torch.zeros_like(buf) for _ in range(world)]
+    import torch.distributed as dist
+
+    dist.all_gather(got, buf.contiguous())
+    if rank == 0:
+        torch.save(got, out_q)
+
+
+def test_sync_buffers_broadcasts_from_the_first_replica_and_shard(tmp_path):
+    """sync_buffers (before eval) makes every rank's buffers equal to global
+    rank 0's, over the replicate and the shard groups."""
+    out = str(tmp_path / "buf.pt")
+    run_ranks(_buffer_worker, 4, out)
+    got = torch.load(out, weights_only=False)
+    for g in got[1:]:
+        torch.testing.assert_close(g, got[0], rtol=0, atol=0)
