@@ -466,3 +466,40 @@ def test_sync_buffers_broadcasts_from_the_first_replica_and_shard(tmp_path):
     got = torch.load(out, weights_only=False)
     for g in got[1:]:
         torch.testing.assert_close(g, got[0], rtol=0, atol=0)
+
+
+def _strict_worker(rank, world, out_q):
+    from parallel_b200.models.config import resolve_config
+    from parallel_b200.models.qwen3 import build_model
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    cfg = cpu_cfg(**{"parallel.dp_shard": 2})
+    pc = ParallelConfig(cfg)
+    pc.set_device_mesh("cpu")
+    src = build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=3).state_dict()
+    m = build_model(resolve_config("tiny-qwen3"), dtype=torch.float32, seed=0)
+    eng = ParallelEngine(m, None, pc, cfg, torch.device("cpu"))
+    partial = {k: v for k, v in src.items() if k != "model.norm.weight"}
+    strict_error = None
+    try:
+        eng.load_state_dict(partial)
+    except RuntimeError as e:
+        strict_error = str(e)
+    eng.load_state_dict(partial, strict=False)
+    full = eng.state_dict()
+    if rank == 0:
+        torch.save({"err": strict_error, "full": full, "src": src}, out_q)
+
+
+def test_load_state_dict_strictness_on_every_rank(tmp_path):
+    """A portable state dict missing a key is rejected with strict=True (on
+    every rank: no rank is left half-loaded) and loads the rest with
+    strict=False."""
+    out = str(tmp_path / "strict.pt")
+    run_ranks(_strict_worker, 2, out)
+    got = torch.load(out, weights_only=False)
+    assert got["err"] is not None and "model.norm.weight" in got["err"], got["err"]
+    for k, v in got["src"].items():
+        if k != "model.norm.weight":
+            torch.testing.assert_close(got["full"][k], v, rtol=0, atol=0, msg=k)
