@@ -104,20 +104,44 @@ def _corrupt_worker(rank, world, d, mode):
             torch.save(payload, p)
         elif mode == "complete":
             os.remove(os.path.join(ck, "COMPLETE"))
+        elif mode == "topology":
+            p = os.path.join(ck, "manifest.json")
+            m = json.load(open(p))
+            m["topology"]["dp_replicate"] = 2
+            json.dump(m, open(p, "w"))
+        elif mode == "rng":
+            p = os.path.join(ck, "rank-state-00001.pt")
+            payload = torch.load(p, weights_only=False)
+            del payload["rng"]["numpy"]
+            torch.save(payload, p)
     torch.distributed.barrier()
-    eng2, _ = _engine(world)
+    if mode == "layout":
+        # the same topology, a different model: 3 decoder layers instead of 2
+        from parallel_b200.models.config import resolve_config
+        from parallel_b200.models.qwen3 import build_model
+        from parallel_b200.parallel.engine import ParallelEngine
+        from parallel_b200.state import ParallelConfig
+
+        cfg = cpu_cfg(**{"parallel.dp_shard": world})
+        pc = ParallelConfig(cfg)
+        pc.set_device_mesh("cpu")
+        m3 = build_model(resolve_config("tiny-qwen3", num_hidden_layers=3), dtype=torch.float32, seed=0)
+        eng2 = ParallelEngine(m3, None, pc, cfg, torch.device("cpu"))
+    else:
+        eng2, _ = _engine(world)
     try:
         eng2.load_checkpoint(ck)
     except RuntimeError as e:
         msg = str(e)
         expect = {"version": "Unsupported checkpoint version", "shard": "parameter shards",
-                  "complete": "COMPLETE"}[mode]
+                  "complete": "COMPLETE", "topology": "topology does not match",
+                  "layout": "layout does not match", "rng": "incomplete RNG state"}[mode]
         assert expect in msg, msg
         return
     raise AssertionError("corrupted checkpoint loaded")
 
 
-@pytest.mark.parametrize("mode", ["version", "shard", "complete"])
+@pytest.mark.parametrize("mode", ["version", "shard", "complete", "topology", "layout", "rng"])
 def test_corrupted_checkpoints_fail_on_every_rank(tmp_path, mode):
     run_ranks(_corrupt_worker, 2, str(tmp_path), mode)
 
