@@ -309,9 +309,11 @@ def run_ours(args, rank, world, local):
     clocks.start()
     for i in range(args.warmup):
         step(dev[i % nb])
-    # (the captured step covers dense data parallelism; model-parallel and MoE
-    # steps run eagerly: MoE routing sizes its grouped GEMMs on the host)
-    use_graph = (not args.no_graph and args.tp == 1 and not engine.model.config.is_moe
+    # (the captured step covers data parallelism, dense or MoE; model-parallel
+    # steps run eagerly: the fused sequence-parallel kernels take host-side flag targets)
+    from parallel_b200.parallel.graph_step import capture_unsupported
+
+    use_graph = (not args.no_graph and capture_unsupported(engine) is None
                  and os.environ.get("PB_GRAPH", "1") != "0")
     if use_graph:
         # one more eager step on the capture stream, then the capture (untimed)

@@ -21,7 +21,10 @@ __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + __expf
 // 8 bf16 per thread per step.
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dh, int64_t lddh,
                                   const __nv_bfloat16* __restrict__ gu, int64_t ldgu,
-                                  __nv_bfloat16* __restrict__ dgu, int64_t lddgu, int T, int I) {
+                                  __nv_bfloat16* __restrict__ dgu, int64_t lddgu, int T, int I,
+                                  const int* __restrict__ tiles128) {
+  // tiles128 (optional, device): only the first 128 * *tiles128 rows are live
+  if (tiles128 != nullptr) T = min(T, *tiles128 * 128);
   const int vec_per_row = I / 8;
   const int64_t total = (int64_t)T * vec_per_row;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
@@ -171,10 +174,10 @@ int grid_for(int64_t work, int threads) {
 }  // namespace
 
 void swiglu_bwd(const void* dh, int64_t lddh, const void* gu, int64_t ldgu, void* dgu,
-                int64_t lddgu, int T, int I, cudaStream_t s) {
+                int64_t lddgu, int T, int I, cudaStream_t s, const int* tiles128) {
   PB_CHECK(I % 8 == 0, "swiglu: I must be a multiple of 8");
   swiglu_bwd_kernel<<<grid_for((int64_t)T * I / 8, 256), 256, 0, s>>>(
-      (const __nv_bfloat16*)dh, lddh, (const __nv_bfloat16*)gu, ldgu, (__nv_bfloat16*)dgu, lddgu, T, I);
+      (const __nv_bfloat16*)dh, lddh, (const __nv_bfloat16*)gu, ldgu, (__nv_bfloat16*)dgu, lddgu, T, I, tiles128);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -57,3 +57,23 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s);
 int64_t attention_bwd_ds_elems(int B, int S, int nq, bool causal);
 
 }  // namespace pb
+
+// Allocation-free attention backward (attention_bwd.cu).  These C entry points
+// have no counterpart in the reference; they serve callers that cannot
+// allocate device memory (see the comment above their definitions).  Return
+// codes of pb_attention_bwd_noalloc: 0 ok, 1 problem larger than the fixed
+// scratch array, 2 invalid arguments, 3 CUDA error (message from
+// pb_attention_bwd_noalloc_last_error, per calling thread).
+extern "C" {
+int pb_attention_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                             const float* lse, void* dq, void* dk, void* dv, int64_t ldq, int64_t ldk, int64_t ldv,
+                             int64_t ldo, int64_t lddo, int64_t lddq, int64_t lddk, int64_t lddv, int B, int S,
+                             int nq, int nkv, int D, float scale, int causal, cudaStream_t stream);
+// bytes of the fixed per-device scratch array
+size_t pb_attention_bwd_noalloc_scratch_bytes(void);
+// message of the calling thread's last failed call ("" after a success)
+const char* pb_attention_bwd_noalloc_last_error(void);
+// bounded-wait status word of the last call on the current device (0 = no
+// wait gave up; -1 = no call yet or a CUDA error); synchronises the device
+int pb_attention_bwd_noalloc_device_status(void);
+}

@@ -723,13 +723,21 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   PB_CHECK(p.D == HD, "attention: head_dim must be 128");
   PB_CHECK(p.nq % p.nkv == 0, "attention: nq must be a multiple of nkv");
   PB_CHECK(p.S % 8 == 0, "attention bwd: sequence length must be a multiple of 8");
-  static bool attr = false;
-  if (!attr) {
-    for (auto k : {attn_bwd_kernel<false, false>, attn_bwd_kernel<true, false>, attn_bwd_kernel<false, true>,
-                   attn_bwd_kernel<true, true>})
-      PB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    PB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DQ_SMEM));
-    attr = true;
+  // the dynamic shared-memory limit is a per-device function attribute
+  {
+    static std::mutex mu;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    PB_CUDA_CHECK(cudaGetDevice(&dev));
+    PB_CHECK(dev >= 0 && dev < 64, "attention bwd: device index out of range");
+    std::lock_guard<std::mutex> lk(mu);
+    if (!attr_set[dev]) {
+      for (auto k : {attn_bwd_kernel<false, false>, attn_bwd_kernel<true, false>, attn_bwd_kernel<false, true>,
+                     attn_bwd_kernel<true, true>})
+        PB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+      PB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DQ_SMEM));
+      attr_set[dev] = true;
+    }
   }
   const bool ds_path = p.ds_buf != nullptr;
   PB_CHECK(ds_path || p.dq_acc != nullptr, "attention bwd: needs a dS tile buffer or a dQ accumulator");
@@ -935,10 +943,15 @@ extern "C" __attribute__((visibility("default"))) int pb_attention_bwd_noalloc(
 // kept in the scratch array; synchronises the device first).
 extern "C" __attribute__((visibility("default"))) int pb_attention_bwd_noalloc_device_status() {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= pb::kMaxDevices || !pb::g_noalloc_base[dev])
-    return -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= pb::kMaxDevices) return -1;
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(pb::g_noalloc_mu);  // the first call on a device writes it under the lock
+    base = pb::g_noalloc_base[dev];
+  }
+  if (base == nullptr) return -1;
   int v = 0;
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;
-  if (cudaMemcpy(&v, pb::g_noalloc_base[dev], sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  if (cudaMemcpy(&v, base, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
   return v;
 }

@@ -175,7 +175,8 @@ void gemm_rs(const at::Tensor& a, const at::Tensor& b, bool b_mn, double alpha, 
 //   mode 2: a [rows, M_group], b [rows, N], out [E, M_group, N]
 void gemm_grouped(int64_t mode, const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const at::Tensor& work,
                   const c10::optional<at::Tensor>& krange, bool b_mn, int64_t epi, double alpha,
-                  const c10::optional<at::Tensor>& r, int64_t b_up_offset, int64_t n_out) {
+                  const c10::optional<at::Tensor>& r, int64_t b_up_offset, int64_t n_out,
+                  const c10::optional<at::Tensor>& tile_expert, const c10::optional<at::Tensor>& n_tiles) {
   CHECK_CUDA_BF16(a);
   CHECK_CUDA_BF16(b);
   TORCH_CHECK(a.is_contiguous() && b.is_contiguous() && out.is_contiguous(), "gemm_grouped: contiguous operands");
@@ -230,6 +231,16 @@ void gemm_grouped(int64_t mode, const at::Tensor& a, const at::Tensor& b, at::Te
     p.R = r->data_ptr();
     p.ldr = r->stride(0);
   }
+  if (tile_expert.has_value() && tile_expert->defined()) {
+    TORCH_CHECK(mode == 1 && n_tiles.has_value() && n_tiles->defined(), "gemm_grouped: device tiles need rows mode");
+    TORCH_CHECK(tile_expert->is_cuda() && tile_expert->scalar_type() == at::kInt && tile_expert->is_contiguous() &&
+                    tile_expert->numel() * 128 == p.M_total,
+                "gemm_grouped: tile_expert int32 [M_pad / 128]");
+    TORCH_CHECK(n_tiles->is_cuda() && n_tiles->scalar_type() == at::kInt && n_tiles->numel() >= 1,
+                "gemm_grouped: n_tiles int32 [1]");
+    p.tile_expert = tile_expert->data_ptr<int>();
+    p.n_tiles = n_tiles->data_ptr<int>();
+  }
   pb::gemm_grouped(p, cur_stream());
 }
 
@@ -246,6 +257,7 @@ void set_error_for_test(int64_t device, int64_t code) {
 
 void register_ops(pybind11::module& m);
 void register_comm(pybind11::module& m);
+void register_moe(pybind11::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "parallel_b200 sm_100a kernels";
@@ -267,10 +279,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped", &gemm_grouped, "grouped (mixture-of-experts) GEMM driven by a device work table",
         pybind11::arg("mode"), pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("out"), pybind11::arg("work"),
         pybind11::arg("krange"), pybind11::arg("b_mn"), pybind11::arg("epi"), pybind11::arg("alpha"),
-        pybind11::arg("r") = pybind11::none(), pybind11::arg("b_up_offset") = 0, pybind11::arg("n_out") = 0);
+        pybind11::arg("r") = pybind11::none(), pybind11::arg("b_up_offset") = 0, pybind11::arg("n_out") = 0,
+        pybind11::arg("tile_expert") = pybind11::none(), pybind11::arg("n_tiles") = pybind11::none());
   m.def("read_error", &read_error);
   m.def("clear_error", &clear_error);
   m.def("set_error_for_test", &set_error_for_test);
   register_ops(m);
   register_comm(m);
+  register_moe(m);
 }

@@ -95,6 +95,12 @@ struct GroupedGemmParams {
   const int4* work = nullptr;
   int n_work = 0;
   const int2* krange = nullptr;
+  // rows mode over a device-described padded matrix: when tile_expert is set,
+  // the work items are every (128-row tile, N tile) of the first *n_tiles
+  // tiles, with the tile's expert from tile_expert; `work` / `n_work` are
+  // unused and the grid is sized for M_total / 128 tiles
+  const int* tile_expert = nullptr;
+  const int* n_tiles = nullptr;
 };
 void gemm_grouped(const GroupedGemmParams& p, cudaStream_t stream);
 

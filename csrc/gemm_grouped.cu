@@ -13,8 +13,12 @@
 //   k (weight gradient): work item {expert e, M tile, N tile};
 //     dW_e = A^T B over the expert's row range only (krange[e], multiples of
 //     64), both operands MN-major views of the row matrices, C = stacked
-//     [E][M][N].  Experts without rows are left out of the work table (the
-//     caller zero-fills their dW).
+//     [E][M][N].  The device-resident MoE layout gives every expert at least
+//     one (zero) tile, so no work item meets an empty K range.
+//   rows mode can also take its items from the device: with tile_expert /
+//     n_tiles set, the items are every (tile, N tile) of the first *n_tiles
+//     128-row tiles (the count the routing plan wrote), so no row count has
+//     to reach the host.
 // Warp roles and the double-buffered TMEM accumulator follow the one-CTA
 // kernel in gemm.cu; each wait is bounded.
 //
@@ -53,7 +57,8 @@ template <int BN, bool A_MN, bool B_MN, bool SWIGLU, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_grouped_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiArgs ep,
                         const int4* __restrict__ work, int n_work, const int2* __restrict__ krange, int M_total,
-                        int M_group, int N, int K, int b_up_row, int* err) {
+                        int M_group, int N, int K, int b_up_row, const int* __restrict__ tile_expert,
+                        const int* __restrict__ n_tiles, int ntn, int* err) {
   using Cfg = GCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int BN_OUT = SWIGLU ? BN / 2 : BN;
@@ -95,6 +100,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // device-described rows mode: every (tile, N tile) of the first *n_tiles tiles
+  if (tile_expert != nullptr) n_work = *((volatile const int*)n_tiles) * ntn;
+  auto item = [&](int w) -> int4 {
+    if (tile_expert == nullptr) return work[w];
+    const int t = w / ntn;
+    return make_int4(tile_expert[t], t, w - t * ntn, 0);
+  };
+
   // K blocks of a work item: all of K (rows mode) or the expert's rows (k mode)
   auto k_span = [&](int e, int& kb0, int& kb1) {
     if (MODE == 2) {
@@ -113,7 +126,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
-        const int4 it = work[w];
+        const int4 it = item(w);
         const int e = it.x, tm = it.y, tn = it.z;
         int kb0, kb1;
         k_span(e, kb0, kb1);
@@ -155,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int local = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x, ++local) {
-        const int e = work[w].x;
+        const int e = item(w).x;
         int kb0, kb1;
         k_span(e, kb0, kb1);
         const int acc = local & 1;
@@ -186,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quarter * 32 + lane;
     int local = 0;
     for (int w = blockIdx.x; w < n_work; w += gridDim.x, ++local) {
-      const int4 it = work[w];
+      const int4 it = item(w);
       const int e = it.x, tm = it.y, tn = it.z;
       const int acc = local & 1;
       if (!mbar_wait(&tfull_bar[acc], (local >> 1) & 1, err)) break;
@@ -244,9 +257,13 @@ void launch_grouped(const GroupedGemmParams& p, cudaStream_t stream) {
     tb = make_tmap_2d_bf16(p.B, p.N, p.rows, p.ldb, 64, BK);
   }
   EpiArgs ep{p.C, p.R, p.ldc, p.ldr, p.alpha, p.epi, SWIGLU ? p.b_up_offset : 0};
-  const int ctas = std::max(1, std::min(num_sms(dev), p.n_work));
+  constexpr int BN_OUT = SWIGLU ? BN / 2 : BN;
+  const int ntn = (p.N + BN_OUT - 1) / BN_OUT;
+  const int max_items = p.tile_expert != nullptr ? (p.M_total / BM) * ntn : p.n_work;
+  const int ctas = std::max(1, std::min(num_sms(dev), max_items));
   kern<<<ctas, kThreads, Cfg::SMEM_BYTES, stream>>>(ta, tb, ep, p.work, p.n_work, p.krange, p.M_total, p.M_group,
-                                                    p.N, p.K, (int)p.b_up_offset, error_word(dev));
+                                                    p.N, p.K, (int)p.b_up_offset, p.tile_expert, p.n_tiles, ntn,
+                                                    error_word(dev));
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -255,7 +272,8 @@ void launch_grouped(const GroupedGemmParams& p, cudaStream_t stream) {
 void gemm_grouped(const GroupedGemmParams& p, cudaStream_t stream) {
   PB_CHECK(p.n_work >= 0 && p.E > 0 && p.N > 0 && p.K > 0, "grouped gemm: sizes");
   PB_CHECK(p.lda % 8 == 0 && p.ldb % 8 == 0 && p.ldc % 8 == 0, "grouped gemm: strides must be multiples of 8");
-  if (p.n_work == 0) return;
+  PB_CHECK(p.tile_expert == nullptr || (p.mode == 1 && p.n_tiles != nullptr), "grouped gemm: device tiles need rows mode");
+  if (p.n_work == 0 && p.tile_expert == nullptr) return;
   if (p.mode == 1) {
     PB_CHECK(p.M_total % BM == 0, "grouped gemm: the row matrix must be 128-row padded");
     if (p.epi == kEpiSwiGLU) return launch_grouped<256, false, false, true, 1>(p, stream);

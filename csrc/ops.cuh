@@ -38,7 +38,7 @@ void qknorm_rope_bwd(const void* dq, int64_t lddq, const void* dk, int64_t lddk,
 // ---- SwiGLU backward (act.cu): gu = [g | u] (row stride ldgu, u at column I)
 // dgu[:, :I] = dh * u * silu'(g), dgu[:, I:] = dh * silu(g)
 void swiglu_bwd(const void* dh, int64_t lddh, const void* gu, int64_t ldgu, void* dgu,
-                int64_t lddgu, int T, int I, cudaStream_t s);
+                int64_t lddgu, int T, int I, cudaStream_t s, const int* tiles128 = nullptr);
 // h = silu(g) * u (used on the CPU-parity path and by the MoE experts)
 
 // ---- embedding (act.cu)

@@ -73,11 +73,18 @@ void qknorm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tenso
                       (int)nkv, D, cur_stream());
 }
 
-void swiglu_bwd(const at::Tensor& dh, const at::Tensor& gu, at::Tensor& dgu) {
+// tiles128 (optional int32 CUDA [1]): only the first 128 * tiles128[0] rows are live
+void swiglu_bwd(const at::Tensor& dh, const at::Tensor& gu, at::Tensor& dgu, const c10::optional<at::Tensor>& tiles128) {
   CHECK_BF16(dh); CHECK_BF16(gu); CHECK_BF16(dgu);
+  const int* tiles = nullptr;
+  if (tiles128.has_value() && tiles128->defined()) {
+    TORCH_CHECK(tiles128->is_cuda() && tiles128->scalar_type() == at::kInt && tiles128->numel() >= 1,
+                "swiglu_bwd: tiles128 int32 CUDA [1]");
+    tiles = tiles128->data_ptr<int>();
+  }
   const c10::cuda::CUDAGuard g(dh.device());
   pb::swiglu_bwd(dh.data_ptr(), dh.stride(0), gu.data_ptr(), gu.stride(0), dgu.data_ptr(), dgu.stride(0),
-                 dh.size(0), dh.size(1), cur_stream());
+                 dh.size(0), dh.size(1), cur_stream(), tiles);
 }
 
 void embedding_fwd(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int64_t v0) {
@@ -311,7 +318,8 @@ void register_ops(pybind11::module& m) {
         py::arg("dw"), py::arg("dres") = py::none());
   m.def("qknorm_rope_fwd", &qknorm_rope_fwd);
   m.def("qknorm_rope_bwd", &qknorm_rope_bwd);
-  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("swiglu_bwd", &swiglu_bwd, pybind11::arg("dh"), pybind11::arg("gu"), pybind11::arg("dgu"),
+        pybind11::arg("tiles128") = pybind11::none());
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("scale_by_scalar", &scale_by_scalar);

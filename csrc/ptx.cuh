@@ -25,6 +25,7 @@ enum ErrorCode : int {
   kErrMbarTimeout = 1,
   kErrPeerTimeout = 2,
   kErrBadArg = 3,
+  kErrMoeCapacity = 4,  // an MoE layout needed more rows than its worst-case buffers
 };
 
 __device__ __forceinline__ void record_error(int* err, int code) {

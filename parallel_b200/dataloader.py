@@ -8,9 +8,10 @@ document that fits; when none fits, the shortest one is cropped), and the
 rows are staged in pinned memory and copied to the device asynchronously.
 ``state`` (pq_idx, rg_idx, epoch, batch_idx, doc_buffer, dataset identity,
 loader config) resumes the stream exactly; resuming rejects changed data
-files or loader configuration.  Semantics follow parallel/parallel/
-dataloader.py:11-213; the packer keeps its buffer ordered by (length,
-arrival) so each pick is O(log n) instead of a scan.
+files or loader configuration.  Behaviour (row-group striding, packing
+choices, resume position and state keys) is that of the reference's
+parallel/parallel/dataloader.py:11-213; the packer keeps its buffer ordered by
+(length, arrival) so each pick is O(log n) instead of a scan.
 
 ``synthetic_data_loader`` yields uniform random token ids of the same shape
 (``data.synthetic=true``).
@@ -28,55 +29,60 @@ from .dataset import list_data_files
 
 
 def _split_data_files(split: str, data_dir: str | None = None) -> list[str]:
-    paths = list_data_files(data_dir)
-    if not paths:
-        raise RuntimeError("No data found; run dataset.py first")
-    if split == "train" and len(paths) < 2:
-        raise RuntimeError("Training requires at least two data files because the final file is reserved for "
-                           "validation")
-    sel = paths[:-1] if split == "train" else paths[-1:]
-    return [str(Path(p).resolve()) for p in sel]
+    """Resolved shard paths of ``split``: the last shard is validation, the
+    rest are training (which therefore needs at least two shards)."""
+    shards = [str(Path(p).resolve()) for p in list_data_files(data_dir)]
+    if not shards:
+        raise RuntimeError("no data shards found; download them with python -m parallel_b200.dataset")
+    if split == "train":
+        if len(shards) == 1:
+            raise RuntimeError("training needs two or more shards: the last shard is the validation split")
+        return shards[:-1]
+    return shards[-1:]
 
 
 def _dataset_identity(paths: list[str]) -> list[dict]:
-    out = []
-    for p in paths:
-        st = Path(p).stat()
-        out.append({"path": p, "size": st.st_size, "mtime_ns": st.st_mtime_ns})
-    return out
+    """(path, size, modification time) of every shard: a resumed loader must
+    see the very same files."""
+    stats = [(p, Path(p).stat()) for p in paths]
+    return [{"path": p, "size": st.st_size, "mtime_ns": st.st_mtime_ns} for p, st in stats]
+
+
+def _resume_position(resume, data_rank: int, data_world: int):
+    """(shard, row group, first text chunk, epoch) to continue from.
+
+    A state records the last chunk handed out (``batch_idx``); the walk goes
+    on with the next chunk of that row group.  A state without a chunk index
+    continues with this rank's next row group of that shard."""
+    if resume is None:
+        return 0, data_rank, 0, 1
+    shard, group, chunk, epoch = resume["pq_idx"], resume.get("rg_idx"), resume.get("batch_idx"), resume.get("epoch", 1)
+    if group is None:
+        return shard, data_rank, 0, epoch
+    if chunk is None:
+        return shard, (group // data_world + 1) * data_world + data_rank, 0, epoch
+    return shard, group, chunk + 1, epoch
 
 
 def _create_batches(split, resume, tokenizer_batch_size, data_rank, data_world_size, file_paths):
+    """Endless walk over this data rank's row groups (every ``data_world_size``-th
+    group of every shard, starting at ``data_rank``), yielding text chunks of
+    ``tokenizer_batch_size`` documents with their position
+    (shard, row group, epoch, chunk); the next epoch restarts at shard 0."""
     import pyarrow.parquet as pq
 
-    r_pq = resume["pq_idx"] if resume is not None else 0
-    r_rg = resume["rg_idx"] if resume is not None else None
-    r_batch = resume.get("batch_idx") if resume is not None else None
-    epoch = resume.get("epoch", 1) if resume is not None else 1
-    first = True
+    shard, group0, chunk0, epoch = _resume_position(resume, data_rank, data_world_size)
     while True:
-        pq_idx = r_pq if first else 0
-        while pq_idx < len(file_paths):
-            pf = pq.ParquetFile(file_paths[pq_idx])
-            if first and r_rg is not None and pq_idx == r_pq:
-                rg = ((r_rg // data_world_size) + 1) * data_world_size + data_rank if r_batch is None else r_rg
-            else:
-                rg = data_rank
-            while rg < pf.num_row_groups:
-                texts = pf.read_row_group(rg).column("text").to_pylist()
-                start = 0
-                if first and pq_idx == r_pq and rg == r_rg and r_batch is not None:
-                    start = r_batch + 1
-                for bi, i in enumerate(range(0, len(texts), tokenizer_batch_size)):
-                    if bi < start:
-                        continue
-                    yield texts[i:i + tokenizer_batch_size], (pq_idx, rg, epoch, bi)
-                r_rg = None
-                r_batch = None
-                rg += data_world_size
-            pq_idx += 1
-        first = False
-        epoch += 1
+        for s in range(shard, len(file_paths)):
+            reader = pq.ParquetFile(file_paths[s])
+            first_group = group0 if s == shard else data_rank
+            for g in range(first_group, reader.num_row_groups, data_world_size):
+                texts = reader.read_row_group(g).column("text").to_pylist()
+                starts = range(0, len(texts), tokenizer_batch_size)
+                skip = chunk0 if (s == shard and g == first_group) else 0
+                for c in range(skip, len(starts)):
+                    yield texts[starts[c]:starts[c] + tokenizer_batch_size], (s, g, epoch, c)
+        shard, group0, chunk0, epoch = 0, data_rank, 0, epoch + 1
 
 
 class _BestFitBuffer:

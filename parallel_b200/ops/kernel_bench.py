@@ -5,8 +5,10 @@
 Each case runs a few warm-up launches, then times ``--iters`` launches with
 CUDA events on the current stream and prints the time per launch and the
 achieved TF/s or GB/s.  With ``--iters 1`` and ``--warmup 3`` the same command
-is the small case used for ``ncu --set full`` captures (select the kernel with
-``-k`` and skip the warm-up launches with ``-s 3``).
+is the small case used for profiler captures, after the same command has run
+to completion without the profiler:
+``ncu --set full --clock-control none -k <kernel> -s 3 -c 1 python -m parallel_b200.ops.kernel_bench <case>
+--iters 1 --warmup 3`` (``--clock-control none`` leaves the GPU's clocks alone).
 """
 from __future__ import annotations
 

@@ -1,21 +1,36 @@
-"""Training checkpoints: portable full model + exact-topology sharded directories.
+"""Training checkpoints: a portable full model file and exact-topology directories.
 
-File formats are the reference's (parallel/parallel/engine/checkpoint.py:
-21-451), so checkpoints interchange:
+The on-disk formats are an interface shared with the reference
+(``parallel/parallel/engine/checkpoint.py:21-451``), so checkpoints written by
+either implementation load in the other:
 
-* portable: one ``torch.save`` of an OrderedDict of CPU tensors (HF keys,
-  full shapes, tied weights as one shared tensor), written by global rank 0
-  to a temp file then ``os.replace``d;
-* sharded directory (``format_version`` 1, kind ``sharded-training-state``):
-  ``model-tp-XXXXX-dp-shard-XXXXX.pt`` (model-parallel) or
-  ``model-shard-XXXXX.pt`` holding ``{format_version, model, optimizer}``,
-  written only by dp_replicate rank 0; ``rank-state-XXXXX.pt`` per rank
-  (RNG python/numpy/torch/cuda, dataloader states, grad scaler, scheduler);
-  ``manifest.json`` (topology, layout, file lists, resolved config,
-  metadata) and a ``COMPLETE`` marker; the temp directory is renamed into
-  place atomically.  Errors on any rank are gathered over a gloo control
-  group so every rank raises together; loading validates version, kind,
-  topology, layout and file sets.
+* portable model: one ``torch.save`` of an ordered dict of full CPU tensors
+  (HF parameter names; tied weights stay one shared tensor);
+* exact-topology directory, ``format_version`` 1, ``kind``
+  ``"sharded-training-state"``:
+
+  - ``model-tp-TTTTT-dp-shard-SSSSS.pt`` (model parallel) or
+    ``model-shard-SSSSS.pt``: ``{"format_version", "model", "optimizer"}``,
+    written by the dp_replicate-0 copy of each shard only;
+  - ``rank-state-RRRRR.pt`` per rank: ``{"format_version", "rank", "rng",
+    "dataloader", "eval_dataloader", "grad_scaler", "scheduler"}``;
+  - ``manifest.json`` (topology, layout, file lists, resolved config, user
+    metadata) and a ``COMPLETE`` marker.
+
+How it is organised here:
+
+* ``_ControlPlane`` runs every decision that must come out the same on all
+  ranks over a gloo group: an action on the root whose outcome (value or
+  error text) is broadcast, or an action on every rank whose failures are
+  gathered, so a failure anywhere raises on every rank together.
+* ``DirectoryLayout`` is the single place that knows the file names.
+* ``_MANIFEST_SCHEMA`` is a declarative table: saving fills the manifest from
+  the same expectations that loading checks; ``_check_rank_state`` is the
+  table of rank-file checks.
+* RNG capture / restore walks one table of generator sources.
+
+The directory is assembled under a hidden sibling and renamed into place
+only after every file and the marker exist.
 """
 from __future__ import annotations
 
@@ -25,80 +40,212 @@ import os
 import random
 import shutil
 import uuid
-from collections import OrderedDict
+from dataclasses import dataclass
 from pathlib import Path
-from typing import Any, Optional
+from typing import Any, Callable, Optional
 
 import numpy as np
 import torch
 import torch.distributed as dist
+from torch.utils._pytree import tree_map
 
 from ..state import Strategies
 
 CHECKPOINT_FORMAT_VERSION = 1
+CHECKPOINT_KIND = "sharded-training-state"
 
 
-def _cpu_tree(v: Any) -> Any:
-    if isinstance(v, torch.Tensor):
-        return v.detach().to(device="cpu", copy=True)
-    if isinstance(v, OrderedDict):
-        return OrderedDict((k, _cpu_tree(x)) for k, x in v.items())
-    if isinstance(v, dict):
-        return {k: _cpu_tree(x) for k, x in v.items()}
-    if isinstance(v, tuple):
-        return tuple(_cpu_tree(x) for x in v)
-    if isinstance(v, list):
-        return [_cpu_tree(x) for x in v]
-    return copy.deepcopy(v)
+class CheckpointError(RuntimeError):
+    """Raised on every rank when any rank failed a checkpoint phase."""
 
 
-def _jsonable(v: Any) -> Any:
-    if v is None or isinstance(v, (str, int, float, bool)):
-        return v
-    if isinstance(v, Path):
-        return str(v)
-    if isinstance(v, dict):
-        return {str(k): _jsonable(x) for k, x in v.items()}
-    if isinstance(v, (list, tuple)):
-        return [_jsonable(x) for x in v]
-    return repr(v)
+# --------------------------------------------------------------------------- value helpers
+def host_copy(tree: Any) -> Any:
+    """Detached CPU copies of every tensor in a nested container; every other
+    leaf is deep-copied, so the result shares nothing with live state."""
+    return tree_map(lambda leaf: leaf.detach().to("cpu", copy=True) if isinstance(leaf, torch.Tensor)
+                    else copy.deepcopy(leaf), tree)
 
 
+def json_safe(value: Any) -> Any:
+    """Plain JSON data for a config / metadata tree: containers become dicts
+    with string keys and lists, paths become strings, and anything JSON has no
+    type for becomes its ``repr``."""
+    if isinstance(value, dict):
+        return {str(k): json_safe(v) for k, v in value.items()}
+    if isinstance(value, (list, tuple)):
+        return [json_safe(v) for v in value]
+    if isinstance(value, os.PathLike):
+        return os.fspath(value)
+    if value is None or isinstance(value, (bool, int, float, str)):
+        return value
+    return repr(value)
+
+
+# --------------------------------------------------------------------------- RNG sources
+_HOST_RNG_SOURCES: dict[str, tuple[Callable[[], Any], Callable[[Any], None]]] = {
+    "python": (random.getstate, random.setstate),
+    "numpy": (np.random.get_state, np.random.set_state),
+    "torch": (torch.get_rng_state, torch.set_rng_state),
+}
+
+
+def _rng_sources(device: torch.device) -> dict:
+    sources = dict(_HOST_RNG_SOURCES)
+    if device.type == "cuda":
+        sources["cuda"] = (lambda: torch.cuda.get_rng_state(device), lambda s: torch.cuda.set_rng_state(s, device))
+    return sources
+
+
+# --------------------------------------------------------------------------- control plane
+class _ControlPlane:
+    """Host-side agreement between ranks (gloo; a no-op without a process group)."""
+
+    def __init__(self):
+        self.distributed = dist.is_initialized()
+        self.group = dist.new_group(backend="gloo") if self.distributed and dist.is_gloo_available() else None
+        self.rank = dist.get_rank() if self.distributed else 0
+        self.world = dist.get_world_size() if self.distributed else 1
+
+    def on_root(self, phase: str, action: Callable[[], Any]) -> Any:
+        """Run ``action`` on global rank 0 and hand its result to every rank;
+        if it raised, every rank raises ``CheckpointError`` naming ``phase``."""
+        outcome = None
+        if self.rank == 0:
+            try:
+                outcome = ("ok", action())
+            except Exception as exc:  # reported on every rank below
+                outcome = ("error", f"{type(exc).__name__}: {exc}")
+        if self.distributed:
+            box = [outcome]
+            dist.broadcast_object_list(box, src=0, group=self.group)
+            outcome = box[0]
+        status, payload = outcome
+        if status != "ok":
+            raise CheckpointError(f"checkpoint {phase} failed: {payload}")
+        return payload
+
+    def on_every_rank(self, phase: str, action: Callable[[], Any],
+                      cleanup: Optional[Callable[[], None]] = None) -> Any:
+        """Run ``action`` on each rank; if any rank raised, every rank raises a
+        ``CheckpointError`` listing each failing rank (``cleanup`` runs first,
+        on rank 0)."""
+        result, failure = None, None
+        try:
+            result = action()
+        except Exception as exc:
+            failure = f"rank {self.rank}: {type(exc).__name__}: {exc}"
+        failures = [failure]
+        if self.distributed:
+            failures = [None] * self.world
+            dist.all_gather_object(failures, failure, group=self.group)
+        failures = [f for f in failures if f is not None]
+        if failures:
+            if cleanup is not None and self.rank == 0:
+                cleanup()
+            raise CheckpointError(f"checkpoint {phase} failed: " + " | ".join(failures))
+        return result
+
+    def fence(self, device: torch.device) -> None:
+        """Finish this rank's queued device work, then meet every rank.
+
+        Checkpoint phases issue collectives on several disjoint NCCL groups
+        (TP, dp_shard, dp_replicate); draining the device before the next
+        world-level step keeps the launch order of communicators independent
+        of timing."""
+        if not self.distributed:
+            return
+        if device.type == "cuda":
+            torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)
+
+
+# --------------------------------------------------------------------------- directory layout
+@dataclass(frozen=True)
+class DirectoryLayout:
+    """File names of one exact-topology checkpoint directory."""
+
+    world_size: int
+    tp_size: int
+    dp_shard_size: int
+    model_parallel: bool
+
+    def model_file(self, shard_rank: int, tp_rank: int) -> str:
+        if self.model_parallel:
+            return f"model-tp-{tp_rank:05d}-dp-shard-{shard_rank:05d}.pt"
+        return f"model-shard-{shard_rank:05d}.pt"
+
+    def model_files(self) -> list[str]:
+        tp_ranks = range(self.tp_size) if self.model_parallel else range(1)
+        return [self.model_file(s, t) for t in tp_ranks for s in range(self.dp_shard_size)]
+
+    @staticmethod
+    def rank_file(rank: int) -> str:
+        return f"rank-state-{rank:05d}.pt"
+
+    def rank_files(self) -> list[str]:
+        return [self.rank_file(r) for r in range(self.world_size)]
+
+
+# --------------------------------------------------------------------------- schemas
+# (manifest key, how the current job computes it, what a mismatch means).  The
+# same table fills the manifest on save and validates it on load.
+_MANIFEST_SCHEMA: list[tuple[str, Callable[["CheckpointManager"], Any], str]] = [
+    ("format_version", lambda m: CHECKPOINT_FORMAT_VERSION,
+     "checkpoint format_version {saved!r} is not supported (this build reads {current!r})"),
+    ("kind", lambda m: CHECKPOINT_KIND, "checkpoint kind {saved!r} is not {current!r}"),
+    ("topology", lambda m: m.topology(),
+     "checkpoint topology does not match this job: saved {saved}, running {current}"),
+    ("layout", lambda m: m.wrapper.checkpoint_layout(),
+     "checkpoint model layout does not match the model being restored"),
+    ("model_files", lambda m: m.layout().model_files(),
+     "checkpoint manifest lists model files {saved} where this topology expects {current}"),
+    ("rank_files", lambda m: m.layout().rank_files(),
+     "checkpoint manifest lists rank-state files {saved} where this topology expects {current}"),
+]
+
+
+def _check_rank_state(payload: dict, rank: int, device: torch.device, has_scaler: bool,
+                      has_scheduler: bool) -> None:
+    rng = payload.get("rng")
+    problems = [
+        (payload.get("format_version") != CHECKPOINT_FORMAT_VERSION,
+         f"rank-state format_version {payload.get('format_version')!r} is not supported"),
+        (payload.get("rank") != rank, f"rank-state file of rank {payload.get('rank')!r} opened by rank {rank}"),
+        (not isinstance(rng, dict) or not set(_HOST_RNG_SOURCES) <= set(rng),
+         "rank state has incomplete RNG state (python, numpy and torch are required)"),
+        (device.type == "cuda" and isinstance(rng, dict) and "cuda" not in rng,
+         "rank state has incomplete RNG state (no CUDA generator state for a CUDA job)"),
+        (has_scaler != (payload.get("grad_scaler") is not None),
+         "grad scaler present in only one of the checkpoint and this job"),
+        (has_scheduler != (payload.get("scheduler") is not None),
+         "LR scheduler present in only one of the checkpoint and this job"),
+    ]
+    for failed, message in problems:
+        if failed:
+            raise ValueError(message)
+
+
+# --------------------------------------------------------------------------- manager
 class CheckpointManager:
+    """Portable and exact-topology checkpoints of one ``ParallelEngine``."""
+
     def __init__(self, engine):
         self.engine = engine
-        self.control_group = (dist.new_group(backend="gloo")
-                              if dist.is_initialized() and dist.is_gloo_available() else None)
+        self.plane = _ControlPlane()
 
-    # ------------------------------------------------------------------ topology
+    # ------------------------------------------------------------------ job description
     @property
-    def wrapper(self):
-        mp = getattr(self.engine, "mp_wrapper", None)
-        if mp is not None and mp.is_active:
-            return mp
-        return self.engine.fsdp_wrapper
+    def device(self) -> torch.device:
+        return torch.device(self.engine.device)
 
     @property
     def rank(self) -> int:
-        return dist.get_rank() if dist.is_initialized() else 0
+        return self.plane.rank
 
     @property
     def world_size(self) -> int:
-        return dist.get_world_size() if dist.is_initialized() else 1
-
-    def _mesh_rank(self, dim: Strategies) -> int:
-        mesh = self.engine.pconfig.device_mesh
-        if mesh is not None and dim.value in (getattr(mesh, "mesh_dim_names", ()) or ()):
-            return mesh.get_local_rank(dim.value)
-        return 0
-
-    @property
-    def shard_rank(self) -> int:
-        return self._mesh_rank(Strategies.DP_SHARD)
-
-    @property
-    def tp_rank(self) -> int:
-        return self._mesh_rank(Strategies.TP)
+        return self.plane.world
 
     @property
     def model_parallel_active(self) -> bool:
@@ -106,72 +253,39 @@ class CheckpointManager:
         return mp is not None and mp.is_active
 
     @property
-    def is_model_writer(self) -> bool:
-        return self._mesh_rank(Strategies.DP_REPLICATE) == 0
+    def wrapper(self):
+        """The object owning the model's state dicts (model-parallel wrapper if
+        active, else the FSDP wrapper, which is a pass-through without FSDP)."""
+        return self.engine.mp_wrapper if self.model_parallel_active else self.engine.fsdp_wrapper
 
-    def _topology(self) -> dict[str, int]:
+    def coordinate(self, dim: Strategies) -> int:
+        mesh = self.engine.pconfig.device_mesh
+        names = tuple(getattr(mesh, "mesh_dim_names", None) or ()) if mesh is not None else ()
+        return mesh.get_local_rank(dim.value) if dim.value in names else 0
+
+    def topology(self) -> dict[str, int]:
         pc = self.engine.pconfig
-        return {"world_size": self.world_size, "dp_replicate_size": getattr(pc, "dp_replicate_size", 1),
-                "dp_shard_size": getattr(pc, "dp_shard_size", 1), "tp_size": getattr(pc, "tp_size", 1),
-                "sp_size": getattr(pc, "sp_size", 1), "ep_size": getattr(pc, "ep_size", 1),
-                "expert_tp_size": getattr(pc, "expert_tp_size", 1)}
+        sizes = {key: getattr(pc, key, 1) for key in
+                 ("dp_replicate_size", "dp_shard_size", "tp_size", "sp_size", "ep_size", "expert_tp_size")}
+        return {"world_size": self.world_size, **sizes}
 
-    # ------------------------------------------------------------------ control plane
-    def _broadcast_root_object(self, value: Any) -> Any:
-        if not dist.is_initialized():
-            return value
-        payload = [value if self.rank == 0 else None]
-        dist.broadcast_object_list(payload, src=0, group=self.control_group)
-        return payload[0]
+    def layout(self) -> DirectoryLayout:
+        t = self.topology()
+        return DirectoryLayout(self.world_size, t["tp_size"], t["dp_shard_size"], self.model_parallel_active)
 
-    def _collect_errors(self, local: Optional[str]) -> list[str]:
-        if not dist.is_initialized():
-            return [local] if local is not None else []
-        errs: list = [None] * self.world_size
-        dist.all_gather_object(errs, local, group=self.control_group)
-        return [e for e in errs if e is not None]
-
-    def _synchronize_collective_phase(self) -> None:
-        """Drain subgroup device work before the next world-level collective so
-        communicator launch order cannot depend on timing."""
-        if not dist.is_initialized():
-            return
-        dev = torch.device(self.engine.device)
-        if dev.type == "cuda":
-            torch.cuda.synchronize(dev)
-        dist.barrier(group=self.control_group)
-
-    def _resolved_config(self) -> Any:
-        cfg = getattr(self.engine, "cfg", None)
-        if cfg is None:
-            return None
-        if hasattr(cfg, "to_container"):
-            return _jsonable(cfg.to_container())
-        return _jsonable(cfg)
-
-    def _rng_state(self) -> dict:
-        st = {"python": random.getstate(), "numpy": np.random.get_state(), "torch": torch.get_rng_state()}
-        if torch.device(self.engine.device).type == "cuda":
-            st["cuda"] = torch.cuda.get_rng_state(self.engine.device)
-        return st
-
-    def _restore_rng_state(self, st: dict) -> None:
-        random.setstate(st["python"])
-        np.random.set_state(st["numpy"])
-        torch.set_rng_state(st["torch"])
-        if "cuda" in st:
-            torch.cuda.set_rng_state(st["cuda"], self.engine.device)
+    def _my_model_file(self) -> str:
+        return self.layout().model_file(self.coordinate(Strategies.DP_SHARD), self.coordinate(Strategies.TP))
 
     # ------------------------------------------------------------------ state dicts
     def full_state_dict(self):
-        st = self.wrapper.full_state_dict()
-        self._synchronize_collective_phase()
-        return st
+        state = self.wrapper.full_state_dict()
+        self.plane.fence(self.device)
+        return state
 
     def load_full_state_dict(self, state_dict, strict: bool = True):
-        res = self.wrapper.load_full_state_dict(state_dict, strict=strict)
-        self._synchronize_collective_phase()
-        return res
+        result = self.wrapper.load_full_state_dict(state_dict, strict=strict)
+        self.plane.fence(self.device)
+        return result
 
     def sharded_state_dict(self) -> dict:
         return self.wrapper.sharded_state_dict()
@@ -179,189 +293,132 @@ class CheckpointManager:
     def load_sharded_state_dict(self, state_dict, strict: bool = True):
         return self.wrapper.load_sharded_state_dict(state_dict, strict=strict)
 
-    # ------------------------------------------------------------------ portable model
+    # ------------------------------------------------------------------ portable file
     def save_full_model(self, path) -> None:
-        """Portable CPU state dict (every rank must call)."""
-        path = Path(path)
+        """Write the portable full model (collective: every rank calls it)."""
+        target = Path(path)
         state = self.full_state_dict()
-        res = None
-        if self.rank == 0:
-            tmp = path.with_name(f".{path.name}.tmp-{uuid.uuid4().hex}")
+
+        def write():
+            if target.exists():
+                raise FileExistsError(f"Checkpoint already exists: {target}")
+            target.parent.mkdir(parents=True, exist_ok=True)
+            partial = target.with_name(f".{target.name}.partial-{uuid.uuid4().hex}")
             try:
-                if path.exists():
-                    raise FileExistsError(f"Checkpoint already exists: {path}")
-                path.parent.mkdir(parents=True, exist_ok=True)
-                torch.save(state, tmp)
-                os.replace(tmp, path)
-                res = {"error": None}
-            except Exception as e:
-                if tmp.exists():
-                    tmp.unlink()
-                res = {"error": f"{type(e).__name__}: {e}"}
-        res = self._broadcast_root_object(res)
-        if res["error"] is not None:
-            raise RuntimeError(f"Failed to save full model: {res['error']}")
+                torch.save(state, partial)
+                os.replace(partial, target)
+            finally:
+                partial.unlink(missing_ok=True)
+
+        self.plane.on_root("full-model save", write)
 
     def load_full_model(self, path, strict: bool = True):
-        state, res = None, None
-        if self.rank == 0:
-            try:
-                state = torch.load(Path(path), map_location="cpu", weights_only=False)
-                res = {"error": None}
-            except Exception as e:
-                res = {"error": f"{type(e).__name__}: {e}"}
-        res = self._broadcast_root_object(res)
-        if res["error"] is not None:
-            raise RuntimeError(f"Failed to load full model: {res['error']}")
-        return self.load_full_state_dict(state, strict=strict)
+        """Read the portable file on rank 0 and distribute it through the
+        wrapper's ``load_full_state_dict`` (collective)."""
+        holder = {}
 
-    # ------------------------------------------------------------------ sharded directory
-    def _prepare_checkpoint_directory(self, path: Path) -> Path:
-        res = None
-        if self.rank == 0:
-            try:
-                if path.exists():
-                    raise FileExistsError(f"Checkpoint already exists: {path}")
-                path.parent.mkdir(parents=True, exist_ok=True)
-                tmp = path.with_name(f".{path.name}.tmp-{uuid.uuid4().hex}")
-                tmp.mkdir()
-                res = {"path": str(tmp), "error": None}
-            except Exception as e:
-                res = {"path": None, "error": f"{type(e).__name__}: {e}"}
-        res = self._broadcast_root_object(res)
-        if res["error"] is not None:
-            raise RuntimeError(f"Failed to initialize checkpoint: {res['error']}")
-        return Path(res["path"])
+        def read():
+            holder["state"] = torch.load(Path(path), map_location="cpu", weights_only=False)
 
-    def _model_file_name(self, shard_rank: int, tp_rank: int | None = None) -> str:
-        if self.model_parallel_active:
-            tp_rank = self.tp_rank if tp_rank is None else tp_rank
-            return f"model-tp-{tp_rank:05d}-dp-shard-{shard_rank:05d}.pt"
-        return f"model-shard-{shard_rank:05d}.pt"
+        self.plane.on_root("full-model load", read)
+        return self.load_full_state_dict(holder.get("state"), strict=strict)
 
-    def _model_file_names(self) -> list[str]:
-        t = self._topology()
-        if self.model_parallel_active:
-            return [self._model_file_name(s, r) for r in range(t["tp_size"]) for s in range(t["dp_shard_size"])]
-        return [self._model_file_name(s) for s in range(t["dp_shard_size"])]
+    # ------------------------------------------------------------------ exact-topology directory
+    def _engine_extras(self) -> tuple[Any, Any]:
+        return getattr(self.engine, "grad_scaler", None), getattr(self.engine, "scheduler", None)
 
-    def _rank_file_name(self, rank: int) -> str:
-        return f"rank-state-{rank:05d}.pt"
+    def _resolved_config(self) -> Any:
+        cfg = getattr(self.engine, "cfg", None)
+        if cfg is None:
+            return None
+        return json_safe(cfg.to_container() if hasattr(cfg, "to_container") else cfg)
+
+    def _write_my_files(self, staging: Path, dataloader_state, eval_dataloader_state) -> None:
+        if self.coordinate(Strategies.DP_REPLICATE) == 0:  # one copy of each shard
+            torch.save({"format_version": CHECKPOINT_FORMAT_VERSION,
+                        "model": self.sharded_state_dict(),
+                        "optimizer": host_copy(self.engine.optimizer.state_dict())},
+                       staging / self._my_model_file())
+        scaler, scheduler = self._engine_extras()
+        torch.save({"format_version": CHECKPOINT_FORMAT_VERSION,
+                    "rank": self.rank,
+                    "rng": {name: get() for name, (get, _) in _rng_sources(self.device).items()},
+                    "dataloader": copy.deepcopy(dataloader_state),
+                    "eval_dataloader": copy.deepcopy(eval_dataloader_state),
+                    "grad_scaler": None if scaler is None else scaler.state_dict(),
+                    "scheduler": None if scheduler is None else scheduler.state_dict()},
+                   staging / DirectoryLayout.rank_file(self.rank))
 
     def save(self, path, *, step: int, dataloader_state=None, eval_dataloader_state=None, metadata=None) -> None:
-        """Atomically save an exact-resume, same-topology sharded checkpoint."""
-        self._synchronize_collective_phase()
-        path = Path(path)
-        tmp = self._prepare_checkpoint_directory(path)
-        local_error = None
-        try:
-            if self.is_model_writer:
-                payload = {"format_version": CHECKPOINT_FORMAT_VERSION, "model": self.sharded_state_dict(),
-                           "optimizer": _cpu_tree(self.engine.optimizer.state_dict())}
-                torch.save(payload, tmp / self._model_file_name(self.shard_rank, self.tp_rank))
-            scaler = getattr(self.engine, "grad_scaler", None)
-            scheduler = getattr(self.engine, "scheduler", None)
-            rank_payload = {
-                "format_version": CHECKPOINT_FORMAT_VERSION, "rank": self.rank, "rng": self._rng_state(),
-                "dataloader": copy.deepcopy(dataloader_state), "eval_dataloader": copy.deepcopy(eval_dataloader_state),
-                "grad_scaler": scaler.state_dict() if scaler is not None else None,
-                "scheduler": scheduler.state_dict() if scheduler is not None else None,
-            }
-            torch.save(rank_payload, tmp / self._rank_file_name(self.rank))
-        except Exception as e:
-            local_error = f"rank {self.rank}: {type(e).__name__}: {e}"
-        errors = self._collect_errors(local_error)
-        if errors:
-            if self.rank == 0:
-                shutil.rmtree(tmp, ignore_errors=True)
-            raise RuntimeError("Failed to write checkpoint: " + " | ".join(errors))
-        res = None
-        if self.rank == 0:
-            try:
-                manifest = {
-                    "format_version": CHECKPOINT_FORMAT_VERSION, "kind": "sharded-training-state", "step": int(step),
-                    "topology": self._topology(), "layout": self.wrapper.checkpoint_layout(),
-                    "model_files": self._model_file_names(),
-                    "rank_files": [self._rank_file_name(r) for r in range(self.world_size)],
-                    "config": self._resolved_config(), "metadata": _jsonable(metadata or {}),
-                }
-                (tmp / "manifest.json").write_text(json.dumps(manifest, indent=2, sort_keys=True) + "\n",
-                                                   encoding="utf-8")
-                (tmp / "COMPLETE").write_text("complete\n", encoding="utf-8")
-                os.replace(tmp, path)
-                res = {"error": None}
-            except Exception as e:
-                shutil.rmtree(tmp, ignore_errors=True)
-                res = {"error": f"{type(e).__name__}: {e}"}
-        res = self._broadcast_root_object(res)
-        if res["error"] is not None:
-            raise RuntimeError(f"Failed to finalize checkpoint: {res['error']}")
+        """Write an exact-resume checkpoint of this topology (collective)."""
+        self.plane.fence(self.device)
+        target = Path(path)
 
-    def _read_manifest(self, path: Path) -> dict:
-        res = None
-        if self.rank == 0:
+        def make_staging():
+            if target.exists():
+                raise FileExistsError(f"Checkpoint already exists: {target}")
+            target.parent.mkdir(parents=True, exist_ok=True)
+            staging = target.with_name(f".{target.name}.partial-{uuid.uuid4().hex}")
+            staging.mkdir()
+            return str(staging)
+
+        staging = Path(self.plane.on_root("directory setup", make_staging))
+        discard = lambda: shutil.rmtree(staging, ignore_errors=True)  # noqa: E731
+        self.plane.on_every_rank(
+            "write", lambda: self._write_my_files(staging, dataloader_state, eval_dataloader_state), cleanup=discard)
+
+        def publish():
+            manifest = {key: compute(self) for key, compute, _ in _MANIFEST_SCHEMA}
+            manifest.update(step=int(step), config=self._resolved_config(), metadata=json_safe(metadata or {}))
             try:
-                if not (path / "COMPLETE").is_file():
-                    raise RuntimeError("Checkpoint has no COMPLETE marker")
-                res = {"manifest": json.loads((path / "manifest.json").read_text(encoding="utf-8")), "error": None}
-            except Exception as e:
-                res = {"manifest": None, "error": f"{type(e).__name__}: {e}"}
-        res = self._broadcast_root_object(res)
-        if res["error"] is not None:
-            raise RuntimeError(f"Failed to read checkpoint: {res['error']}")
-        return res["manifest"]
+                (staging / "manifest.json").write_text(json.dumps(manifest, indent=2, sort_keys=True) + "\n",
+                                                       encoding="utf-8")
+                (staging / "COMPLETE").write_text("complete\n", encoding="utf-8")
+                os.replace(staging, target)
+            except BaseException:
+                discard()
+                raise
+
+        self.plane.on_root("publish", publish)
+
+    def _read_manifest(self, root: Path) -> dict:
+        def read():
+            if not (root / "COMPLETE").is_file():
+                raise FileNotFoundError(f"{root} has no COMPLETE marker (an interrupted or foreign write)")
+            return json.loads((root / "manifest.json").read_text(encoding="utf-8"))
+
+        return self.plane.on_root("manifest read", read)
 
     def load(self, path, *, strict: bool = True) -> dict:
-        """Restore model, optimizer, scaler, scheduler, RNG and data position."""
-        path = Path(path)
-        manifest = self._read_manifest(path)
-        if manifest.get("format_version") != CHECKPOINT_FORMAT_VERSION:
-            raise RuntimeError(f"Unsupported checkpoint version: {manifest.get('format_version')}")
-        if manifest.get("kind") != "sharded-training-state":
-            raise RuntimeError(f"Unsupported checkpoint kind: {manifest.get('kind')}")
-        if manifest.get("topology") != self._topology():
-            raise RuntimeError("Checkpoint topology does not match the current distributed topology: "
-                               f"saved={manifest.get('topology')}, current={self._topology()}")
-        if manifest.get("layout") != self.wrapper.checkpoint_layout():
-            raise RuntimeError("Checkpoint model layout does not match the current model")
-        if manifest.get("model_files") != self._model_file_names():
-            raise RuntimeError("Checkpoint manifest has an invalid model file set")
-        if manifest.get("rank_files") != [self._rank_file_name(r) for r in range(self.world_size)]:
-            raise RuntimeError("Checkpoint manifest has an invalid rank-state file set")
-        local_error, rank_payload = None, None
-        try:
-            mp = torch.load(path / self._model_file_name(self.shard_rank, self.tp_rank), map_location="cpu",
-                            weights_only=False)
-            if mp.get("format_version") != CHECKPOINT_FORMAT_VERSION:
-                raise RuntimeError("Model shard has an unsupported format version")
-            rank_payload = torch.load(path / self._rank_file_name(self.rank), map_location="cpu", weights_only=False)
-            if rank_payload.get("format_version") != CHECKPOINT_FORMAT_VERSION:
-                raise RuntimeError("Rank state has an unsupported format version")
-            if rank_payload.get("rank") != self.rank:
-                raise RuntimeError(f"Loaded rank state for {rank_payload.get('rank')} on rank {self.rank}")
-            rng = rank_payload.get("rng")
-            if not isinstance(rng, dict) or not {"python", "numpy", "torch"}.issubset(rng):
-                raise RuntimeError("Rank state has incomplete RNG state")
-            if torch.device(self.engine.device).type == "cuda" and "cuda" not in rng:
-                raise RuntimeError("Rank state has no CUDA RNG state")
-            scaler = getattr(self.engine, "grad_scaler", None)
-            scheduler = getattr(self.engine, "scheduler", None)
-            if (scaler is None) != (rank_payload.get("grad_scaler") is None):
-                raise RuntimeError("Checkpoint grad-scaler configuration does not match")
-            if (scheduler is None) != (rank_payload.get("scheduler") is None):
-                raise RuntimeError("Checkpoint scheduler configuration does not match")
-            self.load_sharded_state_dict(mp["model"], strict=strict)
-            self.engine.optimizer.load_state_dict(mp["optimizer"])
+        """Restore model, optimizer, scaler, scheduler, RNG and data position
+        from a checkpoint of the same topology (collective)."""
+        root = Path(path)
+        manifest = self._read_manifest(root)
+        for key, compute, problem in _MANIFEST_SCHEMA:  # identical on every rank
+            current = compute(self)
+            if manifest.get(key) != current:
+                raise CheckpointError(problem.format(saved=manifest.get(key), current=current))
+        scaler, scheduler = self._engine_extras()
+
+        def restore():
+            shard = torch.load(root / self._my_model_file(), map_location="cpu", weights_only=False)
+            if shard.get("format_version") != CHECKPOINT_FORMAT_VERSION:
+                raise ValueError(f"model shard format_version {shard.get('format_version')!r} is not supported")
+            state = torch.load(root / DirectoryLayout.rank_file(self.rank), map_location="cpu", weights_only=False)
+            _check_rank_state(state, self.rank, self.device, scaler is not None, scheduler is not None)
+            self.load_sharded_state_dict(shard["model"], strict=strict)
+            self.engine.optimizer.load_state_dict(shard["optimizer"])
             if scaler is not None:
-                scaler.load_state_dict(rank_payload["grad_scaler"])
+                scaler.load_state_dict(state["grad_scaler"])
             if scheduler is not None:
-                scheduler.load_state_dict(rank_payload["scheduler"])
-        except Exception as e:
-            local_error = f"rank {self.rank}: {type(e).__name__}: {e}"
-        errors = self._collect_errors(local_error)
-        if errors:
-            raise RuntimeError("Failed to load checkpoint: " + " | ".join(errors))
-        self._restore_rng_state(rank_payload["rng"])
-        return {"step": manifest["step"], "dataloader_state": rank_payload.get("dataloader"),
-                "eval_dataloader_state": rank_payload.get("eval_dataloader"),
+                scheduler.load_state_dict(state["scheduler"])
+            return state
+
+        state = self.plane.on_every_rank("load", restore)
+        # generators last, so nothing above consumes the restored streams
+        for name, (_, put) in _rng_sources(self.device).items():
+            if name in state["rng"]:
+                put(state["rng"][name])
+        return {"step": manifest["step"], "dataloader_state": state.get("dataloader"),
+                "eval_dataloader_state": state.get("eval_dataloader"),
                 "metadata": manifest.get("metadata", {}), "config": manifest.get("config")}

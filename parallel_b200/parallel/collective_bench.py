@@ -14,8 +14,11 @@ Cases (bf16 N(0,1) inputs from a fixed seed):
   symmetric buffer, then each owner pulls and sums its rows);
 * ``fsdp_ag`` / ``fsdp_rs``  flat-buffer all-gather / reduce-scatter (peer gather / N-peer
   reduce kernels vs NCCL);
-* ``ep``  expert dispatch + combine of top-8 routes over 128 experts (peer row kernels
-  vs NCCL variable all-to-all);
+* ``ep``  one MoE layer forward + backward, top-8 routes over 128 experts: the
+  device-resident peer-memory path (routing plan, dispatch into the owners' padded
+  expert matrices, grouped tcgen05 GEMMs, weighted pull-combine) vs NCCL variable
+  all-to-alls with host-read splits around ``torch._grouped_mm``; uniform and skewed
+  routing;
 * ``ce``  vocabulary-parallel LM head + cross-entropy (peer log-sum-exp merge vs NCCL
   all-reduces).
 
@@ -157,28 +160,64 @@ def case_fsdp_rs(W, rank, dev, nbytes, warmup, iters):
     return _report("fsdp_rs", [n * 2 // (1 << 20), "MB"], t_ours, t_base, 0, (W - 1) * shard * 2)
 
 
-def case_ep(W, rank, dev, tokens, hidden, experts, top_k, warmup, iters):
+def _torch_experts(x, idx, w, w_gu, w_d):
+    """Reference-style expert MLPs of locally received routes: sort by expert,
+    torch grouped GEMMs (``torch._grouped_mm``, the op HF's grouped expert path
+    calls), SwiGLU, routing-weight scaling, unsort."""
+    import torch.nn.functional as F
+
+    flat = idx.reshape(-1)
+    order = torch.argsort(flat, stable=True)
+    counts = torch.bincount(flat, minlength=w_gu.shape[0])
+    offs = torch.cumsum(counts, 0).to(torch.int32)
+    xs = x.index_select(0, order)
+    gu = torch._grouped_mm(xs, w_gu.transpose(1, 2), offs=offs)
+    g, u = gu.chunk(2, dim=-1)
+    y = torch._grouped_mm((F.silu(g) * u).contiguous(), w_d.transpose(1, 2), offs=offs)
+    y = y * w.reshape(-1)[order, None].to(y.dtype)
+    return torch.empty_like(y).index_copy_(0, order, y)
+
+
+def case_ep(W, rank, dev, tokens, hidden, experts, top_k, warmup, iters, inter=768, skew=0.0):
+    """One MoE layer forward + backward: route exchange, expert MLPs, combine.
+    Ours: the device-resident peer-memory path (``PeerExpertTransport``);
+    baseline: NCCL variable all-to-alls with host-read splits around torch
+    grouped GEMMs (the reference's composition)."""
+    from ..ops.moe import routed_experts
     from .model_parallel.expert_parallel import ExpertPartition
-    from .model_parallel.p2p_dispatch import P2PTokenDispatcher
+    from .model_parallel.p2p_dispatch import PeerExpertTransport
     from .model_parallel.token_dispatch import TokenDispatcher
 
     g = torch.Generator(device="cpu").manual_seed(rank)
-    x = torch.randn(tokens, hidden, generator=g).to(dev, torch.bfloat16)
-    idx = torch.stack([torch.randperm(experts, generator=g)[:top_k] for _ in range(tokens)]).to(dev)
-    sc = torch.rand(tokens, top_k, generator=g).to(dev)
+    x = torch.randn(tokens, hidden, generator=g).to(dev, torch.bfloat16).requires_grad_(True)
+    bias = torch.randn(experts, generator=torch.Generator().manual_seed(7)) * skew
+    logits = torch.randn(tokens, experts, generator=g) + bias
+    sc, idx = torch.softmax(logits, -1).topk(top_k, -1)
+    sc, idx = sc.to(dev).requires_grad_(True), idx.to(dev)
     part = ExpertPartition(experts, W, rank)
-    p2p = P2PTokenDispatcher(part, dist.group.WORLD, dev)
+    wg = torch.Generator().manual_seed(100 + rank)
+    w_gu = (torch.randn(part.local_count, 2 * inter, hidden, generator=wg) * 0.02).to(dev, torch.bfloat16)
+    w_d = (torch.randn(part.local_count, hidden, inter, generator=wg) * 0.02).to(dev, torch.bfloat16)
+    w_gu.requires_grad_(True)
+    w_d.requires_grad_(True)
+    transport = PeerExpertTransport(part, dist.group.WORLD, dev)
     nccl = TokenDispatcher(part, dist.group.WORLD)
+    dout = torch.randn(tokens, hidden, generator=g).to(dev, torch.bfloat16)
 
-    def run(d):
-        h, _, _, st = d.dispatch(x, idx, sc)
-        d.combine(h, st)
+    def ours():
+        routed_experts(x, sc, idx, w_gu, w_d, transport).backward(dout)
 
-    t_ours = _time(lambda: run(p2p), warmup, iters)
-    t_base = _time(lambda: run(nccl), warmup, iters)
-    # each route's row crosses the link to its owner and back (uniform routing)
-    link = 2 * tokens * top_k * hidden * 2 * (W - 1) / W
-    return _report("ep_dispatch_combine", [tokens, hidden, experts, top_k], t_ours, t_base, 0, link)
+    def base():
+        h, e, s, st = nccl.dispatch(x, idx, sc)
+        nccl.combine(_torch_experts(h, e, s, w_gu, w_d), st).backward(dout)
+
+    t_ours = _time(ours, warmup, iters)
+    t_base = _time(base, warmup, iters)
+    # each route's row crosses the link to its owner and back, forward and backward
+    link = 4 * tokens * top_k * hidden * 2 * (W - 1) / W
+    flops = 3 * 2 * tokens * top_k * hidden * 3 * inter  # three products, forward + two backward
+    return _report("ep_moe_layer" + ("_skew" if skew else ""), [tokens, hidden, experts, top_k], t_ours, t_base,
+                   flops, link)
 
 
 def case_ce(W, rank, dev, tokens, hidden, vocab, warmup, iters):
@@ -224,8 +263,11 @@ def main(argv=None):
         if "fsdp_rs" in cases:
             results.append(case_fsdp_rs(W, rank, dev, nb, args.warmup, args.iters))
     if "ep" in cases:
-        for tokens in ([8192] if args.quick else [8192, 32768]):
-            results.append(case_ep(W, rank, dev, tokens, 2048, 128, 8, args.warmup, args.iters))
+        # tokens per rank (Qwen3-30B-A3B at B=1, S=4096 under sp=4 has 1024), hidden 2048, top-8 of 128
+        # experts, expert SwiGLU width 768; uniform routing and an N(0, 2)-biased (skewed) router
+        for tokens in ([1024] if args.quick else [1024, 4096]):
+            for skew in (0.0, 2.0):
+                results.append(case_ep(W, rank, dev, tokens, 2048, 128, 8, args.warmup, args.iters, skew=skew))
     if "ce" in cases:
         results.append(case_ce(W, rank, dev, 16384 if not args.quick else 8192, 1024, 151936, args.warmup,
                                args.iters))

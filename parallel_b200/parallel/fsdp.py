@@ -26,18 +26,16 @@ Execution model (B200-first):
 """
 from __future__ import annotations
 
-import copy
 import os
-from collections import OrderedDict
 from typing import Any, Optional
 
 import torch
 import torch.distributed as dist
 import torch.nn as nn
-from torch.distributed.tensor import DTensor
 
 from ..state import Strategies
 from .comm.unit_collectives import make_unit_collectives
+from .fsdp_state import FSDPStateMixin
 from .fsdp_utils import get_fsdp_units, group_named_parameters, local_tensor
 from .param_unit import DPParamUnit
 
@@ -126,7 +124,7 @@ class _UnitFn(torch.autograd.Function):
         return (None, None, None, None, grads[0]) + (None,) * len(ctx.args)
 
 
-class FSDPWrapper:
+class FSDPWrapper(FSDPStateMixin):
     """FSDP over ``model.model.layers`` plus a root unit (see module docstring)."""
 
     def __init__(self, model: nn.Module, pconfig, cpu_offload: bool = False, activation_checkpoint: bool = False,
@@ -155,31 +153,16 @@ class FSDPWrapper:
         self._backward_prepared = False
         self._done_units: set[int] = set()
         self._deferred: dict[int, list] = {}
-        self._state_dict_keys: tuple[str, ...] = ()
-        self._parameter_state_names: dict[int, tuple[str, ...]] = {}
-        self._parameter_state_keys: set[str] = set()
+        self.state_keys: tuple[str, ...] = ()
+        self.state_names: dict[int, tuple[str, ...]] = {}
+        self.param_keys: set[str] = set()
         self._orig_forwards: dict[int, Any] = {}
         self._root_hook = None
         self.coll = None
 
-    # ------------------------------------------------------------------ layout
-    def _capture_state_dict_layout(self) -> None:
-        state = self.model.state_dict(keep_vars=True)
-        ids = {id(p) for p in self.model.parameters()}
-        names: dict[int, list[str]] = {i: [] for i in ids}
-        for name, value in state.items():
-            if id(value) in names:
-                names[id(value)].append(name)
-        missing = [n for n, p in self.model.named_parameters() if not names[id(p)]]
-        if missing:
-            raise RuntimeError(f"Every model parameter must be represented in model.state_dict(); missing: {missing}")
-        self._state_dict_keys = tuple(state.keys())
-        self._parameter_state_names = {i: tuple(v) for i, v in names.items()}
-        self._parameter_state_keys = {n for v in self._parameter_state_names.values() for n in v}
-
     # ------------------------------------------------------------------ sharding
     def shard_model(self):
-        self._capture_state_dict_layout()
+        self._index_state()
         if self.pconfig.dp_shard_size <= 1 or self.pconfig.device_mesh is None:
             return
         if self.units:
@@ -195,7 +178,7 @@ class FSDPWrapper:
         specs = []
         owned: set[int] = set()
         for i, sub in enumerate(layers):
-            named = [(self._parameter_state_names[id(p)][0], p) for _, p in sub.named_parameters()]
+            named = [(self.state_names[id(p)][0], p) for _, p in sub.named_parameters()]
             if owned.intersection(id(p) for _, p in named):
                 raise ValueError("A parameter is shared by multiple FSDP units")
             if not named:
@@ -206,7 +189,7 @@ class FSDPWrapper:
                 specs.append((sub, group, ckpt and gi == 0, sub is not self.model, gi == 0))
         root_specs = []
         if layers != [self.model]:
-            root = [(self._parameter_state_names[id(p)][0], p) for _, p in self.model.named_parameters()
+            root = [(self.state_names[id(p)][0], p) for _, p in self.model.named_parameters()
                     if id(p) not in owned]
             if root:
                 root_specs = [(self.model, g, False, False, False) for g in group_named_parameters(root)]
@@ -458,285 +441,6 @@ class FSDPWrapper:
                 g = local_tensor(p.grad)
                 g.mul_(coef.to(g.device, g.dtype))
         return total
-
-    # ------------------------------------------------------------------ state dicts
-    @staticmethod
-    def _cpu_copy(v: Any) -> Any:
-        if isinstance(v, DTensor):
-            return v._local_tensor.detach().to(device="cpu", copy=True)
-        if isinstance(v, torch.Tensor):
-            return v.detach().to(device="cpu", copy=True)
-        return copy.deepcopy(v)
-
-    def _replicate_rank(self) -> int:
-        mesh = self.pconfig.device_mesh
-        if mesh is not None and Strategies.DP_REPLICATE.value in (mesh.mesh_dim_names or ()):
-            return mesh.get_local_rank(Strategies.DP_REPLICATE.value)
-        return 0
-
-    def _is_checkpoint_replica(self) -> bool:
-        return self._replicate_rank() == 0
-
-    def _full_state_root(self) -> bool:
-        if not self._is_checkpoint_replica():
-            return False
-        if self.is_active:
-            return dist.get_rank(self.dp_shard_group) == 0
-        return not dist.is_initialized() or dist.get_rank() == 0
-
-    def _non_parameter_state_dict(self) -> OrderedDict:
-        cur = self.model.state_dict(keep_vars=True)
-        out = OrderedDict((n, self._cpu_copy(v)) for n, v in cur.items() if n not in self._parameter_state_keys)
-        if hasattr(cur, "_metadata"):
-            out._metadata = copy.deepcopy(cur._metadata)
-        return out
-
-    def _copy_non_parameter_state(self, sd) -> None:
-        cur = self.model.state_dict(keep_vars=True)
-        for name, dst in cur.items():
-            if name in self._parameter_state_keys or name not in sd:
-                continue
-            if isinstance(dst, torch.Tensor):
-                dst.detach().copy_(sd[name])
-
-    def _sync_tensor(self, t: torch.Tensor, group) -> None:
-        src = dist.get_global_rank(group, 0)
-        v = local_tensor(t).detach()
-        if v.device.type == self.device.type:
-            dist.broadcast(v, src=src, group=group)
-            return
-        staged = v.to(self.device)
-        dist.broadcast(staged, src=src, group=group)
-        v.copy_(staged.to(v.device))
-
-    def _sync_replicated_state(self) -> None:
-        group = self.pconfig.group(Strategies.DP_REPLICATE)
-        if group is None:
-            return
-        tensors = list(self.model.buffers())
-        tensors += self.get_sharded_params() if self.is_active else list(self.model.parameters())
-        for t in tensors:
-            self._sync_tensor(t, group)
-
-    def full_state_dict(self) -> Optional[OrderedDict]:
-        """Full CPU state dict on the shard-group root (one unit gathered at a time)."""
-        if not self._state_dict_keys:
-            self._capture_state_dict_layout()
-        if not self._is_checkpoint_replica():
-            return None
-        if not self.is_active:
-            if not self._full_state_root():
-                return None
-            ms = self.model.state_dict(keep_vars=True)
-            out = OrderedDict((n, self._cpu_copy(v)) for n, v in ms.items())
-            if hasattr(ms, "_metadata"):
-                out._metadata = copy.deepcopy(ms._metadata)
-            return out
-        root = self._full_state_root()
-        values: dict[str, torch.Tensor] = {}
-        for u in self.units:
-            was = u.gathered
-            u.all_gather()
-            try:
-                if root:
-                    for m in u.param_metas:
-                        cpu = self._cpu_copy(m.parameter)
-                        for n in self._parameter_state_names[id(m.parameter)]:
-                            values[n] = cpu
-            finally:
-                if not was:
-                    u.free_full_params()
-        if not root:
-            return None
-        nps = self._non_parameter_state_dict()
-        out = OrderedDict((n, values[n] if n in values else nps[n]) for n in self._state_dict_keys)
-        if hasattr(nps, "_metadata"):
-            out._metadata = copy.deepcopy(nps._metadata)
-        return out
-
-    def _validate_full_state_dict(self, sd, strict: bool) -> dict:
-        expected = set(self._state_dict_keys)
-        actual = set(sd.keys())
-        missing = [n for n in self._state_dict_keys if n not in actual]
-        unexpected = [n for n in sd if n not in expected]
-        shapes: dict[str, torch.Size] = {}
-        for u in self.units:
-            for m in u.param_metas:
-                for n in self._parameter_state_names[id(m.parameter)]:
-                    shapes[n] = m.shape
-        for n, v in self.model.state_dict(keep_vars=True).items():
-            if isinstance(v, torch.Tensor) and n not in shapes:
-                shapes[n] = v.shape
-        errors = []
-        if strict and missing:
-            errors.append(f"Missing key(s): {missing}")
-        if strict and unexpected:
-            errors.append(f"Unexpected key(s): {unexpected}")
-        for n in expected & actual:
-            v = sd[n]
-            if n in shapes:
-                if not isinstance(v, torch.Tensor):
-                    errors.append(f"Expected tensor for {n}, got {type(v).__name__}")
-                elif v.shape != shapes[n]:
-                    errors.append(f"Shape mismatch for {n}: expected {tuple(shapes[n])}, got {tuple(v.shape)}")
-        return {"error": "; ".join(errors) if errors else None, "missing": missing, "unexpected": unexpected}
-
-    def _load_units_from(self, sd, is_group_root: bool, group_root: int) -> None:
-        for u in self.units:
-            was = u.gathered
-            u.all_gather()
-            try:
-                if is_group_root:
-                    by_name = {n: m for m in u.param_metas for n in self._parameter_state_names[id(m.parameter)]}
-                    for n in self._state_dict_keys:
-                        if n in by_name and n in sd:
-                            by_name[n].parameter.detach().copy_(sd[n])
-                dist.broadcast(u.full_buffer, src=group_root, group=self.dp_shard_group)
-                u.writeback_shards()
-            finally:
-                if not was:
-                    u.free_full_params()
-
-    def load_full_state_dict(self, state_dict, strict: bool = True):
-        if not self._state_dict_keys:
-            self._capture_state_dict_layout()
-        root = not dist.is_initialized() or dist.get_rank() == 0
-        if root:
-            validation = ({"error": "Global rank zero requires a full state dict", "missing": [], "unexpected": []}
-                          if state_dict is None else self._validate_full_state_dict(state_dict, strict))
-        else:
-            validation = None
-        if dist.is_initialized():
-            payload = [validation]
-            dist.broadcast_object_list(payload, src=0)
-            validation = payload[0]
-        if validation["error"] is not None:
-            raise RuntimeError(f"Error(s) in loading state_dict: {validation['error']}")
-        if self._is_checkpoint_replica():
-            if not self.is_active:
-                if self._full_state_root():
-                    self.model.load_state_dict(state_dict, strict=strict)
-            else:
-                gr = dist.get_global_rank(self.dp_shard_group, 0)
-                is_root = self._full_state_root()
-                self._load_units_from(state_dict, is_root, gr)
-                if is_root:
-                    self._copy_non_parameter_state(state_dict)
-                for b in self.model.buffers():
-                    self._sync_tensor(b, self.dp_shard_group)
-        self._sync_replicated_state()
-        return nn.modules.module._IncompatibleKeys(validation["missing"], validation["unexpected"])
-
-    def load_local_full_state_dict(self, state_dict, strict: bool = True):
-        """Load one full model-parallel-local state dict through the shard group."""
-        if not self.is_active:
-            return self.load_full_state_dict(state_dict, strict=strict)
-        if not self._state_dict_keys:
-            self._capture_state_dict_layout()
-        gr = dist.get_global_rank(self.dp_shard_group, 0)
-        is_root = dist.get_rank(self.dp_shard_group) == 0
-        if self._is_checkpoint_replica():
-            validation = self._validate_full_state_dict(state_dict, strict) if is_root else None
-            payload = [validation]
-            dist.broadcast_object_list(payload, src=gr, group=self.dp_shard_group)
-            validation = payload[0]
-            if validation["error"] is not None:
-                raise RuntimeError(f"Error(s) in loading local state_dict: {validation['error']}")
-            self._load_units_from(state_dict, is_root, gr)
-            if is_root:
-                self._copy_non_parameter_state(state_dict)
-            for b in self.model.buffers():
-                self._sync_tensor(b, self.dp_shard_group)
-        else:
-            validation = {"missing": [], "unexpected": []}
-        self._sync_replicated_state()
-        return nn.modules.module._IncompatibleKeys(validation["missing"], validation["unexpected"])
-
-    def checkpoint_layout(self) -> dict[str, Any]:
-        return {
-            "state_dict_keys": list(self._state_dict_keys),
-            "units": [
-                {
-                    "unit_index": u.unit_index,
-                    "parameters": [
-                        {
-                            "names": list(self._parameter_state_names[id(m.parameter)]),
-                            "shape": list(m.shape),
-                            "stride": list(m.stride),
-                            "numel": m.numel,
-                            "local_shape": list(m.sharded_param._local_tensor.shape),
-                            "placements": [str(pl) for pl in m.sharded_param.placements],
-                            "dtype": str(m.parameter.dtype),
-                            "requires_grad": m.parameter.requires_grad,
-                        }
-                        for m in u.param_metas
-                    ],
-                }
-                for u in self.units
-            ],
-        }
-
-    def sharded_state_dict(self) -> dict[str, Any]:
-        if not self._state_dict_keys:
-            self._capture_state_dict_layout()
-        if not self.is_active:
-            return {"layout": self.checkpoint_layout(), "full_state": self.full_state_dict()}
-        return {"layout": self.checkpoint_layout(),
-                "shards": [self._cpu_copy(p) for p in self.get_sharded_params()],
-                "non_parameter_state": self._non_parameter_state_dict()}
-
-    def load_sharded_state_dict(self, state_dict, strict: bool = True):
-        if not self._state_dict_keys:
-            self._capture_state_dict_layout()
-        if not isinstance(state_dict, dict):
-            raise TypeError("Sharded checkpoint state must be a dictionary")
-        if state_dict.get("layout") != self.checkpoint_layout():
-            raise RuntimeError("Sharded checkpoint layout does not match the current model")
-        if not self.is_active:
-            return self.model.load_state_dict(state_dict["full_state"], strict=strict)
-        shards = state_dict.get("shards", [])
-        params = self.get_sharded_params()
-        if len(shards) != len(params):
-            raise RuntimeError(f"Expected {len(params)} parameter shards, found {len(shards)}")
-        for i, (p, s) in enumerate(zip(params, shards)):
-            if not isinstance(s, torch.Tensor):
-                raise RuntimeError(f"Invalid parameter shard {i}: expected a tensor")
-            loc = p._local_tensor
-            if s.shape != loc.shape or s.dtype != loc.dtype:
-                raise RuntimeError(f"Invalid parameter shard {i}: expected shape/dtype {tuple(loc.shape)}/"
-                                   f"{loc.dtype}, got {tuple(s.shape)}/{s.dtype}")
-        nps = state_dict.get("non_parameter_state", {})
-        if not isinstance(nps, dict):
-            raise TypeError("Checkpoint non-parameter state must be a dictionary")
-        cur = self.model.state_dict(keep_vars=True)
-        expected = [n for n in cur if n not in self._parameter_state_keys]
-        missing = [n for n in expected if n not in nps]
-        unexpected = [n for n in nps if n not in set(expected)]
-        errors = []
-        if strict and missing:
-            errors.append(f"Missing non-parameter key(s): {missing}")
-        if strict and unexpected:
-            errors.append(f"Unexpected non-parameter key(s): {unexpected}")
-        for n in set(expected) & set(nps):
-            dst, src = cur[n], nps[n]
-            if isinstance(dst, torch.Tensor):
-                if not isinstance(src, torch.Tensor):
-                    errors.append(f"Expected tensor for non-parameter state {n}, got {type(src).__name__}")
-                elif src.shape != dst.shape or src.dtype != dst.dtype:
-                    errors.append(f"Invalid non-parameter state for {n}: expected shape/dtype "
-                                  f"{tuple(dst.shape)}/{dst.dtype}, got {tuple(src.shape)}/{src.dtype}")
-        if errors:
-            raise RuntimeError("; ".join(errors))
-        for p, s in zip(params, shards):
-            p._local_tensor.detach().copy_(s)
-        self._copy_non_parameter_state(nps)
-        return nn.modules.module._IncompatibleKeys(missing, unexpected)
-
-    def state_dict(self):
-        return self.full_state_dict()
-
-    def load_state_dict(self, state_dict, strict: bool = True):
-        return self.load_full_state_dict(state_dict, strict=strict)
 
     @property
     def is_active(self) -> bool:

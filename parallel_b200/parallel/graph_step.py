@@ -29,10 +29,11 @@ reuse of a reduce-scatter slot or of a shard comes after the previous
 step's gradient-norm all-reduce, which no rank passes before every rank's
 reductions and gathers of that step have finished.
 
-Not capturable (the runner refuses them, ``capture_unsupported``): MoE
-models (the routing sends the route counts to the host to size the grouped
-expert GEMMs), model parallelism (the fused sequence-parallel kernels use
-host-side flag targets), fp16 loss scaling (host decisions), CPU offload
+MoE layers are capturable: their routing plan, expert GEMM tile counts and
+exchange sizes live on the device (``ops.moe.routed_experts``).
+
+Not capturable (the runner refuses them, ``capture_unsupported``): model
+parallelism (the fused sequence-parallel kernels use host-side flag targets), fp16 loss scaling (host decisions), CPU offload
 (host optimizer), usage bitmaps read on the host (FSDP with
 find_unused_parameters, DP-replicate without FSDP), CPU devices.
 """
@@ -46,8 +47,9 @@ def capture_unsupported(engine) -> str | None:
     """Why the engine's training step cannot be captured (each of these makes
     a host decision or a host read inside the step), or None."""
     fsdp = engine.fsdp_wrapper
-    if getattr(getattr(engine.model, "config", None), "is_moe", False):
-        return "MoE models yet: the routing sizes the grouped expert GEMMs on the host"
+    cfg = getattr(engine.model, "config", None)
+    if getattr(cfg, "is_moe", False) and not (1 <= cfg.num_experts <= 256 and cfg.hidden_size % 8 == 0):
+        return "MoE models whose routing cannot run on the device (more than 256 experts)"
     if engine.mp_wrapper.is_active:
         return "model parallelism (the fused sequence-parallel kernels take host-side flag targets)"
     if engine.grad_scaler.is_enabled():

@@ -1,304 +1,230 @@
 """Checkpoint adapters for model-parallel models.
 
-* ``ModelParallelCheckpoint`` (TP/EP without FSDP): the portable state dict
-  is gathered over TP along each parameter's ``shard_dim`` (and replicated
-  parameters taken from TP rank 0); loading scatters / broadcasts.
-  Exact-topology layout ``{"kind": "model-parallel", "plan", "state"}``.
-* ``ComposedModelParallelCheckpoint`` (TP/EP over FSDP): FSDP's full local
-  state, then TP gather to the portable root; loading goes portable -> TP
-  scatter -> ``FSDPWrapper.load_local_full_state_dict``.  Layout
-  ``{"kind": "model-parallel-fsdp", "plan", "fsdp"}``.
+A model-parallel rank holds TP / EP shards of the parameters.  The portable
+state dict is the HF-layout full model; converting between the two is a join
+(or split) of every parameter along its plan ``shard_dim`` over the TP group,
+with replicated parameters and buffers taken from TP rank 0.  Two adapters
+differ only in where the rank-local tensors live:
 
-Formats and key order are the reference's (parallel/parallel/engine/
-model_parallel/checkpoint.py) so checkpoints interchange.
+* ``ModelParallelCheckpoint`` (TP / EP without FSDP): in the module itself.
+  Exact-topology layout ``{"kind": "model-parallel", "plan", "state"}``; the
+  sharded payload is ``{"layout", "local_state"}``.
+* ``ComposedModelParallelCheckpoint`` (TP / EP over FSDP): in the FSDP
+  units, whose ``full_state_dict`` / ``load_local_full_state_dict`` produce
+  and accept the model-parallel-local full state on the dp_shard root.
+  Layout ``{"kind": "model-parallel-fsdp", "plan", "fsdp"}``; the sharded
+  payload is ``{"layout", "fsdp"}``.
+
+Both validate an incoming portable dict with the shared
+``state_io.StateCatalog`` (full shapes = local shapes with the shard
+dimension multiplied by the TP size) on global rank 0 and share the verdict
+with every rank before any tensor moves.  Formats and key order are the
+reference's (``parallel/parallel/engine/model_parallel/checkpoint.py``), so
+checkpoints interchange.
 """
 from __future__ import annotations
 
-import copy
 from collections import OrderedDict
+from typing import Optional
 
 import torch
 import torch.distributed as dist
-import torch.nn as nn
 
 from ...state import Strategies
+from ..state_io import (Entry, LoadReport, StateCatalog, host_tensor, parameter_names, share_report, tp_assemble,
+                        tp_distribute, with_metadata)
 from .plan import ModelParallelPlan
 
 
-def _cpu(t: torch.Tensor) -> torch.Tensor:
-    return t.detach().to(device="cpu", copy=True)
-
-
-def _mesh_rank(pconfig, dim: Strategies) -> int:
+def _coordinate(pconfig, dim: Strategies) -> int:
     mesh = pconfig.device_mesh
-    if mesh is not None and dim.value in mesh.mesh_dim_names:
-        return mesh.get_local_rank(dim.value)
-    return 0
+    names = tuple(getattr(mesh, "mesh_dim_names", None) or ()) if mesh is not None else ()
+    return mesh.get_local_rank(dim.value) if dim.value in names else 0
 
 
-def _broadcast_validation(validation):
-    if not dist.is_initialized():
-        return validation
-    payload = [validation if dist.get_rank() == 0 else None]
-    dist.broadcast_object_list(payload, src=0)
-    return payload[0]
+class _TPStateAdapter:
+    """Shared machinery: the catalog, the TP join / split loops and the
+    replica fan-out; subclasses say where local tensors come from / go to."""
 
-
-class ModelParallelCheckpoint:
     def __init__(self, model, pconfig, plan: ModelParallelPlan, tp_mesh, device):
         self.model, self.pconfig, self.plan, self.tp_mesh = model, pconfig, plan, tp_mesh
         self.tp_group = tp_mesh.get_group()
+        self.tp_size = tp_mesh.size()
         self.device = torch.device(device)
-        ids = {id(p) for p in model.parameters()}
-        self._parameter_names = {n for n, v in model.state_dict(keep_vars=True).items() if id(v) in ids}
+
+    # -------------------------------------------------------------- rank roles
+    @property
+    def tp_rank(self) -> int:
+        return self.tp_mesh.get_local_rank()
+
+    @property
+    def replica_zero(self) -> bool:
+        return _coordinate(self.pconfig, Strategies.DP_REPLICATE) == 0
+
+    def split_dim(self, name: str) -> Optional[int]:
+        return self.plan.placement_for_parameter(name).shard_dim
+
+    def _entry(self, name: str, local_shape, dtype, is_param: bool) -> Entry:
+        dim = self.split_dim(name) if is_param else None
+        full = list(local_shape)
+        if dim is not None:
+            full[dim] *= self.tp_size
+        return Entry(name, is_param, tuple(full), dtype, dim)
+
+    # -------------------------------------------------------------- subclass interface
+    def catalog(self) -> StateCatalog:
+        raise NotImplementedError
+
+    # -------------------------------------------------------------- portable save
+    def _join(self, local_state, *, dedupe: bool) -> Optional[OrderedDict]:
+        """Portable state on TP rank 0 (None elsewhere) from this rank's local
+        tensors; every TP rank of the group must call."""
+        root = self.tp_rank == 0
+        out = OrderedDict() if root else None
+        # id -> portable tensor (None off the root); every rank records it so
+        # all ranks skip the same collectives for a tied weight's second name
+        joined: dict[int, Optional[torch.Tensor]] = {}
+        for entry in self.catalog():
+            value = local_state[entry.name]
+            if not entry.is_param:
+                if root:
+                    out[entry.name] = host_tensor(value)
+                continue
+            if dedupe and id(value) in joined:  # tied weights stay one tensor
+                if root:
+                    out[entry.name] = joined[id(value)]
+                continue
+            full = tp_assemble(value.to(self.device), entry.tp_dim, self.tp_group, self.tp_size,
+                               root_only=True, i_am_root=root)
+            joined[id(value)] = host_tensor(full) if root else None
+            if root:
+                out[entry.name] = joined[id(value)]
+        return out
+
+    # -------------------------------------------------------------- portable load
+    def _verdict(self, state_dict, strict: bool) -> LoadReport:
+        loader = not dist.is_initialized() or dist.get_rank() == 0
+        report = self.catalog().audit(state_dict, strict, need_value="portable state dict") if loader else None
+        report = share_report(report, src=0)
+        report.raise_if_bad("the portable state dict")
+        return report
+
+    def _split(self, state_dict, report: LoadReport, local_shapes: dict, dtypes: dict):
+        """Yield (name, local tensor) for each present entry; TP rank 0 of the
+        participating group holds ``state_dict`` (the portable dict)."""
+        root = self.tp_rank == 0
+        for entry in self.catalog():
+            if entry.name not in report.present:
+                continue
+            full = state_dict[entry.name] if root else None
+            yield entry.name, tp_distribute(full, entry.tp_dim, local_shapes[entry.name], dtypes[entry.name],
+                                            self.device, self.tp_group, self.tp_size, root)
+
+
+class ModelParallelCheckpoint(_TPStateAdapter):
+    """TP / EP shards held by the module itself (no FSDP)."""
+
+    def __init__(self, model, pconfig, plan: ModelParallelPlan, tp_mesh, device):
+        super().__init__(model, pconfig, plan, tp_mesh, device)
+        self._param_keys = {n for names in parameter_names(model).values() for n in names}
 
     @property
     def is_active(self) -> bool:
         return True
 
-    def _checkpoint_replica(self) -> bool:
-        return _mesh_rank(self.pconfig, Strategies.DP_REPLICATE) == 0
-
-    def _full_state_root(self) -> bool:
-        return self._checkpoint_replica() and self.tp_mesh.get_local_rank() == 0
-
-    def _gather(self, t: torch.Tensor, dim: int) -> torch.Tensor:
-        parts = [torch.empty_like(t) for _ in range(self.tp_mesh.size())]
-        dist.all_gather(parts, t.detach().contiguous(), group=self.tp_group)
-        return torch.cat(parts, dim=dim)
+    def catalog(self) -> StateCatalog:
+        return StateCatalog(self._entry(n, v.shape, v.dtype, n in self._param_keys)
+                            for n, v in self.model.state_dict(keep_vars=True).items())
 
     def full_state_dict(self):
-        if not self._checkpoint_replica():
+        if not self.replica_zero:
             return None
         local = self.model.state_dict(keep_vars=True)
-        root = self._full_state_root()
-        out = OrderedDict() if root else None
-        seen: dict[int, torch.Tensor] = {}
-        for name, v in local.items():
-            if name in self._parameter_names:
-                pl = self.plan.placement_for_parameter(name)
-                full = (v.detach() if root else None) if pl.shard_dim is None else self._gather(v, pl.shard_dim)
-                if root:
-                    cpu = seen.get(id(v))
-                    if cpu is None:
-                        cpu = _cpu(full)
-                        seen[id(v)] = cpu
-                    out[name] = cpu
-            elif root:
-                out[name] = _cpu(v) if isinstance(v, torch.Tensor) else copy.deepcopy(v)
-        if root and hasattr(local, "_metadata"):
-            out._metadata = copy.deepcopy(local._metadata)
-        return out
+        out = self._join(local, dedupe=True)
+        return with_metadata(out, local) if out is not None else None
 
-    def _validate(self, sd, strict: bool) -> dict:
-        exp_state = self.model.state_dict()
-        expected, actual = set(exp_state), set(sd) if sd is not None else set()
-        missing, unexpected = sorted(expected - actual), sorted(actual - expected)
-        errors = []
-        if sd is None:
-            errors.append("global rank zero requires a full state dict")
-        if strict and missing:
-            errors.append(f"Missing key(s): {missing}")
-        if strict and unexpected:
-            errors.append(f"Unexpected key(s): {unexpected}")
-        if sd is not None:
-            for n in expected & actual:
-                src = sd[n]
-                if not isinstance(src, torch.Tensor):
-                    errors.append(f"Expected tensor for {n}")
-                    continue
-                shape = list(exp_state[n].shape)
-                if n in self._parameter_names:
-                    pl = self.plan.placement_for_parameter(n)
-                    if pl.shard_dim is not None:
-                        shape[pl.shard_dim] *= self.tp_mesh.size()
-                if tuple(src.shape) != tuple(shape):
-                    errors.append(f"Shape mismatch for {n}: expected {tuple(shape)}, got {tuple(src.shape)}")
-        return {"error": "; ".join(errors) if errors else None, "missing": missing, "unexpected": unexpected,
-                "available": sorted(actual & expected)}
-
-    def _replica_root_tensor(self, source, shape, dtype):
-        if self.tp_mesh.get_local_rank() != 0:
+    def _from_replica_zero(self, tensor: Optional[torch.Tensor], shape, dtype) -> Optional[torch.Tensor]:
+        """TP rank 0 of every replica gets replica 0's full tensor."""
+        if self.tp_rank != 0:
             return None
-        t = source.to(self.device) if self._checkpoint_replica() else torch.empty(shape, dtype=dtype,
-                                                                                   device=self.device)
+        if self.replica_zero:
+            tensor = tensor.to(self.device)
+        else:
+            tensor = torch.empty(shape, dtype=dtype, device=self.device)
         group = self.pconfig.group(Strategies.DP_REPLICATE)
         if group is not None and self.pconfig.dp_replicate_size > 1:
-            dist.broadcast(t, src=dist.get_global_rank(group, 0), group=group)
-        return t
+            dist.broadcast(tensor, src=dist.get_global_rank(group, 0), group=group)
+        return tensor
 
     def load_full_state_dict(self, state_dict, strict: bool = True):
-        root = not dist.is_initialized() or dist.get_rank() == 0
-        validation = _broadcast_validation(self._validate(state_dict, strict) if root else None)
-        if validation["error"]:
-            raise RuntimeError(f"Error(s) in loading state_dict: {validation['error']}")
-        dest_state = self.model.state_dict(keep_vars=True)
-        tp_root = dist.get_global_rank(self.tp_group, 0)
-        tp_rank = self.tp_mesh.get_local_rank()
-        for name, dst in dest_state.items():
-            if name not in validation["available"]:
-                continue
-            pl = self.plan.placement_for_parameter(name) if name in self._parameter_names else None
-            local_shape = tuple(dst.shape)
-            full_shape = list(local_shape)
-            if pl is not None and pl.shard_dim is not None:
-                full_shape[pl.shard_dim] *= self.tp_mesh.size()
-            src = state_dict[name] if root and name in state_dict else None
-            rep = self._replica_root_tensor(src, tuple(full_shape), dst.dtype)
-            if pl is not None and pl.shard_dim is not None:
-                recv = torch.empty_like(dst, device=self.device)
-                lst = ([s.contiguous() for s in rep.chunk(self.tp_mesh.size(), dim=pl.shard_dim)]
-                       if tp_rank == 0 else None)
-                dist.scatter(recv, scatter_list=lst, src=tp_root, group=self.tp_group)
-            else:
-                recv = rep if tp_rank == 0 else torch.empty(local_shape, dtype=dst.dtype, device=self.device)
-                dist.broadcast(recv, src=tp_root, group=self.tp_group)
-            dst.detach().copy_(recv.to(dst.device))
-        return nn.modules.module._IncompatibleKeys(validation["missing"], validation["unexpected"])
+        report = self._verdict(state_dict, strict)
+        catalog = self.catalog()
+        dest = self.model.state_dict(keep_vars=True)
+        # replica fan-out first, then the TP split of each tensor
+        staged = {}
+        for name in report.present:
+            src = state_dict[name] if (self.replica_zero and self.tp_rank == 0) else None
+            staged[name] = self._from_replica_zero(src, catalog[name].full_shape, dest[name].dtype)
+        shapes = {n: tuple(dest[n].shape) for n in report.present}
+        dtypes = {n: dest[n].dtype for n in report.present}
+        for name, local in self._split(staged, report, shapes, dtypes):
+            dest[name].detach().copy_(local.to(dest[name].device))
+        return report.incompatible_keys()
 
     def checkpoint_layout(self) -> dict:
+        rows = []
         state = self.model.state_dict()
-        return {
-            "kind": "model-parallel",
-            "plan": self.plan.checkpoint_metadata(),
-            "state": [
-                {"name": n, "local_shape": list(v.shape), "dtype": str(v.dtype),
-                 "placement": (self.plan.placement_for_parameter(n).parallelism.value
-                               if n in self._parameter_names else "buffer"),
-                 "shard_dim": (self.plan.placement_for_parameter(n).shard_dim
-                               if n in self._parameter_names else None)}
-                for n, v in state.items()
-            ],
-        }
+        for e in self.catalog():
+            placement = self.plan.placement_for_parameter(e.name) if e.is_param else None
+            rows.append({"name": e.name, "local_shape": list(state[e.name].shape), "dtype": str(e.dtype),
+                         "placement": placement.parallelism.value if placement else "buffer",
+                         "shard_dim": placement.shard_dim if placement else None})
+        return {"kind": "model-parallel", "plan": self.plan.checkpoint_metadata(), "state": rows}
 
     def sharded_state_dict(self) -> dict:
-        state = self.model.state_dict()
-        return {"layout": self.checkpoint_layout(), "local_state": OrderedDict((n, _cpu(v)) for n, v in state.items())}
+        return {"layout": self.checkpoint_layout(),
+                "local_state": OrderedDict((n, host_tensor(v)) for n, v in self.model.state_dict().items())}
 
     def load_sharded_state_dict(self, state_dict, strict: bool = True):
-        if not isinstance(state_dict, dict):
-            raise TypeError("Sharded checkpoint state must be a dictionary")
+        if not isinstance(state_dict, dict) or not isinstance(state_dict.get("local_state"), dict):
+            raise TypeError("a model-parallel shard payload is a dict with a 'local_state' dict")
         if state_dict.get("layout") != self.checkpoint_layout():
-            raise RuntimeError("Sharded checkpoint layout does not match the current model")
-        local = state_dict.get("local_state")
-        if not isinstance(local, dict):
-            raise TypeError("Sharded checkpoint has no local_state dictionary")
-        return self.model.load_state_dict(local, strict=strict)
+            raise RuntimeError("sharded checkpoint layout does not match the current model")
+        return self.model.load_state_dict(state_dict["local_state"], strict=strict)
 
 
-class ComposedModelParallelCheckpoint:
+class ComposedModelParallelCheckpoint(_TPStateAdapter):
+    """TP / EP shards further row-sharded by FSDP units."""
+
     def __init__(self, model, pconfig, plan, tp_mesh, fsdp_wrapper, device):
-        self.model, self.pconfig, self.plan, self.tp_mesh = model, pconfig, plan, tp_mesh
-        self.tp_group = tp_mesh.get_group()
+        super().__init__(model, pconfig, plan, tp_mesh, device)
         self.fsdp = fsdp_wrapper
-        self.device = torch.device(device)
-        self._local_shapes = {}
-        for u in fsdp_wrapper.units:
-            for m in u.param_metas:
-                for n in fsdp_wrapper._parameter_state_names[id(m.parameter)]:
-                    self._local_shapes[n] = tuple(m.shape)
 
     @property
-    def _checkpoint_replica(self) -> bool:
-        return _mesh_rank(self.pconfig, Strategies.DP_REPLICATE) == 0
+    def dp_shard_root(self) -> bool:
+        return _coordinate(self.pconfig, Strategies.DP_SHARD) == 0
 
-    @property
-    def _dp_shard_root(self) -> bool:
-        return _mesh_rank(self.pconfig, Strategies.DP_SHARD) == 0
-
-    @property
-    def _portable_root(self) -> bool:
-        return self._checkpoint_replica and self._dp_shard_root and self.tp_mesh.get_local_rank() == 0
-
-    def _is_parameter(self, name: str) -> bool:
-        return name in self.fsdp._parameter_state_keys
+    def catalog(self) -> StateCatalog:
+        local = self.fsdp.local_catalog()  # model-parallel-local full shapes
+        return StateCatalog(self._entry(e.name, e.full_shape, e.dtype, e.is_param) for e in local)
 
     def full_state_dict(self):
-        local = self.fsdp.full_state_dict()
-        if not self._checkpoint_replica or not self._dp_shard_root:
+        local = self.fsdp.full_state_dict()  # on every dp_shard root of replica 0
+        if not (self.replica_zero and self.dp_shard_root):
             return None
-        root = self._portable_root
-        out = OrderedDict() if root else None
-        tp_root = dist.get_global_rank(self.tp_group, 0)
-        for name in self.fsdp._state_dict_keys:
-            v = local[name]
-            pl = self.plan.placement_for_parameter(name) if self._is_parameter(name) else None
-            if pl is not None and pl.shard_dim is not None:
-                lv = v.to(self.device)
-                parts = [torch.empty_like(lv) for _ in range(self.tp_mesh.size())] if root else None
-                dist.gather(lv, gather_list=parts, dst=tp_root, group=self.tp_group)
-                if root:
-                    out[name] = _cpu(torch.cat(parts, dim=pl.shard_dim))
-            elif root:
-                out[name] = _cpu(v)
-        if root and hasattr(local, "_metadata"):
-            out._metadata = copy.deepcopy(local._metadata)
-        return out
-
-    def _validate(self, sd, strict: bool) -> dict:
-        expected = set(self.fsdp._state_dict_keys)
-        actual = set(sd) if sd is not None else set()
-        missing, unexpected = sorted(expected - actual), sorted(actual - expected)
-        errors = []
-        if sd is None:
-            errors.append("global rank zero requires a portable state dict")
-        if strict and missing:
-            errors.append(f"Missing key(s): {missing}")
-        if strict and unexpected:
-            errors.append(f"Unexpected key(s): {unexpected}")
-        if sd is not None:
-            cur = self.model.state_dict()
-            for n in expected & actual:
-                src = sd[n]
-                if not isinstance(src, torch.Tensor):
-                    errors.append(f"Expected tensor for {n}")
-                    continue
-                if self._is_parameter(n):
-                    shape = list(self._local_shapes[n])
-                    pl = self.plan.placement_for_parameter(n)
-                    if pl.shard_dim is not None:
-                        shape[pl.shard_dim] *= self.tp_mesh.size()
-                else:
-                    shape = list(cur[n].shape)
-                if tuple(src.shape) != tuple(shape):
-                    errors.append(f"Shape mismatch for {n}: expected {tuple(shape)}, got {tuple(src.shape)}")
-        return {"error": "; ".join(errors) if errors else None, "missing": missing, "unexpected": unexpected,
-                "available": sorted(expected & actual)}
-
-    def _local_state_from_portable(self, sd, validation):
-        if not self._checkpoint_replica or not self._dp_shard_root:
-            return None
-        root = self._portable_root
-        tp_root = dist.get_global_rank(self.tp_group, 0)
-        out = OrderedDict()
-        cur = self.model.state_dict()
-        for name in self.fsdp._state_dict_keys:
-            if name not in validation["available"]:
-                continue
-            if self._is_parameter(name):
-                pl = self.plan.placement_for_parameter(name)
-                shape = self._local_shapes[name]
-            else:
-                pl, shape = None, tuple(cur[name].shape)
-            src = sd[name].to(self.device) if root else None
-            recv = torch.empty(shape, dtype=(sd[name].dtype if root else cur[name].dtype), device=self.device)
-            if pl is not None and pl.shard_dim is not None:
-                lst = [s.contiguous() for s in src.chunk(self.tp_mesh.size(), dim=pl.shard_dim)] if root else None
-                dist.scatter(recv, scatter_list=lst, src=tp_root, group=self.tp_group)
-            else:
-                if root:
-                    recv.copy_(src)
-                dist.broadcast(recv, src=tp_root, group=self.tp_group)
-            out[name] = _cpu(recv)
-        return out
+        out = self._join(local, dedupe=False)
+        return with_metadata(out, local) if out is not None else None
 
     def load_full_state_dict(self, state_dict, strict: bool = True):
-        validation = _broadcast_validation(self._validate(state_dict, strict) if dist.get_rank() == 0 else None)
-        if validation["error"] is not None:
-            raise RuntimeError(f"Error(s) in loading portable state_dict: {validation['error']}")
-        local = self._local_state_from_portable(state_dict, validation)
+        report = self._verdict(state_dict, strict)
+        local = None
+        if self.replica_zero and self.dp_shard_root:
+            local_catalog = self.fsdp.local_catalog()
+            shapes = {e.name: e.full_shape for e in local_catalog}
+            dtypes = {e.name: e.dtype for e in local_catalog}
+            local = OrderedDict((n, host_tensor(t)) for n, t in self._split(state_dict, report, shapes, dtypes))
         self.fsdp.load_local_full_state_dict(local, strict=strict)
-        return nn.modules.module._IncompatibleKeys(validation["missing"], validation["unexpected"])
+        return report.incompatible_keys()
 
     def checkpoint_layout(self) -> dict:
         return {"kind": "model-parallel-fsdp", "plan": self.plan.checkpoint_metadata(),
@@ -308,8 +234,8 @@ class ComposedModelParallelCheckpoint:
         return {"layout": self.checkpoint_layout(), "fsdp": self.fsdp.sharded_state_dict()}
 
     def load_sharded_state_dict(self, state_dict, strict: bool = True):
-        if not isinstance(state_dict, dict):
-            raise TypeError("Sharded checkpoint state must be a dictionary")
+        if not isinstance(state_dict, dict) or "fsdp" not in state_dict:
+            raise TypeError("a composed shard payload is a dict with an 'fsdp' entry")
         if state_dict.get("layout") != self.checkpoint_layout():
-            raise RuntimeError("Composite checkpoint layout does not match the model")
+            raise RuntimeError("composed checkpoint layout does not match the model")
         return self.fsdp.load_sharded_state_dict(state_dict["fsdp"], strict=strict)

@@ -21,6 +21,7 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
+from ...ops.moe import LocalExpertTransport, routed_experts, routed_experts_supported
 from ...profiling import collective_profile
 from .token_dispatch import TokenDispatcher
 
@@ -120,14 +121,21 @@ class ReplicatedTokenExpertParallel:
         # FusedTensorParallel of the TP group (NVLink all-reduces of the bf16
         # hidden states / expert outputs) or None
         self.fused = fused
+        self.transport = LocalExpertTransport(partition.local_count, num_experts=partition.num_experts,
+                                              ep_rank=partition.ep_rank, local_only=True)
         self._model = None
 
     def __call__(self, experts, x2, global_index, weights):
-        # localise after the backward all-reduce boundary (see reference note)
+        # the routing weights pass the backward all-reduce boundary before they
+        # are localised, so every rank's weight gradient sums into each route
         weights = _AllReduceBackward.apply(weights, self.group)
-        local_idx, local_w, _ = self.partition.localize_routes(global_index, weights)
         h = _AllReduceBackward.apply(x2, self.group, self.fused)
-        y = experts(h, local_idx, local_w)
+        if routed_experts_supported(h, experts.gate_up_proj, self.partition.num_experts):
+            # device path: routes to other ranks' experts are dropped by the plan
+            y = routed_experts(h, weights, global_index, experts.gate_up_proj, experts.down_proj, self.transport)
+        else:
+            local_idx, local_w, _ = self.partition.localize_routes(global_index, weights)
+            y = experts(h, local_idx, local_w)
         return _AllReduceForward.apply(y, self.group, self.fused)
 
     def apply(self, model) -> None:
@@ -149,16 +157,20 @@ class SequenceParallelExpertParallel:
     def __init__(self, partition: ExpertPartition, group, device=None, collectives: str = "auto"):
         self.partition = partition
         self.group = group
-        # NVLink peer-memory dispatch / combine on CUDA (<= 8 ranks), NCCL / gloo otherwise
-        from .p2p_dispatch import P2PTokenDispatcher
+        # NVLink peer memory with a device-resident routing plan on CUDA (<= 8
+        # ranks); variable all-to-alls with host-read split sizes otherwise
+        from .p2p_dispatch import PeerExpertTransport
 
-        if device is not None and collectives != "nccl" and P2PTokenDispatcher.available(group, device):
-            self.dispatcher = P2PTokenDispatcher(partition, group, device)
-        else:
-            self.dispatcher = TokenDispatcher(partition, group)
+        self.transport = None
+        if device is not None and collectives != "nccl" and PeerExpertTransport.available(group, device):
+            self.transport = PeerExpertTransport(partition, group, device)
+        self.dispatcher = TokenDispatcher(partition, group)
         self._model = None
 
     def __call__(self, experts, x2, global_index, weights):
+        if self.transport is not None and routed_experts_supported(x2, experts.gate_up_proj,
+                                                                   self.partition.num_experts):
+            return routed_experts(x2, weights, global_index, experts.gate_up_proj, experts.down_proj, self.transport)
         hidden, idx, w, state = self.dispatcher.dispatch(x2, global_index, weights)
         y = experts(hidden, idx, w)
         return self.dispatcher.combine(y, state)

@@ -1,25 +1,37 @@
-"""Expert-parallel token dispatch / combine over NVLink peer memory.
+"""Expert-parallel token exchange over NVLink peer memory, without host syncs.
 
-Same interface and semantics as ``TokenDispatcher`` (reference:
-parallel/parallel/engine/model_parallel/token_dispatch.py:101-174), with the
-data plane replaced by the peer-memory row kernels of ``csrc/comm.cu``:
+``PeerExpertTransport`` plugs into ``ops.moe.routed_experts`` (one autograd
+node for dispatch -> expert GEMMs -> combine) for the sequence-parallel
+expert parallelism: each rank routes its own tokens and the owners of the
+chosen experts compute them.  Everything the exchange needs is sized on the
+device:
 
-* dispatch: every route's hidden row (and a 16-byte record: local expert id,
-  score, source route) is stored by one warp straight into the owning rank's
-  symmetric receive buffer, at the row given by the route counts of all
-  ranks (one small all-gather of the per-destination counts; like the
-  reference, the counts go to the host because they size the expert GEMMs);
-  no staging sort / all-to-all / index_select.
-* combine: the owner exposes its expert outputs in a symmetric buffer and
-  each source rank pulls its tokens' top-k rows and sums them in fp32 in one
-  kernel (the reference's all-to-all back + index_add).
-* backward: dispatch's backward is a pull-and-sum (hidden) plus a pull (score
-  gradients); combine's backward pushes each token's output gradient to its
-  routes' rows at the owners.
+* plan: each rank's route histogram over the global experts is written as
+  its row of a [W, E] matrix and summed over the EP group (NVLink small
+  all-reduce, or NCCL), which gives every rank every histogram; the plan
+  kernel then derives every owner's padded expert layout and the destination
+  (owner, row) of each of this rank's routes (``csrc/moe.cu``);
+* dispatch: one kernel stores each route's hidden row straight into its
+  owner's receive matrix (the permutation happens in the store); after a
+  signal barrier the owner copies the live rows out into its padded expert
+  matrix and zeroes the padding;
+* the down-projection GEMM writes the expert outputs into this rank's
+  exchange buffer; after a barrier each source rank pulls its routes' rows
+  and sums them with the routing weights (fp32) - the combine;
+* backward mirrors it: the routing-weight gradient and the weighted output
+  gradient per route, pushed to the owners; the input-gradient GEMM writes
+  into the exchange buffer and each source rank pulls and sums its routes.
 
-Symmetric buffers rotate over two sets; one signal barrier per exchange
-orders reuse (every rank finished exchange n-1 when a rank passes the
-barrier of exchange n).
+Buffers are worst-case sized from the host-known token count (every route of
+every rank could pick this owner), so no count ever reaches the host and an
+MoE step can be captured in a CUDA graph.  Two rotating buffer sets with one
+barrier per exchange order reuse: a rank writes a set only after the barrier
+of the exchange in between, which every rank reaches after its reads of the
+set's previous use.
+
+Reference counterpart: ``parallel/parallel/engine/model_parallel/
+token_dispatch.py:86-174`` (sort, count all-to-all + ``.tolist()``, three
+variable all-to-alls, index_add), which this replaces on CUDA.
 """
 from __future__ import annotations
 
@@ -29,184 +41,107 @@ import torch
 import torch.distributed as dist
 
 from ...ops._ext import ext
+from ...ops.moe import LocalExpertTransport, RoutePlan
 from ...profiling import collective_profile
-from ..comm.p2p import SymmBuffer, p2p_supported
+from ..comm.p2p import P2PSmallAllReduce, SymmBuffer, p2p_supported
 
 
-class _Pool:
-    """Two rotating sets of symmetric buffers: rows [cap, H] bf16 and 16-byte records [cap, 4] int32."""
+class _RowPool:
+    """Two rotating symmetric row buffers [rows_cap, H] bf16 of the EP group."""
 
-    def __init__(self, group, device, cap: int, hidden: int):
-        self.cap, self.hidden = cap, hidden
-        self.rows = [SymmBuffer(cap * hidden, torch.bfloat16, device, group, "ep_rows") for _ in range(2)]
-        self.recs = [SymmBuffer(cap * 4, torch.int32, device, group, "ep_records") for _ in range(2)]
-        self.n = 0
+    def __init__(self, group, device, rows_cap: int, hidden: int):
+        self.rows_cap, self.hidden = rows_cap, hidden
+        self.sets = [SymmBuffer(rows_cap * hidden, torch.bfloat16, device, group, "ep_rows") for _ in range(2)]
+        self.turn = 0
 
-    def next(self):
-        k = self.n % 2
-        self.n += 1
-        return self.rows[k], self.recs[k]
+    def next(self) -> SymmBuffer:
+        buf = self.sets[self.turn % 2]
+        self.turn += 1
+        return buf
 
 
-class P2PTokenDispatcher:
+class PeerExpertTransport(LocalExpertTransport):
+    """Routes of this rank's tokens to the owners of their experts over the
+    EP group's peer memory (see module docstring)."""
+
     def __init__(self, partition, group, device):
+        super().__init__(partition.local_count, num_experts=partition.num_experts, ep_rank=dist.get_rank(group))
         self.partition = partition
         self.group = group
-        self.world_size = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
         self.device = device
         self.limit_s = float(os.environ.get("PB_P2P_TIMEOUT_S", "60"))
-        self.pool: _Pool | None = None
+        self.pool: _RowPool | None = None
+        self.small = P2PSmallAllReduce.get(group, device)
 
     @staticmethod
     def available(group, device) -> bool:
         return device.type == "cuda" and p2p_supported(group)
 
-    def _ensure(self, routes: int, hidden: int) -> _Pool:
-        cap = routes * self.world_size  # every route of every rank could target one owner
+    # ------------------------------------------------------------------ plan
+    def routes_in(self, routes: int) -> int:
+        return routes * self.world  # every rank's routes could pick this owner
+
+    def _histogram(self, topi: torch.Tensor, num_experts: int):
+        mat = torch.empty(self.world, num_experts, dtype=torch.float32, device=topi.device)
+        ext().moe_hist(topi, mat, self.ep_rank)
+        flat = mat.view(-1)
+        with collective_profile("ep_all_reduce", value=flat, mode="p2p" if self.small else "nccl",
+                                detail="route_histograms"):
+            if self.small is not None and flat.numel() <= 3 * self.small.cap:
+                self.small.all_reduce_(flat)
+            else:
+                dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group)
+        return mat, self.ep_rank
+
+    def _rows(self, plan: RoutePlan, hidden: int) -> _RowPool:
         if self.pool is None:
-            self.pool = _Pool(self.group, self.device, cap, hidden)
-        elif cap > self.pool.cap or hidden != self.pool.hidden:
-            raise RuntimeError(f"P2P dispatch buffers were sized for {self.pool.cap} routes x {self.pool.hidden}; "
-                               f"got {cap} x {hidden}")
+            self.pool = _RowPool(self.group, self.device, plan.rows_cap, hidden)
+        elif plan.rows_cap > self.pool.rows_cap or hidden != self.pool.hidden:
+            raise RuntimeError(f"expert exchange buffers hold {self.pool.rows_cap} rows x {self.pool.hidden}; this "
+                               f"layer needs {plan.rows_cap} x {hidden} (the token count per rank must stay fixed)")
         return self.pool
 
     def _barrier(self, buf: SymmBuffer) -> None:
         buf.barrier(0, self.limit_s)
 
-    # ------------------------------------------------------------------ dispatch
-    def dispatch(self, hidden_states, global_indices, scores):
-        if global_indices.shape != scores.shape:
-            raise ValueError("Expert indices and scores must have the same shape")
-        tokens, top_k = global_indices.shape
-        flat_e = global_indices.reshape(-1)
-        dest = self.partition.owner(flat_e).to(torch.int64)
-        order = torch.argsort(dest, stable=True)
-        dest_sorted = dest[order]
-        send = torch.bincount(dest, minlength=self.world_size).to(torch.int64)
-        mat = torch.empty(self.world_size, self.world_size, dtype=torch.int64, device=send.device)
-        with collective_profile("ep_all_gather", value=send, mode="split_counts", detail="route_counts"):
-            dist.all_gather_into_tensor(mat.view(-1), send, group=self.group)
-        m = mat.tolist()  # [src][dst]
-        W, me = self.world_size, self.rank
-        recv_total = sum(m[s][me] for s in range(W))
-        offs_at_dst = torch.tensor([sum(m[s][d] for s in range(me)) for d in range(W)], device=send.device)
-        starts = torch.tensor([sum(m[me][:d]) for d in range(W)], device=send.device)
-        n = flat_e.numel()
-        pos = torch.arange(n, device=send.device)
-        dst_row_sorted = offs_at_dst[dest_sorted] + pos - starts[dest_sorted]
-        # flat-route order (t*K + k): destination rank and row of every route
-        dst_row = torch.empty_like(dst_row_sorted)
-        dst_row[order] = dst_row_sorted
-        src_of_recv = torch.repeat_interleave(torch.arange(W, device=send.device),
-                                              torch.tensor([m[s][me] for s in range(W)], device=send.device))
-        state = _P2PDispatchState(dest.to(torch.int32).contiguous(), dst_row.contiguous(), tokens, top_k,
-                                  recv_total, src_of_recv)
-        local_e = (flat_e - dest * self.partition.local_count).to(torch.int32)
-        rh, rs = _DispatchFn.apply(hidden_states, scores, self, state, local_e, order)
-        re = state.recv_experts
-        return rh, re.unsqueeze(-1), rs.unsqueeze(-1), state
+    # ------------------------------------------------------------------ forward
+    def dispatch(self, x2: torch.Tensor, plan: RoutePlan) -> torch.Tensor:
+        H = x2.shape[1]
+        recv = self._rows(plan, H).next()
+        with collective_profile("ep_dispatch", value=x2, mode="p2p", detail="routes"):
+            ext().moe_dispatch(x2, plan.top_k, plan.route_owner, plan.route_row, list(recv.peer_ptrs), H)
+            self._barrier(recv)
+        x_pad = torch.empty(plan.rows_cap, H, device=x2.device, dtype=x2.dtype)
+        self._pad(recv.tensor.data_ptr(), H, x_pad, plan)
+        return x_pad
 
-    def combine(self, expert_output: torch.Tensor, state):
-        return _CombineFn.apply(expert_output, self, state)
+    def output_buffer(self, plan: RoutePlan, H: int, like: torch.Tensor):
+        send = self._rows(plan, H).next()
+        return send.tensor[: plan.rows_cap * H].view(plan.rows_cap, H), send
 
+    def combine(self, handle: SymmBuffer, plan: RoutePlan, weights, out, keep) -> None:
+        with collective_profile("ep_combine", value=out, mode="p2p", detail="routes"):
+            self._barrier(handle)
+            ext().moe_combine(out, keep, weights, plan.route_owner, plan.route_row, list(handle.peer_ptrs),
+                              out.shape[1])
 
-class _P2PDispatchState:
-    def __init__(self, route_rank, route_row, tokens, top_k, recv_total, src_of_recv):
-        self.route_rank = route_rank  # int32 [T*K]: owner rank of each flat route
-        self.route_row = route_row    # int64 [T*K]: row of the route in the owner's buffers
-        self.num_source_tokens = tokens
-        self.top_k = top_k
-        self.recv_total = recv_total
-        self.src_of_recv = src_of_recv  # [R] source rank of each received row
-        self.recv_experts = None
-        self.recv_src_route = None
+    # ------------------------------------------------------------------ backward
+    def combine_backward(self, dout, keep, weights, plan: RoutePlan):
+        H = dout.shape[1]
+        recv = self._rows(plan, H).next()
+        dw = torch.empty(weights.shape, device=dout.device, dtype=torch.float32)
+        with collective_profile("ep_combine", value=dout, mode="p2p_grad", detail="routes"):
+            ext().moe_combine_bwd(dout, keep, weights, plan.route_owner, plan.route_row, list(recv.peer_ptrs), H, dw)
+            self._barrier(recv)
+        dy_pad = torch.empty(plan.rows_cap, H, device=dout.device, dtype=dout.dtype)
+        self._pad(recv.tensor.data_ptr(), H, dy_pad, plan)
+        return dy_pad, dw
 
+    def grad_buffer(self, plan: RoutePlan, H: int, like: torch.Tensor):
+        return self.output_buffer(plan, H, like)
 
-class _DispatchFn(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, hidden, scores, disp, state, local_e, order):
-        C = ext()
-        T, H = hidden.shape
-        K = state.top_k
-        pool = disp._ensure(T * K, H)
-        rows, recs = pool.next()
-        n = T * K
-        flat_route = torch.arange(n, device=hidden.device)
-        rec = torch.zeros(n, 4, dtype=torch.int32, device=hidden.device)
-        rec[:, 0] = local_e
-        rec[:, 1] = scores.reshape(-1).to(torch.float32).view(torch.int32)
-        rec[:, 2] = flat_route.to(torch.int32)
-        h2 = hidden.reshape(T, H)
-        h2 = h2 if h2.stride(-1) == 1 else h2.contiguous()
-        tok = torch.div(flat_route, K, rounding_mode="floor")
-        with collective_profile("ep_dispatch", value=hidden, mode="p2p", detail="routes"):
-            C.row_scatter(h2, tok, state.route_rank, state.route_row, rows.peer_ptrs, H * 2)
-            C.row_scatter(rec, flat_route, state.route_rank, state.route_row, recs.peer_ptrs, 16)
-            disp._barrier(rows)
-        R = state.recv_total
-        rh = rows.tensor[: R * H].view(R, H).clone()
-        rrec = recs.tensor[: R * 4].view(R, 4).clone()
-        state.recv_experts = rrec[:, 0].to(torch.int64)
-        state.recv_src_route = rrec[:, 2].to(torch.int64)
-        rs = rrec[:, 1].contiguous().view(torch.float32).to(scores.dtype)
-        ctx.disp, ctx.state, ctx.shape, ctx.sdtype = disp, state, (T, H), scores.dtype
-        ctx.sshape = scores.shape
-        return rh, rs
-
-    @staticmethod
-    def backward(ctx, g_h, g_s):
-        C = ext()
-        disp, state = ctx.disp, ctx.state
-        T, H = ctx.shape
-        K = state.top_k
-        rows, recs = disp.pool.next()
-        R = state.recv_total
-        if g_h is None:
-            g_h = torch.zeros(R, H, device=rows.tensor.device, dtype=torch.bfloat16)
-        if g_s is None:
-            g_s = torch.zeros(R, device=rows.tensor.device)
-        rows.tensor[: R * H].view(R, H).copy_(g_h.reshape(R, H))
-        rec = recs.tensor[: R * 4].view(R, 4)
-        rec.zero_()
-        rec[:, 0] = g_s.reshape(R).to(torch.float32).view(torch.int32)
-        with collective_profile("ep_dispatch", value=g_h, mode="p2p_grad", detail="routes"):
-            disp._barrier(rows)
-            dh = torch.empty(T, H, device=g_h.device, dtype=torch.bfloat16)
-            C.row_gather_sum(dh, state.route_rank, state.route_row, rows.peer_ptrs, H)
-            gs = torch.empty(T * K, 4, dtype=torch.int32, device=g_h.device)
-            C.row_gather(gs, state.route_rank, state.route_row, recs.peer_ptrs, 16)
-        dscores = gs[:, 0].contiguous().view(torch.float32).view(ctx.sshape).to(ctx.sdtype)
-        return dh, dscores, None, None, None, None
-
-
-class _CombineFn(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, y, disp, state):
-        C = ext()
-        R, H = y.shape
-        rows, _ = disp.pool.next()
-        rows.tensor[: R * H].view(R, H).copy_(y)
-        T = state.num_source_tokens
-        out = torch.empty(T, H, device=y.device, dtype=torch.bfloat16)
-        with collective_profile("ep_combine", value=y, mode="p2p", detail="routes"):
-            disp._barrier(rows)
-            C.row_gather_sum(out, state.route_rank, state.route_row, rows.peer_ptrs, H)
-        ctx.disp, ctx.state, ctx.R, ctx.ydtype = disp, state, R, y.dtype
-        return out
-
-    @staticmethod
-    def backward(ctx, g):
-        C = ext()
-        disp, state = ctx.disp, ctx.state
-        K = state.top_k
-        T, H = g.shape
-        rows, _ = disp.pool.next()
-        g2 = g if g.stride(-1) == 1 else g.contiguous()
-        flat_route = torch.arange(T * K, device=g.device)
-        tok = torch.div(flat_route, K, rounding_mode="floor")
-        with collective_profile("ep_combine", value=g, mode="p2p_grad", detail="routes"):
-            C.row_scatter(g2.to(torch.bfloat16), tok, state.route_rank, state.route_row, rows.peer_ptrs, H * 2)
-            disp._barrier(rows)
-        gy = rows.tensor[: ctx.R * H].view(ctx.R, H).clone().to(ctx.ydtype)
-        return gy, None, None
+    def gather_grad(self, handle: SymmBuffer, plan: RoutePlan, dx: torch.Tensor) -> None:
+        with collective_profile("ep_dispatch", value=dx, mode="p2p_grad", detail="routes"):
+            self._barrier(handle)
+            ext().moe_combine(dx, None, None, plan.route_owner, plan.route_row, list(handle.peer_ptrs), dx.shape[1])

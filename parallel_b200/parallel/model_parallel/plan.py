@@ -11,8 +11,10 @@ model_parallel/plan.py:9-143).
 from __future__ import annotations
 
 import fnmatch
-from dataclasses import dataclass, field
+import re
+from dataclasses import dataclass, field, fields
 from enum import Enum
+from functools import lru_cache
 from typing import Iterable
 
 
@@ -44,7 +46,7 @@ class ParameterPlacement:
     gradient_reduction: GradientReduction = GradientReduction.NONE
 
     def matches(self, name: str) -> bool:
-        return fnmatch.fnmatchcase(name, self.pattern)
+        return _pattern(self.pattern).match(name) is not None
 
 
 @dataclass(frozen=True)
@@ -56,6 +58,20 @@ class ModelParallelCapabilities:
     fsdp_composition: bool = False
     portable_checkpoint: bool = True
     sharded_checkpoint: bool = True
+
+
+# checkpoint_metadata() records these plan fields, in this order, then the placements
+_METADATA_FIELDS = ("model_type", "tensor_parallel_size", "expert_parallel_size", "expert_tensor_parallel_size",
+                    "sequence_parallel_size")
+
+
+def _plain(value):
+    return value.value if isinstance(value, Enum) else value
+
+
+@lru_cache(maxsize=None)
+def _pattern(glob: str) -> "re.Pattern":
+    return re.compile(fnmatch.translate(glob))
 
 
 @dataclass(frozen=True)
@@ -79,47 +95,53 @@ class ModelParallelPlan:
 
     @property
     def hf_plan(self) -> dict[str, str]:
-        return {r.pattern: r.style for r in self.module_rules}
+        return dict((rule.pattern, rule.style) for rule in self.module_rules)
+
+    def _first_match(self, name: str):
+        """Index of the first placement whose pattern matches ``name`` (the
+        table is ordered most-specific first), or None."""
+        cache = self.__dict__.setdefault("_match_cache", {})
+        if name not in cache:
+            cache[name] = next((i for i, pl in enumerate(self.parameter_placements)
+                                if _pattern(pl.pattern).match(name)), None)
+        return cache[name]
 
     def placement_for_parameter(self, name: str) -> ParameterPlacement:
-        for p in self.parameter_placements:
-            if p.matches(name):
-                return p
-        raise KeyError(f"Model-parallel plan does not classify parameter {name!r}")
+        index = self._first_match(name)
+        if index is None:
+            raise KeyError(f"no placement of the {self.model_type} plan matches parameter {name!r}")
+        return self.parameter_placements[index]
 
     def validate_parameter_coverage(self, names: Iterable[str]) -> None:
-        names = tuple(names)
-        unclassified = []
-        for n in names:
-            try:
-                self.placement_for_parameter(n)
-            except KeyError:
-                unclassified.append(n)
-        if unclassified:
-            raise RuntimeError("Model-parallel plan leaves parameters unclassified: " + ", ".join(unclassified))
-        missing = [p.pattern for p in self.parameter_placements if p.required and not any(p.matches(n) for n in names)]
-        if missing:
-            raise RuntimeError("Model-parallel plan expected parameters matching: " + ", ".join(missing))
+        """Every parameter must have a placement, and every required placement
+        must match at least one parameter."""
+        names = list(names)
+        orphans = [n for n in names if self._first_match(n) is None]
+        if orphans:
+            raise RuntimeError(f"the {self.model_type} plan has no placement for: {', '.join(orphans)}")
+        unmatched = [pl.pattern for pl in self.parameter_placements
+                     if pl.required and not any(_pattern(pl.pattern).match(n) for n in names)]
+        if unmatched:
+            raise RuntimeError(f"the model has no parameter for required plan entries: {', '.join(unmatched)}")
 
     def checkpoint_metadata(self) -> dict:
-        return {
-            "model_type": self.model_type,
-            "tensor_parallel_size": self.tensor_parallel_size,
-            "expert_parallel_size": self.expert_parallel_size,
-            "expert_tensor_parallel_size": self.expert_tensor_parallel_size,
-            "sequence_parallel_size": self.sequence_parallel_size,
-            "parameters": [
-                {"pattern": p.pattern, "parallelism": p.parallelism.value, "shard_dim": p.shard_dim,
-                 "required": p.required, "gradient_reduction": p.gradient_reduction.value}
-                for p in self.parameter_placements
-            ],
-        }
+        """Plan description stored with model-parallel checkpoints and compared
+        for equality when they are loaded (an interchange format)."""
+        meta = {key: getattr(self, key) for key in _METADATA_FIELDS}
+        meta["parameters"] = [{f.name: _plain(getattr(pl, f.name)) for f in fields(ParameterPlacement)}
+                              for pl in self.parameter_placements]
+        return meta
 
     def validate_runtime(self, pconfig) -> None:
-        if self.sequence_parallel_size not in (1, self.tensor_parallel_size):
-            raise ValueError("Sequence parallelism must be disabled or reuse the complete TP group")
-        if pconfig.dp_shard_size > 1 and not self.capabilities.fsdp_composition:
-            raise NotImplementedError(f"{self.model_type} model parallelism does not yet compose with FSDP; "
-                                      "set dp_shard=1")
-        if self.expert_tensor_parallel_size > 1 and not self.capabilities.expert_tensor_parallel:
-            raise NotImplementedError(f"{self.model_type} does not support expert tensor parallelism")
+        checks = (
+            (self.sequence_parallel_size not in (1, self.tensor_parallel_size), ValueError,
+             f"sequence parallel size {self.sequence_parallel_size} must be 1 or the TP size "
+             f"{self.tensor_parallel_size}"),
+            (pconfig.dp_shard_size > 1 and not self.capabilities.fsdp_composition, NotImplementedError,
+             f"the {self.model_type} plan does not compose with FSDP; use dp_shard=1"),
+            (self.expert_tensor_parallel_size > 1 and not self.capabilities.expert_tensor_parallel,
+             NotImplementedError, f"the {self.model_type} plan has no expert tensor parallelism"),
+        )
+        for failed, kind, message in checks:
+            if failed:
+                raise kind(message)

@@ -1,33 +1,50 @@
-"""Registry of plan builders keyed by ``config.model_type``
-(reference: parallel/parallel/engine/model_parallel/registry.py)."""
+"""Lookup of model-parallel plan builders by HF ``config.model_type``.
+
+Plan modules declare themselves with ``@register_model_parallel_plan(type)``
+(behaviour of ``parallel/parallel/engine/model_parallel/registry.py``).  A
+builder is ``(model_config, pconfig) -> ModelParallelPlan``.
+"""
 from __future__ import annotations
 
 from collections.abc import Callable
+from types import MappingProxyType
 
 from .plan import ModelParallelPlan
 
 PlanBuilder = Callable[[object, object], ModelParallelPlan]
-_BUILDERS: dict[str, PlanBuilder] = {}
+
+
+class _PlanTable:
+    def __init__(self):
+        self._builders: dict[str, PlanBuilder] = {}
+        self.view = MappingProxyType(self._builders)
+
+    def add(self, model_type: str, builder: PlanBuilder) -> None:
+        previous = self._builders.get(model_type)
+        if previous is not None and previous is not builder:
+            raise RuntimeError(f"model_type {model_type!r} already has a plan builder ({previous.__qualname__})")
+        self._builders[model_type] = builder
+
+
+_TABLE = _PlanTable()
 
 
 def register_model_parallel_plan(model_type: str):
-    def deco(builder: PlanBuilder) -> PlanBuilder:
-        if model_type in _BUILDERS:
-            raise RuntimeError(f"Duplicate model-parallel plan for {model_type}")
-        _BUILDERS[model_type] = builder
+    """Decorator: make ``builder`` the plan of ``model_type``."""
+    def bind(builder: PlanBuilder) -> PlanBuilder:
+        _TABLE.add(model_type, builder)
         return builder
 
-    return deco
-
-
-def build_model_parallel_plan(config, pconfig) -> ModelParallelPlan:
-    mt = getattr(config, "model_type", None)
-    builder = _BUILDERS.get(mt)
-    if builder is None:
-        raise NotImplementedError(f"Model parallelism does not support model_type={mt!r}; supported model types: "
-                                  + ", ".join(sorted(_BUILDERS)))
-    return builder(config, pconfig)
+    return bind
 
 
 def supported_model_types() -> tuple[str, ...]:
-    return tuple(sorted(_BUILDERS))
+    return tuple(sorted(_TABLE.view))
+
+
+def build_model_parallel_plan(config, pconfig) -> ModelParallelPlan:
+    model_type = getattr(config, "model_type", None)
+    if model_type not in _TABLE.view:
+        raise NotImplementedError(f"no model-parallel plan for model_type {model_type!r} "
+                                  f"(plans exist for: {', '.join(supported_model_types()) or 'none'})")
+    return _TABLE.view[model_type](config, pconfig)

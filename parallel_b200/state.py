@@ -1,21 +1,31 @@
-"""Process state, process-group init and the parallel topology.
+"""Launch environment, process-group start-up and the parallel topology.
 
-``world_size = dp_replicate x dp_shard x tp``; expert parallelism and
-sequence parallelism are folded onto the TP ranks (ep == tp, sp in {1, tp});
-context / pipeline / expert-tensor parallelism are reserved and rejected.
-The physical layout keeps TP ranks adjacent (strides dp_replicate: tp*dp_shard,
-tp: 1, dp_shard: tp) so TP traffic stays on neighbouring GPUs.
+Topology rules (behaviour of the reference's ``parallel/parallel/state.py:
+15-333``, which checkpoints, data sharding and RNG streams depend on):
 
-Same validation rules, mesh strides and RNG seeding policy as the reference
-(parallel/parallel/state.py:15-333).
+* ``world = dp_replicate x dp_shard x tp``.  Expert parallelism and sequence
+  parallelism run on the TP ranks (``ep == tp``, ``sp in {1, tp}``); context
+  parallelism, pipeline parallelism and expert-tensor parallelism are
+  reserved keys that must stay 1.
+* The device mesh has the named dimensions (dp_replicate, tp, dp_shard) in
+  that order, but ranks are laid out TP-innermost: global rank =
+  r * (tp * dp_shard) + s * tp + t for replica r, shard s, TP rank t, so a
+  TP group is a block of neighbouring GPUs.
+* RNG: model initialisation seeds ``seed + tp_rank``; training seeds python /
+  numpy with ``seed + data_rank`` and torch with ``seed + 1000 * data_rank +
+  pp_rank``, so TP ranks of one replica draw identical streams.
+
+The table ``_DIMENSIONS`` drives validation, the mesh and the size
+accessors; each rule of ``_RULES`` is one check with its own message.
 """
 from __future__ import annotations
 
 import os
 import random
+from dataclasses import dataclass
 from datetime import timedelta
 from enum import Enum
-from typing import Optional
+from typing import Callable, Optional
 
 import numpy as np
 import torch
@@ -26,6 +36,8 @@ from .utils import is_dist_initialized
 
 
 class Strategies(str, Enum):
+    """Names of the parallel dimensions (also the device-mesh dim names)."""
+
     DP_REPLICATE = "dp_replicate"
     DP_SHARD = "dp_shard"
     TP = "tp"
@@ -35,190 +47,226 @@ class Strategies(str, Enum):
     PP = "pp"
 
 
-_SUPPORTED_MESH_DIMS = (Strategies.DP_REPLICATE, Strategies.TP, Strategies.DP_SHARD)
-_SUPPORTED_MESH_DIM_NAMES = {d.value for d in _SUPPORTED_MESH_DIMS}
+# --------------------------------------------------------------------------- launch environment
+@dataclass(frozen=True)
+class LaunchEnv:
+    """The launcher's rank variables (torchrun / mp.spawn), read once."""
 
+    rank: int
+    world_size: int
+    local_rank: int
+    backend: Optional[str]
 
-class RuntimeState:
-    """Process-wide singleton of the launcher's rank environment."""
-
-    _state: dict = {}
-
-    def __init__(self, backend: str | None = None):
-        if self.initialized:
-            return
-        self._state["RANK"] = int(os.environ.get("RANK", 0))
-        self._state["WORLD_SIZE"] = int(os.environ.get("WORLD_SIZE", 1))
-        self._state["LOCAL_RANK"] = int(os.environ.get("LOCAL_RANK", 0))
-        self._state["backend"] = backend
+    @classmethod
+    def from_environ(cls, backend: Optional[str] = None) -> "LaunchEnv":
+        env = os.environ
+        return cls(int(env.get("RANK", 0)), int(env.get("WORLD_SIZE", 1)), int(env.get("LOCAL_RANK", 0)), backend)
 
     @property
-    def can_log(self):
+    def can_log(self) -> bool:
         return self.world_size <= 1 or self.rank == 0
 
-    @property
-    def local_rank(self):
-        return self._state.get("LOCAL_RANK", 0)
 
-    @property
-    def rank(self):
-        return self._state.get("RANK", 0)
+_LAUNCH: Optional[LaunchEnv] = None
 
-    @property
-    def world_size(self):
-        return self._state.get("WORLD_SIZE", 1)
 
-    @property
-    def backend(self):
-        return self._state.get("backend", None)
+def RuntimeState(backend: Optional[str] = None) -> LaunchEnv:  # noqa: N802 (kept as the public name)
+    """The process's ``LaunchEnv``; the first call (optionally naming the
+    backend) fixes it for the life of the process."""
+    global _LAUNCH
+    if _LAUNCH is None:
+        _LAUNCH = LaunchEnv.from_environ(backend)
+    return _LAUNCH
 
-    @property
-    def initialized(self):
-        return self._state != {}
+
+def reset_runtime_state() -> None:
+    """Forget the cached launch environment (tests)."""
+    global _LAUNCH
+    _LAUNCH = None
 
 
 def init_dist(cfg, timeout_s: float | None = None) -> None:
-    """Select the device and initialise the default process group."""
+    """Bind this process to its GPU and start the default process group (env
+    rendezvous) when the launcher started more than one rank."""
     device = cfg.config.device_type
-    assert device, "device needs to be set in config"
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if not device:
+        raise ValueError("config.device_type must be set (cuda or cpu)")
+    env = LaunchEnv.from_environ(cfg.config.backend)
     if device == "cuda":
-        torch.cuda.set_device(local_rank)
-    world_size = int(os.environ.get("WORLD_SIZE", "1"))
-    if world_size > 1 and not is_dist_initialized():
-        if cfg.config.backend == "nccl" and device != "cuda":
-            raise RuntimeError("nccl needs to be used with cuda devices")
-        kw = {}
-        if timeout_s is not None:
-            kw["timeout"] = timedelta(seconds=timeout_s)
-        if device == "cuda":
-            kw["device_id"] = torch.device("cuda", local_rank)
-        dist.init_process_group(backend=cfg.config.backend, **kw)
+        torch.cuda.set_device(env.local_rank)
+    if env.world_size <= 1 or is_dist_initialized():
+        return
+    if env.backend == "nccl" and device != "cuda":
+        raise RuntimeError(f"the nccl backend drives CUDA devices; config.device_type is {device!r}")
+    options = {}
+    if timeout_s is not None:
+        options["timeout"] = timedelta(seconds=timeout_s)
+    if device == "cuda":
+        options["device_id"] = torch.device("cuda", env.local_rank)
+    dist.init_process_group(backend=env.backend, **options)
+
+
+# --------------------------------------------------------------------------- topology table
+@dataclass(frozen=True)
+class _Dim:
+    strategy: Strategies
+    attr: str                # ParallelConfig attribute holding the size
+    role: str                # "mesh": own mesh dim; "folded": on the TP ranks; "reserved": must be 1
+
+
+_DIMENSIONS = (
+    _Dim(Strategies.DP_REPLICATE, "dp_replicate_size", "mesh"),
+    _Dim(Strategies.DP_SHARD, "dp_shard_size", "mesh"),
+    _Dim(Strategies.TP, "tp_size", "mesh"),
+    _Dim(Strategies.CP, "cp_size", "reserved"),
+    _Dim(Strategies.SP, "sp_size", "folded"),
+    _Dim(Strategies.EP, "ep_size", "folded"),
+    _Dim(Strategies.PP, "pp_size", "reserved"),
+)
+_MESH_ORDER = (Strategies.DP_REPLICATE, Strategies.TP, Strategies.DP_SHARD)
+
+
+def _size_rule(c: "ParallelConfig"):
+    bad = {k: v for k, v in c.sizes().items() if type(v) is not int or v < 1}
+    if bad:
+        return ValueError(f"parallel sizes must be positive integers; got {bad}")
+
+
+def _world_rule(c: "ParallelConfig"):
+    if c.total_size != c.world_size:
+        return ValueError(f"the parallel layout covers {c.total_size} ranks, which does not match the "
+                          f"{c.world_size} ranks of this job")
+
+
+def _sp_rule(c: "ParallelConfig"):
+    if c.sp_size not in (1, c.tp_size):
+        return ValueError(f"sequence parallelism runs on the TP ranks, so it needs sp == 1 or sp == tp "
+                          f"(sp={c.sp_size}, tp={c.tp_size})")
+
+
+def _reserved_rule(c: "ParallelConfig"):
+    on = {d.strategy.value: getattr(c, d.attr) for d in _DIMENSIONS
+          if d.role == "reserved" and getattr(c, d.attr) > 1}
+    if on:
+        return NotImplementedError(f"{on}: only data (replicate / shard) and tensor parallel dimensions, with "
+                                   "EP and SP on the TP ranks, are built")
+
+
+def _expert_tp_rule(c: "ParallelConfig"):
+    if c.expert_tp_size != 1:
+        return NotImplementedError(f"expert_tp={c.expert_tp_size}: experts are not tensor-parallel here, "
+                                   "expert_tp must be 1")
+
+
+def _ep_rule(c: "ParallelConfig"):
+    if c.ep_size > 1 and c.ep_size != c.tp_size:
+        return ValueError(f"expert parallelism runs on the TP ranks and needs tp == ep (tp={c.tp_size}, "
+                          f"ep={c.ep_size})")
+
+
+_RULES: tuple[Callable[["ParallelConfig"], Optional[Exception]], ...] = (
+    _size_rule, _world_rule, _sp_rule, _reserved_rule, _expert_tp_rule, _ep_rule)
 
 
 class ParallelConfig:
-    """Validated parallel sizes plus the device mesh built from them."""
+    """Validated parallel sizes of ``cfg.parallel`` plus the device mesh."""
 
     def __init__(self, cfg):
-        conf = cfg.parallel
-        self.dp_replicate_size = conf.dp_replicate
-        self.dp_shard_size = conf.dp_shard
-        self.tp_size = conf.tp
-        self.cp_size = conf.cp
-        self.sp_size = conf.sp
-        self.ep_size = conf.ep
-        self.expert_tp_size = conf.get("expert_tp", 1)
-        self.pp_size = conf.pp
+        section = cfg.parallel
+        for d in _DIMENSIONS:
+            setattr(self, d.attr, section.get(d.strategy.value, 1) if hasattr(section, "get")
+                    else getattr(section, d.strategy.value))
+        self.expert_tp_size = section.get("expert_tp", 1) if hasattr(section, "get") else 1
         self.device_mesh: Optional[DeviceMesh] = None
         self.device_type: Optional[str] = None
-        self.rank = dist.get_rank() if is_dist_initialized() else 0
-        self.local_rank = int(os.environ.get("LOCAL_RANK", 0))
-        self.world_size = dist.get_world_size() if is_dist_initialized() else 1
         self._device = None
-        if self.world_size > 1:
-            assert is_dist_initialized()
-        sizes = {
-            "dp_replicate": self.dp_replicate_size, "dp_shard": self.dp_shard_size, "tp": self.tp_size,
-            "cp": self.cp_size, "sp": self.sp_size, "ep": self.ep_size, "expert_tp": self.expert_tp_size,
-            "pp": self.pp_size,
-        }
-        invalid = {n: s for n, s in sizes.items() if not isinstance(s, int) or isinstance(s, bool) or s < 1}
-        if invalid:
-            raise ValueError(f"Parallel dimensions must be positive integers: {invalid}")
-        if self.total_size != self.world_size:
-            raise ValueError(
-                f"Parallel mesh size {self.total_size} does not match distributed world size {self.world_size}"
-            )
-        if self.sp_size not in (1, self.tp_size):
-            raise ValueError("Sequence parallelism reuses the TP ranks and requires sp == 1 or sp == tp")
-        unsupported = {n: s for n, s in sizes.items()
-                       if n not in _SUPPORTED_MESH_DIM_NAMES and n not in {"ep", "expert_tp", "sp"} and s > 1}
-        if unsupported:
-            raise NotImplementedError(
-                f"Only replicated, sharded, and tensor parallel mesh dimensions are implemented: {unsupported}"
-            )
-        if self.expert_tp_size != 1:
-            raise NotImplementedError("Expert tensor parallelism is not implemented yet; expert_tp must be 1")
-        if self.ep_size > 1 and self.tp_size != self.ep_size:
-            raise ValueError("Folded expert parallelism requires tp == ep")
+        joined = is_dist_initialized()
+        self.rank = dist.get_rank() if joined else 0
+        self.world_size = dist.get_world_size() if joined else 1
+        self.local_rank = int(os.environ.get("LOCAL_RANK", 0))
+        if self.world_size > 1 and not joined:
+            raise RuntimeError("a multi-rank job needs the process group started (init_dist) first")
+        for rule in _RULES:
+            problem = rule(self)
+            if problem is not None:
+                raise problem
 
-    # ---- sizes
-    @property
-    def dp_size(self):
-        return self.dp_replicate_size * self.dp_shard_size
+    def sizes(self) -> dict:
+        out = {d.strategy.value: getattr(self, d.attr) for d in _DIMENSIONS}
+        out["expert_tp"] = self.expert_tp_size
+        return out
 
+    # ------------------------------------------------------------------ derived sizes
     @property
-    def dp_enabled(self):
-        return self.dp_size > 1
-
-    @property
-    def model_parallel_size(self):
-        """Physical size of the rank group shared by attention TP and MoE EP."""
+    def model_parallel_size(self) -> int:
+        """Ranks of one TP group (shared by attention TP and MoE EP)."""
         return max(self.tp_size, self.ep_size)
 
     @property
-    def model_parallel_enabled(self):
+    def model_parallel_enabled(self) -> bool:
         return self.model_parallel_size > 1
 
     @property
-    def is_distributed(self):
-        return self.world_size > 1
+    def dp_size(self) -> int:
+        return self.dp_replicate_size * self.dp_shard_size
 
     @property
-    def is_main_process(self):
-        return self.rank == 0
+    def dp_enabled(self) -> bool:
+        return self.dp_size > 1
 
     @property
-    def data_rank(self):
-        return self._mesh_rank(Strategies.DP_REPLICATE) * self.dp_shard_size + self._mesh_rank(Strategies.DP_SHARD)
-
-    @property
-    def data_world_size(self):
+    def data_world_size(self) -> int:
         return self.dp_size
 
     @property
-    def total_size(self):
-        return (self.dp_replicate_size * self.dp_shard_size * self.model_parallel_size * self.cp_size
-                * self.pp_size)
+    def total_size(self) -> int:
+        return self.dp_size * self.model_parallel_size * self.cp_size * self.pp_size
 
-    def __repr__(self):
-        return (f"ParallelConfig(dp_replicate={self.dp_replicate_size}, dp_shard={self.dp_shard_size}, "
-                f"tp={self.tp_size}, cp={self.cp_size}, sp={self.sp_size}, ep={self.ep_size}, "
-                f"expert_tp={self.expert_tp_size}, pp={self.pp_size}, total={self.total_size})")
+    @property
+    def is_distributed(self) -> bool:
+        return self.world_size > 1
 
-    # ---- mesh
-    def get_mesh_dims(self):
-        dims = [x for x in self._supported_mesh_dims() if x[1] > 1]
-        return tuple(zip(*dims))
+    @property
+    def is_main_process(self) -> bool:
+        return self.rank == 0
 
-    def _supported_mesh_dims(self):
-        return [
-            (Strategies.DP_REPLICATE, self.dp_replicate_size),
-            (Strategies.TP, self.tp_size),
-            (Strategies.DP_SHARD, self.dp_shard_size),
-        ]
+    @property
+    def data_rank(self) -> int:
+        """Index of this rank's data stream (TP ranks of a replica share it)."""
+        return self._mesh_rank(Strategies.DP_REPLICATE) * self.dp_shard_size + self._mesh_rank(Strategies.DP_SHARD)
 
-    def _physical_mesh_strides(self, mesh_dim_names):
-        strides = {
-            Strategies.DP_REPLICATE: self.tp_size * self.dp_shard_size,
-            Strategies.TP: 1,
-            Strategies.DP_SHARD: self.tp_size,
-        }
-        return tuple(strides[n] for n in mesh_dim_names)
+    def __repr__(self) -> str:
+        body = ", ".join(f"{k}={v}" for k, v in self.sizes().items())
+        return f"ParallelConfig({body}, total={self.total_size})"
+
+    # ------------------------------------------------------------------ mesh
+    def _mesh_sizes(self) -> dict:
+        return {Strategies.DP_REPLICATE: self.dp_replicate_size, Strategies.TP: self.tp_size,
+                Strategies.DP_SHARD: self.dp_shard_size}
+
+    def _rank_strides(self) -> dict:
+        """Global-rank step of each mesh dimension (TP innermost)."""
+        return {Strategies.TP: 1, Strategies.DP_SHARD: self.tp_size,
+                Strategies.DP_REPLICATE: self.tp_size * self.dp_shard_size}
 
     def get_mesh_layout(self):
-        """(semantic dim names, shape, physical rank strides); TP ranks adjacent."""
-        names, shape = tuple(zip(*self._supported_mesh_dims()))
-        return names, shape, self._physical_mesh_strides(names)
+        """(dim names, sizes, physical rank strides) in mesh order."""
+        sizes, strides = self._mesh_sizes(), self._rank_strides()
+        return _MESH_ORDER, tuple(sizes[d] for d in _MESH_ORDER), tuple(strides[d] for d in _MESH_ORDER)
 
-    def _coord_to_rank(self, coord, strides):
-        return sum(i * s for i, s in zip(coord, strides))
+    def get_mesh_dims(self):
+        """(names, sizes) of the mesh dimensions larger than 1."""
+        sizes = self._mesh_sizes()
+        return tuple(zip(*[(d, sizes[d]) for d in _MESH_ORDER if sizes[d] > 1]))
 
-    def _physical_mesh(self, names, shape, strides):
-        mesh = torch.empty(shape, dtype=torch.int64)
-        for coord in np.ndindex(*shape):
-            mesh[coord] = self._coord_to_rank(coord, strides)
-        return mesh
+    def _physical_mesh(self, names, shape, strides) -> torch.Tensor:
+        """Global rank at every mesh coordinate: sum over dims of index x stride."""
+        table = np.zeros(shape, dtype=np.int64)
+        for axis, (size, stride) in enumerate(zip(shape, strides)):
+            index_shape = [1] * len(shape)
+            index_shape[axis] = size
+            table = table + np.arange(size, dtype=np.int64).reshape(index_shape) * stride
+        return torch.from_numpy(table)
 
     def set_device_mesh(self, device_type: str):
         self.device_type = device_type
@@ -226,51 +274,49 @@ class ParallelConfig:
             self.device_mesh = None
             return None
         names, shape, strides = self.get_mesh_layout()
-        mesh = self._physical_mesh(names, shape, strides)
-        self.device_mesh = DeviceMesh(device_type, mesh, mesh_dim_names=tuple(n.value for n in names))
+        self.device_mesh = DeviceMesh(device_type, self._physical_mesh(names, shape, strides),
+                                      mesh_dim_names=tuple(d.value for d in names))
         return self.device_mesh
 
     @property
-    def device(self):
+    def device(self) -> torch.device:
         if self._device is None:
             self._device = (torch.device("cuda", self.local_rank) if self.device_type == "cuda"
                             else torch.device("cpu"))
         return self._device
 
-    def _mesh_rank(self, dim_name) -> int:
-        name = dim_name.value if isinstance(dim_name, Strategies) else dim_name
-        if self.device_mesh is not None and name in self.device_mesh.mesh_dim_names:
-            return self.device_mesh.get_local_rank(name)
-        return 0
+    def _mesh_rank(self, dim) -> int:
+        name = Strategies(dim).value
+        mesh = self.device_mesh
+        if mesh is None or name not in (mesh.mesh_dim_names or ()):
+            return 0
+        return mesh.get_local_rank(name)
 
-    def group(self, dim_name):
-        """The process group of a mesh dimension, or None if the dim is size 1."""
-        name = dim_name.value if isinstance(dim_name, Strategies) else dim_name
-        if self.device_mesh is None or name not in self.device_mesh.mesh_dim_names:
+    def group(self, dim):
+        """Process group of a mesh dimension, or None where it has size 1."""
+        name = Strategies(dim).value
+        mesh = self.device_mesh
+        if mesh is None or name not in (mesh.mesh_dim_names or ()):
             return None
-        return self.device_mesh.get_group(name)
+        return mesh.get_group(name)
 
-    def dim_size(self, dim_name) -> int:
-        name = dim_name.value if isinstance(dim_name, Strategies) else dim_name
-        return {"dp_replicate": self.dp_replicate_size, "dp_shard": self.dp_shard_size,
-                "tp": self.tp_size}.get(name, 1)
+    def dim_size(self, dim) -> int:
+        return self._mesh_sizes().get(Strategies(dim), 1)
 
-    # ---- RNG policy
-    def model_init_rngs(self, seed: int = 42):
-        """TP ranks get different init seeds."""
-        init_seed = seed + self._mesh_rank(Strategies.TP)
-        torch.manual_seed(init_seed)
-        if self.device_type == "cuda":
-            torch.cuda.manual_seed_all(init_seed)
-
-    def model_train_rngs(self, seed: int = 42):
-        """DP ranks differ (different data); TP ranks of one replica agree."""
-        dp_rank = self.data_rank
-        pp_rank = self._mesh_rank(Strategies.PP)
-        data_seed = seed + dp_rank
-        random.seed(data_seed)
-        np.random.seed(data_seed)
-        torch_seed = seed + dp_rank * 1000 + pp_rank
+    # ------------------------------------------------------------------ RNG policy
+    def _seed_all(self, torch_seed: int, host_seed: Optional[int] = None) -> None:
+        if host_seed is not None:
+            random.seed(host_seed)
+            np.random.seed(host_seed)
         torch.manual_seed(torch_seed)
         if self.device_type == "cuda":
             torch.cuda.manual_seed_all(torch_seed)
+
+    def model_init_rngs(self, seed: int = 42) -> None:
+        """Initialisation draws differ between TP ranks (each builds its own shards)."""
+        self._seed_all(seed + self._mesh_rank(Strategies.TP))
+
+    def model_train_rngs(self, seed: int = 42) -> None:
+        """Training draws differ between data streams and agree within a TP group."""
+        data = self.data_rank
+        self._seed_all(seed + 1000 * data + self._mesh_rank(Strategies.PP), host_seed=seed + data)

@@ -77,7 +77,7 @@ def run_sp(collectives, data, steps_grads, moe=False, sp=True):
     eng = ParallelEngine(m, None, pc, cfg, pc.device, mp_plan=plan)
     ctx0 = eng.model.model.layers[0]._ctx
     if moe and sp:
-        fused = type(ctx0.expert_runtime.dispatcher).__name__ == "P2PTokenDispatcher"
+        fused = type(ctx0.expert_runtime.transport).__name__ == "PeerExpertTransport"
     elif moe:
         fused = getattr(ctx0.expert_runtime, "fused", None) is not None
     else:

@@ -50,10 +50,13 @@ def test_train_step_accumulates_stacked_micro_batches():
         torch.testing.assert_close(p, q, rtol=0, atol=0, msg=n)
 
 
-def test_graph_capture_refuses_moe_models():
+def test_graph_capture_accepts_moe_models_and_needs_cuda():
+    """MoE routing is device-resident, so an MoE engine is not refused for
+    being MoE; on a CPU device the capture is refused for the device."""
     from parallel_b200.models.config import resolve_config
     from parallel_b200.models.qwen3 import build_model
     from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.parallel.graph_step import capture_unsupported
     from parallel_b200.state import ParallelConfig
 
     cfg = cpu_cfg()
@@ -61,7 +64,8 @@ def test_graph_capture_refuses_moe_models():
     pc.set_device_mesh("cpu")
     m = build_model(resolve_config("tiny-qwen3-moe"), dtype=torch.float32, seed=0)
     eng = ParallelEngine(m, None, pc, cfg, torch.device("cpu"))
-    with pytest.raises(NotImplementedError, match="MoE"):
+    assert capture_unsupported(eng) is None
+    with pytest.raises(NotImplementedError, match="CUDA device"):
         eng.enable_graph_capture()
     assert eng._graph_pending is None
 
@@ -95,9 +99,10 @@ def test_capture_unsupported_names_each_host_side_decision():
 
     from parallel_b200.parallel.graph_step import capture_unsupported
 
-    def eng(moe=False, mp=False, scaler=False, fsdp=True, offload=False, unused=False, rep=1, fused=True):
+    def eng(moe=False, mp=False, scaler=False, fsdp=True, offload=False, unused=False, rep=1, fused=True,
+            experts=128):
         opt = NS(enable_graph_hyper=lambda d: None) if fused else NS()
-        return NS(model=NS(config=NS(is_moe=moe)), mp_wrapper=NS(is_active=mp),
+        return NS(model=NS(config=NS(is_moe=moe, num_experts=experts, hidden_size=2048)), mp_wrapper=NS(is_active=mp),
                   grad_scaler=NS(is_enabled=lambda: scaler),
                   fsdp_wrapper=NS(is_active=fsdp, cpu_offload=offload, find_unused_parameters=unused),
                   pconfig=NS(dp_replicate_size=rep), optimizer=opt)
@@ -105,7 +110,8 @@ def test_capture_unsupported_names_each_host_side_decision():
     assert capture_unsupported(eng()) is None
     assert capture_unsupported(eng(fsdp=True, rep=2)) is None          # hybrid: bucket all-reduce, capturable
     assert capture_unsupported(eng(fsdp=False)) is None                 # single device
-    assert "MoE" in capture_unsupported(eng(moe=True))
+    assert capture_unsupported(eng(moe=True)) is None                   # device-resident routing
+    assert "MoE" in capture_unsupported(eng(moe=True, experts=512))
     assert "model parallelism" in capture_unsupported(eng(mp=True))
     assert "fp16" in capture_unsupported(eng(scaler=True))
     assert "cpu_offload" in capture_unsupported(eng(offload=True))

@@ -464,42 +464,6 @@ def test_linear_wgrad_splitk_policy():
     assert _rel_err(acc, g.float().t() @ x.float() + 1.0) < 1e-3
 
 
-def test_grouped_expert_gemms_match_fp32():
-    """_ExpertsFn on the grouped tcgen05 GEMM (uneven and empty experts)
-    against an fp32 per-expert restatement, forward and backward."""
-    from parallel_b200.ops.moe import _ExpertsFn
-
-    torch.manual_seed(9)
-    E, H, I = 8, 256, 384
-    counts = [0, 5, 130, 1, 0, 256, 64, 200]
-    N = sum(counts)
-    xs = (torch.randn(N, H, device="cuda") * 0.5).to(torch.bfloat16).requires_grad_(True)
-    scores = torch.rand(N, device="cuda").requires_grad_(True)
-    w_gu = (torch.randn(E, 2 * I, H, device="cuda") / math.sqrt(H)).to(torch.bfloat16).requires_grad_(True)
-    w_d = (torch.randn(E, H, I, device="cuda") / math.sqrt(I)).to(torch.bfloat16).requires_grad_(True)
-    ys = _ExpertsFn.apply(xs, scores, w_gu, w_d, counts)
-    g = torch.randn_like(ys)
-    ys.backward(g)
-    _check_no_device_error()
-    xf, sf = xs.detach().float().requires_grad_(True), scores.detach().clone().requires_grad_(True)
-    guf, df = w_gu.detach().float().requires_grad_(True), w_d.detach().float().requires_grad_(True)
-    outs, r = [], 0
-    for e, n in enumerate(counts):
-        if n == 0:
-            continue
-        ge, ue = (xf[r:r + n] @ guf[e].t()).chunk(2, dim=-1)
-        outs.append(((torch.nn.functional.silu(ge) * ue) @ df[e].t()) * sf[r:r + n, None])
-        r += n
-    ref = torch.cat(outs)
-    ref.backward(g.float())
-    assert _rel_err(ys, ref) < 2e-2
-    assert _rel_err(xs.grad, xf.grad) < 3e-2
-    assert _rel_err(scores.grad, sf.grad) < 3e-2
-    assert _rel_err(w_gu.grad, guf.grad) < 3e-2
-    assert _rel_err(w_d.grad, df.grad) < 3e-2
-    assert w_gu.grad[0].abs().max().item() == 0 and w_d.grad[4].abs().max().item() == 0  # empty experts
-
-
 @pytest.mark.parametrize("T,E,K,renorm", [(1000, 128, 8, True), (333, 60, 4, False), (64, 256, 16, True)])
 def test_router_matches_torch(T, E, K, renorm):
     """Fused softmax / top-k / renorm / histogram and its backward against fp32 PyTorch."""

@@ -13,6 +13,14 @@ def _pair(name, seed=0):
 
     cfg = resolve_config(name)
     ref = build_model(cfg, dtype=torch.float32, seed=seed)
+    if cfg.is_moe:
+        # spread the router logits (x30) so bf16 rounding cannot flip near-tie
+        # top-k choices between the fp32 and bf16 models: both then route
+        # every token to the same experts and all gradients must agree
+        with torch.no_grad():
+            for n, p in ref.named_parameters():
+                if n.endswith("mlp.gate.weight"):
+                    p.mul_(30.0)
     gpu = build_model(cfg, dtype=torch.bfloat16, seed=seed)
     gpu.load_state_dict({k: v.to(torch.bfloat16) for k, v in ref.state_dict().items()})
     gpu.to("cuda")
@@ -38,11 +46,9 @@ def test_cuda_model_matches_fp32(name):
     gp = dict(gpu.named_parameters())
     for n, p in ref.named_parameters():
         err = _rel(gp[n].grad.cpu(), p.grad)
-        # bf16 rounding flips near-tie top-k routing decisions, so parameters
-        # downstream of the router differ from fp32 by ~0.15-0.2 even in the
-        # plain PyTorch bf16 path; everything else must match tightly
-        routed = cfg.is_moe and (".mlp." in n or "post_attention_layernorm" in n)
-        assert err < (0.3 if routed else 8e-2), (n, err)
+        # the scaled router makes the MoE loss more sensitive to bf16 rounding
+        # upstream of it, hence a uniform 0.1 there (0.08 for the dense model)
+        assert err < (1e-1 if cfg.is_moe else 8e-2), (n, err)
 
 
 def test_engine_trains_on_gpu():

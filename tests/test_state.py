@@ -3,7 +3,7 @@ import pytest
 import torch
 
 from parallel_b200.config import Config
-from parallel_b200.state import ParallelConfig, RuntimeState, Strategies
+from parallel_b200.state import ParallelConfig, RuntimeState, Strategies, reset_runtime_state
 
 
 def _config(**overrides):
@@ -21,8 +21,11 @@ def _fake_world(monkeypatch, n):
 
 def test_runtime_state_defaults_to_single_process(monkeypatch):
     monkeypatch.delenv("WORLD_SIZE", raising=False)
-    RuntimeState._state = {}
-    assert RuntimeState().world_size == 1
+    reset_runtime_state()
+    env = RuntimeState()
+    assert env.world_size == 1 and env.rank == 0 and env.can_log
+    assert RuntimeState(backend="nccl") is env  # fixed by the first call
+    reset_runtime_state()
 
 
 def test_rejects_mesh_world_size_mismatch():

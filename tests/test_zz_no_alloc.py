@@ -35,17 +35,21 @@ def _rel(a, b):
     return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
 
 
-def _call(fn, q, k, v, o, do, lse, dq, dk, dv, B, S, nq, nkv, scale):
+def _call(fn, q, k, v, o, do, lse, dq, dk, dv, B, S, nq, nkv, scale, causal):
     stream = torch.cuda.current_stream().cuda_stream
     return fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr(), dq.data_ptr(),
               dk.data_ptr(), dv.data_ptr(), q.stride(0), k.stride(0), v.stride(0), o.stride(0), do.stride(0),
-              dq.stride(0), dk.stride(0), dv.stride(0), B, S, nq, nkv, 128, scale, 1, stream)
+              dq.stride(0), dk.stride(0), dv.stride(0), B, S, nq, nkv, 128, scale, int(causal), stream)
 
 
-def test_noalloc_matches_allocating_entry_point():
+# S = 200 ends partway through a 128-row tile, which exercises the padding of
+# the per-row scratch and the bounds of the tiled loads
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("S", [256, 200])
+def test_noalloc_matches_allocating_entry_point(causal, S):
     C, lib, fn = _lib()
     torch.manual_seed(11)
-    B, S, nq, nkv, D = 2, 256, 4, 2, 128
+    B, nq, nkv, D = 2, 4, 2, 128
     T = B * S
     scale = 1.0 / math.sqrt(D)
     q = torch.randn(T, nq * D, device="cuda").to(torch.bfloat16)
@@ -53,17 +57,17 @@ def test_noalloc_matches_allocating_entry_point():
     v = torch.randn(T, nkv * D, device="cuda").to(torch.bfloat16)
     o = torch.empty_like(q)
     lse = torch.zeros(B * nq * S + 128, device="cuda")
-    C.attn_fwd(q, k, v, o, lse, B, S, nq, nkv, scale, True)
+    C.attn_fwd(q, k, v, o, lse, B, S, nq, nkv, scale, causal)
     do = torch.randn_like(q)
     # regular (allocating) entry point
     delta = torch.empty(2 * (B * nq * S + 128), device="cuda")
     acc = torch.empty(T, nq * D, device="cuda")
     ref_dq, ref_dk, ref_dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    C.attn_bwd(q, k, v, o, do, lse, delta, acc, ref_dq, ref_dk, ref_dv, B, S, nq, nkv, scale, True)
+    C.attn_bwd(q, k, v, o, do, lse, delta, acc, ref_dq, ref_dk, ref_dv, B, S, nq, nkv, scale, causal)
     lse_exact = lse[: B * nq * S].clone()  # no padding needed by the allocation-free variant
     for _ in range(2):
         dq, dk, dv = torch.full_like(q, 7.0), torch.full_like(k, 7.0), torch.full_like(v, 7.0)
-        rc = _call(fn, q, k, v, o, do, lse_exact, dq, dk, dv, B, S, nq, nkv, scale)
+        rc = _call(fn, q, k, v, o, do, lse_exact, dq, dk, dv, B, S, nq, nkv, scale, causal)
         assert rc == 0, lib.pb_attention_bwd_noalloc_last_error().decode()
         torch.cuda.synchronize()
         assert lib.pb_attention_bwd_noalloc_device_status() == 0
