@@ -50,6 +50,9 @@ def parse():
                     help="tensor-parallel size (model-parallel configs; dp_shard = gpus / tp; eager steps)")
     ap.add_argument("--sp", action="store_true", help="sequence parallelism over the TP group")
     ap.add_argument("--ep", action="store_true", help="expert parallelism over the TP group (MoE models)")
+    ap.add_argument("--router-skew", type=float, default=0.0,
+                    help="MoE: add a per-expert router logit offset drawn from N(0, skew^2) (same on every rank) "
+                         "to skew the routing (the skewed-router workload uses 2.0)")
     return ap.parse_args()
 
 
@@ -292,6 +295,11 @@ def run_ours(args, rank, world, local):
             model._layout_fused_weights()
         model.train()
         engine = ParallelEngine(model, None, pconfig, cfg, device)
+    if args.router_skew > 0 and mcfg.is_moe:
+        bias = torch.randn(mcfg.num_experts, generator=torch.Generator().manual_seed(2024)) * args.router_skew
+        for name, mod in model.named_modules():
+            if name.endswith("mlp.gate"):
+                mod.logit_bias = bias.to(device)
     pconfig.model_train_rngs(seed=42)
     B, S, V = args.batch, args.seq, mcfg.vocab_size
     # ranks of one TP group train on the same batch (data parallelism is across groups)
@@ -510,7 +518,7 @@ def main():
                    "parallelism": parallelism_name(args, world),
                    "activation_checkpoint": world > 1, "overlap_backward_reductions": True,
                    "l2": "working set (weights + activations, several GB) exceeds the 126 MB L2; no flush",
-                   **extra},
+                   **({"router_skew": args.router_skew} if args.router_skew else {}), **extra},
         "clocks": clk,
         "e2e": e2e,
         "gpu_launches": launches,

@@ -146,9 +146,14 @@ class TopKRouter(nn.Module):
         self.num_experts = cfg.num_experts
         self.norm_topk_prob = cfg.norm_topk_prob
         self.weight = nn.Parameter(torch.zeros(cfg.num_experts, cfg.hidden_size))
+        # optional per-expert logit offset (not part of the model's state: a
+        # benchmark knob that skews routing, e.g. N(0, 2) for the skewed-router
+        # workload); None means the plain HF router
+        self.logit_bias: torch.Tensor | None = None
 
     def forward(self, x):
-        return MoE.route(x.reshape(-1, x.shape[-1]), self.weight, self.top_k, self.norm_topk_prob)
+        return MoE.route(x.reshape(-1, x.shape[-1]), self.weight, self.top_k, self.norm_topk_prob,
+                         logit_bias=self.logit_bias)
 
 
 class Experts(nn.Module):

@@ -74,12 +74,17 @@ def _router_kernel_ok(logits: torch.Tensor, top_k: int) -> bool:
             and 1 <= logits.shape[1] <= 256 and 1 <= top_k <= min(16, logits.shape[1]))
 
 
-def route(x2: torch.Tensor, w: torch.Tensor, top_k: int, norm_topk_prob: bool, counts: torch.Tensor | None = None):
+def route(x2: torch.Tensor, w: torch.Tensor, top_k: int, norm_topk_prob: bool, counts: torch.Tensor | None = None,
+          logit_bias: torch.Tensor | None = None):
     """Returns (probs [T, E] fp32 softmax, top-k weights [T, k], top-k index [T, k]).
-    On CUDA ``counts`` (int32 [E]), when given, accumulates the route histogram."""
+    On CUDA ``counts`` (int32 [E]), when given, accumulates the route histogram.
+    ``logit_bias`` ([E], optional) is added to the logits (a benchmark knob
+    that skews the routing; Qwen3-MoE routers have no bias)."""
     from .functional import linear as _linear
 
     logits = _linear(x2.contiguous(), w) if (x2.is_cuda and _gemm_ok(x2, w)) else F.linear(x2, w)
+    if logit_bias is not None:
+        logits = logits + logit_bias.to(logits.dtype)
     if _router_kernel_ok(logits, top_k):
         return _RouterFn.apply(logits, top_k, bool(norm_topk_prob), counts)
     probs = torch.softmax(logits, dim=-1, dtype=torch.float32)
