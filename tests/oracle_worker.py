@@ -33,7 +33,7 @@ def build_engine(cfg, pc):
     from parallel_b200.parallel.engine import ParallelEngine
 
     model, plan = load_causal_lm(cfg, pc, dtype=torch.bfloat16)
-    if plan is None and pc.dp_shard_size <= 1:
+    if plan is not None or pc.dp_shard_size <= 1:  # FSDP places its own shards
         model.to(pc.device)
     return ParallelEngine(model, None, pc, cfg, pc.device, mp_plan=plan)
 
