@@ -32,8 +32,11 @@ reductions and gathers of that step have finished.
 MoE layers are capturable: their routing plan, expert GEMM tile counts and
 exchange sizes live on the device (``ops.moe.routed_experts``).
 
-Not capturable (the runner refuses them, ``capture_unsupported``): model
-parallelism (the fused sequence-parallel kernels use host-side flag targets), fp16 loss scaling (host decisions), CPU offload
+Model parallelism is capturable too: the NVLink kernels of TP / SP / EP wait
+on device epochs and per-call counters that are reset on the stream.
+
+Not capturable (the runner refuses them, ``capture_unsupported``): expert
+parallelism on NCCL all-to-alls (host-read split sizes), fp16 loss scaling (host decisions), CPU offload
 (host optimizer), usage bitmaps read on the host (FSDP with
 find_unused_parameters, DP-replicate without FSDP), CPU devices.
 """
@@ -50,8 +53,10 @@ def capture_unsupported(engine) -> str | None:
     cfg = getattr(engine.model, "config", None)
     if getattr(cfg, "is_moe", False) and not (1 <= cfg.num_experts <= 256 and cfg.hidden_size % 8 == 0):
         return "MoE models whose routing cannot run on the device (more than 256 experts)"
-    if engine.mp_wrapper.is_active:
-        return "model parallelism (the fused sequence-parallel kernels take host-side flag targets)"
+    runtime = getattr(engine.mp_wrapper, "expert_runtime", None) if engine.mp_wrapper.is_active else None
+    if runtime is not None and getattr(runtime, "dispatcher", None) is not None \
+            and getattr(runtime, "transport", "local") is None:
+        return "expert parallelism on NCCL all-to-alls (their split sizes are read on the host)"
     if engine.grad_scaler.is_enabled():
         return "fp16 loss scaling (its skip / rescale decisions are taken on the host)"
     if fsdp.is_active and fsdp.cpu_offload:

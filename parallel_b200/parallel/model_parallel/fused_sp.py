@@ -91,7 +91,6 @@ class FusedSequenceParallel:
         self.ag = []  # 2 x SymmBuffer [rows_local, cols] (this rank's shard)
         self.rs = []  # 2 x SymmBuffer [world * rows_local, cols] (one slot per sender)
         self.flags = []
-        self.flag_calls = [0, 0]
         self.n_ag = 0
         self.n_rs = 0
 
@@ -159,8 +158,10 @@ class FusedSequenceParallel:
                     ext().gemm(x_full, b, out, False, b_mn, EPI_STORE_BF16, 1.0)
             self.n_ag += 1
             return out, x_full
-        self.flag_calls[k] += 1
-        target = self.flag_calls[k] * _PIECES_PER_BLOCK
+        # per-call block counters: zeroed on the stream, so the target is a
+        # constant and a captured CUDA graph replays the same launch
+        self.flags[k].zero_()
+        target = _PIECES_PER_BLOCK
         with collective_profile("sp_all_gather_gemm", value=x_local, mode="fused", flops=2.0 * T * K * n_cols,
                                 link_bytes=(self.world - 1) * rows_local * K * 2):
             buf.barrier(0, self.limit_s)

@@ -71,11 +71,11 @@ def main(argv=None):
         token_bytes = get_token_bytes(tokenizer)
     pconfig.model_train_rngs(seed=seed)
     # engine.compile: the whole training step is captured as a CUDA graph
-    # (ParallelEngine.enable_graph_capture) - FSDP and DP-replicate included,
-    # which the reference's torch.compile path refuses (train.py:45-48)
+    # (ParallelEngine.enable_graph_capture) - FSDP, DP-replicate and model
+    # parallelism on the NVLink data plane included, which the reference's
+    # torch.compile path refuses (train.py:45-66); enable_graph_capture names
+    # anything that cannot be captured
     graph_step = bool(cfg.engine.compile)
-    if graph_step and pconfig.model_parallel_enabled:
-        raise NotImplementedError("engine.compile is not yet supported with folded model parallelism")
     if graph_step and cfg.engine.get("collective_profiling", False):
         raise NotImplementedError("engine.compile replays the step as one graph; per-collective profiling needs "
                                   "eager steps")

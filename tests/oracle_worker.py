@@ -38,6 +38,30 @@ def build_engine(cfg, pc):
     return ParallelEngine(model, None, pc, cfg, pc.device, mp_plan=plan)
 
 
+def graph_vs_eager(cfg, pc, tmp, rank):
+    """The whole-step CUDA graph (engine.compile's path: one eager step on the
+    capture stream, then capture and replay) against eager steps on the same
+    four batches."""
+    g = torch.Generator().manual_seed(77)
+    batches = [torch.randint(0, 2048, (B * pc.data_world_size, S + 1), generator=g) for _ in range(4)]
+    runs = {}
+    for mode in ("eager", "graph"):
+        eng = build_engine(cfg, pc)
+        if mode == "graph":
+            eng.enable_graph_capture(warmup_steps=1)
+        losses = []
+        for tok in batches:
+            mine = tok[pc.data_rank * B:(pc.data_rank + 1) * B].cuda()
+            loss = eng.train_step(mine[:, :-1], mine[:, 1:])
+            losses.append(float(eng.reduce_loss(loss)))
+        runs[mode] = (losses, eng.state_dict(), eng._graph is not None)
+        eng.release_graph()
+    if rank == 0:
+        torch.save(runs, os.path.join(tmp, "graph_result.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     from parallel_b200.config import from_dotlist, load_cfg, merge
     from parallel_b200.ops._ext import check_device_errors
@@ -61,6 +85,8 @@ def main():
     pc.set_device_mesh("cuda")
     dp = pc.data_world_size
     batches = data(world, dp)
+    if os.environ.get("PB_ORACLE_GRAPH") == "1":
+        return graph_vs_eager(cfg, pc, tmp, rank)
     eng = build_engine(cfg, pc)
     losses, norms = [], []
     for tok in batches:

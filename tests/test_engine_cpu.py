@@ -112,7 +112,10 @@ def test_capture_unsupported_names_each_host_side_decision():
     assert capture_unsupported(eng(fsdp=False)) is None                 # single device
     assert capture_unsupported(eng(moe=True)) is None                   # device-resident routing
     assert "MoE" in capture_unsupported(eng(moe=True, experts=512))
-    assert "model parallelism" in capture_unsupported(eng(mp=True))
+    assert capture_unsupported(eng(mp=True)) is None                    # NVLink TP / SP / EP
+    nccl_ep = eng(mp=True)
+    nccl_ep.mp_wrapper.expert_runtime = NS(dispatcher=object(), transport=None)
+    assert "all-to-all" in capture_unsupported(nccl_ep)
     assert "fp16" in capture_unsupported(eng(scaler=True))
     assert "cpu_offload" in capture_unsupported(eng(offload=True))
     assert "find_unused" in capture_unsupported(eng(unused=True))

@@ -10,7 +10,10 @@ Tolerances are the reference's GPU-test tolerances (loss 5e-2 / 5e-3,
 parameters 5e-2 / 5e-3, gradient norm 2e-2 relative;
 ``tests/gpu/test_distributed_gpu.py`` of the reference).  The MoE model's
 router weights are scaled so that bf16 rounding cannot flip a near-tie top-k
-routing decision between the bf16 GPU run and the fp32 oracle."""
+routing decision between the bf16 GPU run and the fp32 oracle.
+
+The graph cases replay the whole model-parallel step as one CUDA graph and
+compare it with eager steps of the same engine configuration."""
 import os
 import subprocess
 import sys
@@ -114,3 +117,34 @@ def test_tp_sp_2gpu_matches_single_process(tmp_path):
 @pytest.mark.parametrize("overlap", ["true", "false"])
 def test_moe_tp_ep_sp_fsdp_4gpu_matches_single_process(tmp_path, overlap):
     _run(tmp_path, "moe_tp_ep_sp_fsdp", 4, overlap=overlap, port=29604 if overlap == "true" else 29605)
+
+
+def _graph_run(tmp_path, case, world, port):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    sys.path.insert(0, HERE)
+    import oracle_worker as W
+
+    _save_model(str(tmp_path / "model"), W.CASES[case][0])
+    env = dict(os.environ, PB_ORACLE_CASE=case, PB_ORACLE_TMP=str(tmp_path), PB_ORACLE_GRAPH="1",
+               NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", str(world), "--master-addr",
+           "127.0.0.1", "--master-port", str(port), os.path.join(HERE, "oracle_worker.py")]
+    subprocess.run(cmd, env=env, check=True, timeout=900)
+    runs = torch.load(tmp_path / "graph_result.pt", weights_only=False)
+    (l_e, s_e, _), (l_g, s_g, captured) = runs["eager"], runs["graph"]
+    assert captured, "the graph engine never captured its step"
+    torch.testing.assert_close(torch.tensor(l_g), torch.tensor(l_e), rtol=2e-3, atol=2e-3)
+    worst = max(_rel(s_g[k], v) for k, v in s_e.items())
+    assert worst < 1e-2, worst
+
+
+def test_tp_sp_graph_step_matches_eager_2gpu(tmp_path):
+    """Model parallelism (TP = SP = 2, NVLink kernels) replayed as one CUDA graph."""
+    _graph_run(tmp_path, "tp_sp", 2, port=29606)
+
+
+def test_moe_tp_ep_sp_fsdp_graph_step_matches_eager_4gpu(tmp_path):
+    """TP + EP + SP over FSDP with the device-resident MoE routing, replayed as
+    one CUDA graph with different routings per step."""
+    _graph_run(tmp_path, "moe_tp_ep_sp_fsdp", 4, port=29607)
