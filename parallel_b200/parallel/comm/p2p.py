@@ -144,6 +144,67 @@ class P2PSmallAllReduce:
         return out[0], out[1]
 
 
+class ReplicaMeanAllReduce:
+    """Mean of a fixed list of bf16 gradient buffers over the dp_replicate
+    group on NVLink peer memory (the reference all-reduces each gradient with
+    NCCL, parallel/parallel/engine/engine.py:224-247).
+
+    One-shot scheme: every rank copies its buffers into its slot of a
+    symmetric staging region (one multi-segment copy kernel), a signal barrier
+    publishes them, and one kernel per 16 buffers sums the R replicas' slots
+    in fp32, scales by 1/R and writes the local buffers.  Each rank reads the
+    other replicas' full buffers over NVLink (R - 1 copies, what a ring
+    all-reduce moves for R <= 2 and close to it for R <= 4) with a single
+    barrier and no reduce-scatter / all-gather phases.  Two staging sets
+    rotate; a rank writes a set only after the barrier of the call in between,
+    which every rank reaches after its reads of the set's previous use.
+    Buffers must be bf16 CUDA, contiguous, 16-byte aligned and a multiple of 8
+    elements (``eligible``); the sizes are fixed by the first call."""
+
+    _instances: dict = {}
+
+    def __init__(self, group, device, sizes: tuple[int, ...]):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.sizes = sizes
+        self.offsets, off = [], 0
+        for n in sizes:
+            self.offsets.append(off)
+            off += -(-n // 8) * 8
+        self.limit_s = float(os.environ.get("PB_P2P_TIMEOUT_S", "60"))
+        self.sets = [SymmBuffer(max(off, 8), torch.bfloat16, device, group, "replica_grads") for _ in range(2)]
+        self.turn = 0
+
+    @staticmethod
+    def eligible(tensors) -> bool:
+        return bool(tensors) and all(t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous()
+                                     and t.numel() % 8 == 0 and t.data_ptr() % 16 == 0 for t in tensors)
+
+    @classmethod
+    def get(cls, group, device, tensors):
+        """The instance for this group and buffer layout (creating it is
+        collective over the group), or None when peer memory or the buffers
+        do not qualify."""
+        if not (device.type == "cuda" and p2p_supported(group) and cls.eligible(tensors)):
+            return None
+        sizes = tuple(t.numel() for t in tensors)
+        key = (id(group), device.index, sizes)
+        if key not in cls._instances:
+            cls._instances[key] = cls(group, device, sizes)
+        return cls._instances[key]
+
+    def mean_(self, tensors) -> None:
+        buf = self.sets[self.turn % 2]
+        self.turn += 1
+        base = buf.tensor.data_ptr()
+        ext().p2p_copy([t.data_ptr() for t in tensors], [base + 2 * o for o in self.offsets],
+                       [2 * t.numel() for t in tensors])
+        buf.barrier(0, self.limit_s)
+        srcs = [[p + 2 * o for o in self.offsets] for p in buf.peer_ptrs]
+        ext().p2p_reduce(srcs, [t.data_ptr() for t in tensors], [t.numel() for t in tensors], 1.0 / self.world,
+                         False)
+
+
 @dataclass
 class _P2PHandle:
     event: Any

@@ -433,35 +433,55 @@ class ParallelEngine:
                 ar.all_reduce_(packed[1:], "sum")
         return packed[:1], (packed[1:] > 0).to(torch.int32)
 
+    def _replica_mean(self, tensors, group, op: str) -> None:
+        """Mean over the replicate group: NVLink peer memory when the buffers
+        qualify (``ReplicaMeanAllReduce``), else one NCCL / gloo all-reduce each."""
+        if not tensors:
+            return
+        peer = None
+        if _cfg_get(self.cfg.engine, "collectives", "auto") != "nccl":
+            from .comm.p2p import ReplicaMeanAllReduce
+
+            peer = ReplicaMeanAllReduce.get(group, self.device, tensors)
+        if peer is not None:
+            with collective_profile(op, payload_bytes=sum(2 * t.numel() for t in tensors), mode="p2p",
+                                    detail="replicate"):
+                peer.mean_(tensors)
+            return
+        for t in tensors:
+            with collective_profile(op, value=t, mode="replicate"):
+                dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+            t.div_(self.pconfig.dp_replicate_size)
+
     def _average_gradients(self):
-        """All-reduce mean of gradients over the replicate group."""
+        """Mean of the gradients over the replicate group."""
         if self.pconfig.dp_replicate_size <= 1 or self.pconfig.device_mesh is None:
             return
         group = self.pconfig.group(Strategies.DP_REPLICATE)
         if self.fsdp_wrapper.is_active:
-            for bucket in self.fsdp_wrapper.grad_buckets():
-                with collective_profile("fsdp_all_reduce", value=bucket, mode="replicate"):
-                    dist.all_reduce(bucket, op=dist.ReduceOp.SUM, group=group)
-                bucket.div_(self.pconfig.dp_replicate_size)
+            self._replica_mean(self.fsdp_wrapper.grad_buckets(), group, "fsdp_all_reduce")
             return
-        # one participation bitmap for all parameters (one all-reduce, one
-        # read-back) instead of the reference's per-parameter flag and sync
-        # (parallel/parallel/engine/engine.py:224-247); replicas without a local
-        # gradient contribute zeros, globally unused parameters keep grad=None
+        # one participation bitmap for all parameters instead of the reference's
+        # per-parameter flag and sync (parallel/parallel/engine/engine.py:224-247);
+        # replicas without a local gradient contribute zeros, globally unused
+        # parameters keep grad=None.  The bitmap is read on the host only by a
+        # rank that lacks a local gradient: where every local gradient exists,
+        # every parameter is used somewhere.
         params = list(self.optimizer_params)
-        has = torch.tensor([int(p.grad is not None) for p in params], dtype=torch.int32, device=self.device)
+        local = [p.grad is not None for p in params]
+        has = torch.tensor([int(x) for x in local], dtype=torch.int32, device=self.device)
         if has.numel():
             dist.all_reduce(has, op=dist.ReduceOp.MAX, group=group)
-        used = has.tolist()
+        used = local if all(local) else has.tolist()
+        grads = []
         for p, u in zip(params, used):
             if not u:
                 p.grad = None
                 continue
             if p.grad is None:
                 p.grad = torch.zeros_like(p)
-            g = local_tensor(p.grad)
-            dist.all_reduce(g, op=dist.ReduceOp.SUM, group=group)
-            g.div_(self.pconfig.dp_replicate_size)
+            grads.append(local_tensor(p.grad))
+        self._replica_mean(grads, group, "dp_all_reduce")
 
     def _grads_are_finite(self) -> bool:
         finite = torch.ones((), dtype=torch.int32, device=self.device)

@@ -17,6 +17,8 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 CASES = {
     # case: (model preset, parallel sizes as a function of the world size)
     "fsdp": ("small-qwen3", lambda w: {"dp_shard": w}),
+    "dp_replicate": ("small-qwen3", lambda w: {"dp_replicate": w}),
+    "hsdp": ("small-qwen3", lambda w: {"dp_replicate": 2, "dp_shard": w // 2}),
     "tp_sp": ("small-qwen3", lambda w: {"tp": w, "sp": w}),
     "moe_tp_ep_sp_fsdp": ("small-qwen3-moe", lambda w: {"tp": 2, "sp": 2, "ep": 2, "dp_shard": w // 2}),
 }

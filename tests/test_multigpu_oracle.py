@@ -110,6 +110,17 @@ def test_fsdp_4gpu_matches_single_process(tmp_path):
     _run(tmp_path, "fsdp", 4, port=29602)
 
 
+def test_dp_replicate_2gpu_matches_single_process(tmp_path):
+    """Replicated data parallelism: the gradient mean over NVLink peer memory."""
+    _run(tmp_path, "dp_replicate", 2, port=29608)
+
+
+def test_hsdp_4gpu_matches_single_process(tmp_path):
+    """dp_replicate = 2 x dp_shard = 2: FSDP reduce-scatter, then the replica
+    mean of the gradient shards over NVLink peer memory."""
+    _run(tmp_path, "hsdp", 4, port=29609)
+
+
 def test_tp_sp_2gpu_matches_single_process(tmp_path):
     _run(tmp_path, "tp_sp", 2, port=29603)
 
