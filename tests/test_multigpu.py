@@ -42,12 +42,15 @@ def test_fsdp_p2p_collectives_match_nccl(tmp_path):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_fused_sequence_parallel_matches_nccl(tmp_path):
-    """tp = sp = 2: all-gather fused into the column-parallel GEMMs and
-    reduce-scatter fused into the row-parallel GEMMs (NVLink) give the same
-    losses and gradients as the NCCL sequence-parallel path."""
+@pytest.mark.parametrize("sp_mode", ["pull", "fused"])
+def test_fused_sequence_parallel_matches_nccl(tmp_path, sp_mode):
+    """tp = sp = 2: the NVLink sequence-parallel data plane (pull: peer gather
+    + GEMM and GEMM + owner-pull reduce; fused: all-gather inside the
+    column-parallel GEMMs, reduce-scatter inside the row-parallel GEMMs) gives
+    the same losses and gradients as the NCCL sequence-parallel path."""
     out = tmp_path / "res_sp.json"
-    env = dict(os.environ, PB_TEST_OUT=str(out), PB_TEST_MODE="sp", PB_TEST_TMP=str(tmp_path), NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, PB_TEST_OUT=str(out), PB_TEST_MODE="sp", PB_TEST_TMP=str(tmp_path), NCCL_NVLS_ENABLE="0",
+               PB_SP_MODE=sp_mode)
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
            "--master-port", "29534", os.path.join(HERE, "multigpu_worker.py")]
     subprocess.run(cmd, env=env, check=True, timeout=600)
