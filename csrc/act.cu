@@ -207,6 +207,78 @@ void scale_by_scalar(void* x, int64_t n, const float* s_dev, cudaStream_t s) {
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
+// Few slices (split-K): a thread per 4 outputs loops over the slices.  Many
+// slices (block partials of a weight gradient): each of 8 warps sums a
+// contiguous range of slices for 128 columns, the block adds the 8 warp
+// results in order.  Both orders are fixed, so the sums are reproducible.
+__global__ void sum_slices_few_kernel(const float* __restrict__ parts, int slices, int64_t len, int64_t stride,
+                                      void* __restrict__ out, bool out_bf16, bool accumulate) {
+  for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 4; i < len;
+       i += (int64_t)gridDim.x * blockDim.x * 4) {
+    const int n = len - i < 4 ? (int)(len - i) : 4;
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < slices; ++k)
+      for (int j = 0; j < n; ++j) a[j] += parts[(int64_t)k * stride + i + j];
+    for (int j = 0; j < n; ++j) {
+      if (out_bf16) {
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + i + j;
+        *o = __float2bfloat16(a[j] + (accumulate ? __bfloat162float(*o) : 0.f));
+      } else {
+        float* o = reinterpret_cast<float*>(out) + i + j;
+        *o = a[j] + (accumulate ? *o : 0.f);
+      }
+    }
+  }
+}
+
+__global__ void sum_slices_many_kernel(const float* __restrict__ parts, int slices, int64_t len, int64_t stride,
+                                       void* __restrict__ out, bool out_bf16, bool accumulate) {
+  __shared__ float part[8][128];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c0 = (int64_t)blockIdx.x * 128;
+  const int per = (slices + 7) / 8;
+  const int k0 = warp * per, k1 = min(slices, k0 + per);
+  float a[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k = k0; k < k1; ++k)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t c = c0 + lane * 4 + j;
+      if (c < len) a[j] += parts[(int64_t)k * stride + c];
+    }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) part[warp][lane * 4 + j] = a[j];
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    const int64_t c = c0 + threadIdx.x;
+    if (c < len) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) t += part[w][threadIdx.x];
+      if (out_bf16) {
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + c;
+        *o = __float2bfloat16(t + (accumulate ? __bfloat162float(*o) : 0.f));
+      } else {
+        float* o = reinterpret_cast<float*>(out) + c;
+        *o = t + (accumulate ? *o : 0.f);
+      }
+    }
+  }
+}
+
+void sum_slices(const float* parts, int slices, int64_t len, int64_t stride, void* out, bool out_bf16,
+                bool accumulate, cudaStream_t s) {
+  PB_CHECK(slices >= 1 && len >= 0 && stride >= len, "sum_slices: shapes");
+  if (len == 0) return;
+  if (slices <= 8) {
+    sum_slices_few_kernel<<<grid_for((len + 3) / 4, 256), 256, 0, s>>>(parts, slices, len, stride, out, out_bf16,
+                                                                       accumulate);
+  } else {
+    sum_slices_many_kernel<<<(unsigned)((len + 127) / 128), 256, 0, s>>>(parts, slices, len, stride, out, out_bf16,
+                                                                        accumulate);
+  }
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
 void cast_f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t s) {
   cast_f32_bf16_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, s>>>(src, (__nv_bfloat16*)dst, n);
   PB_CUDA_CHECK(cudaGetLastError());

@@ -55,8 +55,11 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, 
     p.N = (int)n_out;
     TORCH_CHECK(b_up_offset + n_out <= b.size(0), "gemm: swiglu B too small");
   }
-  TORCH_CHECK(out.size(0) == p.M && out.size(1) == p.N, "gemm: output shape mismatch");
-  const bool f32 = epi == pb::kEpiStoreF32 || epi == pb::kEpiAccumF32 || epi == pb::kEpiAtomicF32;
+  // kEpiSliceF32: out stacks the split-K slices, [splits * M, N]
+  const int64_t out_rows = epi == pb::kEpiSliceF32 ? (int64_t)p.M * splits : p.M;
+  TORCH_CHECK(out.size(0) == out_rows && out.size(1) == p.N, "gemm: output shape mismatch");
+  const bool f32 = epi == pb::kEpiStoreF32 || epi == pb::kEpiAccumF32 || epi == pb::kEpiAtomicF32 ||
+                   epi == pb::kEpiSliceF32;
   TORCH_CHECK(out.scalar_type() == (f32 ? at::kFloat : at::kBFloat16), "gemm: output dtype mismatch");
   if (r.has_value() && r->defined()) {
     CHECK_CUDA_BF16(*r);

@@ -89,8 +89,7 @@ __global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict_
                                                      const int64_t* __restrict__ labels, int T, int V,
                                                      int64_t v0, const float* __restrict__ scale,
                                                      float* __restrict__ row_lse, bool lse_given,
-                                                     float* __restrict__ row_target,
-                                                     float* __restrict__ loss_sum, bool write_grad) {
+                                                     float* __restrict__ row_target, bool write_grad) {
   const int t = blockIdx.x;
   if (t >= T) return;
   __nv_bfloat16* row = logits + (int64_t)t * ld;
@@ -111,7 +110,6 @@ __global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict_
   if (threadIdx.x == 0) {
     const float tgt = inside ? __bfloat162float(row[local]) : 0.f;
     if (row_target) row_target[t] = tgt;
-    if (loss_sum && valid) atomicAdd(loss_sum, lse - tgt);
   }
   if (!write_grad) return;
   __syncthreads();  // the target logit is read before it is overwritten
@@ -155,15 +153,63 @@ __global__ void __launch_bounds__(kThreads) ce_stats_kernel(const __nv_bfloat16*
   }
 }
 
+// One block of 1024 threads: thread i visits rows i, i + 1024, ..., then a
+// shuffle tree and the 32 warp sums in warp order; the same order on every
+// run, so the loss is reproducible (no atomics).
+constexpr int kRedThreads = 1024;
+
+__device__ __forceinline__ float block_sum_fixed(float v) {
+  __shared__ float warp_part[kRedThreads / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) warp_part[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x == 0)
+    for (int w = 0; w < kRedThreads / 32; ++w) t += warp_part[w];
+  return t;  // valid in thread 0
+}
+
+__global__ void __launch_bounds__(kRedThreads) ce_valid_inv_kernel(const int64_t* __restrict__ labels, int T,
+                                                                   float* __restrict__ inv) {
+  float n = 0.f;
+  for (int t = threadIdx.x; t < T; t += kRedThreads) n += labels[t] >= 0 ? 1.f : 0.f;
+  n = block_sum_fixed(n);
+  if (threadIdx.x == 0) inv[0] = 1.f / fmaxf(n, 1.f);
+}
+
+__global__ void __launch_bounds__(kRedThreads) ce_loss_reduce_kernel(const float* __restrict__ lse,
+                                                                     const float* __restrict__ tgt,
+                                                                     const int64_t* __restrict__ labels, int T,
+                                                                     const float* __restrict__ inv,
+                                                                     float* __restrict__ out, bool accumulate) {
+  float a = 0.f;
+  for (int t = threadIdx.x; t < T; t += kRedThreads)
+    if (labels[t] >= 0) a += lse[t] - tgt[t];
+  a = block_sum_fixed(a);
+  if (threadIdx.x == 0) out[0] = a * inv[0] + (accumulate ? out[0] : 0.f);
+}
+
 }  // namespace
+
+void ce_valid_inv(const int64_t* labels, int T, float* inv, cudaStream_t s) {
+  ce_valid_inv_kernel<<<1, kRedThreads, 0, s>>>(labels, T, inv);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+void ce_loss_reduce(const float* lse, const float* tgt, const int64_t* labels, int T, const float* inv, float* out,
+                    bool accumulate, cudaStream_t s) {
+  ce_loss_reduce_kernel<<<1, kRedThreads, 0, s>>>(lse, tgt, labels, T, inv, out, accumulate);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
 
 void ce_fwd_bwd(void* logits, int64_t ld, const int64_t* labels, int T, int V, int64_t v0,
                 const float* scale, float* row_lse, bool lse_given, float* row_target,
-                float* loss_sum, bool write_grad, cudaStream_t s) {
+                bool write_grad, cudaStream_t s) {
   if (T == 0) return;
   PB_CHECK(!write_grad || scale != nullptr, "ce: gradient scale pointer required");
   ce_kernel<<<T, kThreads, 0, s>>>((__nv_bfloat16*)logits, ld, labels, T, V, v0, scale, row_lse,
-                                   lse_given, row_target, loss_sum, write_grad);
+                                   lse_given, row_target, write_grad);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

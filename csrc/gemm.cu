@@ -236,7 +236,8 @@ void gemm_bf16(const GemmParams& p, cudaStream_t stream) {
   PB_CHECK(p.lda % 8 == 0 && p.ldb % 8 == 0, "gemm: lda/ldb must be multiples of 8 elements");
   PB_CHECK((reinterpret_cast<uintptr_t>(p.A) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.B) & 15) == 0,
            "gemm: A/B must be 16-byte aligned");
-  const bool f32 = p.epi == kEpiStoreF32 || p.epi == kEpiAccumF32 || p.epi == kEpiAtomicF32;
+  const bool f32 =
+      p.epi == kEpiStoreF32 || p.epi == kEpiAccumF32 || p.epi == kEpiAtomicF32 || p.epi == kEpiSliceF32;
   PB_CHECK(p.ldc % (f32 ? 4 : 8) == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0,
            "gemm: C must be 16-byte aligned with a 16-byte row stride");
   if (p.epi == kEpiSwiGLU) PB_CHECK(!p.a_mn && !p.b_mn, "gemm: SwiGLU epilogue needs K-major operands");

@@ -23,6 +23,8 @@ enum GemmEpilogue : int {
                           // apart): C(bf16) = silu(g)*u, and if R != null, R(bf16) receives the
                           // raw [g | u] pre-activations (ldr) for the backward.
   kEpiAtomicF32 = 6,      // C(f32) += alpha*acc with atomic adds (split-K partial sums)
+  kEpiSliceF32 = 7,       // split-K: slice s of C(f32) [splits][M][ldc] = alpha*acc of K slice s
+                          // (no atomics; sum_slices adds the slices in a fixed order)
 };
 
 // Sequence-parallel reduce-scatter epilogue: output row m = b*seq + s (a row

@@ -19,6 +19,7 @@ struct EpiArgs {
   int64_t up_col;  // kEpiSwiGLU: column of the "up" half inside R
   ScatterArgs sc;  // sc.nranks > 0: kEpiStoreBf16 rows go to their owners
   int tma;         // CTA-pair kernel: stage tiles in shared memory and store them with TMA
+  int64_t slice_stride;  // kEpiSliceF32: elements between consecutive split-K slices of C
 };
 
 // TMA-store epilogue staging, per epilogue warp: three 32 x 32 bf16 boxes of

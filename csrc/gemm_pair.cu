@@ -258,6 +258,8 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
       const int m = tm * 2 * BM_CTA + (int)rank * BM_CTA + row;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       const uint32_t tempty = mapa_shared(smem_u32(&tempty_bar[acc]), 0);
+      EpiArgs epw = ep;  // kEpiSliceF32: this work item's K slice has its own slice of C
+      if (ep.epi == kEpiSliceF32) epw.C = reinterpret_cast<float*>(ep.C) + (int64_t)(w / num_tiles) * ep.slice_stride;
       if (ep.tma) {
         gemm_detail::epilogue_warp_tma<BN, SWIGLU>(ep, &tmC, &tmR, t_row, stage, lane, m - lane, M, N, tn * BN_OUT,
                                                    [&] {
@@ -265,7 +267,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
                                                      mbar_arrive_cluster(tempty);
                                                    });
       } else {
-        gemm_detail::epilogue_row<BN, SWIGLU>(ep, t_row, m, M, N, tn * BN_OUT);
+        gemm_detail::epilogue_row<BN, SWIGLU>(epw, t_row, m, M, N, tn * BN_OUT);
         tc_fence_before();
         mbar_arrive_cluster(tempty);
       }
@@ -330,6 +332,7 @@ void launch_pair(const GemmParams& p, cudaStream_t stream) {
     tb = B_MN ? make_tmap_2d_bf16(p.B, p.N, p.K, p.ldb, 64, BK)
               : make_tmap_2d_bf16(p.B, p.K, p.N, p.ldb, BK, Cfg::B_HALF);
   EpiArgs ep{p.C, p.R, p.ldc, p.ldr, p.alpha, p.epi, SWIGLU ? p.b_up_offset : 0};
+  ep.slice_stride = (int64_t)p.M * p.ldc;
   if (p.scatter) ep.sc = *p.scatter;
   // TMA-store epilogue for the bf16 store and SwiGLU epilogues into local memory
   // (16-byte aligned bases and row strides; SwiGLU: whole 32-column chunks so a
@@ -372,8 +375,8 @@ void gemm_bf16_pair(const GemmParams& p, cudaStream_t stream) {
     return launch_pair<256, false, true, false, true>(p, stream);
   }
   if (p.scatter) PB_CHECK(p.epi == kEpiStoreBf16 && p.scatter->nranks <= 8, "gemm: scatter needs the bf16 store epilogue");
-  PB_CHECK(p.splits <= 1 || (p.epi == kEpiAtomicF32 && !p.gather && !p.scatter),
-           "gemm: split-K needs the atomic fp32 epilogue");
+  PB_CHECK(p.splits <= 1 || ((p.epi == kEpiAtomicF32 || p.epi == kEpiSliceF32) && !p.gather && !p.scatter),
+           "gemm: split-K needs the atomic or the slice fp32 epilogue");
   if (p.epi == kEpiSwiGLU) return launch_pair<256, false, false, true>(p, stream);
   if (!p.a_mn && !p.b_mn) return launch_pair<256, false, false, false>(p, stream);
   if (!p.a_mn && p.b_mn) return launch_pair<256, false, true, false>(p, stream);

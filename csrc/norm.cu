@@ -8,6 +8,9 @@
 // model_loading.py:17-35); here each is one memory-bound pass.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+#include <mutex>
+
 #include "host_util.h"
 #include "ops.cuh"
 #include "ptx.cuh"
@@ -67,18 +70,21 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
   }
 }
 
-// Block of 8 warps handles `rows_per_block` rows; dw partials in smem.
+// Block of 8 warps handles `rows_per_block` rows; dw partials in a per-warp
+// shared-memory slice (a lane owns its 8-column groups: no atomics), summed in
+// warp order into row blockIdx.x of the block-partial matrix dw [grid, cols].
 __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int64_t lddy,
                                    const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                    const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
                                    __nv_bfloat16* __restrict__ dx, int64_t lddx, float* __restrict__ dw,
                                    int rows, int cols, int rows_per_block,
                                    const __nv_bfloat16* __restrict__ dres, int64_t lddres) {
-  extern __shared__ float sdw[];
-  for (int c = threadIdx.x; c < cols; c += blockDim.x) sdw[c] = 0.f;
-  __syncthreads();
+  extern __shared__ float sdw_all[];  // [warps][cols]
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
+  float* sdw = sdw_all + (threadIdx.x >> 5) * cols;
+  for (int c = lane; c < cols; c += 32) sdw[c] = 0.f;
+  __syncwarp();
   const int r0 = blockIdx.x * rows_per_block;
   const int r1 = min(rows, r0 + rows_per_block);
   for (int row = r0 + (threadIdx.x >> 5); row < r1; row += warps) {
@@ -95,7 +101,7 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int64_t
       for (int j = 0; j < 8; ++j) {
         const float xh = xv[j] * r;
         dot += gv[j] * wv[j] * xh;
-        atomicAdd(&sdw[c + j], gv[j] * bfr(xh));
+        sdw[c + j] += gv[j] * bfr(xh);
       }
     }
     dot = warp_sum(dot) / (float)cols;
@@ -118,7 +124,11 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int64_t
   }
   __syncthreads();
   if (dw)
-    for (int c = threadIdx.x; c < cols; c += blockDim.x) atomicAdd(&dw[c], sdw[c]);
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+      float t = 0.f;
+      for (int w8 = 0; w8 < warps; ++w8) t += sdw_all[w8 * cols + c];
+      dw[(int64_t)blockIdx.x * cols + c] = t;
+    }
 }
 
 // Register-resident variant: cols == CH * 256; lane owns CH chunks of 8
@@ -214,7 +224,7 @@ __global__ void __launch_bounds__(256, 2) rmsnorm_bwd_reg_kernel(
     for (int c = threadIdx.x; c < cols; c += blockDim.x) {
       float t = 0.f;
       for (int w8 = 0; w8 < warps; ++w8) t += sdw[w8 * cols + c];
-      atomicAdd(&dw[c], t);
+      dw[(int64_t)blockIdx.x * cols + c] = t;  // block partial, summed in block order later
     }
   }
 }
@@ -306,8 +316,9 @@ __global__ void qknorm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, in
   }
 }
 
-// Backward of the above; q/k norm weight grads: per-lane registers, then one
-// shared-memory reduction per block.
+// Backward of the above; q/k norm weight grads: per-lane registers, one slice
+// per half warp in shared memory, summed in slot order into row blockIdx.x of
+// the block-partial matrix [grid, 2 * D] (q weights, then k weights).
 __global__ void __launch_bounds__(256, 2) qknorm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dq, int64_t lddq,
                                        const __nv_bfloat16* __restrict__ dk, int64_t lddk,
                                        const __nv_bfloat16* __restrict__ qkv, int64_t ldqkv,
@@ -325,9 +336,7 @@ __global__ void __launch_bounds__(256, 2) qknorm_rope_bwd_kernel(const __nv_bflo
   // shuffle, so a unit costs one DRAM round trip with 2U + 2 loads in flight.
   constexpr int D = 128;
   constexpr int U = 4;
-  __shared__ float sdw[2][D];
-  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) (&sdw[0][0])[i] = 0.f;
-  __syncthreads();
+  __shared__ float sdw[16][2][D];  // [half-warp slot][q / k][column]
   const int lane = threadIdx.x & 31;
   const int hl = lane & 15;
   const int slots = (blockDim.x >> 5) * 2;
@@ -412,13 +421,16 @@ __global__ void __launch_bounds__(256, 2) qknorm_rope_bwd_kernel(const __nv_bflo
   }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    atomicAdd(&sdw[0][hl * 8 + j], acc_q[j]);
-    atomicAdd(&sdw[1][hl * 8 + j], acc_k[j]);
+    sdw[slot][0][hl * 8 + j] = acc_q[j];
+    sdw[slot][1][hl * 8 + j] = acc_k[j];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < D; i += blockDim.x) {
-    if (dqw) atomicAdd(&dqw[i], sdw[0][i]);
-    if (dkw) atomicAdd(&dkw[i], sdw[1][i]);
+  if (dqw != nullptr) {  // dqw: block partials [grid, 2 * D]
+    for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) {
+      float t = 0.f;
+      for (int sl = 0; sl < slots; ++sl) t += sdw[sl][i / D][i % D];
+      dqw[(int64_t)blockIdx.x * 2 * D + i] = t;
+    }
   }
 }
 
@@ -434,14 +446,32 @@ void rmsnorm_fwd(const void* x, int64_t ldx, const void* w, void* y, int64_t ldy
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
+int rmsnorm_bwd_grid(int rows) {
+  const int blocks = num_sms() * 2;  // one wave: two 256-thread blocks per SM
+  const int rpb = (std::max(rows, 1) + blocks - 1) / blocks;
+  return (std::max(rows, 1) + rpb - 1) / rpb;
+}
+
 void rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const void* w,
-                 const float* rstd, void* dx, int64_t lddx, float* dw_acc, int rows, int cols,
+                 const float* rstd, void* dx, int64_t lddx, float* dw_part, int rows, int cols,
                  cudaStream_t s, const void* dres, int64_t lddres) {
   PB_CHECK(cols % 8 == 0, "rmsnorm: cols must be a multiple of 8");
-  const int blocks = num_sms() * 2;  // one wave: two 256-thread blocks per SM
-  const int rpb = (rows + blocks - 1) / blocks;
-  const int grid = (rows + rpb - 1) / rpb;
-  const size_t smem = (size_t)cols * sizeof(float);
+  const int grid = rmsnorm_bwd_grid(rows);
+  const int rpb = (std::max(rows, 1) + grid - 1) / grid;
+  float* dw_acc = dw_part;
+  const size_t smem = (size_t)8 * cols * sizeof(float);  // per-warp partial slices
+  PB_CHECK(smem <= 227 * 1024, "rmsnorm bwd: rows wider than 7264 columns");
+  if (smem > 48 * 1024) {
+    static std::mutex mu;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    PB_CUDA_CHECK(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    if (!attr_set[dev & 63]) {
+      PB_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+      attr_set[dev & 63] = true;
+    }
+  }
   const size_t smem_reg = (size_t)8 * cols * sizeof(float);  // per-warp partials (<= 48 KB)
   if (cols % 256 == 0 && cols <= 1536) {  // wider rows would spill: generic kernel
 #define PB_RMS_BWD(CH)                                                                                     \
@@ -478,20 +508,25 @@ void qknorm_rope_fwd(const void* qkv, int64_t ldqkv, const void* qw, const void*
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
+int qknorm_rope_bwd_grid(int T, int nq, int nkv) {
+  const int units = std::max(1, T * ((nq + nkv + 3) / 4));  // (token, 4 heads) units
+  const int blocks = num_sms() * 2;                         // one wave
+  const int ipb = (units + blocks - 1) / blocks;
+  return (units + ipb - 1) / ipb;
+}
+
 void qknorm_rope_bwd(const void* dq, int64_t lddq, const void* dk, int64_t lddk, const void* qkv,
                      int64_t ldqkv, const void* qw, const void* kw, const void* cos,
                      const void* sin, const float* rstd, void* dqkv, int64_t lddqkv,
-                     float* dqw_acc, float* dkw_acc, int T, int S, int nq, int nkv, int D,
-                     cudaStream_t s) {
+                     float* dw_part, int T, int S, int nq, int nkv, int D, cudaStream_t s) {
   PB_CHECK(D == 128, "qknorm_rope: head_dim 128 only");
-  const int units = T * ((nq + nkv + 3) / 4);  // (token, 4 heads) units
-  const int blocks = num_sms() * 2;            // one wave
-  const int ipb = (units + blocks - 1) / blocks;
-  const int grid = (units + ipb - 1) / ipb;
+  const int units = T * ((nq + nkv + 3) / 4);
+  const int grid = qknorm_rope_bwd_grid(T, nq, nkv);
+  const int ipb = (std::max(units, 1) + grid - 1) / grid;
   qknorm_rope_bwd_kernel<<<grid, 256, 0, s>>>(
       (const __nv_bfloat16*)dq, lddq, (const __nv_bfloat16*)dk, lddk, (const __nv_bfloat16*)qkv,
       ldqkv, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw, (const __nv_bfloat16*)cos,
-      (const __nv_bfloat16*)sin, rstd, (__nv_bfloat16*)dqkv, lddqkv, dqw_acc, dkw_acc, T, S, nq,
+      (const __nv_bfloat16*)sin, rstd, (__nv_bfloat16*)dqkv, lddqkv, dw_part, nullptr, T, S, nq,
       nkv, ipb);
   PB_CUDA_CHECK(cudaGetLastError());
 }

@@ -17,6 +17,16 @@ cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 #define CHECK_F32(t) \
   TORCH_CHECK((t).is_cuda() && (t).scalar_type() == at::kFloat && (t).is_contiguous(), #t " must be contiguous CUDA fp32")
 
+// Finish block partials [slices, len] (row stride `stride`) into `out` (bf16 or f32, contiguous, len elements).
+void finish_partials(const at::Tensor& parts, int slices, int64_t len, int64_t stride, int64_t offset,
+                     at::Tensor& out) {
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.numel() == len &&
+                  (out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kFloat),
+              "weight gradient: contiguous bf16 / fp32 CUDA tensor of ", len, " elements");
+  pb::sum_slices(parts.data_ptr<float>() + offset, slices, len, stride, out.data_ptr(),
+                 out.scalar_type() == at::kBFloat16, false, at::cuda::getCurrentCUDAStream().stream());
+}
+
 float* opt_f32(const c10::optional<at::Tensor>& t) {
   if (!t.has_value() || !t->defined()) return nullptr;
   CHECK_F32(*t);
@@ -44,8 +54,20 @@ void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
     rp = dres->data_ptr();
     ldr = dres->stride(0);
   }
+  // dw (optional, bf16 or fp32 [cols]) is overwritten: block partials, then a fixed-order sum
+  at::Tensor parts;
+  float* pp = nullptr;
+  const int grid = pb::rmsnorm_bwd_grid((int)x.size(0));
+  if (dw.has_value() && dw->defined()) {
+    parts = at::empty({grid, x.size(1)}, x.options().dtype(at::kFloat));
+    pp = parts.data_ptr<float>();
+  }
   pb::rmsnorm_bwd(dy.data_ptr(), dy.stride(0), x.data_ptr(), x.stride(0), w.data_ptr(), rstd.data_ptr<float>(),
-                  dx.data_ptr(), dx.stride(0), opt_f32(dw), x.size(0), x.size(1), cur_stream(), rp, ldr);
+                  dx.data_ptr(), dx.stride(0), pp, x.size(0), x.size(1), cur_stream(), rp, ldr);
+  if (pp) {
+    at::Tensor out = *dw;
+    finish_partials(parts, grid, x.size(1), x.size(1), 0, out);
+  }
 }
 
 void qknorm_rope_fwd(const at::Tensor& qkv, const at::Tensor& qw, const at::Tensor& kw, const at::Tensor& cos,
@@ -67,10 +89,23 @@ void qknorm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tenso
   CHECK_BF16(dq); CHECK_BF16(dk); CHECK_BF16(qkv); CHECK_BF16(dqkv); CHECK_F32(rstd);
   const c10::cuda::CUDAGuard g(qkv.device());
   const int D = (int)qw.size(0);
+  // dqw / dkw (optional, bf16 or fp32 [D]) are overwritten: block partials, then fixed-order sums
+  const bool want = (dqw.has_value() && dqw->defined()) || (dkw.has_value() && dkw->defined());
+  const int grid = pb::qknorm_rope_bwd_grid((int)qkv.size(0), (int)nq, (int)nkv);
+  at::Tensor parts;
+  if (want) parts = at::empty({grid, 2 * D}, qkv.options().dtype(at::kFloat));
   pb::qknorm_rope_bwd(dq.data_ptr(), dq.stride(0), dk.data_ptr(), dk.stride(0), qkv.data_ptr(), qkv.stride(0),
                       qw.data_ptr(), kw.data_ptr(), cos.data_ptr(), sin.data_ptr(), rstd.data_ptr<float>(),
-                      dqkv.data_ptr(), dqkv.stride(0), opt_f32(dqw), opt_f32(dkw), qkv.size(0), (int)S, (int)nq,
-                      (int)nkv, D, cur_stream());
+                      dqkv.data_ptr(), dqkv.stride(0), want ? parts.data_ptr<float>() : nullptr, qkv.size(0), (int)S,
+                      (int)nq, (int)nkv, D, cur_stream());
+  if (dqw.has_value() && dqw->defined()) {
+    at::Tensor out = *dqw;
+    finish_partials(parts, grid, D, 2 * D, 0, out);
+  }
+  if (dkw.has_value() && dkw->defined()) {
+    at::Tensor out = *dkw;
+    finish_partials(parts, grid, D, 2 * D, D, out);
+  }
 }
 
 // tiles128 (optional int32 CUDA [1]): only the first 128 * tiles128[0] rows are live
@@ -170,14 +205,32 @@ void aux_stats_bwd(const at::Tensor& probs, const at::Tensor& gsum, at::Tensor& 
 
 void ce_fwd_bwd(at::Tensor& logits, const at::Tensor& labels, int64_t v0, const c10::optional<at::Tensor>& scale,
                 const c10::optional<at::Tensor>& row_lse, bool lse_given, const c10::optional<at::Tensor>& row_target,
-                const c10::optional<at::Tensor>& loss_sum, bool write_grad) {
+                bool write_grad) {
   CHECK_BF16(logits);
   TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous(), "labels must be contiguous int64");
   TORCH_CHECK(labels.numel() == logits.size(0), "ce: one label per row");
   const c10::cuda::CUDAGuard g(logits.device());
   pb::ce_fwd_bwd(logits.data_ptr(), logits.stride(0), labels.data_ptr<int64_t>(), logits.size(0), logits.size(1),
-                 v0, opt_f32(scale), opt_f32(row_lse), lse_given, opt_f32(row_target), opt_f32(loss_sum),
-                 write_grad, cur_stream());
+                 v0, opt_f32(scale), opt_f32(row_lse), lse_given, opt_f32(row_target), write_grad, cur_stream());
+}
+
+// ce_valid_inv(labels int64 [T], inv fp32 [1]): inv = 1 / max(1, #valid labels)
+void ce_valid_inv(const at::Tensor& labels, at::Tensor& inv) {
+  TORCH_CHECK(labels.is_cuda() && labels.scalar_type() == at::kLong && labels.is_contiguous(), "labels: int64 CUDA");
+  CHECK_F32(inv);
+  const c10::cuda::CUDAGuard g(labels.device());
+  pb::ce_valid_inv(labels.data_ptr<int64_t>(), (int)labels.numel(), inv.data_ptr<float>(), cur_stream());
+}
+
+// ce_loss_reduce(lse, tgt fp32 [T], labels int64 [T], inv fp32 [1], out fp32 [1], accumulate)
+void ce_loss_reduce(const at::Tensor& lse, const at::Tensor& tgt, const at::Tensor& labels, const at::Tensor& inv,
+                    at::Tensor& out, bool accumulate) {
+  CHECK_F32(lse); CHECK_F32(tgt); CHECK_F32(inv); CHECK_F32(out);
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous(), "labels: int64");
+  TORCH_CHECK(lse.numel() == labels.numel() && tgt.numel() == labels.numel(), "ce_loss_reduce: one value per row");
+  const c10::cuda::CUDAGuard g(lse.device());
+  pb::ce_loss_reduce(lse.data_ptr<float>(), tgt.data_ptr<float>(), labels.data_ptr<int64_t>(), (int)labels.numel(),
+                     inv.data_ptr<float>(), out.data_ptr<float>(), accumulate, cur_stream());
 }
 
 void ce_row_stats(const at::Tensor& logits, at::Tensor& row_max, at::Tensor& row_sumexp) {
@@ -185,6 +238,20 @@ void ce_row_stats(const at::Tensor& logits, at::Tensor& row_max, at::Tensor& row
   const c10::cuda::CUDAGuard g(logits.device());
   pb::ce_row_stats(logits.data_ptr(), logits.stride(0), logits.size(0), logits.size(1), row_max.data_ptr<float>(),
                    row_sumexp.data_ptr<float>(), cur_stream());
+}
+
+// sum_slices(parts fp32 [slices, len] (contiguous), out bf16 / fp32 [len], accumulate):
+// out = (accumulate ? out : 0) + sum over slices, in slice order
+void sum_slices(const at::Tensor& parts, at::Tensor& out, bool accumulate) {
+  CHECK_F32(parts);
+  TORCH_CHECK(parts.is_contiguous() && parts.dim() >= 2, "sum_slices: parts [slices, ...] contiguous fp32");
+  const int64_t len = parts.numel() / parts.size(0);
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.numel() == len &&
+                  (out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kFloat),
+              "sum_slices: out");
+  const c10::cuda::CUDAGuard g(parts.device());
+  pb::sum_slices(parts.data_ptr<float>(), (int)parts.size(0), len, len, out.data_ptr(),
+                 out.scalar_type() == at::kBFloat16, accumulate, cur_stream());
 }
 
 void cast_f32_to_bf16(const at::Tensor& src, at::Tensor& dst) {
@@ -228,10 +295,17 @@ void adamw(const std::vector<at::Tensor>& params, const std::vector<at::Tensor>&
                   (int)step, opt_f32(grad_scale), skip_ptr, opt_f32(hyper), grad_f32, state_f32, cur_stream());
 }
 
+// out / flag are overwritten (accumulate = false) or added to (accumulate = true)
 void sumsq(const std::vector<at::Tensor>& grads, const std::vector<double>& weights, at::Tensor& out,
-           const c10::optional<at::Tensor>& flag) {
-  if (grads.empty()) return;
+           const c10::optional<at::Tensor>& flag, bool accumulate) {
   CHECK_F32(out);
+  if (grads.empty()) {
+    if (!accumulate) {
+      out.zero_();
+      if (flag.has_value() && flag->defined()) flag->zero_();
+    }
+    return;
+  }
   const bool f32 = grads[0].scalar_type() == at::kFloat;
   std::vector<pb::NormSeg> segs;
   for (size_t i = 0; i < grads.size(); ++i) {
@@ -242,7 +316,10 @@ void sumsq(const std::vector<at::Tensor>& grads, const std::vector<double>& weig
   int* flag_ptr = nullptr;
   if (flag.has_value() && flag->defined()) flag_ptr = flag->data_ptr<int>();
   const c10::cuda::CUDAGuard g(out.device());
-  pb::sumsq_multi(segs.data(), (int)segs.size(), f32, out.data_ptr<float>(), flag_ptr, cur_stream());
+  at::Tensor parts = at::empty({2 * std::max<int64_t>(1, pb::sumsq_chunks(segs.data(), (int)segs.size()))},
+                               out.options());
+  pb::sumsq_multi(segs.data(), (int)segs.size(), f32, parts.data_ptr<float>(), out.data_ptr<float>(), flag_ptr,
+                  accumulate, cur_stream());
 }
 
 void clip_coef(const at::Tensor& total, double max_norm, at::Tensor& out) {
@@ -329,11 +406,15 @@ void register_ops(pybind11::module& m) {
   m.def("aux_stats_bwd", &aux_stats_bwd);
   m.def("ce_fwd_bwd", &ce_fwd_bwd);
   m.def("ce_row_stats", &ce_row_stats);
+  m.def("ce_valid_inv", &ce_valid_inv);
+  m.def("ce_loss_reduce", &ce_loss_reduce);
   m.def("cast_f32_to_bf16", &cast_f32_to_bf16);
+  m.def("sum_slices", &sum_slices);
   m.def("adamw", &adamw, py::arg("params"), py::arg("grads"), py::arg("exp_avgs"), py::arg("exp_avg_sqs"),
         py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("wd"), py::arg("step"),
         py::arg("grad_scale") = py::none(), py::arg("skip") = py::none(), py::arg("hyper") = py::none());
-  m.def("sumsq", &sumsq);
+  m.def("sumsq", &sumsq, py::arg("grads"), py::arg("weights"), py::arg("out"), py::arg("flag") = py::none(),
+        py::arg("accumulate") = true);
   m.def("clip_coef", &clip_coef);
   m.def("attn_fwd", &attn_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("B"),
         py::arg("S"), py::arg("nq"), py::arg("nkv"), py::arg("scale"), py::arg("causal"),

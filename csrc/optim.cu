@@ -147,9 +147,11 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(SegTable tab, float lr,
   }
 }
 
+// One block per chunk: the chunk's weighted sum of squares and its non-finite
+// bit go to parts[2 * (chunk_base + chunk)] / [.. + 1]; sumsq_finish adds the
+// chunks in chunk order, so the norm has the same bits on every run.
 template <typename GT>
-__global__ void __launch_bounds__(kThreads) sumsq_kernel(NormTable tab, float* __restrict__ out,
-                                                         int* __restrict__ flag) {
+__global__ void __launch_bounds__(kThreads) sumsq_kernel(NormTable tab, float* __restrict__ parts, int chunk_base) {
   const int chunk = blockIdx.x;
   const int si = find_seg(tab.chunk_start, tab.nseg, chunk);
   const NormSeg sg = tab.seg[si];
@@ -166,19 +168,54 @@ __global__ void __launch_bounds__(kThreads) sumsq_kernel(NormTable tab, float* _
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
   const unsigned any_bad = __ballot_sync(0xffffffffu, bad);
   __shared__ float sacc[kThreads / 32];
-  __shared__ int sbad;
-  if (threadIdx.x == 0) sbad = 0;
-  __syncthreads();
+  __shared__ int sbad[kThreads / 32];
   if ((threadIdx.x & 31) == 0) {
     sacc[threadIdx.x >> 5] = acc;
-    if (any_bad) sbad = 1;
+    sbad[threadIdx.x >> 5] = any_bad != 0;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     float t = 0.f;
-    for (int w = 0; w < kThreads / 32; ++w) t += sacc[w];
-    atomicAdd(out, t * sg.weight);
-    if (sbad && flag) atomicExch(flag, 1);
+    int b = 0;
+    for (int w = 0; w < kThreads / 32; ++w) {
+      t += sacc[w];
+      b |= sbad[w];
+    }
+    parts[2 * (int64_t)(chunk_base + chunk)] = t * sg.weight;
+    parts[2 * (int64_t)(chunk_base + chunk) + 1] = (float)b;
+  }
+}
+
+constexpr int kFinishThreads = 1024;
+
+__global__ void __launch_bounds__(kFinishThreads) sumsq_finish_kernel(const float* __restrict__ parts, int chunks,
+                                                                      float* __restrict__ out, int* __restrict__ flag,
+                                                                      bool accumulate) {
+  float a = 0.f;
+  float bad = 0.f;
+  for (int c = threadIdx.x; c < chunks; c += kFinishThreads) {
+    a += parts[2 * (int64_t)c];
+    bad = fmaxf(bad, parts[2 * (int64_t)c + 1]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    bad = fmaxf(bad, __shfl_xor_sync(0xffffffffu, bad, o));
+  }
+  __shared__ float sa[kFinishThreads / 32], sb[kFinishThreads / 32];
+  if ((threadIdx.x & 31) == 0) {
+    sa[threadIdx.x >> 5] = a;
+    sb[threadIdx.x >> 5] = bad;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f, b = 0.f;
+    for (int w = 0; w < kFinishThreads / 32; ++w) {
+      t += sa[w];
+      b = fmaxf(b, sb[w]);
+    }
+    out[0] = t + (accumulate ? out[0] : 0.f);
+    if (flag) flag[0] = (b > 0.f ? 1 : 0) | (accumulate ? flag[0] : 0);
   }
 }
 
@@ -221,7 +258,17 @@ void adamw_multi(const AdamSeg* segs, int nseg, float lr, float beta1, float bet
   }
 }
 
-void sumsq_multi(const NormSeg* segs, int nseg, bool f32, float* out, int* out_flag, cudaStream_t s) {
+int64_t sumsq_chunks(const NormSeg* segs, int nseg) {
+  int64_t chunks = 0;
+  for (int i = 0; i < nseg; ++i) chunks += (segs[i].n + kChunk - 1) / kChunk;
+  return chunks;
+}
+
+void sumsq_multi(const NormSeg* segs, int nseg, bool f32, float* parts, float* out, int* out_flag, bool accumulate,
+                 cudaStream_t s) {
+  const int64_t total = sumsq_chunks(segs, nseg);
+  PB_CHECK(total < (int64_t)1 << 30, "sumsq: too many chunks");
+  int base = 0;
   for (int off = 0; off < nseg; off += kMaxSegs) {
     NormTable tab{};
     tab.nseg = std::min(kMaxSegs, nseg - off);
@@ -234,11 +281,14 @@ void sumsq_multi(const NormSeg* segs, int nseg, bool f32, float* out, int* out_f
     tab.chunk_start[tab.nseg] = chunks;
     if (chunks == 0) continue;
     if (f32)
-      sumsq_kernel<float><<<chunks, kThreads, 0, s>>>(tab, out, out_flag);
+      sumsq_kernel<float><<<chunks, kThreads, 0, s>>>(tab, parts, base);
     else
-      sumsq_kernel<__nv_bfloat16><<<chunks, kThreads, 0, s>>>(tab, out, out_flag);
+      sumsq_kernel<__nv_bfloat16><<<chunks, kThreads, 0, s>>>(tab, parts, base);
     PB_CUDA_CHECK(cudaGetLastError());
+    base += chunks;
   }
+  sumsq_finish_kernel<<<1, kFinishThreads, 0, s>>>(parts, (int)total, out, out_flag, accumulate);
+  PB_CUDA_CHECK(cudaGetLastError());
 }
 
 void clip_coef(const float* total_sumsq, float max_norm, float* scale_out, cudaStream_t s) {

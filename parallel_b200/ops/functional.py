@@ -118,9 +118,10 @@ class _RMSNormFn(torch.autograd.Function):
         if not dy2.is_contiguous():
             dy2 = dy2.contiguous()
         dx = torch.empty_like(x2)
-        dw = torch.zeros(x2.shape[1], device=x2.device, dtype=torch.float32)
+        # the kernel writes block partials and sums them in a fixed order into dw
+        dw = torch.empty(x2.shape[1], device=x2.device, dtype=w.dtype)
         ext().rmsnorm_bwd(dy2, x2, w, rstd, dx, dw)
-        return dx.view(ctx.shape), dw.to(w.dtype), None
+        return dx.view(ctx.shape), dw, None
 
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
@@ -151,7 +152,7 @@ class _ResidualRMSNormFn(torch.autograd.Function):
         x2, w, rstd = ctx.saved_tensors
         H = x2.shape[1]
         dx = torch.empty_like(x2)
-        dw = torch.zeros(H, device=x2.device, dtype=torch.float32)
+        dw = torch.empty(H, device=x2.device, dtype=w.dtype)
         if dy is None:
             return dres, None, None
         dy2 = dy.reshape(-1, H)
@@ -163,7 +164,7 @@ class _ResidualRMSNormFn(torch.autograd.Function):
             if not r2.is_contiguous():
                 r2 = r2.contiguous()
         ext().rmsnorm_bwd(dy2, x2, w, rstd, dx, dw, r2)
-        return dx.view(ctx.shape), dw.to(w.dtype), None
+        return dx.view(ctx.shape), dw, None
 
 
 def residual_rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float):
@@ -237,8 +238,8 @@ class _AttentionFn(torch.autograd.Function):
             dq_acc = torch.empty(T, nq * D, device=h.device, dtype=torch.float32)
         ext().attn_bwd(q, k, v, o, do, lse, delta, dq_acc, dq, dk, dv, B, S, nq, nkv, 1.0 / math.sqrt(D), True,
                        None, ds_buf)
-        dqw = torch.zeros(D, device=h.device, dtype=torch.float32)
-        dkw = torch.zeros(D, device=h.device, dtype=torch.float32)
+        dqw = torch.empty(D, device=h.device, dtype=qw.dtype)
+        dkw = torch.empty(D, device=h.device, dtype=kw.dtype)
         ext().qknorm_rope_bwd(dq, dk, qkv, qw, kw, cos, sin, rstd, dqkv, dqw, dkw, S, nq, nkv)
         wqkv = fused_rows(wq, wk, wv)
         h2 = h.reshape(T, -1)
@@ -248,7 +249,7 @@ class _AttentionFn(torch.autograd.Function):
             dh = G.linear_dgrad(dqkv, wqkv).view(h.shape)
         dw = G.linear_wgrad(dqkv, h2)
         gq, gk, gv = _split_rows(dw, (wq.shape[0], wk.shape[0], wv.shape[0]))
-        return dh, gq, gk, gv, dqw.to(qw.dtype), dkw.to(kw.dtype), None, None, None, None, None, None, None, None, None, None
+        return dh, gq, gk, gv, dqw, dkw, None, None, None, None, None, None, None, None, None, None
 
 
 def attention_block(h, wq, wk, wv, q_norm_w, k_norm_w, inv_freq, B, S, nq, nkv, D, eps, stash=None, sp=None):
@@ -445,24 +446,29 @@ class _LMHeadCEFn(torch.autograd.Function):
         T, H = h.shape
         V = w.shape[0]
         labels = labels.reshape(-1).contiguous()
-        valid = (labels >= 0).sum().clamp_min(1).to(torch.float32)
-        inv = (1.0 / valid).reshape(1)
-        loss_sum = torch.zeros(1, device=h.device, dtype=torch.float32)
+        # 1 / #valid labels, per-row (lse, target logit), and the mean loss
+        # summed over the rows in a fixed order: a few kernels, no atomics
+        inv = torch.empty(1, device=h.device, dtype=torch.float32)
+        ext().ce_valid_inv(labels, inv)
+        lse = torch.empty(T, device=h.device, dtype=torch.float32)
+        tgt = torch.empty(T, device=h.device, dtype=torch.float32)
+        loss = torch.empty(1, device=h.device, dtype=torch.float32)
         rows = max(128, min(T, int(max_block_bytes // (V * 2)) // 128 * 128))
         dh = torch.empty_like(h)
         single = rows >= T
-        dw = None if single else torch.zeros(V, H, device=h.device, dtype=torch.float32)
+        dw = None if single else torch.empty(V, H, device=h.device, dtype=torch.float32)
         for r0 in range(0, T, rows):
             r1 = min(T, r0 + rows)
             hb = h[r0:r1]
             logits = G.linear(hb, w)
-            ext().ce_fwd_bwd(logits, labels[r0:r1], 0, inv, None, False, None, loss_sum, True)
+            ext().ce_fwd_bwd(logits, labels[r0:r1], 0, inv, lse[r0:r1], False, tgt[r0:r1], True)
             G.linear_dgrad(logits, w, out=dh[r0:r1])
             if single:
                 dw = G.linear_wgrad(logits, hb)
             else:
-                G.linear_wgrad(logits, hb, out=dw, accumulate=True)
+                G.linear_wgrad(logits, hb, out=dw, accumulate=r0 > 0)
             del logits
+        ext().ce_loss_reduce(lse, tgt, labels, inv, loss, False)
         if not single:
             dwb = torch.empty(V, H, device=h.device, dtype=w.dtype)
             ext().cast_f32_to_bf16(dw, dwb)
@@ -471,7 +477,7 @@ class _LMHeadCEFn(torch.autograd.Function):
         ctx.tied = tied
         if tied is not None:
             tied.w_head = w
-        return (loss_sum * inv).reshape(())
+        return loss.reshape(())
 
     @staticmethod
     def backward(ctx, g):

@@ -349,15 +349,19 @@ class ParallelEngine:
         max_norm = float(self.cfg.model.clip_grad_norm)
         if cuda and not self.grad_scaler.is_enabled():
             grads, weights = self._grad_lists()
-            sq = torch.zeros(1, dtype=torch.float32, device=self.device)
-            flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+            sq = torch.empty(1, dtype=torch.float32, device=self.device)
+            flag = torch.empty(1, dtype=torch.int32, device=self.device)
             by_dtype: dict = {}
             for g, w in zip(grads, weights):
                 by_dtype.setdefault(g.dtype, ([], []))
                 by_dtype[g.dtype][0].append(g if g.is_contiguous() else g.contiguous())
                 by_dtype[g.dtype][1].append(w)
-            for gs, ws in by_dtype.values():
-                ext().sumsq(gs, ws, sq, flag)
+            if not by_dtype:
+                sq.zero_()
+                flag.zero_()
+            # per-chunk partials summed in chunk order: the norm is reproducible
+            for i, (gs, ws) in enumerate(by_dtype.values()):
+                ext().sumsq(gs, ws, sq, flag, i > 0)
             sq, flag = self._reduce_norm_and_flag(sq, flag)
             scale = None
             if max_norm > 0.0:

@@ -99,12 +99,13 @@ class _VocabParallelLMHeadCE(torch.autograd.Function):
         T, H = h.shape
         V = w.shape[0]
         labels = labels.reshape(-1).contiguous()
-        n_valid = (labels != IGNORE).sum().clamp_min(1).to(torch.float32)
-        inv = (1.0 / n_valid).reshape(1)
+        # labels are in [0, vocab) or IGNORE (< 0): the kernels count labels >= 0
+        inv = torch.empty(1, device=h.device, dtype=torch.float32)
+        ext().ce_valid_inv(labels, inv)
         rows = max(128, min(T, int(block_bytes // (V * 2)) // 128 * 128))
         dh = torch.empty_like(h)
-        dw = torch.zeros(V, H, device=h.device, dtype=torch.float32)
-        loss_sum = torch.zeros(1, device=h.device, dtype=torch.float32)
+        dw = torch.empty(V, H, device=h.device, dtype=torch.float32)
+        loss = torch.empty(1, device=h.device, dtype=torch.float32)
         for r0 in range(0, T, rows):
             r1 = min(T, r0 + rows)
             hb = h[r0:r1]
@@ -119,7 +120,7 @@ class _VocabParallelLMHeadCE(torch.autograd.Function):
                 inside = (lb != IGNORE) & (local >= 0) & (local < V)
                 tl = logits.gather(1, local.clamp(0, V - 1)[:, None])[:, 0].float()
                 lse, tgt = small.lse_merge(mx, se, torch.where(inside, tl, torch.zeros_like(tl)))
-                ext().ce_fwd_bwd(logits, lb, v0, inv, lse, True, None, None, True)
+                ext().ce_fwd_bwd(logits, lb, v0, inv, lse, True, None, True)
             else:
                 gm = mx.clone()
                 dist.all_reduce(gm, op=dist.ReduceOp.MAX, group=group)
@@ -127,17 +128,17 @@ class _VocabParallelLMHeadCE(torch.autograd.Function):
                 dist.all_reduce(se, op=dist.ReduceOp.SUM, group=group)
                 lse = gm + torch.log(se)
                 tgt = torch.empty(r1 - r0, device=h.device)
-                ext().ce_fwd_bwd(logits, lb, v0, inv, lse, True, tgt, None, True)
+                ext().ce_fwd_bwd(logits, lb, v0, inv, lse, True, tgt, True)
                 dist.all_reduce(tgt, op=dist.ReduceOp.SUM, group=group)
-            valid = lb != IGNORE
-            loss_sum += torch.where(valid, lse - tgt, torch.zeros_like(lse)).sum()
+            # every rank holds the global (lse, target): the same fixed-order sum everywhere
+            ext().ce_loss_reduce(lse.contiguous(), tgt.contiguous(), lb, inv, loss, r0 > 0)
             G.linear_dgrad(logits, w, out=dh[r0:r1])
-            G.linear_wgrad(logits, hb, out=dw, accumulate=True)
+            G.linear_wgrad(logits, hb, out=dw, accumulate=r0 > 0)
             del logits
         dwb = torch.empty(V, H, device=h.device, dtype=w.dtype)
         ext().cast_f32_to_bf16(dw, dwb)
         ctx.save_for_backward(dh, dwb)
-        return (loss_sum * inv).reshape(())
+        return loss.reshape(())
 
     @staticmethod
     def backward(ctx, g):

@@ -241,14 +241,23 @@ def test_cross_entropy():
     scale = (1.0 / valid.float()).reshape(1)
     lse = torch.empty(T, device="cuda")
     tgt = torch.empty(T, device="cuda")
-    loss_sum = torch.zeros(1, device="cuda")
+    inv = torch.empty(1, device="cuda")
+    C.ce_valid_inv(labels, inv)
+    assert inv.item() == pytest.approx(scale.item(), rel=1e-6)
     g = logits.clone()
-    C.ce_fwd_bwd(g, labels, 0, scale, lse, False, tgt, loss_sum, True)
+    C.ce_fwd_bwd(g, labels, 0, inv, lse, False, tgt, True)
+    loss = torch.empty(1, device="cuda")
+    C.ce_loss_reduce(lse, tgt, labels, inv, loss, False)
     lf = logits.float().requires_grad_(True)
     ref = torch.nn.functional.cross_entropy(lf, labels, ignore_index=-100)
     ref.backward()
-    assert abs(loss_sum.item() / valid.item() - ref.item()) < 1e-3
+    assert abs(loss.item() - ref.item()) < 1e-3
     assert _rel_err(g, lf.grad) < 1e-2
+    again = torch.empty(1, device="cuda")
+    C.ce_loss_reduce(lse, tgt, labels, inv, again, False)
+    assert torch.equal(loss, again)  # fixed summation order
+    C.ce_loss_reduce(lse, tgt, labels, inv, again, True)
+    assert again.item() == pytest.approx(2 * loss.item(), rel=1e-6)
     _check_no_device_error()
 
 
@@ -283,6 +292,18 @@ def test_adamw_and_sumsq():
     g2[5] = float("nan")
     C.sumsq([g2], [1.0], out, flag)
     assert flag.item() == 1
+    # overwrite mode (no zero fill needed) over several segment tables, twice: same bits
+    big = [torch.randn(30000 + 17 * i, device="cuda").to(torch.bfloat16) for i in range(60)]
+    res = []
+    for _ in range(2):
+        o = torch.full((1,), float("nan"), device="cuda")
+        f = torch.full((1,), 7, device="cuda", dtype=torch.int32)
+        C.sumsq(big, [1.0] * 60, o, f, False)
+        res.append(o)
+        assert f.item() == 0
+    ref = sum(t.float().pow(2).sum() for t in big)
+    assert abs(res[0].item() - ref.item()) / ref.item() < 1e-4
+    assert torch.equal(res[0], res[1])
     _check_no_device_error()
 
 
@@ -446,6 +467,57 @@ def test_gemm_splitk_atomic(M, N, K, splits):
     _check_no_device_error()
     ref = g.float().t() @ x.float() + 0.5
     assert _rel_err(out, ref) < 1e-3
+
+
+@pytest.mark.parametrize("M,N,K,splits", [(1024, 3072, 8192, 3), (1000, 520, 4096, 2)])
+def test_gemm_splitk_slices_sum_in_fixed_order(M, N, K, splits):
+    """Split-K slices stored side by side (epilogue 7) and added by sum_slices:
+    the same result as fp32 PyTorch, and the same bits on every run."""
+    C = _ext()
+    torch.manual_seed(9)
+    g = torch.randn(K, M, device="cuda").to(torch.bfloat16)
+    x = torch.randn(K, N, device="cuda").to(torch.bfloat16)
+    ref = g.float().t() @ x.float()
+    outs = []
+    for _ in range(2):
+        ws = torch.full((splits * M, N), float("nan"), device="cuda")  # every element is written
+        C.gemm(g, x, ws, True, True, 7, 1.0, splits=splits)
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        C.sum_slices(ws.view(splits, M, N), out, False)
+        outs.append(out)
+    _check_no_device_error()
+    assert _rel_err(outs[0], ref) < 1e-2
+    assert torch.equal(outs[0], outs[1])
+    acc = torch.full((M, N), 0.25, device="cuda")
+    C.sum_slices(ws.view(splits, M, N), acc, True)
+    assert _rel_err(acc, ref + 0.25) < 1e-2
+
+
+@pytest.mark.parametrize("T,H", [(3000, 4096), (777, 2048), (40000, 1024)])
+def test_rmsnorm_bwd_weight_grad_is_reproducible(T, H):
+    """Block partials + the fixed-order sum: the norm weight gradient (bf16
+    output, written without a zero fill) matches fp32 and is bitwise stable;
+    H = 4096 takes the generic kernel with more than 48 KB of shared memory."""
+    C = _ext()
+    torch.manual_seed(10)
+    x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(H, device="cuda")).to(torch.bfloat16)
+    y = torch.empty_like(x)
+    rstd = torch.empty(T, device="cuda")
+    C.rmsnorm_fwd(x, w, y, rstd, 1e-6)
+    dy = torch.randn_like(x)
+    dws = []
+    for _ in range(2):
+        dx = torch.empty_like(x)
+        dw = torch.full((H,), float("nan"), device="cuda").to(torch.bfloat16)
+        C.rmsnorm_bwd(dy, x, w, rstd, dx, dw)
+        dws.append(dw)
+    _check_no_device_error()
+    xf = x.float()
+    xhat = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)
+    ref = (dy.float() * xhat).sum(0)
+    assert _rel_err(dws[0], ref) < 1e-2
+    assert torch.equal(dws[0], dws[1])
 
 
 def test_linear_wgrad_splitk_policy():
