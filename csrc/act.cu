@@ -207,61 +207,95 @@ void scale_by_scalar(void* x, int64_t n, const float* s_dev, cudaStream_t s) {
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
-// Few slices (split-K): a thread per 4 outputs loops over the slices.  Many
-// slices (block partials of a weight gradient): each of 8 warps sums a
-// contiguous range of slices for 128 columns, the block adds the 8 warp
-// results in order.  Both orders are fixed, so the sums are reproducible.
-__global__ void sum_slices_few_kernel(const float* __restrict__ parts, int slices, int64_t len, int64_t stride,
-                                      void* __restrict__ out, bool out_bf16, bool accumulate) {
-  for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 4; i < len;
-       i += (int64_t)gridDim.x * blockDim.x * 4) {
-    const int n = len - i < 4 ? (int)(len - i) : 4;
-    float a[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int k = 0; k < slices; ++k)
-      for (int j = 0; j < n; ++j) a[j] += parts[(int64_t)k * stride + i + j];
-    for (int j = 0; j < n; ++j) {
-      if (out_bf16) {
-        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + i + j;
-        *o = __float2bfloat16(a[j] + (accumulate ? __bfloat162float(*o) : 0.f));
-      } else {
-        float* o = reinterpret_cast<float*>(out) + i + j;
-        *o = a[j] + (accumulate ? *o : 0.f);
-      }
+// Few slices (split-K): a thread per 4 outputs issues one 16-byte load per
+// slice, then adds them in slice order.  Many slices (block partials of a
+// weight gradient): a 1024-thread block owns 32 columns, warp w adds slices
+// w, w + 32, ... (one coalesced 128-byte row per load) and the 32 warp sums
+// are added in warp order.  Both orders are fixed, so the sums are
+// reproducible.
+__device__ __forceinline__ void store4_out(void* out, bool out_bf16, bool accumulate, int64_t i, float4 a) {
+  if (out_bf16) {
+    uint2* o = reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(out) + i);
+    if (accumulate) {
+      const uint2 old = *o;
+      const float2 p = unpack_bf16x2(old.x), q = unpack_bf16x2(old.y);
+      a.x += p.x; a.y += p.y; a.z += q.x; a.w += q.y;
     }
+    *o = make_uint2(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w));
+  } else {
+    float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + i);
+    if (accumulate) {
+      const float4 p = *o;
+      a.x += p.x; a.y += p.y; a.z += p.z; a.w += p.w;
+    }
+    *o = a;
   }
 }
 
-__global__ void sum_slices_many_kernel(const float* __restrict__ parts, int slices, int64_t len, int64_t stride,
-                                       void* __restrict__ out, bool out_bf16, bool accumulate) {
-  __shared__ float part[8][128];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t c0 = (int64_t)blockIdx.x * 128;
-  const int per = (slices + 7) / 8;
-  const int k0 = warp * per, k1 = min(slices, k0 + per);
-  float a[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int k = k0; k < k1; ++k)
+__device__ __forceinline__ void store1_out(void* out, bool out_bf16, bool accumulate, int64_t i, float a) {
+  if (out_bf16) {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + i;
+    *o = __float2bfloat16(a + (accumulate ? __bfloat162float(*o) : 0.f));
+  } else {
+    float* o = reinterpret_cast<float*>(out) + i;
+    *o = a + (accumulate ? *o : 0.f);
+  }
+}
+
+constexpr int kFewSlices = 8;
+
+__global__ void sum_slices_few_vec_kernel(const float* __restrict__ parts, int slices, int64_t len4, int64_t stride,
+                                          void* __restrict__ out, bool out_bf16, bool accumulate) {
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < len4; v += (int64_t)gridDim.x * blockDim.x) {
+    float4 x[kFewSlices];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int64_t c = c0 + lane * 4 + j;
-      if (c < len) a[j] += parts[(int64_t)k * stride + c];
-    }
+    for (int k = 0; k < kFewSlices; ++k)
+      if (k < slices) x[k] = __ldcs(reinterpret_cast<const float4*>(parts + (int64_t)k * stride) + v);
+    float4 a = x[0];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) part[warp][lane * 4 + j] = a[j];
-  __syncthreads();
-  if (threadIdx.x < 128) {
-    const int64_t c = c0 + threadIdx.x;
-    if (c < len) {
-      float t = 0.f;
-#pragma unroll
-      for (int w = 0; w < 8; ++w) t += part[w][threadIdx.x];
-      if (out_bf16) {
-        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + c;
-        *o = __float2bfloat16(t + (accumulate ? __bfloat162float(*o) : 0.f));
-      } else {
-        float* o = reinterpret_cast<float*>(out) + c;
-        *o = t + (accumulate ? *o : 0.f);
+    for (int k = 1; k < kFewSlices; ++k)
+      if (k < slices) {
+        a.x += x[k].x; a.y += x[k].y; a.z += x[k].z; a.w += x[k].w;
       }
+    store4_out(out, out_bf16, accumulate, v * 4, a);
+  }
+}
+
+__global__ void sum_slices_few_kernel(const float* __restrict__ parts, int slices, int64_t len, int64_t stride,
+                                      void* __restrict__ out, bool out_bf16, bool accumulate) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < len; i += (int64_t)gridDim.x * blockDim.x) {
+    float a = 0.f;
+    for (int k = 0; k < slices; ++k) a += parts[(int64_t)k * stride + i];
+    store1_out(out, out_bf16, accumulate, i, a);
+  }
+}
+
+__global__ void __launch_bounds__(1024) sum_slices_many_kernel(const float* __restrict__ parts, int slices,
+                                                               int64_t len, int64_t stride, void* __restrict__ out,
+                                                               bool out_bf16, bool accumulate) {
+  __shared__ float part[32][33];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c = (int64_t)blockIdx.x * 32 + lane;
+  float a = 0.f;
+  if (c < len) {
+    int k = warp;
+    for (; k + 96 < slices; k += 128) {  // four independent loads in flight
+      const float x0 = parts[(int64_t)k * stride + c], x1 = parts[(int64_t)(k + 32) * stride + c];
+      const float x2 = parts[(int64_t)(k + 64) * stride + c], x3 = parts[(int64_t)(k + 96) * stride + c];
+      a += x0;
+      a += x1;
+      a += x2;
+      a += x3;
     }
+    for (; k < slices; k += 32) a += parts[(int64_t)k * stride + c];
+  }
+  part[warp][lane] = a;
+  __syncthreads();
+  if (warp == 0 && c < len) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 32; ++w) t += part[w][lane];
+    store1_out(out, out_bf16, accumulate, c, t);
   }
 }
 
@@ -269,11 +303,17 @@ void sum_slices(const float* parts, int slices, int64_t len, int64_t stride, voi
                 bool accumulate, cudaStream_t s) {
   PB_CHECK(slices >= 1 && len >= 0 && stride >= len, "sum_slices: shapes");
   if (len == 0) return;
-  if (slices <= 8) {
-    sum_slices_few_kernel<<<grid_for((len + 3) / 4, 256), 256, 0, s>>>(parts, slices, len, stride, out, out_bf16,
+  if (slices <= kFewSlices) {
+    const bool vec = len % 4 == 0 && stride % 4 == 0 && (reinterpret_cast<uintptr_t>(parts) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(out) & (out_bf16 ? 7 : 15)) == 0;
+    if (vec)
+      sum_slices_few_vec_kernel<<<grid_for(len / 4, 256), 256, 0, s>>>(parts, slices, len / 4, stride, out, out_bf16,
                                                                        accumulate);
+    else
+      sum_slices_few_kernel<<<grid_for(len, 256), 256, 0, s>>>(parts, slices, len, stride, out, out_bf16,
+                                                               accumulate);
   } else {
-    sum_slices_many_kernel<<<(unsigned)((len + 127) / 128), 256, 0, s>>>(parts, slices, len, stride, out, out_bf16,
+    sum_slices_many_kernel<<<(unsigned)((len + 31) / 32), 1024, 0, s>>>(parts, slices, len, stride, out, out_bf16,
                                                                         accumulate);
   }
   PB_CUDA_CHECK(cudaGetLastError());

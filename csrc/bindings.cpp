@@ -23,7 +23,7 @@ cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 //   out: [M, N] bf16 or fp32 depending on epi
 void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, bool b_mn, int64_t epi,
           double alpha, const c10::optional<at::Tensor>& r, int64_t b_up_offset, int64_t n_out, int64_t kernel,
-          int64_t splits) {
+          int64_t splits, const c10::optional<at::Tensor>& ws, bool accumulate) {
   CHECK_CUDA_BF16(a);
   CHECK_CUDA_BF16(b);
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm: 2-D operands expected");
@@ -55,12 +55,22 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, 
     p.N = (int)n_out;
     TORCH_CHECK(b_up_offset + n_out <= b.size(0), "gemm: swiglu B too small");
   }
-  // kEpiSliceF32: out stacks the split-K slices, [splits * M, N]
-  const int64_t out_rows = epi == pb::kEpiSliceF32 ? (int64_t)p.M * splits : p.M;
-  TORCH_CHECK(out.size(0) == out_rows && out.size(1) == p.N, "gemm: output shape mismatch");
-  const bool f32 = epi == pb::kEpiStoreF32 || epi == pb::kEpiAccumF32 || epi == pb::kEpiAtomicF32 ||
-                   epi == pb::kEpiSliceF32;
-  TORCH_CHECK(out.scalar_type() == (f32 ? at::kFloat : at::kBFloat16), "gemm: output dtype mismatch");
+  TORCH_CHECK(out.size(0) == p.M && out.size(1) == p.N, "gemm: output shape mismatch");
+  if (epi == pb::kEpiSplitOrdered) {
+    // ws: fp32 [M, >= N] running sums of the K slices (contents irrelevant);
+    // out: bf16 or fp32, written (or added to, accumulate) by the last slice
+    TORCH_CHECK(ws.has_value() && ws->defined() && ws->is_cuda() && ws->scalar_type() == at::kFloat &&
+                    ws->dim() == 2 && ws->stride(1) == 1 && ws->size(0) >= p.M && ws->size(1) >= p.N,
+                "gemm: the ordered split-K epilogue needs an fp32 workspace [M, N]");
+    TORCH_CHECK(out.scalar_type() == at::kFloat || out.scalar_type() == at::kBFloat16, "gemm: output dtype");
+    p.ws = ws->data_ptr<float>();
+    p.ws_ld = ws->stride(0);
+    p.out_f32 = out.scalar_type() == at::kFloat;
+    p.accumulate = accumulate;
+  } else {
+    const bool f32 = epi == pb::kEpiStoreF32 || epi == pb::kEpiAccumF32 || epi == pb::kEpiAtomicF32;
+    TORCH_CHECK(out.scalar_type() == (f32 ? at::kFloat : at::kBFloat16), "gemm: output dtype mismatch");
+  }
   if (r.has_value() && r->defined()) {
     CHECK_CUDA_BF16(*r);
     TORCH_CHECK(r->stride(1) == 1, "gemm: r needs unit inner stride");
@@ -268,7 +278,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("b"), pybind11::arg("out"), pybind11::arg("a_mn"), pybind11::arg("b_mn"),
         pybind11::arg("epi"), pybind11::arg("alpha"), pybind11::arg("r") = pybind11::none(),
         pybind11::arg("b_up_offset") = 0, pybind11::arg("n_out") = 0, pybind11::arg("kernel") = 0,
-        pybind11::arg("splits") = 1);
+        pybind11::arg("splits") = 1, pybind11::arg("ws") = pybind11::none(), pybind11::arg("accumulate") = false);
   m.def("gemm_ag", &gemm_ag, "GEMM with the sequence-parallel all-gather of A in the same kernel",
         pybind11::arg("dst"), pybind11::arg("src_ptrs"), pybind11::arg("src_ld"), pybind11::arg("flags"),
         pybind11::arg("target"), pybind11::arg("seq"), pybind11::arg("seq_local"), pybind11::arg("batch"),

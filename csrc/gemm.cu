@@ -236,14 +236,15 @@ void gemm_bf16(const GemmParams& p, cudaStream_t stream) {
   PB_CHECK(p.lda % 8 == 0 && p.ldb % 8 == 0, "gemm: lda/ldb must be multiples of 8 elements");
   PB_CHECK((reinterpret_cast<uintptr_t>(p.A) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.B) & 15) == 0,
            "gemm: A/B must be 16-byte aligned");
-  const bool f32 =
-      p.epi == kEpiStoreF32 || p.epi == kEpiAccumF32 || p.epi == kEpiAtomicF32 || p.epi == kEpiSliceF32;
+  const bool f32 = p.epi == kEpiStoreF32 || p.epi == kEpiAccumF32 || p.epi == kEpiAtomicF32 ||
+                   (p.epi == kEpiSplitOrdered && p.out_f32);
   PB_CHECK(p.ldc % (f32 ? 4 : 8) == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0,
            "gemm: C must be 16-byte aligned with a 16-byte row stride");
   if (p.epi == kEpiSwiGLU) PB_CHECK(!p.a_mn && !p.b_mn, "gemm: SwiGLU epilogue needs K-major operands");
   // The CTA-pair kernel (256-row tiles) wins on every training shape measured
   // with M >= 256; smaller M keeps the one-CTA kernel.
-  if (p.kernel == 2 || p.gather || p.scatter || p.splits > 1 || (p.kernel == 0 && p.M >= 256))
+  if (p.kernel == 2 || p.gather || p.scatter || p.splits > 1 || p.epi == kEpiSplitOrdered ||
+      (p.kernel == 0 && p.M >= 256))
     return gemm_bf16_pair(p, stream);
   if (p.epi == kEpiSwiGLU) {
     launch<256, false, false, true>(p, stream);

@@ -23,8 +23,11 @@ enum GemmEpilogue : int {
                           // apart): C(bf16) = silu(g)*u, and if R != null, R(bf16) receives the
                           // raw [g | u] pre-activations (ldr) for the backward.
   kEpiAtomicF32 = 6,      // C(f32) += alpha*acc with atomic adds (split-K partial sums)
-  kEpiSliceF32 = 7,       // split-K: slice s of C(f32) [splits][M][ldc] = alpha*acc of K slice s
-                          // (no atomics; sum_slices adds the slices in a fixed order)
+  kEpiSplitOrdered = 7,   // split-K without atomics: K slice s adds alpha*acc to the fp32 running
+                          // sum of slices 0..s-1 (ws, ld ws_ld) once slice s-1 of the same tile
+                          // published it, and the last slice writes C (bf16, or fp32 when
+                          // out_f32; added to C's old value when accumulate).  The slices add in
+                          // slice order, so the result has the same bits on every run.
 };
 
 // Sequence-parallel reduce-scatter epilogue: output row m = b*seq + s (a row
@@ -68,7 +71,11 @@ struct GemmParams {
   int64_t b_up_offset;  // kEpiSwiGLU: row offset (in N units) of the "up" half of B
   int max_ctas;         // 0 = one CTA per SM
   int kernel = 0;       // 0 = choose, 1 = one-CTA kernel, 2 = CTA-pair kernel
-  int splits = 1;       // split-K slices (CTA-pair kernel, kEpiAtomicF32 only)
+  int splits = 1;       // split-K slices (CTA-pair kernel, kEpiAtomicF32 / kEpiSplitOrdered)
+  float* ws = nullptr;  // kEpiSplitOrdered: fp32 running sums [M, ws_ld] (no initial value needed)
+  int64_t ws_ld = 0;
+  bool out_f32 = false;     // kEpiSplitOrdered: C is fp32 (else bf16)
+  bool accumulate = false;  // kEpiSplitOrdered: C += result
   const ScatterArgs* scatter = nullptr;  // kEpiStoreBf16 rows to their sequence-parallel owners
   const GatherArgs* gather = nullptr;    // A assembled from sequence-parallel shards in-kernel
 };

@@ -19,7 +19,11 @@ struct EpiArgs {
   int64_t up_col;  // kEpiSwiGLU: column of the "up" half inside R
   ScatterArgs sc;  // sc.nranks > 0: kEpiStoreBf16 rows go to their owners
   int tma;         // CTA-pair kernel: stage tiles in shared memory and store them with TMA
-  int64_t slice_stride;  // kEpiSliceF32: elements between consecutive split-K slices of C
+  float* ws;       // kEpiSplitOrdered: fp32 running sums of the K slices
+  int64_t ws_ld;
+  int* cnt;        // kEpiSplitOrdered: per (tile, CTA) count of published epilogue warps
+  int out_f32;     // kEpiSplitOrdered: C is fp32
+  int accum;       // kEpiSplitOrdered: C += result
 };
 
 // TMA-store epilogue staging, per epilogue warp: three 32 x 32 bf16 boxes of

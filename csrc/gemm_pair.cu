@@ -55,6 +55,109 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   return v;
 }
 
+// Ordered split-K (kEpiSplitOrdered).  Work item (tile, slice sl) of a CTA
+// waits until the 4 epilogue warps of (tile, sl - 1) on the same CTA rank have
+// published their rows of the running fp32 sum (*cnt >= 4 * sl), adds its own
+// product and publishes again; the last slice writes the output instead and
+// the fourth of its warps to finish returns the counter to zero for the next
+// launch.  The wait is bounded: on timeout the error word gets
+// kErrSplitTimeout and the warp skips its rows (the host then clears the
+// counters with the error word).  Waits cannot deadlock: every slice waits
+// only on a lower work item, every CTA handles its items in increasing order
+// and all clusters of the persistent grid are resident together.
+__device__ __forceinline__ bool split_wait(const int* cnt, int target, int* err) {
+  bool ok = true;
+  if (target > 0) {
+    const uint64_t t0 = globaltimer();
+    uint32_t it = 0;
+    while (ld_acquire_gpu(cnt) < target) {
+      if ((++it & 63u) == 0) {
+        // another role's error ends the wait only after 20 ms: an error word
+        // left set by an earlier step must not make a healthy slice give up
+        const uint64_t dt = globaltimer() - t0;
+        if (dt > PB_SPIN_LIMIT_NS || (dt > 20000000ull && *((volatile int*)err) != 0)) {
+          record_error(err, kErrSplitTimeout);
+          ok = false;
+          break;
+        }
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
+template <int BN>
+__device__ __forceinline__ void epilogue_split(const EpiArgs& ep, uint32_t t_row, int m, int M, int N, int n_base,
+                                               bool first, bool last, bool ok) {
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    float v[32];
+    tmem_ld32(t_row + c, v);
+    tmem_wait_ld();
+    const int n0 = n_base + c;
+    if (!ok || m >= M || n0 >= N) continue;
+    const bool full = n0 + 32 <= N;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] *= ep.alpha;
+    float* wrow = ep.ws + (int64_t)m * ep.ws_ld + n0;
+    if (!first) {
+      if (full) {
+        const float4* w4 = reinterpret_cast<const float4*>(wrow);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 o = __ldcg(w4 + q);
+          v[q * 4] += o.x; v[q * 4 + 1] += o.y; v[q * 4 + 2] += o.z; v[q * 4 + 3] += o.w;
+        }
+      } else {
+        gemm_detail::for_cols(n0, N, [&](int j) { v[j] += __ldcg(wrow + j); });
+      }
+    }
+    if (!last) {
+      if (full) {
+        float4* w4 = reinterpret_cast<float4*>(wrow);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) __stcg(w4 + q, make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]));
+      } else {
+        gemm_detail::for_cols(n0, N, [&](int j) { __stcg(wrow + j, v[j]); });
+      }
+    } else if (ep.out_f32) {
+      float* dst = reinterpret_cast<float*>(ep.C) + (int64_t)m * ep.ldc + n0;
+      if (full) {
+        float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 o = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+          if (ep.accum) {
+            const float4 p = d4[q];
+            o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+          }
+          d4[q] = o;
+        }
+      } else {
+        gemm_detail::for_cols(n0, N, [&](int j) { dst[j] = ep.accum ? dst[j] + v[j] : v[j]; });
+      }
+    } else {
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ep.C) + (int64_t)m * ep.ldc + n0;
+      if (ep.accum) {
+        float r[32];
+        gemm_detail::load_row_bf16(dst, r, n0, N);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += r[j];
+      }
+      gemm_detail::store_row_bf16(dst, v, n0, N);
+    }
+  }
+}
+
+__device__ __forceinline__ void split_publish(int* cnt, int sl, bool last, int lane) {
+  if (!last) __threadfence();  // this warp's running-sum rows before the count
+  __syncwarp();
+  if (lane == 0) {
+    const int old = atomicAdd(cnt, 1);
+    if (last && old == 4 * sl + 3) atomicExch(cnt, 0);  // every warp of every slice has arrived
+  }
+}
+
 // Copy warps of the gather variant: piece q of the pieces_per_block pieces of
 // block `blk` (kGatherRowsPerPiece rows of K elements, contiguous in both the
 // source shard and the gathered buffer), then publish it on flags[blk].
@@ -258,16 +361,22 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
       const int m = tm * 2 * BM_CTA + (int)rank * BM_CTA + row;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       const uint32_t tempty = mapa_shared(smem_u32(&tempty_bar[acc]), 0);
-      EpiArgs epw = ep;  // kEpiSliceF32: this work item's K slice has its own slice of C
-      if (ep.epi == kEpiSliceF32) epw.C = reinterpret_cast<float*>(ep.C) + (int64_t)(w / num_tiles) * ep.slice_stride;
-      if (ep.tma) {
+      if (ep.epi == kEpiSplitOrdered) {
+        const int sl = w / num_tiles;
+        int* cnt = ep.cnt + 2 * tile + (int)rank;
+        const bool ok = split_wait(cnt, 4 * sl, err);
+        epilogue_split<BN>(ep, t_row, m, M, N, tn * BN_OUT, sl == 0, sl == splits - 1, ok);
+        tc_fence_before();
+        mbar_arrive_cluster(tempty);
+        if (splits > 1) split_publish(cnt, sl, sl == splits - 1, lane);
+      } else if (ep.tma) {
         gemm_detail::epilogue_warp_tma<BN, SWIGLU>(ep, &tmC, &tmR, t_row, stage, lane, m - lane, M, N, tn * BN_OUT,
                                                    [&] {
                                                      tc_fence_before();
                                                      mbar_arrive_cluster(tempty);
                                                    });
       } else {
-        gemm_detail::epilogue_row<BN, SWIGLU>(epw, t_row, m, M, N, tn * BN_OUT);
+        gemm_detail::epilogue_row<BN, SWIGLU>(ep, t_row, m, M, N, tn * BN_OUT);
         tc_fence_before();
         mbar_arrive_cluster(tempty);
       }
@@ -332,7 +441,17 @@ void launch_pair(const GemmParams& p, cudaStream_t stream) {
     tb = B_MN ? make_tmap_2d_bf16(p.B, p.N, p.K, p.ldb, 64, BK)
               : make_tmap_2d_bf16(p.B, p.K, p.N, p.ldb, BK, Cfg::B_HALF);
   EpiArgs ep{p.C, p.R, p.ldc, p.ldr, p.alpha, p.epi, SWIGLU ? p.b_up_offset : 0};
-  ep.slice_stride = (int64_t)p.M * p.ldc;
+  if (p.epi == kEpiSplitOrdered) {
+    const int64_t tiles_mn = ((p.M + 2 * BM_CTA - 1) / (2 * BM_CTA)) * ((p.N + BN - 1) / BN);
+    PB_CHECK(2 * tiles_mn <= kSplitSlotInts, "gemm: ordered split-K supports at most 4096 output tiles");
+    PB_CHECK(p.ws != nullptr && p.ws_ld >= p.N && p.ws_ld % 4 == 0 && (reinterpret_cast<uintptr_t>(p.ws) & 15) == 0,
+             "gemm: ordered split-K needs a 16-byte aligned fp32 workspace with ld % 4 == 0");
+    ep.ws = p.ws;
+    ep.ws_ld = p.ws_ld;
+    ep.cnt = split_counters(dev);
+    ep.out_f32 = p.out_f32 ? 1 : 0;
+    ep.accum = p.accumulate ? 1 : 0;
+  }
   if (p.scatter) ep.sc = *p.scatter;
   // TMA-store epilogue for the bf16 store and SwiGLU epilogues into local memory
   // (16-byte aligned bases and row strides; SwiGLU: whole 32-column chunks so a
@@ -375,8 +494,8 @@ void gemm_bf16_pair(const GemmParams& p, cudaStream_t stream) {
     return launch_pair<256, false, true, false, true>(p, stream);
   }
   if (p.scatter) PB_CHECK(p.epi == kEpiStoreBf16 && p.scatter->nranks <= 8, "gemm: scatter needs the bf16 store epilogue");
-  PB_CHECK(p.splits <= 1 || ((p.epi == kEpiAtomicF32 || p.epi == kEpiSliceF32) && !p.gather && !p.scatter),
-           "gemm: split-K needs the atomic or the slice fp32 epilogue");
+  PB_CHECK(p.splits <= 1 || ((p.epi == kEpiAtomicF32 || p.epi == kEpiSplitOrdered) && !p.gather && !p.scatter),
+           "gemm: split-K needs the atomic or the ordered epilogue");
   if (p.epi == kEpiSwiGLU) return launch_pair<256, false, false, true>(p, stream);
   if (!p.a_mn && !p.b_mn) return launch_pair<256, false, false, false>(p, stream);
   if (!p.a_mn && p.b_mn) return launch_pair<256, false, true, false>(p, stream);

@@ -27,6 +27,12 @@ EncodeTiledFn encode_fn() {
 
 std::mutex g_err_mu;
 std::vector<int*> g_err_words;
+std::vector<unsigned> g_split_next;
+
+// Device block per GPU: the 256-byte error word area, then kSplitSlots
+// counter slots of kSplitSlotInts ints for the ordered split-K epilogue.
+constexpr size_t kErrBytes = 256;
+constexpr size_t kBlockBytes = kErrBytes + (size_t)kSplitSlots * kSplitSlotInts * sizeof(int);
 
 int cur_device(int device) {
   if (device >= 0) return device;
@@ -45,12 +51,21 @@ int* error_word(int device) {
     PB_CUDA_CHECK(cudaGetDevice(&prev));
     PB_CUDA_CHECK(cudaSetDevice(device));
     int* p = nullptr;
-    PB_CUDA_CHECK(cudaMalloc(&p, 256));
-    PB_CUDA_CHECK(cudaMemset(p, 0, 256));
+    PB_CUDA_CHECK(cudaMalloc(&p, kBlockBytes));
+    PB_CUDA_CHECK(cudaMemset(p, 0, kBlockBytes));
     PB_CUDA_CHECK(cudaSetDevice(prev));
     g_err_words[device] = p;
   }
   return g_err_words[device];
+}
+
+int* split_counters(int device) {
+  device = cur_device(device);
+  int* base = error_word(device);
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  if ((int)g_split_next.size() <= device) g_split_next.resize(device + 1, 0u);
+  const unsigned slot = g_split_next[device]++ % kSplitSlots;
+  return base + kErrBytes / sizeof(int) + (size_t)slot * kSplitSlotInts;
 }
 
 int read_error(int device) {
@@ -60,7 +75,8 @@ int read_error(int device) {
 }
 
 void clear_error(int device) {
-  PB_CUDA_CHECK(cudaMemset(error_word(device), 0, sizeof(int)));
+  // a kernel that gave up may have left split-K counters mid-count: reset them too
+  PB_CUDA_CHECK(cudaMemset(error_word(device), 0, kBlockBytes));
 }
 
 int num_sms(int device) {

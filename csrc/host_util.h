@@ -29,6 +29,12 @@ namespace pb {
 // zero-initialised).  Kernels record timeouts there; the host reads it with
 // read_error() and clears it with clear_error().
 int* error_word(int device = -1);
+// Counter slot (kSplitSlotInts zeroed ints) for one ordered split-K GEMM launch:
+// the slots rotate, so launches that may run concurrently on different streams
+// use different counters; each launch leaves its counters at zero.
+constexpr int kSplitSlots = 16;
+constexpr int kSplitSlotInts = 8192;
+int* split_counters(int device = -1);
 int read_error(int device = -1);
 void clear_error(int device = -1);
 

@@ -26,6 +26,7 @@ enum ErrorCode : int {
   kErrPeerTimeout = 2,
   kErrBadArg = 3,
   kErrMoeCapacity = 4,  // an MoE layout needed more rows than its worst-case buffers
+  kErrSplitTimeout = 5,  // a split-K slice waited too long for the previous slice of its tile
 };
 
 __device__ __forceinline__ void record_error(int* err, int code) {

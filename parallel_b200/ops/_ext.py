@@ -66,4 +66,5 @@ def check_device_errors(device: int | None = None) -> None:
     if code:
         _C.clear_error(dev)
         raise RuntimeError(f"parallel_b200 kernel reported error code {code} on cuda:{dev} "
-                           "(1 = pipeline wait timeout, 2 = peer wait timeout)")
+                           "(1 = pipeline wait timeout, 2 = peer wait timeout, 3 = bad argument, "
+                           "4 = MoE layout over capacity, 5 = split-K slice wait timeout)")

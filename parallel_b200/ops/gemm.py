@@ -23,7 +23,7 @@ EPI_ACCUM_BF16 = 3
 EPI_ACCUM_F32 = 4
 EPI_SWIGLU = 5
 EPI_ATOMIC_F32 = 6
-EPI_SLICE_F32 = 7
+EPI_SPLIT_ORDERED = 7
 
 # Split-K for long-K products with few CTA-pair tiles (the weight gradients
 # reduce over all tokens): pick the slice count that minimises waves per unit
@@ -140,13 +140,12 @@ def linear_wgrad(g: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = No
     M, N, K = g2.shape[1], x2.shape[1], g2.shape[0]
     splits = _splitk(M, N, K)
     if splits > 1:
-        # split-K over the tokens: each K slice stores its own fp32 partial
-        # product, one kernel adds the slices in slice order into out (bf16
-        # or fp32, optionally accumulating): no zero fill, no atomics, no cast,
-        # and the same bits on every run
-        ws = torch.empty(splits * M, N, dtype=torch.float32, device=g.device)
-        ext().gemm(g2, x2, ws, True, True, EPI_SLICE_F32, 1.0, splits=splits)
-        ext().sum_slices(ws.view(splits, M, N), out, accumulate)
+        # split-K over the tokens: slice s adds its product to the fp32 running
+        # sum of slices < s inside the GEMM and the last slice writes out (bf16
+        # or fp32, optionally accumulating): no zero fill, no atomics, no
+        # separate cast, and the same bits on every run
+        ws = torch.empty(M, N, dtype=torch.float32, device=g.device)
+        ext().gemm(g2, x2, out, True, True, EPI_SPLIT_ORDERED, 1.0, splits=splits, ws=ws, accumulate=accumulate)
         return out
     if out.dtype == torch.float32:
         epi = EPI_ACCUM_F32 if accumulate else EPI_STORE_F32

@@ -469,28 +469,27 @@ def test_gemm_splitk_atomic(M, N, K, splits):
     assert _rel_err(out, ref) < 1e-3
 
 
-@pytest.mark.parametrize("M,N,K,splits", [(1024, 3072, 8192, 3), (1000, 520, 4096, 2)])
-def test_gemm_splitk_slices_sum_in_fixed_order(M, N, K, splits):
-    """Split-K slices stored side by side (epilogue 7) and added by sum_slices:
-    the same result as fp32 PyTorch, and the same bits on every run."""
+@pytest.mark.parametrize("M,N,K,splits", [(1024, 3072, 8192, 3), (1000, 520, 4096, 2), (256, 1024, 8192, 4)])
+@pytest.mark.parametrize("out_dtype,accumulate", [(torch.bfloat16, False), (torch.float32, True)])
+def test_gemm_splitk_ordered(M, N, K, splits, out_dtype, accumulate):
+    """Ordered split-K (epilogue 7): each K slice adds onto the previous
+    slices' running sum inside the GEMM and the last slice writes the output:
+    the fp32 PyTorch result, the same bits on every run, counters left at
+    zero for the next launch (a second launch agrees with the first)."""
     C = _ext()
     torch.manual_seed(9)
     g = torch.randn(K, M, device="cuda").to(torch.bfloat16)
     x = torch.randn(K, N, device="cuda").to(torch.bfloat16)
-    ref = g.float().t() @ x.float()
+    ref = g.float().t() @ x.float() + (0.25 if accumulate else 0.0)
     outs = []
-    for _ in range(2):
-        ws = torch.full((splits * M, N), float("nan"), device="cuda")  # every element is written
-        C.gemm(g, x, ws, True, True, 7, 1.0, splits=splits)
-        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-        C.sum_slices(ws.view(splits, M, N), out, False)
+    for _ in range(3):
+        ws = torch.full((M, N), float("nan"), device="cuda")  # contents never read before written
+        out = torch.full((M, N), 0.25 if accumulate else float("nan"), device="cuda", dtype=out_dtype)
+        C.gemm(g, x, out, True, True, 7, 1.0, splits=splits, ws=ws, accumulate=accumulate)
         outs.append(out)
     _check_no_device_error()
-    assert _rel_err(outs[0], ref) < 1e-2
-    assert torch.equal(outs[0], outs[1])
-    acc = torch.full((M, N), 0.25, device="cuda")
-    C.sum_slices(ws.view(splits, M, N), acc, True)
-    assert _rel_err(acc, ref + 0.25) < 1e-2
+    assert _rel_err(outs[0], ref) < (1e-2 if out_dtype == torch.bfloat16 else 1e-4)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
 
 
 @pytest.mark.parametrize("T,H", [(3000, 4096), (777, 2048), (40000, 1024)])
