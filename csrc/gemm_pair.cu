@@ -86,11 +86,29 @@ __device__ __forceinline__ bool split_wait(const int* cnt, int target, int* err)
   return __all_sync(0xffffffffu, ok);
 }
 
+// Running-sum rows are read one 32-column chunk ahead (the loads of chunk
+// c + 1 are in flight while chunk c is added and stored), so a slice's
+// epilogue is not a chain of dependent L2 round trips.
+__device__ __forceinline__ bool split_prefetch(const EpiArgs& ep, int m, int M, int N, int n0, float4* dst) {
+  if (m >= M || n0 + 32 > N) return false;
+  const float4* w4 = reinterpret_cast<const float4*>(ep.ws + (int64_t)m * ep.ws_ld + n0);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) dst[q] = __ldcg(w4 + q);
+  return true;
+}
+
 template <int BN>
 __device__ __forceinline__ void epilogue_split(const EpiArgs& ep, uint32_t t_row, int m, int M, int N, int n_base,
                                                bool first, bool last, bool ok) {
+  float4 nx[8];
+  bool nx_ok = !first && ok && split_prefetch(ep, m, M, N, n_base, nx);
 #pragma unroll 1
   for (int c = 0; c < BN; c += 32) {
+    float4 cu[8];
+    const bool cu_ok = nx_ok;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) cu[q] = nx[q];
+    if (c + 32 < BN) nx_ok = !first && ok && split_prefetch(ep, m, M, N, n_base + c + 32, nx);
     float v[32];
     tmem_ld32(t_row + c, v);
     tmem_wait_ld();
@@ -101,12 +119,10 @@ __device__ __forceinline__ void epilogue_split(const EpiArgs& ep, uint32_t t_row
     for (int j = 0; j < 32; ++j) v[j] *= ep.alpha;
     float* wrow = ep.ws + (int64_t)m * ep.ws_ld + n0;
     if (!first) {
-      if (full) {
-        const float4* w4 = reinterpret_cast<const float4*>(wrow);
+      if (cu_ok) {
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const float4 o = __ldcg(w4 + q);
-          v[q * 4] += o.x; v[q * 4 + 1] += o.y; v[q * 4 + 2] += o.z; v[q * 4 + 3] += o.w;
+          v[q * 4] += cu[q].x; v[q * 4 + 1] += cu[q].y; v[q * 4 + 2] += cu[q].z; v[q * 4 + 3] += cu[q].w;
         }
       } else {
         gemm_detail::for_cols(n0, N, [&](int j) { v[j] += __ldcg(wrow + j); });

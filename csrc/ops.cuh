@@ -123,8 +123,11 @@ void router_fwd(const void* logits, int64_t ld, int T, int E, int K, bool renorm
 void router_bwd(const float* probs, const float* dprobs, const float* dtopv, const int64_t* topi, int T, int E, int K,
                 bool renorm, void* dlogits, int64_t ld, cudaStream_t s);
 // Load-balancing loss statistics over probabilities [R, E]: per-expert top-k
-// counts and sums of the second softmax (accumulated into counts / ssum).
-void aux_stats(const float* probs, int R, int E, int K, float* counts, float* ssum, cudaStream_t s);
+// counts and sums of the second softmax.
+// parts: [aux_stats_grid(R), 2E] block partials (counts, then sums), finished
+// by sum_slices in block order (deterministic)
+int aux_stats_grid(int R);
+void aux_stats(const float* probs, int R, int E, int K, float* parts, cudaStream_t s);
 void aux_stats_bwd(const float* probs, const float* gsum, int R, int E, float* dprobs, cudaStream_t s);
 
 }  // namespace pb

@@ -190,8 +190,17 @@ void aux_stats(const at::Tensor& probs, int64_t top_k, at::Tensor& counts, at::T
   TORCH_CHECK(probs.dim() == 2 && counts.numel() == probs.size(1) && ssum.numel() == probs.size(1),
               "aux_stats: probs [R, E], counts / sums [E]");
   const c10::cuda::CUDAGuard g(probs.device());
-  pb::aux_stats(probs.data_ptr<float>(), (int)probs.size(0), (int)probs.size(1), (int)top_k,
-                counts.data_ptr<float>(), ssum.data_ptr<float>(), cur_stream());
+  // counts / ssum are overwritten: block partials, then sums in block order
+  const int E = (int)probs.size(1);
+  const int grid = pb::aux_stats_grid((int)probs.size(0));
+  at::Tensor parts = at::empty({grid, 2 * E}, probs.options());
+  if (probs.size(0) == 0) {
+    parts.zero_();
+  } else {
+    pb::aux_stats(probs.data_ptr<float>(), (int)probs.size(0), E, (int)top_k, parts.data_ptr<float>(), cur_stream());
+  }
+  finish_partials(parts, grid, E, 2 * E, 0, counts);
+  finish_partials(parts, grid, E, 2 * E, E, ssum);
 }
 
 void aux_stats_bwd(const at::Tensor& probs, const at::Tensor& gsum, at::Tensor& dprobs) {

@@ -175,19 +175,21 @@ __global__ void router_bwd_kernel(const float* __restrict__ probs, const float* 
   }
 }
 
+// Block partials of the load-balancing statistics: a warp per row, a lane
+// owns experts lane + 32 i (registers), the block adds its warps' partials in
+// warp order and writes row blockIdx.x of parts [grid, 2E] (counts, then
+// sums); sum_slices adds the blocks in block order.  No atomics: the
+// statistics have the same bits on every run.
 template <int VPL>
-__global__ void aux_stats_kernel(const float* __restrict__ probs, int R, int E, int K, float* __restrict__ counts,
-                                 float* __restrict__ ssum) {
-  extern __shared__ float sh[];  // [2 * E]: counts, sums
-  for (int i = threadIdx.x; i < 2 * E; i += blockDim.x) sh[i] = 0.f;
-  __syncthreads();
+__global__ void aux_stats_kernel(const float* __restrict__ probs, int R, int E, int K, float* __restrict__ parts) {
+  extern __shared__ float sh[];  // [warps][2E]
   const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   const int warps = blockDim.x >> 5;
-  // lane owns experts lane + 32 i: per-warp partials stay in registers
   float acc_s[VPL], acc_c[VPL];
 #pragma unroll
   for (int i = 0; i < VPL; ++i) acc_s[i] = acc_c[i] = 0.f;
-  for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < R; t += gridDim.x * warps) {
+  for (int t = blockIdx.x * warps + warp; t < R; t += gridDim.x * warps) {
     float s[VPL];
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
@@ -204,18 +206,20 @@ __global__ void aux_stats_kernel(const float* __restrict__ probs, int R, int E, 
       if (chosen & (1u << i)) acc_c[i] += 1.f;
     }
   }
+  float* mine = sh + (size_t)warp * 2 * E;
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int e = lane + 32 * i;
     if (e < E) {
-      atomicAdd(&sh[e], acc_c[i]);
-      atomicAdd(&sh[E + e], acc_s[i]);
+      mine[e] = acc_c[i];
+      mine[E + e] = acc_s[i];
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < E; i += blockDim.x) {
-    if (sh[i] != 0.f) atomicAdd(&counts[i], sh[i]);
-    atomicAdd(&ssum[i], sh[E + i]);
+  for (int i = threadIdx.x; i < 2 * E; i += blockDim.x) {
+    float t = 0.f;
+    for (int w = 0; w < warps; ++w) t += sh[(size_t)w * 2 * E + i];
+    parts[(int64_t)blockIdx.x * 2 * E + i] = t;
   }
 }
 
@@ -282,16 +286,17 @@ void router_bwd(const float* probs, const float* dprobs, const float* dtopv, con
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
-void aux_stats(const float* probs, int R, int E, int K, float* counts, float* ssum, cudaStream_t s) {
+int aux_stats_grid(int R) { return std::max(1, std::min(2 * num_sms(), (R + 7) / 8)); }
+
+void aux_stats(const float* probs, int R, int E, int K, float* parts, cudaStream_t s) {
   PB_CHECK(K >= 1 && K <= kMaxTopK && K <= E, "aux stats: 1 <= top_k <= min(16, experts)");
-  if (R == 0) return;
-  const int blocks = std::max(1, std::min(2 * num_sms(), (R + 7) / 8));
-  const size_t sm = 2 * (size_t)E * sizeof(float);
+  const int blocks = aux_stats_grid(R);
+  const size_t sm = 8 * 2 * (size_t)E * sizeof(float);  // 8 warps x (counts, sums)
   switch (vpl_for(E)) {
-    case 1: aux_stats_kernel<1><<<blocks, 256, sm, s>>>(probs, R, E, K, counts, ssum); break;
-    case 2: aux_stats_kernel<2><<<blocks, 256, sm, s>>>(probs, R, E, K, counts, ssum); break;
-    case 4: aux_stats_kernel<4><<<blocks, 256, sm, s>>>(probs, R, E, K, counts, ssum); break;
-    default: aux_stats_kernel<8><<<blocks, 256, sm, s>>>(probs, R, E, K, counts, ssum); break;
+    case 1: aux_stats_kernel<1><<<blocks, 256, sm, s>>>(probs, R, E, K, parts); break;
+    case 2: aux_stats_kernel<2><<<blocks, 256, sm, s>>>(probs, R, E, K, parts); break;
+    case 4: aux_stats_kernel<4><<<blocks, 256, sm, s>>>(probs, R, E, K, parts); break;
+    default: aux_stats_kernel<8><<<blocks, 256, sm, s>>>(probs, R, E, K, parts); break;
   }
   PB_CUDA_CHECK(cudaGetLastError());
 }

@@ -1,6 +1,6 @@
 """Micro-benchmarks of the sm_100a kernels at the Qwen3-0.6B training shapes.
 
-    python -m parallel_b200.ops.kernel_bench attn_fwd|attn_bwd|gemm|gemm_swiglu|gemm_residual|rmsnorm_bwd|qknorm|qknorm_bwd|all [--iters N]
+    python -m parallel_b200.ops.kernel_bench attn_fwd|attn_bwd|gemm|gemm_swiglu|gemm_residual|rmsnorm_bwd|qknorm|qknorm_bwd|wgrad_split|all [--iters N]
 
 Each case runs a few warm-up launches, then times ``--iters`` launches with
 CUDA events on the current stream and prints the time per launch and the
@@ -143,9 +143,39 @@ def case_qknorm_bwd(warmup, iters):
     return f"qk-norm + RoPE bwd {T} tokens x {nh} heads: {us:.1f} us, {moved / us / 1e3:.0f} GB/s"
 
 
+def case_wgrad_split(warmup, iters):
+    """Weight-gradient GEMMs dW[M, N] = g^T x over T = B * S tokens at the
+    0.6B step's split-K shapes: one K slice, split-K with fp32 atomics (zero
+    fill + GEMM + cast) and the ordered split-K epilogue."""
+    from .gemm import EPI_ATOMIC_F32, EPI_SPLIT_ORDERED, EPI_STORE_BF16, _splitk
+
+    C = ext()
+    T = B * S
+    lines = []
+    for name, M, N in (("o_proj", H, NQ * D), ("gate_up", 2 * I, H), ("down", H, I), ("qkv", (NQ + 2 * NKV) * D, H)):
+        g = torch.randn(T, M, device="cuda", dtype=torch.bfloat16)
+        x = torch.randn(T, N, device="cuda", dtype=torch.bfloat16)
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        ws = torch.empty(M, N, device="cuda", dtype=torch.float32)
+        sp = max(2, _splitk(M, N, T))
+        t1 = _time(lambda: C.gemm(g, x, out, True, True, EPI_STORE_BF16, 1.0), warmup, iters)
+
+        def atomic():
+            ws.zero_()
+            C.gemm(g, x, ws, True, True, EPI_ATOMIC_F32, 1.0, splits=sp)
+            C.cast_f32_to_bf16(ws, out)
+
+        ta = _time(atomic, warmup, iters)
+        to = _time(lambda: C.gemm(g, x, out, True, True, EPI_SPLIT_ORDERED, 1.0, splits=sp, ws=ws), warmup, iters)
+        tf = 2 * M * N * T / 1e6
+        lines.append(f"wgrad {name} {M}x{N}x{T}: 1 slice {t1:.1f} us ({tf / t1:.0f} TF/s), {sp} slices atomic+fill+cast "
+                     f"{ta:.1f} us, {sp} slices ordered {to:.1f} us ({tf / to:.0f} TF/s); policy picks {_splitk(M, N, T)}")
+    return "\n".join(lines)
+
+
 CASES = {"attn_fwd": case_attn_fwd, "attn_bwd": case_attn_bwd, "gemm": case_gemm, "gemm_swiglu": case_gemm_swiglu,
          "gemm_residual": case_gemm_residual, "rmsnorm_bwd": case_rmsnorm_bwd, "qknorm": case_qknorm,
-         "qknorm_bwd": case_qknorm_bwd}
+         "qknorm_bwd": case_qknorm_bwd, "wgrad_split": case_wgrad_split}
 
 
 def main(argv=None):

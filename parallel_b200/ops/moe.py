@@ -322,9 +322,9 @@ class _AuxStatsFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, probs, top_k):
         E = probs.shape[1]
-        counts = torch.zeros(E, device=probs.device, dtype=torch.float32)
-        ssum = torch.zeros(E, device=probs.device, dtype=torch.float32)
-        ext().aux_stats(probs, top_k, counts, ssum)
+        counts = torch.empty(E, device=probs.device, dtype=torch.float32)
+        ssum = torch.empty(E, device=probs.device, dtype=torch.float32)
+        ext().aux_stats(probs, top_k, counts, ssum)  # overwritten, summed in a fixed order
         ctx.save_for_backward(probs)
         ctx.mark_non_differentiable(counts)
         return counts, ssum

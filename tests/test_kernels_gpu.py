@@ -579,6 +579,8 @@ def test_aux_loss_stats_match_torch():
     tpe = torch.nn.functional.one_hot(sel, E).float().mean(dim=0)
     ref = torch.sum(tpe * rw.mean(dim=0).unsqueeze(0)) * E
     assert abs(loss.item() - ref.item()) < 1e-5 * max(1.0, abs(ref.item()))
+    again = load_balancing_loss(tuple(p.detach() for p in probs), E, K)
+    assert torch.equal(again, loss.detach())  # block partials added in a fixed order
     loss.backward()
     ref.backward()
     for p, r in zip(probs, ref_probs):
