@@ -284,7 +284,7 @@ def run_ours(args, rank, world, local):
         # model-parallel configs: each rank builds only its local shards (random init)
         from parallel_b200.models.loading import load_causal_lm
 
-        model, plan = load_causal_lm(cfg, pconfig, dtype=torch.bfloat16, seed=1234)
+        model, plan = load_causal_lm(cfg, pconfig, dtype=torch.bfloat16, seed=1234, device=device)
         model.to(device)
         model.train()
         engine = ParallelEngine(model, None, pconfig, cfg, device, mp_plan=plan)
@@ -376,13 +376,53 @@ def _install_omegaconf_stub():
     sys.modules["omegaconf"] = mod
 
 
+def _ensure_reference(ref: str, local: int) -> None:
+    """Provision the unmodified reference into ``baseline/_ref`` when it is
+    missing: the offline wheelhouse install with ``--no-deps`` (``wandb`` is not
+    in the wheelhouse), built from a temporary copy of the source tree named
+    by BASELINE.json's ``reference_path`` because the build writes into its
+    source.  Local rank 0 installs; the other local ranks wait (bounded) for
+    the marker it leaves."""
+    import shutil
+
+    pkg = os.path.join(ref, "parallel")
+    if os.path.isdir(pkg):
+        return
+    marker = os.path.join(tempfile.gettempdir(), "pb_ref_install.done")
+    if local != 0:
+        t0 = time.time()
+        while not os.path.isdir(pkg) and time.time() - t0 < 600:
+            if os.path.exists(marker):
+                break
+            time.sleep(1.0)
+        if not os.path.isdir(pkg):
+            raise RuntimeError("reference not installed in baseline/_ref (local rank 0 did not install it)")
+        return
+    try:
+        src = json.load(open(os.path.join(ROOT, "BASELINE.json"))).get("reference_path", "")
+    except Exception:
+        src = ""
+    wheels = "/opt/wheelhouse"
+    if not src or not os.path.isfile(os.path.join(src, "pyproject.toml")):
+        open(marker, "w").close()
+        raise RuntimeError("reference not installed in baseline/_ref and its source tree is not on this machine")
+    tmp = tempfile.mkdtemp(prefix="pb_ref_src_")
+    shutil.copytree(src, os.path.join(tmp, "src"))
+    cmd = [sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation", "--no-deps",
+           "--find-links", wheels, "--target", ref, os.path.join(tmp, "src")]
+    proc = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True, timeout=600)
+    shutil.rmtree(tmp, ignore_errors=True)
+    open(marker, "w").close()
+    if proc.returncode != 0 or not os.path.isdir(pkg):
+        raise RuntimeError("reference install failed: " + proc.stdout.strip().splitlines()[-1][:200])
+
+
 def run_reference(args, rank, world, local):
     import torch
     import torch.distributed as dist
 
     ref = os.path.join(ROOT, "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref, "parallel")):
-        raise RuntimeError("reference not installed in baseline/_ref")
+    _ensure_reference(ref, local)
     sys.path.insert(0, ref)
     _install_omegaconf_stub()
     import transformers

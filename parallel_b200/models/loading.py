@@ -94,7 +94,7 @@ def _model_config(cfg) -> ModelConfig:
     return mcfg
 
 
-def load_causal_lm(cfg, pconfig, dtype=torch.bfloat16, seed: int | None = None):
+def load_causal_lm(cfg, pconfig, dtype=torch.bfloat16, seed: int | None = None, device=None):
     config = _model_config(cfg)
     if not pconfig.model_parallel_enabled:
         model = build_model(config, dtype=dtype, seed=seed)
@@ -110,5 +110,5 @@ def load_causal_lm(cfg, pconfig, dtype=torch.bfloat16, seed: int | None = None):
     plan = build_model_parallel_plan(config, pconfig)
     plan.validate_runtime(pconfig)
     model = load_tensor_parallel_causal_lm(cfg.model.name, config=config, pconfig=pconfig, plan=plan, dtype=dtype,
-                                           seed=seed)
+                                           seed=seed, device=device)
     return model, plan

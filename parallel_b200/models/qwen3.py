@@ -315,15 +315,18 @@ class Qwen3ForCausalLM(nn.Module):
         ones for norms."""
         std = self.config.initializer_range if std is None else std
         gen = None
+        dev = next(self.parameters()).device
         if seed is not None:
-            gen = torch.Generator(device="cpu").manual_seed(seed)
+            # the draw follows the parameters' device: a model built on the GPU
+            # (large benchmark models) draws there, one parameter at a time
+            gen = torch.Generator(device=dev).manual_seed(seed)
         with torch.no_grad():
             for name, p in self.named_parameters():
                 if name.endswith("norm.weight") or ".q_norm." in name or ".k_norm." in name or "layernorm" in name:
                     p.fill_(1.0)
                 else:
                     if gen is not None:
-                        p.copy_(torch.randn(p.shape, generator=gen, dtype=torch.float32) * std)
+                        p.copy_(torch.randn(p.shape, generator=gen, dtype=torch.float32, device=dev) * std)
                     else:
                         p.normal_(0.0, std)
 

@@ -47,7 +47,18 @@ def load_tensor_parallel_causal_lm(model_name: str, *, config, pconfig, plan: Mo
 
     tp = plan.tensor_parallel_size
     ep = plan.expert_parallel_size
-    model = Qwen3ForCausalLM(config, tp=tp, ep=ep)
+    if device is not None and torch.device(device).type == "cuda":
+        # built, drawn and cast on the GPU: a 30B-class model's local shards
+        # never pass through host memory
+        prev = torch.get_default_dtype()
+        torch.set_default_dtype(dtype)
+        try:
+            with torch.device(device):
+                model = Qwen3ForCausalLM(config, tp=tp, ep=ep)
+        finally:
+            torch.set_default_dtype(prev)
+    else:
+        model = Qwen3ForCausalLM(config, tp=tp, ep=ep)
     model.init_weights(seed=seed)
     model.to(dtype=dtype)
     full = read_state_dict(model_name) if model_name and os.path.isdir(model_name) else None
