@@ -37,7 +37,21 @@ from datetime import timedelta
 import torch
 import torch.distributed as dist
 
-GEMM_PEAK = 1.70e15   # measured cuBLAS bf16 burst on this pool (FLOP/s)
+
+
+def _measured_gemm_peak(default: float = 1.646e15) -> float:
+    """The cuBLAS bf16 burst peak measured on the machine (``MEASURED_PEAKS.json``
+    beside the repository, ``bf16_tflops``), else the last measurement on a
+    B200 of this pool."""
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                        "MEASURED_PEAKS.json")
+    try:
+        return float(json.load(open(path))["bf16_tflops"]) * 1e12
+    except Exception:
+        return default
+
+
+GEMM_PEAK = _measured_gemm_peak()  # FLOP/s
 LINK_BW = 770e9       # measured peer copy per direction (B/s)
 
 

@@ -16,8 +16,6 @@ runtimes are callables the MoE block invokes as
 """
 from __future__ import annotations
 
-from dataclasses import dataclass
-
 import torch
 import torch.distributed as dist
 
@@ -26,45 +24,60 @@ from ...profiling import collective_profile
 from .token_dispatch import TokenDispatcher
 
 
-@dataclass(frozen=True)
 class ExpertPartition:
-    num_experts: int
-    ep_size: int
-    ep_rank: int
+    """Which experts an EP rank owns: the global expert ids are split into
+    ``ep_size`` equal consecutive blocks and block ``r`` lives on rank ``r``
+    (the layout the checkpoint plans and the route plan kernel assume).
 
-    def __post_init__(self):
-        if self.ep_size < 1:
-            raise ValueError("ep_size must be positive")
-        if not 0 <= self.ep_rank < self.ep_size:
-            raise ValueError("ep_rank is outside the expert-parallel group")
-        if self.num_experts % self.ep_size:
-            raise ValueError(f"num_experts ({self.num_experts}) must be divisible by ep_size ({self.ep_size})")
+    ``localize_routes`` maps global route ids to this rank's local ids; a
+    route to another rank's expert becomes the sentinel ``local_count`` with
+    score 0, which every expert kernel skips."""
 
-    @property
-    def local_count(self) -> int:
-        return self.num_experts // self.ep_size
+    __slots__ = ("num_experts", "ep_size", "ep_rank", "local_count", "start", "stop")
 
-    @property
-    def start(self) -> int:
-        return self.ep_rank * self.local_count
+    def __init__(self, num_experts: int, ep_size: int, ep_rank: int):
+        per, rem = divmod(int(num_experts), max(int(ep_size), 1))
+        problems = []
+        if ep_size < 1:
+            problems.append(f"the expert-parallel size is {ep_size}")
+        elif rem:
+            problems.append(f"{num_experts} experts do not split evenly over {ep_size} ranks")
+        if ep_size >= 1 and not 0 <= ep_rank < ep_size:
+            problems.append(f"rank {ep_rank} is not in an expert-parallel group of {ep_size}")
+        if problems:
+            raise ValueError("invalid expert partition: " + "; ".join(problems))
+        self.num_experts, self.ep_size, self.ep_rank = int(num_experts), int(ep_size), int(ep_rank)
+        self.local_count = per
+        self.start, self.stop = ep_rank * per, (ep_rank + 1) * per
 
-    @property
-    def stop(self) -> int:
-        return self.start + self.local_count
+    def __repr__(self) -> str:
+        return (f"ExpertPartition(experts [{self.start}, {self.stop}) of {self.num_experts} on rank "
+                f"{self.ep_rank}/{self.ep_size})")
+
+    def __eq__(self, other) -> bool:
+        return isinstance(other, ExpertPartition) and (self.num_experts, self.ep_size, self.ep_rank) == (
+            other.num_experts, other.ep_size, other.ep_rank)
+
+    def __hash__(self) -> int:
+        return hash((self.num_experts, self.ep_size, self.ep_rank))
 
     @property
     def global_experts(self) -> range:
         return range(self.start, self.stop)
 
     def owner(self, global_expert: torch.Tensor) -> torch.Tensor:
-        return torch.div(global_expert, self.local_count, rounding_mode="floor")
+        """EP rank holding each global expert id."""
+        return global_expert // self.local_count
 
     def localize_routes(self, global_indices: torch.Tensor, scores: torch.Tensor):
+        """(local ids with the sentinel for foreign routes, scores with foreign
+        routes zeroed, mask of the routes this rank computes)."""
         if global_indices.shape != scores.shape:
-            raise ValueError("Expert indices and scores must have the same shape")
-        local_mask = self.owner(global_indices) == self.ep_rank
-        local_idx = (global_indices - self.start).masked_fill(~local_mask, self.local_count)
-        return local_idx, scores.masked_fill(~local_mask, 0), local_mask
+            raise ValueError(f"route ids {tuple(global_indices.shape)} and scores {tuple(scores.shape)} "
+                             "differ in shape")
+        mine = (global_indices >= self.start) & (global_indices < self.stop)
+        local = torch.where(mine, global_indices - self.start, torch.full_like(global_indices, self.local_count))
+        return local, torch.where(mine, scores, torch.zeros_like(scores)), mine
 
 
 def local_expert_range(num_experts: int, ep_size: int, ep_rank: int) -> range:
@@ -72,12 +85,16 @@ def local_expert_range(num_experts: int, ep_size: int, ep_rank: int) -> range:
 
 
 def verify_expert_modules(model, partition: ExpertPartition) -> None:
-    mods = [(n, m) for n, m in model.named_modules() if n.endswith(".mlp.experts") and hasattr(m, "num_experts")]
-    if not mods:
-        raise RuntimeError("Expert-parallel plan found no expert modules")
-    bad = [f"{n}={m.num_experts}" for n, m in mods if m.num_experts != partition.local_count]
-    if bad:
-        raise RuntimeError(f"Expected {partition.local_count} local experts per rank, got " + ", ".join(bad))
+    """Every MoE block of the loaded model must hold exactly this rank's share
+    of the experts (a model built for another EP size fails here)."""
+    counts = {name: mod.num_experts for name, mod in model.named_modules()
+              if name.endswith(".mlp.experts") and hasattr(mod, "num_experts")}
+    if not counts:
+        raise RuntimeError("expert parallelism is planned but the model has no '.mlp.experts' modules")
+    wrong = {name: n for name, n in counts.items() if n != partition.local_count}
+    if wrong:
+        listed = ", ".join(f"{name} holds {n}" for name, n in sorted(wrong.items()))
+        raise RuntimeError(f"each EP rank should hold {partition.local_count} experts per layer: {listed}")
 
 
 def _sum(value, group, fused, mode):
@@ -114,7 +131,28 @@ class _AllReduceForward(torch.autograd.Function):
         return g, None, None
 
 
-class ReplicatedTokenExpertParallel:
+class _ExpertRuntime:
+    """Installs itself as the model's expert runtime (the MoE blocks call
+    ``ctx.expert_runtime(experts, x, global_index, weights)``) and removes
+    itself again; one model at a time."""
+
+    _model = None
+
+    def apply(self, model) -> None:
+        if self._model is not None:
+            raise RuntimeError(f"{type(self).__name__} is already installed on a model")
+        model.ctx.expert_runtime = self
+        model.set_parallel_context(model.ctx)
+        self._model = model
+
+    def close(self) -> None:
+        model, self._model = self._model, None
+        if model is not None:
+            model.ctx.expert_runtime = None
+            model.set_parallel_context(model.ctx)
+
+
+class ReplicatedTokenExpertParallel(_ExpertRuntime):
     def __init__(self, partition: ExpertPartition, group, fused=None):
         self.partition = partition
         self.group = group
@@ -123,7 +161,6 @@ class ReplicatedTokenExpertParallel:
         self.fused = fused
         self.transport = LocalExpertTransport(partition.local_count, num_experts=partition.num_experts,
                                               ep_rank=partition.ep_rank, local_only=True)
-        self._model = None
 
     def __call__(self, experts, x2, global_index, weights):
         # the routing weights pass the backward all-reduce boundary before they
@@ -138,22 +175,8 @@ class ReplicatedTokenExpertParallel:
             y = experts(h, local_idx, local_w)
         return _AllReduceForward.apply(y, self.group, self.fused)
 
-    def apply(self, model) -> None:
-        if self._model is not None:
-            raise RuntimeError("Expert parallel hooks are already installed")
-        ctx = model.ctx
-        ctx.expert_runtime = self
-        model.set_parallel_context(ctx)
-        self._model = model
 
-    def close(self) -> None:
-        if self._model is not None:
-            self._model.ctx.expert_runtime = None
-            self._model.set_parallel_context(self._model.ctx)
-            self._model = None
-
-
-class SequenceParallelExpertParallel:
+class SequenceParallelExpertParallel(_ExpertRuntime):
     def __init__(self, partition: ExpertPartition, group, device=None, collectives: str = "auto"):
         self.partition = partition
         self.group = group
@@ -174,17 +197,3 @@ class SequenceParallelExpertParallel:
         hidden, idx, w, state = self.dispatcher.dispatch(x2, global_index, weights)
         y = experts(hidden, idx, w)
         return self.dispatcher.combine(y, state)
-
-    def apply(self, model) -> None:
-        if self._model is not None:
-            raise RuntimeError("Expert parallel hooks are already installed")
-        ctx = model.ctx
-        ctx.expert_runtime = self
-        model.set_parallel_context(ctx)
-        self._model = model
-
-    def close(self) -> None:
-        if self._model is not None:
-            self._model.ctx.expert_runtime = None
-            self._model.set_parallel_context(self._model.ctx)
-            self._model = None
