@@ -47,7 +47,7 @@ def parse():
     ap.add_argument("--collectives", default="auto")
     ap.add_argument("--no-graph", action="store_true", help="eager steps instead of the captured CUDA-graph step")
     ap.add_argument("--tp", type=int, default=1,
-                    help="tensor-parallel size (model-parallel configs; dp_shard = gpus / tp; eager steps)")
+                    help="tensor-parallel size (model-parallel configs; dp_shard = gpus / tp)")
     ap.add_argument("--sp", action="store_true", help="sequence parallelism over the TP group")
     ap.add_argument("--ep", action="store_true", help="expert parallelism over the TP group (MoE models)")
     ap.add_argument("--router-skew", type=float, default=0.0,
@@ -317,8 +317,8 @@ def run_ours(args, rank, world, local):
     clocks.start()
     for i in range(args.warmup):
         step(dev[i % nb])
-    # (the captured step covers data parallelism, dense or MoE; model-parallel
-    # steps run eagerly: the fused sequence-parallel kernels take host-side flag targets)
+    # the captured step covers data and model parallelism, dense or MoE
+    # (capture_unsupported names the configurations that must stay eager)
     from parallel_b200.parallel.graph_step import capture_unsupported
 
     use_graph = (not args.no_graph and capture_unsupported(engine) is None

@@ -242,3 +242,37 @@ def test_device_error_word_surfaces_as_collective_timeout():
     assert ext().read_error(0) == 0
     eng.train_step(tok[:, :-1], tok[:, 1:])  # the engine keeps working
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("name", ["small-qwen3", "small-qwen3-moe"])
+def test_training_steps_are_bitwise_reproducible(name):
+    """Two engines built from the same weights and fed the same batches end
+    bitwise equal: no kernel of the step accumulates floating point in an
+    order that varies between runs (ordered split-K, block partials summed in
+    block order, rank- and route-ordered reductions)."""
+    from parallel_b200.config import from_dotlist, load_cfg, merge
+    from parallel_b200.ops._ext import check_device_errors
+    from parallel_b200.parallel.engine import ParallelEngine
+    from parallel_b200.state import ParallelConfig
+
+    c = merge(load_cfg(argv=[]), from_dotlist(["config.device_type=cuda", "model.learning_rate=3e-3"]))
+    g = torch.Generator().manual_seed(5)
+    cfg = None
+    runs = []
+    for _ in range(2):
+        cfg, _, gpu = _pair(name)
+        if not runs:
+            toks = [torch.randint(0, cfg.vocab_size, (4, 257), generator=g).cuda() for _ in range(3)]
+        pc = ParallelConfig(c)
+        pc.set_device_mesh("cuda")
+        eng = ParallelEngine(gpu, None, pc, c, torch.device("cuda", 0))
+        losses = [eng.train_step(t[:, :-1], t[:, 1:]).detach().clone() for t in toks]
+        torch.cuda.synchronize()
+        check_device_errors()
+        runs.append((torch.stack(losses), {n: p.detach().clone() for n, p in eng.model.named_parameters()},
+                     eng.last_grad_norm.detach().clone()))
+    (la, pa, na), (lb, pb, nb) = runs
+    assert torch.equal(la, lb), (la, lb)
+    assert torch.equal(na, nb), (na, nb)
+    for n, p in pa.items():
+        assert torch.equal(p, pb[n]), n
