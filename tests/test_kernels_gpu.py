@@ -356,7 +356,10 @@ def _attn_ref(q, k, v, B, S, nq, nkv, causal=True):
 
 @pytest.mark.parametrize("B,S,nq,nkv", [(1, 128, 1, 1), (2, 256, 4, 2), (1, 384, 2, 1), (2, 200, 4, 4),
                                         (1, 1024, 8, 2)])
-def test_attention_fwd_bwd(B, S, nq, nkv):
+@pytest.mark.parametrize("exp_mode", ["f16x2", "f32"])
+def test_attention_fwd_bwd(B, S, nq, nkv, exp_mode, monkeypatch):
+    # the forward's exponentials: two per f16x2 instruction (default) or one f32 each
+    monkeypatch.setenv("PB_ATTN_EXP", exp_mode)
     C = _ext()
     torch.manual_seed(10)
     D = 128
