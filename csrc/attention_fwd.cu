@@ -23,11 +23,8 @@
 // Replaces the SDPA call HF makes for every layer in the reference
 // (attn_implementation="sdpa", parallel/parallel/engine/model_loading.py:22).
 #include <cuda_bf16.h>
-#include <cuda_fp16.h>
 
 #include <algorithm>
-#include <cstdlib>
-#include <cstring>
 #include <mutex>
 
 #include "attention.cuh"
@@ -56,19 +53,7 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Two exponentials per special-function-unit instruction: the exponents are
-// rounded to f16 (11-bit significand: for the x <= 8 that the lazy rescale
-// allows, an absolute error <= 2^-8 in x, i.e. <= 0.27% relative in 2^x,
-// below the 0.39% of the bf16 rounding P gets anyway), exponentiated as an
-// f16 pair and widened to f32 for the row sum and the bf16 pack.
-__device__ __forceinline__ float2 ex2_pair_f16(float lo, float hi) {
-  uint32_t h, e;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(h));
-  return __half22float2(*reinterpret_cast<__half2*>(&e));
-}
-
-template <bool kTrace, bool kF16Exp>
+template <bool kTrace>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int64_t ldo,
@@ -275,15 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pk[64];
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          float a0, a1;
-          if constexpr (kF16Exp) {
-            const float2 e = ex2_pair_f16(fmaf(s[2 * c], scale_log2, -mu), fmaf(s[2 * c + 1], scale_log2, -mu));
-            a0 = e.x;
-            a1 = e.y;
-          } else {
-            a0 = ex2(fmaf(s[2 * c], scale_log2, -mu));
-            a1 = ex2(fmaf(s[2 * c + 1], scale_log2, -mu));
-          }
+          const float a0 = ex2(fmaf(s[2 * c], scale_log2, -mu)), a1 = ex2(fmaf(s[2 * c + 1], scale_log2, -mu));
           r4[c & 3] += a0 + a1;
           pk[c] = pack_bf16x2(a0, a1);
         }
@@ -370,8 +347,7 @@ void attention_fwd(const AttnParams& p, cudaStream_t s) {
     PB_CHECK(dev >= 0 && dev < 64, "attention fwd: device index out of range");
     std::lock_guard<std::mutex> lk(mu);
     if (!attr_set[dev]) {
-      for (auto k : {attn_fwd_kernel<false, false>, attn_fwd_kernel<true, false>, attn_fwd_kernel<false, true>,
-                     attn_fwd_kernel<true, true>})
+      for (auto k : {attn_fwd_kernel<false>, attn_fwd_kernel<true>})
         PB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
       attr_set[dev] = true;
     }
@@ -384,12 +360,7 @@ void attention_fwd(const AttnParams& p, cudaStream_t s) {
   const int tpc = (G % 2 == 0) ? 2 : 1;
   const int n_qt = (p.S + BQ - 1) / BQ;
   const int grid = p.B * (p.nq / tpc) * n_qt;
-  // PB_ATTN_EXP=f32 selects one f32 exponential per element (read per call,
-  // so benchmarks can compare the two in one process)
-  const char* mode = getenv("PB_ATTN_EXP");
-  const bool f16 = !(mode && strcmp(mode, "f32") == 0);
-  auto kern = p.trace ? (f16 ? attn_fwd_kernel<true, true> : attn_fwd_kernel<true, false>)
-                      : (f16 ? attn_fwd_kernel<false, true> : attn_fwd_kernel<false, false>);
+  auto kern = p.trace ? attn_fwd_kernel<true> : attn_fwd_kernel<false>;
   kern<<<grid, kThreads, SMEM_BYTES, s>>>(tq, tk, tv, (__nv_bfloat16*)p.o, p.ldo, p.lse, p.B, p.S, p.nq, p.nkv,
                                           p.scale * kLog2e, p.causal, error_word(), p.trace);
   PB_CUDA_CHECK(cudaGetLastError());

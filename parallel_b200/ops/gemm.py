@@ -25,9 +25,15 @@ EPI_SWIGLU = 5
 EPI_ATOMIC_F32 = 6
 EPI_SPLIT_ORDERED = 7
 
-# Split-K for long-K products with few CTA-pair tiles (the weight gradients
-# reduce over all tokens): pick the slice count that minimises waves per unit
-# of K on the SM pairs, and only when it saves at least 15%.
+# Split-K for long-K products with very few CTA-pair tiles (the weight
+# gradients reduce over all tokens).  The ordered split-K costs a running-sum
+# round trip per extra slice and serialises the slices' epilogues, which the
+# wave arithmetic does not see: measured on B200 at the Qwen3-0.6B step
+# shapes (T = 8192), one slice beats the split for every weight gradient
+# (o_proj 1024x2048: 48.3 vs 49.7 us with 2 slices; gate/up 6144x1024: 89.1 vs
+# 112.4 us with 3; down 1024x3072: 47.8 vs 78.2 us with 3).  So a product is
+# split only when its tiles fill at most a quarter of the SM pairs, where one
+# slice would leave three quarters of the GPU idle.
 _SPLITK_MIN_K = 2048
 
 
@@ -43,13 +49,11 @@ def _splitk(M: int, N: int, K: int, slots: int | None = None) -> int:
         return 1
     slots = slots or _pair_slots()
     tiles = ((M + 255) // 256) * ((N + 255) // 256)
-
-    def cost(s):
-        return -(-tiles * s // slots) / s
-
+    if 4 * tiles > slots:
+        return 1
     best = 1
     for s in (2, 3, 4):
-        if K // s >= _SPLITK_MIN_K and cost(s) < cost(best) and cost(s) <= 0.85 * cost(1):
+        if K // s >= _SPLITK_MIN_K and tiles * s <= slots:
             best = s
     return best
 
