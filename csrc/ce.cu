@@ -10,6 +10,8 @@
 #include <cuda_bf16.h>
 #include <float.h>
 
+#include <algorithm>
+
 #include "host_util.h"
 #include "ops.cuh"
 #include "ptx.cuh"
@@ -55,29 +57,45 @@ __device__ __forceinline__ void block_stats(float& m, float& s) {
 }
 
 // Local row max / sum-exp with 8-wide vector loads (V % 8 == 0 and 16-byte
-// aligned rows) or a scalar fallback.
+// aligned rows) or a scalar fallback.  Each thread keeps a running max and
+// rescales its sum only when a vector raises it (rare after the first few),
+// so the pass costs one exponential per element; kUnroll vectors are loaded
+// before any is used.
+constexpr int kUnroll = 4;
+
 __device__ __forceinline__ void row_local_stats(const __nv_bfloat16* row, int V, bool vec, float& m,
                                                 float& s) {
   m = -FLT_MAX;
   s = 0.f;
   if (vec) {
-    for (int c = threadIdx.x * 8; c < V; c += kThreads * 8) {
-      uint4 raw = *reinterpret_cast<const uint4*>(row + c);
-      const uint32_t* p = &raw.x;
-      float v[8];
+    for (int c0 = threadIdx.x * 8; c0 < V; c0 += kThreads * 8 * kUnroll) {
+      uint4 raw[kUnroll];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float2 f = unpack_bf16x2(p[q]);
-        v[2 * q] = f.x;
-        v[2 * q + 1] = f.y;
+      for (int u = 0; u < kUnroll; ++u) {
+        const int c = c0 + u * kThreads * 8;
+        if (c < V) raw[u] = *reinterpret_cast<const uint4*>(row + c);
       }
-      float lm = v[0];
 #pragma unroll
-      for (int j = 1; j < 8; ++j) lm = fmaxf(lm, v[j]);
-      float ls = 0.f;
+      for (int u = 0; u < kUnroll; ++u) {
+        if (c0 + u * kThreads * 8 >= V) break;
+        const uint32_t* p = &raw[u].x;
+        float v[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) ls += __expf(v[j] - lm);
-      online_merge(m, s, lm, ls);
+        for (int q = 0; q < 4; ++q) {
+          float2 f = unpack_bf16x2(p[q]);
+          v[2 * q] = f.x;
+          v[2 * q + 1] = f.y;
+        }
+        float lm = v[0];
+#pragma unroll
+        for (int j = 1; j < 8; ++j) lm = fmaxf(lm, v[j]);
+        if (lm > m) {
+          s *= __expf(m - lm);  // m == -FLT_MAX: s is 0 and stays 0
+          m = lm;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += __expf(v[j] - m);
+      }
     }
   } else {
     for (int c = threadIdx.x; c < V; c += kThreads) online_merge(m, s, __bfloat162float(row[c]), 1.f);
@@ -85,13 +103,14 @@ __device__ __forceinline__ void row_local_stats(const __nv_bfloat16* row, int V,
   block_stats(m, s);
 }
 
-__global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld,
-                                                     const int64_t* __restrict__ labels, int T, int V,
-                                                     int64_t v0, const float* __restrict__ scale,
-                                                     float* __restrict__ row_lse, bool lse_given,
-                                                     float* __restrict__ row_target, bool write_grad) {
-  const int t = blockIdx.x;
-  if (t >= T) return;
+// stats (optional): the row's (max, sum-exp) partials over n_tiles column
+// tiles, written by the LM-head GEMM's epilogue; merging them replaces the
+// statistics pass over the logits, so the row is read once.
+__device__ __forceinline__ void ce_row(__nv_bfloat16* __restrict__ logits, int64_t ld,
+                                       const int64_t* __restrict__ labels, int t, int V, int64_t v0,
+                                       const float* __restrict__ scale, float* __restrict__ row_lse,
+                                       bool lse_given, float* __restrict__ row_target, bool write_grad,
+                                       const float* __restrict__ stats, int n_tiles) {
   __nv_bfloat16* row = logits + (int64_t)t * ld;
   const bool vec = (V % 8 == 0) && ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
   float lse;
@@ -99,7 +118,18 @@ __global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict_
     lse = row_lse[t];
   } else {
     float m, s;
-    row_local_stats(row, V, vec, m, s);
+    if (stats) {
+      m = -FLT_MAX;
+      s = 0.f;
+      const float2* part = reinterpret_cast<const float2*>(stats) + (int64_t)t * n_tiles;
+      for (int i = threadIdx.x; i < n_tiles; i += kThreads) {
+        const float2 ms = part[i];
+        online_merge(m, s, ms.x, ms.y);
+      }
+      block_stats(m, s);
+    } else {
+      row_local_stats(row, V, vec, m, s);
+    }
     lse = m + __logf(s);
     if (threadIdx.x == 0 && row_lse) row_lse[t] = lse;
   }
@@ -134,6 +164,20 @@ __global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict_
       if (inside && c == local) g -= 1.f;
       row[c] = __float2bfloat16(g * sc);
     }
+  }
+}
+
+// One CTA per row (a grid that walks rows also works: the shared statistics
+// of a row are consumed before the next row's are written).
+__global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld,
+                                                     const int64_t* __restrict__ labels, int T, int V,
+                                                     int64_t v0, const float* __restrict__ scale,
+                                                     float* __restrict__ row_lse, bool lse_given,
+                                                     float* __restrict__ row_target, bool write_grad,
+                                                     const float* __restrict__ stats, int n_tiles) {
+  for (int t = blockIdx.x; t < T; t += gridDim.x) {
+    ce_row(logits, ld, labels, t, V, v0, scale, row_lse, lse_given, row_target, write_grad, stats, n_tiles);
+    __syncthreads();
   }
 }
 
@@ -205,11 +249,12 @@ void ce_loss_reduce(const float* lse, const float* tgt, const int64_t* labels, i
 
 void ce_fwd_bwd(void* logits, int64_t ld, const int64_t* labels, int T, int V, int64_t v0,
                 const float* scale, float* row_lse, bool lse_given, float* row_target,
-                bool write_grad, cudaStream_t s) {
+                bool write_grad, cudaStream_t s, const float* stats, int n_tiles) {
   if (T == 0) return;
   PB_CHECK(!write_grad || scale != nullptr, "ce: gradient scale pointer required");
+  PB_CHECK(stats == nullptr || (n_tiles > 0 && !lse_given), "ce: row statistics need n_tiles > 0");
   ce_kernel<<<T, kThreads, 0, s>>>((__nv_bfloat16*)logits, ld, labels, T, V, v0, scale, row_lse,
-                                   lse_given, row_target, write_grad);
+                                   lse_given, row_target, write_grad, stats, n_tiles);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -243,7 +243,7 @@ void gemm_bf16(const GemmParams& p, cudaStream_t stream) {
   if (p.epi == kEpiSwiGLU) PB_CHECK(!p.a_mn && !p.b_mn, "gemm: SwiGLU epilogue needs K-major operands");
   // The CTA-pair kernel (256-row tiles) wins on every training shape measured
   // with M >= 256; smaller M keeps the one-CTA kernel.
-  if (p.kernel == 2 || p.gather || p.scatter || p.splits > 1 || p.epi == kEpiSplitOrdered ||
+  if (p.kernel == 2 || p.gather || p.scatter || p.splits > 1 || p.epi == kEpiSplitOrdered || p.row_stats ||
       (p.kernel == 0 && p.M >= 256))
     return gemm_bf16_pair(p, stream);
   if (p.epi == kEpiSwiGLU) {

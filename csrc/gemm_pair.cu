@@ -484,6 +484,14 @@ void launch_pair(const GemmParams& p, cudaStream_t stream) {
                                  64);
     ep.tma = 1;
   }
+  if (p.row_stats) {
+    const bool plain = !SWIGLU && !GATHER && BN == kRowStatsCols;
+    PB_CHECK(plain && p.epi == kEpiStoreBf16 && ep.tma == 1 && p.stats_ld >= (p.N + BN - 1) / BN,
+             "gemm: row statistics need the bf16 TMA-store epilogue of the CTA-pair kernel and one entry per "
+             "256-column tile");
+    ep.stats = p.row_stats;
+    ep.stats_ld = p.stats_ld;
+  }
   GatherArgs ga{};
   if (GATHER) ga = *p.gather;
   const int bn_out = SWIGLU ? BN / 2 : BN;
