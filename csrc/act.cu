@@ -23,6 +23,7 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dh, int64_t 
                                   const __nv_bfloat16* __restrict__ gu, int64_t ldgu,
                                   __nv_bfloat16* __restrict__ dgu, int64_t lddgu, int T, int I,
                                   const int* __restrict__ tiles128) {
+  pdl_prologue();
   // tiles128 (optional, device): only the first 128 * *tiles128 rows are live
   if (tiles128 != nullptr) T = min(T, *tiles128 * 128);
   const int vec_per_row = I / 8;
@@ -65,6 +66,7 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids,
                                      const __nv_bfloat16* __restrict__ table, int64_t ldt,
                                      __nv_bfloat16* __restrict__ out, int64_t ldo, int T, int H,
                                      int64_t v0, int64_t vrows) {
+  pdl_prologue();
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -86,6 +88,7 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ sid, const int6
                                      const __nv_bfloat16* __restrict__ dy, int64_t lddy,
                                      __nv_bfloat16* __restrict__ grad, int64_t ldg, int T, int H, int64_t v0,
                                      int64_t vrows, bool accumulate) {
+  pdl_prologue();
   const int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (p >= T) return;
@@ -129,6 +132,7 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ sid, const int6
 // x *= *s in place (bf16), skipped entirely when *s == 1: the incoming
 // gradient of a loss is almost always exactly one, and the check costs no host sync.
 __global__ void scale_by_scalar_kernel(__nv_bfloat16* __restrict__ x, int64_t n, const float* __restrict__ s) {
+  pdl_prologue();
   const float a = *s;
   if (a == 1.f) return;
   for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 8; i < n;
@@ -150,6 +154,7 @@ __global__ void scale_by_scalar_kernel(__nv_bfloat16* __restrict__ x, int64_t n,
 
 __global__ void cast_f32_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst,
                                      int64_t n) {
+  pdl_prologue();
   for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 4; i < n;
        i += (int64_t)gridDim.x * blockDim.x * 4) {
     if (i + 4 <= n) {
@@ -176,7 +181,7 @@ int grid_for(int64_t work, int threads) {
 void swiglu_bwd(const void* dh, int64_t lddh, const void* gu, int64_t ldgu, void* dgu,
                 int64_t lddgu, int T, int I, cudaStream_t s, const int* tiles128) {
   PB_CHECK(I % 8 == 0, "swiglu: I must be a multiple of 8");
-  swiglu_bwd_kernel<<<grid_for((int64_t)T * I / 8, 256), 256, 0, s>>>(
+  launch_k(swiglu_bwd_kernel, grid_for((int64_t)T * I / 8, 256), 256, 0, s,
       (const __nv_bfloat16*)dh, lddh, (const __nv_bfloat16*)gu, ldgu, (__nv_bfloat16*)dgu, lddgu, T, I, tiles128);
   PB_CUDA_CHECK(cudaGetLastError());
 }
@@ -184,7 +189,7 @@ void swiglu_bwd(const void* dh, int64_t lddh, const void* gu, int64_t ldgu, void
 void embedding_fwd(const int64_t* ids, const void* table, int64_t ldt, void* out, int64_t ldo,
                    int T, int H, int64_t vocab_start, int64_t vocab_rows, cudaStream_t s) {
   PB_CHECK(H % 8 == 0, "embedding: H must be a multiple of 8");
-  embedding_fwd_kernel<<<(T + 7) / 8, 256, 0, s>>>(ids, (const __nv_bfloat16*)table, ldt,
+  launch_k(embedding_fwd_kernel, (T + 7) / 8, 256, 0, s, ids, (const __nv_bfloat16*)table, ldt,
                                                    (__nv_bfloat16*)out, ldo, T, H, vocab_start,
                                                    vocab_rows);
   PB_CUDA_CHECK(cudaGetLastError());
@@ -195,7 +200,7 @@ void embedding_bwd(const int64_t* sorted_ids, const int64_t* perm, const void* d
                    cudaStream_t s) {
   PB_CHECK(H % 8 == 0 && lddy % 8 == 0 && ldg % 8 == 0, "embedding: H and strides must be multiples of 8");
   if (T == 0) return;
-  embedding_bwd_kernel<<<(T + 7) / 8, 256, 0, s>>>(sorted_ids, perm, (const __nv_bfloat16*)dy, lddy,
+  launch_k(embedding_bwd_kernel, (T + 7) / 8, 256, 0, s, sorted_ids, perm, (const __nv_bfloat16*)dy, lddy,
                                                    (__nv_bfloat16*)grad, ldg, T, H, vocab_start, vocab_rows,
                                                    accumulate);
   PB_CUDA_CHECK(cudaGetLastError());
@@ -203,7 +208,7 @@ void embedding_bwd(const int64_t* sorted_ids, const int64_t* perm, const void* d
 
 void scale_by_scalar(void* x, int64_t n, const float* s_dev, cudaStream_t s) {
   if (n == 0) return;
-  scale_by_scalar_kernel<<<grid_for(n / 8 + 1, 256), 256, 0, s>>>((__nv_bfloat16*)x, n, s_dev);
+  launch_k(scale_by_scalar_kernel, grid_for(n / 8 + 1, 256), 256, 0, s, (__nv_bfloat16*)x, n, s_dev);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -246,6 +251,7 @@ constexpr int kFewSlices = 8;
 
 __global__ void sum_slices_few_vec_kernel(const float* __restrict__ parts, int slices, int64_t len4, int64_t stride,
                                           void* __restrict__ out, bool out_bf16, bool accumulate) {
+  pdl_prologue();
   for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < len4; v += (int64_t)gridDim.x * blockDim.x) {
     float4 x[kFewSlices];
 #pragma unroll
@@ -263,6 +269,7 @@ __global__ void sum_slices_few_vec_kernel(const float* __restrict__ parts, int s
 
 __global__ void sum_slices_few_kernel(const float* __restrict__ parts, int slices, int64_t len, int64_t stride,
                                       void* __restrict__ out, bool out_bf16, bool accumulate) {
+  pdl_prologue();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < len; i += (int64_t)gridDim.x * blockDim.x) {
     float a = 0.f;
     for (int k = 0; k < slices; ++k) a += parts[(int64_t)k * stride + i];
@@ -273,6 +280,7 @@ __global__ void sum_slices_few_kernel(const float* __restrict__ parts, int slice
 __global__ void __launch_bounds__(1024) sum_slices_many_kernel(const float* __restrict__ parts, int slices,
                                                                int64_t len, int64_t stride, void* __restrict__ out,
                                                                bool out_bf16, bool accumulate) {
+  pdl_prologue();
   __shared__ float part[32][33];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t c = (int64_t)blockIdx.x * 32 + lane;
@@ -307,20 +315,20 @@ void sum_slices(const float* parts, int slices, int64_t len, int64_t stride, voi
     const bool vec = len % 4 == 0 && stride % 4 == 0 && (reinterpret_cast<uintptr_t>(parts) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(out) & (out_bf16 ? 7 : 15)) == 0;
     if (vec)
-      sum_slices_few_vec_kernel<<<grid_for(len / 4, 256), 256, 0, s>>>(parts, slices, len / 4, stride, out, out_bf16,
+      launch_k(sum_slices_few_vec_kernel, grid_for(len / 4, 256), 256, 0, s, parts, slices, len / 4, stride, out, out_bf16,
                                                                        accumulate);
     else
-      sum_slices_few_kernel<<<grid_for(len, 256), 256, 0, s>>>(parts, slices, len, stride, out, out_bf16,
+      launch_k(sum_slices_few_kernel, grid_for(len, 256), 256, 0, s, parts, slices, len, stride, out, out_bf16,
                                                                accumulate);
   } else {
-    sum_slices_many_kernel<<<(unsigned)((len + 31) / 32), 1024, 0, s>>>(parts, slices, len, stride, out, out_bf16,
+    launch_k(sum_slices_many_kernel, (unsigned)((len + 31) / 32), 1024, 0, s, parts, slices, len, stride, out, out_bf16,
                                                                         accumulate);
   }
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
 void cast_f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t s) {
-  cast_f32_bf16_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, s>>>(src, (__nv_bfloat16*)dst, n);
+  launch_k(cast_f32_bf16_kernel, grid_for(n / 4 + 1, 256), 256, 0, s, src, (__nv_bfloat16*)dst, n);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -75,6 +75,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float* __restrict__ DELTA, __nv_bfloat16* __restrict__ dK, int64_t lddk,
                     __nv_bfloat16* __restrict__ dV, int64_t lddv, int B, int S, int nq, int nkv, float scale,
                     bool causal, int* err, long long* trace, __nv_bfloat16* __restrict__ ds_buf) {
+  pdl_prologue();
   // optional per-CTA phase timing (clock64 cycles, kTrace builds only); slots
   // are documented at the use sites
   constexpr int kSlots = kTrace ? kAttnBwdTraceSlots : 1;
@@ -489,6 +490,7 @@ __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ O, int64_
                                      const __nv_bfloat16* __restrict__ dO, int64_t lddo,
                                      const float* __restrict__ lse, float* __restrict__ scratch,
                                      float* __restrict__ dq_acc, int64_t ld_acc, int B, int S, int nq, float scale) {
+  pdl_prologue();
   constexpr int kTok = 16;  // tokens per warp
   const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t rows = (int64_t)B * nq * S;
@@ -565,6 +567,7 @@ __global__ void __launch_bounds__(192, 1)
     attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmK, const __nv_bfloat16* __restrict__ ds_buf,
                        __nv_bfloat16* __restrict__ dq, int64_t lddq, int B, int S, int nq, int nkv, bool causal,
                        int* err) {
+  pdl_prologue();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -704,6 +707,7 @@ __global__ void __launch_bounds__(192, 1)
 
 __global__ void cast_rows_kernel(const float* __restrict__ src, int64_t lds, __nv_bfloat16* __restrict__ dst,
                                  int64_t ldd, int rows, int cols) {
+  pdl_prologue();
   const int64_t total = (int64_t)rows * cols / 4;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
@@ -745,7 +749,7 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   const int64_t rows = (int64_t)p.B * p.nq * p.S;
   const int64_t ld_acc = (int64_t)p.nq * HD;
   const int64_t prep_threads = std::max<int64_t>((int64_t)p.B * p.nq * ((p.S + 15) / 16) * 32, 128);
-  attn_bwd_prep_kernel<<<(unsigned)((prep_threads + 255) / 256), 256, 0, s>>>(
+  launch_k(attn_bwd_prep_kernel, (unsigned)((prep_threads + 255) / 256), 256, 0, s,
       (const __nv_bfloat16*)p.o, p.ldo, (const __nv_bfloat16*)p.dout, p.lddo, p.lse, p.delta,
       ds_path ? nullptr : p.dq_acc, ld_acc, p.B, p.S, p.nq, p.scale);
   PB_CUDA_CHECK(cudaGetLastError());
@@ -760,12 +764,12 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   const int grid = p.B * p.nkv * n_t;
   auto kern = ds_path ? (p.trace ? attn_bwd_kernel<true, true> : attn_bwd_kernel<false, true>)
                       : (p.trace ? attn_bwd_kernel<true, false> : attn_bwd_kernel<false, false>);
-  kern<<<grid, kThreads, SMEM_BYTES, s>>>(tq, tk, tv, tdo, tdq, p.delta + rows + 128, p.delta, (__nv_bfloat16*)p.dk,
+  launch_k(kern, grid, kThreads, SMEM_BYTES, s, tq, tk, tv, tdo, tdq, p.delta + rows + 128, p.delta, (__nv_bfloat16*)p.dk,
                                           p.lddk, (__nv_bfloat16*)p.dv, p.lddv, p.B, p.S, p.nq, p.nkv, p.scale,
                                           p.causal, error_word(), p.trace, (__nv_bfloat16*)p.ds_buf);
   PB_CUDA_CHECK(cudaGetLastError());
   if (ds_path) {
-    attn_bwd_dq_kernel<<<std::min(num_sms(), p.B * p.nq * n_t), 192, DQ_SMEM, s>>>(tk, (const __nv_bfloat16*)p.ds_buf,
+    launch_k(attn_bwd_dq_kernel, std::min(num_sms(), p.B * p.nq * n_t), 192, DQ_SMEM, s, tk, (const __nv_bfloat16*)p.ds_buf,
                                                               (__nv_bfloat16*)p.dq, p.lddq, p.B, p.S, p.nq, p.nkv,
                                                               p.causal, error_word());
     PB_CUDA_CHECK(cudaGetLastError());
@@ -773,7 +777,7 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   }
   const int64_t cast_work = T * ld_acc / 4;
   int cgrid = (int)std::min<int64_t>((cast_work + 255) / 256, (int64_t)num_sms() * 16);
-  cast_rows_kernel<<<cgrid, 256, 0, s>>>(p.dq_acc, ld_acc, (__nv_bfloat16*)p.dq, p.lddq, (int)T, (int)ld_acc);
+  launch_k(cast_rows_kernel, cgrid, 256, 0, s, p.dq_acc, ld_acc, (__nv_bfloat16*)p.dq, p.lddq, (int)T, (int)ld_acc);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -911,7 +915,7 @@ extern "C" __attribute__((visibility("default"))) int pb_attention_bwd_noalloc(
     // the prep kernel zeroes the dq accumulator and the scratch padding
     PB_CUDA_CHECK(cudaMemsetAsync(err, 0, 256, stream));
     const int64_t prep_threads = std::max<int64_t>((int64_t)B * nq * ((S + 15) / 16) * 32, 128);
-    attn_bwd_prep_kernel<<<(unsigned)((prep_threads + 255) / 256), 256, 0, stream>>>(
+    launch_k(attn_bwd_prep_kernel, (unsigned)((prep_threads + 255) / 256), 256, 0, stream,
         (const __nv_bfloat16*)o, ldo, (const __nv_bfloat16*)dout, lddo, lse, delta, dq_acc, ld_acc, B, S, nq, scale);
     PB_CUDA_CHECK(cudaGetLastError());
     const uint64_t uS = S, uB = B;
@@ -921,7 +925,7 @@ extern "C" __attribute__((visibility("default"))) int pb_attention_bwd_noalloc(
     CUtensorMap tdo = make_tmap_3d_bf16(dout, (uint64_t)nq * HD, uS, uB, lddo, uS * lddo, 64, 128, 1);
     CUtensorMap tdq = make_tmap_3d_f32(dq_acc, (uint64_t)ld_acc, uS, uB, ld_acc, uS * ld_acc, 32, 32, 1, true);
     const int n_t = (S + BT - 1) / BT;
-    attn_bwd_kernel<false, false><<<B * nkv * n_t, kThreads, SMEM_BYTES, stream>>>(
+    launch_k(attn_bwd_kernel<false, false>, B * nkv * n_t, kThreads, SMEM_BYTES, stream,
         tq, tk, tv, tdo, tdq, delta + rows + 128, delta, (__nv_bfloat16*)dk, lddk, (__nv_bfloat16*)dv, lddv, B, S,
         nq, nkv, scale, causal != 0, err, nullptr, nullptr);
     PB_CUDA_CHECK(cudaGetLastError());
@@ -929,7 +933,7 @@ extern "C" __attribute__((visibility("default"))) int pb_attention_bwd_noalloc(
     PB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int64_t cast_work = T * ld_acc / 4;
     const int cgrid = (int)std::min<int64_t>((cast_work + 255) / 256, (int64_t)sms * 16);
-    cast_rows_kernel<<<cgrid, 256, 0, stream>>>(dq_acc, ld_acc, (__nv_bfloat16*)dq, lddq, (int)T, (int)ld_acc);
+    launch_k(cast_rows_kernel, cgrid, 256, 0, stream, dq_acc, ld_acc, (__nv_bfloat16*)dq, lddq, (int)T, (int)ld_acc);
     PB_CUDA_CHECK(cudaGetLastError());
   } catch (const std::exception& ex) {
     noalloc_set_msg(ex.what());

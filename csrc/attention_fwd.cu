@@ -59,6 +59,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int64_t ldo,
                     float* __restrict__ LSE, int B, int S, int nq, int nkv, float scale_log2, bool causal,
                     int* err, long long* trace) {
+  pdl_prologue();
   // optional per-CTA phase timing (clock64 cycles, kTrace builds only)
   constexpr int kSlots = kTrace ? 16 : 1;
   long long tacc[kSlots];
@@ -361,7 +362,7 @@ void attention_fwd(const AttnParams& p, cudaStream_t s) {
   const int n_qt = (p.S + BQ - 1) / BQ;
   const int grid = p.B * (p.nq / tpc) * n_qt;
   auto kern = p.trace ? attn_fwd_kernel<true> : attn_fwd_kernel<false>;
-  kern<<<grid, kThreads, SMEM_BYTES, s>>>(tq, tk, tv, (__nv_bfloat16*)p.o, p.ldo, p.lse, p.B, p.S, p.nq, p.nkv,
+  launch_k(kern, grid, kThreads, SMEM_BYTES, s, tq, tk, tv, (__nv_bfloat16*)p.o, p.ldo, p.lse, p.B, p.S, p.nq, p.nkv,
                                           p.scale * kLog2e, p.causal, error_word(), p.trace);
   PB_CUDA_CHECK(cudaGetLastError());
 }

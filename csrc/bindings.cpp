@@ -23,8 +23,7 @@ cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 //   out: [M, N] bf16 or fp32 depending on epi
 void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, bool b_mn, int64_t epi,
           double alpha, const c10::optional<at::Tensor>& r, int64_t b_up_offset, int64_t n_out, int64_t kernel,
-          int64_t splits, const c10::optional<at::Tensor>& ws, bool accumulate,
-          const c10::optional<at::Tensor>& row_stats) {
+          int64_t splits, const c10::optional<at::Tensor>& ws, bool accumulate) {
   CHECK_CUDA_BF16(a);
   CHECK_CUDA_BF16(b);
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm: 2-D operands expected");
@@ -81,16 +80,6 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, 
     TORCH_CHECK(epi != pb::kEpiResidualBf16, "gemm: residual epilogue needs r");
     p.R = nullptr;
     p.ldr = 0;
-  }
-  if (row_stats.has_value() && row_stats->defined()) {
-    // fp32 [M, 2 * n_tiles]: (max, sum-exp) of each row's bf16 outputs per 256-column tile
-    TORCH_CHECK(epi == pb::kEpiStoreBf16 && row_stats->is_cuda() && row_stats->scalar_type() == at::kFloat &&
-                    row_stats->dim() == 2 && row_stats->is_contiguous() && row_stats->size(0) == p.M &&
-                    row_stats->size(1) >= 2 * ((p.N + pb::kRowStatsCols - 1) / pb::kRowStatsCols),
-                "gemm: row_stats must be contiguous fp32 [M, 2 * ceil(N / 256)] with the bf16 store epilogue");
-    TORCH_CHECK(p.M >= 256, "gemm: row statistics need M >= 256 (CTA-pair kernel)");
-    p.row_stats = row_stats->data_ptr<float>();
-    p.stats_ld = row_stats->size(1) / 2;
   }
   pb::gemm_bf16(p, cur_stream());
 }
@@ -289,8 +278,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("b"), pybind11::arg("out"), pybind11::arg("a_mn"), pybind11::arg("b_mn"),
         pybind11::arg("epi"), pybind11::arg("alpha"), pybind11::arg("r") = pybind11::none(),
         pybind11::arg("b_up_offset") = 0, pybind11::arg("n_out") = 0, pybind11::arg("kernel") = 0,
-        pybind11::arg("splits") = 1, pybind11::arg("ws") = pybind11::none(), pybind11::arg("accumulate") = false,
-        pybind11::arg("row_stats") = pybind11::none());
+        pybind11::arg("splits") = 1, pybind11::arg("ws") = pybind11::none(), pybind11::arg("accumulate") = false);
   m.def("gemm_ag", &gemm_ag, "GEMM with the sequence-parallel all-gather of A in the same kernel",
         pybind11::arg("dst"), pybind11::arg("src_ptrs"), pybind11::arg("src_ld"), pybind11::arg("flags"),
         pybind11::arg("target"), pybind11::arg("seq"), pybind11::arg("seq_local"), pybind11::arg("batch"),

@@ -19,7 +19,7 @@
 namespace pb {
 namespace {
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 1024;
 
 __device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2) {
   const float mn = fmaxf(m, m2);
@@ -103,14 +103,13 @@ __device__ __forceinline__ void row_local_stats(const __nv_bfloat16* row, int V,
   block_stats(m, s);
 }
 
-// stats (optional): the row's (max, sum-exp) partials over n_tiles column
-// tiles, written by the LM-head GEMM's epilogue; merging them replaces the
-// statistics pass over the logits, so the row is read once.
+// The gradient pass re-reads the row the statistics pass just read; with
+// 1024-thread CTAs two rows per SM are in flight (about 90 MB at V = 151936),
+// so the re-read mostly hits L2 and the logits cross DRAM once each way.
 __device__ __forceinline__ void ce_row(__nv_bfloat16* __restrict__ logits, int64_t ld,
                                        const int64_t* __restrict__ labels, int t, int V, int64_t v0,
                                        const float* __restrict__ scale, float* __restrict__ row_lse,
-                                       bool lse_given, float* __restrict__ row_target, bool write_grad,
-                                       const float* __restrict__ stats, int n_tiles) {
+                                       bool lse_given, float* __restrict__ row_target, bool write_grad) {
   __nv_bfloat16* row = logits + (int64_t)t * ld;
   const bool vec = (V % 8 == 0) && ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
   float lse;
@@ -118,18 +117,7 @@ __device__ __forceinline__ void ce_row(__nv_bfloat16* __restrict__ logits, int64
     lse = row_lse[t];
   } else {
     float m, s;
-    if (stats) {
-      m = -FLT_MAX;
-      s = 0.f;
-      const float2* part = reinterpret_cast<const float2*>(stats) + (int64_t)t * n_tiles;
-      for (int i = threadIdx.x; i < n_tiles; i += kThreads) {
-        const float2 ms = part[i];
-        online_merge(m, s, ms.x, ms.y);
-      }
-      block_stats(m, s);
-    } else {
-      row_local_stats(row, V, vec, m, s);
-    }
+    row_local_stats(row, V, vec, m, s);
     lse = m + __logf(s);
     if (threadIdx.x == 0 && row_lse) row_lse[t] = lse;
   }
@@ -145,18 +133,28 @@ __device__ __forceinline__ void ce_row(__nv_bfloat16* __restrict__ logits, int64
   __syncthreads();  // the target logit is read before it is overwritten
   const float sc = valid ? scale[0] : 0.f;
   if (vec) {
-    for (int c = threadIdx.x * 8; c < V; c += kThreads * 8) {
-      uint4 raw = *reinterpret_cast<const uint4*>(row + c);
-      uint32_t* p = &raw.x;
+    for (int c0 = threadIdx.x * 8; c0 < V; c0 += kThreads * 8 * kUnroll) {
+      uint4 raw[kUnroll];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float2 f = unpack_bf16x2(p[q]);
-        float g0 = __expf(f.x - lse), g1 = __expf(f.y - lse);
-        if (inside && c + 2 * q == local) g0 -= 1.f;
-        if (inside && c + 2 * q + 1 == local) g1 -= 1.f;
-        p[q] = pack_bf16x2(g0 * sc, g1 * sc);
+      for (int u = 0; u < kUnroll; ++u) {
+        const int c = c0 + u * kThreads * 8;
+        if (c < V) raw[u] = *reinterpret_cast<const uint4*>(row + c);
       }
-      *reinterpret_cast<uint4*>(row + c) = raw;
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int c = c0 + u * kThreads * 8;
+        if (c >= V) break;
+        uint32_t* p = &raw[u].x;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float2 f = unpack_bf16x2(p[q]);
+          float g0 = __expf(f.x - lse), g1 = __expf(f.y - lse);
+          if (inside && c + 2 * q == local) g0 -= 1.f;
+          if (inside && c + 2 * q + 1 == local) g1 -= 1.f;
+          p[q] = pack_bf16x2(g0 * sc, g1 * sc);
+        }
+        *reinterpret_cast<uint4*>(row + c) = raw[u];
+      }
     }
   } else {
     for (int c = threadIdx.x; c < V; c += kThreads) {
@@ -173,10 +171,10 @@ __global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict_
                                                      const int64_t* __restrict__ labels, int T, int V,
                                                      int64_t v0, const float* __restrict__ scale,
                                                      float* __restrict__ row_lse, bool lse_given,
-                                                     float* __restrict__ row_target, bool write_grad,
-                                                     const float* __restrict__ stats, int n_tiles) {
+                                                     float* __restrict__ row_target, bool write_grad) {
+  pdl_prologue();
   for (int t = blockIdx.x; t < T; t += gridDim.x) {
-    ce_row(logits, ld, labels, t, V, v0, scale, row_lse, lse_given, row_target, write_grad, stats, n_tiles);
+    ce_row(logits, ld, labels, t, V, v0, scale, row_lse, lse_given, row_target, write_grad);
     __syncthreads();
   }
 }
@@ -185,6 +183,7 @@ __global__ void __launch_bounds__(kThreads) ce_stats_kernel(const __nv_bfloat16*
                                                            int64_t ld, int T, int V,
                                                            float* __restrict__ row_max,
                                                            float* __restrict__ row_sumexp) {
+  pdl_prologue();
   const int t = blockIdx.x;
   if (t >= T) return;
   const __nv_bfloat16* row = logits + (int64_t)t * ld;
@@ -216,6 +215,7 @@ __device__ __forceinline__ float block_sum_fixed(float v) {
 
 __global__ void __launch_bounds__(kRedThreads) ce_valid_inv_kernel(const int64_t* __restrict__ labels, int T,
                                                                    float* __restrict__ inv) {
+  pdl_prologue();
   float n = 0.f;
   for (int t = threadIdx.x; t < T; t += kRedThreads) n += labels[t] >= 0 ? 1.f : 0.f;
   n = block_sum_fixed(n);
@@ -227,6 +227,7 @@ __global__ void __launch_bounds__(kRedThreads) ce_loss_reduce_kernel(const float
                                                                      const int64_t* __restrict__ labels, int T,
                                                                      const float* __restrict__ inv,
                                                                      float* __restrict__ out, bool accumulate) {
+  pdl_prologue();
   float a = 0.f;
   for (int t = threadIdx.x; t < T; t += kRedThreads)
     if (labels[t] >= 0) a += lse[t] - tgt[t];
@@ -237,31 +238,30 @@ __global__ void __launch_bounds__(kRedThreads) ce_loss_reduce_kernel(const float
 }  // namespace
 
 void ce_valid_inv(const int64_t* labels, int T, float* inv, cudaStream_t s) {
-  ce_valid_inv_kernel<<<1, kRedThreads, 0, s>>>(labels, T, inv);
+  launch_k(ce_valid_inv_kernel, 1, kRedThreads, 0, s, labels, T, inv);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
 void ce_loss_reduce(const float* lse, const float* tgt, const int64_t* labels, int T, const float* inv, float* out,
                     bool accumulate, cudaStream_t s) {
-  ce_loss_reduce_kernel<<<1, kRedThreads, 0, s>>>(lse, tgt, labels, T, inv, out, accumulate);
+  launch_k(ce_loss_reduce_kernel, 1, kRedThreads, 0, s, lse, tgt, labels, T, inv, out, accumulate);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
 void ce_fwd_bwd(void* logits, int64_t ld, const int64_t* labels, int T, int V, int64_t v0,
                 const float* scale, float* row_lse, bool lse_given, float* row_target,
-                bool write_grad, cudaStream_t s, const float* stats, int n_tiles) {
+                bool write_grad, cudaStream_t s) {
   if (T == 0) return;
   PB_CHECK(!write_grad || scale != nullptr, "ce: gradient scale pointer required");
-  PB_CHECK(stats == nullptr || (n_tiles > 0 && !lse_given), "ce: row statistics need n_tiles > 0");
-  ce_kernel<<<T, kThreads, 0, s>>>((__nv_bfloat16*)logits, ld, labels, T, V, v0, scale, row_lse,
-                                   lse_given, row_target, write_grad, stats, n_tiles);
+  launch_k(ce_kernel, T, kThreads, 0, s, (__nv_bfloat16*)logits, ld, labels, T, V, v0, scale, row_lse,
+           lse_given, row_target, write_grad);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
 void ce_row_stats(const void* logits, int64_t ld, int T, int V, float* row_max, float* row_sumexp,
                   cudaStream_t s) {
   if (T == 0) return;
-  ce_stats_kernel<<<T, kThreads, 0, s>>>((const __nv_bfloat16*)logits, ld, T, V, row_max, row_sumexp);
+  launch_k(ce_stats_kernel, T, kThreads, 0, s, (const __nv_bfloat16*)logits, ld, T, V, row_max, row_sumexp);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

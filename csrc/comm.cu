@@ -45,6 +45,7 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 
 __global__ void signal_barrier_kernel(const uint64_t* __restrict__ peer_pads, int rank, int world, int slot_base,
                                       uint32_t* __restrict__ epoch_ctr, uint64_t limit_ns, int* err) {
+  pdl_prologue();
   const int i = threadIdx.x;
   // the epoch lives on the device (one counter per buffer and channel, bumped
   // here), so a captured CUDA graph replays a fresh epoch every time
@@ -92,6 +93,7 @@ constexpr int kCopyUnroll = 4;
 // and kCopyUnroll independent 16-byte loads in flight per thread (remote
 // NVLink loads need many outstanding requests).
 __global__ void __launch_bounds__(512) multi_copy_kernel(CopySegments segs) {
+  pdl_prologue();
   const int64_t total = segs.vec_start[segs.n];
   {
     const int64_t c = blockIdx.x;
@@ -122,6 +124,7 @@ __global__ void __launch_bounds__(512) multi_copy_kernel(CopySegments segs) {
 // per chunk as multi_copy (one segment search per chunk, monotone advance).
 __global__ void __launch_bounds__(512) reduce_segments_kernel(ReduceSegments segs, int world, float scale,
                                                               bool accumulate) {
+  pdl_prologue();
   const int64_t total = segs.vec_start[segs.n];
   {
     const int64_t c = blockIdx.x;
@@ -172,6 +175,7 @@ __global__ void __launch_bounds__(512) reduce_segments_kernel(ReduceSegments seg
 }
 
 __global__ void wait_flag_kernel(const uint32_t* flag, uint32_t target, uint64_t limit_ns, int* status) {
+  pdl_prologue();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   const uint64_t t0 = globaltimer();
   uint32_t n = 0;
@@ -188,6 +192,7 @@ __global__ void wait_flag_kernel(const uint32_t* flag, uint32_t target, uint64_t
 __global__ void row_scatter_kernel(const uint8_t* __restrict__ src, int64_t ld_src, const int64_t* __restrict__ src_row,
                                    const int32_t* __restrict__ dst_rank, const int64_t* __restrict__ dst_row,
                                    PeerBases peers, int64_t ld_dst, int64_t vecs, int64_t n) {
+  pdl_prologue();
   const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
@@ -202,6 +207,7 @@ __global__ void row_scatter_kernel(const uint8_t* __restrict__ src, int64_t ld_s
 __global__ void row_gather_sum_kernel(__nv_bfloat16* __restrict__ dst, int64_t ld_dst, int64_t n_tokens, int k_per,
                                       const int32_t* __restrict__ rank, const int64_t* __restrict__ row,
                                       PeerBases peers, int64_t ld_src, int64_t vecs) {
+  pdl_prologue();
   const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= n_tokens) return;
@@ -233,6 +239,7 @@ __global__ void row_gather_sum_kernel(__nv_bfloat16* __restrict__ dst, int64_t l
 __global__ void row_gather_kernel(uint8_t* __restrict__ dst, int64_t ld_dst, const int32_t* __restrict__ rank,
                                   const int64_t* __restrict__ row, PeerBases peers, int64_t ld_src, int64_t vecs,
                                   int64_t n) {
+  pdl_prologue();
   const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
@@ -258,6 +265,7 @@ __global__ void row_gather_kernel(uint8_t* __restrict__ dst, int64_t ld_dst, con
 __global__ void small_ar_kernel(const float* __restrict__ in, float* __restrict__ out, int64_t units, int op,
                                 PeerBases bases, int rank, int world, int64_t cap, uint32_t* __restrict__ epochs,
                                 uint64_t limit_ns, int* err) {
+  pdl_prologue();
   const int b = blockIdx.x;
   const int uf = op == kArLse3 ? 3 : 1;  // floats per unit
   const int64_t per = (units + gridDim.x - 1) / gridDim.x;
@@ -329,7 +337,7 @@ __global__ void small_ar_kernel(const float* __restrict__ in, float* __restrict_
 void signal_barrier(const uint64_t* peer_pads_dev, int rank, int world, int slot_base, uint32_t* epoch_ctr,
                     uint64_t limit_ns, cudaStream_t s) {
   PB_CHECK(world >= 1 && world <= kMaxPeers, "signal_barrier: world size");
-  signal_barrier_kernel<<<1, 32, 0, s>>>(peer_pads_dev, rank, world, slot_base, epoch_ctr, limit_ns, error_word());
+  launch_k(signal_barrier_kernel, 1, 32, 0, s, peer_pads_dev, rank, world, slot_base, epoch_ctr, limit_ns, error_word());
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -341,18 +349,18 @@ unsigned chunk_grid(int64_t vecs) {
 
 void multi_copy(const CopySegments& segs, cudaStream_t s) {
   if (segs.n == 0) return;
-  multi_copy_kernel<<<chunk_grid(segs.vec_start[segs.n]), 512, 0, s>>>(segs);
+  launch_k(multi_copy_kernel, chunk_grid(segs.vec_start[segs.n]), 512, 0, s, segs);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
 void reduce_segments(const ReduceSegments& segs, int world, float scale, bool accumulate, cudaStream_t s) {
   if (segs.n == 0) return;
-  reduce_segments_kernel<<<chunk_grid(segs.vec_start[segs.n]), 512, 0, s>>>(segs, world, scale, accumulate);
+  launch_k(reduce_segments_kernel, chunk_grid(segs.vec_start[segs.n]), 512, 0, s, segs, world, scale, accumulate);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
 void wait_flag(const uint32_t* flag, uint32_t target, uint64_t limit_ns, int* status, cudaStream_t s) {
-  wait_flag_kernel<<<1, 32, 0, s>>>(flag, target, limit_ns, status);
+  launch_k(wait_flag_kernel, 1, 32, 0, s, flag, target, limit_ns, status);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -362,7 +370,7 @@ void row_scatter(const void* src, int64_t ld_src_bytes, const int64_t* src_row, 
   PB_CHECK(row_bytes % 16 == 0 && ld_src_bytes % 16 == 0 && ld_dst_bytes % 16 == 0, "row_scatter: 16-byte rows");
   if (n == 0) return;
   const int64_t threads = n * 32;
-  row_scatter_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+  launch_k(row_scatter_kernel, (unsigned)((threads + 255) / 256), 256, 0, s,
       reinterpret_cast<const uint8_t*>(src), ld_src_bytes, src_row, dst_rank, dst_row, peers, ld_dst_bytes,
       row_bytes / 16, n);
   PB_CUDA_CHECK(cudaGetLastError());
@@ -373,7 +381,7 @@ void row_gather_sum(void* dst, int64_t ld_dst, int64_t n_tokens, int k_per, cons
   PB_CHECK(cols % 8 == 0 && ld_dst % 8 == 0 && ld_src % 8 == 0, "row_gather_sum: 16-byte rows");
   if (n_tokens == 0) return;
   const int64_t threads = n_tokens * 32;
-  row_gather_sum_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+  launch_k(row_gather_sum_kernel, (unsigned)((threads + 255) / 256), 256, 0, s,
       reinterpret_cast<__nv_bfloat16*>(dst), ld_dst, n_tokens, k_per, rank, row, peers, ld_src, cols / 8);
   PB_CUDA_CHECK(cudaGetLastError());
 }
@@ -383,7 +391,7 @@ void row_gather(void* dst, int64_t ld_dst_bytes, const int32_t* rank, const int6
   PB_CHECK(row_bytes % 16 == 0 && ld_src_bytes % 16 == 0 && ld_dst_bytes % 16 == 0, "row_gather: 16-byte rows");
   if (n == 0) return;
   const int64_t threads = n * 32;
-  row_gather_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(reinterpret_cast<uint8_t*>(dst), ld_dst_bytes, rank,
+  launch_k(row_gather_kernel, (unsigned)((threads + 255) / 256), 256, 0, s, reinterpret_cast<uint8_t*>(dst), ld_dst_bytes, rank,
                                                                       row, peers, ld_src_bytes, row_bytes / 16, n);
   PB_CUDA_CHECK(cudaGetLastError());
 }
@@ -404,7 +412,7 @@ void small_all_reduce(const float* in, float* out, int64_t units, int op, const 
   if (units == 0) return;
   // a fixed grid: every block takes part in every call, so all block epochs
   // (and the parity of the data slots) stay equal from call to call
-  small_ar_kernel<<<kSmallArBlocks, 256, 0, s>>>(in, out, units, op, bases, rank, world, cap_units, block_epochs, limit_ns,
+  launch_k(small_ar_kernel, kSmallArBlocks, 256, 0, s, in, out, units, op, bases, rank, world, cap_units, block_epochs, limit_ns,
                                          error_word());
   PB_CUDA_CHECK(cudaGetLastError());
 }

@@ -46,6 +46,7 @@ template <int BN, bool A_MN, bool B_MN, bool SWIGLU>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 EpiArgs ep, int M, int N, int K, int b_up_row, int* err) {
+  pdl_prologue();
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   // SwiGLU tiles produce BN/2 output columns from BN accumulator columns.
@@ -224,7 +225,7 @@ void launch(const GemmParams& p, cudaStream_t stream) {
   int ctas = num_sms(dev);
   if (p.max_ctas > 0) ctas = std::min(ctas, p.max_ctas);
   ctas = std::max(1, std::min(ctas, tiles));
-  kern<<<ctas, kThreads, Cfg::SMEM_BYTES, stream>>>(ta, tb, ep, p.M, p.N, p.K,
+  launch_k(kern, ctas, kThreads, Cfg::SMEM_BYTES, stream, ta, tb, ep, p.M, p.N, p.K,
                                                    (int)p.b_up_offset, error_word(dev));
   PB_CUDA_CHECK(cudaGetLastError());
 }
@@ -243,7 +244,7 @@ void gemm_bf16(const GemmParams& p, cudaStream_t stream) {
   if (p.epi == kEpiSwiGLU) PB_CHECK(!p.a_mn && !p.b_mn, "gemm: SwiGLU epilogue needs K-major operands");
   // The CTA-pair kernel (256-row tiles) wins on every training shape measured
   // with M >= 256; smaller M keeps the one-CTA kernel.
-  if (p.kernel == 2 || p.gather || p.scatter || p.splits > 1 || p.epi == kEpiSplitOrdered || p.row_stats ||
+  if (p.kernel == 2 || p.gather || p.scatter || p.splits > 1 || p.epi == kEpiSplitOrdered ||
       (p.kernel == 0 && p.M >= 256))
     return gemm_bf16_pair(p, stream);
   if (p.epi == kEpiSwiGLU) {

@@ -78,14 +78,7 @@ struct GemmParams {
   bool accumulate = false;  // kEpiSplitOrdered: C += result
   const ScatterArgs* scatter = nullptr;  // kEpiStoreBf16 rows to their sequence-parallel owners
   const GatherArgs* gather = nullptr;    // A assembled from sequence-parallel shards in-kernel
-  // kEpiStoreBf16 (CTA-pair kernel, M >= 256): per output row and 256-column
-  // tile, the max and the sum of exp(x - max) of the row's bf16 outputs, as
-  // row_stats[(m * stats_ld + tile) * 2 + {0, 1}] (the cross-entropy row
-  // statistics of LM-head logits, computed while the tile is in TMEM)
-  float* row_stats = nullptr;
-  int64_t stats_ld = 0;
 };
-constexpr int kRowStatsCols = 256;  // output columns per row-statistics entry
 
 // Grouped (mixture-of-experts) products, gemm_grouped.cu.  work: int4 per
 // tile {expert, M tile, N tile, 0}; rows of one expert start at a 128-row

@@ -2,7 +2,6 @@
 // thread owns one output row of a tile and reads its accumulator row from
 // TMEM 32 columns at a time.
 #pragma once
-#include <float.h>
 #include <cuda_bf16.h>
 
 #include "gemm.cuh"
@@ -25,8 +24,6 @@ struct EpiArgs {
   int* cnt;        // kEpiSplitOrdered: per (tile, CTA) count of published epilogue warps
   int out_f32;     // kEpiSplitOrdered: C is fp32
   int accum;       // kEpiSplitOrdered: C += result
-  float* stats;    // TMA bf16 store: per (row, tile) max / sum-exp of the bf16 outputs
-  int64_t stats_ld;
 };
 
 // TMA-store epilogue staging, per epilogue warp: three 32 x 32 bf16 boxes of
@@ -204,7 +201,6 @@ __device__ __forceinline__ void epilogue_warp_tma(const EpiArgs& ep, const CUten
                                                   int n_base, Release release) {
   constexpr int BN_OUT = SWIGLU ? BN / 2 : BN;
   const bool rows_in = y0 < M;
-  float st_m = -FLT_MAX, st_s = 0.f;  // row statistics (ep.stats)
 #pragma unroll 1
   for (int c = 0; c < BN_OUT; c += 32) {
     float a[32], b[32];
@@ -237,23 +233,6 @@ __device__ __forceinline__ void epilogue_warp_tma(const EpiArgs& ep, const CUten
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j) a[j] *= ep.alpha;
-      if (ep.stats) {
-        // statistics of the values the store writes (rounded to bf16), over
-        // the columns inside [0, N): running max, sum rescaled when it grows
-        float v[32];
-        float cm = -FLT_MAX;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          v[j] = (n0 + j < N) ? __bfloat162float(__float2bfloat16(a[j])) : -FLT_MAX;
-          cm = fmaxf(cm, v[j]);
-        }
-        if (cm > st_m) {
-          st_s *= __expf(st_m - cm);
-          st_m = cm;
-        }
-#pragma unroll
-        for (int j = 0; j < 32; ++j) st_s += (n0 + j < N) ? __expf(v[j] - st_m) : 0.f;
-      }
       // two boxes alternate: chunk c may be staged while chunk c - 1 drains
       box0 = stage + ((c >> 5) & 1) * kEpiBoxBytes;
       if (lane == 0) bulk_wait_group_read<1>();
@@ -270,11 +249,6 @@ __device__ __forceinline__ void epilogue_warp_tma(const EpiArgs& ep, const CUten
       }
     }
     if (lane == 0) bulk_commit_group();
-  }
-  if (!SWIGLU && ep.stats && y0 + lane < M && n_base < N) {
-    float* dst = ep.stats + ((int64_t)(y0 + lane) * ep.stats_ld + n_base / BN_OUT) * 2;
-    dst[0] = st_m;
-    dst[1] = st_s;
   }
 }
 

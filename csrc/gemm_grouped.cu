@@ -59,6 +59,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int4* __restrict__ work, int n_work, const int2* __restrict__ krange, int M_total,
                         int M_group, int N, int K, int b_up_row, const int* __restrict__ tile_expert,
                         const int* __restrict__ n_tiles, int ntn, int* err) {
+  pdl_prologue();
   using Cfg = GCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int BN_OUT = SWIGLU ? BN / 2 : BN;
@@ -261,7 +262,7 @@ void launch_grouped(const GroupedGemmParams& p, cudaStream_t stream) {
   const int ntn = (p.N + BN_OUT - 1) / BN_OUT;
   const int max_items = p.tile_expert != nullptr ? (p.M_total / BM) * ntn : p.n_work;
   const int ctas = std::max(1, std::min(num_sms(dev), max_items));
-  kern<<<ctas, kThreads, Cfg::SMEM_BYTES, stream>>>(ta, tb, ep, p.work, p.n_work, p.krange, p.M_total, p.M_group,
+  launch_k(kern, ctas, kThreads, Cfg::SMEM_BYTES, stream, ta, tb, ep, p.work, p.n_work, p.krange, p.M_total, p.M_group,
                                                     p.N, p.K, (int)p.b_up_offset, p.tile_expert, p.n_tiles, ntn,
                                                     error_word(dev));
   PB_CUDA_CHECK(cudaGetLastError());

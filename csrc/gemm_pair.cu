@@ -213,6 +213,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiArgs ep,
                      int M, int N, int K, int b_up_row, int* err, const __grid_constant__ GatherArgs ga,
                      int splits, const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR) {
+  pdl_prologue();
   using Cfg = PairCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int B_HALF = Cfg::B_HALF;
@@ -427,11 +428,13 @@ void launch_pair(const GemmParams& p, cudaStream_t stream) {
   int dev = 0;
   PB_CUDA_CHECK(cudaGetDevice(&dev));
   cudaLaunchConfig_t cfg{};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // pdl_prologue() (ptx.cuh)
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cfg.blockDim = dim3(GATHER ? kThreads + 64 : kThreads, 1, 1);
@@ -484,14 +487,6 @@ void launch_pair(const GemmParams& p, cudaStream_t stream) {
                                  64);
     ep.tma = 1;
   }
-  if (p.row_stats) {
-    const bool plain = !SWIGLU && !GATHER && BN == kRowStatsCols;
-    PB_CHECK(plain && p.epi == kEpiStoreBf16 && ep.tma == 1 && p.stats_ld >= (p.N + BN - 1) / BN,
-             "gemm: row statistics need the bf16 TMA-store epilogue of the CTA-pair kernel and one entry per "
-             "256-column tile");
-    ep.stats = p.row_stats;
-    ep.stats_ld = p.stats_ld;
-  }
   GatherArgs ga{};
   if (GATHER) ga = *p.gather;
   const int bn_out = SWIGLU ? BN / 2 : BN;
@@ -500,6 +495,7 @@ void launch_pair(const GemmParams& p, cudaStream_t stream) {
   if (p.max_ctas > 0) clusters = std::min(clusters, std::max(1, p.max_ctas / 2));
   clusters = std::max(1, std::min(clusters, tiles));
   cfg.gridDim = dim3(2 * clusters, 1, 1);
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   PB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, ep, p.M, p.N, p.K, (int)p.b_up_offset, error_word(dev), ga,
                                    std::max(1, p.splits), tc, tr));
 }

@@ -1,5 +1,6 @@
 #include "host_util.h"
 
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -41,6 +42,14 @@ int cur_device(int device) {
   return d;
 }
 }  // namespace
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("PB_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 int* error_word(int device) {
   device = cur_device(device);

@@ -8,6 +8,7 @@
 
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 namespace pb {
 
@@ -39,6 +40,31 @@ int read_error(int device = -1);
 void clear_error(int device = -1);
 
 int num_sms(int device = -1);
+
+// Programmatic dependent launch (PB_PDL, read once; default on): every kernel
+// of this library is launched with programmatic stream serialization and
+// starts with pdl_prologue() (ptx.cuh), which waits for the previous kernel
+// of the stream to complete and flush before anything else runs, then lets
+// the next kernel be launched.  The next kernel's launch and block set-up
+// thus overlap this kernel's tail instead of following its completion; the
+// data order is unchanged (each kernel still starts its work after its
+// predecessor finished).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  PB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
 
 // Encode a 2-D bf16 tiled tensor map with 128-byte swizzle.
 //   inner/outer: extents in elements; row_stride_elems: stride of the outer

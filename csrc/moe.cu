@@ -53,6 +53,7 @@ constexpr int kPlanWarps = kPlanThreads / 32;
 
 __global__ void __launch_bounds__(1024) moe_hist_kernel(const int64_t* __restrict__ topi, int64_t n_routes, int E,
                                                         float* __restrict__ mat, int mat_rows, int row) {
+  pdl_prologue();
   extern __shared__ int hist[];
   for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
   __syncthreads();
@@ -81,6 +82,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
                     int32_t* __restrict__ route_row, int32_t* __restrict__ own_cnt, int32_t* __restrict__ own_off,
                     int2* __restrict__ krange, int32_t* __restrict__ tile_expert, int32_t* __restrict__ n_tiles,
                     int tiles_cap, int* err) {
+  pdl_prologue();
   __shared__ PlanSmem sm;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int owners = E / E_loc;
@@ -168,6 +170,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
 __global__ void moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int K,
                                     const int32_t* __restrict__ owner, const int32_t* __restrict__ row,
                                     PeerBases dst, int64_t ldd, int64_t vecs, int64_t n_routes) {
+  pdl_prologue();
   const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n_routes) return;
@@ -183,6 +186,7 @@ __global__ void moe_copy_pad_kernel(const __nv_bfloat16* __restrict__ src, int64
                                     int64_t ldd, int64_t vecs, const int32_t* __restrict__ tile_expert,
                                     const int32_t* __restrict__ n_tiles, const int32_t* __restrict__ own_cnt,
                                     const int32_t* __restrict__ own_off) {
+  pdl_prologue();
   const int64_t row0 = (int64_t)blockIdx.x * 16;
   const int tiles = *n_tiles;
   if (row0 >= (int64_t)tiles * 128) return;
@@ -218,6 +222,7 @@ __global__ void moe_combine_kernel(__nv_bfloat16* __restrict__ out, int64_t ldo,
                                    const float* __restrict__ w, const int32_t* __restrict__ owner,
                                    const int32_t* __restrict__ row, PeerBases src, int64_t lds, int K, int64_t vecs,
                                    int64_t n_tokens) {
+  pdl_prologue();
   const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= n_tokens) return;
@@ -249,6 +254,7 @@ __global__ void moe_combine_bwd_kernel(const __nv_bfloat16* __restrict__ dout, i
                                        const int32_t* __restrict__ owner, const int32_t* __restrict__ row,
                                        PeerBases dst, int64_t ldd, int K, int64_t vecs, int64_t n_routes,
                                        float* __restrict__ dw) {
+  pdl_prologue();
   const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n_routes) return;
@@ -286,7 +292,7 @@ unsigned warp_blocks(int64_t warps) { return (unsigned)((warps * 32 + 255) / 256
 
 void moe_hist(const int64_t* topi, int64_t n_routes, int E, float* mat, int mat_rows, int row, cudaStream_t s) {
   PB_CHECK(E >= 1 && E <= kMoeMaxExperts && row >= 0 && row < mat_rows, "moe_hist: sizes");
-  moe_hist_kernel<<<1, 1024, E * sizeof(int), s>>>(topi, n_routes, E, mat, mat_rows, row);
+  launch_k(moe_hist_kernel, 1, 1024, E * sizeof(int), s, topi, n_routes, E, mat, mat_rows, row);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -296,7 +302,7 @@ void moe_plan(const MoePlanArgs& a, cudaStream_t s) {
   PB_CHECK(a.my_row >= 0 && a.my_row < a.mat_rows, "moe_plan: histogram row");
   int dev = 0;
   PB_CUDA_CHECK(cudaGetDevice(&dev));
-  moe_plan_kernel<<<1, kPlanThreads, 0, s>>>(a.topi, a.n_routes, a.mat, a.mat_rows, a.my_row, a.E, a.E_loc, a.ep_rank,
+  launch_k(moe_plan_kernel, 1, kPlanThreads, 0, s, a.topi, a.n_routes, a.mat, a.mat_rows, a.my_row, a.E, a.E_loc, a.ep_rank,
                                              a.local_only, a.route_owner, a.route_row, a.own_cnt, a.own_off,
                                              reinterpret_cast<int2*>(a.krange), a.tile_expert, a.n_tiles, a.tiles_cap,
                                              error_word(dev));
@@ -307,7 +313,7 @@ void moe_dispatch(const void* x, int64_t ldx, int K, const int32_t* owner, const
                   int64_t ldd, int64_t cols, int64_t n_routes, cudaStream_t s) {
   PB_CHECK(cols % 8 == 0 && ldx % 8 == 0 && ldd % 8 == 0, "moe_dispatch: 16-byte rows");
   if (n_routes == 0) return;
-  moe_dispatch_kernel<<<warp_blocks(n_routes), 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, K, owner,
+  launch_k(moe_dispatch_kernel, warp_blocks(n_routes), 256, 0, s, reinterpret_cast<const __nv_bfloat16*>(x), ldx, K, owner,
                                                             row, dst, ldd, cols / 8, n_routes);
   PB_CUDA_CHECK(cudaGetLastError());
 }
@@ -317,7 +323,7 @@ void moe_copy_pad(const void* src, int64_t lds, void* dst, int64_t ldd, int64_t 
                   cudaStream_t s) {
   PB_CHECK(cols % 8 == 0 && lds % 8 == 0 && ldd % 8 == 0, "moe_copy_pad: 16-byte rows");
   if (tiles_cap == 0) return;
-  moe_copy_pad_kernel<<<(unsigned)(tiles_cap * 8), dim3(64, 4), 0, s>>>(
+  launch_k(moe_copy_pad_kernel, (unsigned)(tiles_cap * 8), dim3(64, 4), 0, s,
       reinterpret_cast<const __nv_bfloat16*>(src), lds, reinterpret_cast<__nv_bfloat16*>(dst), ldd, cols / 8,
       tile_expert, n_tiles, own_cnt, own_off);
   PB_CUDA_CHECK(cudaGetLastError());
@@ -327,7 +333,7 @@ void moe_combine(void* out, int64_t ldo, void* keep, const float* w, const int32
                  const PeerBases& src, int64_t lds, int K, int64_t cols, int64_t n_tokens, cudaStream_t s) {
   PB_CHECK(cols % 8 == 0 && ldo % 8 == 0 && lds % 8 == 0, "moe_combine: 16-byte rows");
   if (n_tokens == 0) return;
-  moe_combine_kernel<<<warp_blocks(n_tokens), 256, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), ldo,
+  launch_k(moe_combine_kernel, warp_blocks(n_tokens), 256, 0, s, reinterpret_cast<__nv_bfloat16*>(out), ldo,
                                                            reinterpret_cast<__nv_bfloat16*>(keep), w, owner, row, src,
                                                            lds, K, cols / 8, n_tokens);
   PB_CUDA_CHECK(cudaGetLastError());
@@ -338,7 +344,7 @@ void moe_combine_bwd(const void* dout, int64_t ldo, const void* kept, const floa
                      float* dw, cudaStream_t s) {
   PB_CHECK(cols % 8 == 0 && ldo % 8 == 0 && ldd % 8 == 0, "moe_combine_bwd: 16-byte rows");
   if (n_routes == 0) return;
-  moe_combine_bwd_kernel<<<warp_blocks(n_routes), 256, 0, s>>>(
+  launch_k(moe_combine_bwd_kernel, warp_blocks(n_routes), 256, 0, s,
       reinterpret_cast<const __nv_bfloat16*>(dout), ldo, reinterpret_cast<const __nv_bfloat16*>(kept), w, owner, row,
       dst, ldd, K, cols / 8, n_routes, dw);
   PB_CUDA_CHECK(cudaGetLastError());

@@ -44,6 +44,7 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
 __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
                                    int64_t ldy, float* __restrict__ rstd, int rows, int cols, float eps) {
+  pdl_prologue();
   const int warps = blockDim.x >> 5;
   const int row = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -79,6 +80,7 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int64_t
                                    __nv_bfloat16* __restrict__ dx, int64_t lddx, float* __restrict__ dw,
                                    int rows, int cols, int rows_per_block,
                                    const __nv_bfloat16* __restrict__ dres, int64_t lddres) {
+  pdl_prologue();
   extern __shared__ float sdw_all[];  // [warps][cols]
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -141,6 +143,7 @@ __global__ void __launch_bounds__(256, 2) rmsnorm_bwd_reg_kernel(
     const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dres,
     int64_t lddres, __nv_bfloat16* __restrict__ dx, int64_t lddx, float* __restrict__ dw, int rows,
     int rows_per_block) {
+  pdl_prologue();
   // One warp per row, all of the row's loads (x, dy, dres) issued before the
   // reduction and kept packed in registers, so a row costs one DRAM round
   // trip.  Weight-grad partials live in a per-warp shared-memory slice (each
@@ -246,6 +249,7 @@ __global__ void qknorm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, in
                                        __nv_bfloat16* __restrict__ q_out, int64_t ldq,
                                        __nv_bfloat16* __restrict__ k_out, int64_t ldk,
                                        float* __restrict__ rstd, int T, int S, int nq, int nkv, float eps) {
+  pdl_prologue();
   // A half warp per unit = (token, U consecutive heads): the token's cos / sin
   // rows are loaded once and all U input rows are issued before the first
   // reduction (one DRAM round trip per unit).  The bf16 products / sums of the
@@ -330,6 +334,7 @@ __global__ void __launch_bounds__(256, 2) qknorm_rope_bwd_kernel(const __nv_bflo
                                        __nv_bfloat16* __restrict__ dqkv, int64_t lddqkv,
                                        float* __restrict__ dqw, float* __restrict__ dkw, int T, int S,
                                        int nq, int nkv, int units_per_block) {
+  pdl_prologue();
   // A half warp per unit = (token, group of U consecutive heads): the token's
   // cos / sin rows are loaded once per unit and every head's gradient and
   // input rows (2 x 16 bytes per lane per head) are issued before the first
@@ -440,7 +445,7 @@ void rmsnorm_fwd(const void* x, int64_t ldx, const void* w, void* y, int64_t ldy
                  int rows, int cols, float eps, cudaStream_t s) {
   PB_CHECK(cols % 8 == 0, "rmsnorm: cols must be a multiple of 8");
   const int warps = 8;
-  rmsnorm_fwd_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, s>>>(
+  launch_k(rmsnorm_fwd_kernel, (rows + warps - 1) / warps, warps * 32, 0, s,
       (const __nv_bfloat16*)x, ldx, (const __nv_bfloat16*)w, (__nv_bfloat16*)y, ldy, rstd, rows,
       cols, eps);
   PB_CUDA_CHECK(cudaGetLastError());
@@ -476,7 +481,7 @@ void rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const
   if (cols % 256 == 0 && cols <= 1536) {  // wider rows would spill: generic kernel
 #define PB_RMS_BWD(CH)                                                                                     \
   case CH:                                                                                                \
-    rmsnorm_bwd_reg_kernel<CH><<<grid, 256, smem_reg, s>>>(                                                \
+    launch_k(rmsnorm_bwd_reg_kernel<CH>, grid, 256, smem_reg, s,                                                 \
         (const __nv_bfloat16*)dy, lddy, (const __nv_bfloat16*)x, ldx, (const __nv_bfloat16*)w, rstd,      \
         (const __nv_bfloat16*)dres, lddres, (__nv_bfloat16*)dx, lddx, dw_acc, rows, rpb);                 \
     break;
@@ -487,7 +492,7 @@ void rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const
     PB_CUDA_CHECK(cudaGetLastError());
     return;
   }
-  rmsnorm_bwd_kernel<<<grid, 256, smem, s>>>((const __nv_bfloat16*)dy, lddy, (const __nv_bfloat16*)x,
+  launch_k(rmsnorm_bwd_kernel, grid, 256, smem, s, (const __nv_bfloat16*)dy, lddy, (const __nv_bfloat16*)x,
                                              ldx, (const __nv_bfloat16*)w, rstd, (__nv_bfloat16*)dx,
                                              lddx, dw_acc, rows, cols, rpb, (const __nv_bfloat16*)dres,
                                              lddres);
@@ -501,7 +506,7 @@ void qknorm_rope_fwd(const void* qkv, int64_t ldqkv, const void* qw, const void*
   PB_CHECK(D == 128, "qknorm_rope: head_dim 128 only");
   const int units = T * ((nq + nkv + 3) / 4);  // (token, 4 heads) units
   const int per_block = 16;                    // 8 warps x 2 half-warps
-  qknorm_rope_fwd_kernel<<<(units + per_block - 1) / per_block, 256, 0, s>>>(
+  launch_k(qknorm_rope_fwd_kernel, (units + per_block - 1) / per_block, 256, 0, s,
       (const __nv_bfloat16*)qkv, ldqkv, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw,
       (const __nv_bfloat16*)cos, (const __nv_bfloat16*)sin, (__nv_bfloat16*)q_out, ldq,
       (__nv_bfloat16*)k_out, ldk, rstd, T, S, nq, nkv, eps);
@@ -523,7 +528,7 @@ void qknorm_rope_bwd(const void* dq, int64_t lddq, const void* dk, int64_t lddk,
   const int units = T * ((nq + nkv + 3) / 4);
   const int grid = qknorm_rope_bwd_grid(T, nq, nkv);
   const int ipb = (std::max(units, 1) + grid - 1) / grid;
-  qknorm_rope_bwd_kernel<<<grid, 256, 0, s>>>(
+  launch_k(qknorm_rope_bwd_kernel, grid, 256, 0, s,
       (const __nv_bfloat16*)dq, lddq, (const __nv_bfloat16*)dk, lddk, (const __nv_bfloat16*)qkv,
       ldqkv, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw, (const __nv_bfloat16*)cos,
       (const __nv_bfloat16*)sin, rstd, (__nv_bfloat16*)dqkv, lddqkv, dw_part, nullptr, T, S, nq,

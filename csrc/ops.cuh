@@ -66,7 +66,7 @@ void scale_by_scalar(void* x, int64_t n, const float* s_dev, cudaStream_t s);
 // (zeros for ignored rows).
 void ce_fwd_bwd(void* logits, int64_t ld, const int64_t* labels, int T, int V, int64_t v0,
                 const float* scale, float* row_lse, bool lse_given, float* row_target,
-                bool write_grad, cudaStream_t s, const float* stats = nullptr, int n_tiles = 0);
+                bool write_grad, cudaStream_t s);
 // inv[0] = 1 / max(1, #{t : labels[t] >= 0})   (one block)
 void ce_valid_inv(const int64_t* labels, int T, float* inv, cudaStream_t s);
 // out[0] = (accumulate ? out[0] : 0) + inv[0] * sum over valid rows of (lse - tgt),

@@ -212,26 +212,15 @@ void aux_stats_bwd(const at::Tensor& probs, const at::Tensor& gsum, at::Tensor& 
                     dprobs.data_ptr<float>(), cur_stream());
 }
 
-// stats (optional, fp32 [T, 2 * n_tiles]): row (max, sum-exp) partials per
-// 256-column tile from the GEMM that produced the logits (gemm(row_stats=...))
 void ce_fwd_bwd(at::Tensor& logits, const at::Tensor& labels, int64_t v0, const c10::optional<at::Tensor>& scale,
                 const c10::optional<at::Tensor>& row_lse, bool lse_given, const c10::optional<at::Tensor>& row_target,
-                bool write_grad, const c10::optional<at::Tensor>& stats) {
+                bool write_grad) {
   CHECK_BF16(logits);
   TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous(), "labels must be contiguous int64");
   TORCH_CHECK(labels.numel() == logits.size(0), "ce: one label per row");
-  int n_tiles = 0;
-  if (stats.has_value() && stats->defined()) {
-    CHECK_F32(*stats);
-    TORCH_CHECK(stats->dim() == 2 && stats->is_contiguous() && stats->size(0) == logits.size(0) &&
-                    stats->size(1) % 2 == 0 && stats->size(1) / 2 >= (logits.size(1) + 255) / 256,
-                "ce: stats must be contiguous fp32 [T, 2 * n_tiles] covering the row");
-    n_tiles = (int)(stats->size(1) / 2);
-  }
   const c10::cuda::CUDAGuard g(logits.device());
   pb::ce_fwd_bwd(logits.data_ptr(), logits.stride(0), labels.data_ptr<int64_t>(), logits.size(0), logits.size(1),
-                 v0, opt_f32(scale), opt_f32(row_lse), lse_given, opt_f32(row_target), write_grad, cur_stream(),
-                 opt_f32(stats), n_tiles);
+                 v0, opt_f32(scale), opt_f32(row_lse), lse_given, opt_f32(row_target), write_grad, cur_stream());
 }
 
 // ce_valid_inv(labels int64 [T], inv fp32 [1]): inv = 1 / max(1, #valid labels)
@@ -424,9 +413,7 @@ void register_ops(pybind11::module& m) {
   m.def("router_bwd", &router_bwd);
   m.def("aux_stats", &aux_stats);
   m.def("aux_stats_bwd", &aux_stats_bwd);
-  m.def("ce_fwd_bwd", &ce_fwd_bwd, py::arg("logits"), py::arg("labels"), py::arg("v0"), py::arg("scale"),
-        py::arg("row_lse"), py::arg("lse_given"), py::arg("row_target"), py::arg("write_grad"),
-        py::arg("stats") = py::none());
+  m.def("ce_fwd_bwd", &ce_fwd_bwd);
   m.def("ce_row_stats", &ce_row_stats);
   m.def("ce_valid_inv", &ce_valid_inv);
   m.def("ce_loss_reduce", &ce_loss_reduce);

@@ -105,6 +105,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(SegTable tab, float lr,
                                                          const float* __restrict__ gscale,
                                                          const int* __restrict__ skip,
                                                          const float* __restrict__ hyper) {
+  pdl_prologue();
   if (skip && *skip) return;
   const float gs = gscale ? *gscale : 1.f;
   if (hyper) {  // {lr, 1 - beta1^t, sqrt(1 - beta2^t)} from the device (CUDA-graph replays)
@@ -152,6 +153,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(SegTable tab, float lr,
 // chunks in chunk order, so the norm has the same bits on every run.
 template <typename GT>
 __global__ void __launch_bounds__(kThreads) sumsq_kernel(NormTable tab, float* __restrict__ parts, int chunk_base) {
+  pdl_prologue();
   const int chunk = blockIdx.x;
   const int si = find_seg(tab.chunk_start, tab.nseg, chunk);
   const NormSeg sg = tab.seg[si];
@@ -191,6 +193,7 @@ constexpr int kFinishThreads = 1024;
 __global__ void __launch_bounds__(kFinishThreads) sumsq_finish_kernel(const float* __restrict__ parts, int chunks,
                                                                       float* __restrict__ out, int* __restrict__ flag,
                                                                       bool accumulate) {
+  pdl_prologue();
   float a = 0.f;
   float bad = 0.f;
   for (int c = threadIdx.x; c < chunks; c += kFinishThreads) {
@@ -220,6 +223,7 @@ __global__ void __launch_bounds__(kFinishThreads) sumsq_finish_kernel(const floa
 }
 
 __global__ void clip_coef_kernel(const float* total, float max_norm, float* out) {
+  pdl_prologue();
   const float n = sqrtf(*total);
   out[0] = fminf(max_norm / (n + 1e-6f), 1.f);
 }
@@ -243,16 +247,16 @@ void adamw_multi(const AdamSeg* segs, int nseg, float lr, float beta1, float bet
     tab.chunk_start[tab.nseg] = chunks;
     if (chunks == 0) continue;
     if (grad_f32 && state_f32)
-      adamw_kernel<float, float><<<chunks, kThreads, 0, s>>>(tab, lr, beta1, beta2, eps, wd, bc1,
+      launch_k(adamw_kernel<float, float>, chunks, kThreads, 0, s, tab, lr, beta1, beta2, eps, wd, bc1,
                                                              bc2_sqrt, grad_scale_dev, skip_dev, hyper_dev);
     else if (grad_f32)
-      adamw_kernel<float, __nv_bfloat16><<<chunks, kThreads, 0, s>>>(
+      launch_k(adamw_kernel<float, __nv_bfloat16>, chunks, kThreads, 0, s,
           tab, lr, beta1, beta2, eps, wd, bc1, bc2_sqrt, grad_scale_dev, skip_dev, hyper_dev);
     else if (state_f32)
-      adamw_kernel<__nv_bfloat16, float><<<chunks, kThreads, 0, s>>>(
+      launch_k(adamw_kernel<__nv_bfloat16, float>, chunks, kThreads, 0, s,
           tab, lr, beta1, beta2, eps, wd, bc1, bc2_sqrt, grad_scale_dev, skip_dev, hyper_dev);
     else
-      adamw_kernel<__nv_bfloat16, __nv_bfloat16><<<chunks, kThreads, 0, s>>>(
+      launch_k(adamw_kernel<__nv_bfloat16, __nv_bfloat16>, chunks, kThreads, 0, s,
           tab, lr, beta1, beta2, eps, wd, bc1, bc2_sqrt, grad_scale_dev, skip_dev, hyper_dev);
     PB_CUDA_CHECK(cudaGetLastError());
   }
@@ -281,18 +285,18 @@ void sumsq_multi(const NormSeg* segs, int nseg, bool f32, float* parts, float* o
     tab.chunk_start[tab.nseg] = chunks;
     if (chunks == 0) continue;
     if (f32)
-      sumsq_kernel<float><<<chunks, kThreads, 0, s>>>(tab, parts, base);
+      launch_k(sumsq_kernel<float>, chunks, kThreads, 0, s, tab, parts, base);
     else
-      sumsq_kernel<__nv_bfloat16><<<chunks, kThreads, 0, s>>>(tab, parts, base);
+      launch_k(sumsq_kernel<__nv_bfloat16>, chunks, kThreads, 0, s, tab, parts, base);
     PB_CUDA_CHECK(cudaGetLastError());
     base += chunks;
   }
-  sumsq_finish_kernel<<<1, kFinishThreads, 0, s>>>(parts, (int)total, out, out_flag, accumulate);
+  launch_k(sumsq_finish_kernel, 1, kFinishThreads, 0, s, parts, (int)total, out, out_flag, accumulate);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
 void clip_coef(const float* total_sumsq, float max_norm, float* scale_out, cudaStream_t s) {
-  clip_coef_kernel<<<1, 1, 0, s>>>(total_sumsq, max_norm, scale_out);
+  launch_k(clip_coef_kernel, 1, 1, 0, s, total_sumsq, max_norm, scale_out);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -19,6 +19,17 @@
 
 namespace pb {
 
+
+// Programmatic dependent launch (launch_k in host_util.h): the first statement
+// of every kernel.  griddepcontrol.wait returns once the previous kernel of the
+// stream has completed and its memory is visible (immediately when the kernel
+// was launched without the attribute); launch_dependents then lets the next
+// kernel's blocks be scheduled as soon as every block of this one has started.
+__device__ __forceinline__ void pdl_prologue() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Error codes written to the device error word (first writer wins).
 enum ErrorCode : int {
   kErrNone = 0,

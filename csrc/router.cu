@@ -24,6 +24,7 @@
 #include <algorithm>
 
 #include "host_util.h"
+#include "ptx.cuh"
 #include "ops.cuh"
 
 namespace pb {
@@ -103,6 +104,7 @@ template <int VPL>
 __global__ void router_fwd_kernel(const __nv_bfloat16* __restrict__ logits, int64_t ld, int T, int E, int K,
                                   bool renorm, float* __restrict__ probs, float* __restrict__ topv,
                                   int64_t* __restrict__ topi, int* __restrict__ counts) {
+  pdl_prologue();
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -136,6 +138,7 @@ template <int VPL>
 __global__ void router_bwd_kernel(const float* __restrict__ probs, const float* __restrict__ dprobs,
                                   const float* __restrict__ dtopv, const int64_t* __restrict__ topi, int T, int E,
                                   int K, bool renorm, __nv_bfloat16* __restrict__ dlogits, int64_t ld) {
+  pdl_prologue();
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -182,6 +185,7 @@ __global__ void router_bwd_kernel(const float* __restrict__ probs, const float* 
 // statistics have the same bits on every run.
 template <int VPL>
 __global__ void aux_stats_kernel(const float* __restrict__ probs, int R, int E, int K, float* __restrict__ parts) {
+  pdl_prologue();
   extern __shared__ float sh[];  // [warps][2E]
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -226,6 +230,7 @@ __global__ void aux_stats_kernel(const float* __restrict__ probs, int R, int E, 
 template <int VPL>
 __global__ void aux_stats_bwd_kernel(const float* __restrict__ probs, const float* __restrict__ gsum, int R, int E,
                                      float* __restrict__ dprobs) {
+  pdl_prologue();
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= R) return;
@@ -264,10 +269,10 @@ void router_fwd(const void* logits, int64_t ld, int T, int E, int K, bool renorm
   if (T == 0) return;
   const dim3 grid((T + 7) / 8), block(256);
   switch (vpl_for(E)) {
-    case 1: router_fwd_kernel<1><<<grid, block, 0, s>>>((const __nv_bfloat16*)logits, ld, T, E, K, renorm, probs, topv, topi, counts); break;
-    case 2: router_fwd_kernel<2><<<grid, block, 0, s>>>((const __nv_bfloat16*)logits, ld, T, E, K, renorm, probs, topv, topi, counts); break;
-    case 4: router_fwd_kernel<4><<<grid, block, 0, s>>>((const __nv_bfloat16*)logits, ld, T, E, K, renorm, probs, topv, topi, counts); break;
-    default: router_fwd_kernel<8><<<grid, block, 0, s>>>((const __nv_bfloat16*)logits, ld, T, E, K, renorm, probs, topv, topi, counts); break;
+    case 1: launch_k(router_fwd_kernel<1>, grid, block, 0, s, (const __nv_bfloat16*)logits, ld, T, E, K, renorm, probs, topv, topi, counts); break;
+    case 2: launch_k(router_fwd_kernel<2>, grid, block, 0, s, (const __nv_bfloat16*)logits, ld, T, E, K, renorm, probs, topv, topi, counts); break;
+    case 4: launch_k(router_fwd_kernel<4>, grid, block, 0, s, (const __nv_bfloat16*)logits, ld, T, E, K, renorm, probs, topv, topi, counts); break;
+    default: launch_k(router_fwd_kernel<8>, grid, block, 0, s, (const __nv_bfloat16*)logits, ld, T, E, K, renorm, probs, topv, topi, counts); break;
   }
   PB_CUDA_CHECK(cudaGetLastError());
 }
@@ -278,10 +283,10 @@ void router_bwd(const float* probs, const float* dprobs, const float* dtopv, con
   const dim3 grid((T + 7) / 8), block(256);
   auto* dl = (__nv_bfloat16*)dlogits;
   switch (vpl_for(E)) {
-    case 1: router_bwd_kernel<1><<<grid, block, 0, s>>>(probs, dprobs, dtopv, topi, T, E, K, renorm, dl, ld); break;
-    case 2: router_bwd_kernel<2><<<grid, block, 0, s>>>(probs, dprobs, dtopv, topi, T, E, K, renorm, dl, ld); break;
-    case 4: router_bwd_kernel<4><<<grid, block, 0, s>>>(probs, dprobs, dtopv, topi, T, E, K, renorm, dl, ld); break;
-    default: router_bwd_kernel<8><<<grid, block, 0, s>>>(probs, dprobs, dtopv, topi, T, E, K, renorm, dl, ld); break;
+    case 1: launch_k(router_bwd_kernel<1>, grid, block, 0, s, probs, dprobs, dtopv, topi, T, E, K, renorm, dl, ld); break;
+    case 2: launch_k(router_bwd_kernel<2>, grid, block, 0, s, probs, dprobs, dtopv, topi, T, E, K, renorm, dl, ld); break;
+    case 4: launch_k(router_bwd_kernel<4>, grid, block, 0, s, probs, dprobs, dtopv, topi, T, E, K, renorm, dl, ld); break;
+    default: launch_k(router_bwd_kernel<8>, grid, block, 0, s, probs, dprobs, dtopv, topi, T, E, K, renorm, dl, ld); break;
   }
   PB_CUDA_CHECK(cudaGetLastError());
 }
@@ -293,10 +298,10 @@ void aux_stats(const float* probs, int R, int E, int K, float* parts, cudaStream
   const int blocks = aux_stats_grid(R);
   const size_t sm = 8 * 2 * (size_t)E * sizeof(float);  // 8 warps x (counts, sums)
   switch (vpl_for(E)) {
-    case 1: aux_stats_kernel<1><<<blocks, 256, sm, s>>>(probs, R, E, K, parts); break;
-    case 2: aux_stats_kernel<2><<<blocks, 256, sm, s>>>(probs, R, E, K, parts); break;
-    case 4: aux_stats_kernel<4><<<blocks, 256, sm, s>>>(probs, R, E, K, parts); break;
-    default: aux_stats_kernel<8><<<blocks, 256, sm, s>>>(probs, R, E, K, parts); break;
+    case 1: launch_k(aux_stats_kernel<1>, blocks, 256, sm, s, probs, R, E, K, parts); break;
+    case 2: launch_k(aux_stats_kernel<2>, blocks, 256, sm, s, probs, R, E, K, parts); break;
+    case 4: launch_k(aux_stats_kernel<4>, blocks, 256, sm, s, probs, R, E, K, parts); break;
+    default: launch_k(aux_stats_kernel<8>, blocks, 256, sm, s, probs, R, E, K, parts); break;
   }
   PB_CUDA_CHECK(cudaGetLastError());
 }
@@ -305,10 +310,10 @@ void aux_stats_bwd(const float* probs, const float* gsum, int R, int E, float* d
   if (R == 0) return;
   const dim3 grid((R + 7) / 8), block(256);
   switch (vpl_for(E)) {
-    case 1: aux_stats_bwd_kernel<1><<<grid, block, 0, s>>>(probs, gsum, R, E, dprobs); break;
-    case 2: aux_stats_bwd_kernel<2><<<grid, block, 0, s>>>(probs, gsum, R, E, dprobs); break;
-    case 4: aux_stats_bwd_kernel<4><<<grid, block, 0, s>>>(probs, gsum, R, E, dprobs); break;
-    default: aux_stats_bwd_kernel<8><<<grid, block, 0, s>>>(probs, gsum, R, E, dprobs); break;
+    case 1: launch_k(aux_stats_bwd_kernel<1>, grid, block, 0, s, probs, gsum, R, E, dprobs); break;
+    case 2: launch_k(aux_stats_bwd_kernel<2>, grid, block, 0, s, probs, gsum, R, E, dprobs); break;
+    case 4: launch_k(aux_stats_bwd_kernel<4>, grid, block, 0, s, probs, gsum, R, E, dprobs); break;
+    default: launch_k(aux_stats_bwd_kernel<8>, grid, block, 0, s, probs, gsum, R, E, dprobs); break;
   }
   PB_CUDA_CHECK(cudaGetLastError());
 }

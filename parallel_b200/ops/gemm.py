@@ -62,25 +62,9 @@ def _rows(t: torch.Tensor) -> torch.Tensor:
     return t.reshape(-1, t.shape[-1])
 
 
-def row_stats_supported(x2: torch.Tensor, n_out: int) -> bool:
-    """Whether ``linear(..., row_stats=...)`` can produce the per-row
-    statistics in the GEMM's epilogue (CTA-pair kernel, TMA-store output)."""
-    return (use_kernels(x2) and x2.shape[0] >= 256 and n_out % 8 == 0 and x2.stride(-1) == 1
-            and x2.shape[-1] % 8 == 0)
-
-
-def row_stats_buffer(rows: int, n_out: int, device) -> torch.Tensor:
-    """fp32 [rows, 2 * ceil(n_out / 256)]: (max, sum of exp(x - max)) of each
-    output row's bf16 values per 256-column tile."""
-    return torch.empty(rows, 2 * (-(-n_out // 256)), dtype=torch.float32, device=device)
-
-
 def linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None,
-           out: torch.Tensor | None = None, row_stats: torch.Tensor | None = None) -> torch.Tensor:
-    """``x @ w.T (+ residual)`` for x [..., K], w [N, K].  ``row_stats``
-    (``row_stats_buffer``; needs ``row_stats_supported``) also receives the
-    softmax statistics of each output row, computed while the tile is in
-    tensor memory (the cross-entropy of LM-head logits then reads them once)."""
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """``x @ w.T (+ residual)`` for x [..., K], w [N, K]."""
     lead = x.shape[:-1]
     x2 = _rows(x)
     if not use_kernels(x2):
@@ -92,11 +76,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = Non
     if out is None:
         out = torch.empty(x2.shape[0], w.shape[0], dtype=torch.bfloat16, device=x.device)
     if residual is not None:
-        if row_stats is not None:
-            raise ValueError("linear: row statistics need the plain bf16 store (no residual)")
         ext().gemm(x2, w, out, False, False, EPI_RESIDUAL_BF16, 1.0, _rows(residual))
-    elif row_stats is not None:
-        ext().gemm(x2, w, out, False, False, EPI_STORE_BF16, 1.0, row_stats=row_stats)
     else:
         ext().gemm(x2, w, out, False, False, EPI_STORE_BF16, 1.0)
     return out.reshape(*lead, w.shape[0])

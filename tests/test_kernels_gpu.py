@@ -589,46 +589,3 @@ def test_aux_loss_stats_match_torch():
     for p, r in zip(probs, ref_probs):
         assert _rel_err(p.grad, r.grad) < 1e-4
     _check_no_device_error()
-
-
-def test_gemm_row_stats_and_cross_entropy_from_them():
-    """The bf16-store GEMM's row statistics (max / sum-exp per 256-column tile
-    of the rounded outputs) merge to the row log-sum-exp, and the cross-entropy
-    that consumes them matches the one that makes its own statistics pass."""
-    from parallel_b200.ops.gemm import EPI_STORE_BF16, row_stats_buffer
-
-    C = _ext()
-    torch.manual_seed(21)
-    T, V, K = 512, 1000, 256  # V: a partial last tile (1000 = 3 * 256 + 232)
-    h = torch.randn(T, K, device="cuda").to(torch.bfloat16)
-    w = (0.1 * torch.randn(V, K, device="cuda")).to(torch.bfloat16)
-    logits = torch.empty(T, V, device="cuda", dtype=torch.bfloat16)
-    stats = row_stats_buffer(T, V, "cuda")
-    C.gemm(h, w, logits, False, False, EPI_STORE_BF16, 1.0, row_stats=stats)
-    _check_no_device_error()
-    ref = torch.empty_like(logits)
-    C.gemm(h, w, ref, False, False, EPI_STORE_BF16, 1.0)
-    assert torch.equal(logits, ref)  # the statistics leave the stored values alone
-    lf = logits.float()
-    st = stats.view(T, -1, 2)
-    for i in range(st.shape[1]):
-        blk = lf[:, i * 256:(i + 1) * 256]
-        torch.testing.assert_close(st[:, i, 0], blk.max(-1).values, rtol=0, atol=0)
-        torch.testing.assert_close(st[:, i, 1], torch.exp(blk - blk.max(-1, keepdim=True).values).sum(-1),
-                                   rtol=1e-4, atol=1e-4)
-    labels = torch.randint(0, V, (T,), device="cuda")
-    labels[::7] = -100
-    scale = torch.full((1,), 1.0 / T, device="cuda")
-    out = []
-    for use in (False, True):
-        lg = logits.clone()
-        lse, tgt = torch.empty(T, device="cuda"), torch.empty(T, device="cuda")
-        C.ce_fwd_bwd(lg, labels, 0, scale, lse, False, tgt, True, stats if use else None)
-        _check_no_device_error()
-        out.append((lg, lse, tgt))
-    (g0, l0, t0), (g1, l1, t1) = out
-    valid = labels >= 0
-    torch.testing.assert_close(l1, torch.logsumexp(lf, -1), rtol=1e-5, atol=1e-5)
-    torch.testing.assert_close(l1[valid], l0[valid], rtol=1e-5, atol=1e-5)
-    assert torch.equal(t1, t0)
-    assert _rel_err(g1, g0) < 1e-2
