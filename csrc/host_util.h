@@ -41,14 +41,14 @@ void clear_error(int device = -1);
 
 int num_sms(int device = -1);
 
-// Programmatic dependent launch (PB_PDL, read once; default on): every kernel
-// of this library is launched with programmatic stream serialization and
-// starts with pdl_prologue() (ptx.cuh), which waits for the previous kernel
-// of the stream to complete and flush before anything else runs, then lets
-// the next kernel be launched.  The next kernel's launch and block set-up
-// thus overlap this kernel's tail instead of following its completion; the
-// data order is unchanged (each kernel still starts its work after its
-// predecessor finished).
+// Programmatic dependent launch (PB_PDL=1, read once; default off).  Every
+// kernel of this library starts with pdl_prologue() (ptx.cuh), which waits
+// for the previous kernel of the stream to complete and flush before anything
+// else runs; with PB_PDL=1 launch_k also sets programmatic stream
+// serialization, so the next kernel's launch and block set-up overlap this
+// kernel's tail instead of following its completion.  The data order is the
+// same either way (each kernel starts its work after its predecessor
+// finished); without the attribute the prologue is a no-op.
 bool pdl_enabled();
 
 template <typename... KArgs, typename... Args>
