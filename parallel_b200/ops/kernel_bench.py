@@ -1,6 +1,6 @@
 """Micro-benchmarks of the sm_100a kernels at the Qwen3-0.6B training shapes.
 
-    python -m parallel_b200.ops.kernel_bench attn_fwd|attn_bwd|ce|gemm|gemm_swiglu|gemm_residual|rmsnorm_bwd|qknorm|qknorm_bwd|wgrad_split|all [--iters N]
+    python -m parallel_b200.ops.kernel_bench attn_fwd|attn_bwd|ce|gemm|gemm_vs_cublas|gemm_swiglu|gemm_residual|rmsnorm_bwd|qknorm|qknorm_bwd|wgrad_split|all [--iters N]
 
 Each case runs a few warm-up launches, then times ``--iters`` launches with
 CUDA events on the current stream and prints the time per launch and the
@@ -188,7 +188,43 @@ def case_ce(warmup, iters):
     return f"cross-entropy fwd+bwd {T}x{V}: {us:.1f} us, {2 * T * V * 2 / us / 1e3:.0f} GB/s"
 
 
-CASES = {"attn_fwd": case_attn_fwd, "ce": case_ce, "attn_bwd": case_attn_bwd, "gemm": case_gemm, "gemm_swiglu": case_gemm_swiglu,
+def case_gemm_vs_cublas(warmup, iters):
+    """Every GEMM of one Qwen3-0.6B training step (forward x W^T, input
+    gradient g W, weight gradient g^T x for the five projections), this
+    repository's CTA-pair kernel with the plain bf16 store against cuBLAS
+    through torch.mm with the same operand layouts and a preallocated output."""
+    from .gemm import EPI_STORE_BF16
+
+    C = ext()
+    T, V = B * S, 151936
+    qkv = (NQ + 2 * NKV) * D
+    layers = {"qkv": (qkv, H), "o_proj": (H, NQ * D), "gate_up": (2 * I, H), "down": (H, I), "lm_head": (V, H)}
+    lines, tot = [], [0.0, 0.0, 0.0]
+    for name, (n_out, k_in) in layers.items():
+        w = (0.02 * torch.randn(n_out, k_in, device="cuda")).to(torch.bfloat16)
+        x = torch.randn(T, k_in, device="cuda", dtype=torch.bfloat16)
+        g = torch.randn(T, n_out, device="cuda", dtype=torch.bfloat16)
+        for kind, (M, N, K), ours, ref in (
+                ("fwd", (T, n_out, k_in), lambda o: C.gemm(x, w, o, False, False, EPI_STORE_BF16, 1.0),
+                 lambda o: torch.mm(x, w.t(), out=o)),
+                ("dgrad", (T, k_in, n_out), lambda o: C.gemm(g, w, o, False, True, EPI_STORE_BF16, 1.0),
+                 lambda o: torch.mm(g, w, out=o)),
+                ("wgrad", (n_out, k_in, T), lambda o: C.gemm(g, x, o, True, True, EPI_STORE_BF16, 1.0),
+                 lambda o: torch.mm(g.t(), x, out=o))):
+            out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            t_ours = _time(lambda: ours(out), warmup, iters)
+            t_ref = _time(lambda: ref(out), warmup, iters)
+            tf = 2 * M * N * K / 1e6
+            lines.append(f"{name:8s} {kind:5s} {M}x{N}x{K}: ours {t_ours:8.1f} us ({tf / t_ours:5.0f} TF/s)  "
+                         f"cuBLAS {t_ref:8.1f} us ({tf / t_ref:5.0f} TF/s)  ratio {t_ref / t_ours:.2f}")
+            tot[0] += t_ours * (28 if name != "lm_head" else 1)
+            tot[1] += t_ref * (28 if name != "lm_head" else 1)
+        del w, x, g
+    lines.append(f"one step (28 layers + LM head): ours {tot[0] / 1e3:.2f} ms, cuBLAS {tot[1] / 1e3:.2f} ms")
+    return "\n".join(lines)
+
+
+CASES = {"attn_fwd": case_attn_fwd, "ce": case_ce, "gemm_vs_cublas": case_gemm_vs_cublas, "attn_bwd": case_attn_bwd, "gemm": case_gemm, "gemm_swiglu": case_gemm_swiglu,
          "gemm_residual": case_gemm_residual, "rmsnorm_bwd": case_rmsnorm_bwd, "qknorm": case_qknorm,
          "qknorm_bwd": case_qknorm_bwd, "wgrad_split": case_wgrad_split}
 
