@@ -55,7 +55,10 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, 
     p.N = (int)n_out;
     TORCH_CHECK(b_up_offset + n_out <= b.size(0), "gemm: swiglu B too small");
   }
-  TORCH_CHECK(out.size(0) == p.M && out.size(1) == p.N, "gemm: output shape mismatch");
+  // split-K into fp32 slabs: out is [splits * M, N], slab s = rows [s * M, (s + 1) * M)
+  const int64_t out_rows = (epi == pb::kEpiStoreF32 && splits > 1) ? (int64_t)p.M * splits : p.M;
+  TORCH_CHECK(out.size(0) == out_rows && out.size(1) == p.N, "gemm: output shape mismatch");
+  TORCH_CHECK(out_rows == p.M || out.stride(0) == p.N, "gemm: fp32 slabs must be contiguous [splits * M, N]");
   if (epi == pb::kEpiSplitOrdered) {
     // ws: fp32 [M, >= N] running sums of the K slices (contents irrelevant);
     // out: bf16 or fp32, written (or added to, accumulate) by the last slice

@@ -16,7 +16,8 @@ namespace pb {
 enum GemmEpilogue : int {
   kEpiStoreBf16 = 0,      // C(bf16) = alpha*acc
   kEpiResidualBf16 = 1,   // C(bf16) = alpha*acc + R(bf16)
-  kEpiStoreF32 = 2,       // C(f32)  = alpha*acc
+  kEpiStoreF32 = 2,       // C(f32)  = alpha*acc; with splits > 1, K slice s writes slab s of
+                          // C [splits, M, ldc] (fp32 partials, summed afterwards in slice order)
   kEpiAccumBf16 = 3,      // C(bf16) += alpha*acc
   kEpiAccumF32 = 4,       // C(f32)  += alpha*acc
   kEpiSwiGLU = 5,         // B rows [0,N) are gate, [N,2N) are up (same ldb, "b_up_offset" rows

@@ -32,7 +32,10 @@ struct EpiArgs {
 // free of bank conflicts.
 constexpr int kEpiBox = 32;
 constexpr int kEpiBoxBytes = kEpiBox * kEpiBox * 2;
-constexpr int kEpiWarpBytes = 3 * kEpiBoxBytes;
+// (8 KB: the SwiGLU epilogue's three bf16 boxes, or two 32 x 32 fp32 boxes)
+constexpr int kEpiWarpBytes = 8192;
+constexpr int kEpiBoxF32Bytes = kEpiBox * kEpiBox * 4;
+static_assert(3 * kEpiBoxBytes <= kEpiWarpBytes && 2 * kEpiBoxF32Bytes <= kEpiWarpBytes, "epilogue staging");
 
 // Output row pointer of row m for the bf16 store epilogue.
 __device__ __forceinline__ __nv_bfloat16* out_row_bf16(const EpiArgs& ep, int m) {
@@ -248,6 +251,46 @@ __device__ __forceinline__ void epilogue_warp_tma(const EpiArgs& ep, const CUten
         tma_store_2d(tmR, stage + 2 * kEpiBoxBytes, (int)ep.up_col + n0, y0);
       }
     }
+    if (lane == 0) bulk_commit_group();
+  }
+}
+
+// One row of a 32 x 32 fp32 box of 128-byte rows with the 128-byte swizzle:
+// 16-byte chunk q of row r sits at chunk q ^ (r & 7).
+__device__ __forceinline__ void stage_row_swz128_f32(uint8_t* box, int r, const float* v) {
+  uint8_t* row = box + r * 128;
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    *reinterpret_cast<float4*>(row + ((q ^ (r & 7)) << 4)) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+
+// fp32 store epilogue through TMA tile stores (ep.tma == 2): the tile of K
+// slice `slab` goes to slab `slab` of the [slabs, M, ldc] output (the split-K
+// partials that sum_slices adds in slice order; slab 0 of 1 otherwise).  The
+// tensor map's per-slab row bound keeps the rows past M of a partial tile out
+// of the next slab.
+template <int BN, typename Release>
+__device__ __forceinline__ void epilogue_warp_tma_f32(const EpiArgs& ep, const CUtensorMap* tmC, uint32_t t_row,
+                                                      uint8_t* stage, int lane, int y0, int M, int N, int n_base,
+                                                      int slab, Release release) {
+  const bool rows_in = y0 < M;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    float a[32];
+    tmem_ld32(t_row + c, a);
+    tmem_wait_ld();
+    if (c + 32 >= BN) release();
+    const int n0 = n_base + c;
+    const bool store = rows_in && n0 < N;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) a[j] *= ep.alpha;
+    uint8_t* box = stage + ((c >> 5) & 1) * kEpiBoxF32Bytes;
+    if (lane == 0) bulk_wait_group_read<1>();
+    __syncwarp();
+    if (store) stage_row_swz128_f32(box, lane, a);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && store) tma_store_3d(tmC, box, n0, y0, slab);
     if (lane == 0) bulk_commit_group();
   }
 }

@@ -386,6 +386,12 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
         tc_fence_before();
         mbar_arrive_cluster(tempty);
         if (splits > 1) split_publish(cnt, sl, sl == splits - 1, lane);
+      } else if (ep.tma == 2) {
+        gemm_detail::epilogue_warp_tma_f32<BN>(ep, &tmC, t_row, stage, lane, m - lane, M, N, tn * BN_OUT,
+                                               w / num_tiles, [&] {
+                                                 tc_fence_before();
+                                                 mbar_arrive_cluster(tempty);
+                                               });
       } else if (ep.tma) {
         gemm_detail::epilogue_warp_tma<BN, SWIGLU>(ep, &tmC, &tmR, t_row, stage, lane, m - lane, M, N, tn * BN_OUT,
                                                    [&] {
@@ -487,6 +493,16 @@ void launch_pair(const GemmParams& p, cudaStream_t stream) {
                                  64);
     ep.tma = 1;
   }
+  // fp32 store through TMA (and split-K into per-slice slabs [splits, M, ldc])
+  if (!SWIGLU && !GATHER && !p.scatter && p.epi == kEpiStoreF32 && p.C &&
+      (reinterpret_cast<uintptr_t>(p.C) & 15) == 0 && (p.ldc * 4) % 16 == 0) {
+    const int slabs = std::max(1, p.splits);
+    tc = make_tmap_3d_f32(p.C, p.N, p.M, slabs, p.ldc, (uint64_t)p.M * p.ldc, gemm_detail::kEpiBox,
+                          gemm_detail::kEpiBox, 1, true);
+    ep.tma = 2;
+  }
+  PB_CHECK(p.splits <= 1 || p.epi != kEpiStoreF32 || ep.tma == 2,
+           "gemm: split-K into fp32 slabs needs a 16-byte aligned output with a 16-byte row stride");
   GatherArgs ga{};
   if (GATHER) ga = *p.gather;
   const int bn_out = SWIGLU ? BN / 2 : BN;
@@ -514,8 +530,9 @@ void gemm_bf16_pair(const GemmParams& p, cudaStream_t stream) {
     return launch_pair<256, false, true, false, true>(p, stream);
   }
   if (p.scatter) PB_CHECK(p.epi == kEpiStoreBf16 && p.scatter->nranks <= 8, "gemm: scatter needs the bf16 store epilogue");
-  PB_CHECK(p.splits <= 1 || ((p.epi == kEpiAtomicF32 || p.epi == kEpiSplitOrdered) && !p.gather && !p.scatter),
-           "gemm: split-K needs the atomic or the ordered epilogue");
+  PB_CHECK(p.splits <= 1 || ((p.epi == kEpiAtomicF32 || p.epi == kEpiSplitOrdered || p.epi == kEpiStoreF32) &&
+                               !p.gather && !p.scatter),
+           "gemm: split-K needs the atomic, the ordered or the fp32 slab epilogue");
   if (p.epi == kEpiSwiGLU) return launch_pair<256, false, false, true>(p, stream);
   if (!p.a_mn && !p.b_mn) return launch_pair<256, false, false, false>(p, stream);
   if (!p.a_mn && p.b_mn) return launch_pair<256, false, true, false>(p, stream);

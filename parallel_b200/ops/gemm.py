@@ -25,16 +25,18 @@ EPI_SWIGLU = 5
 EPI_ATOMIC_F32 = 6
 EPI_SPLIT_ORDERED = 7
 
-# Split-K for long-K products with very few CTA-pair tiles (the weight
-# gradients reduce over all tokens).  The ordered split-K costs a running-sum
-# round trip per extra slice and serialises the slices' epilogues, which the
-# wave arithmetic does not see: measured on B200 at the Qwen3-0.6B step
-# shapes (T = 8192), one slice beats the split for every weight gradient
-# (o_proj 1024x2048: 48.3 vs 49.7 us with 2 slices; gate/up 6144x1024: 89.1 vs
-# 112.4 us with 3; down 1024x3072: 47.8 vs 78.2 us with 3).  So a product is
-# split only when its tiles fill at most a quarter of the SM pairs, where one
-# slice would leave three quarters of the GPU idle.
+# Split-K for long-K products with few CTA-pair tiles (the weight gradients
+# reduce over all tokens).  Each K slice writes its fp32 partial tile into its
+# own slab with TMA tile stores and one pass adds the slabs in slice order (no
+# waits between slices, no atomics, the same bits on every run).  The slice
+# count minimises a wave model: ceil(tiles * s / pairs) / s waves of the unsplit
+# tile time, plus the slab round trip (write and read of s fp32 partials).
+# Measured on B200 at T = 8192, the o_proj weight gradient (1024 x 2048, 32
+# tiles on 74 SM pairs) is the step's product that gains; the ordered split-K
+# (each slice waiting for the previous one's running sum) lost on every shape.
 _SPLITK_MIN_K = 2048
+_PAIR_TFLOPS = 22e12    # one SM pair's bf16 rate inside a long-K tile (measured ~0.7 of peak)
+_SLAB_BYTES_PER_S = 5e12
 
 
 def _pair_slots() -> int:
@@ -49,11 +51,16 @@ def _splitk(M: int, N: int, K: int, slots: int | None = None) -> int:
         return 1
     slots = slots or _pair_slots()
     tiles = ((M + 255) // 256) * ((N + 255) // 256)
-    if 4 * tiles > slots:
-        return 1
+    t_tile = 2.0 * 256 * 256 * K / _PAIR_TFLOPS
+
+    def cost(s):
+        waves = -(-tiles * s // slots) / s
+        slab = 0.0 if s == 1 else 2.0 * s * M * N * 4 / _SLAB_BYTES_PER_S
+        return waves * t_tile + slab
+
     best = 1
     for s in (2, 3, 4):
-        if K // s >= _SPLITK_MIN_K and tiles * s <= slots:
+        if K // s >= _SPLITK_MIN_K and cost(s) < 0.9 * cost(best):
             best = s
     return best
 
@@ -143,13 +150,13 @@ def linear_wgrad(g: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = No
         accumulate = False
     M, N, K = g2.shape[1], x2.shape[1], g2.shape[0]
     splits = _splitk(M, N, K)
-    if splits > 1:
-        # split-K over the tokens: slice s adds its product to the fp32 running
-        # sum of slices < s inside the GEMM and the last slice writes out (bf16
-        # or fp32, optionally accumulating): no zero fill, no atomics, no
-        # separate cast, and the same bits on every run
-        ws = torch.empty(M, N, dtype=torch.float32, device=g.device)
-        ext().gemm(g2, x2, out, True, True, EPI_SPLIT_ORDERED, 1.0, splits=splits, ws=ws, accumulate=accumulate)
+    if splits > 1 and out.is_contiguous():
+        # split-K over the tokens: slice s stores its fp32 partial in slab s,
+        # then the slabs are added in slice order into out (bf16 or fp32,
+        # optionally accumulating)
+        slabs = torch.empty(splits * M, N, dtype=torch.float32, device=g.device)
+        ext().gemm(g2, x2, slabs, True, True, EPI_STORE_F32, 1.0, splits=splits)
+        ext().sum_slices(slabs.view(splits, M * N), out.view(-1), accumulate)
         return out
     if out.dtype == torch.float32:
         epi = EPI_ACCUM_F32 if accumulate else EPI_STORE_F32

@@ -147,7 +147,7 @@ def case_wgrad_split(warmup, iters):
     """Weight-gradient GEMMs dW[M, N] = g^T x over T = B * S tokens at the
     0.6B step's split-K shapes: one K slice, split-K with fp32 atomics (zero
     fill + GEMM + cast) and the ordered split-K epilogue."""
-    from .gemm import EPI_ATOMIC_F32, EPI_SPLIT_ORDERED, EPI_STORE_BF16, _splitk
+    from .gemm import EPI_ATOMIC_F32, EPI_SPLIT_ORDERED, EPI_STORE_BF16, EPI_STORE_F32, _splitk
 
     C = ext()
     T = B * S
@@ -167,9 +167,17 @@ def case_wgrad_split(warmup, iters):
 
         ta = _time(atomic, warmup, iters)
         to = _time(lambda: C.gemm(g, x, out, True, True, EPI_SPLIT_ORDERED, 1.0, splits=sp, ws=ws), warmup, iters)
+        slabs = torch.empty(sp * M, N, device="cuda", dtype=torch.float32)
+
+        def slab():
+            C.gemm(g, x, slabs, True, True, EPI_STORE_F32, 1.0, splits=sp)
+            C.sum_slices(slabs.view(sp, M * N), out.view(-1), False)
+
+        tsl = _time(slab, warmup, iters)
         tf = 2 * M * N * T / 1e6
         lines.append(f"wgrad {name} {M}x{N}x{T}: 1 slice {t1:.1f} us ({tf / t1:.0f} TF/s), {sp} slices atomic+fill+cast "
-                     f"{ta:.1f} us, {sp} slices ordered {to:.1f} us ({tf / to:.0f} TF/s); policy picks {_splitk(M, N, T)}")
+                     f"{ta:.1f} us, {sp} slices ordered {to:.1f} us ({tf / to:.0f} TF/s), {sp} fp32 slabs + sum "
+                     f"{tsl:.1f} us ({tf / tsl:.0f} TF/s); policy picks {_splitk(M, N, T)}")
     return "\n".join(lines)
 
 
