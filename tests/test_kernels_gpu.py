@@ -591,7 +591,7 @@ def test_aux_loss_stats_match_torch():
     _check_no_device_error()
 
 
-@pytest.mark.parametrize("M,N,K,splits", [(1024, 2048, 8192, 2), (300, 200, 8192, 3), (512, 1024, 16384, 4)])
+@pytest.mark.parametrize("M,N,K,splits", [(1024, 2048, 8192, 2), (296, 200, 8192, 3), (512, 1024, 16384, 4)])
 def test_gemm_splitk_fp32_slabs(M, N, K, splits):
     """Split-K into per-slice fp32 slabs (TMA tile stores) and the slice-order
     sum: matches fp32, partial tiles stay inside their own slab, and the result
