@@ -147,7 +147,7 @@ def case_wgrad_split(warmup, iters):
     """Weight-gradient GEMMs dW[M, N] = g^T x over T = B * S tokens at the
     0.6B step's split-K shapes: one K slice, split-K with fp32 atomics (zero
     fill + GEMM + cast) and the ordered split-K epilogue."""
-    from .gemm import EPI_ATOMIC_F32, EPI_SPLIT_ORDERED, EPI_STORE_BF16, EPI_STORE_F32, _splitk
+    from .gemm import EPI_ATOMIC_F32, EPI_SPLIT_ORDERED, EPI_STORE_BF16, EPI_STORE_F32
 
     C = ext()
     T = B * S
@@ -157,7 +157,7 @@ def case_wgrad_split(warmup, iters):
         x = torch.randn(T, N, device="cuda", dtype=torch.bfloat16)
         out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
         ws = torch.empty(M, N, device="cuda", dtype=torch.float32)
-        sp = max(2, _splitk(M, N, T))
+        sp = 2
         t1 = _time(lambda: C.gemm(g, x, out, True, True, EPI_STORE_BF16, 1.0), warmup, iters)
 
         def atomic():
@@ -174,10 +174,12 @@ def case_wgrad_split(warmup, iters):
             C.sum_slices(slabs.view(sp, M * N), out.view(-1), False)
 
         tsl = _time(slab, warmup, iters)
+        sk_ws = torch.empty(C.gemm_streamk_ws_floats(), device="cuda")
+        tsk = _time(lambda: C.gemm(g, x, out, True, True, EPI_STORE_BF16, 1.0, streamk_ws=sk_ws), warmup, iters)
         tf = 2 * M * N * T / 1e6
         lines.append(f"wgrad {name} {M}x{N}x{T}: 1 slice {t1:.1f} us ({tf / t1:.0f} TF/s), {sp} slices atomic+fill+cast "
                      f"{ta:.1f} us, {sp} slices ordered {to:.1f} us ({tf / to:.0f} TF/s), {sp} fp32 slabs + sum "
-                     f"{tsl:.1f} us ({tf / tsl:.0f} TF/s); policy picks {_splitk(M, N, T)}")
+                     f"{tsl:.1f} us ({tf / tsl:.0f} TF/s), stream-K launch {tsk:.1f} us ({tf / tsk:.0f} TF/s)")
     return "\n".join(lines)
 
 
@@ -201,9 +203,8 @@ def case_gemm_vs_cublas(warmup, iters):
     gradient g W, weight gradient g^T x for the five projections), this
     repository's CTA-pair kernel with the plain bf16 store against cuBLAS
     through torch.mm with the same operand layouts and a preallocated output."""
-    from .gemm import EPI_STORE_BF16
+    from . import gemm as G
 
-    C = ext()
     T, V = B * S, 151936
     qkv = (NQ + 2 * NKV) * D
     layers = {"qkv": (qkv, H), "o_proj": (H, NQ * D), "gate_up": (2 * I, H), "down": (H, I), "lm_head": (V, H)}
@@ -212,12 +213,12 @@ def case_gemm_vs_cublas(warmup, iters):
         w = (0.02 * torch.randn(n_out, k_in, device="cuda")).to(torch.bfloat16)
         x = torch.randn(T, k_in, device="cuda", dtype=torch.bfloat16)
         g = torch.randn(T, n_out, device="cuda", dtype=torch.bfloat16)
+        # ours: the entry points the training step calls (they pick the tile
+        # schedule: whole tiles, or stream-K for few-tile long-K products)
         for kind, (M, N, K), ours, ref in (
-                ("fwd", (T, n_out, k_in), lambda o: C.gemm(x, w, o, False, False, EPI_STORE_BF16, 1.0),
-                 lambda o: torch.mm(x, w.t(), out=o)),
-                ("dgrad", (T, k_in, n_out), lambda o: C.gemm(g, w, o, False, True, EPI_STORE_BF16, 1.0),
-                 lambda o: torch.mm(g, w, out=o)),
-                ("wgrad", (n_out, k_in, T), lambda o: C.gemm(g, x, o, True, True, EPI_STORE_BF16, 1.0),
+                ("fwd", (T, n_out, k_in), lambda o: G.linear(x, w, out=o), lambda o: torch.mm(x, w.t(), out=o)),
+                ("dgrad", (T, k_in, n_out), lambda o: G.linear_dgrad(g, w, out=o), lambda o: torch.mm(g, w, out=o)),
+                ("wgrad", (n_out, k_in, T), lambda o: G.linear_wgrad(g, x, out=o),
                  lambda o: torch.mm(g.t(), x, out=o))):
             out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
             t_ours = _time(lambda: ours(out), warmup, iters)
@@ -232,7 +233,33 @@ def case_gemm_vs_cublas(warmup, iters):
     return "\n".join(lines)
 
 
-CASES = {"attn_fwd": case_attn_fwd, "ce": case_ce, "gemm_vs_cublas": case_gemm_vs_cublas, "attn_bwd": case_attn_bwd, "gemm": case_gemm, "gemm_swiglu": case_gemm_swiglu,
+def _oproj_wgrad_operands():
+    T = B * S
+    g = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    x = torch.randn(T, NQ * D, device="cuda", dtype=torch.bfloat16)
+    return g, x, torch.empty(H, NQ * D, device="cuda", dtype=torch.bfloat16)
+
+
+def case_wgrad_oproj(warmup, iters):
+    """The o_proj weight gradient (1024 x 2048 x 8192), one K slice, plain bf16
+    store: the small case for profiler captures of the weight-gradient GEMM."""
+    from .gemm import EPI_STORE_BF16
+
+    C = ext()
+    g, x, out = _oproj_wgrad_operands()
+    us = _time(lambda: C.gemm(g, x, out, True, True, EPI_STORE_BF16, 1.0), warmup, iters)
+    return f"wgrad o_proj one slice: {us:.1f} us, {2 * out.numel() * g.shape[0] / us / 1e6:.0f} TF/s"
+
+
+def case_wgrad_oproj_cublas(warmup, iters):
+    """The same product through cuBLAS (torch.mm with the same layouts)."""
+    g, x, out = _oproj_wgrad_operands()
+    us = _time(lambda: torch.mm(g.t(), x, out=out), warmup, iters)
+    return f"wgrad o_proj cuBLAS: {us:.1f} us, {2 * out.numel() * g.shape[0] / us / 1e6:.0f} TF/s"
+
+
+CASES = {"attn_fwd": case_attn_fwd, "ce": case_ce, "gemm_vs_cublas": case_gemm_vs_cublas,
+         "wgrad_oproj": case_wgrad_oproj, "wgrad_oproj_cublas": case_wgrad_oproj_cublas, "attn_bwd": case_attn_bwd, "gemm": case_gemm, "gemm_swiglu": case_gemm_swiglu,
          "gemm_residual": case_gemm_residual, "rmsnorm_bwd": case_rmsnorm_bwd, "qknorm": case_qknorm,
          "qknorm_bwd": case_qknorm_bwd, "wgrad_split": case_wgrad_split}
 
