@@ -23,8 +23,7 @@ cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 //   out: [M, N] bf16 or fp32 depending on epi
 void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, bool b_mn, int64_t epi,
           double alpha, const c10::optional<at::Tensor>& r, int64_t b_up_offset, int64_t n_out, int64_t kernel,
-          int64_t splits, const c10::optional<at::Tensor>& ws, bool accumulate,
-          const c10::optional<at::Tensor>& streamk_ws) {
+          int64_t splits, const c10::optional<at::Tensor>& ws, bool accumulate) {
   CHECK_CUDA_BF16(a);
   CHECK_CUDA_BF16(b);
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm: 2-D operands expected");
@@ -84,14 +83,6 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, 
     TORCH_CHECK(epi != pb::kEpiResidualBf16, "gemm: residual epilogue needs r");
     p.R = nullptr;
     p.ldr = 0;
-  }
-  if (streamk_ws.has_value() && streamk_ws->defined()) {
-    // fp32 scratch of at least gemm_streamk_ws_floats(); the launcher uses it
-    // only where an even split of the k-blocks over the SM pairs pays off
-    TORCH_CHECK(streamk_ws->is_cuda() && streamk_ws->scalar_type() == at::kFloat && streamk_ws->is_contiguous(),
-                "gemm: streamk_ws must be contiguous fp32 CUDA memory");
-    p.streamk_ws = streamk_ws->data_ptr<float>();
-    p.streamk_ws_floats = streamk_ws->numel();
   }
   pb::gemm_bf16(p, cur_stream());
 }
@@ -290,10 +281,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("b"), pybind11::arg("out"), pybind11::arg("a_mn"), pybind11::arg("b_mn"),
         pybind11::arg("epi"), pybind11::arg("alpha"), pybind11::arg("r") = pybind11::none(),
         pybind11::arg("b_up_offset") = 0, pybind11::arg("n_out") = 0, pybind11::arg("kernel") = 0,
-        pybind11::arg("splits") = 1, pybind11::arg("ws") = pybind11::none(), pybind11::arg("accumulate") = false,
-        pybind11::arg("streamk_ws") = pybind11::none());
-  m.def("gemm_streamk_ws_floats", &pb::gemm_streamk_ws_floats,
-        "fp32 elements of the scratch a stream-K GEMM launch may use");
+        pybind11::arg("splits") = 1, pybind11::arg("ws") = pybind11::none(), pybind11::arg("accumulate") = false);
   m.def("gemm_ag", &gemm_ag, "GEMM with the sequence-parallel all-gather of A in the same kernel",
         pybind11::arg("dst"), pybind11::arg("src_ptrs"), pybind11::arg("src_ld"), pybind11::arg("flags"),
         pybind11::arg("target"), pybind11::arg("seq"), pybind11::arg("seq_local"), pybind11::arg("batch"),

@@ -79,16 +79,7 @@ struct GemmParams {
   bool accumulate = false;  // kEpiSplitOrdered: C += result
   const ScatterArgs* scatter = nullptr;  // kEpiStoreBf16 rows to their sequence-parallel owners
   const GatherArgs* gather = nullptr;    // A assembled from sequence-parallel shards in-kernel
-  // Stream-K workspace (fp32, >= gemm_streamk_ws_floats()): when set, the
-  // launcher may split the (tile, k-block) units evenly over the SM pairs
-  // (kEpiStoreBf16 / kEpiStoreF32 / kEpiAccum*, no gather / scatter / split-K)
-  // where whole tiles would leave many pairs idle; pieces of shared tiles are
-  // summed in K order by a fix-up kernel, so every run gives the same bits.
-  float* streamk_ws = nullptr;
-  int64_t streamk_ws_floats = 0;
 };
-// fp32 workspace a stream-K launch may use: two 256 x 256 tiles per SM pair
-int64_t gemm_streamk_ws_floats();
 
 // Grouped (mixture-of-experts) products, gemm_grouped.cu.  work: int4 per
 // tile {expert, M tile, N tile, 0}; rows of one expert start at a 128-row

@@ -285,14 +285,7 @@ __device__ __forceinline__ void epilogue_warp_tma_f32(const EpiArgs& ep, const C
 #pragma unroll
     for (int j = 0; j < 32; ++j) a[j] *= ep.alpha;
     uint8_t* box = stage + ((c >> 5) & 1) * kEpiBoxF32Bytes;
-    // the first chunk waits for every earlier store of this warp: the previous
-    // item may have staged bf16 boxes that overlap these fp32 ones
-    if (lane == 0) {
-      if (c == 0)
-        bulk_wait_group_read<0>();
-      else
-        bulk_wait_group_read<1>();
-    }
+    if (lane == 0) bulk_wait_group_read<1>();
     __syncwarp();
     if (store) stage_row_swz128_f32(box, lane, a);
     fence_proxy_async_smem();

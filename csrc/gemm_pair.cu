@@ -21,7 +21,6 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
-#include <cmath>
 #include <mutex>
 
 #include "gemm.cuh"
@@ -175,47 +174,6 @@ __device__ __forceinline__ void split_publish(int* cnt, int sl, bool last, int l
   }
 }
 
-// Work items of one CTA pair, walked identically by the producer, the MMA
-// issuer and the epilogue warps.
-//   regular:  w = cid, cid + nc, ... < num_tiles * splits; tile = w % num_tiles,
-//             K slice w / num_tiles (tag = the slice).
-//   stream-K: the pair owns the units [b(cid), b(cid + 1)) of the
-//             num_tiles * num_kb (tile, 64-deep k-block) units, b(c) = c * U / nc,
-//             in order; an item is the part of one tile inside that range.  A
-//             whole tile gets tag -1 (normal epilogue); a piece of a tile gets
-//             the workspace slot 2 * cid (the pair's first item) or 2 * cid + 1
-//             (its last), where its fp32 partial goes for streamk_fixup_kernel.
-struct WorkIter {
-  int num_tiles, num_kb, kb_per, num_work, nc, cid, sk, w;
-  int64_t u, u0, u1;
-  __device__ WorkIter(int num_tiles_, int num_kb_, int splits, int nc_, int cid_, int sk_)
-      : num_tiles(num_tiles_), num_kb(num_kb_), kb_per((num_kb_ + splits - 1) / splits),
-        num_work(num_tiles_ * splits), nc(nc_), cid(cid_), sk(sk_), w(cid_) {
-    const int64_t U = (int64_t)num_tiles_ * num_kb_;
-    u0 = u = (int64_t)cid_ * U / nc_;
-    u1 = (int64_t)(cid_ + 1) * U / nc_;
-  }
-  __device__ bool next(int& tile, int& kb0, int& kb1, int& tag) {
-    if (!sk) {
-      if (w >= num_work) return false;
-      tile = w % num_tiles;
-      tag = w / num_tiles;
-      kb0 = tag * kb_per;
-      kb1 = min(num_kb, kb0 + kb_per);
-      w += nc;
-      return true;
-    }
-    if (u >= u1) return false;
-    tile = (int)(u / num_kb);
-    kb0 = (int)(u % num_kb);
-    const int64_t left = u1 - u;
-    kb1 = left < (int64_t)(num_kb - kb0) ? kb0 + (int)left : num_kb;
-    tag = (kb0 == 0 && kb1 == num_kb) ? -1 : 2 * cid + (u == u0 ? 0 : 1);
-    u += kb1 - kb0;
-    return true;
-  }
-};
-
 // Copy warps of the gather variant: piece q of the pieces_per_block pieces of
 // block `blk` (kGatherRowsPerPiece rows of K elements, contiguous in both the
 // source shard and the gathered buffer), then publish it on flags[blk].
@@ -254,8 +212,7 @@ template <int BN, bool A_MN, bool B_MN, bool SWIGLU, bool GATHER>
 __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiArgs ep,
                      int M, int N, int K, int b_up_row, int* err, const __grid_constant__ GatherArgs ga,
-                     int splits, const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR,
-                     int streamk, const __grid_constant__ CUtensorMap tmW) {
+                     int splits, const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR) {
   pdl_prologue();
   using Cfg = PairCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
@@ -309,6 +266,9 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
   const int tiles_n = (N + BN_OUT - 1) / BN_OUT;
   const int num_tiles = tiles_m * tiles_n;
   const int num_kb = (K + BK - 1) / BK;
+  // work item w = (tile, K slice): tile = w % num_tiles, slice = w / num_tiles
+  const int kb_per = (num_kb + splits - 1) / splits;
+  const int num_work = num_tiles * splits;
   const int n_clusters = gridDim.x >> 1;
   const int cid = blockIdx.x >> 1;
 
@@ -317,9 +277,9 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      WorkIter it(num_tiles, num_kb, splits, n_clusters, cid, streamk);
-      int tile, kb0, kb1, tag;
-      while (ok && it.next(tile, kb0, kb1, tag)) {
+      for (int w = cid; w < num_work && ok; w += n_clusters) {
+        const int tile = w % num_tiles;
+        const int kb0 = (w / num_tiles) * kb_per, kb1 = min(num_kb, kb0 + kb_per);
         const int tm = GATHER ? ga.m_order[tile % tiles_m] : tile % tiles_m, tn = tile / tiles_m;
         const int a_row = tm * 2 * BM_CTA + (int)rank * BM_CTA;
         if constexpr (GATHER) {
@@ -371,9 +331,8 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      WorkIter it(num_tiles, num_kb, splits, n_clusters, cid, streamk);
-      int tile, kb0, kb1, tag;
-      for (; ok && it.next(tile, kb0, kb1, tag); ++local) {
+      for (int w = cid; w < num_work && ok; w += n_clusters, ++local) {
+        const int kb0 = (w / num_tiles) * kb_per, kb1 = min(num_kb, kb0 + kb_per);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, err)) break;
@@ -409,9 +368,8 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
     const int row = quarter * 32 + lane;
     uint8_t* stage = sEpi + quarter * gemm_detail::kEpiWarpBytes;
     int local = 0;
-    WorkIter it(num_tiles, num_kb, splits, n_clusters, cid, streamk);
-    int tile, kb0, kb1, tag;
-    for (; it.next(tile, kb0, kb1, tag); ++local) {
+    for (int w = cid; w < num_work; w += n_clusters, ++local) {
+      const int tile = w % num_tiles;
       const int tm = GATHER ? ga.m_order[tile % tiles_m] : tile % tiles_m, tn = tile / tiles_m;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
@@ -420,16 +378,8 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
       const int m = tm * 2 * BM_CTA + (int)rank * BM_CTA + row;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       const uint32_t tempty = mapa_shared(smem_u32(&tempty_bar[acc]), 0);
-      if (streamk && tag >= 0) {
-        // a piece of a tile shared with other pairs: its fp32 partial goes to
-        // workspace slot `tag` (rows / columns local to the 256 x 256 tile)
-        gemm_detail::epilogue_warp_tma_f32<BN>(ep, &tmW, t_row, stage, lane, (int)rank * BM_CTA + quarter * 32,
-                                               2 * BM_CTA, BN, 0, tag, [&] {
-                                                 tc_fence_before();
-                                                 mbar_arrive_cluster(tempty);
-                                               });
-      } else if (ep.epi == kEpiSplitOrdered) {
-        const int sl = tag;
+      if (ep.epi == kEpiSplitOrdered) {
+        const int sl = w / num_tiles;
         int* cnt = ep.cnt + 2 * tile + (int)rank;
         const bool ok = split_wait(cnt, 4 * sl, err);
         epilogue_split<BN>(ep, t_row, m, M, N, tn * BN_OUT, sl == 0, sl == splits - 1, ok);
@@ -438,7 +388,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
         if (splits > 1) split_publish(cnt, sl, sl == splits - 1, lane);
       } else if (ep.tma == 2) {
         gemm_detail::epilogue_warp_tma_f32<BN>(ep, &tmC, t_row, stage, lane, m - lane, M, N, tn * BN_OUT,
-                                               tag < 0 ? 0 : tag, [&] {
+                                               w / num_tiles, [&] {
                                                  tc_fence_before();
                                                  mbar_arrive_cluster(tempty);
                                                });
@@ -455,7 +405,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
       }
     }
     // the tile stores must have finished before the kernel's shared memory goes
-    if ((ep.tma || streamk) && lane == 0) bulk_wait_group<0>();
+    if (ep.tma && lane == 0) bulk_wait_group<0>();
   }
 
   // On an error path the MMA issuer may have left MMAs in flight: drain them
@@ -473,67 +423,6 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 64 : kThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
   }
-}
-
-// Stream-K fix-up: one block per output tile.  A tile whose k-blocks lie in the
-// ranges of several pairs (first owner c0 .. last owner c1) is the sum of their
-// fp32 pieces, taken in K order: the piece of pair c sits in workspace slot
-// 2c when pair c's range starts inside this tile (its first item) and 2c + 1
-// otherwise (its last item).  Whole tiles were written by the GEMM.
-__device__ __forceinline__ int64_t sk_bound(int c, int64_t U, int nc) { return (int64_t)c * U / nc; }
-
-__device__ __forceinline__ int sk_owner(int64_t u, int64_t U, int nc) {
-  int c = (int)(u * nc / U);
-  while (c + 1 < nc && sk_bound(c + 1, U, nc) <= u) ++c;
-  while (c > 0 && sk_bound(c, U, nc) > u) --c;
-  return c;
-}
-
-__global__ void __launch_bounds__(256) streamk_fixup_kernel(const float* __restrict__ ws, void* __restrict__ C,
-                                                            int64_t ldc, int M, int N, int tiles_m, int num_tiles,
-                                                            int num_kb, int nc, int epi) {
-  pdl_prologue();
-  const int tile = blockIdx.x;
-  const int64_t U = (int64_t)num_tiles * num_kb;
-  const int64_t t0 = (int64_t)tile * num_kb;
-  const int c0 = sk_owner(t0, U, nc), c1 = sk_owner(t0 + num_kb - 1, U, nc);
-  if (c0 == c1) return;
-  const int tm = tile % tiles_m, tn = tile / tiles_m;
-  for (int idx = threadIdx.x; idx < 256 * 64; idx += blockDim.x) {
-    const int r = idx >> 6, col = (idx & 63) * 4;
-    const int m = tm * 256 + r, n = tn * 256 + col;
-    if (m >= M || n >= N) continue;
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int c = c0; c <= c1; ++c) {
-      const int slot = sk_bound(c, U, nc) >= t0 ? 2 * c : 2 * c + 1;
-      const float4 v = __ldcs(reinterpret_cast<const float4*>(ws + ((int64_t)slot * 256 + r) * 256 + col));
-      a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
-    }
-    const float o[4] = {a.x, a.y, a.z, a.w};
-    if (epi == kEpiStoreF32 || epi == kEpiAccumF32) {
-      float* dst = reinterpret_cast<float*>(C) + (int64_t)m * ldc + n;
-      for (int j = 0; j < 4 && n + j < N; ++j) dst[j] = (epi == kEpiAccumF32 ? dst[j] : 0.f) + o[j];
-    } else {
-      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)m * ldc + n;
-      for (int j = 0; j < 4 && n + j < N; ++j)
-        dst[j] = __float2bfloat16((epi == kEpiAccumBf16 ? __bfloat162float(dst[j]) : 0.f) + o[j]);
-    }
-  }
-}
-
-// Stream-K pays off when whole tiles leave many SM pairs idle in the last wave
-// and the pieces are long: modelled time (waves of the unsplit tile time, at a
-// measured ~0.7 of the tensor peak per pair) against the even split plus the
-// fix-up traffic (the shared tiles' fp32 pieces written and read back).
-bool streamk_worth_it(int num_tiles, int num_kb, int clusters) {
-  if (num_kb < 32 || num_tiles >= 4 * clusters) return false;
-  const double t_tile = 2.0 * 256 * 256 * 64 * num_kb / 22e12;
-  const double waves = (double)num_tiles / clusters;
-  const double t_reg = std::ceil(waves) * t_tile;
-  const double shared_tiles = std::min<double>(num_tiles, clusters);
-  const double pieces = 1.0 + std::max(1.0, (double)clusters / num_tiles);
-  const double t_fix = 3e-6 + shared_tiles * pieces * 256.0 * 256 * 4 * 2 / 8e12;
-  return waves * t_tile + t_fix < 0.92 * t_reg;
 }
 
 template <int BN, bool A_MN, bool B_MN, bool SWIGLU, bool GATHER = false>
@@ -620,36 +509,14 @@ void launch_pair(const GemmParams& p, cudaStream_t stream) {
   const int tiles = ((p.M + 2 * BM_CTA - 1) / (2 * BM_CTA)) * ((p.N + bn_out - 1) / bn_out) * std::max(1, p.splits);
   int clusters = max_clusters[dev & 63];
   if (p.max_ctas > 0) clusters = std::min(clusters, std::max(1, p.max_ctas / 2));
-  // stream-K: every pair gets an even share of the (tile, k-block) units
-  const int num_kb = (p.K + BK - 1) / BK;
-  const bool sk_epi = p.epi == kEpiStoreBf16 || p.epi == kEpiStoreF32 || p.epi == kEpiAccumBf16 ||
-                      p.epi == kEpiAccumF32;
-  int streamk = 0;
-  CUtensorMap tw{};
-  if (!SWIGLU && !GATHER && BN == 256 && p.streamk_ws && sk_epi && !p.scatter && p.splits <= 1 && !p.R &&
-      (int64_t)tiles * num_kb >= clusters && streamk_worth_it(tiles, num_kb, clusters) &&
-      p.streamk_ws_floats >= (int64_t)2 * clusters * 256 * 256 &&
-      (reinterpret_cast<uintptr_t>(p.streamk_ws) & 15) == 0) {
-    streamk = 1;
-    tw = make_tmap_3d_f32(p.streamk_ws, 256, 256, (uint64_t)2 * clusters, 256, 256 * 256, gemm_detail::kEpiBox,
-                          gemm_detail::kEpiBox, 1, true);
-  } else {
-    clusters = std::max(1, std::min(clusters, tiles));
-  }
+  clusters = std::max(1, std::min(clusters, tiles));
   cfg.gridDim = dim3(2 * clusters, 1, 1);
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   PB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, ep, p.M, p.N, p.K, (int)p.b_up_offset, error_word(dev), ga,
-                                   std::max(1, p.splits), tc, tr, streamk, tw));
-  if (streamk) {
-    const int tiles_m = (p.M + 2 * BM_CTA - 1) / (2 * BM_CTA);
-    launch_k(streamk_fixup_kernel, tiles, 256, 0, stream, p.streamk_ws, p.C, p.ldc, p.M, p.N, tiles_m, tiles,
-             num_kb, clusters, p.epi);
-  }
+                                   std::max(1, p.splits), tc, tr));
 }
 
 }  // namespace
-
-int64_t gemm_streamk_ws_floats() { return (int64_t)2 * (num_sms() / 2 + 1) * 256 * 256; }
 
 void gemm_bf16_pair(const GemmParams& p, cudaStream_t stream) {
   if (p.gather) {

@@ -25,22 +25,44 @@ EPI_SWIGLU = 5
 EPI_ATOMIC_F32 = 6
 EPI_SPLIT_ORDERED = 7
 
-# Long-K products with few output tiles (the weight gradients reduce over all
-# tokens) run stream-K where the launcher's model says it pays (an even share
-# of the 64-deep k-blocks per SM pair, the pieces of shared tiles summed in K
-# order by a fix-up kernel; csrc/gemm_pair.cu).  Measured on B200 at T = 8192
-# the ordered split-K (each K slice adding onto the previous slice's running
-# sum) lost on every weight gradient of the 0.6B step, and split-K into fp32
-# slabs helped only the o_proj weight gradient (49.8 -> 39.3 us).
+# Split-K for long-K products with few CTA-pair tiles (the weight gradients
+# reduce over all tokens).  Each K slice writes its fp32 partial tile into its
+# own slab with TMA tile stores and one pass adds the slabs in slice order (no
+# waits between slices, no atomics, the same bits on every run).  The slice
+# count minimises a wave model: ceil(tiles * s / pairs) / s waves of the unsplit
+# tile time, plus the slab round trip (write and read of s fp32 partials).
+# Measured on B200 at T = 8192, the o_proj weight gradient (1024 x 2048, 32
+# tiles on 74 SM pairs) is the step's product that gains; the ordered split-K
+# (each slice waiting for the previous one's running sum) lost on every shape.
+_SPLITK_MIN_K = 2048
+_PAIR_TFLOPS = 22e12    # one SM pair's bf16 rate inside a long-K tile (measured ~0.7 of peak)
+_SLAB_BYTES_PER_S = 5e12
 
 
-def _streamk_ws(device) -> torch.Tensor:
-    """Scratch for a stream-K launch (two fp32 256 x 256 tiles per SM pair,
-    ~38 MB on B200), from the caching allocator: the launcher decides per
-    product whether an even split of the k-blocks over the SM pairs pays off
-    (the weight gradients with few output tiles, long-K input gradients) and
-    leaves the scratch unused otherwise."""
-    return torch.empty(ext().gemm_streamk_ws_floats(), dtype=torch.float32, device=device)
+def _pair_slots() -> int:
+    try:
+        return max(1, torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count // 2)
+    except Exception:
+        return 74
+
+
+def _splitk(M: int, N: int, K: int, slots: int | None = None) -> int:
+    if M < 256 or K < 2 * _SPLITK_MIN_K:
+        return 1
+    slots = slots or _pair_slots()
+    tiles = ((M + 255) // 256) * ((N + 255) // 256)
+    t_tile = 2.0 * 256 * 256 * K / _PAIR_TFLOPS
+
+    def cost(s):
+        waves = -(-tiles * s // slots) / s
+        slab = 0.0 if s == 1 else 2.0 * s * M * N * 4 / _SLAB_BYTES_PER_S
+        return waves * t_tile + slab
+
+    best = 1
+    for s in (2, 3, 4):
+        if K // s >= _SPLITK_MIN_K and cost(s) < 0.9 * cost(best):
+            best = s
+    return best
 
 
 def _rows(t: torch.Tensor) -> torch.Tensor:
@@ -104,8 +126,7 @@ def linear_dgrad(g: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = No
     epi = EPI_ACCUM_BF16 if accumulate else EPI_STORE_BF16
     if out.dtype == torch.float32:
         epi = EPI_ACCUM_F32 if accumulate else EPI_STORE_F32
-    ws = _streamk_ws(g.device) if g2.shape[1] >= 2048 else None  # long K only
-    ext().gemm(g2, w, out, False, True, epi, 1.0, streamk_ws=ws)
+    ext().gemm(g2, w, out, False, True, epi, 1.0)
     return out
 
 
@@ -128,15 +149,19 @@ def linear_wgrad(g: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = No
         out = torch.empty(g2.shape[1], x2.shape[1], dtype=out_dtype, device=g.device)
         accumulate = False
     M, N, K = g2.shape[1], x2.shape[1], g2.shape[0]
+    splits = _splitk(M, N, K)
+    if splits > 1 and out.is_contiguous():
+        # split-K over the tokens: slice s stores its fp32 partial in slab s,
+        # then the slabs are added in slice order into out (bf16 or fp32,
+        # optionally accumulating)
+        slabs = torch.empty(splits * M, N, dtype=torch.float32, device=g.device)
+        ext().gemm(g2, x2, slabs, True, True, EPI_STORE_F32, 1.0, splits=splits)
+        ext().sum_slices(slabs.view(splits, M * N), out.view(-1), accumulate)
+        return out
     if out.dtype == torch.float32:
         epi = EPI_ACCUM_F32 if accumulate else EPI_STORE_F32
     else:
         epi = EPI_ACCUM_BF16 if accumulate else EPI_STORE_BF16
-    if M >= 256 and K >= 2048:
-        # few output tiles over a long K (all tokens): the launcher may run it
-        # stream-K (even share of k-blocks per SM pair, fixed-order fix-up)
-        ext().gemm(g2, x2, out, True, True, epi, 1.0, streamk_ws=_streamk_ws(g.device))
-        return out
     ext().gemm(g2, x2, out, True, True, epi, 1.0)
     return out
 

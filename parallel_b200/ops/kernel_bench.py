@@ -147,7 +147,7 @@ def case_wgrad_split(warmup, iters):
     """Weight-gradient GEMMs dW[M, N] = g^T x over T = B * S tokens at the
     0.6B step's split-K shapes: one K slice, split-K with fp32 atomics (zero
     fill + GEMM + cast) and the ordered split-K epilogue."""
-    from .gemm import EPI_ATOMIC_F32, EPI_SPLIT_ORDERED, EPI_STORE_BF16, EPI_STORE_F32
+    from .gemm import EPI_ATOMIC_F32, EPI_SPLIT_ORDERED, EPI_STORE_BF16, EPI_STORE_F32, _splitk
 
     C = ext()
     T = B * S
@@ -174,12 +174,10 @@ def case_wgrad_split(warmup, iters):
             C.sum_slices(slabs.view(sp, M * N), out.view(-1), False)
 
         tsl = _time(slab, warmup, iters)
-        sk_ws = torch.empty(C.gemm_streamk_ws_floats(), device="cuda")
-        tsk = _time(lambda: C.gemm(g, x, out, True, True, EPI_STORE_BF16, 1.0, streamk_ws=sk_ws), warmup, iters)
         tf = 2 * M * N * T / 1e6
         lines.append(f"wgrad {name} {M}x{N}x{T}: 1 slice {t1:.1f} us ({tf / t1:.0f} TF/s), {sp} slices atomic+fill+cast "
                      f"{ta:.1f} us, {sp} slices ordered {to:.1f} us ({tf / to:.0f} TF/s), {sp} fp32 slabs + sum "
-                     f"{tsl:.1f} us ({tf / tsl:.0f} TF/s), stream-K launch {tsk:.1f} us ({tf / tsk:.0f} TF/s)")
+                     f"{tsl:.1f} us ({tf / tsl:.0f} TF/s); policy picks {_splitk(M, N, T)}")
     return "\n".join(lines)
 
 
@@ -214,7 +212,7 @@ def case_gemm_vs_cublas(warmup, iters):
         x = torch.randn(T, k_in, device="cuda", dtype=torch.bfloat16)
         g = torch.randn(T, n_out, device="cuda", dtype=torch.bfloat16)
         # ours: the entry points the training step calls (they pick the tile
-        # schedule: whole tiles, or stream-K for few-tile long-K products)
+        # schedule: whole tiles, or split-K for few-tile long-K products)
         for kind, (M, N, K), ours, ref in (
                 ("fwd", (T, n_out, k_in), lambda o: G.linear(x, w, out=o), lambda o: torch.mm(x, w.t(), out=o)),
                 ("dgrad", (T, k_in, n_out), lambda o: G.linear_dgrad(g, w, out=o), lambda o: torch.mm(g, w, out=o)),
