@@ -9,6 +9,8 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "host_util.h"
@@ -323,7 +325,8 @@ __global__ void qknorm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, in
 // Backward of the above; q/k norm weight grads: per-lane registers, one slice
 // per half warp in shared memory, summed in slot order into row blockIdx.x of
 // the block-partial matrix [grid, 2 * D] (q weights, then k weights).
-__global__ void __launch_bounds__(256, 2) qknorm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dq, int64_t lddq,
+template <int U, int MINB>
+__global__ void __launch_bounds__(256, MINB) qknorm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dq, int64_t lddq,
                                        const __nv_bfloat16* __restrict__ dk, int64_t lddk,
                                        const __nv_bfloat16* __restrict__ qkv, int64_t ldqkv,
                                        const __nv_bfloat16* __restrict__ qw,
@@ -340,7 +343,6 @@ __global__ void __launch_bounds__(256, 2) qknorm_rope_bwd_kernel(const __nv_bflo
   // input rows (2 x 16 bytes per lane per head) are issued before the first
   // shuffle, so a unit costs one DRAM round trip with 2U + 2 loads in flight.
   constexpr int D = 128;
-  constexpr int U = 4;
   __shared__ float sdw[16][2][D];  // [half-warp slot][q / k][column]
   const int lane = threadIdx.x & 31;
   const int hl = lane & 15;
@@ -513,9 +515,24 @@ void qknorm_rope_fwd(const void* qkv, int64_t ldqkv, const void* qw, const void*
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
+// Unit width U (heads per half-warp unit) and resident blocks per SM of the
+// backward: PB_QKN_BWD=<U>x<blocks> (read per call; 4x2, 2x3, 2x4 or 1x6), default 4x2.
+struct QknBwdCfg {
+  int u, blocks;
+};
+
+QknBwdCfg qknorm_bwd_cfg() {
+  const char* v = getenv("PB_QKN_BWD");
+  if (v && strcmp(v, "2x3") == 0) return {2, 3};
+  if (v && strcmp(v, "2x4") == 0) return {2, 4};
+  if (v && strcmp(v, "1x6") == 0) return {1, 6};
+  return {4, 2};
+}
+
 int qknorm_rope_bwd_grid(int T, int nq, int nkv) {
-  const int units = std::max(1, T * ((nq + nkv + 3) / 4));  // (token, 4 heads) units
-  const int blocks = num_sms() * 2;                         // one wave
+  const QknBwdCfg c = qknorm_bwd_cfg();
+  const int units = std::max(1, T * ((nq + nkv + c.u - 1) / c.u));  // (token, U heads) units
+  const int blocks = num_sms() * c.blocks;                          // one wave
   const int ipb = (units + blocks - 1) / blocks;
   return (units + ipb - 1) / ipb;
 }
@@ -525,10 +542,14 @@ void qknorm_rope_bwd(const void* dq, int64_t lddq, const void* dk, int64_t lddk,
                      const void* sin, const float* rstd, void* dqkv, int64_t lddqkv,
                      float* dw_part, int T, int S, int nq, int nkv, int D, cudaStream_t s) {
   PB_CHECK(D == 128, "qknorm_rope: head_dim 128 only");
-  const int units = T * ((nq + nkv + 3) / 4);
+  const QknBwdCfg c = qknorm_bwd_cfg();
+  const int units = T * ((nq + nkv + c.u - 1) / c.u);
   const int grid = qknorm_rope_bwd_grid(T, nq, nkv);
   const int ipb = (std::max(units, 1) + grid - 1) / grid;
-  launch_k(qknorm_rope_bwd_kernel, grid, 256, 0, s,
+  auto kern = c.u == 4 ? qknorm_rope_bwd_kernel<4, 2>
+                       : c.u == 1 ? qknorm_rope_bwd_kernel<1, 6>
+                                  : (c.blocks == 4 ? qknorm_rope_bwd_kernel<2, 4> : qknorm_rope_bwd_kernel<2, 3>);
+  launch_k(kern, grid, 256, 0, s,
       (const __nv_bfloat16*)dq, lddq, (const __nv_bfloat16*)dk, lddk, (const __nv_bfloat16*)qkv,
       ldqkv, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw, (const __nv_bfloat16*)cos,
       (const __nv_bfloat16*)sin, rstd, (__nv_bfloat16*)dqkv, lddqkv, dw_part, nullptr, T, S, nq,
