@@ -133,8 +133,9 @@ class MLP(nn.Module):
         self.up_proj = Linear(H, I)
         self.down_proj = Linear(I, H)
 
-    def forward(self, x, residual=None):
-        return Fx.swiglu_mlp(x, self.gate_proj.weight, self.up_proj.weight, self.down_proj.weight, residual)
+    def forward(self, x, residual=None, output_unused: bool = False):
+        return Fx.swiglu_mlp(x, self.gate_proj.weight, self.up_proj.weight, self.down_proj.weight, residual,
+                             output_unused)
 
 
 class TopKRouter(nn.Module):
@@ -259,7 +260,10 @@ class DecoderLayer(nn.Module):
             y = self.mlp(h)
             y = ctx.comm.reduce_scatter_sequence(y, ctx) if ctx.sp else ctx.comm.reduce_from_tp(y, ctx)
             return x + y
-        return self.mlp(h, residual=x)
+        # in an activation-checkpoint recompute the layer output only carries
+        # the gradient (the FSDP unit differentiates through it), so the final
+        # down projection is skipped there
+        return self.mlp(h, residual=x, output_unused=getattr(self, "_recomputing", False))
 
 
 class Qwen3Model(nn.Module):

@@ -318,7 +318,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = Non
 # ----------------------------------------------------------------- SwiGLU MLP
 class _MLPFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, wg, wu, wd, residual):
+    def forward(ctx, x, wg, wu, wd, residual, output_unused=False):
         I = wg.shape[0]
         x2 = x.reshape(-1, x.shape[-1])
         if not x2.is_contiguous():
@@ -326,7 +326,13 @@ class _MLPFn(torch.autograd.Function):
         wgu = fused_rows(wg, wu)
         h, gu = G.linear_swiglu(x2, wgu, I)
         r2 = None if residual is None else residual.reshape(-1, wd.shape[0])
-        out = G.linear(h, wd, residual=r2)
+        if output_unused:
+            # activation-checkpoint recompute: only the saved tensors matter (the
+            # backward of the down projection needs h and its weight, not its
+            # output), so the down GEMM is not run and the output is left unset
+            out = torch.empty(x2.shape[0], wd.shape[0], device=x.device, dtype=x.dtype)
+        else:
+            out = G.linear(h, wd, residual=r2)
         ctx.save_for_backward(x2, wg, wu, wd, gu, h)
         ctx.has_res = residual is not None
         ctx.in_shape = x.shape
@@ -346,13 +352,15 @@ class _MLPFn(torch.autograd.Function):
         wgu = fused_rows(wg, wu)
         dx = G.linear_dgrad(dgu, wgu).view(ctx.in_shape)
         dwgu = G.linear_wgrad(dgu, x2)
-        return dx, dwgu[:I], dwgu[I:], dwd, (dy if ctx.has_res else None)
+        return dx, dwgu[:I], dwgu[I:], dwd, (dy if ctx.has_res else None), None
 
 
-def swiglu_mlp(x, wg, wu, wd, residual=None):
-    """``residual + down(silu(gate x) * up x)``."""
+def swiglu_mlp(x, wg, wu, wd, residual=None, output_unused: bool = False):
+    """``residual + down(silu(gate x) * up x)``.  ``output_unused`` (CUDA): the
+    caller only differentiates through the result (an activation-checkpoint
+    recompute), so its value is not computed; gradients are unchanged."""
     if x.is_cuda:
-        return _MLPFn.apply(x, wg, wu, wd, residual)
+        return _MLPFn.apply(x, wg, wu, wd, residual, output_unused)
     y = F.linear(F.silu(F.linear(x, wg)) * F.linear(x, wu), wd)
     if residual is not None:
         y = residual + y

@@ -100,11 +100,15 @@ class _UnitFn(torch.autograd.Function):
             if stash is not None:
                 stash["mode"] = "reuse"
             unit.module._attn_stash = stash
+            # the recomputed output only carries gy into autograd.grad below:
+            # layers may skip computing its value (the dense MLP's down GEMM)
+            unit.module._recomputing = True
             try:
                 with torch.enable_grad():
                     y, extras = _run_layer(unit, ctx.fwd, xi, ctx.args)
             finally:
                 unit.module._attn_stash = None
+                unit.module._recomputing = False
                 ctx.stash = None
         else:
             xi, y, extras = ctx.inner

@@ -276,3 +276,26 @@ def test_training_steps_are_bitwise_reproducible(name):
     assert torch.equal(na, nb), (na, nb)
     for n, p in pa.items():
         assert torch.equal(p, pb[n]), n
+
+
+def test_mlp_recompute_without_output_gives_the_same_gradients():
+    """The activation-checkpoint recompute runs the dense MLP with its output
+    unused (the down GEMM is skipped); differentiating through that output
+    gives bitwise the gradients of the full forward."""
+    from parallel_b200.ops import functional as Fx
+
+    torch.manual_seed(3)
+    T, H, I = 512, 256, 512
+    x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    res = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    wg, wu = (0.05 * torch.randn(I, H, device="cuda")).to(torch.bfloat16), (0.05 * torch.randn(I, H, device="cuda")).to(torch.bfloat16)
+    wd = (0.05 * torch.randn(H, I, device="cuda")).to(torch.bfloat16)
+    gy = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    grads = []
+    for unused in (False, True):
+        leaves = [t.detach().clone().requires_grad_(True) for t in (x, wg, wu, wd, res)]
+        y = Fx.swiglu_mlp(leaves[0], leaves[1], leaves[2], leaves[3], leaves[4], output_unused=unused)
+        grads.append(torch.autograd.grad([y], leaves, [gy]))
+    torch.cuda.synchronize()
+    for a, b in zip(*grads):
+        assert torch.equal(a, b)
