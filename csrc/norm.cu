@@ -9,8 +9,6 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
-#include <cstdlib>
-#include <cstring>
 #include <mutex>
 
 #include "host_util.h"
@@ -81,7 +79,7 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int64_t
                                    const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
                                    __nv_bfloat16* __restrict__ dx, int64_t lddx, float* __restrict__ dw,
                                    int rows, int cols, int rows_per_block,
-                                   const __nv_bfloat16* __restrict__ dres, int64_t lddres, PartialsOut fin) {
+                                   const __nv_bfloat16* __restrict__ dres, int64_t lddres) {
   pdl_prologue();
   extern __shared__ float sdw_all[];  // [warps][cols]
   const int warps = blockDim.x >> 5;
@@ -127,14 +125,12 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int64_t
     }
   }
   __syncthreads();
-  if (dw) {
+  if (dw)
     for (int c = threadIdx.x; c < cols; c += blockDim.x) {
       float t = 0.f;
       for (int w8 = 0; w8 < warps; ++w8) t += sdw_all[w8 * cols + c];
       dw[(int64_t)blockIdx.x * cols + c] = t;
     }
-    finish_partials_in_kernel(dw, cols, cols, gridDim.x, fin);
-  }
 }
 
 // Register-resident variant: cols == CH * 256; lane owns CH chunks of 8
@@ -146,7 +142,7 @@ __global__ void __launch_bounds__(256, 2) rmsnorm_bwd_reg_kernel(
     const __nv_bfloat16* __restrict__ dy, int64_t lddy, const __nv_bfloat16* __restrict__ x, int64_t ldx,
     const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dres,
     int64_t lddres, __nv_bfloat16* __restrict__ dx, int64_t lddx, float* __restrict__ dw, int rows,
-    int rows_per_block, PartialsOut fin) {
+    int rows_per_block) {
   pdl_prologue();
   // One warp per row, all of the row's loads (x, dy, dres) issued before the
   // reduction and kept packed in registers, so a row costs one DRAM round
@@ -231,9 +227,8 @@ __global__ void __launch_bounds__(256, 2) rmsnorm_bwd_reg_kernel(
     for (int c = threadIdx.x; c < cols; c += blockDim.x) {
       float t = 0.f;
       for (int w8 = 0; w8 < warps; ++w8) t += sdw[w8 * cols + c];
-      dw[(int64_t)blockIdx.x * cols + c] = t;  // block partial, summed in block order
+      dw[(int64_t)blockIdx.x * cols + c] = t;  // block partial, summed in block order later
     }
-    finish_partials_in_kernel(dw, cols, cols, gridDim.x, fin);
   }
 }
 
@@ -339,7 +334,7 @@ __global__ void __launch_bounds__(256, MINB) qknorm_rope_bwd_kernel(const __nv_b
                                        const float* __restrict__ rstd,
                                        __nv_bfloat16* __restrict__ dqkv, int64_t lddqkv,
                                        float* __restrict__ dqw, float* __restrict__ dkw, int T, int S,
-                                       int nq, int nkv, int units_per_block, PartialsOut fin) {
+                                       int nq, int nkv, int units_per_block) {
   pdl_prologue();
   // A half warp per unit = (token, group of U consecutive heads): the token's
   // cos / sin rows are loaded once per unit and every head's gradient and
@@ -441,7 +436,6 @@ __global__ void __launch_bounds__(256, MINB) qknorm_rope_bwd_kernel(const __nv_b
       for (int sl = 0; sl < slots; ++sl) t += sdw[sl][i / D][i % D];
       dqw[(int64_t)blockIdx.x * 2 * D + i] = t;
     }
-    finish_partials_in_kernel(dqw, 2 * D, 2 * D, gridDim.x, fin);
   }
 }
 
@@ -465,7 +459,7 @@ int rmsnorm_bwd_grid(int rows) {
 
 void rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const void* w,
                  const float* rstd, void* dx, int64_t lddx, float* dw_part, int rows, int cols,
-                 cudaStream_t s, const void* dres, int64_t lddres, const PartialsOut& fin) {
+                 cudaStream_t s, const void* dres, int64_t lddres) {
   PB_CHECK(cols % 8 == 0, "rmsnorm: cols must be a multiple of 8");
   const int grid = rmsnorm_bwd_grid(rows);
   const int rpb = (std::max(rows, 1) + grid - 1) / grid;
@@ -489,7 +483,7 @@ void rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const
   case CH:                                                                                                \
     launch_k(rmsnorm_bwd_reg_kernel<CH>, grid, 256, smem_reg, s,                                                 \
         (const __nv_bfloat16*)dy, lddy, (const __nv_bfloat16*)x, ldx, (const __nv_bfloat16*)w, rstd,      \
-        (const __nv_bfloat16*)dres, lddres, (__nv_bfloat16*)dx, lddx, dw_acc, rows, rpb, fin);            \
+        (const __nv_bfloat16*)dres, lddres, (__nv_bfloat16*)dx, lddx, dw_acc, rows, rpb);                 \
     break;
     switch (cols / 256) {
       PB_RMS_BWD(1) PB_RMS_BWD(2) PB_RMS_BWD(3) PB_RMS_BWD(4) PB_RMS_BWD(5) PB_RMS_BWD(6)
@@ -501,7 +495,7 @@ void rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const
   launch_k(rmsnorm_bwd_kernel, grid, 256, smem, s, (const __nv_bfloat16*)dy, lddy, (const __nv_bfloat16*)x,
                                              ldx, (const __nv_bfloat16*)w, rstd, (__nv_bfloat16*)dx,
                                              lddx, dw_acc, rows, cols, rpb, (const __nv_bfloat16*)dres,
-                                             lddres, fin);
+                                             lddres);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -520,18 +514,14 @@ void qknorm_rope_fwd(const void* qkv, int64_t ldqkv, const void* qw, const void*
 }
 
 // Unit width U (heads per half-warp unit) and resident blocks per SM of the
-// backward: PB_QKN_BWD=<U>x<blocks> (read per call; 4x2, 2x3, 2x4 or 1x6), default 4x2.
+// backward.  Measured on B200 at 8192 tokens x 24 heads: 4 x 2 blocks 43.3 us;
+// narrower units with more blocks spill registers and lose (2 x 3: 57.5 us,
+// 2 x 4: 67.8 us, 1 x 6: 83.5 us).
 struct QknBwdCfg {
   int u, blocks;
 };
 
-QknBwdCfg qknorm_bwd_cfg() {
-  const char* v = getenv("PB_QKN_BWD");
-  if (v && strcmp(v, "2x3") == 0) return {2, 3};
-  if (v && strcmp(v, "2x4") == 0) return {2, 4};
-  if (v && strcmp(v, "1x6") == 0) return {1, 6};
-  return {4, 2};
-}
+QknBwdCfg qknorm_bwd_cfg() { return {4, 2}; }
 
 int qknorm_rope_bwd_grid(int T, int nq, int nkv) {
   const QknBwdCfg c = qknorm_bwd_cfg();
@@ -544,21 +534,17 @@ int qknorm_rope_bwd_grid(int T, int nq, int nkv) {
 void qknorm_rope_bwd(const void* dq, int64_t lddq, const void* dk, int64_t lddk, const void* qkv,
                      int64_t ldqkv, const void* qw, const void* kw, const void* cos,
                      const void* sin, const float* rstd, void* dqkv, int64_t lddqkv,
-                     float* dw_part, int T, int S, int nq, int nkv, int D, cudaStream_t s,
-                     const PartialsOut& fin) {
+                     float* dw_part, int T, int S, int nq, int nkv, int D, cudaStream_t s) {
   PB_CHECK(D == 128, "qknorm_rope: head_dim 128 only");
   const QknBwdCfg c = qknorm_bwd_cfg();
   const int units = T * ((nq + nkv + c.u - 1) / c.u);
   const int grid = qknorm_rope_bwd_grid(T, nq, nkv);
   const int ipb = (std::max(units, 1) + grid - 1) / grid;
-  auto kern = c.u == 4 ? qknorm_rope_bwd_kernel<4, 2>
-                       : c.u == 1 ? qknorm_rope_bwd_kernel<1, 6>
-                                  : (c.blocks == 4 ? qknorm_rope_bwd_kernel<2, 4> : qknorm_rope_bwd_kernel<2, 3>);
-  launch_k(kern, grid, 256, 0, s,
+  launch_k(qknorm_rope_bwd_kernel<4, 2>, grid, 256, 0, s,
       (const __nv_bfloat16*)dq, lddq, (const __nv_bfloat16*)dk, lddk, (const __nv_bfloat16*)qkv,
       ldqkv, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw, (const __nv_bfloat16*)cos,
       (const __nv_bfloat16*)sin, rstd, (__nv_bfloat16*)dqkv, lddqkv, dw_part, nullptr, T, S, nq,
-      nkv, ipb, fin);
+      nkv, ipb);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

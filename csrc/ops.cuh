@@ -3,7 +3,6 @@
 // pointers and run on the given stream; shapes are validated by the Python
 // bindings.
 #pragma once
-#include "partials.cuh"
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -22,7 +21,7 @@ void rmsnorm_fwd(const void* x, int64_t ldx, const void* w, void* y, int64_t ldy
 int rmsnorm_bwd_grid(int rows);
 void rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const void* w,
                  const float* rstd, void* dx, int64_t lddx, float* dw_part, int rows, int cols,
-                 cudaStream_t s, const void* dres = nullptr, int64_t lddres = 0, const PartialsOut& fin = PartialsOut());
+                 cudaStream_t s, const void* dres = nullptr, int64_t lddres = 0);
 
 // ---- per-head RMSNorm of q and k + rotate-half RoPE (norm.cu)
 // qkv: [T, (nq + 2*nkv) * D] (row stride ldqkv); writes q_out [T, nq*D],
@@ -40,7 +39,7 @@ int qknorm_rope_bwd_grid(int T, int nq, int nkv);
 void qknorm_rope_bwd(const void* dq, int64_t lddq, const void* dk, int64_t lddk, const void* qkv,
                      int64_t ldqkv, const void* qw, const void* kw, const void* cos,
                      const void* sin, const float* rstd, void* dqkv, int64_t lddqkv,
-                     float* dw_part, int T, int S, int nq, int nkv, int D, cudaStream_t s, const PartialsOut& fin = PartialsOut());
+                     float* dw_part, int T, int S, int nq, int nkv, int D, cudaStream_t s);
 
 // ---- SwiGLU backward (act.cu): gu = [g | u] (row stride ldgu, u at column I)
 // dgu[:, :I] = dh * u * silu'(g), dgu[:, I:] = dh * silu(g)

@@ -6,7 +6,6 @@
 #include <vector>
 
 #include "attention.cuh"
-#include "host_util.h"
 #include "ops.cuh"
 
 namespace {
@@ -26,27 +25,6 @@ void finish_partials(const at::Tensor& parts, int slices, int64_t len, int64_t s
               "weight gradient: contiguous bf16 / fp32 CUDA tensor of ", len, " elements");
   pb::sum_slices(parts.data_ptr<float>() + offset, slices, len, stride, out.data_ptr(),
                  out.scalar_type() == at::kBFloat16, false, at::cuda::getCurrentCUDAStream().stream());
-}
-
-// The producing kernel sums its block partials itself (partials.cuh): outputs
-// (bf16 or fp32, contiguous; out0 holds the first len0 columns, out1 the rest)
-// and a zeroed counter slot of this device.
-pb::PartialsOut kernel_finish(const at::Tensor& out0, const at::Tensor* out1, int64_t len0, int device) {
-  pb::PartialsOut f;
-  const at::Tensor& ref = out0.defined() ? out0 : *out1;
-  for (const at::Tensor* t : {&out0, out1}) {
-    if (t == nullptr || !t->defined()) continue;
-    TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->numel() == len0 &&
-                    (t->scalar_type() == at::kBFloat16 || t->scalar_type() == at::kFloat) &&
-                    t->scalar_type() == ref.scalar_type(),
-                "weight gradient: contiguous bf16 / fp32 CUDA tensor of ", len0, " elements");
-  }
-  f.out0 = out0.defined() ? out0.data_ptr() : nullptr;
-  f.out1 = (out1 && out1->defined()) ? out1->data_ptr() : nullptr;
-  f.len0 = (int)len0;
-  f.out_bf16 = ref.scalar_type() == at::kBFloat16 ? 1 : 0;
-  f.counters = reinterpret_cast<unsigned*>(pb::split_counters(device));
-  return f;
 }
 
 float* opt_f32(const c10::optional<at::Tensor>& t) {
@@ -84,10 +62,12 @@ void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
     parts = at::empty({grid, x.size(1)}, x.options().dtype(at::kFloat));
     pp = parts.data_ptr<float>();
   }
-  pb::PartialsOut fin;
-  if (pp) fin = kernel_finish(*dw, nullptr, x.size(1), x.get_device());
   pb::rmsnorm_bwd(dy.data_ptr(), dy.stride(0), x.data_ptr(), x.stride(0), w.data_ptr(), rstd.data_ptr<float>(),
-                  dx.data_ptr(), dx.stride(0), pp, x.size(0), x.size(1), cur_stream(), rp, ldr, fin);
+                  dx.data_ptr(), dx.stride(0), pp, x.size(0), x.size(1), cur_stream(), rp, ldr);
+  if (pp) {
+    at::Tensor out = *dw;
+    finish_partials(parts, grid, x.size(1), x.size(1), 0, out);
+  }
 }
 
 void qknorm_rope_fwd(const at::Tensor& qkv, const at::Tensor& qw, const at::Tensor& kw, const at::Tensor& cos,
@@ -117,10 +97,15 @@ void qknorm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tenso
   pb::qknorm_rope_bwd(dq.data_ptr(), dq.stride(0), dk.data_ptr(), dk.stride(0), qkv.data_ptr(), qkv.stride(0),
                       qw.data_ptr(), kw.data_ptr(), cos.data_ptr(), sin.data_ptr(), rstd.data_ptr<float>(),
                       dqkv.data_ptr(), dqkv.stride(0), want ? parts.data_ptr<float>() : nullptr, qkv.size(0), (int)S,
-                      (int)nq, (int)nkv, D, cur_stream(),
-                      want ? kernel_finish(dqw.has_value() && dqw->defined() ? *dqw : at::Tensor(),
-                                           dkw.has_value() && dkw->defined() ? &*dkw : nullptr, D, qkv.get_device())
-                           : pb::PartialsOut());
+                      (int)nq, (int)nkv, D, cur_stream());
+  if (dqw.has_value() && dqw->defined()) {
+    at::Tensor out = *dqw;
+    finish_partials(parts, grid, D, 2 * D, 0, out);
+  }
+  if (dkw.has_value() && dkw->defined()) {
+    at::Tensor out = *dkw;
+    finish_partials(parts, grid, D, 2 * D, D, out);
+  }
 }
 
 // tiles128 (optional int32 CUDA [1]): only the first 128 * tiles128[0] rows are live
