@@ -299,3 +299,28 @@ def test_mlp_recompute_without_output_gives_the_same_gradients():
     torch.cuda.synchronize()
     for a, b in zip(*grads):
         assert torch.equal(a, b)
+
+
+def test_decoder_layer_recompute_flag_keeps_gradients():
+    """A dense decoder layer run as the FSDP unit's activation-checkpoint
+    recompute (``_recomputing`` set: the down projection is skipped) gives
+    bitwise the input and parameter gradients of a normal run."""
+    cfg, _, gpu = _pair("small-qwen3")
+    layer = gpu.model.layers[0]
+    B, S = 2, 256
+    layer._seq = (B, S)
+    layer._inv_freq = gpu.model.rotary_emb.inv_freq
+    torch.manual_seed(9)
+    x = torch.randn(B, S, cfg.hidden_size, device="cuda").to(torch.bfloat16)
+    gy = torch.randn_like(x)
+    params = [p for p in layer.parameters()]
+    grads = []
+    for recompute in (False, True):
+        layer._recomputing = recompute
+        xi = x.detach().requires_grad_(True)
+        y = layer(xi)
+        grads.append(torch.autograd.grad([y], [xi] + params, [gy], allow_unused=True))
+    layer._recomputing = False
+    torch.cuda.synchronize()
+    for a, b in zip(*grads):
+        assert (a is None and b is None) or torch.equal(a, b)
