@@ -161,10 +161,25 @@ __global__ void __launch_bounds__(kThreads) sumsq_kernel(NormTable tab, float* _
   const int64_t end = min(sg.n, base + kChunk);
   float acc = 0.f;
   bool bad = false;
-  for (int64_t i = base + threadIdx.x; i < end; i += kThreads) {
+  int64_t i0 = base;
+  if ((reinterpret_cast<uintptr_t>(sg.g) & 31) == 0) {
+    // 8 elements (one 16- or 32-byte load) per thread per step
+    const int64_t vend = base + ((end - base) / 8) * 8;
+    for (int64_t j = base + threadIdx.x * 8; j < vend; j += kThreads * 8) {
+      float g[8];
+      ld8<GT>(sg.g, j, g);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        bad |= !isfinite(g[k]);
+        acc = fmaf(g[k], g[k], acc);
+      }
+    }
+    i0 = vend;
+  }
+  for (int64_t i = i0 + threadIdx.x; i < end; i += kThreads) {
     const float g = ldf<GT>(sg.g, i);
     bad |= !isfinite(g);
-    acc += g * g;
+    acc = fmaf(g, g, acc);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
