@@ -63,10 +63,10 @@ class DPParamUnit:
         self.gradient_reduction_mode = "overlapped" if overlap_backward_reductions else "deferred"
         self._named_params = list(named_parameters if named_parameters is not None else module.named_parameters())
         if not self._named_params:
-            raise ValueError("DPParamUnit requires at least one parameter")
+            raise ValueError(f"FSDP unit {unit_index}: no parameters to shard")
         rg = {p.requires_grad for _, p in self._named_params}
         if len(rg) != 1:
-            raise ValueError("A DPParamUnit cannot mix trainable and frozen parameters")
+            raise ValueError(f"FSDP unit {unit_index}: trainable and frozen parameters must go to separate units")
         self.requires_grad = rg.pop()
         self.device = device or self._named_params[0][1].device
         self.world_size = self.mesh.size()
@@ -105,17 +105,17 @@ class DPParamUnit:
 
     def shard(self) -> None:
         if self._is_sharded:
-            raise RuntimeError(f"FSDP unit {self.unit_index} is already sharded")
+            raise RuntimeError(f"FSDP unit {self.unit_index}: shard() was already called")
         N, r = self.world_size, self.rank
         self.param_metas.clear()
         for name, p in self._named_params:
             if isinstance(p, DTensor):
-                raise NotImplementedError("DPParamUnit shards plain (model-parallel local) parameters")
+                raise NotImplementedError(f"FSDP unit {self.unit_index}: {name} is a DTensor; units shard plain local tensors")
             if p.ndim == 0:
-                raise ValueError(f"FSDP parameter {name} must have at least one dimension")
+                raise ValueError(f"FSDP unit {self.unit_index}: {name} is a scalar; dim-0 sharding needs rows")
             refs = self._find_module_refs(p)
             if not refs:
-                raise RuntimeError(f"Could not find module registration for parameter {name}")
+                raise RuntimeError(f"FSDP unit {self.unit_index}: {name} is not registered on any module of the unit")
             meta = ParamMeta(name=name, shape=p.shape, stride=tuple(p.stride()), numel=p.numel(), parameter=p,
                              module_refs=refs)
             meta.padded_rows = (p.shape[0] + N - 1) // N
@@ -226,7 +226,7 @@ class DPParamUnit:
     def writeback_shards(self) -> None:
         """Copy the gathered parameters into this rank's shards (checkpoint load)."""
         if self.full_buffer is None:
-            raise RuntimeError("Parameters must be gathered before writing back shards")
+            raise RuntimeError(f"FSDP unit {self.unit_index}: write-back of shards needs the gathered parameters")
         for m in self.param_metas:
             start = min(self.rank * m.padded_rows, m.shape[0])
             m.padded_shard.zero_()
@@ -242,7 +242,7 @@ class DPParamUnit:
         the shard group and accumulated into ``grad_bucket``.
         """
         if self._pending is not None:
-            raise RuntimeError(f"Gradient reduction already in flight for FSDP unit {self.unit_index}")
+            raise RuntimeError(f"FSDP unit {self.unit_index}: its previous gradient reduction has not finished")
         self._participation = [g is not None for g in grads]
         accumulate = self._grad_valid
         if self.grad_bucket is None:
