@@ -153,9 +153,9 @@ def dist_data_loader(tokenizer, B, T, split, tokenizer_batch_size=128, device="c
     }
     if resume_state_dict is not None:
         if resume_state_dict.get("dataset") != identity:
-            raise RuntimeError("Cannot resume dataloader because the dataset files have changed")
+            raise RuntimeError("dataloader state was saved for different data files; refusing to resume")
         if resume_state_dict.get("loader_config") != loader_config:
-            raise RuntimeError("Cannot resume dataloader because its configuration has changed")
+            raise RuntimeError("dataloader state was saved with a different batch / sequence / tokenizer setup; refusing to resume")
     batches = _create_batches(split, resume_state_dict, tokenizer_batch_size, data_rank, data_world, paths)
     bos = tokenizer.bos_token_id
     docs = copy.deepcopy(resume_state_dict.get("doc_buffer", []) if resume_state_dict is not None else [])

@@ -47,7 +47,7 @@ class ParallelEngine:
         self.device = device
         self.use_amp = cfg.config.use_amp
         if self.use_amp and cfg.config.amp_dtype not in ("bf16", "fp16"):
-            raise ValueError("amp_dtype must be either 'bf16' or 'fp16' when AMP is enabled")
+            raise ValueError("config.amp_dtype has to be 'bf16' or 'fp16' when config.use_amp is set")
         self.amp_dtype = DTYPE_DICT.get(cfg.config.amp_dtype, torch.float32)
         self.grad_scaler = torch.amp.GradScaler(pconfig.device_type or device.type,
                                                 enabled=self.use_amp and self.amp_dtype == torch.float16)
@@ -293,7 +293,7 @@ class ParallelEngine:
             msg = f"device error code {err} during the previous step (1 = pipeline wait, 2 = peer wait timeout)"
             raise CollectiveTimeout(msg) if err == 2 else RuntimeError(msg)
         if bad:
-            raise FloatingPointError("Non-finite gradients encountered")
+            raise FloatingPointError("gradient norm is not finite (inf or nan in some gradient); step skipped")
 
     def _defer_nonfinite_check(self, flag: torch.Tensor):
         self._pending_nonfinite = flag
@@ -392,7 +392,7 @@ class ParallelEngine:
             if not self.grad_scaler.is_enabled():
                 self.optimizer.zero_grad(set_to_none=True)
                 self.fsdp_wrapper.zero_grad()
-                raise FloatingPointError("Non-finite gradients encountered")
+                raise FloatingPointError("gradient norm is not finite (inf or nan in some gradient); step skipped")
             self.grad_scaler.update(new_scale=self.grad_scaler.get_scale() / 2.0)
         else:
             if self.grad_scaler.is_enabled():

@@ -170,7 +170,7 @@ class FSDPWrapper(FSDPStateMixin):
         if self.pconfig.dp_shard_size <= 1 or self.pconfig.device_mesh is None:
             return
         if self.units:
-            raise RuntimeError("FSDPWrapper.shard_model() can only be called once")
+            raise RuntimeError("the model is already sharded (shard_model() runs once)")
         self.dp_shard_mesh = self.pconfig.device_mesh[Strategies.DP_SHARD.value]
         self.dp_shard_group = self.dp_shard_mesh.get_group()
         # host-resident shards cannot live in symmetric device memory
@@ -184,7 +184,7 @@ class FSDPWrapper(FSDPStateMixin):
         for i, sub in enumerate(layers):
             named = [(self.state_names[id(p)][0], p) for _, p in sub.named_parameters()]
             if owned.intersection(id(p) for _, p in named):
-                raise ValueError("A parameter is shared by multiple FSDP units")
+                raise ValueError("a parameter appears in two FSDP units; each parameter needs exactly one owner")
             if not named:
                 continue
             owned.update(id(p) for _, p in named)
@@ -199,7 +199,7 @@ class FSDPWrapper(FSDPStateMixin):
                 root_specs = [(self.model, g, False, False, False) for g in group_named_parameters(root)]
                 owned.update(id(p) for _, p in root)
         if owned != {id(p) for p in self.model.parameters()}:
-            raise RuntimeError("Every model parameter must belong to exactly one FSDP unit")
+            raise RuntimeError("some model parameters ended up in no FSDP unit")
         all_specs = root_specs + specs
         for i, (sub, named, ckpt, reshard, primary) in enumerate(all_specs):
             unit = DPParamUnit(sub, self.dp_shard_mesh, i, self.coll, cpu_offload=self.cpu_offload,
@@ -321,16 +321,16 @@ class FSDPWrapper(FSDPStateMixin):
         if not self.is_active:
             return
         if not isinstance(loss, torch.Tensor):
-            raise TypeError("FSDPWrapper.prepare_backward() requires a loss tensor")
+            raise TypeError("prepare_backward() takes the loss tensor of the step")
         if self._backward_prepared:
-            raise RuntimeError("FSDP backward is already prepared")
+            raise RuntimeError("prepare_backward() was called twice in one step")
         self._done_units.clear()
         self._deferred.clear()
         self._backward_prepared = True
 
     def _unit_backward_done(self, unit: DPParamUnit, grads: list) -> None:
         if not self._backward_prepared:
-            raise RuntimeError("FSDP unit became ready before prepare_backward()")
+            raise RuntimeError("an FSDP unit finished its backward before prepare_backward() was called")
         self._done_units.add(unit.unit_index)
         missing = [m.name for m, g in zip(unit.param_metas, grads) if g is None]
         if missing and not self.find_unused_parameters:
@@ -353,7 +353,7 @@ class FSDPWrapper(FSDPStateMixin):
         if not self.is_active:
             return
         if not self._backward_prepared:
-            raise RuntimeError("FSDP backward was not prepared before finalization")
+            raise RuntimeError("finalize_backward() without prepare_backward() in this step")
         # root units: gradients arrived through autograd on the full params
         for u in self.root_units:
             grads = [m.parameter.grad for m in u.param_metas]

@@ -45,7 +45,7 @@ class SequenceParallelRuntime:
             raise RuntimeError("Sequence-parallel runtime is already installed")
         layers = list(model.model.layers)
         if not layers:
-            raise RuntimeError("Sequence parallelism requires decoder layers")
+            raise RuntimeError("sequence parallelism found no decoder layers in the model")
         ctx = model.ctx
         ctx.sp = True
         model.set_parallel_context(ctx)

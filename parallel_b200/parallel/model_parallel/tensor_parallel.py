@@ -22,11 +22,11 @@ from .plan import GradientReduction, ModelParallelPlan, ParameterParallelism
 def tensor_parallel_mesh(pconfig):
     mesh = pconfig.device_mesh
     if mesh is None:
-        raise RuntimeError("Tensor parallelism requires a DeviceMesh")
+        raise RuntimeError("tensor parallelism needs the device mesh (set_device_mesh first)")
     if mesh.ndim == 1:
         return mesh
     if Strategies.TP.value not in mesh.mesh_dim_names:
-        raise RuntimeError("The distributed DeviceMesh has no tp dimension")
+        raise RuntimeError("the device mesh has no 'tp' dimension")
     return mesh[Strategies.TP.value]
 
 

@@ -67,7 +67,7 @@ def main(argv=None):
         from transformers import AutoTokenizer
 
         tokenizer = AutoTokenizer.from_pretrained(cfg.model.name)
-        logger.info("Collecting token bytes...")
+        logger.info("Measuring the byte length of every token for bits-per-byte...")
         token_bytes = get_token_bytes(tokenizer)
     pconfig.model_train_rngs(seed=seed)
     # engine.compile: the whole training step is captured as a CUDA graph
@@ -91,7 +91,7 @@ def main(argv=None):
         engine.enable_graph_capture(warmup_steps=2)
     resume = None
     if cfg.config.resume_from:
-        logger.info(f"Loading checkpoint from {cfg.config.resume_from}")
+        logger.info(f"Resuming from checkpoint {cfg.config.resume_from}")
         resume = engine.load_checkpoint(cfg.config.resume_from)
     B, T = cfg.model.per_device_batch_size, cfg.model.max_seq_length
     if synthetic:

@@ -69,11 +69,11 @@ def test_resume_rejects_changed_config_or_data(tmp_path):
     st = copy.deepcopy(st)
     bad = copy.deepcopy(st)
     bad["loader_config"]["batch_size"] = 99
-    with pytest.raises(RuntimeError, match="configuration has changed"):
+    with pytest.raises(RuntimeError, match="different batch"):
         next(_loader(tmp_path, state=bad))
     p = tmp_path / "shard_00000.parquet"
     os.utime(p, ns=(p.stat().st_atime_ns, p.stat().st_mtime_ns + 10 ** 9))
-    with pytest.raises(RuntimeError, match="dataset files have changed"):
+    with pytest.raises(RuntimeError, match="different data files"):
         next(_loader(tmp_path, state=st))
 
 
