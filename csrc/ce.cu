@@ -7,12 +7,8 @@
 // labels != -100; transformers/loss/loss_utils.py) on the non-model-parallel
 // path and DTensor loss_parallel cross-entropy on the vocab-sharded path
 // (parallel/parallel/engine/model_parallel/loss_parallel.py:22-69).
-#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 #include <float.h>
-
-#include <algorithm>
-#include <mutex>
 
 #include "host_util.h"
 #include "ops.cuh"
@@ -21,7 +17,7 @@
 namespace pb {
 namespace {
 
-constexpr int kThreads = 1024;
+constexpr int kThreads = 512;
 
 __device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2) {
   const float mn = fmaxf(m, m2);
@@ -30,9 +26,8 @@ __device__ __forceinline__ void online_merge(float& m, float& s, float m2, float
   m = mn;
 }
 
-template <int NT>
-__device__ __forceinline__ void block_stats_n(float& m, float& s) {
-  __shared__ float sm[NT / 32], ss[NT / 32];
+__device__ __forceinline__ void block_stats(float& m, float& s) {
+  __shared__ float sm[kThreads / 32], ss[kThreads / 32];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
@@ -43,8 +38,8 @@ __device__ __forceinline__ void block_stats_n(float& m, float& s) {
   if (lane == 0) { sm[w] = m; ss[w] = s; }
   __syncthreads();
   if (w == 0) {
-    m = lane < NT / 32 ? sm[lane] : -FLT_MAX;
-    s = lane < NT / 32 ? ss[lane] : 0.f;
+    m = lane < kThreads / 32 ? sm[lane] : -FLT_MAX;
+    s = lane < kThreads / 32 ? ss[lane] : 0.f;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
@@ -59,48 +54,30 @@ __device__ __forceinline__ void block_stats_n(float& m, float& s) {
   __syncthreads();
 }
 
-__device__ __forceinline__ void block_stats(float& m, float& s) { block_stats_n<kThreads>(m, s); }
-
 // Local row max / sum-exp with 8-wide vector loads (V % 8 == 0 and 16-byte
-// aligned rows) or a scalar fallback.  Each thread keeps a running max and
-// rescales its sum only when a vector raises it (rare after the first few),
-// so the pass costs one exponential per element; kUnroll vectors are loaded
-// before any is used.
-constexpr int kUnroll = 4;
-
+// aligned rows) or a scalar fallback.
 __device__ __forceinline__ void row_local_stats(const __nv_bfloat16* row, int V, bool vec, float& m,
                                                 float& s) {
   m = -FLT_MAX;
   s = 0.f;
   if (vec) {
-    for (int c0 = threadIdx.x * 8; c0 < V; c0 += kThreads * 8 * kUnroll) {
-      uint4 raw[kUnroll];
+    for (int c = threadIdx.x * 8; c < V; c += kThreads * 8) {
+      uint4 raw = *reinterpret_cast<const uint4*>(row + c);
+      const uint32_t* p = &raw.x;
+      float v[8];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int c = c0 + u * kThreads * 8;
-        if (c < V) raw[u] = *reinterpret_cast<const uint4*>(row + c);
+      for (int q = 0; q < 4; ++q) {
+        float2 f = unpack_bf16x2(p[q]);
+        v[2 * q] = f.x;
+        v[2 * q + 1] = f.y;
       }
+      float lm = v[0];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        if (c0 + u * kThreads * 8 >= V) break;
-        const uint32_t* p = &raw[u].x;
-        float v[8];
+      for (int j = 1; j < 8; ++j) lm = fmaxf(lm, v[j]);
+      float ls = 0.f;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float2 f = unpack_bf16x2(p[q]);
-          v[2 * q] = f.x;
-          v[2 * q + 1] = f.y;
-        }
-        float lm = v[0];
-#pragma unroll
-        for (int j = 1; j < 8; ++j) lm = fmaxf(lm, v[j]);
-        if (lm > m) {
-          s *= __expf(m - lm);  // m == -FLT_MAX: s is 0 and stays 0
-          m = lm;
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) s += __expf(v[j] - m);
-      }
+      for (int j = 0; j < 8; ++j) ls += __expf(v[j] - lm);
+      online_merge(m, s, lm, ls);
     }
   } else {
     for (int c = threadIdx.x; c < V; c += kThreads) online_merge(m, s, __bfloat162float(row[c]), 1.f);
@@ -108,13 +85,14 @@ __device__ __forceinline__ void row_local_stats(const __nv_bfloat16* row, int V,
   block_stats(m, s);
 }
 
-// The gradient pass re-reads the row the statistics pass just read; with
-// 1024-thread CTAs two rows per SM are in flight (about 90 MB at V = 151936),
-// so the re-read mostly hits L2 and the logits cross DRAM once each way.
-__device__ __forceinline__ void ce_row(__nv_bfloat16* __restrict__ logits, int64_t ld,
-                                       const int64_t* __restrict__ labels, int t, int V, int64_t v0,
-                                       const float* __restrict__ scale, float* __restrict__ row_lse,
-                                       bool lse_given, float* __restrict__ row_target, bool write_grad) {
+__global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld,
+                                                     const int64_t* __restrict__ labels, int T, int V,
+                                                     int64_t v0, const float* __restrict__ scale,
+                                                     float* __restrict__ row_lse, bool lse_given,
+                                                     float* __restrict__ row_target, bool write_grad) {
+  pdl_prologue();
+  const int t = blockIdx.x;
+  if (t >= T) return;
   __nv_bfloat16* row = logits + (int64_t)t * ld;
   const bool vec = (V % 8 == 0) && ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
   float lse;
@@ -138,28 +116,18 @@ __device__ __forceinline__ void ce_row(__nv_bfloat16* __restrict__ logits, int64
   __syncthreads();  // the target logit is read before it is overwritten
   const float sc = valid ? scale[0] : 0.f;
   if (vec) {
-    for (int c0 = threadIdx.x * 8; c0 < V; c0 += kThreads * 8 * kUnroll) {
-      uint4 raw[kUnroll];
+    for (int c = threadIdx.x * 8; c < V; c += kThreads * 8) {
+      uint4 raw = *reinterpret_cast<const uint4*>(row + c);
+      uint32_t* p = &raw.x;
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int c = c0 + u * kThreads * 8;
-        if (c < V) raw[u] = *reinterpret_cast<const uint4*>(row + c);
+      for (int q = 0; q < 4; ++q) {
+        float2 f = unpack_bf16x2(p[q]);
+        float g0 = __expf(f.x - lse), g1 = __expf(f.y - lse);
+        if (inside && c + 2 * q == local) g0 -= 1.f;
+        if (inside && c + 2 * q + 1 == local) g1 -= 1.f;
+        p[q] = pack_bf16x2(g0 * sc, g1 * sc);
       }
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int c = c0 + u * kThreads * 8;
-        if (c >= V) break;
-        uint32_t* p = &raw[u].x;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float2 f = unpack_bf16x2(p[q]);
-          float g0 = __expf(f.x - lse), g1 = __expf(f.y - lse);
-          if (inside && c + 2 * q == local) g0 -= 1.f;
-          if (inside && c + 2 * q + 1 == local) g1 -= 1.f;
-          p[q] = pack_bf16x2(g0 * sc, g1 * sc);
-        }
-        *reinterpret_cast<uint4*>(row + c) = raw[u];
-      }
+      *reinterpret_cast<uint4*>(row + c) = raw;
     }
   } else {
     for (int c = threadIdx.x; c < V; c += kThreads) {
@@ -167,117 +135,6 @@ __device__ __forceinline__ void ce_row(__nv_bfloat16* __restrict__ logits, int64
       if (inside && c == local) g -= 1.f;
       row[c] = __float2bfloat16(g * sc);
     }
-  }
-}
-
-// One CTA per row (a grid that walks rows also works: the shared statistics
-// of a row are consumed before the next row's are written).
-__global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld,
-                                                     const int64_t* __restrict__ labels, int T, int V,
-                                                     int64_t v0, const float* __restrict__ scale,
-                                                     float* __restrict__ row_lse, bool lse_given,
-                                                     float* __restrict__ row_target, bool write_grad) {
-  pdl_prologue();
-  for (int t = blockIdx.x; t < T; t += gridDim.x) {
-    ce_row(logits, ld, labels, t, V, v0, scale, row_lse, lse_given, row_target, write_grad);
-    __syncthreads();
-  }
-}
-
-// Cluster-resident variant for wide rows: a cluster of kClusterCtas CTAs owns
-// one row, each CTA one contiguous quarter kept in its shared memory.  The
-// quarter is read from DRAM once (statistics on the fly, running max), the
-// CTAs exchange their (max, sum-exp) through distributed shared memory and
-// merge them in rank order, and the gradient is computed from shared memory
-// and written once: the logits cross DRAM once each way with no reliance on
-// L2 for a second read.
-constexpr int kClusterCtas = 4;
-constexpr int kClusterThreads = 512;
-
-__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kClusterThreads)
-    ce_cluster_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld, const int64_t* __restrict__ labels, int V,
-                      int64_t v0, const float* __restrict__ scale, float* __restrict__ row_lse,
-                      float* __restrict__ row_target, bool write_grad) {
-  pdl_prologue();
-  namespace cg = cooperative_groups;
-  cg::cluster_group cluster = cg::this_cluster();
-  extern __shared__ uint4 s_row[];          // this CTA's part of the row (16-byte vectors)
-  __shared__ float2 s_stat[kClusterCtas];   // per-rank (max, sum-exp), read by every CTA of the cluster
-  const int part = (int)cluster.block_rank();
-  const int64_t t = blockIdx.x / kClusterCtas;
-  const int nvec = V / 8 / kClusterCtas;    // vectors per part (V % (8 * kClusterCtas) == 0)
-  uint4* row4 = reinterpret_cast<uint4*>(logits + t * ld) + (int64_t)part * nvec;
-  float m = -FLT_MAX, s = 0.f;
-  for (int i0 = threadIdx.x; i0 < nvec; i0 += kClusterThreads * kUnroll) {
-    uint4 raw[kUnroll];
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int i = i0 + u * kClusterThreads;
-      if (i < nvec) raw[u] = row4[i];
-    }
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int i = i0 + u * kClusterThreads;
-      if (i >= nvec) break;
-      s_row[i] = raw[u];
-      const uint32_t* p = &raw[u].x;
-      float v[8];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 f = unpack_bf16x2(p[q]);
-        v[2 * q] = f.x;
-        v[2 * q + 1] = f.y;
-      }
-      float lm = v[0];
-#pragma unroll
-      for (int j = 1; j < 8; ++j) lm = fmaxf(lm, v[j]);
-      if (lm > m) {
-        s *= __expf(m - lm);
-        m = lm;
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) s += __expf(v[j] - m);
-    }
-  }
-  block_stats_n<kClusterThreads>(m, s);
-  if (threadIdx.x == 0) s_stat[part] = make_float2(m, s);
-  cluster.sync();  // every part's statistics written (and every s_row filled)
-  float gm = -FLT_MAX, gs = 0.f;
-#pragma unroll
-  for (int r = 0; r < kClusterCtas; ++r) {
-    const float2 o = *cluster.map_shared_rank(&s_stat[r], r);
-    online_merge(gm, gs, o.x, o.y);
-  }
-  cluster.sync();  // no CTA leaves (or reuses s_stat) while others still read it
-  const float lse = gm + __logf(gs);
-  const int64_t label = labels[t];
-  const bool valid = label >= 0;
-  const int64_t local = label - v0;
-  const bool inside = valid && local >= 0 && local < V;
-  const int64_t lo = (int64_t)part * nvec * 8;
-  const bool mine = inside && local >= lo && local < lo + (int64_t)nvec * 8;
-  if (threadIdx.x == 0) {
-    if (part == 0 && row_lse) row_lse[t] = lse;
-    if (row_target && (mine || (!inside && part == 0))) {
-      const int64_t li = local - lo;
-      row_target[t] = mine ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(s_row)[li]) : 0.f;
-    }
-  }
-  if (!write_grad) return;
-  const float sc = valid ? scale[0] : 0.f;
-  for (int i = threadIdx.x; i < nvec; i += kClusterThreads) {
-    uint4 raw = s_row[i];
-    uint32_t* p = &raw.x;
-    const int64_t c = lo + (int64_t)i * 8;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float2 f = unpack_bf16x2(p[q]);
-      float g0 = __expf(f.x - lse), g1 = __expf(f.y - lse);
-      if (inside && c + 2 * q == local) g0 -= 1.f;
-      if (inside && c + 2 * q + 1 == local) g1 -= 1.f;
-      p[q] = pack_bf16x2(g0 * sc, g1 * sc);
-    }
-    row4[i] = raw;
   }
 }
 
@@ -355,28 +212,8 @@ void ce_fwd_bwd(void* logits, int64_t ld, const int64_t* labels, int T, int V, i
                 bool write_grad, cudaStream_t s) {
   if (T == 0) return;
   PB_CHECK(!write_grad || scale != nullptr, "ce: gradient scale pointer required");
-  const size_t part_bytes = (size_t)V * 2 / kClusterCtas;
-  if (!lse_given && V % (8 * kClusterCtas) == 0 && V >= 4096 && part_bytes <= 96 * 1024 && ld % 8 == 0 &&
-      (reinterpret_cast<uintptr_t>(logits) & 15) == 0 && (int64_t)T * kClusterCtas < (int64_t)INT32_MAX) {
-    static std::mutex mu;
-    static size_t attr_bytes[64] = {0};
-    int dev = 0;
-    PB_CUDA_CHECK(cudaGetDevice(&dev));
-    {
-      std::lock_guard<std::mutex> lk(mu);
-      if (attr_bytes[dev & 63] < part_bytes) {
-        PB_CUDA_CHECK(cudaFuncSetAttribute(ce_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)part_bytes));
-        attr_bytes[dev & 63] = part_bytes;
-      }
-    }
-    launch_k(ce_cluster_kernel, T * kClusterCtas, kClusterThreads, part_bytes, s, (__nv_bfloat16*)logits, ld, labels,
-             V, v0, scale, row_lse, row_target, write_grad);
-    PB_CUDA_CHECK(cudaGetLastError());
-    return;
-  }
   launch_k(ce_kernel, T, kThreads, 0, s, (__nv_bfloat16*)logits, ld, labels, T, V, v0, scale, row_lse,
-           lse_given, row_target, write_grad);
+                                   lse_given, row_target, write_grad);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -230,7 +230,7 @@ def test_swiglu_bwd():
     _check_no_device_error()
 
 
-@pytest.mark.parametrize("V", [5000, 8192, 151936])  # 8192 / 151936: the 4-CTA cluster kernel
+@pytest.mark.parametrize("V", [5000, 8192, 151936])
 def test_cross_entropy(V):
     C = _ext()
     torch.manual_seed(7)
