@@ -143,8 +143,9 @@ def case_fsdp_ag(W, rank, dev, nbytes, warmup, iters):
     buf, n = _flat_buffers(W, dev, nbytes)
     shard = n // W
     full = torch.empty(n, device=dev, dtype=torch.bfloat16)
-    src = [p for p in buf.peer_ptrs]
-    dst = [full.data_ptr() + r * shard * 2 for r in range(W)]
+    order = [(rank + i) % W for i in range(W)]  # as the FSDP gather: own shard first, then rank+1, ...
+    src = [buf.peer_ptrs[r] for r in order]
+    dst = [full.data_ptr() + r * shard * 2 for r in order]
 
     def ours():
         buf.barrier(0, 60.0)

@@ -272,7 +272,11 @@ class P2PUnitCollectives:
         full = torch.empty(unit.full_numel, dtype=unit.local_bucket.dtype, device=unit.device)
         src, dst, nb = [], [], []
         fbase = full.data_ptr()
-        for r in range(self.world):
+        # each rank starts with its own shard and walks the peers from rank+1:
+        # the copy kernel's blocks run roughly in segment order, and a common
+        # order would have every rank read the same source's NVLink port at once
+        for i in range(self.world):
+            r = (self.rank + i) % self.world
             for m in unit.param_metas:
                 if m.padded_numel == 0:
                     continue

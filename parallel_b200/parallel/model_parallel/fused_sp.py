@@ -47,15 +47,20 @@ from ..comm.p2p import SymmBuffer, p2p_supported
 _PIECES_PER_BLOCK = 256 // 16  # kGatherRowsPerPiece = 16 rows per copy piece
 
 
-def pull_gather_plan(peer_ptrs: list[int], dst_ptr: int, batch: int, seq: int, cols: int, es: int = 2):
+def pull_gather_plan(peer_ptrs: list[int], dst_ptr: int, batch: int, seq: int, cols: int, es: int = 2,
+                     rank: int = 0):
     """Peer-gather arguments (src, dst, nbytes) that assemble the gathered
     [batch*seq, cols] activation from every rank's [batch*seq/world, cols]
-    shard: rank j holds positions [j*sl, (j+1)*sl) of every sequence."""
+    shard: rank j holds positions [j*sl, (j+1)*sl) of every sequence.  The
+    segments start at ``rank``'s own shard and walk the peers from rank+1, so
+    the ranks of a group read different sources at any moment."""
     world = len(peer_ptrs)
     sl = seq // world
     seg = sl * cols * es
     src, dst = [], []
-    for j, p in enumerate(peer_ptrs):
+    for i in range(world):
+        j = (rank + i) % world
+        p = peer_ptrs[j]
         for b in range(batch):
             src.append(p + b * seg)
             dst.append(dst_ptr + (b * seq + j * sl) * cols * es)
@@ -155,7 +160,7 @@ class FusedSequenceParallel:
             with collective_profile("sp_all_gather_gemm", value=x_local, mode="pull", flops=2.0 * T * K * n_cols,
                                     link_bytes=(self.world - 1) * rows_local * K * 2):
                 buf.barrier(0, self.limit_s)
-                ext().p2p_copy(*pull_gather_plan(buf.peer_ptrs, x_full.data_ptr(), batch, seq, K))
+                ext().p2p_copy(*pull_gather_plan(buf.peer_ptrs, x_full.data_ptr(), batch, seq, K, rank=self.rank))
                 if swiglu_inter:
                     ext().gemm(x_full, b, out, False, False, EPI_SWIGLU, 1.0, gu_out, up, n_out)
                 else:
@@ -270,13 +275,19 @@ class FusedTensorParallel:
             ext().gemm(x, b, out, False, b_mn, EPI_STORE_BF16, 1.0)
         return out, x
 
+    def _order(self) -> list[int]:
+        """Peer order of this rank's copies: itself first, then rank+1, ...
+        (a common order would send every rank to the same peer at once)."""
+        return [(self.rank + i) % self.world for i in range(self.world)]
+
     def _reduce_and_gather(self, rs, red, y: torch.Tensor, slot: int) -> None:
         rs.barrier(0, self.limit_s)
         base = rs.tensor.data_ptr()
         ext().p2p_reduce([[base + s * slot * 2] for s in range(self.world)], [red.tensor.data_ptr()], [slot],
                          1.0, False)
         red.barrier(0, self.limit_s)
-        ext().p2p_copy(list(red.peer_ptrs), [y.data_ptr() + r * slot * 2 for r in range(self.world)],
+        order = self._order()
+        ext().p2p_copy([red.peer_ptrs[r] for r in order], [y.data_ptr() + r * slot * 2 for r in order],
                        [slot * 2] * self.world)
 
     def try_all_reduce(self, x: torch.Tensor):
@@ -300,8 +311,9 @@ class FusedTensorParallel:
         slot = rows_local * N
         y = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
         with collective_profile("tp_all_reduce", value=x2, mode="p2p"):
-            ext().p2p_copy([x2.data_ptr() + r * slot * 2 for r in range(self.world)],
-                           [rs.peer_ptrs[r] + self.rank * slot * 2 for r in range(self.world)], [slot * 2] * self.world)
+            order = self._order()
+            ext().p2p_copy([x2.data_ptr() + r * slot * 2 for r in order],
+                           [rs.peer_ptrs[r] + self.rank * slot * 2 for r in order], [slot * 2] * self.world)
             self._reduce_and_gather(rs, red, y, slot)
         self.n += 1
         return y.view(x.shape)

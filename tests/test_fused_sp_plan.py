@@ -45,8 +45,11 @@ def test_pull_gather_assembles_every_sequence_in_position_order(world, batch, se
         s.copy_(torch.arange(s.numel(), dtype=torch.float32).view_as(s) + 1000 * j)
     for rank in range(world):
         full = A.alloc((batch * seq, cols))
-        src, dst, nbytes = pull_gather_plan([s.data_ptr() for s in shards], full.data_ptr(), batch, seq, cols)
+        ptrs = [s.data_ptr() for s in shards]
+        src, dst, nbytes = pull_gather_plan(ptrs, full.data_ptr(), batch, seq, cols, rank=rank)
         assert all(x % 16 == 0 for x in src + dst + nbytes)   # the copy kernel's alignment rule
+        # the rank reads its own shard first, then rank+1, ...: ranks start on different sources
+        assert src[0] == ptrs[rank] and src[batch] == ptrs[(rank + 1) % world]
         A.copy(src, dst, nbytes)
         want = torch.cat([torch.cat([shards[j][b * sl:(b + 1) * sl] for j in range(world)]) for b in range(batch)])
         assert torch.equal(full, want)
