@@ -18,6 +18,14 @@
 //                    peers of src_peer[i] (+ out[i] when accumulating), bf16 in
 //                    and out, fp32 sums.
 //   wait_flag        test hook: bounded wait on a flag that nobody sets.
+//   multimem_all_reduce  NVLS all-reduce of a bf16 buffer bound to an NVLink
+//                    multicast object: each rank reads its 1/world slice
+//                    through the switch with multimem.ld_reduce (the switch
+//                    sums every GPU's copy, fp32 accumulation) and stores the
+//                    result back with multimem.st (the switch writes it to
+//                    every GPU).  Each GPU receives the slice sums once and
+//                    the broadcast once: half the NVLink traffic of a
+//                    reduce-scatter followed by an all-gather over peer loads.
 //
 // Reference counterpart: the NCCL all_gather_into_tensor / reduce_scatter_
 // tensor / all_reduce calls of parallel/parallel/engine/_dp_param_unit.py:
@@ -172,6 +180,45 @@ __global__ void __launch_bounds__(512) reduce_segments_kernel(ReduceSegments seg
       *reinterpret_cast<uint4*>(dst) = o;
     }
   }
+}
+
+constexpr int kMmUnroll = 4;
+
+// Vectors [lo, hi) of the multicast range: out = scale * sum over ranks.
+__global__ void __launch_bounds__(512) multimem_all_reduce_kernel(uint4* __restrict__ mc, int64_t lo, int64_t hi,
+                                                                  float scale) {
+  pdl_prologue();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t base = lo + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < hi; base += kMmUnroll * stride) {
+    uint4 v[kMmUnroll];
+#pragma unroll
+    for (int u = 0; u < kMmUnroll; ++u) {
+      const int64_t i = base + u * stride;
+      if (i < hi)
+        asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v[u].x), "=r"(v[u].y), "=r"(v[u].z), "=r"(v[u].w)
+                     : "l"(mc + i)
+                     : "memory");
+    }
+#pragma unroll
+    for (int u = 0; u < kMmUnroll; ++u) {
+      const int64_t i = base + u * stride;
+      if (i >= hi) continue;
+      if (scale != 1.f) {
+        uint32_t* w = &v[u].x;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(w[q]);
+          w[q] = pack_bf16x2(f.x * scale, f.y * scale);
+        }
+      }
+      asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(mc + i), "r"(v[u].x),
+                   "r"(v[u].y), "r"(v[u].z), "r"(v[u].w)
+                   : "memory");
+    }
+  }
+  // the closing barrier publishes these stores to the other ranks
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
 __global__ void wait_flag_kernel(const uint32_t* flag, uint32_t target, uint64_t limit_ns, int* status) {
@@ -356,6 +403,33 @@ void multi_copy(const CopySegments& segs, cudaStream_t s) {
 void reduce_segments(const ReduceSegments& segs, int world, float scale, bool accumulate, cudaStream_t s) {
   if (segs.n == 0) return;
   launch_k(reduce_segments_kernel, chunk_grid(segs.vec_start[segs.n]), 512, 0, s, segs, world, scale, accumulate);
+  PB_CUDA_CHECK(cudaGetLastError());
+}
+
+bool device_multicast_supported(int device) {
+  using GetAttrFn = CUresult (*)(int*, CUdevice_attribute, CUdevice);
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuDeviceGetAttribute", &p, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || p == nullptr)
+    return false;
+  int v = 0;
+  if (reinterpret_cast<GetAttrFn>(p)(&v, CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED, (CUdevice)device) != CUDA_SUCCESS)
+    return false;
+  return v != 0;
+}
+
+void multimem_all_reduce(void* mc, int64_t nelem, int rank, int world, float scale, cudaStream_t s) {
+  PB_CHECK(world >= 1 && world <= kMaxPeers && rank >= 0 && rank < world, "multimem_all_reduce: rank / world");
+  PB_CHECK(nelem % 8 == 0 && reinterpret_cast<uintptr_t>(mc) % 16 == 0, "multimem_all_reduce: 16-byte vectors");
+  const int64_t vecs = nelem / 8;
+  const int64_t per = (vecs + world - 1) / world;
+  const int64_t lo = std::min<int64_t>(vecs, per * rank), hi = std::min<int64_t>(vecs, lo + per);
+  if (hi <= lo) return;
+  // enough 16-byte requests in flight to cover the switch round trip; at most
+  // four 512-thread blocks per SM
+  const int64_t blocks = std::min<int64_t>((hi - lo + 512 * kMmUnroll - 1) / (512 * kMmUnroll), 148 * 4);
+  launch_k(multimem_all_reduce_kernel, (unsigned)blocks, 512, 0, s, reinterpret_cast<uint4*>(mc), lo, hi, scale);
   PB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -32,6 +32,13 @@ void signal_barrier(const uint64_t* peer_pads_dev, int rank, int world, int slot
 void multi_copy(const CopySegments& segs, cudaStream_t s);
 void reduce_segments(const ReduceSegments& segs, int world, float scale, bool accumulate, cudaStream_t s);
 void wait_flag(const uint32_t* flag, uint32_t target, uint64_t limit_ns, int* status, cudaStream_t s);
+// NVLS all-reduce over a multicast address (bf16, nelem % 8 == 0): this rank
+// reduces and broadcasts vectors [rank, rank + 1) * ceil(vecs / world).  The
+// caller brackets it with barriers (inputs staged; broadcasts landed).
+void multimem_all_reduce(void* mc, int64_t nelem, int rank, int world, float scale, cudaStream_t s);
+// CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED of a device (switch multicast and
+// in-switch reduction), read through the driver entry point.
+bool device_multicast_supported(int device);
 
 // Expert-parallel row exchange over peer memory (one warp per row, 16-byte
 // vectors; row_bytes and all strides multiples of 16 bytes).

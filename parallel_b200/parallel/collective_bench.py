@@ -20,7 +20,10 @@ Cases (bf16 N(0,1) inputs from a fixed seed):
   all-to-alls with host-read splits around ``torch._grouped_mm``; uniform and skewed
   routing;
 * ``ce``  vocabulary-parallel LM head + cross-entropy (peer log-sum-exp merge vs NCCL
-  all-reduces).
+  all-reduces);
+* ``all_reduce``  flat bf16 all-reduce: in-switch NVLS (``multimem``) where the
+  fabric has it, the peer-load path as ``pull_us``, NCCL as the baseline (not in
+  the default list: ``--cases all_reduce``).
 
 Every time is device time with CUDA events after warm-up, the max over ranks.
 ``roofline`` is the slower of the FLOPs at the measured bf16 GEMM peak and the
@@ -175,6 +178,36 @@ def case_fsdp_rs(W, rank, dev, nbytes, warmup, iters):
     return _report("fsdp_rs", [n * 2 // (1 << 20), "MB"], t_ours, t_base, 0, (W - 1) * shard * 2)
 
 
+def case_all_reduce(W, rank, dev, nbytes, warmup, iters):
+    """bf16 SUM all-reduce of one flat buffer.  ours: the in-switch NVLS
+    all-reduce (``NvlsAllReduce``: multimem.ld_reduce of this rank's slice,
+    multimem.st of the sum) when the fabric has it, else the peer-load mean
+    path; pull: the peer-load path (copy into a symmetric slot, barrier, every
+    rank reads and sums all slots); baseline: NCCL all_reduce.  Roofline: each
+    GPU receives the buffer once (in-switch reduction)."""
+    from .comm.p2p import NvlsAllReduce, ReplicaMeanAllReduce
+
+    n = nbytes // 2
+    x = torch.randn(n, generator=torch.Generator().manual_seed(rank)).to(dev, torch.bfloat16)
+    y = torch.empty_like(x)
+    nv = NvlsAllReduce.get(dist.group.WORLD, dev, n, force=True)
+    prev = os.environ.get("PB_NVLS")
+    os.environ["PB_NVLS"] = "0"
+    try:
+        peer = ReplicaMeanAllReduce.get(dist.group.WORLD, dev, [y])
+    finally:
+        if prev is None:
+            os.environ.pop("PB_NVLS", None)
+        else:
+            os.environ["PB_NVLS"] = prev
+    t_pull = _time(lambda: peer.mean_([y]), warmup, iters)
+    t_ours = _time(lambda: nv.all_reduce_([x], 1.0, outs=[y]), warmup, iters) if nv is not None else t_pull
+    t_base = _time(lambda: dist.all_reduce(y), warmup, iters)
+    out = _report("all_reduce" + ("_nvls" if nv is not None else "_p2p"), [nbytes >> 20, "MB"], t_ours, t_base, 0,
+                  nbytes, pull_us=t_pull)
+    return out
+
+
 def _torch_experts(x, idx, w, w_gu, w_d):
     """Reference-style expert MLPs of locally received routes: sort by expert,
     torch grouped GEMMs (``torch._grouped_mm``, the op HF's grouped expert path
@@ -277,6 +310,9 @@ def main(argv=None):
             results.append(case_fsdp_ag(W, rank, dev, nb, args.warmup, args.iters))
         if "fsdp_rs" in cases:
             results.append(case_fsdp_rs(W, rank, dev, nb, args.warmup, args.iters))
+    if "all_reduce" in cases:
+        for nb in flat:
+            results.append(case_all_reduce(W, rank, dev, nb, args.warmup, args.iters))
     if "ep" in cases:
         # tokens per rank (Qwen3-30B-A3B at B=1, S=4096 under sp=4 has 1024), hidden 2048, top-8 of 128
         # experts, expert SwiGLU width 768; uniform routing and an N(0, 2)-biased (skewed) router

@@ -172,7 +172,9 @@ class ReplicaMeanAllReduce:
             self.offsets.append(off)
             off += -(-n // 8) * 8
         self.limit_s = float(os.environ.get("PB_P2P_TIMEOUT_S", "60"))
-        self.sets = [SymmBuffer(max(off, 8), torch.bfloat16, device, group, "replica_grads") for _ in range(2)]
+        self.nvls = NvlsAllReduce.get(group, device, off)
+        self.sets = [] if self.nvls is not None else [
+            SymmBuffer(max(off, 8), torch.bfloat16, device, group, "replica_grads") for _ in range(2)]
         self.turn = 0
 
     @staticmethod
@@ -194,6 +196,9 @@ class ReplicaMeanAllReduce:
         return cls._instances[key]
 
     def mean_(self, tensors) -> None:
+        if self.nvls is not None:
+            self.nvls.all_reduce_(tensors, 1.0 / self.world)
+            return
         buf = self.sets[self.turn % 2]
         self.turn += 1
         base = buf.tensor.data_ptr()
@@ -203,6 +208,109 @@ class ReplicaMeanAllReduce:
         srcs = [[p + 2 * o for o in self.offsets] for p in buf.peer_ptrs]
         ext().p2p_reduce(srcs, [t.data_ptr() for t in tensors], [t.numel() for t in tensors], 1.0 / self.world,
                          False)
+
+
+def nvls_mode() -> str:
+    """``PB_NVLS``: ``0`` never uses the in-switch all-reduce, ``1`` uses it
+    wherever the probe passes, ``auto`` (default) as ``1`` for groups of
+    more than two ranks, where it halves the NVLink traffic of the peer-load
+    all-reduce (at two ranks both move the same bytes)."""
+    return os.environ.get("PB_NVLS", "auto")
+
+
+class NvlsAllReduce:
+    """All-reduce of bf16 buffers through the NVSwitch (NVLS): the symmetric
+    staging buffer is bound to an NVLink multicast object, every rank reduces
+    its 1/world slice with ``multimem.ld_reduce`` (the switch sums all GPUs'
+    copies, fp32 accumulation) and writes the result to every GPU with one
+    ``multimem.st`` (``csrc/comm.cu``).  Each GPU then receives every byte once,
+    where the peer-load scheme (owners pull and sum, then everyone gathers)
+    receives it 2 (world - 1) / world times.
+
+    Capability probe (``get``): the device reports switch multicast
+    (``CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED``), every rank of the group
+    agrees, and the symmetric allocation came back with a multicast address;
+    otherwise None and the caller keeps its peer-load path.  The reference
+    all-reduces with NCCL (parallel/parallel/engine/engine.py:224-247), which
+    picks NVLS itself when the fabric offers it.
+
+    Staging: copy in, barrier, reduce + broadcast, barrier, copy out.  After
+    the second barrier no rank reads or writes another's buffer any more, so
+    one buffer serves every call."""
+
+    _instances: dict = {}
+
+    def __init__(self, group, device, capacity: int):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.capacity = -(-capacity // 8) * 8
+        self.limit_s = float(os.environ.get("PB_P2P_TIMEOUT_S", "60"))
+        self.buf = SymmBuffer(self.capacity, torch.bfloat16, device, group, "nvls_all_reduce")
+        # the multicast mapping covers the allocation from its base (the handle's
+        # own buffer pointer); the payload starts `off` bytes in (guard words in
+        # the debug mode) and must end inside it
+        h = self.buf.handle
+        mc = int(getattr(h, "multicast_ptr", 0) or 0)
+        off = self.buf.tensor.data_ptr() - int(list(h.buffer_ptrs)[self.rank])
+        inside = int(getattr(h, "offset", 0) or 0) == 0 and 0 <= off and off + 2 * self.capacity <= int(h.buffer_size)
+        self.mc = mc + off if (mc and inside) else 0
+
+    @staticmethod
+    def probe(group, device) -> bool:
+        """True on every rank when every rank's device supports switch
+        multicast (collective over ``group``; CUDA devices only)."""
+        if device.type != "cuda" or not p2p_supported(group):
+            return False
+        ok = torch.tensor([1 if ext().device_multicast_supported(device.index) else 0], device=device,
+                          dtype=torch.int32)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        return bool(ok.item())
+
+    @classmethod
+    def get(cls, group, device, capacity: int, force: bool = False):
+        """The group's instance holding at least ``capacity`` elements, or
+        None when NVLS is off (``PB_NVLS``) or not available.  Creating it is
+        collective over the group."""
+        mode = nvls_mode()
+        world = dist.get_world_size(group)
+        if device.type != "cuda" or mode == "0" or (mode == "auto" and world <= 2 and not force):
+            return None
+        key = (id(group), device.index)
+        inst = cls._instances.get(key)
+        if inst is not None and inst.capacity >= capacity:
+            return inst if inst.mc else None
+        if torch.cuda.is_current_stream_capturing():  # the probe and the allocation are host-synchronous
+            return None
+        if not cls.probe(group, device):
+            return None
+        inst = cls(group, device, capacity)
+        ok = torch.tensor([1 if inst.mc else 0], device=device, dtype=torch.int32)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if not ok.item():
+            inst.mc = 0
+        cls._instances[key] = inst
+        return inst if inst.mc else None
+
+    def all_reduce_(self, tensors, scale: float = 1.0, outs=None) -> None:
+        """Each bf16 tensor's scale x sum over the group, written in place or
+        into ``outs`` (same shapes).  Tensors are contiguous, 16-byte aligned,
+        a multiple of 8 elements and together at most ``capacity`` elements."""
+        outs = tensors if outs is None else outs
+        offs, off = [], 0
+        for t in tensors:
+            offs.append(off)
+            off += t.numel()
+        if off > self.capacity:
+            raise ValueError(f"{off} elements exceed the {self.capacity}-element NVLS buffer")
+        base = self.buf.tensor.data_ptr()
+        ext().p2p_copy([t.data_ptr() for t in tensors], [base + 2 * o for o in offs],
+                       [2 * t.numel() for t in tensors])
+        self.buf.barrier(0, self.limit_s)
+        ext().multimem_all_reduce(self.mc, off, self.rank, self.world, scale)
+        self.buf.barrier(1, self.limit_s)
+        ext().p2p_copy([base + 2 * o for o in offs], [t.data_ptr() for t in outs],
+                       [2 * t.numel() for t in tensors])
 
 
 @dataclass

@@ -448,8 +448,8 @@ class ParallelEngine:
 
             peer = ReplicaMeanAllReduce.get(group, self.device, tensors)
         if peer is not None:
-            with collective_profile(op, payload_bytes=sum(2 * t.numel() for t in tensors), mode="p2p",
-                                    detail="replicate"):
+            with collective_profile(op, payload_bytes=sum(2 * t.numel() for t in tensors),
+                                    mode="nvls" if peer.nvls is not None else "p2p", detail="replicate"):
                 peer.mean_(tensors)
             return
         for t in tensors:

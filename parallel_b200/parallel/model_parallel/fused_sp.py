@@ -42,7 +42,7 @@ import torch.distributed as dist
 from ...ops._ext import ext
 from ...ops.gemm import EPI_STORE_BF16, EPI_SWIGLU
 from ...profiling import collective_profile
-from ..comm.p2p import SymmBuffer, p2p_supported
+from ..comm.p2p import NvlsAllReduce, SymmBuffer, p2p_supported
 
 _PIECES_PER_BLOCK = 256 // 16  # kGatherRowsPerPiece = 16 rows per copy piece
 
@@ -291,14 +291,22 @@ class FusedTensorParallel:
                        [slot * 2] * self.world)
 
     def try_all_reduce(self, x: torch.Tensor):
-        """SUM of a bf16 CUDA tensor over the group on the same buffers (row
-        blocks pushed to their owners, owner reduce, gather); None when the
-        shape does not fit (rows % world, or larger than the buffers sized by
-        the first call), so the caller falls back to NCCL."""
+        """SUM of a bf16 CUDA tensor over the group: through the switch
+        (``NvlsAllReduce``) where the group has NVLS, else on the same buffers
+        as the sequence-parallel collectives (row blocks pushed to their
+        owners, owner reduce, gather).  None when the shape does not fit
+        (rows % world, or larger than the buffers sized by the first call), so
+        the caller falls back to NCCL."""
         if not (x.is_cuda and x.dtype == torch.bfloat16 and x.dim() >= 1 and x.shape[-1] % 8 == 0):
             return None
-        x2 = x.reshape(-1, x.shape[-1])
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
         M, N = x2.shape
+        nv = NvlsAllReduce.get(self.group, x.device, M * N)
+        if nv is not None and x2.data_ptr() % 16 == 0:
+            y = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
+            with collective_profile("tp_all_reduce", value=x2, mode="nvls"):
+                nv.all_reduce_([x2], 1.0, outs=[y])
+            return y.view(x.shape)
         if M % self.world:
             return None
         rows_local = M // self.world

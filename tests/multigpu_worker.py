@@ -204,7 +204,81 @@ def main_small():
     dist.destroy_process_group()
 
 
+def main_nvls():
+    """In-switch all-reduce (multimem) against an fp32 sum of the same bf16
+    inputs: several tensors, a mean scale, the replicate-mean wrapper and a
+    replayed CUDA graph.  Writes {"skipped": why} where the fabric has no NVLS."""
+    from parallel_b200.ops._ext import check_device_errors
+    from parallel_b200.parallel.comm.p2p import NvlsAllReduce, ReplicaMeanAllReduce
+
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    rank, W = dist.get_rank(), dist.get_world_size()
+    group = dist.group.WORLD
+    out = {}
+    nv = NvlsAllReduce.get(group, dev, 1 << 22, force=True)
+    if nv is None:
+        out["skipped"] = "no switch multicast on this fabric (probe or multicast address)"
+    else:
+        g = torch.Generator(device="cpu").manual_seed(7 + rank)
+        worst = 0.0
+        for sizes, scale in (([8], 1.0), ([4096, 1 << 20, 24], 1.0), ([3 * (1 << 20)], 1.0 / W)):
+            xs = [torch.randn(n, generator=g).to(dev, torch.bfloat16) for n in sizes]
+            ref = [x.float() for x in xs]
+            for r in ref:
+                dist.all_reduce(r)
+            got = [x.clone() for x in xs]
+            nv.all_reduce_(got, scale)
+            for a, b in zip(got, ref):
+                b = (b * scale).to(torch.bfloat16).float()
+                worst = max(worst, ((a.float() - b).abs().max() / (b.abs().max() + 1e-12)).item())
+        # the replicate mean takes the NVLS path when PB_NVLS=1
+        grads = [torch.randn(n, generator=g).to(dev, torch.bfloat16) for n in (1024, 65536)]
+        ref = [t.float() for t in grads]
+        for r in ref:
+            dist.all_reduce(r)
+        rm = ReplicaMeanAllReduce.get(group, dev, grads)
+        out["replica_uses_nvls"] = rm is not None and rm.nvls is not None
+        rm.mean_(grads)
+        for a, b in zip(grads, ref):
+            b = (b / W).to(torch.bfloat16).float()
+            worst = max(worst, ((a.float() - b).abs().max() / (b.abs().max() + 1e-12)).item())
+        # graph replay (device epochs in the barriers)
+        x = torch.full((4096,), float(rank + 1), device=dev, dtype=torch.bfloat16)
+        y = torch.empty_like(x)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            nv.all_reduce_([x], 1.0, outs=[y])
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            nv.all_reduce_([x], 1.0, outs=[y])
+        for i in range(3):
+            x.fill_(float(rank + 1 + i))
+            graph.replay()
+            torch.cuda.synchronize()
+            expect = sum(r + 1 + i for r in range(W))
+            worst = max(worst, abs(float(y[0]) - expect) / expect, abs(float(y[-1]) - expect) / expect)
+        graph.reset()
+        check_device_errors()
+        out["worst"] = worst
+    t = torch.tensor([out.get("worst", 0.0)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    out["worst"] = t.item()
+    if rank == 0:
+        with open(os.environ["PB_TEST_OUT"], "w") as f:
+            json.dump(out, f)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
+    if os.environ.get("PB_TEST_MODE") == "nvls":
+        return main_nvls()
     if os.environ.get("PB_TEST_MODE") == "sp":
         return main_sp()
     if os.environ.get("PB_TEST_MODE") == "small":

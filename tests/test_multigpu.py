@@ -109,3 +109,21 @@ def test_fused_tensor_parallel_matches_nccl(tmp_path, moe):
     for a, b in zip(res["fused"], res["nccl"]):
         assert abs(a - b) < 2e-2 * max(1.0, abs(b)), res
     assert res["grad_rel_diff"] < 3e-2, res
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_nvls_all_reduce_matches_fp32_sum(tmp_path):
+    """In-switch all-reduce (multimem.ld_reduce + multimem.st over the
+    multicast address of the symmetric buffer) equals an fp32 sum of the same
+    bf16 inputs rounded once; also through the replicate-mean wrapper and in a
+    replayed CUDA graph.  Skips where the fabric offers no switch multicast."""
+    out = tmp_path / "res_nvls.json"
+    env = dict(os.environ, PB_TEST_OUT=str(out), PB_TEST_MODE="nvls", PB_NVLS="1")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+           "--master-port", "29538", os.path.join(HERE, "multigpu_worker.py")]
+    subprocess.run(cmd, env=env, check=True, timeout=600)
+    res = json.loads(out.read_text())
+    if "skipped" in res:
+        pytest.skip(res["skipped"])
+    assert res["replica_uses_nvls"], res
+    assert res["worst"] < 8e-3, res
