@@ -35,7 +35,9 @@ void wait_flag(const uint32_t* flag, uint32_t target, uint64_t limit_ns, int* st
 // NVLS all-reduce over a multicast address (bf16, nelem % 8 == 0): this rank
 // reduces and broadcasts vectors [rank, rank + 1) * ceil(vecs / world).  The
 // caller brackets it with barriers (inputs staged; broadcasts landed).
-void multimem_all_reduce(void* mc, int64_t nelem, int rank, int world, float scale, cudaStream_t s);
+// blocks: grid size (0 = default); unroll: requests in flight per thread (4 or 8).
+void multimem_all_reduce(void* mc, int64_t nelem, int rank, int world, float scale, cudaStream_t s, int blocks = 0,
+                         int unroll = 4);
 // CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED of a device (switch multicast and
 // in-switch reduction), read through the driver entry point.
 bool device_multicast_supported(int device);

@@ -81,8 +81,10 @@ void p2p_reduce(const std::vector<std::vector<int64_t>>& src, const std::vector<
 
 // NVLS all-reduce of nelem bf16 values at the multicast address mc (see
 // comm.cuh); the caller stages the inputs and brackets the call with barriers.
-void multimem_all_reduce(int64_t mc, int64_t nelem, int64_t rank, int64_t world, double scale) {
-  pb::multimem_all_reduce(reinterpret_cast<void*>(mc), nelem, (int)rank, (int)world, (float)scale, cur_stream());
+void multimem_all_reduce(int64_t mc, int64_t nelem, int64_t rank, int64_t world, double scale, int64_t blocks,
+                         int64_t unroll) {
+  pb::multimem_all_reduce(reinterpret_cast<void*>(mc), nelem, (int)rank, (int)world, (float)scale, cur_stream(),
+                          (int)blocks, (int)unroll);
 }
 
 bool device_multicast_supported(int64_t device) { return pb::device_multicast_supported((int)device); }
@@ -190,7 +192,8 @@ void register_comm(pybind11::module& m) {
   m.def("p2p_copy", &p2p_copy);
   m.def("p2p_reduce", &p2p_reduce);
   m.def("wait_flag", &wait_flag);
-  m.def("multimem_all_reduce", &multimem_all_reduce);
+  m.def("multimem_all_reduce", &multimem_all_reduce, pybind11::arg("mc"), pybind11::arg("nelem"), pybind11::arg("rank"),
+        pybind11::arg("world"), pybind11::arg("scale"), pybind11::arg("blocks") = 0, pybind11::arg("unroll") = 4);
   m.def("device_multicast_supported", &device_multicast_supported);
   m.def("small_ar_region_floats", &small_ar_region_floats);
   m.def("small_all_reduce", &small_all_reduce);
