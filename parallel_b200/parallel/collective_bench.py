@@ -183,8 +183,9 @@ def case_all_reduce(W, rank, dev, nbytes, warmup, iters):
     all-reduce (``NvlsAllReduce``: multimem.ld_reduce of this rank's slice,
     multimem.st of the sum) when the fabric has it, else the peer-load mean
     path; pull: the peer-load path (copy into a symmetric slot, barrier, every
-    rank reads and sums all slots); baseline: NCCL all_reduce.  Roofline: each
-    GPU receives the buffer once (in-switch reduction)."""
+    rank reads and sums all slots); baseline: NCCL all_reduce.  Roofline: the
+    bytes each GPU receives, S (1 + 1/W) in the switch scheme (its reduced
+    slice, then every slice of the broadcast), 2 S (W - 1) / W otherwise."""
     from .comm.p2p import NvlsAllReduce, ReplicaMeanAllReduce
 
     n = nbytes // 2
@@ -204,7 +205,7 @@ def case_all_reduce(W, rank, dev, nbytes, warmup, iters):
     t_ours = _time(lambda: nv.all_reduce_([x], 1.0, outs=[y]), warmup, iters) if nv is not None else t_pull
     t_base = _time(lambda: dist.all_reduce(y), warmup, iters)
     out = _report("all_reduce" + ("_nvls" if nv is not None else "_p2p"), [nbytes >> 20, "MB"], t_ours, t_base, 0,
-                  nbytes, pull_us=t_pull)
+                  nbytes * (W + 1) / W if nv is not None else 2 * nbytes * (W - 1) / W, pull_us=t_pull)
     return out
 
 
