@@ -1,6 +1,6 @@
 """Micro-benchmarks of the sm_100a kernels at the Qwen3-0.6B training shapes.
 
-    python -m parallel_b200.ops.kernel_bench attn_fwd|attn_bwd|ce|gemm|gemm_vs_cublas|gemm_swiglu|gemm_residual|rmsnorm_bwd|qknorm|qknorm_bwd|wgrad_split|all [--iters N]
+    python -m parallel_b200.ops.kernel_bench attn_fwd|attn_bwd|ce|gemm|gemm_vs_cublas|gemm_swiglu|gemm_residual|moe_layer|rmsnorm_bwd|qknorm|qknorm_bwd|wgrad_split|all [--iters N]
 
 Each case runs a few warm-up launches, then times ``--iters`` launches with
 CUDA events on the current stream and prints the time per launch and the
@@ -256,7 +256,54 @@ def case_wgrad_oproj_cublas(warmup, iters):
     return f"wgrad o_proj cuBLAS: {us:.1f} us, {2 * out.numel() * g.shape[0] / us / 1e6:.0f} TF/s"
 
 
-CASES = {"attn_fwd": case_attn_fwd, "ce": case_ce, "gemm_vs_cublas": case_gemm_vs_cublas,
+def case_moe_layer(warmup, iters):
+    """One expert layer forward + backward at the per-rank shape of
+    Qwen3-30B-A3B under EP = SP = 4 (32 local experts, hidden 2048, expert
+    SwiGLU width 768, 8,192 routed rows, about 256 per expert): this
+    repository's device-resident path (routing plan, dispatch into the padded
+    expert matrix, tcgen05 grouped GEMMs with the SwiGLU epilogue, weighted
+    combine; ``ops.moe.routed_experts``) against torch's composition (sort by
+    expert, ``torch._grouped_mm``, SwiGLU, weights, unsort, sum over the
+    top-k), the one the reference's HF expert modules run."""
+    import torch.nn.functional as F
+
+    from .moe import LocalExpertTransport, routed_experts
+
+    E, Hd, Iw, T, K = 32, 2048, 768, 1024, 8
+    g = torch.Generator(device="cpu").manual_seed(0)
+    x = torch.randn(T, Hd, generator=g).to("cuda", torch.bfloat16).requires_grad_(True)
+    sc, idx = torch.softmax(torch.randn(T, E, generator=g), -1).topk(K, -1)
+    sc, idx = sc.cuda().requires_grad_(True), idx.cuda()
+    w_gu = (torch.randn(E, 2 * Iw, Hd, generator=g) * 0.02).to("cuda", torch.bfloat16).requires_grad_(True)
+    w_d = (torch.randn(E, Hd, Iw, generator=g) * 0.02).to("cuda", torch.bfloat16).requires_grad_(True)
+    dout = torch.randn(T, Hd, generator=g).to("cuda", torch.bfloat16)
+    transport = LocalExpertTransport(E)
+
+    def ours():
+        routed_experts(x, sc, idx, w_gu, w_d, transport).backward(dout)
+
+    def torch_path():
+        flat = idx.reshape(-1)
+        order = torch.argsort(flat, stable=True)
+        offs = torch.cumsum(torch.bincount(flat, minlength=E), 0).to(torch.int32)
+        xs = x.repeat_interleave(K, 0).index_select(0, order)
+        gu = torch._grouped_mm(xs, w_gu.transpose(1, 2), offs=offs)
+        gt, up = gu.chunk(2, dim=-1)
+        y = torch._grouped_mm((F.silu(gt) * up).contiguous(), w_d.transpose(1, 2), offs=offs)
+        y = y * sc.reshape(-1)[order, None].to(y.dtype)
+        out = torch.empty_like(y).index_copy_(0, order, y).view(T, K, Hd).sum(1)
+        out.backward(dout)
+
+    t_ours = _time(ours, warmup, iters)
+    t_torch = _time(torch_path, warmup, iters)
+    flops = 3 * 2 * T * K * Hd * 3 * Iw  # three products, forward + two backward
+    from ..parallel.collective_bench import GEMM_PEAK as peak  # measured cuBLAS bf16 burst
+    return (f"expert layer fwd+bwd ({T * K} routes, {E} experts, H {Hd}, I {Iw}): ours {t_ours:.1f} us "
+            f"({flops / t_ours / 1e6:.0f} TF/s, {flops / t_ours / 1e6 / (peak / 1e12):.2f} of measured bf16), "
+            f"torch._grouped_mm path {t_torch:.1f} us, speedup {t_torch / t_ours:.2f}x")
+
+
+CASES = {"attn_fwd": case_attn_fwd, "moe_layer": case_moe_layer, "ce": case_ce, "gemm_vs_cublas": case_gemm_vs_cublas,
          "wgrad_oproj": case_wgrad_oproj, "wgrad_oproj_cublas": case_wgrad_oproj_cublas, "attn_bwd": case_attn_bwd, "gemm": case_gemm, "gemm_swiglu": case_gemm_swiglu,
          "gemm_residual": case_gemm_residual, "rmsnorm_bwd": case_rmsnorm_bwd, "qknorm": case_qknorm,
          "qknorm_bwd": case_qknorm_bwd, "wgrad_split": case_wgrad_split}
