@@ -297,6 +297,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("krange"), pybind11::arg("b_mn"), pybind11::arg("epi"), pybind11::arg("alpha"),
         pybind11::arg("r") = pybind11::none(), pybind11::arg("b_up_offset") = 0, pybind11::arg("n_out") = 0,
         pybind11::arg("tile_expert") = pybind11::none(), pybind11::arg("n_tiles") = pybind11::none());
+  m.def("grouped_tile_n", [](int64_t mode, int64_t n) { return (int64_t)pb::grouped_bn((int)mode, (int)n); },
+        "column tile width of the grouped GEMM for a product with n output columns (mode 1 rows, 2 k)");
   m.def("read_error", &read_error);
   m.def("clear_error", &clear_error);
   m.def("set_error_for_test", &set_error_for_test);

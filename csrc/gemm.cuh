@@ -113,6 +113,9 @@ struct GroupedGemmParams {
   const int* n_tiles = nullptr;
 };
 void gemm_grouped(const GroupedGemmParams& p, cudaStream_t stream);
+// Column tile width (128 or 256) the grouped GEMM uses for a product with N
+// output columns in `mode` (1 rows, 2 k); k-mode work tables tile N by it.
+int grouped_bn(int mode, int N);
 
 // Dispatches to the one-CTA (gemm.cu) or the CTA-pair (gemm_pair.cu) kernel.
 void gemm_bf16(const GemmParams& p, cudaStream_t stream);

@@ -210,11 +210,13 @@ def _empty_work(device) -> torch.Tensor:
 
 def _k_work(num_local: int, m_group: int, n: int, device) -> torch.Tensor:
     """Weight-gradient work items {expert, M tile, N tile, 0} of every local
-    expert (each expert's K range comes from the route plan)."""
-    key = (num_local, m_group, n, str(device))
+    expert (each expert's K range comes from the route plan); N tiles are as
+    wide as the kernel's k-mode tile for this N."""
+    bn = int(ext().grouped_tile_n(2, n))
+    key = (num_local, m_group, n, bn, str(device))
     if key not in _K_WORK:
         items = [(e, tm, tn, 0) for e in range(num_local) for tm in range(-(-m_group // 128))
-                 for tn in range(-(-n // 128))]
+                 for tn in range(-(-n // bn))]
         _K_WORK[key] = torch.tensor(items, dtype=torch.int32, device=device)
     return _K_WORK[key]
 
