@@ -4,7 +4,9 @@
 # change (needs inotifywait or fswatch locally).
 #
 #   ./sync.sh HOST [PORT] [--watch]
-#   REMOTE_DIR=/root/parallel_b200 SSH_KEY=~/.ssh/id_ed25519 ./sync.sh 10.0.0.5 22
+#   REMOTE_USER=ubuntu REMOTE_DIR=work/parallel_b200 SSH_KEY=~/.ssh/id_ed25519 ./sync.sh 10.0.0.5 22
+#
+# REMOTE_DIR is relative to the remote user's home unless it starts with /.
 #
 # The compiled extension is not copied: run ./install.sh on the node (the
 # kernels are built for the node's own toolchain).
@@ -20,7 +22,8 @@ for a in "${@:2}"; do
         *) PORT=$a ;;
     esac
 done
-REMOTE_DIR=${REMOTE_DIR:-/root/parallel_b200}
+REMOTE_USER=${REMOTE_USER:-root}
+REMOTE_DIR=${REMOTE_DIR:-parallel_b200}
 SSH_KEY=${SSH_KEY:-$HOME/.ssh/id_ed25519}
 SSH="ssh -p $PORT -i $SSH_KEY -o StrictHostKeyChecking=accept-new"
 
@@ -29,7 +32,7 @@ sync_once() {
         --exclude '.git/' --exclude '__pycache__/' --exclude '*.pyc' --exclude '.pytest_cache/' \
         --exclude 'build/' --exclude '*.egg-info/' --exclude '*.so' --exclude '*.o' \
         --exclude '.ninja*' --exclude 'checkpoints/' --exclude 'wandb/' --exclude 'baseline/_ref/' \
-        ./ "root@$HOST:$REMOTE_DIR/"
+        ./ "$REMOTE_USER@$HOST:$REMOTE_DIR/"
     echo "synced to $HOST:$REMOTE_DIR"
 }
 
