@@ -206,6 +206,14 @@ def case_all_reduce(W, rank, dev, nbytes, warmup, iters):
     t_base = _time(lambda: dist.all_reduce(y), warmup, iters)
     out = _report("all_reduce" + ("_nvls" if nv is not None else "_p2p"), [nbytes >> 20, "MB"], t_ours, t_base, 0,
                   nbytes * (W + 1) / W if nv is not None else 2 * nbytes * (W - 1) / W, pull_us=t_pull)
+    if nv is not None:
+        # numerics of the timed path: against an fp32 NCCL sum of the same bf16 inputs
+        ref = x.float()
+        dist.all_reduce(ref)
+        nv.all_reduce_([x], 1.0, outs=[y])
+        err = ((y.float() - ref).abs().max() / ref.abs().max().clamp_min(1e-12)).reshape(1)
+        dist.all_reduce(err, op=dist.ReduceOp.MAX)
+        out["max_rel_err"] = float(err)
     return out
 
 
